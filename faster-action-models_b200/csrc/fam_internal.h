@@ -1,0 +1,74 @@
+// Internal declarations shared by the libfam translation units (not part of
+// the public C ABI; the public surface is include/fam.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fam {
+
+// ----------------------------------------------------------------- errors
+// Records a message for fam_last_error() and returns the non-zero status.
+int set_error(const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+
+// Device status word of the current device (allocated on first use, one int).
+int* device_status_word();
+
+// ------------------------------------------------------------------- TMA
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride
+// `row_stride` elements; box = 64 columns x box_rows rows, 128-byte swizzle,
+// out-of-bounds elements read as zero.
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                       uint64_t row_stride, uint32_t box_rows);
+
+// ------------------------------------------------------------------ GEMM
+enum EpiKind : int { kEpiStore = 0, kEpiPartial = 1, kEpiResidual = 2 };
+enum ActKind : int { kActNone = 0, kActGeluTanh = 1 };
+
+struct GemmEpilogue {
+  int kind;                 // EpiKind
+  int act;                  // ActKind (store only)
+  int out_bf16;             // store: 1 = bf16 output, 0 = fp32
+  int features_on_a;        // 1: A rows index output features (weights-as-A)
+  void* out;
+  long long out_sa;         // output element stride per A-row index
+  long long out_sb;         // output element stride per B-row index
+  long long split_stride;   // partial: element stride between split-K slices
+  const __nv_bfloat16* bias;   // bias[feature] (nullable)
+  // residual: out += (gate_w[f] + gate_t[off(token) + f]) * (acc + bias[f])
+  // with off(token) = batch * gate_bstride + (token in first frame ? 0 : gate_gstride)
+  const __nv_bfloat16* gate_w;
+  const float* gate_t;
+  int tokens_per_batch;
+  int first_frame_tokens;   // 0: a single gate row per batch
+  long long gate_bstride;
+  long long gate_gstride;
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int kb_per_split;
+  int a_is_const;           // operand constant for the launch chain (prefetched early)
+  int b_is_const;
+  int* status;
+  GemmEpilogue epi;
+};
+
+struct GemmPlan {
+  CUtensorMap ta;
+  CUtensorMap tb;
+  GemmArgs args;
+  int bn;
+  int splits;
+};
+
+int gemm_pick_bn(int n);
+int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M, int N,
+              int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,
+              int* status);
+cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl);
+
+}  // namespace fam

@@ -1,0 +1,356 @@
+// tcgen05 bf16 GEMM:  D[m][n] = sum_k A[m][k] * B[n][k]   (both operands K-major)
+//
+// One CTA computes one 128 x BN output tile over a contiguous range of the K
+// dimension (split-K when gridDim.z > 1).  Warp roles (192 threads):
+//   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle);
+//   warp 1      allocates TMEM and (lane 0) issues tcgen05.mma, 4 x K=16 per
+//               stage, accumulating in fp32 in TMEM; commits free stages;
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lane
+//               quarter w%4) and apply bias / GELU / gated residual / split-K
+//               partial stores.
+//
+// The same kernel serves both operand orientations used by the models:
+//   * small-M action GEMMs (8..256 tokens) run "weights as A": A = W[out,in]
+//     so the 128-row MMA dimension walks output features and the token count
+//     is the MMA N (16..256).  These are HBM-bound weight streams.
+//   * large-M backbone GEMMs (1760 x B tokens) run "activations as A".
+// The epilogue addresses the output through element strides for the A-row and
+// B-row index, so either orientation writes a row-major [tokens, features]
+// result.
+//
+// Programmatic dependent launch: the operand that is constant for the whole
+// launch chain (the weights) is prefetched for the first ring stages before
+// griddepcontrol.wait; the operand produced by the previous kernel is loaded
+// after it.  All global writes happen after the wait.
+#include "fam_common.cuh"
+#include "fam_internal.h"
+
+namespace fam {
+
+constexpr int kGemmThreads = 192;
+constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle atom)
+constexpr int kBM = 128;         // MMA M
+
+__host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
+__host__ __device__ constexpr int gemm_stages(int bn) {
+  // Small-N tiles keep the CTA under ~113 KB so that two launches of the chain
+  // can be resident on one SM (programmatic launch overlap); large-N tiles are
+  // compute bound and take a deeper ring.
+  return bn <= 64 ? (110 * 1024) / gemm_stage_bytes(bn) : (200 * 1024) / gemm_stage_bytes(bn);
+}
+__host__ __device__ constexpr int gemm_smem_bytes(int bn) {
+  return gemm_stages(bn) * gemm_stage_bytes(bn) + 1024 /*align slack*/ + 256 /*barriers*/;
+}
+__host__ __device__ constexpr uint32_t gemm_tmem_cols(int bn) {
+  return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
+}
+
+// Apply the epilogue to 16 accumulator values of A-row `a_row`, B-rows
+// b0..b0+15.
+__device__ __forceinline__ void gemm_epilogue_apply(const GemmArgs& args, const GemmEpilogue& e,
+                                                    int a_row, int b0, int split, float* v) {
+  if (e.kind == kEpiPartial) {
+    float* out = reinterpret_cast<float*>(e.out) + split * e.split_stride +
+                 static_cast<long long>(a_row) * e.out_sa;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (b0 + j < args.N) out[static_cast<long long>(b0 + j) * e.out_sb] = v[j];
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int b = b0 + j;
+    const int feat = e.features_on_a ? a_row : b;
+    float x = v[j];
+    if (e.bias != nullptr && b < args.N) x += bf2f(e.bias[feat]);
+    if (e.act == kActGeluTanh) x = gelu_tanh(x);
+    v[j] = x;
+  }
+  if (e.kind == kEpiStore) {
+    if (e.out_bf16) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out);
+      const bool vec = (e.out_sb == 1) && (b0 + 16 <= args.N) && ((e.out_sa & 7) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+      if (vec) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+          pk[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(a_row) * e.out_sa + b0);
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (b0 + j < args.N)
+            out[static_cast<long long>(a_row) * e.out_sa + static_cast<long long>(b0 + j) * e.out_sb] =
+                f2bf(v[j]);
+      }
+    } else {
+      float* out = reinterpret_cast<float*>(e.out);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (b0 + j < args.N)
+          out[static_cast<long long>(a_row) * e.out_sa + static_cast<long long>(b0 + j) * e.out_sb] = v[j];
+    }
+    return;
+  }
+  // kEpiResidual: out_f32 += gate * x
+  float* out = reinterpret_cast<float*>(e.out);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int b = b0 + j;
+    if (b >= args.N) continue;
+    const int feat = e.features_on_a ? a_row : b;
+    const int tok = e.features_on_a ? b : a_row;
+    float g = 1.0f;
+    if (e.gate_t != nullptr) {
+      const int bi = tok / e.tokens_per_batch;
+      const int within = tok - bi * e.tokens_per_batch;
+      const int grp = (e.first_frame_tokens > 0 && within >= e.first_frame_tokens) ? 1 : 0;
+      g = e.gate_t[bi * e.gate_bstride + grp * e.gate_gstride + feat];
+      if (e.gate_w != nullptr) g += bf2f(e.gate_w[feat]);
+    }
+    float* dst = out + static_cast<long long>(a_row) * e.out_sa + static_cast<long long>(b) * e.out_sb;
+    *dst = *dst + g * v[j];
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  constexpr int STAGES = gemm_stages(BN);
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_BYTES = BN * kBK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = gemm_tmem_cols(BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM;
+  const int n0 = blockIdx.y * BN;
+  const int split = blockIdx.z;
+  const int kb_total = (args.K + kBK - 1) / kBK;
+  const int kb_begin = split * args.kb_per_split;
+  const int kb_end = min(kb_total, kb_begin + args.kb_per_split);
+  const int nkb = kb_end - kb_begin;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // Every CTA of this launch is resident and owns its TMEM: let the next
+  // kernel of the chain start its prologue.
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0 && nkb > 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      const uint64_t polA = args.a_is_const ? pol_w : pol_x;
+      const uint64_t polB = args.b_is_const ? pol_w : pol_x;
+      const int pre = min(nkb, STAGES);
+      // Prologue: constant operand first (may run before the previous kernel ends).
+      for (int i = 0; i < pre; ++i) {
+        const int kc = (kb_begin + i) * kBK;
+        uint8_t* sa = smem + i * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
+        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], kc, m0, polA);
+        if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], kc, n0, polB);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const int kc = (kb_begin + i) * kBK;
+        uint8_t* sa = smem + i * STAGE_BYTES;
+        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], kc, m0, polA);
+        if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], kc, n0, polB);
+      }
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t use = static_cast<uint32_t>(i / STAGES);
+        if (*abort_flag) break;
+        if (!mbar_wait(&empty[s], (use - 1) & 1, args.status, kErrWaitEmpty)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int kc = (kb_begin + i) * kBK;
+        uint8_t* sa = smem + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        tma_load_2d(sa, &tmA, &full[s], kc, m0, polA);
+        tma_load_2d(sa + A_BYTES, &tmB, &full[s], kc, n0, polB);
+        issued = i + 1;
+      }
+      // Drain: every issued copy has landed before the CTA can exit (on the
+      // normal path these waits return at once).
+      for (int j = max(0, issued - STAGES); j < issued; ++j) {
+        mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1, args.status,
+                  kErrWaitFull);
+      }
+    } else if (lane == 0) {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        if (*abort_flag) break;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(i / STAGES) & 1, args.status,
+                       kErrWaitFull)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = umma_desc_sw128(smem + s * STAGE_BYTES);
+        const uint64_t db = umma_desc_sw128(smem + s * STAGE_BYTES + A_BYTES);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          // +32 bytes along K inside the swizzle atom = +2 in the 16-byte-unit address field
+          umma_bf16_ss(tmem_base, da + 2 * k, db + 2 * k, idesc, (i | k) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int sp = warp & 3;  // TMEM lane quarter accessible to this warp
+    const int a_row = m0 + sp * 32 + lane;
+    pdl_wait();
+    const bool ok = mbar_wait(accum, 0, args.status, kErrWaitAccum);
+    tc_fence_after();
+    if (!ok) *abort_flag = 1;
+    const GemmEpilogue& e = args.epi;
+    if (ok && !*abort_flag && nkb > 0) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        __syncwarp();
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + c, v);
+        if (a_row < args.M) gemm_epilogue_apply(args, e, a_row, n0 + c, split, v);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+template <int BN>
+static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                                  int splits, cudaStream_t stream, bool pdl) {
+  static bool attr_set = false;
+  constexpr int smem = gemm_smem_bytes(BN);
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.M + kBM - 1) / kBM, (a.N + BN - 1) / BN, splits);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BN>, ta, tb, a);
+}
+
+int gemm_pick_bn(int n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
+  switch (p.bn) {
+    case 16: return launch_gemm_bn<16>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 32: return launch_gemm_bn<32>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 64: return launch_gemm_bn<64>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 128: return launch_gemm_bn<128>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 256: return launch_gemm_bn<256>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// Build a launch plan.  A is [M, K] with row stride lda (elements), B is [N, K]
+// with row stride ldb.  `splits` > 1 requires the partial epilogue.
+int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M,
+              int N, int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const,
+              bool b_is_const, int* status) {
+  if (M <= 0 || N <= 0 || K <= 0) return set_error("gemm: empty problem");
+  if ((K % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0)
+    return set_error("gemm: K and row strides must be multiples of 8 elements (16 bytes)");
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return set_error("gemm: operand base addresses must be 16-byte aligned");
+  if (bn == 0) bn = gemm_pick_bn(N);
+  const int kb_total = (K + kBK - 1) / kBK;
+  if (splits < 1) splits = 1;
+  if (splits > kb_total) splits = kb_total;
+  const int kps = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kps - 1) / kps;  // no empty split
+  if (splits > 1 && epi.kind != kEpiPartial)
+    return set_error("gemm: split-K requires the partial epilogue");
+  if (epi.kind == kEpiResidual && epi.gate_t != nullptr && epi.tokens_per_batch <= 0)
+    return set_error("gemm: residual gate needs tokens_per_batch > 0");
+  if (!make_tmap_bf16_2d(&p->ta, A, static_cast<uint64_t>(M), static_cast<uint64_t>(K),
+                         static_cast<uint64_t>(lda), kBM))
+    return set_error("gemm: cuTensorMapEncodeTiled failed for A");
+  if (!make_tmap_bf16_2d(&p->tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                         static_cast<uint64_t>(ldb), static_cast<uint32_t>(bn)))
+    return set_error("gemm: cuTensorMapEncodeTiled failed for B");
+  p->bn = bn;
+  p->splits = splits;
+  p->args.M = M;
+  p->args.N = N;
+  p->args.K = K;
+  p->args.kb_per_split = kps;
+  p->args.a_is_const = a_is_const ? 1 : 0;
+  p->args.b_is_const = b_is_const ? 1 : 0;
+  p->args.status = status;
+  p->args.epi = epi;
+  return 0;
+}
+
+}  // namespace fam

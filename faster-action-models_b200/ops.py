@@ -1,0 +1,92 @@
+"""Op-level wrappers over the C ABI, taking torch CUDA tensors.
+
+torch is used only for device memory and the current stream; all arithmetic
+runs in libfam.so kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import GemmDesc, check, lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+         bias: Optional[torch.Tensor] = None, act: str = "none", out_dtype=torch.bfloat16,
+         weights_as_a: bool = False, splits: int = 1, tile_n: int = 0,
+         residual: Optional[torch.Tensor] = None, gate_w: Optional[torch.Tensor] = None,
+         gate_t: Optional[torch.Tensor] = None, tokens_per_batch: int = 0,
+         first_frame_tokens: int = 0, gate_batch_stride: int = 0, gate_group_stride: int = 0,
+         pdl: bool = False) -> torch.Tensor:
+    """Linear layer on the tensor cores.
+
+    weights_as_a=False:  a = activations [T, K], b = weight [F, K] -> [T, F]
+    weights_as_a=True:   a = weight [F, K], b = activations [T, K] -> [T, F]
+    splits > 1 returns fp32 split-K partials [splits, T, F] (no bias).
+    residual (fp32 [T, F]) is updated in place: residual += gate * (x W^T + bias).
+    """
+    _require(a, torch.bfloat16, "a")
+    _require(b, torch.bfloat16, "b")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f"gemm shapes {tuple(a.shape)} x {tuple(b.shape)}")
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("gemm operands must be K-contiguous")
+    M, K = a.shape
+    N = b.shape[0]
+    T, F = (N, M) if weights_as_a else (M, N)
+    d = GemmDesc()
+    d.a, d.lda, d.b, d.ldb = a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0)
+    d.m, d.n, d.k = M, N, K
+    d.splits, d.tile_n = splits, tile_n
+    d.activation = _lib.FAM_ACT_GELU_TANH if act == "gelu_tanh" else _lib.FAM_ACT_NONE
+    d.features_on_a = 1 if weights_as_a else 0
+    d.a_is_const = 1 if weights_as_a else 0
+    d.b_is_const = 0 if weights_as_a else 1
+    d.pdl = 1 if pdl else 0
+    d.bias = _ptr(bias)
+    if residual is not None:
+        _require(residual, torch.float32, "residual")
+        out = residual
+        d.epilogue = _lib.FAM_EPI_RESIDUAL
+        d.out_dtype = _lib.FAM_DTYPE_F32
+        d.gate_w, d.gate_t = _ptr(gate_w), _ptr(gate_t)
+        d.tokens_per_batch = tokens_per_batch if tokens_per_batch > 0 else T
+        d.first_frame_tokens = first_frame_tokens
+        d.gate_batch_stride, d.gate_group_stride = gate_batch_stride, gate_group_stride
+    elif splits > 1:
+        d.epilogue = _lib.FAM_EPI_PARTIAL
+        d.out_dtype = _lib.FAM_DTYPE_F32
+        if out is None:
+            out = torch.empty((splits, T, F), device=a.device, dtype=torch.float32)
+        d.out_stride_split = T * F
+    else:
+        d.epilogue = _lib.FAM_EPI_STORE
+        d.out_dtype = _lib.FAM_DTYPE_BF16 if out_dtype == torch.bfloat16 else _lib.FAM_DTYPE_F32
+        if out is None:
+            out = torch.empty((T, F), device=a.device, dtype=out_dtype)
+    ld = out.stride(-2)
+    if weights_as_a:
+        d.out_stride_a, d.out_stride_b = 1, ld
+    else:
+        d.out_stride_a, d.out_stride_b = ld, 1
+    d.out = out.data_ptr()
+    check(lib().fam_gemm(C.byref(d), C.c_void_p(_stream())), "fam_gemm")
+    return out

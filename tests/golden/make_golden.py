@@ -1,0 +1,237 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run in a container that has the reference checkout (read-only is fine):
+
+    python tests/golden/make_golden.py --reference /path/to/faster-action-models
+
+It imports the reference's own FastWAM modules (FastWAM/src/fastwam/...),
+builds small seeded random-init models with the reference constructors, runs
+the reference code paths of the hot path on the CPU and saves
+{config, state dicts, inputs, outputs} as ``*.pt`` files beside this script.
+The reference cannot travel to the GPU machines, so these fixtures are the
+reference's voice in the test suite there.
+
+Reference code paths exercised:
+  c0  ActionDiT.forward Euler loop + ActionAE.decode          (fp32)
+        FastWAM/src/fastwam/models/wan22/action_dit.py:333-362
+        FastWAM/src/fastwam/models/action_ae.py:154-187
+  c1  FastWAM._denoise_action_with_video_cache + scheduler     (bf16)
+        FastWAM/src/fastwam/models/wan22/fastwam.py:771-804, 1241-1263
+        FastWAM/src/fastwam/models/wan22/mot.py:528-578
+  c2  WanVideoDiT.prepare + MoT.prefill_video_cache_tensor     (bf16)
+        FastWAM/src/fastwam/models/wan22/wan_video_dit.py:640-720
+        FastWAM/src/fastwam/models/wan22/mot.py:474-526
+      plus the final hidden state through DiTBlock.forward (wan_video_dit.py:248-267)
+  sched / masks / rope / sinusoid: scheduler_continuous.py:63-88, fastwam.py:429-451,
+        wan_video_dit.py:30-60, 489-523
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+import types
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def _import_reference(ref_root: Path):
+    src = ref_root / "FastWAM" / "src"
+    if not src.exists():
+        raise SystemExit(f"reference sources not found under {src}")
+    # fastwam.utils imports imageio for video I/O, which this path never uses.
+    for name in ("imageio", "imageio.v3"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.path.insert(0, str(src))
+    from fastwam.models.wan22.action_dit import ActionDiT
+    from fastwam.models.wan22.wan_video_dit import (WanVideoDiT, sinusoidal_embedding_1d,
+                                                    precompute_freqs_cis, precompute_freqs_cis_3d,
+                                                    rope_apply)
+    from fastwam.models.wan22.mot import MoT
+    from fastwam.models.wan22.fastwam import FastWAM
+    from fastwam.models.wan22.schedulers.scheduler_continuous import \
+        WanContinuousFlowMatchScheduler
+    from fastwam.models.action_ae import ActionAE, ActionAEConfig
+    return SimpleNamespace(**locals())
+
+
+def _round_params_bf16(module):
+    """Round every parameter to bf16-representable values (keeps fixtures small
+    and lets an fp32 model and a bf16 kernel see identical weights)."""
+    with torch.no_grad():
+        for p in module.parameters():
+            p.copy_(p.to(torch.bfloat16).to(p.dtype))
+
+
+def _sd(module, dtype):
+    return {k: v.detach().to(dtype).clone() for k, v in module.state_dict().items()}
+
+
+def make_c0(R):
+    """Standalone CAE-style expert + Action-VAE decoder, fp32 (config 0 shape family)."""
+    torch.manual_seed(0)
+    cfg = dict(hidden_dim=32, action_dim=16, ffn_dim=128, text_dim=96, freq_dim=256, eps=1e-6,
+               num_heads=4, attn_head_dim=8, num_layers=3)
+    dit = R.ActionDiT(**cfg).eval()
+    ae_cfg = R.ActionAEConfig(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16,
+                              decoder_hidden=32, video_cond_dim=0, variational=True)
+    ae = R.ActionAE(ae_cfg).eval()
+    _round_params_bf16(dit)
+    _round_params_bf16(ae)
+    g = torch.Generator().manual_seed(0)
+    ctx = torch.randn(1, 24, 96, generator=g).bfloat16().float()
+    noise = torch.randn(1, 8, 16, generator=g)
+    sched = R.WanContinuousFlowMatchScheduler(shift=5.0)
+    ts, ds = sched.build_inference_schedule(4, device="cpu", dtype=torch.float32, shift_override=1.0)
+    x = noise.clone()
+    vs = []
+    with torch.no_grad():
+        for t, d in zip(ts, ds):
+            v = dit(x, t.unsqueeze(0), ctx)
+            vs.append(v.clone())
+            x = sched.step(v, d, x)
+        chunk = ae.decode(x)
+    return {
+        "kind": "c0", "dit_cfg": cfg, "dec_cfg": dict(action_dim=7, action_horizon=32, num_tokens=8,
+                                                      latent_dim=16, decoder_hidden=32),
+        "num_steps": 4, "shift": 1.0,
+        "dit": _sd(dit, torch.bfloat16), "ae": _sd(ae, torch.bfloat16),
+        "context": ctx.bfloat16(), "noise": noise,
+        "timesteps": ts, "deltas": ds, "velocities": torch.stack(vs), "latent": x, "chunk": chunk,
+    }
+
+
+def make_c1(R):
+    """Action expert over a video K/V cache, bf16 (config 1 shape family)."""
+    torch.manual_seed(1)
+    cfg = dict(hidden_dim=64, action_dim=7, ffn_dim=256, text_dim=96, freq_dim=256, eps=1e-6,
+               num_heads=4, attn_head_dim=16, num_layers=2)
+    dit = R.ActionDiT(**cfg).to(torch.bfloat16).eval()
+    Sv, tpf, Sa, C = 40, 10, 8, 12
+    g = torch.Generator().manual_seed(1)
+    ctx = torch.randn(1, C, 96, generator=g).bfloat16()
+    ctx_mask = torch.ones(1, C, dtype=torch.bool)
+    ctx_mask[0, C - 3:] = False
+    cache_k = [torch.randn(1, Sv, 64, generator=g).bfloat16() for _ in range(2)]
+    cache_v = [torch.randn(1, Sv, 64, generator=g).bfloat16() for _ in range(2)]
+    noise = torch.randn(1, Sa, 7, generator=g).bfloat16()
+    # FastWAM._build_mot_attention_mask, called unbound with only what it reads.
+    host = SimpleNamespace(video_expert=SimpleNamespace(
+        build_video_to_video_mask=lambda video_seq_len, video_tokens_per_frame, device:
+        R.WanVideoDiT.build_video_to_video_mask(
+            SimpleNamespace(video_attention_mask_mode="first_frame_causal"), video_seq_len,
+            video_tokens_per_frame, device)))
+    mask = R.FastWAM._build_mot_attention_mask(host, Sv, Sa, tpf, torch.device("cpu"))
+    action_mask = mask[Sv:, :]
+    # MoT needs a video expert with the same layer count / heads / head dim.
+    video = R.WanVideoDiT(hidden_dim=32, in_dim=16, ffn_dim=64, out_dim=16, text_dim=96,
+                          freq_dim=256, eps=1e-6, patch_size=(1, 2, 2), num_heads=4,
+                          attn_head_dim=16, num_layers=2, has_image_input=False,
+                          seperated_timestep=True).to(torch.bfloat16)
+    mot = R.MoT({"video": video, "action": dit}).eval()
+    mot_host = SimpleNamespace(action_expert=dit, mot=mot)
+    sched = R.WanContinuousFlowMatchScheduler(shift=5.0)
+    ts, ds = sched.build_inference_schedule(3, device="cpu", dtype=torch.bfloat16)
+    x = noise.clone()
+    vs = []
+    with torch.no_grad():
+        for t, d in zip(ts, ds):
+            v = R.FastWAM._denoise_action_with_video_cache(
+                mot_host, latents_action=x, timestep_action=t.unsqueeze(0).to(torch.bfloat16),
+                context=ctx, context_mask=ctx_mask, video_cache_k=cache_k, video_cache_v=cache_v,
+                action_attention_mask=action_mask)
+            vs.append(v.clone())
+            x = sched.step(v, d, x)
+    return {
+        "kind": "c1", "dit_cfg": cfg, "num_steps": 3, "shift": 5.0, "tokens_per_frame": tpf,
+        "dit": _sd(dit, torch.bfloat16), "context": ctx, "context_mask": ctx_mask,
+        "cache_k": torch.stack(cache_k), "cache_v": torch.stack(cache_v), "noise": noise,
+        "action_mask": action_mask, "timesteps": ts, "deltas": ds,
+        "velocities": torch.stack(vs), "latent": x,
+    }
+
+
+def make_c2(R):
+    """Video DiT prefill producing the per-layer K/V cache, bf16 (config 2 shape family)."""
+    torch.manual_seed(2)
+    # head_dim 24 splits into even (8, 8, 8) RoPE parts, as 128 -> (44, 42, 42) does.
+    vcfg = dict(hidden_dim=96, in_dim=16, ffn_dim=128, out_dim=16, text_dim=96, freq_dim=256,
+                eps=1e-6, patch_size=(1, 2, 2), num_heads=4, attn_head_dim=24, num_layers=2,
+                has_image_input=False, seperated_timestep=True,
+                video_attention_mask_mode="first_frame_causal")
+    video = R.WanVideoDiT(**vcfg).to(torch.bfloat16).eval()
+    action = R.ActionDiT(hidden_dim=32, action_dim=7, ffn_dim=64, text_dim=96, freq_dim=256,
+                         eps=1e-6, num_heads=4, attn_head_dim=24, num_layers=2).to(torch.bfloat16)
+    mot = R.MoT({"video": video, "action": action}).eval()
+    g = torch.Generator().manual_seed(2)
+    latents = torch.randn(1, 16, 3, 4, 6, generator=g).bfloat16()
+    C = 12
+    ctx = torch.randn(1, C, 96, generator=g).bfloat16()
+    ctx_mask = torch.ones(1, C, dtype=torch.bool)
+    ctx_mask[0, -2:] = False
+    timestep = torch.tensor([500.0]).bfloat16()
+    with torch.no_grad():
+        (tokens, t, t_mod, vctx, vctx_mask, freqs, f, h, w, tpf) = video.prepare(
+            x=latents, timestep=timestep, context=ctx, context_mask=ctx_mask, action=None,
+            fuse_vae_embedding_in_latents=True)
+        vmask = video.build_video_to_video_mask(tokens.shape[1], tpf, torch.device("cpu"))
+        ks, vs = mot.prefill_video_cache_tensor(
+            video_tokens=tokens, video_freqs=freqs, video_t_mod=t_mod, video_context=vctx,
+            video_context_mask=vctx_mask, video_attention_mask=vmask)
+        x = tokens
+        for blk in video.blocks:
+            x = blk(x, vctx, t_mod, freqs, context_mask=vctx_mask, self_attn_mask=vmask)
+    cfg = {k: vcfg[k] for k in ("hidden_dim", "in_dim", "ffn_dim", "out_dim", "text_dim",
+                                "freq_dim", "eps", "num_heads", "attn_head_dim", "num_layers")}
+    cfg["patch_size"] = list(vcfg["patch_size"])
+    return {
+        "kind": "c2", "dit_cfg": cfg, "video": _sd(video, torch.bfloat16), "latents": latents,
+        "context": ctx, "context_mask": ctx_mask, "timestep": timestep, "tokens": tokens,
+        "t_mod": t_mod, "context_emb": vctx, "freqs": freqs, "grid": (f, h, w),
+        "tokens_per_frame": tpf, "video_mask": vmask, "cache_k": torch.stack(ks),
+        "cache_v": torch.stack(vs), "hidden": x,
+    }
+
+
+def make_primitives(R):
+    """Known-answer vectors for the small numeric building blocks."""
+    g = torch.Generator().manual_seed(3)
+    pos = torch.tensor([0.0, 1.0, 250.0, 500.0, 936.0, 1000.0])
+    x = torch.randn(2, 5, 4 * 16, generator=g).bfloat16()
+    freqs1 = R.precompute_freqs_cis(16, end=1024)[:5].view(5, 1, -1)
+    f3 = R.precompute_freqs_cis_3d(128)
+    sched = R.WanContinuousFlowMatchScheduler(shift=5.0)
+    out = {"kind": "primitives"}
+    for n, s in ((10, 1.0), (10, 5.0), (4, 1.0), (4, 5.0)):
+        for dt in (torch.float32, torch.bfloat16):
+            t, d = sched.build_inference_schedule(n, device="cpu", dtype=dt, shift_override=s)
+            out[f"sched_{n}_{s}_{str(dt).split('.')[-1]}"] = (t, d)
+    out.update({
+        "sin_pos": pos, "sin_f32": R.sinusoidal_embedding_1d(256, pos),
+        "sin_bf16": R.sinusoidal_embedding_1d(256, pos.bfloat16()),
+        "rope_x": x, "rope_out": R.rope_apply(x, freqs1, 4),
+        "freqs3_shapes": [tuple(t.shape) for t in f3],
+        "freqs3_row7": torch.cat([t[7] for t in f3]),
+    })
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    R = _import_reference(Path(args.reference))
+    torch.set_num_threads(4)
+    for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
+                     ("c2_video_prefill", make_c2), ("primitives", make_primitives)):
+        fx = fn(R)
+        path = OUT / f"{name}.pt"
+        torch.save(fx, path)
+        print(f"{path.name}: {path.stat().st_size / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()

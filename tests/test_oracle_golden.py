@@ -1,0 +1,111 @@
+"""Pins the CPU oracle to the reference: every committed golden fixture was
+produced by running the reference's own modules (tests/golden/make_golden.py);
+the oracle, given the same state dicts and inputs, must reproduce them."""
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import fam_oracle as O
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _load(name):
+    return torch.load(GOLDEN / f"{name}.pt", weights_only=False)
+
+
+def _f32(sd):
+    return {k: v.float() for k, v in sd.items()}
+
+
+def _same(got, ref, atol=0.0):
+    got, ref = got.float(), ref.float()
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    err = (got - ref).abs().max().item()
+    assert err <= atol, f"max |d| = {err}"
+
+
+def test_primitives_match_reference():
+    fx = _load("primitives")
+    _same(O.sinusoidal_embedding_1d(256, fx["sin_pos"]), fx["sin_f32"])
+    _same(O.sinusoidal_embedding_1d(256, fx["sin_pos"].bfloat16()), fx["sin_bf16"])
+    freqs = O.precompute_freqs_cis(16, end=1024)[:5].view(5, 1, -1)
+    _same(O.rope_apply(fx["rope_x"], freqs, 4), fx["rope_out"])
+    f3 = O.precompute_freqs_cis_3d(128)
+    assert [tuple(t.shape) for t in f3] == fx["freqs3_shapes"]
+    assert torch.equal(torch.cat([t[7] for t in f3]), fx["freqs3_row7"])
+    for key, (t_ref, d_ref) in ((k, v) for k, v in fx.items() if k.startswith("sched_")):
+        _, n, s, dt = key.split("_")
+        t, d = O.build_inference_schedule(int(n), float(s), dtype=getattr(torch, {"float32": "float32", "bfloat16": "bfloat16"}[dt]))
+        assert torch.equal(t, t_ref) and torch.equal(d, d_ref), key
+
+
+def test_schedule_known_answers():
+    # shift 1, 4 steps: t = 1000, 750, 500, 250 and delta = -0.25
+    t, d = O.build_inference_schedule(4, 1.0)
+    assert t.tolist() == [1000.0, 750.0, 500.0, 250.0]
+    assert torch.allclose(d, torch.full((4,), -0.25))
+    # bf16 rounding of the shifted schedule: 937.5 -> 936
+    t5, _ = O.build_inference_schedule(4, 5.0, dtype=torch.bfloat16)
+    assert t5[1].item() == 936.0
+
+
+def test_c0_cae_chunk_matches_reference():
+    fx = _load("c0_cae_expert")
+    cfg = O.DiTConfig(**{k: fx["dit_cfg"][k] for k in ("hidden_dim", "ffn_dim", "num_heads",
+                                                       "attn_head_dim", "num_layers", "text_dim",
+                                                       "freq_dim", "eps", "action_dim")})
+    dcfg = O.DecoderConfig(**fx["dec_cfg"])
+    chunk, latent, vs = O.cae_chunk(_f32(fx["dit"]), cfg, _f32(fx["ae"]), dcfg, fx["noise"],
+                                    fx["context"].float(), num_steps=4, shift=1.0,
+                                    return_trace=True)
+    _same(torch.stack(vs), fx["velocities"], 1e-5)
+    _same(latent, fx["latent"], 1e-5)
+    _same(chunk, fx["chunk"], 1e-5)
+
+
+def test_c1_action_cache_matches_reference():
+    fx = _load("c1_action_cache")
+    c = fx["dit_cfg"]
+    cfg = O.DiTConfig(**{k: c[k] for k in ("hidden_dim", "ffn_dim", "num_heads", "attn_head_dim",
+                                           "num_layers", "text_dim", "freq_dim", "eps",
+                                           "action_dim")})
+    x, vs = O.action_chunk_with_cache(fx["dit"], cfg, fx["noise"], fx["context"],
+                                      fx["context_mask"], list(fx["cache_k"]), list(fx["cache_v"]),
+                                      fx["action_mask"], fx["num_steps"], fx["shift"],
+                                      return_trace=True)
+    _same(torch.stack(vs), fx["velocities"])
+    _same(x, fx["latent"])
+
+
+def test_c1_mask_matches_reference():
+    fx = _load("c1_action_cache")
+    Sv = fx["cache_k"].shape[2]
+    Sa = fx["noise"].shape[1]
+    m = O.build_mot_attention_mask(Sv, Sa, fx["tokens_per_frame"])
+    assert torch.equal(m[Sv:, :], fx["action_mask"])
+
+
+def test_c2_video_prefill_matches_reference():
+    fx = _load("c2_video_prefill")
+    c = fx["dit_cfg"]
+    cfg = O.DiTConfig(hidden_dim=c["hidden_dim"], ffn_dim=c["ffn_dim"], num_heads=c["num_heads"],
+                      attn_head_dim=c["attn_head_dim"], num_layers=c["num_layers"],
+                      text_dim=c["text_dim"], freq_dim=c["freq_dim"], eps=c["eps"],
+                      in_dim=c["in_dim"], out_dim=c["out_dim"], patch_size=tuple(c["patch_size"]))
+    p = fx["video"]
+    tokens, t, t_mod, ctx, ctx_mask, freqs, grid, tpf = O.video_prepare(
+        p, cfg, fx["latents"], fx["timestep"], fx["context"], fx["context_mask"])
+    _same(tokens, fx["tokens"])
+    _same(t_mod, fx["t_mod"])
+    _same(ctx, fx["context_emb"])
+    assert torch.equal(freqs, fx["freqs"])
+    assert grid == tuple(fx["grid"]) and tpf == fx["tokens_per_frame"]
+    vmask = O.build_video_to_video_mask(tokens.shape[1], tpf)
+    assert torch.equal(vmask, fx["video_mask"])
+    ks, vs, hidden = O.prefill_video_cache(p, cfg, tokens, freqs, t_mod, ctx, ctx_mask, vmask,
+                                           return_hidden=True)
+    _same(torch.stack(ks), fx["cache_k"])
+    _same(torch.stack(vs), fx["cache_v"])
+    _same(hidden, fx["hidden"])
