@@ -1,0 +1,587 @@
+// Host runtime of the action expert: owns the weight tensor maps, lays out the
+// caller's workspace, enqueues one action chunk (or one model evaluation) as a
+// chain of programmatic-dependent launches, and captures that chain into a
+// CUDA graph that is replayed while the call's pointers and sizes repeat.
+//
+// Launch chain of one Euler step (per block l of L):
+//   gemm qkv (split-K) -> qkv_post -> joint attention (video cache ++ action)
+//   -> gemm o (split-K) -> resid_norm(gate_msa, norm3) -> gemm cross-q ->
+//   rms_rows -> cross attention -> gemm cross-o -> resid_norm(AdaLN mlp)
+//   -> gemm ffn.0 (+GELU) -> gemm ffn.2 (split-K) -> resid_norm(gate_mlp, next AdaLN)
+// then head + Euler update.  Step-invariant work is hoisted to the chunk
+// prologue: the time MLP of every step's timestep, the text embedding and
+// every block's cross-attention K/V (RMSNorm'd K) of the context.
+#include <string.h>
+
+#include <cmath>
+#include <memory>
+#include <vector>
+
+#include "../../include/fam.h"
+#include "fam_internal.h"
+#include "fam_kernels.h"
+
+using namespace fam;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
+
+// Split-K so that tiles x splits fills ~one wave of 148 SMs, at least two
+// 64-wide K blocks per split.
+int choose_splits(int n_out, int k, int rows) {
+  const int bn = gemm_pick_bn(rows);
+  const int tiles = ((n_out + 127) / 128) * ((rows + bn - 1) / bn);
+  const int kb = (k + 63) / 64;
+  int s = 148 / tiles;
+  if (s < 1) s = 1;
+  if (s > kb / 2) s = kb / 2 > 0 ? kb / 2 : 1;
+  const int kps = (kb + s - 1) / s;
+  return (kb + kps - 1) / kps;
+}
+
+struct WsLayout {
+  size_t x, h, part, q, ka, va, ao, qc, ci, fh, apart, ctr, tmod, sin, th1, th2, cemb, ch1, ckv, vel;
+  size_t total;
+  int s_qkv, s_o, s_cq, s_co, s_f2;
+};
+
+WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
+  WsLayout w = {};
+  const size_t rows = static_cast<size_t>(B) * Sa, crow = static_cast<size_t>(B) * C;
+  const int D = c.hidden_dim, HD = c.num_heads * c.head_dim, F = c.ffn_dim;
+  w.s_qkv = choose_splits(3 * HD, D, static_cast<int>(rows));
+  w.s_o = choose_splits(D, HD, static_cast<int>(rows));
+  w.s_cq = choose_splits(HD, D, static_cast<int>(rows));
+  w.s_co = choose_splits(D, HD, static_cast<int>(rows));
+  w.s_f2 = choose_splits(D, F, static_cast<int>(rows));
+  size_t part_elems = 0;
+  auto upd = [&](size_t e) { part_elems = e > part_elems ? e : part_elems; };
+  upd(static_cast<size_t>(w.s_qkv) * rows * 3 * HD);
+  upd(static_cast<size_t>(w.s_o) * rows * D);
+  upd(static_cast<size_t>(w.s_cq) * rows * HD);
+  upd(static_cast<size_t>(w.s_co) * rows * D);
+  upd(static_cast<size_t>(w.s_f2) * rows * D);
+  const int nsplit_joint = 8;  // upper bound used for the partial buffer
+  size_t apart = attn_partial_bytes(B, c.num_heads, Sa, c.head_dim, 64);
+  (void)nsplit_joint;
+  const int q_tiles = (Sa + 63) / 64;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  };
+  w.x = take(rows * D * 4);
+  w.h = take(rows * (D > HD ? D : HD) * 2);
+  w.part = take(part_elems * 4);
+  w.q = take(rows * HD * 2);
+  w.ka = take(rows * HD * 2);
+  w.va = take(rows * HD * 2);
+  w.ao = take(rows * HD * 2);
+  w.qc = take(rows * HD * 2);
+  w.ci = take(rows * HD * 2);
+  w.fh = take(rows * F * 2);
+  w.apart = take(apart);
+  w.ctr = take(static_cast<size_t>(B) * c.num_heads * q_tiles * 4);
+  w.tmod = take(static_cast<size_t>(N) * 6 * D * 4);
+  w.sin = take(static_cast<size_t>(N) * c.freq_dim * 2);
+  w.th1 = take(static_cast<size_t>(N) * D * 2);
+  w.th2 = take(static_cast<size_t>(N) * D * 2);
+  w.cemb = take(crow * D * 2);
+  w.ch1 = take(crow * D * 2);
+  w.ckv = take(static_cast<size_t>(c.num_layers) * crow * 2 * HD * 2);
+  w.vel = take(rows * c.action_dim * 2);
+  w.total = off;
+  return w;
+}
+
+// Everything that identifies a captured launch sequence.
+struct CallKey {
+  std::vector<uintptr_t> ptrs;
+  std::vector<float> vals;
+  bool operator==(const CallKey& o) const { return ptrs == o.ptrs && vals == o.vals; }
+};
+
+}  // namespace
+
+struct fam_action_expert {
+  fam_action_config cfg;
+  fam_action_weights w;
+  std::vector<fam_action_layer> layers;
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  CallKey graph_key;
+  int* status = nullptr;
+};
+
+namespace {
+
+struct Ctx {
+  fam_action_expert* e;
+  const fam_action_io* io;
+  char* ws;
+  WsLayout L;
+  int rows, crow;
+  cudaStream_t st;
+  bool pdl;
+};
+
+template <typename T>
+T* wsp(const Ctx& c, size_t off) {
+  return reinterpret_cast<T*>(c.ws + off);
+}
+
+#define FAM_TRY(expr)                                  \
+  do {                                                 \
+    cudaError_t _e = (expr);                           \
+    if (_e != cudaSuccess) return check_cuda(_e, #expr); \
+  } while (0)
+#define FAM_TRYI(expr)  \
+  do {                  \
+    int _r = (expr);    \
+    if (_r) return _r;  \
+  } while (0)
+
+// out = act(A-weights x B-activations + bias) or split partials.
+int gemm_w(const Ctx& c, const void* W, const void* bias, int n_out, int k, const void* act,
+           long long act_ld, int rows, int splits, int act_kind, void* out, long long out_ld,
+           bool out_f32) {
+  GemmEpilogue e = {};
+  e.features_on_a = 1;
+  e.act = act_kind;
+  e.out = out;
+  e.out_sa = 1;
+  e.out_sb = out_ld;
+  if (splits > 1) {
+    e.kind = kEpiPartial;
+    e.split_stride = static_cast<long long>(rows) * out_ld;
+  } else {
+    e.kind = kEpiStore;
+    e.out_bf16 = out_f32 ? 0 : 1;
+    e.bias = bf(bias);
+  }
+  GemmPlan p;
+  FAM_TRYI(gemm_plan(&p, W, k, act, act_ld, n_out, rows, k, splits, 0, e, true, false, c.e->status));
+  FAM_TRY(gemm_launch(p, c.st, c.pdl));
+  return 0;
+}
+
+ModRows step_mod(const Ctx& c, int step, const void* mod_w, int tokens_per_batch) {
+  ModRows m = {};
+  m.tmod = wsp<float>(c, c.L.tmod) + static_cast<size_t>(step) * 6 * c.e->cfg.hidden_dim;
+  m.mod_w = bf(mod_w);
+  m.tokens_per_batch = tokens_per_batch;
+  m.first_frame_tokens = 0;
+  m.bstride = 0;
+  m.gstride = 0;
+  return m;
+}
+
+// Time MLP of every step + text embedding + per-block cross K/V.
+int enqueue_prologue(const Ctx& c, const float* timesteps, int N) {
+  const fam_action_config& g = c.e->cfg;
+  const fam_action_weights& w = c.e->w;
+  const int D = g.hidden_dim, HD = g.num_heads * g.head_dim;
+  StepTimes st = {};
+  for (int i = 0; i < N; ++i) st.t[i] = timesteps[i];
+  // First launch of the chain follows a memset node: plain stream order.
+  FAM_TRY(launch_sinusoid(st, N, g.freq_dim, wsp<__nv_bfloat16>(c, c.L.sin), c.st, false));
+  // time_embedding: Linear -> SiLU -> Linear ; time_projection: SiLU -> Linear
+  FAM_TRYI(gemm_w(c, w.time0_w, w.time0_b, D, g.freq_dim, wsp<void>(c, c.L.sin), g.freq_dim, N, 1,
+                  kActSilu, wsp<void>(c, c.L.th1), D, false));
+  FAM_TRYI(gemm_w(c, w.time2_w, w.time2_b, D, D, wsp<void>(c, c.L.th1), D, N, 1, kActSilu,
+                  wsp<void>(c, c.L.th2), D, false));
+  FAM_TRYI(gemm_w(c, w.tproj_w, w.tproj_b, 6 * D, D, wsp<void>(c, c.L.th2), D, N, 1, kActNone,
+                  wsp<void>(c, c.L.tmod), 6 * D, true));
+  if (c.crow > 0) {
+    // text_embedding: Linear -> GELU(tanh) -> Linear
+    FAM_TRYI(gemm_w(c, w.text0_w, w.text0_b, D, g.text_dim, c.io->context, g.text_dim, c.crow, 1,
+                    kActGeluTanh, wsp<void>(c, c.L.ch1), D, false));
+    FAM_TRYI(gemm_w(c, w.text2_w, w.text2_b, D, D, wsp<void>(c, c.L.ch1), D, c.crow, 1, kActNone,
+                    wsp<void>(c, c.L.cemb), D, false));
+    for (int l = 0; l < g.num_layers; ++l) {
+      const fam_action_layer& ly = c.e->layers[l];
+      __nv_bfloat16* ckv = wsp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.crow * 2 * HD;
+      FAM_TRYI(gemm_w(c, ly.ckv_w, ly.ckv_b, 2 * HD, D, wsp<void>(c, c.L.cemb), D, c.crow, 1,
+                      kActNone, ckv, 2 * HD, false));
+      RmsRowsArgs r = {};
+      r.nsplit = 0;
+      r.in = ckv;
+      r.in_stride = 2 * HD;
+      r.w = bf(ly.cnorm_k);
+      r.out = ckv;
+      r.out_stride = 2 * HD;
+      r.N = HD;
+      r.eps = g.eps;
+      FAM_TRY(launch_rms_rows(r, c.crow, c.st, c.pdl));
+    }
+  }
+  return 0;
+}
+
+// One model evaluation at step index `step`; velocity -> vel; Euler when apply.
+int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float delta, bool apply) {
+  const fam_action_config& g = c.e->cfg;
+  const fam_action_weights& w = c.e->w;
+  const fam_action_io& io = *c.io;
+  const int D = g.hidden_dim, HD = g.num_heads * g.head_dim, F = g.ffn_dim, Lyr = g.num_layers;
+  const int rows = c.rows, Sa = io.action_tokens;
+  float* x = wsp<float>(c, c.L.x);
+  __nv_bfloat16* h = wsp<__nv_bfloat16>(c, c.L.h);
+  float* part = wsp<float>(c, c.L.part);
+
+  EncodeArgs ea = {};
+  ea.latent = bf(latent);
+  ea.enc_w = bf(w.enc_w);
+  ea.enc_b = bf(w.enc_b);
+  ea.x = x;
+  ea.h = h;
+  ea.mod = step_mod(c, step, c.e->layers[0].modulation, Sa);
+  ea.A = g.action_dim;
+  ea.D = D;
+  ea.eps = g.eps;
+  FAM_TRY(launch_encode_adaln(ea, rows, c.st, c.pdl));
+
+  const float scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(g.head_dim));
+  for (int l = 0; l < Lyr; ++l) {
+    const fam_action_layer& ly = c.e->layers[l];
+    // --- self / joint attention
+    FAM_TRYI(gemm_w(c, ly.qkv_w, nullptr, 3 * HD, D, h, D, rows, c.L.s_qkv, kActNone, part, 3 * HD, true));
+    QkvPostArgs qa = {};
+    qa.partials = part;
+    qa.split_stride = static_cast<long long>(rows) * 3 * HD;
+    qa.nsplit = c.L.s_qkv;
+    qa.bias = bf(ly.qkv_b);
+    qa.norm_q = bf(ly.norm_q);
+    qa.norm_k = bf(ly.norm_k);
+    qa.rope = static_cast<const float2*>(w.rope);
+    qa.rows_per_batch = Sa;
+    qa.q_out = wsp<__nv_bfloat16>(c, c.L.q);
+    qa.k_out = wsp<__nv_bfloat16>(c, c.L.ka);
+    qa.v_out = wsp<__nv_bfloat16>(c, c.L.va);
+    qa.out_stride = HD;
+    qa.HD = HD;
+    qa.head_dim = g.head_dim;
+    qa.eps = g.eps;
+    if (c.L.s_qkv == 1) {  // single split: partial buffer holds fp32 (no bias)
+      qa.nsplit = 1;
+    }
+    FAM_TRY(launch_qkv_post(qa, rows, c.st, c.pdl));
+
+    AttnArgs aa = {};
+    aa.q = wsp<__nv_bfloat16>(c, c.L.q);
+    aa.q_bs = static_cast<long long>(Sa) * HD;
+    aa.q_ts = HD;
+    if (io.video_tokens > 0) {
+      aa.k1 = bf(io.video_k[l]);
+      aa.v1 = bf(io.video_v[l]);
+      aa.kv1_bs = io.video_batch_stride;
+      aa.kv1_ts = io.video_token_stride;
+      aa.S1 = io.video_tokens;
+    }
+    aa.k2 = wsp<__nv_bfloat16>(c, c.L.ka);
+    aa.v2 = wsp<__nv_bfloat16>(c, c.L.va);
+    aa.kv2_bs = static_cast<long long>(Sa) * HD;
+    aa.kv2_ts = HD;
+    aa.S2 = Sa;
+    aa.mask2d = io.attn_mask;
+    aa.mask_rs = io.video_tokens + Sa;
+    aa.Sq = Sa;
+    aa.H = g.num_heads;
+    aa.scale_log2 = scale_log2;
+    aa.out = wsp<__nv_bfloat16>(c, c.L.ao);
+    aa.out_bs = static_cast<long long>(Sa) * HD;
+    aa.out_ts = HD;
+    aa.part = wsp<float>(c, c.L.apart);
+    aa.counters = wsp<int>(c, c.L.ctr);
+    const int skv = io.video_tokens + Sa;
+    aa.keys_per_split = 256;
+    aa.nsplit = (skv + 255) / 256;
+    if (aa.nsplit > 64) {
+      aa.nsplit = 64;
+      aa.keys_per_split = ((skv + 63) / 64 + 63) / 64 * 64;
+      aa.nsplit = (skv + aa.keys_per_split - 1) / aa.keys_per_split;
+    }
+    aa.status = c.e->status;
+    FAM_TRY(launch_attention(aa, io.batch, g.head_dim, c.st, c.pdl));
+
+    FAM_TRYI(gemm_w(c, ly.o_w, nullptr, D, HD, aa.out, HD, rows, c.L.s_o, kActNone, part, D, true));
+    ResidNormArgs r1 = {};
+    r1.x = x;
+    r1.partials = part;
+    r1.split_stride = static_cast<long long>(rows) * D;
+    r1.nsplit = c.L.s_o;
+    r1.bias = bf(ly.o_b);
+    r1.gate_chunk = 2;  // gate_msa
+    r1.norm_mode = kNormAffine;
+    r1.norm_w = bf(ly.norm3_w);
+    r1.norm_b = bf(ly.norm3_b);
+    r1.mod = step_mod(c, step, ly.modulation, Sa);
+    r1.h = h;
+    r1.h_stride = D;
+    r1.D = D;
+    r1.eps = g.eps;
+    FAM_TRY(launch_resid_norm(r1, rows, c.st, c.pdl));
+
+    // --- cross attention (no gate)
+    if (c.crow > 0) {
+      FAM_TRYI(gemm_w(c, ly.cq_w, nullptr, HD, D, h, D, rows, c.L.s_cq, kActNone, part, HD, true));
+      RmsRowsArgs rq = {};
+      rq.partials = part;
+      rq.split_stride = static_cast<long long>(rows) * HD;
+      rq.nsplit = c.L.s_cq;
+      rq.bias = bf(ly.cq_b);
+      rq.w = bf(ly.cnorm_q);
+      rq.out = wsp<__nv_bfloat16>(c, c.L.qc);
+      rq.out_stride = HD;
+      rq.N = HD;
+      rq.eps = g.eps;
+      FAM_TRY(launch_rms_rows(rq, rows, c.st, c.pdl));
+      AttnArgs ca = {};
+      ca.q = rq.out;
+      ca.q_bs = static_cast<long long>(Sa) * HD;
+      ca.q_ts = HD;
+      const __nv_bfloat16* ckv = wsp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.crow * 2 * HD;
+      ca.k1 = ckv;
+      ca.v1 = ckv + HD;
+      ca.kv1_bs = static_cast<long long>(io.context_tokens) * 2 * HD;
+      ca.kv1_ts = 2 * HD;
+      ca.S1 = io.context_tokens;
+      ca.key_mask = io.context_mask;
+      ca.key_mask_bs = io.context_tokens;
+      ca.Sq = Sa;
+      ca.H = g.num_heads;
+      ca.scale_log2 = scale_log2;
+      ca.out = wsp<__nv_bfloat16>(c, c.L.ci);
+      ca.out_bs = static_cast<long long>(Sa) * HD;
+      ca.out_ts = HD;
+      ca.nsplit = 1;
+      ca.keys_per_split = io.context_tokens;
+      ca.counters = wsp<int>(c, c.L.ctr);
+      ca.part = wsp<float>(c, c.L.apart);
+      ca.status = c.e->status;
+      FAM_TRY(launch_attention(ca, io.batch, g.head_dim, c.st, c.pdl));
+      FAM_TRYI(gemm_w(c, ly.co_w, nullptr, D, HD, ca.out, HD, rows, c.L.s_co, kActNone, part, D, true));
+    }
+    ResidNormArgs r2 = {};
+    r2.x = x;
+    r2.partials = c.crow > 0 ? part : nullptr;
+    r2.split_stride = static_cast<long long>(rows) * D;
+    r2.nsplit = c.L.s_co;
+    r2.bias = bf(ly.co_b);
+    r2.gate_chunk = -1;
+    r2.norm_mode = kNormAdaLN;
+    r2.shift_chunk = 3;  // shift_mlp, scale_mlp
+    r2.nmod = step_mod(c, step, ly.modulation, Sa);
+    r2.h = h;
+    r2.h_stride = D;
+    r2.D = D;
+    r2.eps = g.eps;
+    FAM_TRY(launch_resid_norm(r2, rows, c.st, c.pdl));
+
+    // --- FFN
+    FAM_TRYI(gemm_w(c, ly.ffn0_w, ly.ffn0_b, F, D, h, D, rows, 1, kActGeluTanh,
+                    wsp<void>(c, c.L.fh), F, false));
+    FAM_TRYI(gemm_w(c, ly.ffn2_w, nullptr, D, F, wsp<void>(c, c.L.fh), F, rows, c.L.s_f2, kActNone,
+                    part, D, true));
+    ResidNormArgs r3 = {};
+    r3.x = x;
+    r3.partials = part;
+    r3.split_stride = static_cast<long long>(rows) * D;
+    r3.nsplit = c.L.s_f2;
+    r3.bias = bf(ly.ffn2_b);
+    r3.gate_chunk = 5;  // gate_mlp
+    r3.mod = step_mod(c, step, ly.modulation, Sa);
+    r3.D = D;
+    r3.eps = g.eps;
+    if (l + 1 < Lyr) {  // next block's AdaLN (shift_msa, scale_msa)
+      r3.norm_mode = kNormAdaLN;
+      r3.shift_chunk = 0;
+      r3.nmod = step_mod(c, step, c.e->layers[l + 1].modulation, Sa);
+      r3.h = h;
+      r3.h_stride = D;
+    } else {
+      r3.norm_mode = kNormNone;
+    }
+    FAM_TRY(launch_resid_norm(r3, rows, c.st, c.pdl));
+  }
+  HeadArgs ha = {};
+  ha.x = x;
+  ha.head_w = bf(w.head_w);
+  ha.head_b = bf(w.head_b);
+  ha.velocity = static_cast<__nv_bfloat16*>(vel);
+  ha.latent = const_cast<__nv_bfloat16*>(bf(latent));
+  ha.delta = delta;
+  ha.apply_euler = apply ? 1 : 0;
+  ha.rows = rows;
+  ha.A = g.action_dim;
+  ha.D = D;
+  FAM_TRY(launch_head_euler(ha, c.st, c.pdl));
+  return 0;
+}
+
+int validate_io(const fam_action_expert* e, const fam_action_io* io, int N) {
+  if (e == nullptr || io == nullptr) return set_error("null expert or io");
+  if (io->batch <= 0 || io->action_tokens <= 0) return set_error("batch and action_tokens must be > 0");
+  if (io->action_tokens > 1024) return set_error("action_tokens %d exceeds the RoPE table", io->action_tokens);
+  if (io->action_tokens > e->w.rope_positions)
+    return set_error("rope table has %d positions, need %d", e->w.rope_positions, io->action_tokens);
+  if (io->context_tokens < 0 || (io->context_tokens > 0 && io->context == nullptr))
+    return set_error("context missing");
+  if (io->video_tokens < 0 || (io->video_tokens > 0 && (io->video_k == nullptr || io->video_v == nullptr)))
+    return set_error("video cache pointers missing");
+  if (N <= 0 || N > kMaxSteps) return set_error("num_steps must be in [1, %d]", kMaxSteps);
+  size_t need = layout(e->cfg, io->batch, io->action_tokens, io->context_tokens, N).total;
+  if (io->workspace == nullptr || io->workspace_bytes < need)
+    return set_error("workspace too small: %zu bytes given, %zu needed", io->workspace_bytes, need);
+  return 0;
+}
+
+int enqueue_chunk(const Ctx& c, void* latent, const float* ts, const float* ds, int N, void* trace) {
+  const size_t ctr_bytes = static_cast<size_t>(c.io->batch) * c.e->cfg.num_heads *
+                           ((c.io->action_tokens + 63) / 64) * 4;
+  FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
+  FAM_TRYI(enqueue_prologue(c, ts, N));
+  const size_t vel_elems = static_cast<size_t>(c.rows) * c.e->cfg.action_dim;
+  for (int i = 0; i < N; ++i) {
+    void* vel = trace != nullptr ? static_cast<void*>(static_cast<__nv_bfloat16*>(trace) + i * vel_elems)
+                                 : wsp<void>(c, c.L.vel);
+    FAM_TRYI(enqueue_step(c, i, latent, vel, ds[i], true));
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fam_action_expert_create(const fam_action_config* cfg, const fam_action_weights* w,
+                             fam_action_expert** out) {
+  if (cfg == nullptr || w == nullptr || out == nullptr) return set_error("null argument");
+  if (cfg->head_dim != 64 && cfg->head_dim != 128)
+    return set_error("head_dim %d unsupported (64 or 128)", cfg->head_dim);
+  if (cfg->hidden_dim % 64 || cfg->ffn_dim % 64 || cfg->text_dim % 8 || cfg->freq_dim % 64)
+    return set_error("hidden/ffn dims must be multiples of 64, text_dim of 8");
+  if (cfg->num_layers <= 0 || w->layers == nullptr) return set_error("no layers");
+  if (cfg->action_dim > 64) return set_error("action_dim must be <= 64");
+  if (w->rope == nullptr || w->rope_positions <= 0) return set_error("missing RoPE table");
+  int rc0 = 0;
+  auto e = std::make_unique<fam_action_expert>();
+  e->cfg = *cfg;
+  e->w = *w;
+  e->layers.assign(w->layers, w->layers + cfg->num_layers);
+  e->w.layers = e->layers.data();
+  rc0 = check_cuda(gemm_init_attributes(), "gemm attributes");
+  if (rc0) return rc0;
+  rc0 = check_cuda(attn_init_attributes(), "attention attributes");
+  if (rc0) return rc0;
+  e->status = device_status_word();
+  if (e->status == nullptr) return set_error("could not allocate the device status word");
+  int rc = check_cuda(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking), "stream create");
+  if (rc) return rc;
+  *out = e.release();
+  return FAM_OK;
+}
+
+int fam_action_expert_destroy(fam_action_expert* e) {
+  if (e == nullptr) return FAM_OK;
+  if (e->graph) cudaGraphExecDestroy(e->graph);
+  if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
+  delete e;
+  return FAM_OK;
+}
+
+int fam_action_workspace_size(const fam_action_expert* e, int32_t batch, int32_t action_tokens,
+                              int32_t context_tokens, int32_t max_steps, size_t* bytes) {
+  if (e == nullptr || bytes == nullptr) return set_error("null argument");
+  if (batch <= 0 || action_tokens <= 0 || context_tokens < 0 || max_steps <= 0)
+    return set_error("bad sizes");
+  *bytes = layout(e->cfg, batch, action_tokens, context_tokens, max_steps).total;
+  return FAM_OK;
+}
+
+int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent,
+                     const float* timesteps, const float* deltas, int32_t num_steps,
+                     void* velocity_trace, int32_t use_graph, void* stream) {
+  FAM_TRYI(validate_io(e, io, num_steps));
+  if (latent == nullptr || timesteps == nullptr || deltas == nullptr) return set_error("null latent/schedule");
+  Ctx c;
+  c.e = e;
+  c.io = io;
+  c.ws = static_cast<char*>(io->workspace);
+  c.L = layout(e->cfg, io->batch, io->action_tokens, io->context_tokens, num_steps);
+  c.rows = io->batch * io->action_tokens;
+  c.crow = io->batch * io->context_tokens;
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  if (!use_graph) {
+    c.st = user;
+    c.pdl = true;
+    FAM_TRYI(enqueue_chunk(c, latent, timesteps, deltas, num_steps, velocity_trace));
+    return check_cuda(cudaGetLastError(), "fam_action_chunk launch");
+  }
+  CallKey key;
+  key.ptrs = {reinterpret_cast<uintptr_t>(io->workspace), reinterpret_cast<uintptr_t>(latent),
+              reinterpret_cast<uintptr_t>(io->context), reinterpret_cast<uintptr_t>(io->context_mask),
+              reinterpret_cast<uintptr_t>(io->attn_mask), reinterpret_cast<uintptr_t>(velocity_trace),
+              static_cast<uintptr_t>(io->batch), static_cast<uintptr_t>(io->action_tokens),
+              static_cast<uintptr_t>(io->context_tokens), static_cast<uintptr_t>(io->video_tokens),
+              static_cast<uintptr_t>(io->video_batch_stride), static_cast<uintptr_t>(io->video_token_stride),
+              static_cast<uintptr_t>(num_steps)};
+  for (int l = 0; io->video_tokens > 0 && l < e->cfg.num_layers; ++l) {
+    key.ptrs.push_back(reinterpret_cast<uintptr_t>(io->video_k[l]));
+    key.ptrs.push_back(reinterpret_cast<uintptr_t>(io->video_v[l]));
+  }
+  key.vals.assign(timesteps, timesteps + num_steps);
+  key.vals.insert(key.vals.end(), deltas, deltas + num_steps);
+  if (e->graph == nullptr || !(key == e->graph_key)) {
+    if (e->graph) {
+      cudaGraphExecDestroy(e->graph);
+      e->graph = nullptr;
+    }
+    c.st = e->cap_stream;
+    c.pdl = true;
+    FAM_TRY(cudaStreamBeginCapture(c.st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_chunk(c, latent, timesteps, deltas, num_steps, velocity_trace);
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(c.st, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (ce != cudaSuccess) return check_cuda(ce, "end capture");
+    ce = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+      e->graph = nullptr;
+      return check_cuda(ce, "graph instantiate");
+    }
+    e->graph_key = key;
+  }
+  return check_cuda(cudaGraphLaunch(e->graph, user), "graph launch");
+}
+
+int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* io, const void* latent,
+                            float timestep, void* velocity, void* stream) {
+  FAM_TRYI(validate_io(e, io, 1));
+  if (latent == nullptr || velocity == nullptr) return set_error("null latent/velocity");
+  Ctx c;
+  c.e = e;
+  c.io = io;
+  c.ws = static_cast<char*>(io->workspace);
+  c.L = layout(e->cfg, io->batch, io->action_tokens, io->context_tokens, 1);
+  c.rows = io->batch * io->action_tokens;
+  c.crow = io->batch * io->context_tokens;
+  c.st = static_cast<cudaStream_t>(stream);
+  c.pdl = true;
+  const size_t ctr_bytes = static_cast<size_t>(io->batch) * e->cfg.num_heads * ((io->action_tokens + 63) / 64) * 4;
+  FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
+  FAM_TRYI(enqueue_prologue(c, &timestep, 1));
+  FAM_TRYI(enqueue_step(c, 0, latent, velocity, 0.0f, false));
+  return check_cuda(cudaGetLastError(), "fam_action_denoise_step launch");
+}
+
+}  // extern "C"

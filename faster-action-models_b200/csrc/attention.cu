@@ -1,0 +1,354 @@
+// Masked flash attention for the DiT blocks (SDPA with a bool mask, scale
+// 1/sqrt(d): FastWAM/src/fastwam/models/wan22/wan_video_dit.py:13-22).
+//
+// One CTA = 4 warps = a 64-query tile of one (batch, head), over one split of
+// the key range.  Keys come from up to two token-major sources: the cached
+// video K/V of the layer and the fresh K/V of the current tokens (the joint
+// attention of mot.py:560-566 concatenates exactly these two).  K/V blocks of
+// 64 keys stream through a double-buffered shared-memory ring with cp.async;
+// QK^T and PV run on bf16 mma.sync tensor-core fragments with an fp32 online
+// softmax in exp2 form.  With several key splits (decode-style, few queries,
+// long cache) every split writes an unnormalised partial (O, m, l) and the
+// last CTA to arrive for a (batch, head, query tile) merges them in split
+// order (deterministic) and resets its arrival counter.
+//
+// Masks: an explicit [Sq, Skv] bool mask shared by the batch (the MoT action
+// rows of fastwam.py:429-451), a per-batch key mask (text context padding),
+// and the first-frame-causal rule of the video self-attention
+// (wan_video_dit.py:514-518) as a descriptor instead of a materialised mask.
+#include "fam_common.cuh"
+#include "fam_kernels.h"
+
+namespace fam {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnQTile = 16 * kAttnWarps;  // 64 queries
+constexpr int kAttnKB = 64;                  // keys per block
+
+template <int HD>
+struct AttnSmem {
+  static constexpr int kRow = HD + 8;  // padded row (bank-conflict free fragment loads)
+  static constexpr int kBlockElems = kAttnKB * kRow;
+  static constexpr int kBytes = 2 /*stages*/ * 2 /*K,V*/ * kBlockElems * 2;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const uint32_t s = smem_u32(smem);
+  const int n = valid ? 16 : 0;  // zero-fill rows past the end
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Key j of (b, h): pointer to its K (or V) row slice, or null past the end.
+__device__ __forceinline__ const __nv_bfloat16* kv_row(const AttnArgs& a, bool is_v, int b, int h,
+                                                       int j, int hd) {
+  if (j < a.S1) {
+    const __nv_bfloat16* base = is_v ? a.v1 : a.k1;
+    return base + b * a.kv1_bs + static_cast<long long>(j) * a.kv1_ts + h * hd;
+  }
+  j -= a.S1;
+  if (j < a.S2) {
+    const __nv_bfloat16* base = is_v ? a.v2 : a.k2;
+    return base + b * a.kv2_bs + static_cast<long long>(j) * a.kv2_ts + h * hd;
+  }
+  return nullptr;
+}
+
+template <int HD>
+__device__ __forceinline__ void load_kv_block(const AttnArgs& a, __nv_bfloat16* sk,
+                                              __nv_bfloat16* sv, int b, int h, int j0, int j_end) {
+  constexpr int kChunks = HD / 8;  // 16-byte chunks per row
+  for (int idx = threadIdx.x; idx < kAttnKB * kChunks; idx += blockDim.x) {
+    const int r = idx / kChunks, c = idx % kChunks;
+    const int j = j0 + r;
+    const bool valid = j < j_end;
+    const __nv_bfloat16* kp = valid ? kv_row(a, false, b, h, j, HD) : nullptr;
+    const __nv_bfloat16* vp = valid ? kv_row(a, true, b, h, j, HD) : nullptr;
+    cp_async16(sk + r * AttnSmem<HD>::kRow + c * 8, valid ? kp + c * 8 : a.q, valid);
+    cp_async16(sv + r * AttnSmem<HD>::kRow + c * 8, valid ? vp + c * 8 : a.q, valid);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  __nv_bfloat16* smem = reinterpret_cast<__nv_bfloat16*>(attn_smem);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x % a.nsplit;
+  const int qt = blockIdx.x / a.nsplit;
+  const int q_tiles = (a.Sq + kAttnQTile - 1) / kAttnQTile;
+  const int skv = a.S1 + a.S2;
+  const int k_begin = split * a.keys_per_split;
+  const int k_end = min(skv, k_begin + a.keys_per_split);
+  const int qw0 = qt * kAttnQTile + warp * 16;  // first query of this warp
+  const int qr0 = qw0 + g, qr1 = qw0 + g + 8;   // the two rows this thread owns
+
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // Q fragments (A operand, row-major 16 x HD) straight from global.
+  constexpr int KS = HD / 16;
+  uint32_t qf[KS][4];
+  {
+    const __nv_bfloat16* q0 = a.q + b * a.q_bs + static_cast<long long>(min(qr0, a.Sq - 1)) * a.q_ts + h * HD;
+    const __nv_bfloat16* q1 = a.q + b * a.q_bs + static_cast<long long>(min(qr1, a.Sq - 1)) * a.q_ts + h * HD;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      qf[kk][0] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 2 * t);
+      qf[kk][1] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 2 * t);
+      qf[kk][2] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 8 + 2 * t);
+      qf[kk][3] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 8 + 2 * t);
+    }
+  }
+
+  constexpr int NT = HD / 8;  // output dim tiles
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+  const int nblocks = k_end > k_begin ? (k_end - k_begin + kAttnKB - 1) / kAttnKB : 0;
+  __nv_bfloat16* sK[2] = {smem, smem + 2 * AttnSmem<HD>::kBlockElems};
+  __nv_bfloat16* sV[2] = {smem + AttnSmem<HD>::kBlockElems, smem + 3 * AttnSmem<HD>::kBlockElems};
+
+  // Row-level key limits of the first-frame-causal rule.
+  const int ff = a.first_frame_tokens;
+  const int lim0 = (ff > 0 && qr0 < ff) ? ff : skv;
+  const int lim1 = (ff > 0 && qr1 < ff) ? ff : skv;
+  const uint8_t* km = a.key_mask != nullptr ? a.key_mask + b * a.key_mask_bs : nullptr;
+  const uint8_t* mr0 = a.mask2d != nullptr ? a.mask2d + static_cast<long long>(min(qr0, a.Sq - 1)) * a.mask_rs : nullptr;
+  const uint8_t* mr1 = a.mask2d != nullptr ? a.mask2d + static_cast<long long>(min(qr1, a.Sq - 1)) * a.mask_rs : nullptr;
+
+  if (nblocks > 0) load_kv_block<HD>(a, sK[0], sV[0], b, h, k_begin, k_end);
+  cp_async_commit();
+  for (int blk = 0; blk < nblocks; ++blk) {
+    const int cur = blk & 1;
+    if (blk + 1 < nblocks)
+      load_kv_block<HD>(a, sK[cur ^ 1], sV[cur ^ 1], b, h, k_begin + (blk + 1) * kAttnKB, k_end);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+
+    const __nv_bfloat16* K = sK[cur];
+    const __nv_bfloat16* V = sV[cur];
+    const int j0 = k_begin + blk * kAttnKB;
+    // S = Q K^T for 64 keys: 8 tiles of 8 keys.
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
+      const __nv_bfloat16* kr = K + (n * 8 + g) * AttnSmem<HD>::kRow;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t bf[2];
+        bf[0] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 2 * t);
+        bf[1] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 8 + 2 * t);
+        mma_bf16_16816(s[n], qf[kk], bf);
+      }
+    }
+    // scale + mask, row max
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = j0 + n * 8 + 2 * t + e;
+        bool ok = j < k_end;
+        if (ok && km != nullptr) ok = km[j] != 0;
+        bool ok0 = ok && j < lim0 && qr0 < a.Sq && (mr0 == nullptr || mr0[j] != 0);
+        bool ok1 = ok && j < lim1 && qr1 < a.Sq && (mr1 == nullptr || mr1[j] != 0);
+        s[n][e] = ok0 ? s[n][e] * a.scale_log2 : -INFINITY;
+        s[n][2 + e] = ok1 ? s[n][2 + e] * a.scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[n][e]);
+        mx1 = fmaxf(mx1, s[n][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.0f : mn0;
+    const float base1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.0f, ps1 = 0.0f;
+    uint32_t pf[4][4];  // P as A fragments: 4 k-steps of 16 keys
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p0 = exp2f(s[n][0] - base0), p1 = exp2f(s[n][1] - base0);
+      const float p2 = exp2f(s[n][2] - base1), p3 = exp2f(s[n][3] - base1);
+      ps0 += p0 + p1;
+      ps1 += p2 + p3;
+      const int ks = n >> 1, hi = n & 1;
+      pf[ks][hi ? 2 : 0] = pack_bf16(p0, p1);
+      pf[ks][hi ? 3 : 1] = pack_bf16(p2, p3);
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      o[i][0] *= al0;
+      o[i][1] *= al0;
+      o[i][2] *= al1;
+      o[i][3] *= al1;
+    }
+    // O += P V : B fragments of V via ldmatrix.trans (rows = keys).
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        uint32_t bf[2];
+        const int r = ks * 16 + (lane & 15);
+        const uint32_t addr = smem_u32(V + r * AttnSmem<HD>::kRow + i * 8);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                     : "=r"(bf[0]), "=r"(bf[1])
+                     : "r"(addr));
+        mma_bf16_16816(o[i], pf[ks], bf);
+      }
+    }
+    __syncthreads();
+  }
+
+  // Full row sums across the 4 threads of a quad.
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  if (a.nsplit == 1) {
+    const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f;
+    const float inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const int d = i * 8 + 2 * t;
+      if (qr0 < a.Sq)
+        *reinterpret_cast<uint32_t*>(a.out + b * a.out_bs + static_cast<long long>(qr0) * a.out_ts + h * HD + d) =
+            pack_bf16(o[i][0] * inv0, o[i][1] * inv0);
+      if (qr1 < a.Sq)
+        *reinterpret_cast<uint32_t*>(a.out + b * a.out_bs + static_cast<long long>(qr1) * a.out_ts + h * HD + d) =
+            pack_bf16(o[i][2] * inv1, o[i][3] * inv1);
+    }
+    return;
+  }
+
+  // ---- split-K partials + last-arriving-CTA merge
+  const int Sq_pad = q_tiles * kAttnQTile;
+  const long long unit = (static_cast<long long>(b) * a.H + h) * a.nsplit;  // (b, h) base
+  float* po = a.part + (unit + split) * Sq_pad * HD;
+  float* pml = a.part + static_cast<long long>(gridDim.z) * a.H * a.nsplit * Sq_pad * HD +
+               (unit + split) * Sq_pad * 2;
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int d = i * 8 + 2 * t;
+    *reinterpret_cast<float2*>(po + static_cast<long long>(qr0) * HD + d) = make_float2(o[i][0], o[i][1]);
+    *reinterpret_cast<float2*>(po + static_cast<long long>(qr1) * HD + d) = make_float2(o[i][2], o[i][3]);
+  }
+  if (t == 0) {
+    *reinterpret_cast<float2*>(pml + qr0 * 2) = make_float2(m0, l0);
+    *reinterpret_cast<float2*>(pml + qr1 * 2) = make_float2(m1, l1);
+  }
+  __threadfence();
+  __syncthreads();
+  int* ctr = a.counters + (static_cast<long long>(b) * a.H + h) * q_tiles + qt;
+  if (threadIdx.x == 0) s_last = (atomicAdd(ctr, 1) == a.nsplit - 1) ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Merge: thread handles (query, dim-pair) items of this query tile.
+  const float* po0 = a.part + unit * Sq_pad * HD;
+  const float* pml0 = a.part + static_cast<long long>(gridDim.z) * a.H * a.nsplit * Sq_pad * HD + unit * Sq_pad * 2;
+  for (int idx = threadIdx.x; idx < kAttnQTile * (HD / 2); idx += blockDim.x) {
+    const int ql = idx / (HD / 2);
+    const int d = (idx % (HD / 2)) * 2;
+    const int q = qt * kAttnQTile + ql;
+    if (q >= a.Sq) continue;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < a.nsplit; ++s2) M = fmaxf(M, __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2));
+    const float base = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+    for (int s2 = 0; s2 < a.nsplit; ++s2) {
+      const float ms = __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2);
+      const float ls = __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2 + 1);
+      const float w = exp2f(ms - base);
+      L += w * ls;
+      const float2 ov = __ldcg(reinterpret_cast<const float2*>(po0 + (static_cast<long long>(s2) * Sq_pad + q) * HD + d));
+      acc0 += w * ov.x;
+      acc1 += w * ov.y;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    *reinterpret_cast<uint32_t*>(a.out + b * a.out_bs + static_cast<long long>(q) * a.out_ts + h * HD + d) =
+        pack_bf16(acc0 * inv, acc1 * inv);
+  }
+  if (threadIdx.x == 0) *ctr = 0;  // ready for the next launch
+}
+
+size_t attn_partial_bytes(int B, int H, int Sq, int head_dim, int nsplit) {
+  if (nsplit <= 1) return 0;
+  const int q_tiles = (Sq + kAttnQTile - 1) / kAttnQTile;
+  const size_t Sq_pad = static_cast<size_t>(q_tiles) * kAttnQTile;
+  return static_cast<size_t>(B) * H * nsplit * Sq_pad * (head_dim + 2) * sizeof(float);
+}
+
+template <int HD>
+static cudaError_t launch_attn_hd(const AttnArgs& a, int B, cudaStream_t st, bool pdl) {
+  constexpr int smem = AttnSmem<HD>::kBytes;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int q_tiles = (a.Sq + kAttnQTile - 1) / kAttnQTile;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(q_tiles * a.nsplit, a.H, B);
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr_l[1];
+  attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_l[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr_l;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
+}
+
+cudaError_t attn_init_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       AttnSmem<64>::kBytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              AttnSmem<128>::kBytes);
+}
+
+cudaError_t launch_attention(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl) {
+  if (head_dim == 64) return launch_attn_hd<64>(a, B, st, pdl);
+  if (head_dim == 128) return launch_attn_hd<128>(a, B, st, pdl);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fam

@@ -26,7 +26,7 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
 
 // ------------------------------------------------------------------ GEMM
 enum EpiKind : int { kEpiStore = 0, kEpiPartial = 1, kEpiResidual = 2 };
-enum ActKind : int { kActNone = 0, kActGeluTanh = 1 };
+enum ActKind : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };
 
 struct GemmEpilogue {
   int kind;                 // EpiKind
@@ -70,5 +70,9 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
               int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,
               int* status);
 cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl);
+// Sets the dynamic shared-memory limits of every kernel instantiation (call
+// once per device before any stream capture).
+cudaError_t gemm_init_attributes();
+cudaError_t attn_init_attributes();
 
 }  // namespace fam

@@ -64,7 +64,8 @@ __device__ __forceinline__ void gemm_epilogue_apply(const GemmArgs& args, const 
     const int feat = e.features_on_a ? a_row : b;
     float x = v[j];
     if (e.bias != nullptr && b < args.N) x += bf2f(e.bias[feat]);
-    if (e.act == kActGeluTanh) x = gelu_tanh(x);
+    if (e.act == kActGeluTanh) x = gelu_tanh(rbf(x));
+    else if (e.act == kActSilu) x = silu(rbf(x));
     v[j] = x;
   }
   if (e.kind == kEpiStore) {
@@ -293,6 +294,17 @@ static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BN>, ta, tb, a);
+}
+
+cudaError_t gemm_init_attributes() {
+  cudaError_t e;
+#define FAM_SET(BN)                                                                          \
+  e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           gemm_smem_bytes(BN));                                             \
+  if (e != cudaSuccess) return e;
+  FAM_SET(16) FAM_SET(32) FAM_SET(64) FAM_SET(128) FAM_SET(256)
+#undef FAM_SET
+  return cudaSuccess;
 }
 
 int gemm_pick_bn(int n) {

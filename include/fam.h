@@ -51,6 +51,7 @@ extern "C" {
 
 #define FAM_ACT_NONE 0
 #define FAM_ACT_GELU_TANH 1
+#define FAM_ACT_SILU 2
 
 FAM_API int fam_version(int* major, int* minor, int* patch);
 
@@ -102,6 +103,106 @@ typedef struct fam_gemm_desc {
 } fam_gemm_desc;
 
 FAM_API int fam_gemm(const fam_gemm_desc* desc, void* stream);
+
+/* ======================================================================
+ * Action expert (ActionDiT + MoT action path) — BASELINE configs 1 and 3.
+ *
+ * Replaces, for a bf16 model:
+ *   ActionDiT.prepare / post         FastWAM/src/fastwam/models/wan22/action_dit.py:312-331
+ *   MoT.forward_action_with_video_cache_tensor   .../wan22/mot.py:528-578
+ *   FastWAM._denoise_action_with_video_cache     .../wan22/fastwam.py:771-804
+ *   the Euler loop of FastWAM.infer_action       .../wan22/fastwam.py:1241-1263
+ *   WanContinuousFlowMatchScheduler.step         .../wan22/schedulers/scheduler_continuous.py:82-88
+ * Weights are the reference state_dict tensors (bf16, device resident); the
+ * q/k/v projections of each block are passed concatenated ([3*HD, D] rows
+ * q, k, v) and the cross-attention k/v concatenated ([2*HD, D]).  The
+ * handle keeps the pointers (the caller owns the memory).
+ * ====================================================================== */
+typedef struct fam_action_config {
+  int32_t hidden_dim;   /* D */
+  int32_t action_dim;   /* A */
+  int32_t ffn_dim;      /* F */
+  int32_t text_dim;     /* T */
+  int32_t freq_dim;     /* sinusoid width (256) */
+  int32_t num_heads;    /* H */
+  int32_t head_dim;     /* d (64 or 128); HD = H * d */
+  int32_t num_layers;   /* L */
+  float eps;            /* LayerNorm / RMSNorm eps */
+} fam_action_config;
+
+typedef struct fam_action_layer {
+  const void* modulation;                  /* [6, D]            blocks.i.modulation */
+  const void* qkv_w; const void* qkv_b;    /* [3HD, D], [3HD]   self_attn.{q,k,v} */
+  const void* norm_q; const void* norm_k;  /* [HD]              self_attn.norm_{q,k} */
+  const void* o_w; const void* o_b;        /* [D, HD], [D]      self_attn.o */
+  const void* norm3_w; const void* norm3_b;/* [D]               norm3 */
+  const void* cq_w; const void* cq_b;      /* [HD, D], [HD]     cross_attn.q */
+  const void* cnorm_q; const void* cnorm_k;/* [HD]              cross_attn.norm_{q,k} */
+  const void* ckv_w; const void* ckv_b;    /* [2HD, D], [2HD]   cross_attn.{k,v} */
+  const void* co_w; const void* co_b;      /* [D, HD], [D]      cross_attn.o */
+  const void* ffn0_w; const void* ffn0_b;  /* [F, D], [F]       ffn.0 */
+  const void* ffn2_w; const void* ffn2_b;  /* [D, F], [D]       ffn.2 */
+} fam_action_layer;
+
+typedef struct fam_action_weights {
+  const void* enc_w; const void* enc_b;        /* [D, A]  action_encoder */
+  const void* text0_w; const void* text0_b;    /* [D, T]  text_embedding.0 */
+  const void* text2_w; const void* text2_b;    /* [D, D]  text_embedding.2 */
+  const void* time0_w; const void* time0_b;    /* [D, 256] time_embedding.0 */
+  const void* time2_w; const void* time2_b;    /* [D, D]  time_embedding.2 */
+  const void* tproj_w; const void* tproj_b;    /* [6D, D] time_projection.1 */
+  const void* head_w; const void* head_b;      /* [A, D]  head */
+  const fam_action_layer* layers;              /* host array [L] */
+  const void* rope;        /* f32 [rope_positions, d/2, 2] (cos, sin) of precompute_freqs_cis(d) */
+  int32_t rope_positions;
+} fam_action_weights;
+
+typedef struct fam_action_expert fam_action_expert;
+
+/* Per-call inputs.  All device pointers; the K/V cache of layer l is
+ * video_k[l][b * video_batch_stride + s * video_token_stride + c] (c < HD),
+ * i.e. the reference's list of [B, Sv, HD] tensors (MoT.prefill_video_cache_tensor
+ * output).  attn_mask is the [Sa, Sv + Sa] action-row slice of the MoT mask
+ * (True = attend; NULL = all True).  context_mask [B, C] (NULL = all valid). */
+typedef struct fam_action_io {
+  int32_t batch;
+  int32_t action_tokens;     /* Sa */
+  int32_t context_tokens;    /* C */
+  int32_t video_tokens;      /* Sv (0: standalone expert, no cache) */
+  const void* context;       /* bf16 [B, C, T] */
+  const uint8_t* context_mask;
+  const void* const* video_k;/* host array [L] of device pointers */
+  const void* const* video_v;
+  int64_t video_batch_stride;
+  int64_t video_token_stride;
+  const uint8_t* attn_mask;
+  void* workspace;
+  size_t workspace_bytes;
+} fam_action_io;
+
+FAM_API int fam_action_expert_create(const fam_action_config* cfg, const fam_action_weights* w,
+                                     fam_action_expert** out);
+FAM_API int fam_action_expert_destroy(fam_action_expert* e);
+
+/* Workspace bytes for a call with these sizes (max_steps >= num_steps of the call). */
+FAM_API int fam_action_workspace_size(const fam_action_expert* e, int32_t batch,
+                                      int32_t action_tokens, int32_t context_tokens,
+                                      int32_t max_steps, size_t* bytes);
+
+/* One whole action chunk: num_steps Euler steps at the given (already
+ * dtype-rounded) timesteps and deltas (host arrays), latent updated in place
+ * (bf16 [B, Sa, A]).  velocity_trace (bf16 [num_steps, B, Sa, A]) is optional.
+ * use_graph != 0 captures the launch sequence once into a CUDA graph and
+ * replays it while the pointers and sizes stay the same. */
+FAM_API int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent,
+                             const float* timesteps, const float* deltas, int32_t num_steps,
+                             void* velocity_trace, int32_t use_graph, void* stream);
+
+/* One model evaluation (FastWAM._denoise_action_with_video_cache): the
+ * velocity bf16 [B, Sa, A] for latent at the given timestep; no Euler update. */
+FAM_API int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* io,
+                                    const void* latent, float timestep, void* velocity,
+                                    void* stream);
 
 #ifdef __cplusplus
 }
