@@ -47,3 +47,9 @@ def declare(lib) -> None:
     for n in ("fam_action_expert_create", "fam_action_expert_destroy", "fam_action_workspace_size",
               "fam_action_chunk", "fam_action_denoise_step"):
         getattr(lib, n).restype = C.c_int
+    declare_counts(lib)
+
+
+def declare_counts(lib) -> None:
+    lib.fam_action_launch_count.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
+    lib.fam_action_launch_count.restype = C.c_int

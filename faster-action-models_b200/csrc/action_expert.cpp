@@ -116,6 +116,7 @@ struct fam_action_expert {
   cudaGraphExec_t graph = nullptr;
   CallKey graph_key;
   int* status = nullptr;
+  int launch_count = 0;  // kernels enqueued by the last chunk / step call
 };
 
 namespace {
@@ -145,6 +146,12 @@ T* wsp(const Ctx& c, size_t off) {
     int _r = (expr);    \
     if (_r) return _r;  \
   } while (0)
+// A kernel launch of the chain (counted for fam_action_launch_count).
+#define FAM_LAUNCH(expr)    \
+  do {                      \
+    FAM_TRY(expr);          \
+    ++c.e->launch_count;    \
+  } while (0)
 
 // out = act(A-weights x B-activations + bias) or split partials.
 int gemm_w(const Ctx& c, const void* W, const void* bias, int n_out, int k, const void* act,
@@ -166,7 +173,7 @@ int gemm_w(const Ctx& c, const void* W, const void* bias, int n_out, int k, cons
   }
   GemmPlan p;
   FAM_TRYI(gemm_plan(&p, W, k, act, act_ld, n_out, rows, k, splits, 0, e, true, false, c.e->status));
-  FAM_TRY(gemm_launch(p, c.st, c.pdl));
+  FAM_LAUNCH(gemm_launch(p, c.st, c.pdl));
   return 0;
 }
 
@@ -189,7 +196,7 @@ int enqueue_prologue(const Ctx& c, const float* timesteps, int N) {
   StepTimes st = {};
   for (int i = 0; i < N; ++i) st.t[i] = timesteps[i];
   // First launch of the chain follows a memset node: plain stream order.
-  FAM_TRY(launch_sinusoid(st, N, g.freq_dim, wsp<__nv_bfloat16>(c, c.L.sin), c.st, false));
+  FAM_LAUNCH(launch_sinusoid(st, N, g.freq_dim, wsp<__nv_bfloat16>(c, c.L.sin), c.st, false));
   // time_embedding: Linear -> SiLU -> Linear ; time_projection: SiLU -> Linear
   FAM_TRYI(gemm_w(c, w.time0_w, w.time0_b, D, g.freq_dim, wsp<void>(c, c.L.sin), g.freq_dim, N, 1,
                   kActSilu, wsp<void>(c, c.L.th1), D, false));
@@ -217,7 +224,7 @@ int enqueue_prologue(const Ctx& c, const float* timesteps, int N) {
       r.out_stride = 2 * HD;
       r.N = HD;
       r.eps = g.eps;
-      FAM_TRY(launch_rms_rows(r, c.crow, c.st, c.pdl));
+      FAM_LAUNCH(launch_rms_rows(r, c.crow, c.st, c.pdl));
     }
   }
   return 0;
@@ -244,7 +251,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
   ea.A = g.action_dim;
   ea.D = D;
   ea.eps = g.eps;
-  FAM_TRY(launch_encode_adaln(ea, rows, c.st, c.pdl));
+  FAM_LAUNCH(launch_encode_adaln(ea, rows, c.st, c.pdl));
 
   const float scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(g.head_dim));
   for (int l = 0; l < Lyr; ++l) {
@@ -270,7 +277,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     if (c.L.s_qkv == 1) {  // single split: partial buffer holds fp32 (no bias)
       qa.nsplit = 1;
     }
-    FAM_TRY(launch_qkv_post(qa, rows, c.st, c.pdl));
+    FAM_LAUNCH(launch_qkv_post(qa, rows, c.st, c.pdl));
 
     AttnArgs aa = {};
     aa.q = wsp<__nv_bfloat16>(c, c.L.q);
@@ -307,7 +314,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       aa.nsplit = (skv + aa.keys_per_split - 1) / aa.keys_per_split;
     }
     aa.status = c.e->status;
-    FAM_TRY(launch_attention(aa, io.batch, g.head_dim, c.st, c.pdl));
+    FAM_LAUNCH(launch_attention(aa, io.batch, g.head_dim, c.st, c.pdl));
 
     FAM_TRYI(gemm_w(c, ly.o_w, nullptr, D, HD, aa.out, HD, rows, c.L.s_o, kActNone, part, D, true));
     ResidNormArgs r1 = {};
@@ -325,7 +332,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     r1.h_stride = D;
     r1.D = D;
     r1.eps = g.eps;
-    FAM_TRY(launch_resid_norm(r1, rows, c.st, c.pdl));
+    FAM_LAUNCH(launch_resid_norm(r1, rows, c.st, c.pdl));
 
     // --- cross attention (no gate)
     if (c.crow > 0) {
@@ -340,7 +347,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       rq.out_stride = HD;
       rq.N = HD;
       rq.eps = g.eps;
-      FAM_TRY(launch_rms_rows(rq, rows, c.st, c.pdl));
+      FAM_LAUNCH(launch_rms_rows(rq, rows, c.st, c.pdl));
       AttnArgs ca = {};
       ca.q = rq.out;
       ca.q_bs = static_cast<long long>(Sa) * HD;
@@ -364,7 +371,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       ca.counters = wsp<int>(c, c.L.ctr);
       ca.part = wsp<float>(c, c.L.apart);
       ca.status = c.e->status;
-      FAM_TRY(launch_attention(ca, io.batch, g.head_dim, c.st, c.pdl));
+      FAM_LAUNCH(launch_attention(ca, io.batch, g.head_dim, c.st, c.pdl));
       FAM_TRYI(gemm_w(c, ly.co_w, nullptr, D, HD, ca.out, HD, rows, c.L.s_co, kActNone, part, D, true));
     }
     ResidNormArgs r2 = {};
@@ -381,7 +388,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     r2.h_stride = D;
     r2.D = D;
     r2.eps = g.eps;
-    FAM_TRY(launch_resid_norm(r2, rows, c.st, c.pdl));
+    FAM_LAUNCH(launch_resid_norm(r2, rows, c.st, c.pdl));
 
     // --- FFN
     FAM_TRYI(gemm_w(c, ly.ffn0_w, ly.ffn0_b, F, D, h, D, rows, 1, kActGeluTanh,
@@ -407,7 +414,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     } else {
       r3.norm_mode = kNormNone;
     }
-    FAM_TRY(launch_resid_norm(r3, rows, c.st, c.pdl));
+    FAM_LAUNCH(launch_resid_norm(r3, rows, c.st, c.pdl));
   }
   HeadArgs ha = {};
   ha.x = x;
@@ -420,7 +427,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
   ha.rows = rows;
   ha.A = g.action_dim;
   ha.D = D;
-  FAM_TRY(launch_head_euler(ha, c.st, c.pdl));
+  FAM_LAUNCH(launch_head_euler(ha, c.st, c.pdl));
   return 0;
 }
 
@@ -442,6 +449,7 @@ int validate_io(const fam_action_expert* e, const fam_action_io* io, int N) {
 }
 
 int enqueue_chunk(const Ctx& c, void* latent, const float* ts, const float* ds, int N, void* trace) {
+  c.e->launch_count = 0;
   const size_t ctr_bytes = static_cast<size_t>(c.io->batch) * c.e->cfg.num_heads *
                            ((c.io->action_tokens + 63) / 64) * 4;
   FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
@@ -564,6 +572,12 @@ int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent
   return check_cuda(cudaGraphLaunch(e->graph, user), "graph launch");
 }
 
+int fam_action_launch_count(const fam_action_expert* e, int32_t* count) {
+  if (e == nullptr || count == nullptr) return set_error("null argument");
+  *count = e->launch_count;
+  return FAM_OK;
+}
+
 int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* io, const void* latent,
                             float timestep, void* velocity, void* stream) {
   FAM_TRYI(validate_io(e, io, 1));
@@ -578,6 +592,7 @@ int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* io, const
   c.st = static_cast<cudaStream_t>(stream);
   c.pdl = true;
   const size_t ctr_bytes = static_cast<size_t>(io->batch) * e->cfg.num_heads * ((io->action_tokens + 63) / 64) * 4;
+  e->launch_count = 0;
   FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
   FAM_TRYI(enqueue_prologue(c, &timestep, 1));
   FAM_TRYI(enqueue_step(c, 0, latent, velocity, 0.0f, false));

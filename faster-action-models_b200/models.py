@@ -251,6 +251,12 @@ class ActionExpertEngine:
         io.workspace, io.workspace_bytes = ws.data_ptr(), ws.numel()
         return io
 
+    def launch_count(self) -> int:
+        """Kernels the last chunk / step call enqueued (a graph replay launches the same)."""
+        n = C.c_int32()
+        check(lib().fam_action_launch_count(self.handle, C.byref(n)), "fam_action_launch_count")
+        return n.value
+
     def denoise_step(self, latents, timestep, context, context_mask=None, cache_k=None,
                      cache_v=None, attn_mask=None) -> torch.Tensor:
         """One model evaluation (FastWAM._denoise_action_with_video_cache, fastwam.py:771-804)."""

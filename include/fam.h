@@ -204,6 +204,10 @@ FAM_API int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* i
                                     const void* latent, float timestep, void* velocity,
                                     void* stream);
 
+/* Number of kernels the last fam_action_chunk / fam_action_denoise_step call
+ * enqueued (a graph replay launches the same set). */
+FAM_API int fam_action_launch_count(const fam_action_expert* e, int32_t* count);
+
 #ifdef __cplusplus
 }
 #endif
