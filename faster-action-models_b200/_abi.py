@@ -48,8 +48,29 @@ def declare(lib) -> None:
               "fam_action_chunk", "fam_action_denoise_step"):
         getattr(lib, n).restype = C.c_int
     declare_counts(lib)
+    declare_ops(lib)
 
 
 def declare_counts(lib) -> None:
     lib.fam_action_launch_count.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
     lib.fam_action_launch_count.restype = C.c_int
+
+
+class AttentionDesc(C.Structure):
+    _fields_ = [("batch", C.c_int32), ("heads", C.c_int32), ("head_dim", C.c_int32),
+                ("q_tokens", C.c_int32), ("q", vp), ("q_batch_stride", C.c_int64),
+                ("q_token_stride", C.c_int64), ("k1", vp), ("v1", vp),
+                ("kv1_batch_stride", C.c_int64), ("kv1_token_stride", C.c_int64),
+                ("kv1_tokens", C.c_int32), ("k2", vp), ("v2", vp),
+                ("kv2_batch_stride", C.c_int64), ("kv2_token_stride", C.c_int64),
+                ("kv2_tokens", C.c_int32), ("mask", vp), ("mask_row_stride", C.c_int64),
+                ("key_mask", vp), ("key_mask_batch_stride", C.c_int64),
+                ("first_frame_tokens", C.c_int32), ("kv_splits", C.c_int32), ("out", vp),
+                ("out_batch_stride", C.c_int64), ("out_token_stride", C.c_int64)]
+
+
+def declare_ops(lib) -> None:
+    lib.fam_attention_workspace_size.argtypes = [C.POINTER(AttentionDesc), C.POINTER(C.c_size_t)]
+    lib.fam_attention.argtypes = [C.POINTER(AttentionDesc), vp, C.c_size_t, vp]
+    for n in ("fam_attention_workspace_size", "fam_attention"):
+        getattr(lib, n).restype = C.c_int

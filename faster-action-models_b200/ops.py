@@ -90,3 +90,45 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
     d.out = out.data_ptr()
     check(lib().fam_gemm(C.byref(d), C.c_void_p(_stream())), "fam_gemm")
     return out
+
+
+def attention_desc(q, k1, v1, heads, k2=None, v2=None, mask=None, key_mask=None,
+                   first_frame_tokens: int = 0, kv_splits: int = 0, out=None):
+    """Descriptor for fam_attention over token-major [B, S, H*d] bf16 tensors."""
+    from ._abi import AttentionDesc
+    B, Sq, HD = q.shape
+    hd = HD // heads
+    if out is None:
+        out = torch.empty_like(q)
+    d = AttentionDesc()
+    d.batch, d.heads, d.head_dim, d.q_tokens = B, heads, hd, Sq
+    d.q, d.q_batch_stride, d.q_token_stride = q.data_ptr(), q.stride(0), q.stride(1)
+    d.k1, d.v1 = k1.data_ptr(), v1.data_ptr()
+    d.kv1_batch_stride, d.kv1_token_stride, d.kv1_tokens = k1.stride(0), k1.stride(1), k1.shape[1]
+    if k2 is not None:
+        d.k2, d.v2 = k2.data_ptr(), v2.data_ptr()
+        d.kv2_batch_stride, d.kv2_token_stride, d.kv2_tokens = k2.stride(0), k2.stride(1), k2.shape[1]
+    if mask is not None:
+        d.mask, d.mask_row_stride = mask.data_ptr(), mask.stride(0)
+    if key_mask is not None:
+        d.key_mask, d.key_mask_batch_stride = key_mask.data_ptr(), key_mask.stride(0)
+    d.first_frame_tokens, d.kv_splits = first_frame_tokens, kv_splits
+    d.out, d.out_batch_stride, d.out_token_stride = out.data_ptr(), out.stride(0), out.stride(1)
+    return d, out
+
+
+def attention(q, k1, v1, heads, k2=None, v2=None, mask=None, key_mask=None,
+              first_frame_tokens: int = 0, kv_splits: int = 0, out=None) -> torch.Tensor:
+    """Masked attention (flash_attention of wan_video_dit.py:13-22) through fam_attention.
+    Masks are uint8 (nonzero = attend); the caller keeps every tensor alive."""
+    for t in (q, k1, v1) + ((k2, v2) if k2 is not None else ()):
+        _require(t, torch.bfloat16, "attention operand")
+    d, out = attention_desc(q, k1, v1, heads, k2, v2, mask, key_mask, first_frame_tokens,
+                            kv_splits, out)
+    n = C.c_size_t()
+    check(lib().fam_attention_workspace_size(C.byref(d), C.byref(n)), "fam_attention_workspace_size")
+    ws = torch.empty(max(1, n.value), dtype=torch.uint8, device=q.device)
+    check(lib().fam_attention(C.byref(d), ws.data_ptr(), ws.numel(), C.c_void_p(_stream())),
+          "fam_attention")
+    out._fam_ws = ws  # keep the workspace alive until the caller drops the output
+    return out

@@ -104,6 +104,46 @@ typedef struct fam_gemm_desc {
 
 FAM_API int fam_gemm(const fam_gemm_desc* desc, void* stream);
 
+/* Masked multi-head attention, softmax(q k^T / sqrt(d)) v with a bool mask,
+ * over the concatenation of two key/value sources (source 2 may be empty).
+ * Replaces flash_attention / MoT._mixed_attention
+ * (FastWAM/src/fastwam/models/wan22/wan_video_dit.py:13-22, mot.py:88-103,
+ * 506-512, 560-566).  All tensors bf16, token-major with head h at columns
+ * [h * head_dim, (h + 1) * head_dim) of each row:
+ *   q[b * q_batch_stride + t * q_token_stride + h * head_dim + i]
+ * Keys j < kv1_tokens come from source 1, the rest from source 2.  A key is
+ * attended when mask[t * mask_row_stride + j] != 0 (NULL: all), key_mask
+ * [b * key_mask_batch_stride + j] != 0 (NULL: all) and, when
+ * first_frame_tokens > 0, queries t < first_frame_tokens see only keys
+ * j < first_frame_tokens.  head_dim is 64 or 128.  With several key splits
+ * the partial results go to the caller's workspace. */
+typedef struct fam_attention_desc {
+  int32_t batch, heads, head_dim, q_tokens;
+  const void* q;
+  int64_t q_batch_stride, q_token_stride;
+  const void* k1;
+  const void* v1;
+  int64_t kv1_batch_stride, kv1_token_stride;
+  int32_t kv1_tokens;
+  const void* k2;
+  const void* v2;
+  int64_t kv2_batch_stride, kv2_token_stride;
+  int32_t kv2_tokens;
+  const uint8_t* mask;
+  int64_t mask_row_stride;
+  const uint8_t* key_mask;
+  int64_t key_mask_batch_stride;
+  int32_t first_frame_tokens;
+  int32_t kv_splits; /* 0: chosen to fill the GPU */
+  void* out;
+  int64_t out_batch_stride, out_token_stride;
+} fam_attention_desc;
+
+FAM_API int fam_attention_workspace_size(const fam_attention_desc* desc, size_t* bytes);
+FAM_API int fam_attention(const fam_attention_desc* desc, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+
 /* ======================================================================
  * Action expert (ActionDiT + MoT action path) — BASELINE configs 1 and 3.
  *

@@ -1,0 +1,50 @@
+"""fam_attention (split-KV flash attention, two key sources, masks) against torch fp32 SDPA."""
+import pytest
+import torch
+
+from oracle import fam_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, heads, mask=None):
+    return O.flash_attention(q.float(), k.float(), v.float(), heads, mask)
+
+
+@pytest.mark.parametrize("B,H,hd,Sq,S1,S2,splits", [
+    (1, 16, 64, 32, 1760, 32, 0), (2, 4, 64, 8, 130, 8, 3), (1, 24, 128, 200, 200, 0, 1),
+    (2, 2, 128, 70, 300, 17, 0), (3, 4, 64, 32, 0, 40, 0)])
+def test_attention_matches_sdpa(fam_ops, B, H, hd, Sq, S1, S2, splits):
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + Sq + S1)
+    HD = H * hd
+    q = torch.randn(B, Sq, HD, device="cuda", generator=g).bfloat16()
+    k1 = torch.randn(B, max(S1, 1), HD, device="cuda", generator=g).bfloat16()[:, :S1]
+    v1 = torch.randn(B, max(S1, 1), HD, device="cuda", generator=g).bfloat16()[:, :S1]
+    k2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16() if S2 else None
+    v2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16() if S2 else None
+    mask = (torch.rand(Sq, S1 + S2, device="cuda", generator=g) > 0.3)
+    mask[:, -1] = True  # every query keeps at least one key
+    out = fam_ops.attention(q, k1, v1, H, k2, v2, mask=mask.to(torch.uint8), kv_splits=splits)
+    torch.cuda.synchronize()
+    kk = torch.cat([k1, k2], 1) if S2 else k1
+    vv = torch.cat([v1, v2], 1) if S2 else v1
+    ref = _ref(q, kk, vv, H, mask)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+def test_first_frame_causal_and_key_mask(fam_ops):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    B, H, hd, S, ff = 2, 4, 128, 300, 44
+    q = torch.randn(B, S, H * hd, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, S, H * hd, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, S, H * hd, device="cuda", generator=g).bfloat16()
+    out = fam_ops.attention(q, k, v, H, first_frame_tokens=ff)
+    ref = _ref(q, k, v, H, O.build_video_to_video_mask(S, ff).cuda())
+    assert (out.float() - ref).abs().max().item() < 2e-2
+    km = torch.ones(B, S, dtype=torch.uint8, device="cuda")
+    km[1, 250:] = 0
+    out2 = fam_ops.attention(q, k, v, H, key_mask=km)
+    ref2 = torch.cat([_ref(q[:1], k[:1], v[:1], H), _ref(q[1:], k[1:, :250], v[1:, :250], H)])
+    torch.cuda.synchronize()
+    assert (out2.float() - ref2).abs().max().item() < 2e-2
