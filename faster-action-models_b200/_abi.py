@@ -72,5 +72,6 @@ class AttentionDesc(C.Structure):
 def declare_ops(lib) -> None:
     lib.fam_attention_workspace_size.argtypes = [C.POINTER(AttentionDesc), C.POINTER(C.c_size_t)]
     lib.fam_attention.argtypes = [C.POINTER(AttentionDesc), vp, C.c_size_t, vp]
-    for n in ("fam_attention_workspace_size", "fam_attention"):
+    lib.fam_attention_static_scratch.argtypes = [C.POINTER(AttentionDesc), vp]
+    for n in ("fam_attention_workspace_size", "fam_attention", "fam_attention_static_scratch"):
         getattr(lib, n).restype = C.c_int

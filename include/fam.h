@@ -143,6 +143,16 @@ FAM_API int fam_attention_workspace_size(const fam_attention_desc* desc, size_t*
 FAM_API int fam_attention(const fam_attention_desc* desc, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* fam_attention for callers that cannot allocate device memory (an embedded
+ * plugin that does not own the process's allocator, a control loop that
+ * forbids allocation after start-up, an FFI host without a device
+ * allocator).  No counterpart in the reference: its PyTorch path allocates
+ * freely.  The split partials live in a static device array of 8 MiB per GPU
+ * (held by every GPU that loads the library until exit); calls needing more
+ * are rejected with FAM_ERR_INVALID.  Allocates nothing.  The first call on a
+ * device looks the array up and should precede any stream capture there.
+ * All calls on a device share the array: calls that overlap on the GPU race. */
+FAM_API int fam_attention_static_scratch(const fam_attention_desc* desc, void* stream);
 
 /* ======================================================================
  * Action expert (ActionDiT + MoT action path) — BASELINE configs 1 and 3.

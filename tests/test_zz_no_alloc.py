@@ -1,0 +1,60 @@
+"""fam_attention_static_scratch: the attention entry point for callers that cannot
+allocate device memory (a plugin that does not own its host process's allocator, a
+control loop that forbids allocation once running, an FFI host with no device
+allocator).  It must give the same result as fam_attention with a caller workspace,
+on two calls in a row (the second finds the first call's leftovers in the shared
+static scratch), and reject a problem larger than its fixed scratch.
+
+This file is collected last on purpose (tests/test_zz_*), and passes both alone in a
+fresh process and after the rest of the suite."""
+import ctypes as C
+import importlib
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ops = importlib.import_module("faster-action-models_b200.ops")
+_lib = importlib.import_module("faster-action-models_b200._lib")
+
+
+def _case(B, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    H, hd, Sq, S1, S2 = 16, 64, 32, 1760, 32
+    HD = H * hd
+    q = torch.randn(B, Sq, HD, device="cuda", generator=g).bfloat16()
+    k1 = torch.randn(B, S1, HD, device="cuda", generator=g).bfloat16()
+    v1 = torch.randn(B, S1, HD, device="cuda", generator=g).bfloat16()
+    k2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16()
+    v2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16()
+    mask = (torch.rand(Sq, S1 + S2, device="cuda", generator=g) > 0.2).to(torch.uint8)
+    mask[:, -1] = 1
+    return q, k1, v1, H, k2, v2, mask
+
+
+def test_static_scratch_matches_workspace_entry_point_twice():
+    lib = _lib.lib()
+    for call, seed in ((0, 11), (1, 12)):
+        q, k1, v1, H, k2, v2, mask = _case(2, seed)
+        ref = ops.attention(q, k1, v1, H, k2, v2, mask=mask)
+        d, out = ops.attention_desc(q, k1, v1, H, k2, v2, mask=mask)
+        n = C.c_size_t()
+        _lib.check(lib.fam_attention_workspace_size(C.byref(d), C.byref(n)), "workspace size")
+        assert n.value > 0, "the case must use split scratch"
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.fam_attention_static_scratch(C.byref(d), C.c_void_p(stream)),
+                   "fam_attention_static_scratch")
+        torch.cuda.synchronize()
+        err = (out.float() - ref.float()).abs().max().item()
+        assert err <= 2e-2, f"call {call}: max|d| {err}"
+
+
+def test_static_scratch_rejects_oversized_problem():
+    lib = _lib.lib()
+    q, k1, v1, H, k2, v2, mask = _case(4, 13)
+    # 28 key splits x 4 batches x 16 heads of partials: ~30 MB, beyond the 8 MiB array
+    d, out = ops.attention_desc(q, k1, v1, H, k2, v2, mask=mask, kv_splits=28)
+    rc = lib.fam_attention_static_scratch(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 1  # FAM_ERR_INVALID
+    assert "scratch" in _lib.last_error()
