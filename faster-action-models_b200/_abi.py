@@ -49,6 +49,7 @@ def declare(lib) -> None:
         getattr(lib, n).restype = C.c_int
     declare_counts(lib)
     declare_ops(lib)
+    declare_cae(lib)
 
 
 def declare_counts(lib) -> None:
@@ -74,4 +75,52 @@ def declare_ops(lib) -> None:
     lib.fam_attention.argtypes = [C.POINTER(AttentionDesc), vp, C.c_size_t, vp]
     lib.fam_attention_static_scratch.argtypes = [C.POINTER(AttentionDesc), vp]
     for n in ("fam_attention_workspace_size", "fam_attention", "fam_attention_static_scratch"):
+        getattr(lib, n).restype = C.c_int
+
+
+fp = C.c_void_p  # const float* (device)
+
+
+class CaeLayer(C.Structure):
+    _fields_ = [(n, fp) for n in (
+        "modulation", "qkv_w", "qkv_b", "norm_q", "norm_k", "o_w", "o_b", "norm3_w", "norm3_b",
+        "cq_w", "cq_b", "cnorm_q", "cnorm_k", "ckv_w", "ckv_b", "co_w", "co_b", "ffn0_w",
+        "ffn0_b", "ffn2_w", "ffn2_b")]
+
+
+class CaeWeights(C.Structure):
+    _fields_ = [(n, fp) for n in (
+        "enc_w", "enc_b", "text0_w", "text0_b", "text2_w", "text2_b", "time0_w", "time0_b",
+        "time2_w", "time2_b", "tproj_w", "tproj_b", "head_w", "head_b")] + [
+        ("layers", C.POINTER(CaeLayer)), ("rope", fp), ("rope_positions", C.c_int32)]
+
+
+class DecoderConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("action_dim", "action_horizon", "num_tokens",
+                                         "latent_dim", "hidden", "num_suites")]
+
+
+class DecoderStage(C.Structure):
+    _fields_ = [(n, fp) for n in ("convt_w", "convt_b", "gn0_w", "gn0_b", "c1_w", "c1_b",
+                                  "gn1_w", "gn1_b", "c2_w", "c2_b", "gn2_w", "gn2_b")] + [
+        ("stride", C.c_int32)]
+
+
+class DecoderWeights(C.Structure):
+    _fields_ = [("in_w", fp), ("in_b", fp), ("out_w", fp), ("out_b", fp), ("suite_embed", fp),
+                ("stages", C.POINTER(DecoderStage)), ("num_stages", C.c_int32)]
+
+
+def declare_cae(lib) -> None:
+    i32, sz = C.c_int32, C.c_size_t
+    lib.fam_cae_workspace_size.argtypes = [C.POINTER(ActionConfig), i32, i32, C.POINTER(sz)]
+    lib.fam_cae_chunk.argtypes = [C.POINTER(ActionConfig), C.POINTER(CaeWeights), i32, i32, vp,
+                                  i32, i32, vp, vp, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                  i32, vp, vp, sz, vp]
+    lib.fam_decoder_workspace_size.argtypes = [C.POINTER(DecoderConfig), C.POINTER(DecoderWeights),
+                                               i32, C.POINTER(sz)]
+    lib.fam_action_decode.argtypes = [C.POINTER(DecoderConfig), C.POINTER(DecoderWeights), i32,
+                                      vp, vp, vp, vp, sz, vp]
+    for n in ("fam_cae_workspace_size", "fam_cae_chunk", "fam_decoder_workspace_size",
+              "fam_action_decode"):
         getattr(lib, n).restype = C.c_int

@@ -68,7 +68,7 @@ WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
   const int nsplit_joint = 8;  // upper bound used for the partial buffer
   size_t apart = attn_partial_bytes(B, c.num_heads, Sa, c.head_dim, 64);
   (void)nsplit_joint;
-  const int q_tiles = (Sa + 63) / 64;
+  const int q_tiles = attn_query_tiles(Sa);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
@@ -306,13 +306,8 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     aa.part = wsp<float>(c, c.L.apart);
     aa.counters = wsp<int>(c, c.L.ctr);
     const int skv = io.video_tokens + Sa;
-    aa.keys_per_split = 256;
-    aa.nsplit = (skv + 255) / 256;
-    if (aa.nsplit > 64) {
-      aa.nsplit = 64;
-      aa.keys_per_split = ((skv + 63) / 64 + 63) / 64 * 64;
-      aa.nsplit = (skv + aa.keys_per_split - 1) / aa.keys_per_split;
-    }
+    aa.nsplit = attn_auto_splits(io.batch * g.num_heads * attn_query_tiles(Sa), skv,
+                                 &aa.keys_per_split);
     aa.status = c.e->status;
     FAM_LAUNCH(launch_attention(aa, io.batch, g.head_dim, c.st, c.pdl));
 
@@ -451,7 +446,7 @@ int validate_io(const fam_action_expert* e, const fam_action_io* io, int N) {
 int enqueue_chunk(const Ctx& c, void* latent, const float* ts, const float* ds, int N, void* trace) {
   c.e->launch_count = 0;
   const size_t ctr_bytes = static_cast<size_t>(c.io->batch) * c.e->cfg.num_heads *
-                           ((c.io->action_tokens + 63) / 64) * 4;
+                           attn_query_tiles(c.io->action_tokens) * 4;
   FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
   FAM_TRYI(enqueue_prologue(c, ts, N));
   const size_t vel_elems = static_cast<size_t>(c.rows) * c.e->cfg.action_dim;
@@ -591,7 +586,7 @@ int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* io, const
   c.crow = io->batch * io->context_tokens;
   c.st = static_cast<cudaStream_t>(stream);
   c.pdl = true;
-  const size_t ctr_bytes = static_cast<size_t>(io->batch) * e->cfg.num_heads * ((io->action_tokens + 63) / 64) * 4;
+  const size_t ctr_bytes = static_cast<size_t>(io->batch) * e->cfg.num_heads * attn_query_tiles(io->action_tokens) * 4;
   e->launch_count = 0;
   FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
   FAM_TRYI(enqueue_prologue(c, &timestep, 1));

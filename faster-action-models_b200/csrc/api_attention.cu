@@ -23,19 +23,18 @@ int attention_prepare(const fam_attention_desc* d, AttnArgs* a, AttnScratch* s) 
   if ((d->q_token_stride | d->kv1_token_stride | d->kv2_token_stride | d->out_token_stride) & 7)
     return set_error("attention: token strides must be multiples of 8 elements");
   const int skv = d->kv1_tokens + d->kv2_tokens;
-  const int q_tiles = (d->q_tokens + 63) / 64;
+  const int q_tiles = attn_query_tiles(d->q_tokens);
   const int units = d->batch * d->heads * q_tiles;
   int splits = d->kv_splits;
-  if (splits <= 0) {  // fill ~two waves of 148 SMs, >= 128 keys per split
-    splits = (296 + units - 1) / units;
-    const int max_by_keys = (skv + 127) / 128;
-    if (splits > max_by_keys) splits = max_by_keys;
-    if (splits < 1) splits = 1;
+  int kps = 0;
+  if (splits <= 0) {
+    splits = attn_auto_splits(units, skv, &kps);
+  } else {
+    if (splits > 64) splits = 64;
+    kps = (skv + splits - 1) / splits;
+    kps = (kps + 63) / 64 * 64;
+    splits = (skv + kps - 1) / kps;
   }
-  if (splits > 64) splits = 64;
-  int kps = (skv + splits - 1) / splits;
-  kps = (kps + 63) / 64 * 64;
-  splits = (skv + kps - 1) / kps;
   *a = AttnArgs{};
   a->q = static_cast<const __nv_bfloat16*>(d->q);
   a->q_bs = d->q_batch_stride;

@@ -1,0 +1,168 @@
+// C ABI of the compact action expert (fam_cae_*) and the Action-VAE decoder.
+#include <string.h>
+
+#include "../../include/fam.h"
+#include "fam_cae.h"
+#include "fam_internal.h"
+
+using namespace fam;
+
+namespace {
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+size_t cae_ws(const fam_action_config& c, int B, int C) {
+  const size_t kv = static_cast<size_t>(c.num_layers) * B * C * c.num_heads * c.head_dim * sizeof(float);
+  return 2 * align256(kv);
+}
+
+int check_cae(const fam_action_config* c) {
+  if (c == nullptr) return set_error("cae: null config");
+  const int HD = c->num_heads * c->head_dim;
+  if (c->hidden_dim > kCaeMaxD || HD > kCaeMaxHD || c->head_dim > kCaeMaxHd || c->head_dim % 2 ||
+      c->ffn_dim > kCaeMaxF || c->num_layers > kCaeMaxLayers || c->num_layers <= 0 ||
+      c->action_dim > 64 || c->freq_dim > 256 || c->freq_dim % 2)
+    return set_error("cae: configuration exceeds the compact-expert limits (hidden<=64, H*d<=64, "
+                     "d<=32, ffn<=256, blocks<=32, action<=64, freq<=256)");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fam_cae_workspace_size(const fam_action_config* cfg, int32_t batch, int32_t context_tokens,
+                           size_t* bytes) {
+  int rc = check_cae(cfg);
+  if (rc) return rc;
+  if (bytes == nullptr || batch <= 0 || context_tokens < 0) return set_error("cae: bad sizes");
+  *bytes = cae_ws(*cfg, batch, context_tokens > 0 ? context_tokens : 1);
+  return FAM_OK;
+}
+
+int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch,
+                  int32_t tokens, const void* context, int32_t context_bf16, int32_t context_tokens,
+                  const uint8_t* context_mask, float* latent, const float* timesteps,
+                  const float* deltas, int32_t num_steps, float* velocity_trace, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  int rc = check_cae(cfg);
+  if (rc) return rc;
+  if (w == nullptr || w->layers == nullptr || latent == nullptr || timesteps == nullptr ||
+      deltas == nullptr)
+    return set_error("cae: null argument");
+  if (batch <= 0 || tokens <= 0 || tokens > kCaeMaxS) return set_error("cae: tokens must be in [1, %d]", kCaeMaxS);
+  if (num_steps <= 0 || num_steps > kMaxSteps) return set_error("cae: num_steps must be in [1, %d]", kMaxSteps);
+  if (context_tokens <= 0 || context == nullptr) return set_error("cae: a context is required");
+  if (w->rope == nullptr || w->rope_positions < tokens) return set_error("cae: RoPE table too short");
+  const size_t need = cae_ws(*cfg, batch, context_tokens);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error("cae: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  const int HD = cfg->num_heads * cfg->head_dim;
+  const size_t kv_bytes = align256(static_cast<size_t>(cfg->num_layers) * batch * context_tokens * HD * sizeof(float));
+  float* ctx_k = static_cast<float*>(workspace);
+  float* ctx_v = reinterpret_cast<float*>(static_cast<char*>(workspace) + kv_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  CaeCtxArgs ca;
+  memset(&ca, 0, sizeof(ca));
+  if (context_bf16)
+    ca.ctx_bf16 = static_cast<const __nv_bfloat16*>(context);
+  else
+    ca.ctx_f32 = static_cast<const float*>(context);
+  ca.rows = batch * context_tokens;
+  ca.T = cfg->text_dim;
+  ca.D = cfg->hidden_dim;
+  ca.HD = HD;
+  ca.L = cfg->num_layers;
+  ca.text0_w = w->text0_w;
+  ca.text0_b = w->text0_b;
+  ca.text2_w = w->text2_w;
+  ca.text2_b = w->text2_b;
+  for (int l = 0; l < cfg->num_layers; ++l) ca.layers[l] = w->layers[l];
+  ca.ctx_k = ctx_k;
+  ca.ctx_v = ctx_v;
+  ca.eps = cfg->eps;
+  rc = check_cuda(launch_cae_context(ca, st, false), "cae context launch");
+  if (rc) return rc;
+
+  CaeStepArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.w.enc_w = w->enc_w;
+  sa.w.enc_b = w->enc_b;
+  sa.w.text0_w = w->text0_w;
+  sa.w.text0_b = w->text0_b;
+  sa.w.text2_w = w->text2_w;
+  sa.w.text2_b = w->text2_b;
+  sa.w.time0_w = w->time0_w;
+  sa.w.time0_b = w->time0_b;
+  sa.w.time2_w = w->time2_w;
+  sa.w.time2_b = w->time2_b;
+  sa.w.tproj_w = w->tproj_w;
+  sa.w.tproj_b = w->tproj_b;
+  sa.w.head_w = w->head_w;
+  sa.w.head_b = w->head_b;
+  for (int l = 0; l < cfg->num_layers; ++l) sa.w.layers[l] = w->layers[l];
+  sa.rope = w->rope;
+  sa.ctx_k = ctx_k;
+  sa.ctx_v = ctx_v;
+  sa.ctx_mask = context_mask;
+  sa.latent = latent;
+  sa.trace = velocity_trace;
+  for (int i = 0; i < num_steps; ++i) {
+    sa.timesteps.t[i] = timesteps[i];
+    sa.deltas.t[i] = deltas[i];
+  }
+  sa.num_steps = num_steps;
+  sa.B = batch;
+  sa.S = tokens;
+  sa.A = cfg->action_dim;
+  sa.D = cfg->hidden_dim;
+  sa.HD = HD;
+  sa.hd = cfg->head_dim;
+  sa.F = cfg->ffn_dim;
+  sa.C = context_tokens;
+  sa.L = cfg->num_layers;
+  sa.freq_dim = cfg->freq_dim;
+  sa.eps = cfg->eps;
+  return check_cuda(launch_cae_steps(sa, st, true), "cae steps launch");
+}
+
+int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_decoder_weights* w,
+                               int32_t batch, size_t* bytes) {
+  if (cfg == nullptr || w == nullptr || bytes == nullptr || batch <= 0) return set_error("decoder: bad argument");
+  if (w->num_stages > kDecMaxStages) return set_error("decoder: at most %d stages", kDecMaxStages);
+  *bytes = 3 * align256(decoder_scratch_floats(*cfg, w->stages, w->num_stages, batch) * sizeof(float));
+  return FAM_OK;
+}
+
+int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_weights* w, int32_t batch,
+                      const float* z, const int32_t* suite_ids, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  size_t need = 0;
+  int rc = fam_decoder_workspace_size(cfg, w, batch, &need);
+  if (rc) return rc;
+  if (z == nullptr || out == nullptr) return set_error("decoder: null z/out");
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error("decoder: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  DecArgs a;
+  memset(&a, 0, sizeof(a));
+  a.cfg = *cfg;
+  a.in_w = w->in_w;
+  a.in_b = w->in_b;
+  a.out_w = w->out_w;
+  a.out_b = w->out_b;
+  a.suite_embed = w->suite_embed;
+  for (int i = 0; i < w->num_stages; ++i) a.stages[i] = w->stages[i];
+  a.num_stages = w->num_stages;
+  a.z = z;
+  a.suite_ids = suite_ids;
+  a.out = out;
+  const size_t part = need / 3;
+  a.buf0 = static_cast<float*>(workspace);
+  a.buf1 = reinterpret_cast<float*>(static_cast<char*>(workspace) + part);
+  a.buf2 = reinterpret_cast<float*>(static_cast<char*>(workspace) + 2 * part);
+  a.B = batch;
+  return check_cuda(launch_action_decoder(a, static_cast<cudaStream_t>(stream)), "decoder launch");
+}
+
+}  // extern "C"

@@ -1,14 +1,15 @@
 // Masked flash attention for the DiT blocks (SDPA with a bool mask, scale
 // 1/sqrt(d): FastWAM/src/fastwam/models/wan22/wan_video_dit.py:13-22).
 //
-// One CTA = 4 warps = a 64-query tile of one (batch, head), over one split of
-// the key range.  Keys come from up to two token-major sources: the cached
-// video K/V of the layer and the fresh K/V of the current tokens (the joint
-// attention of mot.py:560-566 concatenates exactly these two).  K/V blocks of
-// 64 keys stream through a double-buffered shared-memory ring with cp.async;
+// One CTA = WARPS warps = a (16 x WARPS)-query tile of one (batch, head), over
+// one split of the key range.  Keys come from up to two token-major sources:
+// the cached video K/V of the layer and the fresh K/V of the current tokens
+// (the joint attention of mot.py:560-566 concatenates exactly these two).
+// K/V blocks of 64 keys stream through a double-buffered shared-memory ring
+// with cp.async; the block's attend/ignore bits are staged next to them.
 // QK^T and PV run on bf16 mma.sync tensor-core fragments with an fp32 online
-// softmax in exp2 form.  With several key splits (decode-style, few queries,
-// long cache) every split writes an unnormalised partial (O, m, l) and the
+// softmax in exp2 form.  With several key splits (decode-style: few queries,
+// a long cache) every split writes an unnormalised partial (O, m, l) and the
 // last CTA to arrive for a (batch, head, query tile) merges them in split
 // order (deterministic) and resets its arrival counter.
 //
@@ -21,15 +22,16 @@
 
 namespace fam {
 
-constexpr int kAttnWarps = 4;
-constexpr int kAttnQTile = 16 * kAttnWarps;  // 64 queries
-constexpr int kAttnKB = 64;                  // keys per block
+constexpr int kAttnKB = 64;  // keys per block
 
-template <int HD>
-struct AttnSmem {
-  static constexpr int kRow = HD + 8;  // padded row (bank-conflict free fragment loads)
+template <int HD, int WARPS>
+struct AttnCfg {
+  static constexpr int kQTile = 16 * WARPS;
+  static constexpr int kRow = HD + 8;  // padded row: conflict-free fragment loads
   static constexpr int kBlockElems = kAttnKB * kRow;
-  static constexpr int kBytes = 2 /*stages*/ * 2 /*K,V*/ * kBlockElems * 2;
+  static constexpr int kKVBytes = 2 /*stages*/ * 2 /*K,V*/ * kBlockElems * 2;
+  static constexpr int kMaskBytes = 2 /*stages*/ * kQTile * kAttnKB;
+  static constexpr int kBytes = kKVBytes + kMaskBytes;
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
@@ -57,7 +59,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Key j of (b, h): pointer to its K (or V) row slice, or null past the end.
+// Key j of (b, h): pointer to its K (or V) row slice.
 __device__ __forceinline__ const __nv_bfloat16* kv_row(const AttnArgs& a, bool is_v, int b, int h,
                                                        int j, int hd) {
   if (j < a.S1) {
@@ -65,32 +67,51 @@ __device__ __forceinline__ const __nv_bfloat16* kv_row(const AttnArgs& a, bool i
     return base + b * a.kv1_bs + static_cast<long long>(j) * a.kv1_ts + h * hd;
   }
   j -= a.S1;
-  if (j < a.S2) {
-    const __nv_bfloat16* base = is_v ? a.v2 : a.k2;
-    return base + b * a.kv2_bs + static_cast<long long>(j) * a.kv2_ts + h * hd;
-  }
-  return nullptr;
+  const __nv_bfloat16* base = is_v ? a.v2 : a.k2;
+  return base + b * a.kv2_bs + static_cast<long long>(j) * a.kv2_ts + h * hd;
 }
 
-template <int HD>
+template <int HD, int WARPS>
 __device__ __forceinline__ void load_kv_block(const AttnArgs& a, __nv_bfloat16* sk,
                                               __nv_bfloat16* sv, int b, int h, int j0, int j_end) {
+  using Cfg = AttnCfg<HD, WARPS>;
   constexpr int kChunks = HD / 8;  // 16-byte chunks per row
   for (int idx = threadIdx.x; idx < kAttnKB * kChunks; idx += blockDim.x) {
     const int r = idx / kChunks, c = idx % kChunks;
     const int j = j0 + r;
     const bool valid = j < j_end;
-    const __nv_bfloat16* kp = valid ? kv_row(a, false, b, h, j, HD) : nullptr;
-    const __nv_bfloat16* vp = valid ? kv_row(a, true, b, h, j, HD) : nullptr;
-    cp_async16(sk + r * AttnSmem<HD>::kRow + c * 8, valid ? kp + c * 8 : a.q, valid);
-    cp_async16(sv + r * AttnSmem<HD>::kRow + c * 8, valid ? vp + c * 8 : a.q, valid);
+    const __nv_bfloat16* kp = valid ? kv_row(a, false, b, h, j, HD) + c * 8 : a.q;
+    const __nv_bfloat16* vp = valid ? kv_row(a, true, b, h, j, HD) + c * 8 : a.q;
+    cp_async16(sk + r * Cfg::kRow + c * 8, kp, valid);
+    cp_async16(sv + r * Cfg::kRow + c * 8, vp, valid);
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnArgs a) {
+// attend bits of the (query tile, key block): 1 = attend.
+template <int HD, int WARPS>
+__device__ __forceinline__ void stage_mask(const AttnArgs& a, uint8_t* sm, int b, int q0, int j0,
+                                           int j_end) {
+  using Cfg = AttnCfg<HD, WARPS>;
+  const uint8_t* km = a.key_mask != nullptr ? a.key_mask + b * a.key_mask_bs : nullptr;
+  const int ff = a.first_frame_tokens;
+  for (int idx = threadIdx.x; idx < Cfg::kQTile * kAttnKB; idx += blockDim.x) {
+    const int qi = idx / kAttnKB, jj = idx % kAttnKB;
+    const int q = q0 + qi, j = j0 + jj;
+    bool ok = j < j_end && q < a.Sq;
+    if (ok && ff > 0 && q < ff) ok = j < ff;
+    if (ok && km != nullptr) ok = km[j] != 0;
+    if (ok && a.mask2d != nullptr) ok = a.mask2d[static_cast<long long>(q) * a.mask_rs + j] != 0;
+    sm[idx] = ok ? 1 : 0;
+  }
+}
+
+template <int HD, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a) {
+  using Cfg = AttnCfg<HD, WARPS>;
+  constexpr int QT = Cfg::kQTile;
   extern __shared__ __align__(16) uint8_t attn_smem[];
   __nv_bfloat16* smem = reinterpret_cast<__nv_bfloat16*>(attn_smem);
+  uint8_t* smask = attn_smem + Cfg::kKVBytes;
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,12 +119,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
   const int h = blockIdx.y, b = blockIdx.z;
   const int split = blockIdx.x % a.nsplit;
   const int qt = blockIdx.x / a.nsplit;
-  const int q_tiles = (a.Sq + kAttnQTile - 1) / kAttnQTile;
+  const int q_tiles = (a.Sq + QT - 1) / QT;
   const int skv = a.S1 + a.S2;
   const int k_begin = split * a.keys_per_split;
   const int k_end = min(skv, k_begin + a.keys_per_split);
-  const int qw0 = qt * kAttnQTile + warp * 16;  // first query of this warp
-  const int qr0 = qw0 + g, qr1 = qw0 + g + 8;   // the two rows this thread owns
+  const int q0 = qt * QT;
+  const int qr0 = q0 + warp * 16 + g, qr1 = qr0 + 8;  // the two rows this thread owns
+  const bool has_mask = a.mask2d != nullptr || a.key_mask != nullptr || a.first_frame_tokens > 0;
 
   pdl_wait();
   pdl_launch_dependents();
@@ -112,14 +134,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
   constexpr int KS = HD / 16;
   uint32_t qf[KS][4];
   {
-    const __nv_bfloat16* q0 = a.q + b * a.q_bs + static_cast<long long>(min(qr0, a.Sq - 1)) * a.q_ts + h * HD;
-    const __nv_bfloat16* q1 = a.q + b * a.q_bs + static_cast<long long>(min(qr1, a.Sq - 1)) * a.q_ts + h * HD;
+    const __nv_bfloat16* qa = a.q + b * a.q_bs + static_cast<long long>(min(qr0, a.Sq - 1)) * a.q_ts + h * HD;
+    const __nv_bfloat16* qb = a.q + b * a.q_bs + static_cast<long long>(min(qr1, a.Sq - 1)) * a.q_ts + h * HD;
 #pragma unroll
     for (int kk = 0; kk < KS; ++kk) {
-      qf[kk][0] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 2 * t);
-      qf[kk][1] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 2 * t);
-      qf[kk][2] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 8 + 2 * t);
-      qf[kk][3] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 8 + 2 * t);
+      qf[kk][0] = *reinterpret_cast<const uint32_t*>(qa + kk * 16 + 2 * t);
+      qf[kk][1] = *reinterpret_cast<const uint32_t*>(qb + kk * 16 + 2 * t);
+      qf[kk][2] = *reinterpret_cast<const uint32_t*>(qa + kk * 16 + 8 + 2 * t);
+      qf[kk][3] = *reinterpret_cast<const uint32_t*>(qb + kk * 16 + 8 + 2 * t);
     }
   }
 
@@ -130,36 +152,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
   const int nblocks = k_end > k_begin ? (k_end - k_begin + kAttnKB - 1) / kAttnKB : 0;
-  __nv_bfloat16* sK[2] = {smem, smem + 2 * AttnSmem<HD>::kBlockElems};
-  __nv_bfloat16* sV[2] = {smem + AttnSmem<HD>::kBlockElems, smem + 3 * AttnSmem<HD>::kBlockElems};
+  __nv_bfloat16* sK[2] = {smem, smem + 2 * Cfg::kBlockElems};
+  __nv_bfloat16* sV[2] = {smem + Cfg::kBlockElems, smem + 3 * Cfg::kBlockElems};
+  uint8_t* sM[2] = {smask, smask + QT * kAttnKB};
 
-  // Row-level key limits of the first-frame-causal rule.
-  const int ff = a.first_frame_tokens;
-  const int lim0 = (ff > 0 && qr0 < ff) ? ff : skv;
-  const int lim1 = (ff > 0 && qr1 < ff) ? ff : skv;
-  const uint8_t* km = a.key_mask != nullptr ? a.key_mask + b * a.key_mask_bs : nullptr;
-  const uint8_t* mr0 = a.mask2d != nullptr ? a.mask2d + static_cast<long long>(min(qr0, a.Sq - 1)) * a.mask_rs : nullptr;
-  const uint8_t* mr1 = a.mask2d != nullptr ? a.mask2d + static_cast<long long>(min(qr1, a.Sq - 1)) * a.mask_rs : nullptr;
-
-  if (nblocks > 0) load_kv_block<HD>(a, sK[0], sV[0], b, h, k_begin, k_end);
+  if (nblocks > 0) {
+    load_kv_block<HD, WARPS>(a, sK[0], sV[0], b, h, k_begin, k_end);
+    if (has_mask) stage_mask<HD, WARPS>(a, sM[0], b, q0, k_begin, k_end);
+  }
   cp_async_commit();
   for (int blk = 0; blk < nblocks; ++blk) {
     const int cur = blk & 1;
-    if (blk + 1 < nblocks)
-      load_kv_block<HD>(a, sK[cur ^ 1], sV[cur ^ 1], b, h, k_begin + (blk + 1) * kAttnKB, k_end);
+    const int j0 = k_begin + blk * kAttnKB;
+    if (blk + 1 < nblocks) {
+      load_kv_block<HD, WARPS>(a, sK[cur ^ 1], sV[cur ^ 1], b, h, j0 + kAttnKB, k_end);
+      if (has_mask) stage_mask<HD, WARPS>(a, sM[cur ^ 1], b, q0, j0 + kAttnKB, k_end);
+    }
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
 
     const __nv_bfloat16* K = sK[cur];
     const __nv_bfloat16* V = sV[cur];
-    const int j0 = k_begin + blk * kAttnKB;
+    const uint8_t* M = sM[cur];
     // S = Q K^T for 64 keys: 8 tiles of 8 keys.
     float s[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
-      const __nv_bfloat16* kr = K + (n * 8 + g) * AttnSmem<HD>::kRow;
+      const __nv_bfloat16* kr = K + (n * 8 + g) * Cfg::kRow;
 #pragma unroll
       for (int kk = 0; kk < KS; ++kk) {
         uint32_t bf[2];
@@ -170,15 +191,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
     }
     // scale + mask, row max
     float mx0 = -INFINITY, mx1 = -INFINITY;
+    const int r0 = warp * 16 + g, r1 = r0 + 8;  // rows inside the tile
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int j = j0 + n * 8 + 2 * t + e;
-        bool ok = j < k_end;
-        if (ok && km != nullptr) ok = km[j] != 0;
-        bool ok0 = ok && j < lim0 && qr0 < a.Sq && (mr0 == nullptr || mr0[j] != 0);
-        bool ok1 = ok && j < lim1 && qr1 < a.Sq && (mr1 == nullptr || mr1[j] != 0);
+        const int jj = n * 8 + 2 * t + e;
+        bool ok0, ok1;
+        if (has_mask) {
+          ok0 = M[r0 * kAttnKB + jj] != 0;
+          ok1 = M[r1 * kAttnKB + jj] != 0;
+        } else {
+          const bool kv_ok = j0 + jj < k_end;
+          ok0 = kv_ok && qr0 < a.Sq;
+          ok1 = kv_ok && qr1 < a.Sq;
+        }
         s[n][e] = ok0 ? s[n][e] * a.scale_log2 : -INFINITY;
         s[n][2 + e] = ok1 ? s[n][2 + e] * a.scale_log2 : -INFINITY;
         mx0 = fmaxf(mx0, s[n][e]);
@@ -223,7 +250,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
       for (int i = 0; i < NT; ++i) {
         uint32_t bf[2];
         const int r = ks * 16 + (lane & 15);
-        const uint32_t addr = smem_u32(V + r * AttnSmem<HD>::kRow + i * 8);
+        const uint32_t addr = smem_u32(V + r * Cfg::kRow + i * 8);
         asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
                      : "=r"(bf[0]), "=r"(bf[1])
                      : "r"(addr));
@@ -255,12 +282,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
     return;
   }
 
-  // ---- split-K partials + last-arriving-CTA merge
-  const int Sq_pad = q_tiles * kAttnQTile;
+  // ---- split partials + last-arriving-CTA merge
+  const int Sq_pad = q_tiles * QT;
   const long long unit = (static_cast<long long>(b) * a.H + h) * a.nsplit;  // (b, h) base
+  const long long ml_base = static_cast<long long>(gridDim.z) * a.H * a.nsplit * Sq_pad * HD;
   float* po = a.part + (unit + split) * Sq_pad * HD;
-  float* pml = a.part + static_cast<long long>(gridDim.z) * a.H * a.nsplit * Sq_pad * HD +
-               (unit + split) * Sq_pad * 2;
+  float* pml = a.part + ml_base + (unit + split) * Sq_pad * 2;
 #pragma unroll
   for (int i = 0; i < NT; ++i) {
     const int d = i * 8 + 2 * t;
@@ -278,76 +305,122 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const AttnAr
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // Merge: thread handles (query, dim-pair) items of this query tile.
+  // Merge in two passes over smem (the K/V ring is free now): per query the
+  // split weights exp2(m_s - M) / L, then every output element as an
+  // independent weighted sum over splits.
+  float* wsm = reinterpret_cast<float*>(attn_smem);  // [QT][nsplit]
   const float* po0 = a.part + unit * Sq_pad * HD;
-  const float* pml0 = a.part + static_cast<long long>(gridDim.z) * a.H * a.nsplit * Sq_pad * HD + unit * Sq_pad * 2;
-  for (int idx = threadIdx.x; idx < kAttnQTile * (HD / 2); idx += blockDim.x) {
-    const int ql = idx / (HD / 2);
-    const int d = (idx % (HD / 2)) * 2;
-    const int q = qt * kAttnQTile + ql;
-    if (q >= a.Sq) continue;
+  const float* pml0 = a.part + ml_base + unit * Sq_pad * 2;
+  for (int ql = threadIdx.x; ql < QT; ql += blockDim.x) {
+    const int q = q0 + ql;
     float M = -INFINITY;
     for (int s2 = 0; s2 < a.nsplit; ++s2) M = fmaxf(M, __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2));
     const float base = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+    float L = 0.0f;
     for (int s2 = 0; s2 < a.nsplit; ++s2) {
-      const float ms = __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2);
-      const float ls = __ldcg(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2 + 1);
-      const float w = exp2f(ms - base);
-      L += w * ls;
-      const float2 ov = __ldcg(reinterpret_cast<const float2*>(po0 + (static_cast<long long>(s2) * Sq_pad + q) * HD + d));
-      acc0 += w * ov.x;
-      acc1 += w * ov.y;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(pml0 + (static_cast<long long>(s2) * Sq_pad + q) * 2));
+      const float w = exp2f(ml.x - base);
+      wsm[ql * a.nsplit + s2] = w;
+      L += w * ml.y;
     }
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    *reinterpret_cast<uint32_t*>(a.out + b * a.out_bs + static_cast<long long>(q) * a.out_ts + h * HD + d) =
-        pack_bf16(acc0 * inv, acc1 * inv);
+    for (int s2 = 0; s2 < a.nsplit; ++s2) wsm[ql * a.nsplit + s2] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < QT * (HD / 4); idx += blockDim.x) {
+    const int ql = idx / (HD / 4);
+    const int d = (idx % (HD / 4)) * 4;
+    const int q = q0 + ql;
+    if (q >= a.Sq) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* wq = wsm + ql * a.nsplit;
+#pragma unroll 4
+    for (int s2 = 0; s2 < a.nsplit; ++s2) {
+      const float4 ov = __ldcg(reinterpret_cast<const float4*>(po0 + (static_cast<long long>(s2) * Sq_pad + q) * HD + d));
+      const float w = wq[s2];
+      acc.x += w * ov.x;
+      acc.y += w * ov.y;
+      acc.z += w * ov.z;
+      acc.w += w * ov.w;
+    }
+    uint2 pk;
+    pk.x = pack_bf16(acc.x, acc.y);
+    pk.y = pack_bf16(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(a.out + b * a.out_bs + static_cast<long long>(q) * a.out_ts + h * HD + d) = pk;
   }
   if (threadIdx.x == 0) *ctr = 0;  // ready for the next launch
 }
 
+// Query-tile width used for a launch: 32 queries for small query counts (the
+// action tokens), 64 otherwise.
+static int attn_warps(int Sq) { return Sq <= 32 ? 2 : 4; }
+
 size_t attn_partial_bytes(int B, int H, int Sq, int head_dim, int nsplit) {
   if (nsplit <= 1) return 0;
-  const int q_tiles = (Sq + kAttnQTile - 1) / kAttnQTile;
-  const size_t Sq_pad = static_cast<size_t>(q_tiles) * kAttnQTile;
+  const int qt = 16 * attn_warps(Sq);
+  const size_t Sq_pad = static_cast<size_t>((Sq + qt - 1) / qt) * qt;
   return static_cast<size_t>(B) * H * nsplit * Sq_pad * (head_dim + 2) * sizeof(float);
 }
 
-template <int HD>
-static cudaError_t launch_attn_hd(const AttnArgs& a, int B, cudaStream_t st, bool pdl) {
-  constexpr int smem = AttnSmem<HD>::kBytes;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  const int q_tiles = (a.Sq + kAttnQTile - 1) / kAttnQTile;
+int attn_query_tiles(int Sq) {
+  const int qt = 16 * attn_warps(Sq);
+  return (Sq + qt - 1) / qt;
+}
+
+int attn_auto_splits(int units, int skv, int* keys_per_split) {
+  int splits = (296 + units - 1) / units;
+  const int max_by_keys = (skv + 127) / 128;
+  if (splits > max_by_keys) splits = max_by_keys;
+  if (splits < 1) splits = 1;
+  if (splits > 64) splits = 64;
+  int kps = (skv + splits - 1) / splits;
+  kps = (kps + kAttnKB - 1) / kAttnKB * kAttnKB;
+  *keys_per_split = kps;
+  return (skv + kps - 1) / kps;
+}
+
+template <int HD, int WARPS>
+static cudaError_t launch_attn_cfg(const AttnArgs& a, int B, cudaStream_t st, bool pdl) {
+  using Cfg = AttnCfg<HD, WARPS>;
+  // The merge reuses the K/V ring for QT x nsplit weights.
+  if (a.nsplit > 64 || Cfg::kQTile * a.nsplit * 4 > Cfg::kKVBytes) return cudaErrorInvalidValue;
+  const int q_tiles = (a.Sq + Cfg::kQTile - 1) / Cfg::kQTile;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(q_tiles * a.nsplit, a.H, B);
-  cfg.blockDim = dim3(kAttnWarps * 32);
-  cfg.dynamicSmemBytes = smem;
+  cfg.blockDim = dim3(WARPS * 32);
+  cfg.dynamicSmemBytes = Cfg::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr_l[1];
   attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr_l[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr_l;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
+  return cudaLaunchKernelEx(&cfg, attention_kernel<HD, WARPS>, a);
 }
 
 cudaError_t attn_init_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       AttnSmem<64>::kBytes);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              AttnSmem<128>::kBytes);
+#define FAM_ATTN_ATTR(HD, W)                                                                  \
+  {                                                                                           \
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, W>,                             \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                         AttnCfg<HD, W>::kBytes);                             \
+    if (e != cudaSuccess) return e;                                                           \
+  }
+  FAM_ATTN_ATTR(64, 2) FAM_ATTN_ATTR(64, 4) FAM_ATTN_ATTR(128, 2) FAM_ATTN_ATTR(128, 4)
+#undef FAM_ATTN_ATTR
+  return cudaSuccess;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl) {
-  if (head_dim == 64) return launch_attn_hd<64>(a, B, st, pdl);
-  if (head_dim == 128) return launch_attn_hd<128>(a, B, st, pdl);
+  static bool attrs = false;
+  if (!attrs) {
+    cudaError_t e = attn_init_attributes();
+    if (e != cudaSuccess) return e;
+    attrs = true;
+  }
+  const bool small = attn_warps(a.Sq) == 2;
+  if (head_dim == 64) return small ? launch_attn_cfg<64, 2>(a, B, st, pdl) : launch_attn_cfg<64, 4>(a, B, st, pdl);
+  if (head_dim == 128) return small ? launch_attn_cfg<128, 2>(a, B, st, pdl) : launch_attn_cfg<128, 4>(a, B, st, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -146,6 +146,11 @@ cudaError_t launch_encode_adaln(const EncodeArgs& a, int rows, cudaStream_t st, 
 cudaError_t launch_head_euler(const HeadArgs& a, cudaStream_t st, bool pdl);
 // Bytes of split partials the attention launch needs (0 when nsplit == 1).
 size_t attn_partial_bytes(int B, int H, int Sq, int head_dim, int nsplit);
+// Query tiles per (batch, head) of an attention launch over Sq queries (the
+// arrival counters hold one int per batch x head x tile).
+int attn_query_tiles(int Sq);
+// Key splits that fill about two waves of the GPU with >= 128 keys each.
+int attn_auto_splits(int units, int skv, int* keys_per_split);
 cudaError_t launch_attention(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl);
 
 }  // namespace fam

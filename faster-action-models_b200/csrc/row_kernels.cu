@@ -56,55 +56,118 @@ __device__ __forceinline__ float mod_value(const ModRows& m, long long off, int 
   return v;
 }
 
+// Vector helpers: 4 consecutive columns per thread (128-bit fp32 loads, 64-bit
+// bf16 loads), all split-K partial loads of a group issued back to back.
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 ld_bf4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+__device__ __forceinline__ void st_bf4(__nv_bfloat16* p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+__device__ __forceinline__ float4 rbf4(float4 v) {
+  return make_float4(rbf(v.x), rbf(v.y), rbf(v.z), rbf(v.w));
+}
+// Sum over splits of partials[s * split_stride + off .. +3] in split order.
+__device__ __forceinline__ float4 sum_splits4(const float* partials, long long split_stride,
+                                              int nsplit, long long off) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int s = 0;
+  for (; s + 4 <= nsplit; s += 4) {
+    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(partials + (s + 0) * split_stride + off));
+    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(partials + (s + 1) * split_stride + off));
+    const float4 v2 = __ldcg(reinterpret_cast<const float4*>(partials + (s + 2) * split_stride + off));
+    const float4 v3 = __ldcg(reinterpret_cast<const float4*>(partials + (s + 3) * split_stride + off));
+    acc = f4add(acc, f4add(f4add(v0, v1), f4add(v2, v3)));
+  }
+  for (; s < nsplit; ++s)
+    acc = f4add(acc, __ldcg(reinterpret_cast<const float4*>(partials + s * split_stride + off)));
+  return acc;
+}
+// Modulation chunk c for 4 features: bf16(bf16(t_mod) + modulation).
+__device__ __forceinline__ float4 mod_value4(const ModRows& m, long long off, int c, int f, int D) {
+  float4 t = rbf4(*reinterpret_cast<const float4*>(m.tmod + off + static_cast<long long>(c) * D + f));
+  if (m.mod_w != nullptr) {
+    const float4 w = ld_bf4(m.mod_w + c * D + f);
+    t = rbf4(make_float4(t.x + w.x, t.y + w.y, t.z + w.z, t.w + w.w));
+  }
+  return t;
+}
+
 // ---------------------------------------------------------------- resid_norm
-// Dynamic shared memory: D floats (the updated row).
+// Each thread owns column groups g = threadIdx.x + i * blockDim.x (4 columns
+// each, at most kMaxGroups); the updated row stays in registers.
+constexpr int kMaxGroups = 4;  // D <= 4 * 4 * 256 = 4096
 __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNormArgs a) {
-  extern __shared__ float srow[];
   __shared__ float red[33];
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
   const int D = a.D;
+  const int G = D / 4;
   float* x = a.x + static_cast<long long>(row) * D;
   const long long moff = a.mod.tmod != nullptr ? mod_row_offset(a.mod, row) : 0;
   const long long noff = a.nmod.tmod != nullptr ? mod_row_offset(a.nmod, row) : 0;
+  float4 v[kMaxGroups];
   float lsum = 0.0f;
-  for (int f = threadIdx.x; f < D; f += blockDim.x) {
-    float v = x[f];
+#pragma unroll
+  for (int i = 0; i < kMaxGroups; ++i) {
+    const int g = threadIdx.x + i * blockDim.x;
+    if (g >= G) break;
+    const int f = 4 * g;
+    float4 xv = *reinterpret_cast<const float4*>(x + f);
     if (a.partials != nullptr) {
-      float y = 0.0f;
-      for (int s = 0; s < a.nsplit; ++s)
-        y += __ldcg(a.partials + static_cast<long long>(s) * a.split_stride +
-                    static_cast<long long>(row) * D + f);
-      if (a.bias != nullptr) y += bf2f(a.bias[f]);
-      y = rbf(y);  // the reference's Linear output is a bf16 tensor
-      const float g = (a.gate_chunk >= 0) ? mod_value(a.mod, moff, a.gate_chunk, f, D) : 1.0f;
-      v += g * y;
-      if (a.round_residual) v = rbf(v);
-      x[f] = v;
+      float4 y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * D + f);
+      if (a.bias != nullptr) y = f4add(y, ld_bf4(a.bias + f));
+      y = rbf4(y);  // the reference's Linear output is a bf16 tensor
+      const float4 gt = (a.gate_chunk >= 0) ? mod_value4(a.mod, moff, a.gate_chunk, f, D)
+                                            : make_float4(1.f, 1.f, 1.f, 1.f);
+      xv = make_float4(xv.x + gt.x * y.x, xv.y + gt.y * y.y, xv.z + gt.z * y.z, xv.w + gt.w * y.w);
+      if (a.round_residual) xv = rbf4(xv);
+      *reinterpret_cast<float4*>(x + f) = xv;
     }
-    srow[f] = v;
-    lsum += v;
+    v[i] = xv;
+    lsum += xv.x + xv.y + xv.z + xv.w;
   }
   if (a.norm_mode == kNormNone) return;
   const float mean = block_sum(lsum, red) / D;
   float lvar = 0.0f;
-  for (int f = threadIdx.x; f < D; f += blockDim.x) {
-    const float d = srow[f] - mean;
-    lvar += d * d;
+#pragma unroll
+  for (int i = 0; i < kMaxGroups; ++i) {
+    const int g = threadIdx.x + i * blockDim.x;
+    if (g >= G) break;
+    const float4 d = make_float4(v[i].x - mean, v[i].y - mean, v[i].z - mean, v[i].w - mean);
+    lvar += d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w;
   }
   const float rstd = rsqrtf(block_sum(lvar, red) / D + a.eps);
   __nv_bfloat16* h = a.h + static_cast<long long>(row) * a.h_stride;
-  for (int f = threadIdx.x; f < D; f += blockDim.x) {
-    float n = (srow[f] - mean) * rstd;
+#pragma unroll
+  for (int i = 0; i < kMaxGroups; ++i) {
+    const int g = threadIdx.x + i * blockDim.x;
+    if (g >= G) break;
+    const int f = 4 * g;
+    float4 n = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd,
+                           (v[i].w - mean) * rstd);
     if (a.norm_mode == kNormAffine) {
-      n = n * bf2f(a.norm_w[f]) + bf2f(a.norm_b[f]);
+      const float4 w = ld_bf4(a.norm_w + f), b = ld_bf4(a.norm_b + f);
+      n = make_float4(n.x * w.x + b.x, n.y * w.y + b.y, n.z * w.z + b.z, n.w * w.w + b.w);
     } else {  // AdaLN: LN(x) * (1 + scale) + shift
-      const float shift = mod_value(a.nmod, noff, a.shift_chunk, f, D);
-      const float scale = mod_value(a.nmod, noff, a.shift_chunk + 1, f, D);
-      n = rbf(n) * (1.0f + scale) + shift;
+      const float4 sh = mod_value4(a.nmod, noff, a.shift_chunk, f, D);
+      const float4 sc = mod_value4(a.nmod, noff, a.shift_chunk + 1, f, D);
+      n = rbf4(n);
+      n = make_float4(n.x * (1.f + sc.x) + sh.x, n.y * (1.f + sc.y) + sh.y, n.z * (1.f + sc.z) + sh.z,
+                      n.w * (1.f + sc.w) + sh.w);
     }
-    h[f] = f2bf(n);
+    st_bf4(h + f, n);
   }
 }
 
@@ -118,28 +181,23 @@ __global__ void __launch_bounds__(kRowThreads) qkv_post_kernel(const QkvPostArgs
   const int row = blockIdx.x;
   const int HD = a.HD;
   const int N3 = 3 * HD;
-  float* sq = sbuf;
-  float* sk = sbuf + HD;
+  float* sq = sbuf;  // [0, HD) q, [HD, 2HD) k
   float ssq = 0.0f, ssk = 0.0f;
-  for (int f = threadIdx.x; f < N3; f += blockDim.x) {
-    float y = 0.0f;
-    if (a.nsplit > 0) {
-      for (int s = 0; s < a.nsplit; ++s)
-        y += __ldcg(a.partials + static_cast<long long>(s) * a.split_stride +
-                    static_cast<long long>(row) * N3 + f);
+  for (int g = threadIdx.x; g < N3 / 4; g += blockDim.x) {
+    const int f = 4 * g;
+    float4 y;
+    if (a.nsplit > 0)
+      y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * N3 + f);
+    else
+      y = ld_bf4(a.qkv_bf16 + static_cast<long long>(row) * N3 + f);
+    if (a.bias != nullptr) y = f4add(y, ld_bf4(a.bias + f));
+    y = rbf4(y);
+    const float s2 = y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
+    if (f < 2 * HD) {
+      *reinterpret_cast<float4*>(sq + f) = y;
+      if (f < HD) ssq += s2; else ssk += s2;
     } else {
-      y = bf2f(a.qkv_bf16[static_cast<long long>(row) * N3 + f]);
-    }
-    if (a.bias != nullptr) y += bf2f(a.bias[f]);
-    y = rbf(y);
-    if (f < HD) {
-      sq[f] = y;
-      ssq += y * y;
-    } else if (f < 2 * HD) {
-      sk[f - HD] = y;
-      ssk += y * y;
-    } else {
-      a.v_out[static_cast<long long>(row) * a.out_stride + (f - 2 * HD)] = f2bf(y);
+      st_bf4(a.v_out + static_cast<long long>(row) * a.out_stride + (f - 2 * HD), y);
     }
   }
   const float rq = rsqrtf(block_sum(ssq, red) / HD + a.eps);
@@ -147,29 +205,25 @@ __global__ void __launch_bounds__(kRowThreads) qkv_post_kernel(const QkvPostArgs
   const int pos = row % a.rows_per_batch;
   const int half = a.head_dim / 2;
   const float2* tab = a.rope + static_cast<long long>(pos) * half;
-  // Each thread rotates pairs (2i, 2i+1) of q and of k.
-  for (int pidx = threadIdx.x; pidx < HD / 2; pidx += blockDim.x) {
-    const int f0 = 2 * pidx;
-    const int i = pidx % half;  // pair index inside the head
-    const float2 cs = tab[i];   // (cos, sin)
-    {
-      const float x0 = rbf(rbf(sq[f0] * rq) * bf2f(a.norm_q[f0]));
-      const float x1 = rbf(rbf(sq[f0 + 1] * rq) * bf2f(a.norm_q[f0 + 1]));
-      __nv_bfloat162 o = __floats2bfloat162_rn(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x);
-      *reinterpret_cast<__nv_bfloat162*>(a.q_out + static_cast<long long>(row) * a.out_stride + f0) = o;
-    }
-    {
-      const float x0 = rbf(rbf(sk[f0] * rk) * bf2f(a.norm_k[f0]));
-      const float x1 = rbf(rbf(sk[f0 + 1] * rk) * bf2f(a.norm_k[f0 + 1]));
-      __nv_bfloat162 o = __floats2bfloat162_rn(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x);
-      *reinterpret_cast<__nv_bfloat162*>(a.k_out + static_cast<long long>(row) * a.out_stride + f0) = o;
-    }
+  for (int g = threadIdx.x; g < HD / 2; g += blockDim.x) {  // q groups then k groups
+    const bool is_k = g >= HD / 4;
+    const int f = 4 * (is_k ? g - HD / 4 : g);
+    const float r = is_k ? rk : rq;
+    const float4 y = *reinterpret_cast<const float4*>(sq + (is_k ? HD : 0) + f);
+    const float4 w = ld_bf4((is_k ? a.norm_k : a.norm_q) + f);
+    const float x0 = rbf(rbf(y.x * r) * w.x), x1 = rbf(rbf(y.y * r) * w.y);
+    const float x2 = rbf(rbf(y.z * r) * w.z), x3 = rbf(rbf(y.w * r) * w.w);
+    const int i = (f % a.head_dim) / 2;  // first pair index inside the head (even)
+    const float4 cs = *reinterpret_cast<const float4*>(tab + i);  // (cos_i, sin_i, cos_i+1, sin_i+1)
+    const float4 o = make_float4(x0 * cs.x - x1 * cs.y, x0 * cs.y + x1 * cs.x,
+                                 x2 * cs.z - x3 * cs.w, x2 * cs.w + x3 * cs.z);
+    st_bf4((is_k ? a.k_out : a.q_out) + static_cast<long long>(row) * a.out_stride + f, o);
   }
 }
 
 // ------------------------------------------------------------------ rms_rows
 // out = RMSNorm(sum partials + bias) * w, one CTA per row.  With nsplit == 0
-// the input is a bf16 matrix (in place allowed).
+// the input is a bf16 matrix (in place allowed).  dynamic smem: N floats.
 __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const RmsRowsArgs a) {
   extern __shared__ float sbuf[];
   __shared__ float red[33];
@@ -177,23 +231,26 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const RmsRowsArgs
   pdl_launch_dependents();
   const int row = blockIdx.x;
   float ss = 0.0f;
-  for (int f = threadIdx.x; f < a.N; f += blockDim.x) {
-    float y = 0.0f;
-    if (a.nsplit > 0) {
-      for (int s = 0; s < a.nsplit; ++s)
-        y += __ldcg(a.partials + static_cast<long long>(s) * a.split_stride +
-                    static_cast<long long>(row) * a.N + f);
-    } else {
-      y = bf2f(a.in[static_cast<long long>(row) * a.in_stride + f]);
-    }
-    if (a.bias != nullptr) y += bf2f(a.bias[f]);
-    y = rbf(y);
-    sbuf[f] = y;
-    ss += y * y;
+  for (int g = threadIdx.x; g < a.N / 4; g += blockDim.x) {
+    const int f = 4 * g;
+    float4 y;
+    if (a.nsplit > 0)
+      y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * a.N + f);
+    else
+      y = ld_bf4(a.in + static_cast<long long>(row) * a.in_stride + f);
+    if (a.bias != nullptr) y = f4add(y, ld_bf4(a.bias + f));
+    y = rbf4(y);
+    *reinterpret_cast<float4*>(sbuf + f) = y;
+    ss += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
   }
   const float r = rsqrtf(block_sum(ss, red) / a.N + a.eps);
-  for (int f = threadIdx.x; f < a.N; f += blockDim.x)
-    a.out[static_cast<long long>(row) * a.out_stride + f] = f2bf(rbf(sbuf[f] * r) * bf2f(a.w[f]));
+  for (int g = threadIdx.x; g < a.N / 4; g += blockDim.x) {
+    const int f = 4 * g;
+    const float4 y = *reinterpret_cast<const float4*>(sbuf + f);
+    const float4 w = ld_bf4(a.w + f);
+    st_bf4(a.out + static_cast<long long>(row) * a.out_stride + f,
+           make_float4(rbf(y.x * r) * w.x, rbf(y.y * r) * w.y, rbf(y.z * r) * w.z, rbf(y.w * r) * w.w));
+  }
 }
 
 // ------------------------------------------------------------------ sinusoid
@@ -302,10 +359,8 @@ static cudaError_t ensure_smem(const void* fn, size_t bytes) {
 }
 
 cudaError_t launch_resid_norm(const ResidNormArgs& a, int rows, cudaStream_t st, bool pdl) {
-  const size_t smem = sizeof(float) * a.D;
-  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(resid_norm_kernel), smem);
-  if (e != cudaSuccess) return e;
-  return launch_pdl(resid_norm_kernel, dim3(rows), dim3(kRowThreads), smem, st, pdl, a);
+  if (a.D % 4 != 0 || a.D > 4 * kMaxGroups * kRowThreads) return cudaErrorInvalidValue;
+  return launch_pdl(resid_norm_kernel, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
 }
 
 cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, bool pdl) {

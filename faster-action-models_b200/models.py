@@ -136,9 +136,15 @@ class ActionDiT(nn.Module):
     def num_layers(self) -> int:
         return len(self.blocks)
 
-    def engine(self) -> "ActionExpertEngine":
+    def is_compact(self) -> bool:
+        """Hidden <= 64 experts (the CAE expert) run the persistent fp32 kernel."""
+        return (self.hidden_dim <= 64 and self.num_heads * self.attn_head_dim <= 64
+                and self.attn_head_dim <= 32 and self.ffn_dim <= 256)
+
+    def engine(self):
+        """ActionExpertEngine (bf16 tcgen05 path) or CAEEngine (compact experts)."""
         if self._engine is None:
-            self._engine = ActionExpertEngine(self)
+            self._engine = CAEEngine(self) if self.is_compact() else ActionExpertEngine(self)
         return self._engine
 
     def forward(self, action_tokens, timestep, context, context_mask=None):
@@ -288,6 +294,269 @@ class ActionExpertEngine:
                                      trace.data_ptr() if trace is not None else None,
                                      1 if use_graph else 0, C.c_void_p(st)), "fam_action_chunk")
         return (lat, trace) if return_trace else lat
+
+
+# ---------------------------------------------------- compact expert engine
+def _f32(t: torch.Tensor, dev) -> torch.Tensor:
+    return t.detach().to(device=dev, dtype=torch.float32).contiguous()
+
+
+class CAEEngine:
+    """Compact action expert (hidden <= 64): fp32 weights, the whole Euler loop of a
+    chunk in two launches (fam_cae_chunk)."""
+
+    def __init__(self, dit: "ActionDiT"):
+        p = next(dit.parameters())
+        if not p.is_cuda:
+            raise RuntimeError("ActionDiT must be on a CUDA device for the libfam path")
+        self.dev = p.device
+        self.dit = dit
+        self.keep: List[torch.Tensor] = []
+
+        def ptr(t):
+            t = _f32(t, self.dev)
+            self.keep.append(t)
+            return t.data_ptr()
+
+        layers = (_abi.CaeLayer * dit.num_layers)()
+        for i, b in enumerate(dit.blocks):
+            sa, ca, L = b.self_attn, b.cross_attn, layers[i]
+            L.modulation = ptr(b.modulation.reshape(6, -1))
+            L.qkv_w = ptr(torch.cat([sa.q.weight, sa.k.weight, sa.v.weight], 0))
+            L.qkv_b = ptr(torch.cat([sa.q.bias, sa.k.bias, sa.v.bias], 0))
+            L.norm_q, L.norm_k = ptr(sa.norm_q.weight), ptr(sa.norm_k.weight)
+            L.o_w, L.o_b = ptr(sa.o.weight), ptr(sa.o.bias)
+            L.norm3_w, L.norm3_b = ptr(b.norm3.weight), ptr(b.norm3.bias)
+            L.cq_w, L.cq_b = ptr(ca.q.weight), ptr(ca.q.bias)
+            L.cnorm_q, L.cnorm_k = ptr(ca.norm_q.weight), ptr(ca.norm_k.weight)
+            L.ckv_w = ptr(torch.cat([ca.k.weight, ca.v.weight], 0))
+            L.ckv_b = ptr(torch.cat([ca.k.bias, ca.v.bias], 0))
+            L.co_w, L.co_b = ptr(ca.o.weight), ptr(ca.o.bias)
+            L.ffn0_w, L.ffn0_b = ptr(b.ffn[0].weight), ptr(b.ffn[0].bias)
+            L.ffn2_w, L.ffn2_b = ptr(b.ffn[2].weight), ptr(b.ffn[2].bias)
+        w = _abi.CaeWeights()
+        for name, mod in (("enc", dit.action_encoder), ("text0", dit.text_embedding[0]),
+                          ("text2", dit.text_embedding[2]), ("time0", dit.time_embedding[0]),
+                          ("time2", dit.time_embedding[2]), ("tproj", dit.time_projection[1]),
+                          ("head", dit.head)):
+            setattr(w, name + "_w", ptr(mod.weight))
+            setattr(w, name + "_b", ptr(mod.bias))
+        self._layers = layers
+        w.layers = layers
+        w.rope = ptr(rope_table(dit.attn_head_dim))
+        w.rope_positions = 1024
+        self._w = w
+        self.cfg = _abi.ActionConfig(dit.hidden_dim, dit.action_dim, dit.ffn_dim, dit.text_dim,
+                                     dit.freq_dim, dit.num_heads, dit.attn_head_dim,
+                                     dit.num_layers, float(dit.eps))
+        self.ws: Optional[torch.Tensor] = None
+
+    def chunk(self, latents, timesteps: Sequence[float], deltas: Sequence[float], context,
+              context_mask=None, return_trace: bool = False, out: Optional[torch.Tensor] = None):
+        """Euler loop over ActionDiT.forward (action_dit.py:333-362) -> fp32 latent [B,S,A]."""
+        lat = out if out is not None else latents.to(device=self.dev, dtype=torch.float32).clone()
+        B, S, A = lat.shape
+        ctx = context if context.is_cuda and context.dtype in (torch.bfloat16, torch.float32) \
+            else context.to(self.dev, torch.float32)
+        ctx = ctx.contiguous()
+        C_ = ctx.shape[1]
+        cm = None
+        if context_mask is not None:
+            cm = context_mask.to(device=self.dev, dtype=torch.uint8).expand(B, C_).contiguous()
+        n = C.c_size_t()
+        check(lib().fam_cae_workspace_size(C.byref(self.cfg), B, C_, C.byref(n)), "fam_cae_workspace_size")
+        if self.ws is None or self.ws.numel() < n.value:
+            self.ws = torch.empty(n.value, dtype=torch.uint8, device=self.dev)
+        N = len(timesteps)
+        trace = torch.empty((N, B, S, A), dtype=torch.float32, device=self.dev) if return_trace else None
+        ts = (C.c_float * N)(*[float(t) for t in timesteps])
+        ds = (C.c_float * N)(*[float(d) for d in deltas])
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        check(lib().fam_cae_chunk(C.byref(self.cfg), C.byref(self._w), B, S, ctx.data_ptr(),
+                                  1 if ctx.dtype == torch.bfloat16 else 0, C_,
+                                  cm.data_ptr() if cm is not None else None, lat.data_ptr(), ts, ds,
+                                  N, trace.data_ptr() if trace is not None else None,
+                                  self.ws.data_ptr(), self.ws.numel(), C.c_void_p(st)),
+              "fam_cae_chunk")
+        self._hold = (ctx, cm)
+        return (lat, trace) if return_trace else lat
+
+    def denoise_step(self, latents, timestep, context, context_mask=None):
+        """One model evaluation (ActionDiT.forward) -> velocity fp32 [B,S,A]."""
+        t = float(timestep.reshape(-1)[0].item()) if torch.is_tensor(timestep) else float(timestep)
+        _, tr = self.chunk(latents, [t], [0.0], context, context_mask, return_trace=True)
+        return tr[0]
+
+
+# ------------------------------------------------------------ action VAE
+from dataclasses import dataclass
+
+
+@dataclass
+class ActionAEConfig:
+    """FastWAM/src/fastwam/models/action_ae.py:16-30."""
+
+    action_dim: int = 7
+    action_horizon: int = 32
+    num_tokens: int = 4
+    latent_dim: int = 8
+    encoder_hidden: int = 128
+    decoder_hidden: int = 128
+    video_cond_dim: int = 12288
+    variational: bool = False
+    beta_kl: float = 1e-2
+    free_bits: float = 0.0
+    recon_loss: str = "mse"
+    num_suites: int = 0
+    sigreg_lambda: float = 0.0
+
+
+def _factorise_ratio(ratio: int) -> List[int]:
+    """ActionEncoder._factorise_ratio (action_ae.py:95-107)."""
+    if ratio == 1:
+        return [1]
+    out = []
+    for f in (4, 2, 3):
+        while ratio % f == 0:
+            out.append(f)
+            ratio //= f
+    if ratio > 1:
+        out.append(ratio)
+    return out
+
+
+class ResidualConv1dBlock(nn.Module):
+    """action_ae.py:33-47 (layout)."""
+
+    def __init__(self, channels: int, kernel_size: int = 3):
+        super().__init__()
+        pad = kernel_size // 2
+        self.net = nn.Sequential(nn.Conv1d(channels, channels, kernel_size, padding=pad),
+                                 nn.GroupNorm(min(8, channels), channels), nn.SiLU(),
+                                 nn.Conv1d(channels, channels, kernel_size, padding=pad),
+                                 nn.GroupNorm(min(8, channels), channels))
+
+
+class ActionEncoder(nn.Module):
+    """action_ae.py:50-121 (parameter layout; encoding is not on the denoising path)."""
+
+    def __init__(self, cfg: ActionAEConfig):
+        super().__init__()
+        self.cfg = cfg
+        if cfg.action_horizon % cfg.num_tokens:
+            raise ValueError("action_horizon must be divisible by num_tokens")
+        self.input_proj = nn.Linear(cfg.action_dim, cfg.encoder_hidden)
+        self.cond_proj = (nn.Sequential(nn.Linear(cfg.video_cond_dim, cfg.encoder_hidden), nn.SiLU(),
+                                        nn.Linear(cfg.encoder_hidden, cfg.encoder_hidden))
+                          if cfg.video_cond_dim > 0 else None)
+        self.strides = _factorise_ratio(cfg.action_horizon // cfg.num_tokens)
+        layers: List[nn.Module] = []
+        for s in self.strides:
+            layers += [nn.Conv1d(cfg.encoder_hidden, cfg.encoder_hidden, kernel_size=s * 2 - 1,
+                                 stride=s, padding=s - 1),
+                       nn.GroupNorm(min(8, cfg.encoder_hidden), cfg.encoder_hidden), nn.SiLU(),
+                       ResidualConv1dBlock(cfg.encoder_hidden)]
+        self.down = nn.Sequential(*layers)
+        self.suite_embed = None
+        if cfg.num_suites > 0:
+            self.suite_embed = nn.Embedding(cfg.num_suites, cfg.encoder_hidden)
+            nn.init.zeros_(self.suite_embed.weight)
+        self.bottleneck = nn.Linear(cfg.encoder_hidden, cfg.latent_dim * (2 if cfg.variational else 1))
+
+
+class ActionDecoder(nn.Module):
+    """action_ae.py:123-166 (same parameters); forward runs fam_action_decode."""
+
+    def __init__(self, cfg: ActionAEConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.input_proj = nn.Linear(cfg.latent_dim, cfg.decoder_hidden)
+        self.strides = _factorise_ratio(cfg.action_horizon // cfg.num_tokens)
+        layers: List[nn.Module] = []
+        for s in self.strides:
+            layers += [nn.ConvTranspose1d(cfg.decoder_hidden, cfg.decoder_hidden, kernel_size=s * 2,
+                                          stride=s, padding=s // 2),
+                       nn.GroupNorm(min(8, cfg.decoder_hidden), cfg.decoder_hidden), nn.SiLU(),
+                       ResidualConv1dBlock(cfg.decoder_hidden)]
+        self.up = nn.Sequential(*layers)
+        self.output_proj = nn.Linear(cfg.decoder_hidden, cfg.action_dim)
+        self.suite_embed = None
+        if cfg.num_suites > 0:
+            self.suite_embed = nn.Embedding(cfg.num_suites, cfg.decoder_hidden)
+            nn.init.zeros_(self.suite_embed.weight)
+        self._packed = None
+        self.register_load_state_dict_post_hook(lambda m, k: setattr(m, "_packed", None))
+
+    def _apply(self, fn, *args, **kwargs):
+        self._packed = None
+        return super()._apply(fn, *args, **kwargs)
+
+    def _pack(self):
+        dev = self.input_proj.weight.device
+        keep: List[torch.Tensor] = []
+
+        def ptr(t):
+            t = _f32(t, dev)
+            keep.append(t)
+            return t.data_ptr()
+
+        stages = (_abi.DecoderStage * len(self.strides))()
+        for i, s in enumerate(self.strides):
+            ct, gn0, rb = self.up[4 * i], self.up[4 * i + 1], self.up[4 * i + 3].net
+            st = stages[i]
+            st.convt_w, st.convt_b = ptr(ct.weight), ptr(ct.bias)
+            st.gn0_w, st.gn0_b = ptr(gn0.weight), ptr(gn0.bias)
+            st.c1_w, st.c1_b = ptr(rb[0].weight), ptr(rb[0].bias)
+            st.gn1_w, st.gn1_b = ptr(rb[1].weight), ptr(rb[1].bias)
+            st.c2_w, st.c2_b = ptr(rb[3].weight), ptr(rb[3].bias)
+            st.gn2_w, st.gn2_b = ptr(rb[4].weight), ptr(rb[4].bias)
+            st.stride = s
+        w = _abi.DecoderWeights()
+        w.in_w, w.in_b = ptr(self.input_proj.weight), ptr(self.input_proj.bias)
+        w.out_w, w.out_b = ptr(self.output_proj.weight), ptr(self.output_proj.bias)
+        w.suite_embed = ptr(self.suite_embed.weight) if self.suite_embed is not None else None
+        w.stages = stages
+        w.num_stages = len(self.strides)
+        c = self.cfg
+        cfg = _abi.DecoderConfig(c.action_dim, c.action_horizon, c.num_tokens, c.latent_dim,
+                                 c.decoder_hidden, c.num_suites)
+        self._packed = (cfg, w, stages, keep)
+
+    def forward(self, z: torch.Tensor, suite_ids: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not z.is_cuda:
+            raise RuntimeError("ActionDecoder runs on CUDA through libfam")
+        if self._packed is None:
+            self._pack()
+        cfg, w, _, _ = self._packed
+        zz = z.to(torch.float32).contiguous()
+        B = zz.shape[0]
+        out = torch.empty((B, self.cfg.action_horizon, self.cfg.action_dim), device=z.device)
+        n = C.c_size_t()
+        check(lib().fam_decoder_workspace_size(C.byref(cfg), C.byref(w), B, C.byref(n)),
+              "fam_decoder_workspace_size")
+        ws = torch.empty(n.value, dtype=torch.uint8, device=z.device)
+        sid = None
+        if suite_ids is not None and self.suite_embed is not None:
+            sid = suite_ids.to(device=z.device, dtype=torch.int32).contiguous()
+        check(lib().fam_action_decode(C.byref(cfg), C.byref(w), B, zz.data_ptr(),
+                                      sid.data_ptr() if sid is not None else None, out.data_ptr(),
+                                      ws.data_ptr(), ws.numel(),
+                                      C.c_void_p(torch.cuda.current_stream(z.device).cuda_stream)),
+              "fam_action_decode")
+        return out
+
+
+class ActionAE(nn.Module):
+    """action_ae.py:169-187: same state_dict; decode() on libfam."""
+
+    def __init__(self, cfg: ActionAEConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.encoder = ActionEncoder(cfg)
+        self.decoder = ActionDecoder(cfg)
+
+    def decode(self, z: torch.Tensor, suite_ids: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.decoder(z, suite_ids=suite_ids)
 
 
 # ---------------------------------------------------------------- schedule

@@ -258,6 +258,84 @@ FAM_API int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* i
  * enqueued (a graph replay launches the same set). */
 FAM_API int fam_action_launch_count(const fam_action_expert* e, int32_t* count);
 
+/* ======================================================================
+ * Compact action expert (hidden width <= 64, e.g. the CAE expert of
+ * CAE-FastWAM and BASELINE config 0): the whole Euler loop of a chunk in two
+ * launches — the context side (text embedding + every block's cross K/V) and
+ * one persistent kernel per sample running every step x block.  fp32
+ * arithmetic and fp32 weights (the reference's fp32 configuration).
+ *
+ * Replaces ActionDiT.forward called in the flow-matching loop
+ *   FastWAM/src/fastwam/models/wan22/action_dit.py:312-362,
+ *   .../wan22/wan_video_dit.py:248-267 (DiTBlock.forward),
+ *   .../wan22/fastwam.py:1241-1263 and scheduler_continuous.py:82-88.
+ * Limits: tokens <= 32, hidden <= 64, heads*head_dim <= 64, head_dim <= 32,
+ * ffn <= 256, blocks <= 32, action channels <= 64.
+ * ====================================================================== */
+typedef struct fam_cae_layer {
+  const float *modulation, *qkv_w, *qkv_b, *norm_q, *norm_k, *o_w, *o_b, *norm3_w, *norm3_b,
+      *cq_w, *cq_b, *cnorm_q, *cnorm_k, *ckv_w, *ckv_b, *co_w, *co_b, *ffn0_w, *ffn0_b, *ffn2_w,
+      *ffn2_b; /* same shapes and meaning as fam_action_layer, fp32 */
+} fam_cae_layer;
+
+typedef struct fam_cae_weights {
+  const float *enc_w, *enc_b, *text0_w, *text0_b, *text2_w, *text2_b, *time0_w, *time0_b,
+      *time2_w, *time2_b, *tproj_w, *tproj_b, *head_w, *head_b;
+  const fam_cae_layer* layers; /* host array [num_layers] */
+  const float* rope;           /* f32 [rope_positions, head_dim/2, 2] */
+  int32_t rope_positions;
+} fam_cae_weights;
+
+/* Workspace bytes of fam_cae_chunk for batch x context_tokens. */
+FAM_API int fam_cae_workspace_size(const fam_action_config* cfg, int32_t batch,
+                                   int32_t context_tokens, size_t* bytes);
+
+/* latent: f32 [B, S, A] updated in place; context: [B, C, T] f32 (context_bf16
+ * == 0) or bf16; context_mask u8 [B, C] or NULL; velocity_trace f32
+ * [num_steps, B, S, A] or NULL; timesteps / deltas host arrays [num_steps]. */
+FAM_API int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch,
+                          int32_t tokens, const void* context, int32_t context_bf16,
+                          int32_t context_tokens, const uint8_t* context_mask, float* latent,
+                          const float* timesteps, const float* deltas, int32_t num_steps,
+                          float* velocity_trace, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ======================================================================
+ * Action-VAE decoder (ActionAE.decode / ActionDecoder.forward,
+ * FastWAM/src/fastwam/models/action_ae.py:123-166, 184-187), fp32:
+ * input_proj (+ suite embedding) -> per stride s: ConvTranspose1d(h, h, 2s, s,
+ * s/2) -> GroupNorm(min(8, h)) -> SiLU -> residual [Conv1d k3 -> GN -> SiLU ->
+ * Conv1d k3 -> GN] -> crop / zero-pad to action_horizon -> output_proj.
+ * ====================================================================== */
+typedef struct fam_decoder_config {
+  int32_t action_dim, action_horizon, num_tokens, latent_dim, hidden, num_suites;
+} fam_decoder_config;
+
+typedef struct fam_decoder_stage {
+  const float *convt_w, *convt_b; /* up.{4i}: [h, h, 2s], [h] */
+  const float *gn0_w, *gn0_b;     /* up.{4i+1} */
+  const float *c1_w, *c1_b;       /* up.{4i+3}.net.0: [h, h, 3] */
+  const float *gn1_w, *gn1_b;     /* up.{4i+3}.net.1 */
+  const float *c2_w, *c2_b;       /* up.{4i+3}.net.3 */
+  const float *gn2_w, *gn2_b;     /* up.{4i+3}.net.4 */
+  int32_t stride;
+} fam_decoder_stage;
+
+typedef struct fam_decoder_weights {
+  const float *in_w, *in_b;       /* input_proj [h, latent] */
+  const float *out_w, *out_b;     /* output_proj [A, h] */
+  const float* suite_embed;       /* [num_suites, h] or NULL */
+  const fam_decoder_stage* stages;/* host array */
+  int32_t num_stages;
+} fam_decoder_weights;
+
+FAM_API int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_decoder_weights* w,
+                                       int32_t batch, size_t* bytes);
+/* z: f32 [B, num_tokens, latent]; suite_ids: int32 [B] or NULL; out: f32 [B, horizon, A]. */
+FAM_API int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_weights* w,
+                              int32_t batch, const float* z, const int32_t* suite_ids, float* out,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,23 @@ def test_action_dit_state_dict_matches_reference_layout_and_init():
     assert dit._engine is None
 
 
+def test_cae_expert_and_action_ae_layout_and_init():
+    fx = torch.load(GOLDEN / "c0_cae_expert.pt", weights_only=False)
+    torch.manual_seed(0)  # make_golden.py: seed, ActionDiT, then ActionAE, then bf16 rounding
+    dit = M.ActionDiT(**fx["dit_cfg"])
+    c = fx["dec_cfg"]
+    ae = M.ActionAE(M.ActionAEConfig(action_dim=c["action_dim"], action_horizon=c["action_horizon"],
+                                     num_tokens=c["num_tokens"], latent_dim=c["latent_dim"],
+                                     decoder_hidden=c["decoder_hidden"], video_cond_dim=0,
+                                     variational=True))
+    for mod, key in ((dit, "dit"), (ae, "ae")):
+        sd = {k: v.to(torch.bfloat16) for k, v in mod.state_dict().items()}
+        assert list(sd.keys()) == list(fx[key].keys()), key
+        for k, v in fx[key].items():
+            assert torch.equal(sd[k], v), f"{key}: {k}"
+    assert dit.is_compact()
+
+
 def test_schedule_helper_matches_oracle():
     for n, s in ((10, 1.0), (4, 5.0), (7, 3.0)):
         for dt in (torch.float32, torch.bfloat16):
