@@ -50,6 +50,7 @@ def declare(lib) -> None:
     declare_counts(lib)
     declare_ops(lib)
     declare_cae(lib)
+    declare_video(lib)
 
 
 def declare_counts(lib) -> None:
@@ -123,4 +124,38 @@ def declare_cae(lib) -> None:
                                       vp, vp, vp, vp, sz, vp]
     for n in ("fam_cae_workspace_size", "fam_cae_chunk", "fam_decoder_workspace_size",
               "fam_action_decode"):
+        getattr(lib, n).restype = C.c_int
+
+
+class VideoConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden_dim", "in_dim", "ffn_dim", "text_dim", "freq_dim",
+                                         "num_heads", "head_dim", "num_layers", "patch_t",
+                                         "patch_h", "patch_w")] + [("eps", C.c_float)]
+
+
+class VideoWeights(C.Structure):
+    _fields_ = [(n, vp) for n in ("patch_w", "patch_b", "text0_w", "text0_b", "text2_w", "text2_b",
+                                  "time0_w", "time0_b", "time2_w", "time2_b", "tproj_w",
+                                  "tproj_b")] + [("layers", C.POINTER(ActionLayer))]
+
+
+class VideoIO(C.Structure):
+    _fields_ = [("batch", C.c_int32), ("frames", C.c_int32), ("height", C.c_int32),
+                ("width", C.c_int32), ("context_tokens", C.c_int32), ("latents", vp),
+                ("timesteps", C.POINTER(C.c_float)), ("context", vp), ("context_mask", vp),
+                ("rope", vp), ("first_frame_causal", C.c_int32), ("cache_k", C.POINTER(vp)),
+                ("cache_v", C.POINTER(vp)), ("hidden_out", vp), ("workspace", vp),
+                ("workspace_bytes", C.c_size_t)]
+
+
+def declare_video(lib) -> None:
+    i32, sz = C.c_int32, C.c_size_t
+    lib.fam_video_expert_create.argtypes = [C.POINTER(VideoConfig), C.POINTER(VideoWeights),
+                                            C.POINTER(vp)]
+    lib.fam_video_expert_destroy.argtypes = [vp]
+    lib.fam_video_workspace_size.argtypes = [vp, i32, i32, i32, C.POINTER(sz)]
+    lib.fam_video_prefill.argtypes = [vp, C.POINTER(VideoIO), i32, vp]
+    lib.fam_video_launch_count.argtypes = [vp, C.POINTER(C.c_int32)]
+    for n in ("fam_video_expert_create", "fam_video_expert_destroy", "fam_video_workspace_size",
+              "fam_video_prefill", "fam_video_launch_count"):
         getattr(lib, n).restype = C.c_int

@@ -137,6 +137,14 @@ struct AttnArgs {
   int* status;
 };
 
+struct PatchArgs {
+  const __nv_bfloat16* in;   // [B, Cin, F, H, W]
+  __nv_bfloat16* out;        // [B * S, Cin * pt * ph * pw]
+  long long B;
+  int Cin, F, H, W, pt, ph, pw;
+};
+cudaError_t launch_patchify(const PatchArgs& a, cudaStream_t st);
+
 cudaError_t launch_resid_norm(const ResidNormArgs& a, int rows, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, bool pdl);
 cudaError_t launch_rms_rows(const RmsRowsArgs& a, int rows, cudaStream_t st, bool pdl);

@@ -296,6 +296,228 @@ class ActionExpertEngine:
         return (lat, trace) if return_trace else lat
 
 
+# ------------------------------------------------------------ video DiT
+class Head(nn.Module):
+    """wan_video_dit.py:287-306 (parameter layout)."""
+
+    def __init__(self, dim: int, out_dim: int, patch_size, eps: float):
+        super().__init__()
+        self.dim = dim
+        self.patch_size = patch_size
+        self.norm = nn.LayerNorm(dim, eps=eps, elementwise_affine=False)
+        self.head = nn.Linear(dim, out_dim * math.prod(patch_size))
+        self.modulation = nn.Parameter(torch.randn(1, 2, dim) / dim ** 0.5)
+
+
+def rope_table_3d(head_dim: int, f: int, h: int, w: int, theta: float = 10000.0) -> torch.Tensor:
+    """Per-token (cos, sin) of WanVideoDiT.get_freqs (wan_video_dit.py:37-51, 406-415): the
+    head is split (d - 2(d//3), d//3, d//3) over (frame, row, column); angles in fp64,
+    stored fp32 [f*h*w, d/2, 2]."""
+    def freqs(dim):
+        return 1.0 / (theta ** (torch.arange(0, dim, 2)[: dim // 2].double() / dim))
+    df = head_dim - 2 * (head_dim // 3)
+    dh = head_dim // 3
+    ff, fh, fw = freqs(df), freqs(dh), freqs(dh)
+    fi = torch.arange(f, dtype=torch.float64).view(f, 1, 1, 1).expand(f, h, w, 1)
+    hi = torch.arange(h, dtype=torch.float64).view(1, h, 1, 1).expand(f, h, w, 1)
+    wi = torch.arange(w, dtype=torch.float64).view(1, 1, w, 1).expand(f, h, w, 1)
+    ang = torch.cat([fi * ff, hi * fh, wi * fw], dim=-1).reshape(f * h * w, -1)
+    return torch.stack([ang.cos(), ang.sin()], dim=-1).float().contiguous()
+
+
+class WanVideoDiT(nn.Module):
+    """Video expert (wan_video_dit.py:308-405): same constructor signature, parameters and
+    construction order.  prefill() runs WanVideoDiT.prepare + MoT.prefill_video_cache_tensor
+    through fam_video_prefill."""
+
+    def __init__(self, hidden_dim: int, in_dim: int, ffn_dim: int, out_dim: int, text_dim: int,
+                 freq_dim: int, eps: float, patch_size, num_heads: int, attn_head_dim: int,
+                 num_layers: int, has_image_input: bool, has_image_pos_emb: bool = False,
+                 has_ref_conv: bool = False, add_control_adapter: bool = False,
+                 in_dim_control_adapter: int = 24, seperated_timestep: bool = False,
+                 require_vae_embedding: bool = False, require_clip_embedding: bool = False,
+                 fuse_vae_embedding_in_latents: bool = True, action_conditioned: bool = False,
+                 action_dim: int = 7, action_group_causal_mask_mode="causal",
+                 video_attention_mask_mode: str = "bidirectional",
+                 use_gradient_checkpointing: bool = False):
+        super().__init__()
+        if has_image_input or require_clip_embedding or require_vae_embedding:
+            raise ValueError("image input / clip / vae embeddings are not supported (as in the reference)")
+        if attn_head_dim % 2:
+            raise ValueError("attn_head_dim must be even for RoPE")
+        self.hidden_dim, self.in_dim, self.freq_dim = hidden_dim, in_dim, freq_dim
+        self.patch_size = tuple(patch_size)
+        self.num_heads, self.attn_head_dim, self.eps = num_heads, attn_head_dim, eps
+        self.ffn_dim, self.text_dim = ffn_dim, text_dim
+        self.seperated_timestep = seperated_timestep
+        self.fuse_vae_embedding_in_latents = fuse_vae_embedding_in_latents
+        self.video_attention_mask_mode = str(video_attention_mask_mode)
+        self.action_conditioned = action_conditioned
+        self.action_dim = action_dim
+        self.patch_embedding = nn.Conv3d(in_dim, hidden_dim, kernel_size=patch_size, stride=patch_size)
+        self.text_embedding = nn.Sequential(nn.Linear(text_dim, hidden_dim), nn.GELU(approximate="tanh"),
+                                            nn.Linear(hidden_dim, hidden_dim))
+        self.time_embedding = nn.Sequential(nn.Linear(freq_dim, hidden_dim), nn.SiLU(),
+                                            nn.Linear(hidden_dim, hidden_dim))
+        self.time_projection = nn.Sequential(nn.SiLU(), nn.Linear(hidden_dim, hidden_dim * 6))
+        self.blocks = nn.ModuleList([DiTBlock(hidden_dim, attn_head_dim, num_heads, ffn_dim, eps)
+                                     for _ in range(num_layers)])
+        self.head = Head(hidden_dim, out_dim, patch_size, eps)
+        if has_ref_conv:
+            self.ref_conv = nn.Conv2d(16, hidden_dim, kernel_size=(2, 2), stride=(2, 2))
+        if action_conditioned:
+            self.action_embedding = nn.Linear(action_dim, hidden_dim)
+        self.use_gradient_checkpointing = use_gradient_checkpointing
+        self._engine = None
+        self.register_load_state_dict_post_hook(lambda m, k: setattr(m, "_engine", None))
+
+    def _apply(self, fn, *args, **kwargs):
+        self._engine = None
+        return super()._apply(fn, *args, **kwargs)
+
+    @property
+    def num_layers(self) -> int:
+        return len(self.blocks)
+
+    def engine(self) -> "VideoPrefillEngine":
+        if self._engine is None:
+            self._engine = VideoPrefillEngine(self)
+        return self._engine
+
+    def prefill(self, latents, timestep, context, context_mask=None, return_hidden=False):
+        return self.engine().prefill(latents, timestep, context, context_mask, return_hidden)
+
+
+class VideoPrefillEngine:
+    """Packed bf16 weights + fam_video_expert handle + workspace of one WanVideoDiT."""
+
+    def __init__(self, dit: WanVideoDiT):
+        p = next(dit.parameters())
+        if not p.is_cuda:
+            raise RuntimeError("WanVideoDiT must be on a CUDA device for the libfam path")
+        if not (dit.seperated_timestep and dit.fuse_vae_embedding_in_latents):
+            raise ValueError("only the separated-timestep, fused-VAE-latent path exists (as in the reference)")
+        self.dev = p.device
+        self.dit = dit
+        self.keep: List[torch.Tensor] = []
+        bfw = lambda t: t.detach().to(device=self.dev, dtype=torch.bfloat16).contiguous()
+
+        def ptr(t):
+            self.keep.append(t)
+            return t.data_ptr()
+
+        layers = (_abi.ActionLayer * dit.num_layers)()
+        for i, b in enumerate(dit.blocks):
+            sa, ca, L = b.self_attn, b.cross_attn, layers[i]
+            L.modulation = ptr(bfw(b.modulation.reshape(6, -1)))
+            L.qkv_w = ptr(bfw(torch.cat([sa.q.weight, sa.k.weight, sa.v.weight], 0)))
+            L.qkv_b = ptr(bfw(torch.cat([sa.q.bias, sa.k.bias, sa.v.bias], 0)))
+            L.norm_q, L.norm_k = ptr(bfw(sa.norm_q.weight)), ptr(bfw(sa.norm_k.weight))
+            L.o_w, L.o_b = ptr(bfw(sa.o.weight)), ptr(bfw(sa.o.bias))
+            L.norm3_w, L.norm3_b = ptr(bfw(b.norm3.weight)), ptr(bfw(b.norm3.bias))
+            L.cq_w, L.cq_b = ptr(bfw(ca.q.weight)), ptr(bfw(ca.q.bias))
+            L.cnorm_q, L.cnorm_k = ptr(bfw(ca.norm_q.weight)), ptr(bfw(ca.norm_k.weight))
+            L.ckv_w = ptr(bfw(torch.cat([ca.k.weight, ca.v.weight], 0)))
+            L.ckv_b = ptr(bfw(torch.cat([ca.k.bias, ca.v.bias], 0)))
+            L.co_w, L.co_b = ptr(bfw(ca.o.weight)), ptr(bfw(ca.o.bias))
+            L.ffn0_w, L.ffn0_b = ptr(bfw(b.ffn[0].weight)), ptr(bfw(b.ffn[0].bias))
+            L.ffn2_w, L.ffn2_b = ptr(bfw(b.ffn[2].weight)), ptr(bfw(b.ffn[2].bias))
+        w = _abi.VideoWeights()
+        w.patch_w = ptr(bfw(dit.patch_embedding.weight.reshape(dit.hidden_dim, -1)))
+        w.patch_b = ptr(bfw(dit.patch_embedding.bias))
+        for name, mod in (("text0", dit.text_embedding[0]), ("text2", dit.text_embedding[2]),
+                          ("time0", dit.time_embedding[0]), ("time2", dit.time_embedding[2]),
+                          ("tproj", dit.time_projection[1])):
+            setattr(w, name + "_w", ptr(bfw(mod.weight)))
+            setattr(w, name + "_b", ptr(bfw(mod.bias)))
+        self._layers = layers
+        w.layers = layers
+        pt, ph, pw = dit.patch_size
+        cfg = _abi.VideoConfig(dit.hidden_dim, dit.in_dim, dit.ffn_dim, dit.text_dim, dit.freq_dim,
+                               dit.num_heads, dit.attn_head_dim, dit.num_layers, pt, ph, pw,
+                               float(dit.eps))
+        self._w = w
+        h = C.c_void_p()
+        with torch.cuda.device(self.dev):
+            check(lib().fam_video_expert_create(C.byref(cfg), C.byref(w), C.byref(h)),
+                  "fam_video_expert_create")
+        self.handle = h
+        self.ws: Optional[torch.Tensor] = None
+        self._rope = {}
+        self.last = None
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                lib().fam_video_expert_destroy(h)
+            except Exception:
+                pass
+
+    def launch_count(self) -> int:
+        n = C.c_int32()
+        check(lib().fam_video_launch_count(self.handle, C.byref(n)), "fam_video_launch_count")
+        return n.value
+
+    def rope(self, f, h, w) -> torch.Tensor:
+        key = (f, h, w)
+        if key not in self._rope:
+            self._rope[key] = rope_table_3d(self.dit.attn_head_dim, f, h, w).to(self.dev)
+        return self._rope[key]
+
+    def prefill(self, latents, timestep, context, context_mask=None, return_hidden=False,
+                cache_k=None, cache_v=None, hidden=None, use_graph=True):
+        """WanVideoDiT.prepare + MoT.prefill_video_cache_tensor: returns the per-block K and V
+        lists ([B, S, H*d] bf16) and, with return_hidden, the final token states (fp32)."""
+        d = self.dit
+        lat = latents.to(device=self.dev, dtype=torch.bfloat16).contiguous()
+        B, _, Fr, Hh, Ww = lat.shape
+        pt, ph, pw = d.patch_size
+        f, hh, ww = Fr // pt, Hh // ph, Ww // pw
+        S = f * hh * ww
+        HD = d.num_heads * d.attn_head_dim
+        if cache_k is None:
+            cache_k = [torch.empty(B, S, HD, dtype=torch.bfloat16, device=self.dev) for _ in range(d.num_layers)]
+            cache_v = [torch.empty(B, S, HD, dtype=torch.bfloat16, device=self.dev) for _ in range(d.num_layers)]
+        if return_hidden and hidden is None:
+            hidden = torch.empty(B, S, d.hidden_dim, dtype=torch.float32, device=self.dev)
+        ctx = context.to(device=self.dev, dtype=torch.bfloat16).contiguous()
+        Cc = ctx.shape[1]
+        cm = None
+        if context_mask is not None:
+            cm = context_mask.to(device=self.dev, dtype=torch.uint8).expand(B, Cc).contiguous()
+        tsv = timestep.reshape(-1).float().tolist() if torch.is_tensor(timestep) else [float(timestep)]
+        if len(tsv) == 1:
+            tsv = tsv * B
+        io = _abi.VideoIO()
+        io.batch, io.frames, io.height, io.width, io.context_tokens = B, Fr, Hh, Ww, Cc
+        io.latents = lat.data_ptr()
+        ts = (C.c_float * B)(*tsv)
+        io.timesteps = ts
+        io.context = ctx.data_ptr()
+        io.context_mask = cm.data_ptr() if cm is not None else None
+        rope = self.rope(f, hh, ww)
+        io.rope = rope.data_ptr()
+        io.first_frame_causal = 1 if d.video_attention_mask_mode == "first_frame_causal" else 0
+        if d.video_attention_mask_mode not in ("first_frame_causal", "bidirectional"):
+            raise ValueError("video_attention_mask_mode must be first_frame_causal or bidirectional")
+        kp = (C.c_void_p * d.num_layers)(*[k.data_ptr() for k in cache_k])
+        vpp = (C.c_void_p * d.num_layers)(*[v.data_ptr() for v in cache_v])
+        io.cache_k = C.cast(kp, C.POINTER(C.c_void_p))
+        io.cache_v = C.cast(vpp, C.POINTER(C.c_void_p))
+        io.hidden_out = hidden.data_ptr() if hidden is not None else None
+        n = C.c_size_t()
+        check(lib().fam_video_workspace_size(self.handle, B, S, Cc, C.byref(n)), "fam_video_workspace_size")
+        if self.ws is None or self.ws.numel() < n.value:
+            self.ws = torch.empty(n.value, dtype=torch.uint8, device=self.dev)
+        io.workspace, io.workspace_bytes = self.ws.data_ptr(), self.ws.numel()
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        check(lib().fam_video_prefill(self.handle, C.byref(io), 1 if use_graph else 0, C.c_void_p(st)),
+              "fam_video_prefill")
+        self.last = (lat, ctx, cm, rope, kp, vpp, ts)  # keep inputs alive until the work is done
+        return (cache_k, cache_v, hidden) if return_hidden else (cache_k, cache_v)
+
+
 # ---------------------------------------------------- compact expert engine
 def _f32(t: torch.Tensor, dev) -> torch.Tensor:
     return t.detach().to(device=dev, dtype=torch.float32).contiguous()

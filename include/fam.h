@@ -259,6 +259,59 @@ FAM_API int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* i
 FAM_API int fam_action_launch_count(const fam_action_expert* e, int32_t* count);
 
 /* ======================================================================
+ * Video DiT prefill (WanVideoDiT backbone) — BASELINE config 2.
+ *
+ * Replaces, for a bf16 model with separated per-token timesteps:
+ *   WanVideoDiT.prepare              FastWAM/src/fastwam/models/wan22/wan_video_dit.py:640-720
+ *   MoT.prefill_video_cache_tensor   .../wan22/mot.py:474-526
+ * The first latent frame's tokens use timestep 0 (wan_video_dit.py:671-677),
+ * so the time MLP runs on two rows per sample and every block reads the
+ * (first frame, rest) modulation pair.  Outputs per block the post-RMSNorm +
+ * RoPE K and the raw V, [B, S, H*d] bf16 each, and optionally the final token
+ * states (fp32 [B, S, D]; computing them adds the last block's post block).
+ * Blocks use the fam_action_layer layout.
+ * ====================================================================== */
+typedef struct fam_video_config {
+  int32_t hidden_dim, in_dim, ffn_dim, text_dim, freq_dim, num_heads, head_dim, num_layers;
+  int32_t patch_t, patch_h, patch_w;
+  float eps;
+} fam_video_config;
+
+typedef struct fam_video_weights {
+  const void *patch_w, *patch_b;   /* [D, in*pt*ph*pw] (Conv3d weight flattened), [D] */
+  const void *text0_w, *text0_b, *text2_w, *text2_b;
+  const void *time0_w, *time0_b, *time2_w, *time2_b, *tproj_w, *tproj_b;
+  const fam_action_layer* layers;  /* host array [L] */
+} fam_video_weights;
+
+typedef struct fam_video_expert fam_video_expert;
+
+typedef struct fam_video_io {
+  int32_t batch, frames, height, width; /* latent grid [B, in, F, H, W] */
+  int32_t context_tokens;
+  const void* latents;        /* bf16 [B, in, F, H, W] */
+  const float* timesteps;     /* host [B], already rounded to the model dtype */
+  const void* context;        /* bf16 [B, C, T] */
+  const uint8_t* context_mask;/* [B, C] or NULL */
+  const float* rope;          /* f32 [S, d/2, 2] per token (3-D RoPE of the grid) */
+  int32_t first_frame_causal; /* 1: first-frame tokens attend only to the first frame */
+  void* const* cache_k;       /* host array [L] of device [B, S, H*d] bf16 */
+  void* const* cache_v;
+  float* hidden_out;          /* f32 [B, S, D] or NULL */
+  void* workspace;
+  size_t workspace_bytes;
+} fam_video_io;
+
+FAM_API int fam_video_expert_create(const fam_video_config* cfg, const fam_video_weights* w,
+                                    fam_video_expert** out);
+FAM_API int fam_video_expert_destroy(fam_video_expert* e);
+FAM_API int fam_video_workspace_size(const fam_video_expert* e, int32_t batch, int32_t tokens,
+                                     int32_t context_tokens, size_t* bytes);
+FAM_API int fam_video_prefill(fam_video_expert* e, const fam_video_io* io, int32_t use_graph,
+                              void* stream);
+FAM_API int fam_video_launch_count(const fam_video_expert* e, int32_t* count);
+
+/* ======================================================================
  * Compact action expert (hidden width <= 64, e.g. the CAE expert of
  * CAE-FastWAM and BASELINE config 0): the whole Euler loop of a chunk in two
  * launches — the context side (text embedding + every block's cross K/V) and

@@ -49,6 +49,27 @@ def test_cae_expert_and_action_ae_layout_and_init():
     assert dit.is_compact()
 
 
+def test_wan_video_dit_layout_init_and_rope():
+    fx = torch.load(GOLDEN / "c2_video_prefill.pt", weights_only=False)
+    c = fx["dit_cfg"]
+    torch.manual_seed(2)  # make_golden.py seeds, then builds WanVideoDiT first
+    dit = M.WanVideoDiT(hidden_dim=c["hidden_dim"], in_dim=c["in_dim"], ffn_dim=c["ffn_dim"],
+                        out_dim=c["out_dim"], text_dim=c["text_dim"], freq_dim=c["freq_dim"],
+                        eps=c["eps"], patch_size=tuple(c["patch_size"]), num_heads=c["num_heads"],
+                        attn_head_dim=c["attn_head_dim"], num_layers=c["num_layers"],
+                        has_image_input=False, seperated_timestep=True,
+                        video_attention_mask_mode="first_frame_causal").to(torch.bfloat16)
+    sd = dit.state_dict()
+    assert list(sd.keys()) == list(fx["video"].keys())
+    for k, v in fx["video"].items():
+        assert torch.equal(sd[k], v), k
+    f, h, w = fx["grid"]
+    tab = M.rope_table_3d(c["attn_head_dim"], f, h, w)
+    ref = fx["freqs"].reshape(f * h * w, -1)
+    assert torch.allclose(tab[..., 0], ref.real.float(), atol=1e-6)
+    assert torch.allclose(tab[..., 1], ref.imag.float(), atol=1e-6)
+
+
 def test_schedule_helper_matches_oracle():
     for n, s in ((10, 1.0), (4, 5.0), (7, 3.0)):
         for dt in (torch.float32, torch.bfloat16):
