@@ -1,0 +1,133 @@
+"""Policy-level entry points built from the libfam engines.
+
+FastWAMActionPolicy.infer_action follows FastWAM.infer_action
+(FastWAM/src/fastwam/models/wan22/fastwam.py:1080-1274) from the first-frame
+latents on: seeded CPU noise, video prefill at timestep 0 into the per-block
+K/V cache, the MoT attention mask (action rows see the first video frame and
+every action token, fastwam.py:429-451), the flow-matching Euler loop of the
+action expert over the cache, and the optional Action-VAE decode, returning
+the chunk as fp32 on the CPU.  The observation VAE encode that produces the
+first-frame latents, and prompt encoding, are outside this path.
+
+CAEPipeline is BASELINE config 4: the video backbone forward once per chunk,
+the compact action expert cross-attending the backbone's final token states,
+and the Action-VAE decoder, over a batch of independent rollouts processed in
+micro-batches.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from .models import ActionAE, ActionDiT, WanVideoDiT, build_inference_schedule
+
+
+def mot_action_mask(video_seq_len: int, action_seq_len: int, tokens_per_frame: int,
+                    device=None) -> torch.Tensor:
+    """Action rows [Sa, Sv + Sa] of FastWAM._build_mot_attention_mask (fastwam.py:429-451):
+    every action token, and the first video frame only."""
+    m = torch.zeros(action_seq_len, video_seq_len + action_seq_len, dtype=torch.uint8, device=device)
+    m[:, video_seq_len:] = 1
+    m[:, :min(tokens_per_frame, video_seq_len)] = 1
+    return m
+
+
+class FastWAMActionPolicy:
+    def __init__(self, video_expert: WanVideoDiT, action_expert: ActionDiT,
+                 action_vae: Optional[ActionAE] = None, action_infer_shift: float = 5.0,
+                 torch_dtype=torch.bfloat16):
+        if video_expert.num_heads != action_expert.num_heads or \
+                video_expert.attn_head_dim != action_expert.attn_head_dim or \
+                video_expert.num_layers != action_expert.num_layers:
+            raise ValueError("experts must share layer count, heads and head dim (mot.py:38-52)")
+        self.video_expert = video_expert
+        self.action_expert = action_expert
+        self.action_vae = action_vae
+        self.shift = float(action_infer_shift)
+        self.torch_dtype = torch_dtype
+        self.device = next(action_expert.parameters()).device
+
+    @torch.no_grad()
+    def infer_action(self, first_frame_latents: torch.Tensor, context: torch.Tensor,
+                     context_mask: torch.Tensor, action_horizon: int, num_inference_steps: int = 20,
+                     sigma_shift: Optional[float] = None, seed: Optional[int] = None,
+                     return_action_latents: bool = False) -> dict:
+        vid, act = self.video_expert, self.action_expert
+        gen = None if seed is None else torch.Generator(device="cpu").manual_seed(seed)
+        latent_horizon = self.action_vae.cfg.num_tokens if self.action_vae is not None else action_horizon
+        noise = torch.randn((1, latent_horizon, act.action_dim), generator=gen, dtype=torch.float32)
+        lat = noise.to(device=self.device, dtype=self.torch_dtype)
+        # video prefill at timestep 0 (fastwam.py:1175-1234)
+        k, v = vid.prefill(first_frame_latents, torch.zeros(first_frame_latents.shape[0]), context,
+                           context_mask)
+        pt, ph, pw = vid.patch_size
+        tpf = (first_frame_latents.shape[3] // ph) * (first_frame_latents.shape[4] // pw)
+        Sv = k[0].shape[1]
+        mask = mot_action_mask(Sv, latent_horizon, tpf, device=self.device)
+        ts, ds = build_inference_schedule(num_inference_steps,
+                                          self.shift if sigma_shift is None else float(sigma_shift),
+                                          dtype=self.torch_dtype)
+        lat = act.engine().chunk(lat, ts, ds, context, context_mask, k, v, mask)
+        out = {}
+        if self.action_vae is not None:
+            out["action"] = self.action_vae.decode(lat.float())[0].to(dtype=self.torch_dtype).float().cpu()
+        else:
+            out["action"] = lat[0].float().cpu()
+        if return_action_latents:
+            out["action_latents"] = lat[0].float().cpu()
+        return out
+
+
+class CAEPipeline:
+    """backbone forward -> compact expert over its final token states ->
+    Action-VAE decode, for a batch of rollouts in micro-batches."""
+
+    def __init__(self, video: WanVideoDiT, expert: ActionDiT, ae: ActionAE, num_steps: int = 4,
+                 shift: float = 1.0, micro_batch: int = 16):
+        if not expert.is_compact():
+            raise ValueError("CAEPipeline expects a compact (hidden <= 64) action expert")
+        if expert.text_dim != video.hidden_dim:
+            raise ValueError("the expert's text_dim must equal the backbone hidden width")
+        self.video, self.expert, self.ae = video, expert, ae
+        self.ts, self.ds = build_inference_schedule(num_steps, shift, dtype=torch.float32)
+        self.micro_batch = micro_batch
+        self._bufs = {}
+
+    def _buffers(self, b: int, S: int, dev):
+        """Per micro-batch size: the K/V cache the prefill writes (the attention source of
+        every block) and the final token states, allocated once so that the captured
+        launch graphs replay."""
+        key = (b, S)
+        if key not in self._bufs:
+            v = self.video
+            HD = v.num_heads * v.attn_head_dim
+            ks = [torch.empty(b, S, HD, dtype=torch.bfloat16, device=dev) for _ in range(v.num_layers)]
+            vs = [torch.empty(b, S, HD, dtype=torch.bfloat16, device=dev) for _ in range(v.num_layers)]
+            hid = torch.empty(b, S, v.hidden_dim, dtype=torch.float32, device=dev)
+            self._bufs[key] = (ks, vs, hid)
+        return self._bufs[key]
+
+    @torch.no_grad()
+    def __call__(self, latents: torch.Tensor, timestep, context: torch.Tensor,
+                 context_mask: Optional[torch.Tensor], noise: torch.Tensor) -> torch.Tensor:
+        """latents [B, in, F, H, W], noise [B, num_tokens, latent_dim] -> actions [B, horizon, A]."""
+        B = latents.shape[0]
+        outs = []
+        t = timestep if torch.is_tensor(timestep) else torch.full((B,), float(timestep))
+        t = t.reshape(-1)
+        if t.numel() == 1:
+            t = t.expand(B)
+        for s in range(0, B, self.micro_batch):
+            e = min(B, s + self.micro_batch)
+            cm = context_mask[s:e] if context_mask is not None else None
+            pt, ph, pw = self.video.patch_size
+            S = (latents.shape[2] // pt) * (latents.shape[3] // ph) * (latents.shape[4] // pw)
+            ks, vs, hid = self._buffers(e - s, S, latents.device)
+            _, _, hidden = self.video.engine().prefill(latents[s:e], t[s:e], context[s:e], cm,
+                                                       return_hidden=True, cache_k=ks, cache_v=vs,
+                                                       hidden=hid)
+            lat = self.expert.engine().chunk(noise[s:e].to(hidden.device, torch.float32),
+                                             self.ts, self.ds, hidden)
+            outs.append(self.ae.decode(lat))
+        return torch.cat(outs)

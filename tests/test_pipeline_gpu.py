@@ -1,0 +1,104 @@
+"""Policy-level paths on the GPU vs the oracle composition of the same reference steps:
+FastWAMActionPolicy.infer_action (video prefill at t=0 -> MoT action chunk over the cache
+-> Action-VAE decode) and the config-4 CAE pipeline (backbone final states -> compact
+expert -> decoder) over a micro-batched batch of rollouts."""
+import importlib
+
+import pytest
+import torch
+
+from oracle import fam_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+M = importlib.import_module("faster-action-models_b200.models")
+P = importlib.import_module("faster-action-models_b200.pipeline")
+R = importlib.import_module("faster-action-models_b200.replicas")
+
+
+def _cos(a, b):
+    return torch.nn.functional.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0).item()
+
+
+def _video(D, H, hd, F, T, L, Cin, seed):
+    torch.manual_seed(seed)
+    return M.WanVideoDiT(hidden_dim=D, in_dim=Cin, ffn_dim=F, out_dim=Cin, text_dim=T, freq_dim=256,
+                         eps=1e-6, patch_size=(1, 2, 2), num_heads=H, attn_head_dim=hd,
+                         num_layers=L, has_image_input=False, seperated_timestep=True,
+                         video_attention_mask_mode="first_frame_causal")
+
+
+def test_infer_action_policy():
+    D, H, hd, L, T, Cin = 256, 2, 128, 2, 64, 16
+    vid = _video(D, H, hd, 512, T, L, Cin, 0).to(torch.bfloat16)
+    torch.manual_seed(1)
+    act = M.ActionDiT(hidden_dim=256, action_dim=16, ffn_dim=512, text_dim=T, freq_dim=256, eps=1e-6,
+                      num_heads=H, attn_head_dim=hd, num_layers=L).to(torch.bfloat16)
+    ae = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16,
+                                     decoder_hidden=64, video_cond_dim=0))
+    g = torch.Generator().manual_seed(2)
+    lat = torch.randn(1, Cin, 1, 8, 12, generator=g).bfloat16()  # one observation frame
+    ctx = torch.randn(1, 9, T, generator=g).bfloat16()
+    cm = torch.ones(1, 9, dtype=torch.bool)
+    # oracle composition (fp32 on the same bf16 weights)
+    vcfg = O.DiTConfig(hidden_dim=D, ffn_dim=512, num_heads=H, attn_head_dim=hd, num_layers=L,
+                       text_dim=T, in_dim=Cin, out_dim=Cin)
+    acfg = O.DiTConfig(hidden_dim=256, ffn_dim=512, num_heads=H, attn_head_dim=hd, num_layers=L,
+                       text_dim=T, action_dim=16)
+    vsd = {k: v.float() for k, v in vid.state_dict().items()}
+    asd = {k: v.float() for k, v in act.state_dict().items()}
+    dsd = {k: v.float() for k, v in ae.state_dict().items()}
+    tok, _, tmod, cemb, cmask, freqs, _, tpf = O.video_prepare(vsd, vcfg, lat.float(), torch.zeros(1),
+                                                               ctx.float(), cm)
+    ks, vs = O.prefill_video_cache(vsd, vcfg, tok, freqs, tmod, cemb, cmask,
+                                   O.build_video_to_video_mask(tok.shape[1], tpf))
+    Sv = tok.shape[1]
+    amask = O.build_mot_attention_mask(Sv, 8, tpf)[Sv:, :]
+    noise = torch.randn((1, 8, 16), generator=torch.Generator().manual_seed(42))
+    ref_lat = O.action_chunk_with_cache(asd, acfg, noise.bfloat16().float(), ctx.float(), cm, ks, vs,
+                                        amask, 4, 5.0)
+    ref = O.action_decode(dsd, O.DecoderConfig(7, 32, 8, 16, 64), ref_lat)[0]
+    pol = P.FastWAMActionPolicy(vid.cuda(), act.cuda(), ae.cuda(), action_infer_shift=5.0)
+    out = pol.infer_action(lat.cuda(), ctx.cuda(), cm.cuda(), action_horizon=32,
+                           num_inference_steps=4, seed=42, return_action_latents=True)
+    assert out["action"].shape == (32, 7) and out["action"].device.type == "cpu"
+    assert _cos(out["action_latents"], ref_lat[0]) >= 0.999
+    err = (out["action"] - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()) and _cos(out["action"], ref) >= 0.999, err
+
+
+def test_cae_pipeline_microbatched():
+    D, H, hd, L, T, Cin = 256, 2, 128, 2, 64, 16
+    vid = _video(D, H, hd, 512, T, L, Cin, 3).to(torch.bfloat16)
+    torch.manual_seed(4)
+    exp = M.ActionDiT(hidden_dim=32, action_dim=16, ffn_dim=128, text_dim=D, freq_dim=256, eps=1e-6,
+                      num_heads=4, attn_head_dim=8, num_layers=3)
+    ae = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16,
+                                     decoder_hidden=64, video_cond_dim=0))
+    B = 5
+    g = torch.Generator().manual_seed(5)
+    lat = torch.randn(B, Cin, 3, 8, 12, generator=g).bfloat16()
+    ctx = torch.randn(B, 6, T, generator=g).bfloat16()
+    cm = torch.ones(B, 6, dtype=torch.bool)
+    noise = R.seeded_noise(range(B), (8, 16))
+    t = torch.full((B,), 500.0).bfloat16()
+    vcfg = O.DiTConfig(hidden_dim=D, ffn_dim=512, num_heads=H, attn_head_dim=hd, num_layers=L,
+                       text_dim=T, in_dim=Cin, out_dim=Cin)
+    ecfg = O.DiTConfig(hidden_dim=32, ffn_dim=128, num_heads=4, attn_head_dim=8, num_layers=3,
+                       text_dim=D, action_dim=16)
+    vsd = {k: v.float() for k, v in vid.state_dict().items()}
+    esd = {k: v.float() for k, v in exp.state_dict().items()}
+    dsd = {k: v.float() for k, v in ae.state_dict().items()}
+    tok, _, tmod, cemb, cmask, freqs, _, tpf = O.video_prepare(vsd, vcfg, lat.float(), t.float(),
+                                                               ctx.float(), cm)
+    _, _, hidden = O.prefill_video_cache(vsd, vcfg, tok, freqs, tmod, cemb, cmask,
+                                         O.build_video_to_video_mask(tok.shape[1], tpf),
+                                         return_hidden=True)
+    ref = O.cae_chunk(esd, ecfg, dsd, O.DecoderConfig(7, 32, 8, 16, 64), noise, hidden,
+                      num_steps=4, shift=1.0)
+    pipe = P.CAEPipeline(vid.cuda(), exp.cuda(), ae.cuda(), num_steps=4, shift=1.0, micro_batch=2)
+    got = pipe(lat.cuda(), t, ctx.cuda(), cm.cuda(), noise.cuda()).cpu()
+    got2 = pipe(lat.cuda(), t, ctx.cuda(), cm.cuda(), noise.cuda()).cpu()  # graph replays
+    assert torch.equal(got, got2)
+    err = (got - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()) and _cos(got, ref) >= 0.999, err
