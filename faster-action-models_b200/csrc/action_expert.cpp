@@ -289,6 +289,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       aa.kv1_bs = io.video_batch_stride;
       aa.kv1_ts = io.video_token_stride;
       aa.S1 = io.video_tokens;
+      aa.kv1_const = 1;  // the video cache is a call input
     }
     aa.k2 = wsp<__nv_bfloat16>(c, c.L.ka);
     aa.v2 = wsp<__nv_bfloat16>(c, c.L.va);

@@ -30,7 +30,7 @@ struct AttnCfg {
   static constexpr int kRow = HD + 8;  // padded row: conflict-free fragment loads
   static constexpr int kBlockElems = kAttnKB * kRow;
   static constexpr int kKVBytes = 2 /*stages*/ * 2 /*K,V*/ * kBlockElems * 2;
-  static constexpr int kMaskBytes = 2 /*stages*/ * kQTile * kAttnKB;
+  static constexpr int kMaskBytes = 2 /*stages*/ * (kQTile * kAttnKB + kAttnKB);
   static constexpr int kBytes = kKVBytes + kMaskBytes;
 };
 
@@ -87,21 +87,42 @@ __device__ __forceinline__ void load_kv_block(const AttnArgs& a, __nv_bfloat16* 
   }
 }
 
-// attend bits of the (query tile, key block): 1 = attend.
+// Raw mask bytes of the (query tile, key block) -> sm[QT][64], and the per-batch
+// key-mask bytes -> sk[64].  16-byte cp.async copies with zero fill past the
+// row end (or past Sq) when the strides allow; plain byte loads otherwise.
+// Bytes of keys >= skv are zero (ignored by the validity test anyway).
 template <int HD, int WARPS>
-__device__ __forceinline__ void stage_mask(const AttnArgs& a, uint8_t* sm, int b, int q0, int j0,
-                                           int j_end) {
+__device__ __forceinline__ void stage_mask(const AttnArgs& a, uint8_t* sm, uint8_t* sk, int b,
+                                           int q0, int j0, int skv) {
   using Cfg = AttnCfg<HD, WARPS>;
-  const uint8_t* km = a.key_mask != nullptr ? a.key_mask + b * a.key_mask_bs : nullptr;
-  const int ff = a.first_frame_tokens;
-  for (int idx = threadIdx.x; idx < Cfg::kQTile * kAttnKB; idx += blockDim.x) {
-    const int qi = idx / kAttnKB, jj = idx % kAttnKB;
-    const int q = q0 + qi, j = j0 + jj;
-    bool ok = j < j_end && q < a.Sq;
-    if (ok && ff > 0 && q < ff) ok = j < ff;
-    if (ok && km != nullptr) ok = km[j] != 0;
-    if (ok && a.mask2d != nullptr) ok = a.mask2d[static_cast<long long>(q) * a.mask_rs + j] != 0;
-    sm[idx] = ok ? 1 : 0;
+  if (a.mask2d != nullptr) {
+    const bool vec = (a.mask_rs % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.mask2d) & 15) == 0);
+    if (vec) {
+      for (int idx = threadIdx.x; idx < Cfg::kQTile * (kAttnKB / 16); idx += blockDim.x) {
+        const int qi = idx / (kAttnKB / 16), c = idx % (kAttnKB / 16);
+        const int q = q0 + qi, j = j0 + 16 * c;
+        int n = skv - j;
+        n = n < 0 ? 0 : (n > 16 ? 16 : n);
+        if (q >= a.Sq) n = 0;
+        const uint8_t* src = n > 0 ? a.mask2d + static_cast<long long>(q) * a.mask_rs + j : a.mask2d;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sm + qi * kAttnKB + 16 * c)),
+                     "l"(src), "r"(n)
+                     : "memory");
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < Cfg::kQTile * kAttnKB; idx += blockDim.x) {
+        const int qi = idx / kAttnKB, jj = idx % kAttnKB;
+        const int q = q0 + qi, j = j0 + jj;
+        sm[idx] = (q < a.Sq && j < skv) ? a.mask2d[static_cast<long long>(q) * a.mask_rs + j] : 0;
+      }
+    }
+  }
+  if (a.key_mask != nullptr) {
+    const uint8_t* km = a.key_mask + b * a.key_mask_bs;
+    for (int jj = threadIdx.x; jj < kAttnKB; jj += blockDim.x) {
+      const int j = j0 + jj;
+      sk[jj] = j < skv ? km[j] : 0;
+    }
   }
 }
 
@@ -125,8 +146,22 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
   const int k_end = min(skv, k_begin + a.keys_per_split);
   const int q0 = qt * QT;
   const int qr0 = q0 + warp * 16 + g, qr1 = qr0 + 8;  // the two rows this thread owns
-  const bool has_mask = a.mask2d != nullptr || a.key_mask != nullptr || a.first_frame_tokens > 0;
+  const bool use_m2 = a.mask2d != nullptr, use_km = a.key_mask != nullptr;
+  const int ff = a.first_frame_tokens;
+  const int nblocks = k_end > k_begin ? (k_end - k_begin + kAttnKB - 1) / kAttnKB : 0;
+  __nv_bfloat16* sK[2] = {smem, smem + 2 * Cfg::kBlockElems};
+  __nv_bfloat16* sV[2] = {smem + Cfg::kBlockElems, smem + 3 * Cfg::kBlockElems};
+  uint8_t* sM[2] = {smask, smask + QT * kAttnKB};
+  uint8_t* sKm[2] = {smask + 2 * QT * kAttnKB, smask + 2 * QT * kAttnKB + kAttnKB};
 
+  // The first key block streams in before the programmatic-launch wait when it
+  // lies in a source that no earlier kernel of the chain writes (the video K/V
+  // cache); masks are call inputs and always qualify.
+  const bool pre = a.kv1_const && nblocks > 0 && min(k_begin + kAttnKB, k_end) <= a.S1;
+  if (pre) {
+    load_kv_block<HD, WARPS>(a, sK[0], sV[0], b, h, k_begin, k_end);
+    stage_mask<HD, WARPS>(a, sM[0], sKm[0], b, q0, k_begin, skv);
+  }
   pdl_wait();
   pdl_launch_dependents();
 
@@ -151,14 +186,9 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
   for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
-  const int nblocks = k_end > k_begin ? (k_end - k_begin + kAttnKB - 1) / kAttnKB : 0;
-  __nv_bfloat16* sK[2] = {smem, smem + 2 * Cfg::kBlockElems};
-  __nv_bfloat16* sV[2] = {smem + Cfg::kBlockElems, smem + 3 * Cfg::kBlockElems};
-  uint8_t* sM[2] = {smask, smask + QT * kAttnKB};
-
-  if (nblocks > 0) {
+  if (!pre && nblocks > 0) {
     load_kv_block<HD, WARPS>(a, sK[0], sV[0], b, h, k_begin, k_end);
-    if (has_mask) stage_mask<HD, WARPS>(a, sM[0], b, q0, k_begin, k_end);
+    stage_mask<HD, WARPS>(a, sM[0], sKm[0], b, q0, k_begin, skv);
   }
   cp_async_commit();
   for (int blk = 0; blk < nblocks; ++blk) {
@@ -166,7 +196,7 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
     const int j0 = k_begin + blk * kAttnKB;
     if (blk + 1 < nblocks) {
       load_kv_block<HD, WARPS>(a, sK[cur ^ 1], sV[cur ^ 1], b, h, j0 + kAttnKB, k_end);
-      if (has_mask) stage_mask<HD, WARPS>(a, sM[cur ^ 1], b, q0, j0 + kAttnKB, k_end);
+      stage_mask<HD, WARPS>(a, sM[cur ^ 1], sKm[cur ^ 1], b, q0, j0 + kAttnKB, skv);
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -175,6 +205,7 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
     const __nv_bfloat16* K = sK[cur];
     const __nv_bfloat16* V = sV[cur];
     const uint8_t* M = sM[cur];
+    const uint8_t* Km = sKm[cur];
     // S = Q K^T for 64 keys: 8 tiles of 8 keys.
     float s[8][4];
 #pragma unroll
@@ -197,14 +228,14 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int jj = n * 8 + 2 * t + e;
-        bool ok0, ok1;
-        if (has_mask) {
-          ok0 = M[r0 * kAttnKB + jj] != 0;
-          ok1 = M[r1 * kAttnKB + jj] != 0;
-        } else {
-          const bool kv_ok = j0 + jj < k_end;
-          ok0 = kv_ok && qr0 < a.Sq;
-          ok1 = kv_ok && qr1 < a.Sq;
+        const int j = j0 + jj;
+        bool kv_ok = j < k_end;
+        if (use_km) kv_ok = kv_ok && Km[jj] != 0;
+        bool ok0 = kv_ok && qr0 < a.Sq && (ff == 0 || qr0 >= ff || j < ff);
+        bool ok1 = kv_ok && qr1 < a.Sq && (ff == 0 || qr1 >= ff || j < ff);
+        if (use_m2) {
+          ok0 = ok0 && M[r0 * kAttnKB + jj] != 0;
+          ok1 = ok1 && M[r1 * kAttnKB + jj] != 0;
         }
         s[n][e] = ok0 ? s[n][e] * a.scale_log2 : -INFINITY;
         s[n][2 + e] = ok1 ? s[n][2 + e] * a.scale_log2 : -INFINITY;

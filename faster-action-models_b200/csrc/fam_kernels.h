@@ -116,6 +116,7 @@ struct AttnArgs {
   const __nv_bfloat16* v1;
   long long kv1_bs, kv1_ts;
   int S1;
+  int kv1_const;                 // source 1 is not written by earlier kernels of the chain
   const __nv_bfloat16* k2;
   const __nv_bfloat16* v2;
   long long kv2_bs, kv2_ts;

@@ -109,14 +109,33 @@ __device__ __forceinline__ float4 mod_value4(const ModRows& m, long long off, in
 constexpr int kMaxGroups = 4;  // D <= 4 * 4 * 256 = 4096
 __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNormArgs a) {
   __shared__ float red[33];
-  pdl_wait();
-  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int D = a.D;
   const int G = D / 4;
   float* x = a.x + static_cast<long long>(row) * D;
   const long long moff = a.mod.tmod != nullptr ? mod_row_offset(a.mod, row) : 0;
   const long long noff = a.nmod.tmod != nullptr ? mod_row_offset(a.nmod, row) : 0;
+  // Constants of the chain (bias, gate, norm affine / shift / scale) load before
+  // the programmatic-launch wait; only x and the partials depend on it.
+  float4 cb[kMaxGroups], cg[kMaxGroups], c0[kMaxGroups], c1[kMaxGroups];
+#pragma unroll
+  for (int i = 0; i < kMaxGroups; ++i) {
+    const int g = threadIdx.x + i * blockDim.x;
+    if (g >= G) break;
+    const int f = 4 * g;
+    cb[i] = (a.partials != nullptr && a.bias != nullptr) ? ld_bf4(a.bias + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+    cg[i] = (a.partials != nullptr && a.gate_chunk >= 0) ? mod_value4(a.mod, moff, a.gate_chunk, f, D)
+                                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+    if (a.norm_mode == kNormAffine) {
+      c0[i] = ld_bf4(a.norm_w + f);
+      c1[i] = ld_bf4(a.norm_b + f);
+    } else if (a.norm_mode == kNormAdaLN) {
+      c0[i] = mod_value4(a.nmod, noff, a.shift_chunk, f, D);      // shift
+      c1[i] = mod_value4(a.nmod, noff, a.shift_chunk + 1, f, D);  // scale
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
   float4 v[kMaxGroups];
   float lsum = 0.0f;
 #pragma unroll
@@ -127,10 +146,8 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
     float4 xv = *reinterpret_cast<const float4*>(x + f);
     if (a.partials != nullptr) {
       float4 y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * D + f);
-      if (a.bias != nullptr) y = f4add(y, ld_bf4(a.bias + f));
-      y = rbf4(y);  // the reference's Linear output is a bf16 tensor
-      const float4 gt = (a.gate_chunk >= 0) ? mod_value4(a.mod, moff, a.gate_chunk, f, D)
-                                            : make_float4(1.f, 1.f, 1.f, 1.f);
+      y = rbf4(f4add(y, cb[i]));  // the reference's Linear output is a bf16 tensor
+      const float4 gt = cg[i];
       xv = make_float4(xv.x + gt.x * y.x, xv.y + gt.y * y.y, xv.z + gt.z * y.z, xv.w + gt.w * y.w);
       if (a.round_residual) xv = rbf4(xv);
       *reinterpret_cast<float4*>(x + f) = xv;
@@ -158,11 +175,11 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
     float4 n = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd,
                            (v[i].w - mean) * rstd);
     if (a.norm_mode == kNormAffine) {
-      const float4 w = ld_bf4(a.norm_w + f), b = ld_bf4(a.norm_b + f);
+      const float4 w = c0[i], b = c1[i];
       n = make_float4(n.x * w.x + b.x, n.y * w.y + b.y, n.z * w.z + b.z, n.w * w.w + b.w);
     } else {  // AdaLN: LN(x) * (1 + scale) + shift
-      const float4 sh = mod_value4(a.nmod, noff, a.shift_chunk, f, D);
-      const float4 sc = mod_value4(a.nmod, noff, a.shift_chunk + 1, f, D);
+      const float4 sh = c0[i];
+      const float4 sc = c1[i];
       n = rbf4(n);
       n = make_float4(n.x * (1.f + sc.x) + sh.x, n.y * (1.f + sc.y) + sh.y, n.z * (1.f + sc.z) + sh.z,
                       n.w * (1.f + sc.w) + sh.w);
