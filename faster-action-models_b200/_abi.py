@@ -19,11 +19,18 @@ class ActionLayer(C.Structure):
         "ffn0_b", "ffn2_w", "ffn2_b")]
 
 
+class ActionStacks(C.Structure):
+    _fields_ = [(n, vp) for n in (
+        "qkv_w", "o_w", "cq_w", "co_w", "ffn0_w", "ffn2_w", "qkv_b", "o_b", "cq_b", "co_b",
+        "ffn0_b", "ffn2_b", "norm_q", "norm_k", "cnorm_q", "norm3_w", "norm3_b", "modulation")]
+
+
 class ActionWeights(C.Structure):
     _fields_ = [(n, vp) for n in (
         "enc_w", "enc_b", "text0_w", "text0_b", "text2_w", "text2_b", "time0_w", "time0_b",
         "time2_w", "time2_b", "tproj_w", "tproj_b", "head_w", "head_b")] + [
-        ("layers", C.POINTER(ActionLayer)), ("rope", vp), ("rope_positions", C.c_int32)]
+        ("layers", C.POINTER(ActionLayer)), ("rope", vp), ("rope_positions", C.c_int32),
+        ("stacks", C.POINTER(ActionStacks))]
 
 
 class ActionIO(C.Structure):
@@ -56,6 +63,10 @@ def declare(lib) -> None:
 def declare_counts(lib) -> None:
     lib.fam_action_launch_count.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
     lib.fam_action_launch_count.restype = C.c_int
+    lib.fam_action_set_mode.argtypes = [C.c_void_p, C.c_int32]
+    lib.fam_action_set_mode.restype = C.c_int
+    lib.fam_action_last_path.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
+    lib.fam_action_last_path.restype = C.c_int
 
 
 class AttentionDesc(C.Structure):

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "../../include/fam.h"
+#include "action_fused.h"
 #include "fam_internal.h"
 #include "fam_kernels.h"
 
@@ -45,6 +46,8 @@ int choose_splits(int n_out, int k, int rows) {
 
 struct WsLayout {
   size_t x, h, part, q, ka, va, ao, qc, ci, fh, apart, ctr, tmod, sin, th1, th2, cemb, ch1, ckv, vel;
+  size_t fsync, fssq, fpart;  // fused-kernel barrier / merge counters, RMS sums, split partials
+  size_t fsync_bytes, fssq_bytes;
   size_t total;
   int s_qkv, s_o, s_cq, s_co, s_f2;
 };
@@ -95,6 +98,14 @@ WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
   w.ch1 = take(crow * D * 2);
   w.ckv = take(static_cast<size_t>(c.num_layers) * crow * 2 * HD * 2);
   w.vel = take(rows * c.action_dim * 2);
+  // fused persistent kernel (batch 1): counters, per-token RMS sums, split partials
+  // [go, abort, merge counters] padded to a 128-byte line, then one flag line per CTA
+  w.fsync_bytes = ((2 + static_cast<size_t>(N) * c.num_layers * c.num_heads + 31) / 32 * 32 +
+                   static_cast<size_t>(kFusedMaxCtas) * 32) * 4;
+  w.fssq_bytes = static_cast<size_t>(N) * c.num_layers * 3 * kFusedRows * 4;
+  w.fsync = take(w.fsync_bytes);
+  w.fssq = take(w.fssq_bytes);
+  w.fpart = take(static_cast<size_t>(c.num_heads) * 64 * kFusedRows * 66 * 4);
   w.total = off;
   return w;
 }
@@ -117,6 +128,12 @@ struct fam_action_expert {
   CallKey graph_key;
   int* status = nullptr;
   int launch_count = 0;  // kernels enqueued by the last chunk / step call
+  bool has_stacks = false;
+  fam_action_stacks stacks = {};
+  CUtensorMap tm[6];     // stacked weights for the fused kernel
+  int num_sms = 0;
+  int mode = FAM_ACTION_AUTO;
+  int last_path = 0;
 };
 
 namespace {
@@ -459,9 +476,112 @@ int enqueue_chunk(const Ctx& c, void* latent, const float* ts, const float* ds, 
   return 0;
 }
 
+// Whether the fused persistent kernel can run this call.
+bool fused_eligible(const fam_action_expert* e, const fam_action_io* io, int N) {
+  const fam_action_config& g = e->cfg;
+  const int HD = g.num_heads * g.head_dim;
+  if (!e->has_stacks || e->num_sms < 64 || e->num_sms > kFusedMaxCtas) return false;
+  if (io->batch != 1 || io->action_tokens > kFusedRows || g.head_dim != 64 || g.action_dim > 16) return false;
+  if (g.hidden_dim % 256 || HD % 128 || g.ffn_dim % 128 || g.hidden_dim > 1024) return false;
+  if (g.num_layers > kFusedMaxLayers || io->context_tokens > 256 || N > kMaxSteps) return false;
+  if (3 * HD / 128 + HD / 128 + g.ffn_dim / 128 > e->num_sms) return false;
+  const int skv = io->video_tokens + io->action_tokens;
+  if ((skv + kFusedKeysPerSplit - 1) / kFusedKeysPerSplit > kFusedMaxSplits) return false;
+  if (io->video_tokens > 0 && (io->video_token_stride % 8)) return false;
+  return true;
+}
+
+int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float* ds, int N,
+                        void* trace) {
+  fam_action_expert* e = c.e;
+  const fam_action_config& g = e->cfg;
+  const fam_action_io& io = *c.io;
+  const int HD = g.num_heads * g.head_dim;
+  e->launch_count = 0;
+  FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.fsync), 0, c.L.fsync_bytes, c.st));
+  FAM_TRY(cudaMemsetAsync(wsp<void>(c, c.L.fssq), 0, c.L.fssq_bytes, c.st));
+  FAM_TRYI(enqueue_prologue(c, ts, N));
+  FusedArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int p = 0; p < 6; ++p) a.tm[p] = e->tm[p];
+  const fam_action_stacks& s = e->stacks;
+  a.qkv_b = bf(s.qkv_b);
+  a.o_b = bf(s.o_b);
+  a.cq_b = bf(s.cq_b);
+  a.co_b = bf(s.co_b);
+  a.ffn0_b = bf(s.ffn0_b);
+  a.ffn2_b = bf(s.ffn2_b);
+  a.norm_q = bf(s.norm_q);
+  a.norm_k = bf(s.norm_k);
+  a.cnorm_q = bf(s.cnorm_q);
+  a.norm3_w = bf(s.norm3_w);
+  a.norm3_b = bf(s.norm3_b);
+  a.modulation = bf(s.modulation);
+  a.enc_w = bf(e->w.enc_w);
+  a.enc_b = bf(e->w.enc_b);
+  a.head_w = bf(e->w.head_w);
+  a.head_b = bf(e->w.head_b);
+  a.tmod = wsp<float>(c, c.L.tmod);
+  a.rope = static_cast<const float2*>(e->w.rope);
+  for (int l = 0; l < g.num_layers; ++l) {
+    a.vk[l] = io.video_tokens > 0 ? bf(io.video_k[l]) : nullptr;
+    a.vv[l] = io.video_tokens > 0 ? bf(io.video_v[l]) : nullptr;
+  }
+  a.v_ts = io.video_token_stride;
+  a.Sv = io.video_tokens;
+  a.mask2d = io.attn_mask;
+  a.ckv = wsp<__nv_bfloat16>(c, c.L.ckv);
+  a.ctx_mask = io.context_mask;
+  a.C = io.context_tokens;
+  a.x = wsp<float>(c, c.L.x);
+  a.q = wsp<__nv_bfloat16>(c, c.L.q);
+  a.ka = wsp<__nv_bfloat16>(c, c.L.ka);
+  a.va = wsp<__nv_bfloat16>(c, c.L.va);
+  a.ao = wsp<__nv_bfloat16>(c, c.L.ao);
+  a.qc = wsp<__nv_bfloat16>(c, c.L.qc);
+  a.ci = wsp<__nv_bfloat16>(c, c.L.ci);
+  a.fh = wsp<__nv_bfloat16>(c, c.L.fh);
+  a.ssq = wsp<float>(c, c.L.fssq);
+  a.apart = wsp<float>(c, c.L.fpart);
+  a.sync = wsp<unsigned>(c, c.L.fsync);
+  a.flags = a.sync + (2 + static_cast<size_t>(N) * g.num_layers * g.num_heads + 31) / 32 * 32;
+  a.status = e->status;
+  a.latent = static_cast<__nv_bfloat16*>(latent);
+  a.trace = static_cast<__nv_bfloat16*>(trace);
+  for (int i = 0; i < N; ++i) a.deltas.t[i] = ds[i];
+  a.N = N;
+  a.L = g.num_layers;
+  a.R = io.action_tokens;
+  a.Sa = io.action_tokens;
+  a.D = g.hidden_dim;
+  a.HD = HD;
+  a.H = g.num_heads;
+  a.hd = g.head_dim;
+  a.F = g.ffn_dim;
+  a.A = g.action_dim;
+  a.splits = (io.video_tokens + io.action_tokens + kFusedKeysPerSplit - 1) / kFusedKeysPerSplit;
+  a.eps = g.eps;
+  a.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(g.head_dim));
+  FAM_LAUNCH(launch_fused_chunk(a, e->num_sms, c.st));
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int fam_action_set_mode(fam_action_expert* e, int32_t mode) {
+  if (e == nullptr || mode < FAM_ACTION_AUTO || mode > FAM_ACTION_FUSED) return set_error("bad mode");
+  if (mode == FAM_ACTION_FUSED && !e->has_stacks) return set_error("fused mode needs stacked weights");
+  e->mode = mode;
+  return FAM_OK;
+}
+
+int fam_action_last_path(const fam_action_expert* e, int32_t* path) {
+  if (e == nullptr || path == nullptr) return set_error("null argument");
+  *path = e->last_path;
+  return FAM_OK;
+}
 
 int fam_action_expert_create(const fam_action_config* cfg, const fam_action_weights* w,
                              fam_action_expert** out) {
@@ -487,6 +607,32 @@ int fam_action_expert_create(const fam_action_config* cfg, const fam_action_weig
   if (e->status == nullptr) return set_error("could not allocate the device status word");
   int rc = check_cuda(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking), "stream create");
   if (rc) return rc;
+  if (w->stacks != nullptr) {
+    const fam_action_stacks& s = *w->stacks;
+    const int D = cfg->hidden_dim, HD = cfg->num_heads * cfg->head_dim, F = cfg->ffn_dim;
+    const uint64_t L = static_cast<uint64_t>(cfg->num_layers);
+    const void* base[6] = {s.qkv_w, s.o_w, s.cq_w, s.co_w, s.ffn0_w, s.ffn2_w};
+    const uint64_t rows[6] = {3ull * HD, static_cast<uint64_t>(D), static_cast<uint64_t>(HD),
+                              static_cast<uint64_t>(D), static_cast<uint64_t>(F), static_cast<uint64_t>(D)};
+    const uint64_t cols[6] = {static_cast<uint64_t>(D), static_cast<uint64_t>(HD), static_cast<uint64_t>(D),
+                              static_cast<uint64_t>(HD), static_cast<uint64_t>(D), static_cast<uint64_t>(F)};
+    bool ok = true;
+    for (int p = 0; p < 6 && ok; ++p)
+      ok = base[p] != nullptr && make_tmap_bf16_2d(&e->tm[p], base[p], L * rows[p], cols[p], cols[p], 128);
+    if (ok) {
+      e->stacks = s;
+      e->w.stacks = &e->stacks;
+      e->has_stacks = true;
+      rc = check_cuda(fused_init_attributes(), "fused kernel attributes");
+      if (rc) return rc;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      rc = check_cuda(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+      if (rc) return rc;
+    } else {
+      e->w.stacks = nullptr;
+    }
+  }
   *out = e.release();
   return FAM_OK;
 }
@@ -521,10 +667,20 @@ int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent
   c.rows = io->batch * io->action_tokens;
   c.crow = io->batch * io->context_tokens;
   cudaStream_t user = static_cast<cudaStream_t>(stream);
+  const bool fused_ok = fused_eligible(e, io, num_steps);
+  if (e->mode == FAM_ACTION_FUSED && !fused_ok)
+    return set_error("fam_action_chunk: the fused kernel cannot run this call (batch 1, <= 32 tokens, "
+                     "head_dim 64, widths multiple of 128, stacked weights)");
+  const bool fused = fused_ok && e->mode != FAM_ACTION_CHAIN;
+  e->last_path = fused ? 2 : 1;
+  auto enqueue = [&](const Ctx& cc) {
+    return fused ? enqueue_chunk_fused(cc, latent, timesteps, deltas, num_steps, velocity_trace)
+                 : enqueue_chunk(cc, latent, timesteps, deltas, num_steps, velocity_trace);
+  };
   if (!use_graph) {
     c.st = user;
     c.pdl = true;
-    FAM_TRYI(enqueue_chunk(c, latent, timesteps, deltas, num_steps, velocity_trace));
+    FAM_TRYI(enqueue(c));
     return check_cuda(cudaGetLastError(), "fam_action_chunk launch");
   }
   CallKey key;
@@ -534,7 +690,7 @@ int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent
               static_cast<uintptr_t>(io->batch), static_cast<uintptr_t>(io->action_tokens),
               static_cast<uintptr_t>(io->context_tokens), static_cast<uintptr_t>(io->video_tokens),
               static_cast<uintptr_t>(io->video_batch_stride), static_cast<uintptr_t>(io->video_token_stride),
-              static_cast<uintptr_t>(num_steps)};
+              static_cast<uintptr_t>(num_steps), static_cast<uintptr_t>(fused ? 2 : 1)};
   for (int l = 0; io->video_tokens > 0 && l < e->cfg.num_layers; ++l) {
     key.ptrs.push_back(reinterpret_cast<uintptr_t>(io->video_k[l]));
     key.ptrs.push_back(reinterpret_cast<uintptr_t>(io->video_v[l]));
@@ -549,7 +705,7 @@ int fam_action_chunk(fam_action_expert* e, const fam_action_io* io, void* latent
     c.st = e->cap_stream;
     c.pdl = true;
     FAM_TRY(cudaStreamBeginCapture(c.st, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_chunk(c, latent, timesteps, deltas, num_steps, velocity_trace);
+    int rc = enqueue(c);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(c.st, &g);
     if (rc) {

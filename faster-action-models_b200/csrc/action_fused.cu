@@ -1,0 +1,1259 @@
+// Fused persistent action chunk: every Euler step x every block of the action
+// expert in ONE cooperative launch, one CTA per SM.
+//
+// At batch 1 the action path is latency bound (32 token rows against 0.8 GB
+// of weights per model evaluation): a chain of small kernels pays a launch /
+// grid-drain latency per op.  Here the weight stream is decoupled from the
+// activation dependency chain:
+//
+//   warp 0 (producer)   walks this CTA's static list of GEMM work items for the
+//                       whole chunk and TMA-loads their 128 x 64 weight tiles
+//                       into an 8-stage shared-memory ring as fast as the ring
+//                       drains — weights never depend on activations, so the
+//                       stream runs ahead across phase and step boundaries;
+//   warps 1..11         run the phases: stage the MMA B operand (the token
+//   (workers)           rows) straight from the fp32 residual stream with the
+//                       block's LayerNorm / AdaLN folded in, issue tcgen05.mma
+//                       (warp 1 lane 0) into a 128 x 32 fp32 TMEM accumulator,
+//                       and apply the epilogue in warps 2..5 (bias, RMSNorm
+//                       statistics, RoPE, GELU, gated residual adds as fp32
+//                       atomics into the residual stream).  Attention phases
+//                       use bf16 mma.sync fragments over cp.async-staged K/V.
+//
+// Per block the phases are separated by grid barriers:
+//   qkv GEMM (AdaLN1 prologue; q/k RMSNorm sums + weight + RoPE epilogue)
+//   -> joint attention over [video cache ; action] (RMSNorm scales applied to
+//      the logits; split-KV merged by the last CTA per head)
+//   -> o GEMM (+= gate_msa, split by head)  -> cross-q GEMM (norm3 prologue)
+//   -> cross attention -> cross-o GEMM (+=) -> ffn.0 GEMM (AdaLN2 prologue,
+//      GELU epilogue) -> ffn.2 GEMM (+= gate_mlp, split by ffn.0 tile)
+// and each step starts with action_encoder and ends with head + Euler update.
+//
+// RMSNorm over the whole H*d row (wan_video_dit.py:146-157) is applied as a
+// per-token scale: RMSNorm(y)*w then RoPE equals s(y) * RoPE(y*w) because the
+// rotation is linear, so the GEMM epilogue stores RoPE(y*w) and accumulates
+// sum(y^2) per token; the attention multiplies q by s_q and the logits of the
+// fresh keys by s_k.  Reference numerics otherwise as the separate kernels:
+// DiTBlock.forward (wan_video_dit.py:248-267), MoT joint attention
+// (mot.py:528-578), scheduler step (scheduler_continuous.py:82-88).
+#include "action_fused.h"
+#include "fam_common.cuh"
+#include "fam_internal.h"
+#include "fam_mma.cuh"
+
+namespace fam {
+
+constexpr int kATile = 128 * 64 * 2;          // one weight tile (16 KB)
+constexpr int kBBlock = kFusedRows * 128;     // one B k-block: 32 rows x 128 B (4 KB)
+constexpr int kKvRow = 64 + 8;                // padded K/V row (head_dim 64)
+constexpr int kFusedIssuers = 4;               // MMA-issuing threads per GEMM item
+constexpr int kFusedIssuer1 = 6;               // warps kFusedIssuer1.. host issuers 1..
+static_assert(kFusedIssuer1 + kFusedIssuers - 1 <= kFusedThreads / 32 && kFusedIssuers % 2 == 0, "issuer warps");
+constexpr int kSplitStride = kFusedRows * 64 + kFusedRows * 2;  // floats per split partial
+// Staging layout for the GEMM phases: the B operand (<= 16 K blocks = 64 KB,
+// D <= 1024), then the RoPE (cos, sin) slices of the q/k epilogue warps
+// (4 x 32 tokens x 16 pairs), then the LayerNorm constants (2 x D fp32).
+constexpr int kStgRope = 16 * kBBlock;
+constexpr int kStgLnConst = kStgRope + 4 * kFusedRows * 16 * 8;
+static_assert(kStgLnConst + 2 * 1024 * 4 <= kFusedStaging, "staging layout");
+
+struct FusedSmemTail {
+  uint64_t full[kFusedRing];
+  uint64_t empty[kFusedRing];
+  uint64_t accum;
+  uint32_t tmem;
+  volatile int abort;
+  float stat[kFusedRows][2];
+  float scale[2][kFusedRows];                 // per-row q scale, per-key scale
+  int last;
+};
+
+__host__ __device__ constexpr size_t fused_tail_offset() {
+  return static_cast<size_t>(kFusedRing) * kATile + kFusedStaging;
+}
+size_t fused_smem_bytes() { return fused_tail_offset() + sizeof(FusedSmemTail) + 1024; }
+
+__device__ __forceinline__ void bar_workers() {
+  asm volatile("barrier.sync 1, %0;" ::"r"(kFusedWorkers) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------- schedule
+struct FItem {
+  int n;       // 128-row tile of the output features
+  int sub;     // head (o, co), ffn.0 tile (ffn2), 0 otherwise
+  int kb0;     // first 64-wide K block
+  int nkb;     // K blocks
+};
+
+__device__ __forceinline__ int f_rows(const FusedArgs& a, int p) {
+  switch (p) {
+    case kFQkv: return 3 * a.HD;
+    case kFO: return a.D;
+    case kFCq: return a.HD;
+    case kFCo: return a.D;
+    case kFFfn0: return a.F;
+    default: return a.D;
+  }
+}
+// Split-K items of the residual GEMMs take a group of heads (o, cross-o) or of
+// ffn.0 tiles (ffn.2): fewer fp32 atomic contributions per output element.
+__device__ __forceinline__ int f_head_group(const FusedArgs& a) {
+  return (a.H % 4 == 0) ? 4 : ((a.H % 2 == 0) ? 2 : 1);
+}
+__device__ __forceinline__ int f_ffn_group(const FusedArgs& a) {
+  const int js = a.F / 128;
+  return (js % 4 == 0) ? 4 : ((js % 2 == 0) ? 2 : 1);
+}
+__device__ __forceinline__ int f_count(const FusedArgs& a, int p) {
+  const int nt = f_rows(a, p) / 128;
+  if (p == kFO || p == kFCo) return nt * (a.H / f_head_group(a));
+  if (p == kFFfn2) return nt * (a.F / 128 / f_ffn_group(a));
+  return nt;
+}
+// CTA offsets spread the full-K tiles (qkv, cross-q, ffn.0) over distinct SMs.
+__device__ __forceinline__ int f_offset(const FusedArgs& a, int p) {
+  switch (p) {
+    case kFQkv: return 0;
+    case kFCq: return 3 * a.HD / 128;
+    case kFFfn0: return 3 * a.HD / 128 + a.HD / 128;
+    default: return 3 * a.HD / 128 + a.HD / 128 + a.F / 128;
+  }
+}
+__device__ __forceinline__ FItem f_item(const FusedArgs& a, int p, int i) {
+  FItem it;
+  const int kbs_full = a.D / 64;
+  if (p == kFO || p == kFCo) {
+    const int hg = f_head_group(a), groups = a.H / hg;
+    it.n = i / groups;
+    it.sub = i % groups;
+    it.kb0 = it.sub * hg * (a.hd / 64);
+    it.nkb = hg * (a.hd / 64);
+  } else if (p == kFFfn2) {
+    const int fg = f_ffn_group(a), groups = a.F / 128 / fg;
+    it.n = i / groups;
+    it.sub = i % groups;
+    it.kb0 = it.sub * 2 * fg;
+    it.nkb = 2 * fg;
+  } else {
+    it.n = i;
+    it.sub = 0;
+    it.kb0 = 0;
+    it.nkb = kbs_full;
+  }
+  return it;
+}
+__device__ __forceinline__ int f_first(const FusedArgs& a, int p, int cta, int G) {
+  return ((cta - f_offset(a, p)) % G + G) % G;
+}
+
+// ----------------------------------------------------------- grid barrier
+// Flag barrier (no contended atomic, one propagation hop): every CTA
+// release-stores the barrier index into its own 128-byte flag line, and worker
+// thread i of every CTA acquire-polls the line of CTA i.  Every wait is
+// bounded; a timeout or an abort raised elsewhere sets the abort word and
+// every CTA leaves its phase loop.
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ bool poll_ge(const FusedArgs& a, const unsigned* p, unsigned target,
+                                        FusedSmemTail* tl) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire(p) < target) {
+    if (ld_acquire(a.sync + 1) != 0 || globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (ld_acquire(a.sync + 1) == 0) record_error(a.status, kErrWaitFull);
+      atomicExch(a.sync + 1, 1u);
+      tl->abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool grid_sync(const FusedArgs& a, unsigned& epoch, FusedSmemTail* tl) {
+  // The CTA barrier orders the phase's writes of every worker before the
+  // flag thread's fence + release store (cumulative), as in a cooperative
+  // grid sync: one fence per CTA, not one per thread.
+  bar_workers();
+  ++epoch;
+  const int wt = threadIdx.x - 32;
+  if (wt == 0) {
+    __threadfence();
+    st_release(a.flags + blockIdx.x * 32, epoch);
+  }
+  // one hop: worker thread i of every CTA waits for CTA i's arrival
+  if (wt < static_cast<int>(gridDim.x)) poll_ge(a, a.flags + wt * 32, epoch, tl);
+  bar_workers();
+  return tl->abort == 0;
+}
+
+// -------------------------------------------------------- B operand staging
+// Write 8 bf16 (16 bytes) as chunk c of row r of K block kb, 128-byte swizzle
+// (the layout a TMA SWIZZLE_128B load produces and the UMMA descriptor reads).
+__device__ __forceinline__ void stage_chunk(uint8_t* stg, int kb, int r, int c, uint4 v) {
+  *reinterpret_cast<uint4*>(stg + kb * kBBlock + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  u.x = pack_bf16(f[0], f[1]);
+  u.y = pack_bf16(f[2], f[3]);
+  u.z = pack_bf16(f[4], f[5]);
+  u.w = pack_bf16(f[6], f[7]);
+  return u;
+}
+
+// modulation chunk c of block l at step s for feature f: bf16(bf16(t_mod) + modulation)
+__device__ __forceinline__ float f_mod(const FusedArgs& a, int step, int l, int c, int f) {
+  const float t = rbf(a.tmod[static_cast<long long>(step) * 6 * a.D + c * a.D + f]);
+  return rbf(t + bf2f(a.modulation[(static_cast<long long>(l) * 6 + c) * a.D + f]));
+}
+
+__device__ __forceinline__ void ld_bf8(const __nv_bfloat16* p, float* o) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = __low2float(h[i]);
+    o[2 * i + 1] = __high2float(h[i]);
+  }
+}
+__device__ __forceinline__ void ld_f8(const float* p, float* o) {
+  const float4 a0 = *reinterpret_cast<const float4*>(p), a1 = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a0.x; o[1] = a0.y; o[2] = a0.z; o[3] = a0.w;
+  o[4] = a1.x; o[5] = a1.y; o[6] = a1.z; o[7] = a1.w;
+}
+
+// LayerNorm of the residual rows into the B staging.  mode 0: AdaLN with
+// chunks (c0, c0+1); mode 1: affine norm3 of block l.  Each lane owns the
+// 8-wide column chunks lane + 32u (u < NCH, D = 256 NCH).
+//
+// The per-column constants (1 + scale and shift, or the norm3 weight and
+// bias) do not depend on the residual: ln_const_prefetch stores them as fp32
+// into shared memory behind the B operand at the end of the phase before,
+// after this CTA's own items of that phase (the staging is free then; with
+// the CTA offsets of the schedule the LayerNorm-GEMM CTAs are idle in the
+// phase before, so the prefetch is off the critical path), and every item of
+// the phase reads them there.  The residual rows are loaded up front so the L2
+// round trips overlap: the warp's first two rows together, the third while
+// the first two are normalised.
+__device__ __forceinline__ void bf8_unpack(const uint4& u, float* o) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = __low2float(h[i]);
+    o[2 * i + 1] = __high2float(h[i]);
+  }
+}
+
+// fp32 [D] multiplier then [D] addend at stg + kStgLnConst; worker thread t
+// handles the 8-wide column chunk t.
+__device__ void ln_const_prefetch(const FusedArgs& a, uint8_t* stg, int step, int l, int mode, int c0) {
+  const int D = a.D;
+  for (int ch = threadIdx.x - 32; ch < D / 8; ch += kFusedWorkers) {
+    const int f0 = ch * 8;
+    float m[8], ad[8];
+    if (mode == 0) {
+      float t0[8], t1[8], w0[8], w1[8];
+      const float* tm = a.tmod + static_cast<long long>(step) * 6 * D;
+      ld_f8(tm + c0 * D + f0, t0);
+      ld_f8(tm + (c0 + 1) * D + f0, t1);
+      ld_bf8(a.modulation + (static_cast<long long>(l) * 6 + c0) * D + f0, w0);
+      ld_bf8(a.modulation + (static_cast<long long>(l) * 6 + c0 + 1) * D + f0, w1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ad[e] = rbf(rbf(t0[e]) + w0[e]);        // shift
+        m[e] = 1.f + rbf(rbf(t1[e]) + w1[e]);   // 1 + scale
+      }
+    } else {
+      ld_bf8(a.norm3_w + static_cast<long long>(l) * D + f0, m);
+      ld_bf8(a.norm3_b + static_cast<long long>(l) * D + f0, ad);
+    }
+    float* cm = reinterpret_cast<float*>(stg + kStgLnConst) + f0;
+    float* ca = cm + D;
+    reinterpret_cast<float4*>(cm)[0] = make_float4(m[0], m[1], m[2], m[3]);
+    reinterpret_cast<float4*>(cm)[1] = make_float4(m[4], m[5], m[6], m[7]);
+    reinterpret_cast<float4*>(ca)[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+    reinterpret_cast<float4*>(ca)[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+  }
+}
+
+// L2 load kept at its place in the program (volatile asm): the residual rows
+// of the next LayerNorm rows are issued before the current row is
+// normalised, and the compiler would otherwise sink them to their first use.
+__device__ __forceinline__ float4 ld_cg_f4_early(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <int NCH>
+__device__ __forceinline__ void ln_load_row(const FusedArgs& a, int r, int lane, float (&v)[NCH * 8]) {
+  const float* xr = a.x + static_cast<long long>(r) * (NCH * 256);
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int ch = lane + 32 * u;
+    float4 p0 = make_float4(0.f, 0.f, 0.f, 0.f), p1 = p0;
+    if (r < a.R) {
+      p0 = ld_cg_f4_early(xr + ch * 8);
+      p1 = ld_cg_f4_early(xr + ch * 8 + 4);
+    }
+    v[8 * u + 0] = p0.x; v[8 * u + 1] = p0.y; v[8 * u + 2] = p0.z; v[8 * u + 3] = p0.w;
+    v[8 * u + 4] = p1.x; v[8 * u + 5] = p1.y; v[8 * u + 6] = p1.z; v[8 * u + 7] = p1.w;
+  }
+}
+
+template <int NCH>
+__device__ __forceinline__ void ln_store_row(const FusedArgs& a, uint8_t* stg, int r, int lane, int mode,
+                                             const float (&f)[NCH * 8]) {
+  constexpr int D = NCH * 256;
+  if (r >= a.R) {
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int ch = lane + 32 * u;
+      stage_chunk(stg, ch >> 3, r, ch & 7, make_uint4(0, 0, 0, 0));
+    }
+    return;
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCH * 8; ++i) sum += f[i];
+  const float mean = warp_sum(sum) / D;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCH * 8; ++i) {
+    const float d = f[i] - mean;
+    var += d * d;
+  }
+  const float rstd = rsqrtf(warp_sum(var) / D + a.eps);
+  const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst);
+  const float4* ca = cm + D / 4;
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int ch = lane + 32 * u;
+    const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = ca[2 * ch], a1 = ca[2 * ch + 1];
+    const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float n = (f[u * 8 + e] - mean) * rstd;
+      o[e] = mode == 0 ? rbf(n) * mv[e] + av[e] : n * mv[e] + av[e];
+    }
+    stage_chunk(stg, ch >> 3, r, ch & 7, pack8(o));
+  }
+}
+
+template <int NCH>
+__device__ void stage_layernorm_t(const FusedArgs& a, uint8_t* stg, int mode) {
+  const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int r0 = wid, r1 = wid + 11, r2 = wid + 22;  // 11 worker warps over 32 rows
+  float xa[NCH * 8], xb[NCH * 8];
+  ln_load_row<NCH>(a, r0, lane, xa);
+  ln_load_row<NCH>(a, r1, lane, xb);
+  ln_store_row<NCH>(a, stg, r0, lane, mode, xa);
+  if (r2 < kFusedRows) ln_load_row<NCH>(a, r2, lane, xa);
+  ln_store_row<NCH>(a, stg, r1, lane, mode, xb);
+  if (r2 < kFusedRows) ln_store_row<NCH>(a, stg, r2, lane, mode, xa);
+}
+
+__device__ void stage_layernorm(const FusedArgs& a, uint8_t* stg, int mode) {
+  switch (a.D >> 8) {
+    case 1: stage_layernorm_t<1>(a, stg, mode); break;
+    case 2: stage_layernorm_t<2>(a, stg, mode); break;
+    case 3: stage_layernorm_t<3>(a, stg, mode); break;
+    default: stage_layernorm_t<4>(a, stg, mode); break;
+  }
+}
+
+// Copy columns [col0, col0 + 64 * nkb) of a bf16 [R, ld] buffer into the
+// staging (nkb <= 8: at most 6 16-byte chunks per worker thread).  All loads
+// are issued before the first shared-memory store so they overlap.
+__device__ void stage_copy(const FusedArgs& a, uint8_t* stg, const __nv_bfloat16* src, long long ld,
+                           int col0, int nkb) {
+  constexpr int kMaxPer = (kFusedRows * 64 + kFusedWorkers - 1) / kFusedWorkers;  // 8 K blocks
+  const int per_row = nkb * 8;
+  const int total = kFusedRows * per_row;
+  uint4 v[kMaxPer];
+#pragma unroll
+  for (int u = 0; u < kMaxPer; ++u) {
+    const int idx = threadIdx.x - 32 + u * kFusedWorkers;
+    const int r = idx / per_row, ch = idx % per_row;
+    v[u] = make_uint4(0, 0, 0, 0);
+    if (idx < total && r < a.R) v[u] = __ldcg(reinterpret_cast<const uint4*>(src + r * ld + col0 + ch * 8));
+  }
+#pragma unroll
+  for (int u = 0; u < kMaxPer; ++u) {
+    const int idx = threadIdx.x - 32 + u * kFusedWorkers;
+    const int r = idx / per_row, ch = idx % per_row;
+    if (idx < total) stage_chunk(stg, ch >> 3, r, ch & 7, v[u]);
+  }
+}
+
+// ------------------------------------------------------------- epilogues
+// Per-feature constants of an epilogue, loaded before the accumulator wait so
+// their latency overlaps the MMA: bias, and the RMSNorm weight (qkv q/k,
+// cross-q) or the residual gate (o, ffn.2); plus the RoPE (cos, sin) of every
+// token for the q/k features.
+// The epilogue runs on 8 warps: warps 2..5 take the tokens 0..15 and warps
+// 6..9 the tokens 16..31 of the TMEM lane quarter warp % 4 (one output
+// feature per lane), so two warps share every scheduler.
+constexpr int kEpiTokens = kFusedRows / 2;
+
+struct EpiConst {
+  float bias, mul;
+  const float2* rope;  // [16 tokens][16 pairs] of this warp's features (shared memory)
+};
+
+__device__ __forceinline__ void epi_load(const FusedArgs& a, uint8_t* stg, int p, int step, int l,
+                                         const FItem& it, int f, int t0, EpiConst& c) {
+  const int D = a.D, HD = a.HD;
+  c.mul = 1.f;
+  switch (p) {
+    case kFQkv: {
+      const int type = f / HD, ff = f % HD;
+      c.bias = bf2f(a.qkv_b[static_cast<long long>(l) * 3 * HD + f]);
+      if (type == 2) return;
+      c.mul = bf2f((type == 0 ? a.norm_q : a.norm_k)[static_cast<long long>(l) * HD + ff]);
+      // this warp's 16 rotation pairs (lanes 2i, 2i+1 share pair i) for its
+      // tokens -> shared memory
+      const int lane = threadIdx.x & 31, q = (threadIdx.x >> 5) & 3;
+      const int pi0 = (ff % a.hd - lane) >> 1;
+      float2* sr = reinterpret_cast<float2*>(stg + kStgRope) + (q * kFusedRows + t0) * 16;
+      float2 cs[kEpiTokens * 16 / 32];
+#pragma unroll
+      for (int k = 0; k < kEpiTokens * 16 / 32; ++k) {
+        const int idx = lane + 32 * k, j = t0 + (idx >> 4), pl = idx & 15;
+        cs[k] = j < a.R ? a.rope[(j % a.Sa) * (a.hd >> 1) + pi0 + pl] : make_float2(1.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < kEpiTokens * 16 / 32; ++k) sr[lane + 32 * k] = cs[k];
+      __syncwarp();
+      c.rope = sr;
+      return;
+    }
+    case kFO:
+    case kFCo:
+    case kFFfn2: {
+      const __nv_bfloat16* bptr = p == kFO ? a.o_b : (p == kFCo ? a.co_b : a.ffn2_b);
+      if (p == kFO) c.mul = f_mod(a, step, l, 2, f);
+      if (p == kFFfn2) c.mul = f_mod(a, step, l, 5, f);
+      c.bias = it.sub == 0 ? bf2f(bptr[static_cast<long long>(l) * D + f]) : 0.f;
+      return;
+    }
+    case kFCq:
+      c.bias = bf2f(a.cq_b[static_cast<long long>(l) * HD + f]);
+      c.mul = bf2f(a.cnorm_q[static_cast<long long>(l) * HD + f]);
+      return;
+    default:
+      c.bias = bf2f(a.ffn0_b[static_cast<long long>(l) * a.F + f]);
+      return;
+  }
+}
+
+// Per-token sums over the 32 lanes for the 16 tokens of a warp: after the
+// recursive halving (15 shuffles) lanes l and l ^ 16 hold the half sums of
+// token l & 15, one more exchange completes them.
+__device__ __forceinline__ float warp_transpose_sum16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = upper ? v[i] : v[i + w];
+      const float keep = upper ? v[i + w] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
+}
+
+// Epilogue of one output feature f (this lane) for the tokens t0 .. t0 + 15.
+__device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int step, int l, int f, int t0,
+                                              const EpiConst& c, float (&v)[kEpiTokens]) {
+  const int lane = threadIdx.x & 31;
+  const int R = a.R, D = a.D, HD = a.HD;
+  switch (p) {
+    case kFQkv: {
+      const int type = f / HD, ff = f % HD;
+      if (type == 2) {
+#pragma unroll
+        for (int j = 0; j < kEpiTokens; ++j)
+          if (t0 + j < R) a.va[(t0 + j) * HD + ff] = f2bf(rbf(v[j] + c.bias));
+        return;
+      }
+      float* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + type) * kFusedRows;
+      __nv_bfloat16* dst = type == 0 ? a.q : a.ka;
+#pragma unroll
+      for (int j = 0; j < kEpiTokens; ++j) {
+        const float y = rbf(v[j] + c.bias);
+        v[j] = y * y;
+        const float z = rbf(y * c.mul);
+        const float pz = __shfl_xor_sync(0xffffffffu, z, 1);
+        const float2 cs = c.rope[j * 16 + (lane >> 1)];
+        const float o = (lane & 1) ? (pz * cs.y + z * cs.x) : (z * cs.x - pz * cs.y);
+        if (t0 + j < R) dst[(t0 + j) * HD + ff] = f2bf(o);
+      }
+      const float mine = warp_transpose_sum16(v);  // lanes l, l ^ 16: token t0 + (l & 15)
+      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, mine);
+      return;
+    }
+    case kFO:
+    case kFCo:
+    case kFFfn2:
+#pragma unroll
+      for (int j = 0; j < kEpiTokens; ++j)
+        if (t0 + j < R) atomicAdd(a.x + (t0 + j) * D + f, c.mul * (v[j] + c.bias));
+      return;
+    case kFCq: {
+      float* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + 2) * kFusedRows;
+#pragma unroll
+      for (int j = 0; j < kEpiTokens; ++j) {
+        const float y = rbf(v[j] + c.bias);
+        v[j] = y * y;
+        if (t0 + j < R) a.qc[(t0 + j) * HD + f] = f2bf(rbf(y * c.mul));
+      }
+      const float mine = warp_transpose_sum16(v);
+      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, mine);
+      return;
+    }
+    default:  // ffn.0 + GELU(tanh)
+#pragma unroll
+      for (int j = 0; j < kEpiTokens; ++j)
+        if (t0 + j < R) a.fh[(t0 + j) * a.F + f] = f2bf(gelu_tanh(rbf(v[j] + c.bias)));
+      return;
+  }
+}
+
+// One GEMM work item on the workers (the weight tiles arrive through the ring).
+__device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, FusedSmemTail* tl,
+                          int p, int step, int l, const FItem& it, uint32_t& ring_it,
+                          uint32_t& items_done) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1. B operand
+  switch (p) {
+    case kFQkv: stage_layernorm(a, stg, 0); break;
+    case kFCq: stage_layernorm(a, stg, 1); break;
+    case kFFfn0: stage_layernorm(a, stg, 0); break;
+    case kFO: stage_copy(a, stg, a.ao, a.HD, it.kb0 * 64, it.nkb); break;
+    case kFCo: stage_copy(a, stg, a.ci, a.HD, it.kb0 * 64, it.nkb); break;
+    default: stage_copy(a, stg, a.fh, a.F, it.kb0 * 64, it.nkb); break;
+  }
+  fence_async_smem();
+  bar_workers();
+  // 2. MMA: kFusedIssuers issuing threads (lane 0 of warps 1, 6, 7, 8; issuer
+  // j takes the K blocks k = j mod kFusedIssuers) into separate TMEM
+  // accumulators summed by the epilogue.  A single thread's tcgen05.mma issue
+  // rate (with its barrier wait and commit per K block) bounds a skinny
+  // (N = 32) GEMM; independent issuers multiply it.  Descriptors advance in
+  // their address field (address >> 4): kATile per ring slot, kBBlock per B K
+  // block.
+  const int j = warp == 1 ? 0 : warp - (kFusedIssuer1 - 1);
+  if ((warp == 1 || (warp >= kFusedIssuer1 && warp < kFusedIssuer1 + kFusedIssuers - 1)) && lane == 0) {
+    const uint32_t idesc = umma_idesc_bf16(128, kFusedRows);
+    const uint64_t da0 = umma_desc_sw128(ring), db0 = umma_desc_sw128(stg);
+    const uint32_t acc = tl->tmem + j * kFusedRows;
+    bool ok = tl->abort == 0;
+    for (int k = j; k < it.nkb && ok; k += kFusedIssuers) {
+      const uint32_t r = ring_it + k, s = r % kFusedRing;
+      ok = mbar_wait(&tl->full[s], (r / kFusedRing) & 1, a.status, kErrWaitFull);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t da = da0 + static_cast<uint64_t>(s * (kATile >> 4));
+      const uint64_t db = db0 + static_cast<uint64_t>(k * (kBBlock >> 4));
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_bf16_ss(acc, da + 2 * kk, db + 2 * kk, idesc, (k > j || kk != 0) ? 1u : 0u);
+      umma_commit(&tl->empty[s]);
+    }
+    if (!ok) tl->abort = 1;
+    umma_commit(&tl->accum);  // kFusedIssuers arrivals complete the phase
+  }
+  const int nkb = it.nkb;
+  ring_it += nkb;
+  // 3. epilogue (warps 2..9: TMEM lane quarter warp % 4, tokens t0 .. t0 + 15)
+  if (warp >= 2 && warp <= 9) {
+    const int q = warp & 3, t0 = warp >= 6 ? kEpiTokens : 0;
+    const int f = it.n * 128 + q * 32 + lane;
+    EpiConst c;
+    epi_load(a, stg, p, step, l, it, f, t0, c);
+    const bool ok = mbar_wait(&tl->accum, items_done & 1, a.status, kErrWaitAccum);
+    tc_fence_after();
+    if (!ok) tl->abort = 1;
+    // the issuers' accumulators (an issuer without K blocks left its
+    // accumulator stale: selected out), one TMEM wait
+    float v[kEpiTokens];
+    const uint32_t tq = tl->tmem + (static_cast<uint32_t>(q * 32) << 16) + t0;
+    {
+      uint32_t r[kFusedIssuers][16];
+#pragma unroll
+      for (int jj = 0; jj < kFusedIssuers; ++jj) tmem_ld16_nowait(tq + jj * kFusedRows, r[jj]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < kEpiTokens; ++i) {
+        float t = __uint_as_float(r[0][i]);
+#pragma unroll
+        for (int jj = 1; jj < kFusedIssuers; ++jj) t += jj < nkb ? __uint_as_float(r[jj][i]) : 0.f;
+        v[i] = t;
+      }
+    }
+    if (ok && !tl->abort) gemm_epilogue(a, p, step, l, f, t0, c, v);
+    tc_fence_before();
+  }
+  ++items_done;
+  bar_workers();
+}
+
+// --------------------------------------------------------------- attention
+// One (head, key split) of an attention over [source1 (Sv1 keys) ; source2 (S2
+// keys)] for the R query rows: 8 worker warps = 2 query groups x 4 blocks of
+// 64 keys.  Source 2 keys are scaled per key (RMSNorm of the fresh k); q rows
+// by qscale.  Writes either the final output (nsplit == 1) or a split partial
+// merged by the last-arriving CTA of the head.
+struct AttnItem {
+  const __nv_bfloat16* k1;  // source 1 rows: k1 + j * ts1 (head offset applied)
+  const __nv_bfloat16* v1;
+  long long ts1;
+  int S1;
+  const __nv_bfloat16* k2;  // source 2 rows: k2 + j * ts2
+  const __nv_bfloat16* v2;
+  long long ts2;
+  int S2;
+  const float* kscale2;     // [S2] sum of squares of the fresh keys (null: 1)
+  const __nv_bfloat16* qp;  // q rows: qp + r * qts (head offset applied)
+  long long qts;
+  const float* qscale;      // [R] sum of squares of q rows (null: 1)
+  const uint8_t* mask2d;    // [R, S1 + S2] (row stride mrs) or null
+  long long mrs;
+  const uint8_t* key_mask;  // [S1 + S2] or null
+  int k0, k1end;            // key range of this split
+  __nv_bfloat16* out;       // final output rows: out + r * ots (head offset applied)
+  long long ots;
+  float* part;              // this split's partial [32][66] (nsplit > 1)
+  float* part_head;         // all splits of the head
+  unsigned* counter;        // arrival counter of the head
+  int nsplit;
+};
+
+// Staging of an attention item: K / V [256][kKvRow] each, the attend bytes
+// [32][256], the key mask [256] and the q rows [32][kKvRow].
+struct AttnSmem {
+  __nv_bfloat16 *sK, *sV, *sQ;
+  uint8_t *sM, *sKm;
+};
+__device__ __forceinline__ AttnSmem attn_smem(uint8_t* stg) {
+  AttnSmem m;
+  m.sK = reinterpret_cast<__nv_bfloat16*>(stg);
+  m.sV = m.sK + 256 * kKvRow;
+  m.sM = reinterpret_cast<uint8_t*>(m.sV + 256 * kKvRow);
+  m.sKm = m.sM + kFusedRows * 256;
+  m.sQ = reinterpret_cast<__nv_bfloat16*>(m.sKm + 256);
+  return m;
+}
+static_assert(2 * 256 * (64 + 8) * 2 + kFusedRows * 256 + 256 + kFusedRows * (64 + 8) * 2 + 256 * 4 <=
+                  kFusedStaging,
+              "attention staging");
+static_assert(kFusedMaxSplits * (kFusedRows * 64 + kFusedRows * 2) * 4 + (kFusedMaxSplits + 1) * kFusedRows * 4 <=
+                  kFusedStaging,
+              "split partials of a head fit the staging");
+
+// The part of an item that no earlier phase of the launch writes: the source
+// 1 rows (video cache or context K / V), the attend bytes and the key mask.
+// A CTA issues it for its next attention item at the end of the phase before
+// (one cp.async group), so the HBM reads overlap that phase and its barrier.
+__device__ void attn_stage_const(const FusedArgs& a, uint8_t* stg, const AttnItem& t) {
+  const AttnSmem m = attn_smem(stg);
+  const int nkeys = t.k1end - t.k0;
+  for (int idx = threadIdx.x - 32; idx < 256 * 8; idx += kFusedWorkers) {
+    const int r = idx >> 3, c = idx & 7;
+    const int j = t.k0 + r;
+    if (r < nkeys && j >= t.S1) continue;  // a fresh key: staged after the barrier
+    const bool valid = r < nkeys;
+    cp_async16(m.sK + r * kKvRow + c * 8, valid ? t.k1 + j * t.ts1 + c * 8 : a.q, valid);
+    cp_async16(m.sV + r * kKvRow + c * 8, valid ? t.v1 + j * t.ts1 + c * 8 : a.q, valid);
+  }
+  if (t.mask2d != nullptr) {
+    if (t.mrs % 16 == 0 && (reinterpret_cast<uintptr_t>(t.mask2d) & 15) == 0 && t.k0 % 16 == 0) {
+      for (int idx = threadIdx.x - 32; idx < kFusedRows * 16; idx += kFusedWorkers) {
+        const int r = idx >> 4, c = idx & 15;
+        const int j = t.k0 + 16 * c;
+        int n = t.k1end - j;
+        n = n < 0 ? 0 : (n > 16 ? 16 : n);
+        if (r >= a.R) n = 0;
+        const uint8_t* src = n > 0 ? t.mask2d + r * t.mrs + j : t.mask2d;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(m.sM + r * 256 + 16 * c)),
+                     "l"(src), "r"(n)
+                     : "memory");
+      }
+    } else {
+      for (int idx = threadIdx.x - 32; idx < kFusedRows * 256; idx += kFusedWorkers) {
+        const int r = idx >> 8, jj = idx & 255;
+        m.sM[idx] = (jj < nkeys && r < a.R) ? t.mask2d[r * t.mrs + t.k0 + jj] : 0;
+      }
+    }
+  }
+  for (int jj = threadIdx.x - 32; jj < 256; jj += kFusedWorkers)
+    m.sKm[jj] = jj < nkeys ? (t.key_mask != nullptr ? t.key_mask[t.k0 + jj] : 1) : 0;
+  cp_async_commit();
+}
+
+__device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, const AttnItem& t,
+                               bool prefetched) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const AttnSmem m = attn_smem(stg);
+  __nv_bfloat16* sK = m.sK;
+  __nv_bfloat16* sV = m.sV;
+  const uint8_t* sM = m.sM;
+  const uint8_t* sKm = m.sKm;
+  const int nkeys = t.k1end - t.k0;
+  if (!prefetched) attn_stage_const(a, stg, t);
+  // fresh keys (source 2) and the q rows: written by the phase before
+  for (int idx = threadIdx.x - 32; idx < 256 * 8; idx += kFusedWorkers) {
+    const int r = idx >> 3, c = idx & 7;
+    const int j = t.k0 + r;
+    if (r >= nkeys || j < t.S1) continue;
+    cp_async16(sK + r * kKvRow + c * 8, t.k2 + (j - t.S1) * t.ts2 + c * 8, true);
+    cp_async16(sV + r * kKvRow + c * 8, t.v2 + (j - t.S1) * t.ts2 + c * 8, true);
+  }
+  for (int idx = threadIdx.x - 32; idx < kFusedRows * 8; idx += kFusedWorkers) {
+    const int r = idx >> 3, c = idx & 7;
+    cp_async16(m.sQ + r * kKvRow + c * 8, r < a.R ? t.qp + r * t.qts + c * 8 : a.q, r < a.R);
+  }
+  cp_async_commit();
+  // per-row q scale and per-key scale of the fresh keys (RMSNorm as a scale)
+  for (int i = threadIdx.x - 32; i < kFusedRows; i += kFusedWorkers) {
+    tl->scale[0][i] = (t.qscale != nullptr && i < a.R)
+                          ? rsqrtf(__ldcg(t.qscale + i) / a.HD + a.eps) : 1.f;
+    tl->scale[1][i] = (t.kscale2 != nullptr && i < t.S2)
+                          ? rsqrtf(__ldcg(t.kscale2 + i) / a.HD + a.eps) : 1.f;
+  }
+  cp_async_wait<0>();
+  bar_workers();
+  // per-key logit factor: scale_log2 x the RMSNorm scale of a fresh key, 0
+  // for a key outside the split or masked out by the key mask
+  const int k0 = t.k0, S1 = t.S1;
+  float* sKsc = reinterpret_cast<float*>(m.sQ + kFusedRows * kKvRow);
+  for (int jj = threadIdx.x - 32; jj < 256; jj += kFusedWorkers) {
+    const int j = k0 + jj;
+    const float ks = j >= S1 && jj < nkeys ? tl->scale[1][j - S1] : 1.f;
+    sKsc[jj] = (jj < nkeys && sKm[jj] != 0) ? ks * a.scale_log2 : 0.f;
+  }
+  bar_workers();
+
+  const int wi = warp - 1;                 // 0..10
+  const bool active = wi < 8;
+  const int qg = wi & 1, kq = wi >> 1;     // query group, key block
+  float o[8][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int r0 = qg * 16 + g, r1 = r0 + 8;
+  if (active) {
+    // Q fragments, scaled per row
+    uint32_t qf[4][4];
+    const float s0 = tl->scale[0][r0], s1 = tl->scale[0][r1];
+    const bool v0 = r0 < a.R, v1 = r1 < a.R;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int col = kk * 16 + hh * 8 + 2 * tq;
+        float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
+        if (v0) {
+          const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(m.sQ + r0 * kKvRow + col);
+          x0 = __low2float(p) * s0;
+          x1 = __high2float(p) * s0;
+        }
+        if (v1) {
+          const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(m.sQ + r1 * kKvRow + col);
+          y0 = __low2float(p) * s1;
+          y1 = __high2float(p) * s1;
+        }
+        qf[kk][hh * 2 + 0] = pack_bf16(x0, x1);
+        qf[kk][hh * 2 + 1] = pack_bf16(y0, y1);
+      }
+    }
+    float s[8][4];
+    const int kb = kq * 64;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+      const __nv_bfloat16* kr = sK + (kb + n * 8 + g) * kKvRow;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t bfr[2];
+        bfr[0] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 2 * tq);
+        bfr[1] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 8 + 2 * tq);
+        mma_bf16_16816(s[n], qf[kk], bfr);
+      }
+    }
+    // masks: the key factor (2 per n, one 8-byte load) and the attend bytes of
+    // rows r0 / r1 (2 per n, one 2-byte load each)
+    const bool m2 = t.mask2d != nullptr;
+    const uint8_t* mr0 = sM + r0 * 256;
+    const uint8_t* mr1 = sM + r1 * 256;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int jj = kb + n * 8 + 2 * tq;
+      const float2 kf = *reinterpret_cast<const float2*>(sKsc + jj);
+      const unsigned a0 = m2 ? *reinterpret_cast<const uint16_t*>(mr0 + jj) : 0x0101u;
+      const unsigned a1 = m2 ? *reinterpret_cast<const uint16_t*>(mr1 + jj) : 0x0101u;
+      const bool ok00 = v0 && kf.x != 0.f && (a0 & 0xffu), ok01 = v0 && kf.y != 0.f && (a0 >> 8);
+      const bool ok10 = v1 && kf.x != 0.f && (a1 & 0xffu), ok11 = v1 && kf.y != 0.f && (a1 >> 8);
+      s[n][0] = ok00 ? s[n][0] * kf.x : -INFINITY;
+      s[n][1] = ok01 ? s[n][1] * kf.y : -INFINITY;
+      s[n][2] = ok10 ? s[n][2] * kf.x : -INFINITY;
+      s[n][3] = ok11 ? s[n][3] * kf.y : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    m0 = mx0;
+    m1 = mx1;
+    const float b0 = m0 == -INFINITY ? 0.f : m0, b1 = m1 == -INFINITY ? 0.f : m1;
+    uint32_t pf[4][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p0 = exp2f(s[n][0] - b0), p1 = exp2f(s[n][1] - b0);
+      const float p2 = exp2f(s[n][2] - b1), p3 = exp2f(s[n][3] - b1);
+      l0 += p0 + p1;
+      l1 += p2 + p3;
+      const int ks2 = n >> 1, hi = n & 1;
+      pf[ks2][hi ? 2 : 0] = pack_bf16(p0, p1);
+      pf[ks2][hi ? 3 : 1] = pack_bf16(p2, p3);
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+    for (int ks2 = 0; ks2 < 4; ++ks2) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t bfr[2];
+        const int r = kb + ks2 * 16 + (lane & 15);
+        const uint32_t addr = smem_u32(sV + r * kKvRow + i * 8);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                     : "=r"(bfr[0]), "=r"(bfr[1])
+                     : "r"(addr));
+        mma_bf16_16816(o[i], pf[ks2], bfr);
+      }
+    }
+  }
+  bar_workers();  // K/V staging no longer read: reuse it for the block merge
+  // block partials: O [4][32][kCombRow] (padded rows: conflict-free stores),
+  // (m, l) [4][32][2], then per (block, row) weights and per row 1 / L
+  constexpr int kCombRow = 64 + 4;
+  float* comb = reinterpret_cast<float*>(stg);
+  float* cml = comb + 4 * kFusedRows * kCombRow;
+  float* cw = cml + 4 * kFusedRows * 2;            // [4][32]
+  float* crow = cw + 4 * kFusedRows;               // [32][2]: M, L
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = i * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(comb + (kq * kFusedRows + r0) * kCombRow + d) = make_float2(o[i][0], o[i][1]);
+      *reinterpret_cast<float2*>(comb + (kq * kFusedRows + r1) * kCombRow + d) = make_float2(o[i][2], o[i][3]);
+    }
+    if (tq == 0) {
+      cml[(kq * kFusedRows + r0) * 2] = m0;
+      cml[(kq * kFusedRows + r0) * 2 + 1] = l0;
+      cml[(kq * kFusedRows + r1) * 2] = m1;
+      cml[(kq * kFusedRows + r1) * 2 + 1] = l1;
+    }
+  }
+  bar_workers();
+  const int nsplit = t.nsplit;
+  for (int r = threadIdx.x - 32; r < kFusedRows; r += kFusedWorkers) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) M = fmaxf(M, cml[(b * kFusedRows + r) * 2]);
+    const float base = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float w = exp2f(cml[(b * kFusedRows + r) * 2] - base);
+      cw[b * kFusedRows + r] = w;
+      L += w * cml[(b * kFusedRows + r) * 2 + 1];
+    }
+    crow[r * 2] = M;
+    crow[r * 2 + 1] = L;
+  }
+  bar_workers();
+  // merge the 4 key blocks: the split's (O, m, l), four dims per thread.  A
+  // split partial is O [32][64] followed by (m, l) [32][2] (kSplitStride floats).
+  __nv_bfloat16* out = t.out;
+  float* part = t.part;
+  const long long ots = t.ots;
+  for (int idx = threadIdx.x - 32; idx < kFusedRows * 16; idx += kFusedWorkers) {
+    const int r = idx >> 4, d = (idx & 15) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float w = cw[b * kFusedRows + r];
+      const float4 ov = *reinterpret_cast<const float4*>(comb + (b * kFusedRows + r) * kCombRow + d);
+      acc.x += w * ov.x;
+      acc.y += w * ov.y;
+      acc.z += w * ov.z;
+      acc.w += w * ov.w;
+    }
+    if (nsplit == 1) {
+      const float L = crow[r * 2 + 1], inv = L > 0.f ? 1.f / L : 0.f;
+      if (r < a.R) {
+        uint2 pk;
+        pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+        pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(out + r * ots + d) = pk;
+      }
+    } else {
+      *reinterpret_cast<float4*>(part + r * 64 + d) = acc;
+      if (d == 0) *reinterpret_cast<float2*>(part + kFusedRows * 64 + r * 2) = make_float2(crow[r * 2], crow[r * 2 + 1]);
+    }
+  }
+  if (nsplit == 1) {
+    bar_workers();
+    return;
+  }
+  // publish the partial (CTA barrier, then one fence + counter atomic), and
+  // the last arriving split merges: its counter thread fences again before
+  // the CTA reads the other splits' partials through L2
+  bar_workers();
+  if (threadIdx.x == 32) {
+    __threadfence();
+    const bool last = atomicAdd(t.counter, 1u) == static_cast<unsigned>(nsplit - 1);
+    if (last) __threadfence();
+    tl->last = last ? 1 : 0;
+  }
+  bar_workers();
+  if (tl->last) {
+    // every split's partial -> shared memory in one cp.async group (L2 reads,
+    // kSplitStride floats each), then per (split, row) weights, then the
+    // output rows
+    float* sp_all = reinterpret_cast<float*>(stg);
+    const float* part_head = t.part_head;
+    const int nchunk = nsplit * kSplitStride / 4;
+    for (int c = threadIdx.x - 32; c < nchunk; c += kFusedWorkers)
+      cp_async16(sp_all + c * 4, part_head + c * 4, true);
+    cp_async_commit();
+    cp_async_wait<0>();
+    bar_workers();
+    float* wts = sp_all + nsplit * kSplitStride;   // [nsplit][32], then 1 / L [32]
+    for (int r = threadIdx.x - 32; r < kFusedRows; r += kFusedWorkers) {
+      float M = -INFINITY;
+      for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2]);
+      const float base = M == -INFINITY ? 0.f : M;
+      float L = 0.f;
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const float w = exp2f(sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2] - base);
+        wts[sp * kFusedRows + r] = w;
+        L += w * sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2 + 1];
+      }
+      wts[nsplit * kFusedRows + r] = L > 0.f ? 1.f / L : 0.f;
+    }
+    bar_workers();
+    for (int idx = threadIdx.x - 32; idx < a.R * 16; idx += kFusedWorkers) {
+      const int r = idx >> 4, d = (idx & 15) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const float4 ov = *reinterpret_cast<const float4*>(sp_all + sp * kSplitStride + r * 64 + d);
+        const float w = wts[sp * kFusedRows + r];
+        acc.x += w * ov.x;
+        acc.y += w * ov.y;
+        acc.z += w * ov.z;
+        acc.w += w * ov.w;
+      }
+      const float inv = wts[nsplit * kFusedRows + r];
+      uint2 pk;
+      pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+      pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+      *reinterpret_cast<uint2*>(out + r * ots + d) = pk;
+    }
+  }
+  bar_workers();
+}
+
+
+// Attention work items.  Joint attention item i = (head, key split); cross
+// attention item h = head.  Their CTAs start after the qkv CTAs (joint) and
+// after the cross-q CTAs (cross), so that they are idle in the phase before
+// and can prefetch their constant K / V there.
+__device__ __forceinline__ int attn_joint_first(const FusedArgs& a, int cta, int G) {
+  const int off = 3 * a.HD / 128;
+  return ((cta - off) % G + G) % G;
+}
+__device__ __forceinline__ int attn_cross_first(const FusedArgs& a, int cta, int G) {
+  const int off = 3 * a.HD / 128 + a.HD / 128;
+  return ((cta - off) % G + G) % G;
+}
+
+__device__ AttnItem joint_item(const FusedArgs& a, int step, int l, int i) {
+  const int h = i / a.splits, sp = i % a.splits;
+  const float* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
+  AttnItem t;
+  t.k1 = a.vk[l] + h * a.hd;
+  t.v1 = a.vv[l] + h * a.hd;
+  t.ts1 = a.v_ts;
+  t.S1 = a.Sv;
+  t.k2 = a.ka + h * a.hd;
+  t.v2 = a.va + h * a.hd;
+  t.ts2 = a.HD;
+  t.S2 = a.Sa;
+  t.kscale2 = ssq + kFusedRows;
+  t.qp = a.q + h * a.hd;
+  t.qts = a.HD;
+  t.qscale = ssq;
+  t.mask2d = a.mask2d;
+  t.mrs = a.Sv + a.Sa;
+  t.key_mask = nullptr;
+  t.k0 = sp * kFusedKeysPerSplit;
+  t.k1end = min(a.Sv + a.Sa, t.k0 + kFusedKeysPerSplit);
+  t.out = a.ao + h * a.hd;
+  t.ots = a.HD;
+  t.part_head = a.apart + static_cast<long long>(h) * a.splits * kSplitStride;
+  t.part = t.part_head + sp * kSplitStride;
+  t.counter = a.sync + 2 + (static_cast<long long>(step) * a.L + l) * a.H + h;
+  t.nsplit = a.splits;
+  return t;
+}
+
+__device__ AttnItem cross_item(const FusedArgs& a, int step, int l, int h) {
+  const float* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
+  const __nv_bfloat16* kv = a.ckv + static_cast<long long>(l) * a.C * 2 * a.HD;
+  AttnItem t;
+  t.k1 = kv + h * a.hd;
+  t.v1 = kv + a.HD + h * a.hd;
+  t.ts1 = 2 * a.HD;
+  t.S1 = a.C;
+  t.k2 = nullptr;
+  t.v2 = nullptr;
+  t.ts2 = 0;
+  t.S2 = 0;
+  t.kscale2 = nullptr;
+  t.qp = a.qc + h * a.hd;
+  t.qts = a.HD;
+  t.qscale = ssq + 2 * kFusedRows;
+  t.mask2d = nullptr;
+  t.mrs = 0;
+  t.key_mask = a.ctx_mask;
+  t.k0 = 0;
+  t.k1end = a.C;
+  t.out = a.ci + h * a.hd;
+  t.ots = a.HD;
+  t.part = nullptr;
+  t.part_head = nullptr;
+  t.counter = nullptr;
+  t.nsplit = 1;
+  return t;
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __grid_constant__ FusedArgs a) {
+  extern __shared__ uint8_t fused_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fused_smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem;
+  uint8_t* stg = smem + kFusedRing * kATile;
+  FusedSmemTail* tl = reinterpret_cast<FusedSmemTail*>(smem + fused_tail_offset());
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFusedRing; ++s) {
+      mbar_init(&tl->full[s], 1);
+      mbar_init(&tl->empty[s], 1);
+    }
+    mbar_init(&tl->accum, kFusedIssuers);
+    tl->abort = 0;
+    fence_mbar_init();
+    for (int p = 0; p < 6; ++p) tma_prefetch_desc(&a.tm[p]);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tl->tmem, kFusedIssuers * kFusedRows);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ------------------------------------------------ weight producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      uint32_t it = 0;
+      for (int step = 0; step < a.N && !tl->abort; ++step)
+        for (int l = 0; l < a.L && !tl->abort; ++l)
+          for (int p = 0; p < 6 && !tl->abort; ++p) {
+            const int cnt = f_count(a, p), rows = f_rows(a, p);
+            for (int i = f_first(a, p, cta, G); i < cnt && !tl->abort; i += G) {
+              const FItem itm = f_item(a, p, i);
+              for (int k = 0; k < itm.nkb; ++k) {
+                const int s = it % kFusedRing;
+                if (it >= kFusedRing &&
+                    !mbar_wait(&tl->empty[s], ((it / kFusedRing) - 1) & 1, a.status, kErrWaitEmpty)) {
+                  tl->abort = 1;
+                  break;
+                }
+                mbar_arrive_expect_tx(&tl->full[s], kATile);
+                tma_load_2d(ring + s * kATile, &a.tm[p], &tl->full[s], (itm.kb0 + k) * 64,
+                            l * rows + itm.n * 128, pol);
+                ++it;
+              }
+            }
+          }
+      // drain: the last issued tiles have landed (consumed on the normal path)
+      const uint32_t first = it > kFusedRing ? it - kFusedRing : 0;
+      for (uint32_t j = first; j < it; ++j)
+        mbar_wait(&tl->full[j % kFusedRing], (j / kFusedRing) & 1, a.status, kErrWaitFull);
+    }
+  } else {
+    // ------------------------------------------------------ workers
+    uint32_t ring_it = 0, items_done = 0, epoch = 0;
+    const int R = a.R, D = a.D;
+    const bool has_qkv = f_first(a, kFQkv, cta, G) < f_count(a, kFQkv);
+    const bool has_cq = f_first(a, kFCq, cta, G) < f_count(a, kFCq);
+    const bool has_ffn0 = f_first(a, kFFfn0, cta, G) < f_count(a, kFFfn0);
+    for (int step = 0; step < a.N && !tl->abort; ++step) {
+      if (step == 0) {
+        // action_encoder of the first step: x = bf16(enc_w latent + enc_b); later
+        // steps encode right after their head / Euler update (same warp, same row)
+        for (int idx = cta * kFusedWorkers + threadIdx.x - 32; idx < R * D; idx += G * kFusedWorkers) {
+          const int r = idx / D, f = idx % D;
+          float acc = bf2f(a.enc_b[f]);
+          for (int c = 0; c < a.A; ++c) acc += bf2f(a.enc_w[f * a.A + c]) * bf2f(__ldcg(a.latent + r * a.A + c));
+          a.x[idx] = rbf(acc);
+        }
+        if (has_qkv) ln_const_prefetch(a, stg, step, 0, 0, 0);
+        if (!grid_sync(a, epoch, tl)) break;
+      }
+      for (int l = 0; l < a.L && !tl->abort; ++l) {
+        // qkv
+        for (int i = f_first(a, kFQkv, cta, G); i < f_count(a, kFQkv); i += G)
+          gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i), ring_it, items_done);
+        if (attn_joint_first(a, cta, G) < a.H * a.splits)
+          attn_stage_const(a, stg, joint_item(a, step, l, attn_joint_first(a, cta, G)));
+        if (!grid_sync(a, epoch, tl)) break;
+        // joint attention: items (head, split); the first item's constant
+        // K / V were prefetched at the end of the qkv phase
+        for (int i = attn_joint_first(a, cta, G); i < a.H * a.splits; i += G)
+          attention_item(a, stg, tl, joint_item(a, step, l, i), i == attn_joint_first(a, cta, G));
+        if (!grid_sync(a, epoch, tl)) break;
+        for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += G)
+          gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i), ring_it, items_done);
+        if (has_cq) ln_const_prefetch(a, stg, step, l, 1, 0);
+        if (!grid_sync(a, epoch, tl)) break;
+        for (int i = f_first(a, kFCq, cta, G); i < f_count(a, kFCq); i += G)
+          gemm_item(a, ring, stg, tl, kFCq, step, l, f_item(a, kFCq, i), ring_it, items_done);
+        if (a.C > 0 && attn_cross_first(a, cta, G) < a.H)
+          attn_stage_const(a, stg, cross_item(a, step, l, attn_cross_first(a, cta, G)));
+        if (!grid_sync(a, epoch, tl)) break;
+        // cross attention: one item per head over the context (constant K / V
+        // prefetched at the end of the cross-q phase)
+        for (int h = attn_cross_first(a, cta, G); h < a.H && a.C > 0; h += G)
+          attention_item(a, stg, tl, cross_item(a, step, l, h), h == attn_cross_first(a, cta, G));
+        if (!grid_sync(a, epoch, tl)) break;
+        for (int i = f_first(a, kFCo, cta, G); i < f_count(a, kFCo); i += G)
+          gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i), ring_it, items_done);
+        if (has_ffn0) ln_const_prefetch(a, stg, step, l, 0, 3);
+        if (!grid_sync(a, epoch, tl)) break;
+        for (int i = f_first(a, kFFfn0, cta, G); i < f_count(a, kFFfn0); i += G)
+          gemm_item(a, ring, stg, tl, kFFfn0, step, l, f_item(a, kFFfn0, i), ring_it, items_done);
+        if (!grid_sync(a, epoch, tl)) break;
+        for (int i = f_first(a, kFFfn2, cta, G); i < f_count(a, kFFfn2); i += G)
+          gemm_item(a, ring, stg, tl, kFFfn2, step, l, f_item(a, kFFfn2, i), ring_it, items_done);
+        if (has_qkv && l + 1 < a.L) ln_const_prefetch(a, stg, step, l + 1, 0, 0);
+        if (!grid_sync(a, epoch, tl)) break;
+      }
+      if (tl->abort) break;
+      // head + Euler update + the next step's action_encoder: one CTA per token
+      // row (row-local, no barrier between): warps take the velocity channels,
+      // one thread per channel updates the latent, every thread re-encodes
+      // features of the row.
+      for (int r = cta; r < R; r += G) {
+        const int wi = warp - 1, wt = threadIdx.x - 32;
+        float* svel = &tl->stat[0][0];
+        float* slat = &tl->stat[kFusedRows / 2][0];
+        const float* xr = a.x + static_cast<long long>(r) * D;
+        for (int c = wi; c < a.A; c += 11) {
+          float acc = 0.f;
+#pragma unroll 4
+          for (int ch = lane; ch < D / 8; ch += 32) {
+            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(xr + ch * 8));
+            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(xr + ch * 8 + 4));
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            float wv[8];
+            ld_bf8(a.head_w + static_cast<long long>(c) * D + ch * 8, wv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc += rbf(xv[e]) * wv[e];
+          }
+          acc = warp_sum(acc);
+          if (lane == 0) svel[c] = rbf(acc + bf2f(a.head_b[c]));
+        }
+        bar_workers();
+        if (wt < a.A) {
+          const float vel = svel[wt];
+          const float d = rbf(a.deltas.t[step]);
+          const float lat = bf2f(f2bf(bf2f(__ldcg(a.latent + r * a.A + wt)) + rbf(vel * d)));
+          if (a.trace != nullptr) a.trace[(static_cast<long long>(step) * R + r) * a.A + wt] = f2bf(vel);
+          a.latent[r * a.A + wt] = f2bf(lat);
+          slat[wt] = lat;
+        }
+        bar_workers();
+        if (step + 1 < a.N) {
+#pragma unroll 3
+          for (int f = wt; f < D; f += kFusedWorkers) {
+            float acc = bf2f(a.enc_b[f]);
+            for (int c = 0; c < a.A; ++c) acc += bf2f(a.enc_w[f * a.A + c]) * slat[c];
+            a.x[static_cast<long long>(r) * D + f] = rbf(acc);
+          }
+        }
+      }
+      if (has_qkv && step + 1 < a.N) ln_const_prefetch(a, stg, step + 1, 0, 0, 0);
+      if (!grid_sync(a, epoch, tl)) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tl->tmem, kFusedIssuers * kFusedRows);
+  }
+}
+
+cudaError_t fused_init_attributes() {
+  return cudaFuncSetAttribute(fused_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(fused_smem_bytes()));
+}
+
+cudaError_t launch_fused_chunk(const FusedArgs& a, int grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = fused_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fused_chunk_kernel, a);
+}
+
+}  // namespace fam

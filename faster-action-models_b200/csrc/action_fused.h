@@ -1,0 +1,60 @@
+// Arguments of the fused persistent action-chunk kernel (internal).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fam_kernels.h"
+
+namespace fam {
+
+constexpr int kFusedMaxLayers = 32;
+constexpr int kFusedRows = 32;        // token rows of one sample (MMA N, zero padded)
+constexpr int kFusedThreads = 384;    // warp 0 weight producer, warps 1..11 workers
+constexpr int kFusedWorkers = 352;
+constexpr int kFusedRing = 8;         // 128 x 64 bf16 weight tiles in flight per CTA (128 KB)
+constexpr int kFusedStaging = 88 * 1024;
+constexpr int kFusedKeysPerSplit = 256;
+constexpr int kFusedMaxSplits = 10;   // joint-attention key splits per head (partials merged in shared memory)
+constexpr int kFusedMaxCtas = 256;  // barrier flag lines reserved
+
+enum FusedGemm : int { kFQkv = 0, kFO = 1, kFCq = 2, kFCo = 3, kFFfn0 = 4, kFFfn2 = 5 };
+
+struct FusedArgs {
+  CUtensorMap tm[6];                 // stacked weights [L * N, K] per FusedGemm
+  // stacked per-block vectors (bf16)
+  const __nv_bfloat16 *qkv_b, *o_b, *cq_b, *co_b, *ffn0_b, *ffn2_b;
+  const __nv_bfloat16 *norm_q, *norm_k, *cnorm_q, *norm3_w, *norm3_b, *modulation;
+  const __nv_bfloat16 *enc_w, *enc_b, *head_w, *head_b;
+  const float* tmod;                 // [N, 6D]
+  const float2* rope;                // [positions, hd/2]
+  const __nv_bfloat16* vk[kFusedMaxLayers];
+  const __nv_bfloat16* vv[kFusedMaxLayers];
+  long long v_ts;                    // cache token stride (elements)
+  int Sv;
+  const uint8_t* mask2d;             // [Sa, Sv + Sa] or null
+  const __nv_bfloat16* ckv;          // [L, C, 2HD]: RMSNorm'd K then V per context token
+  const uint8_t* ctx_mask;           // [C] or null
+  int C;
+  // workspace
+  float* x;                          // [R, D]
+  __nv_bfloat16 *q, *ka, *va, *ao, *qc, *ci, *fh;
+  float* ssq;                        // [N][L][3][32] (zeroed per launch)
+  float* apart;                      // [H][splits][32][hd + 2]
+  unsigned* sync;                    // [0] barrier go word, [1] abort, [2..] merge counters [N][L][H]
+  unsigned* flags;                   // per-CTA barrier arrival lines (32 words apart)
+  int* status;
+  __nv_bfloat16* latent;             // [R, A]
+  __nv_bfloat16* trace;              // [N, R, A] or null
+  StepTimes deltas;
+  int N, L, R, Sa, D, HD, H, hd, F, A, splits;
+  float eps, scale_log2;
+};
+
+size_t fused_smem_bytes();
+cudaError_t launch_fused_chunk(const FusedArgs& a, int grid, cudaStream_t st);
+cudaError_t fused_init_attributes();
+
+}  // namespace fam

@@ -19,6 +19,7 @@
 // (wan_video_dit.py:514-518) as a descriptor instead of a materialised mask.
 #include "fam_common.cuh"
 #include "fam_kernels.h"
+#include "fam_mma.cuh"
 
 namespace fam {
 
@@ -33,31 +34,6 @@ struct AttnCfg {
   static constexpr int kMaskBytes = 2 /*stages*/ * (kQTile * kAttnKB + kAttnKB);
   static constexpr int kBytes = kKVBytes + kMaskBytes;
 };
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  const uint32_t s = smem_u32(smem);
-  const int n = valid ? 16 : 0;  // zero-fill rows past the end
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, const uint32_t* b) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
 
 // Key j of (b, h): pointer to its K (or V) row slice.
 __device__ __forceinline__ const __nv_bfloat16* kv_row(const AttnArgs& a, bool is_v, int b, int h,

@@ -169,23 +169,44 @@ class ActionExpertEngine:
             self.keep.append(t)
             return t.data_ptr()
 
+        # Every per-block tensor is packed into one contiguous stack over the blocks
+        # (block i at rows i * N): the launch chain uses per-block slices, the fused
+        # persistent kernel streams whole stacks through single tensor maps.
+        blocks = list(dit.blocks)
+
+        def stack(fn):
+            t = torch.stack([fn(b).detach().to(device=self.dev, dtype=torch.bfloat16)
+                             for b in blocks]).contiguous()
+            self.keep.append(t)
+            return t
+
+        S = {
+            "modulation": stack(lambda b: b.modulation.reshape(6, -1)),
+            "qkv_w": stack(lambda b: torch.cat([b.self_attn.q.weight, b.self_attn.k.weight,
+                                                b.self_attn.v.weight], 0)),
+            "qkv_b": stack(lambda b: torch.cat([b.self_attn.q.bias, b.self_attn.k.bias,
+                                                b.self_attn.v.bias], 0)),
+            "norm_q": stack(lambda b: b.self_attn.norm_q.weight),
+            "norm_k": stack(lambda b: b.self_attn.norm_k.weight),
+            "o_w": stack(lambda b: b.self_attn.o.weight), "o_b": stack(lambda b: b.self_attn.o.bias),
+            "norm3_w": stack(lambda b: b.norm3.weight), "norm3_b": stack(lambda b: b.norm3.bias),
+            "cq_w": stack(lambda b: b.cross_attn.q.weight), "cq_b": stack(lambda b: b.cross_attn.q.bias),
+            "cnorm_q": stack(lambda b: b.cross_attn.norm_q.weight),
+            "cnorm_k": stack(lambda b: b.cross_attn.norm_k.weight),
+            "ckv_w": stack(lambda b: torch.cat([b.cross_attn.k.weight, b.cross_attn.v.weight], 0)),
+            "ckv_b": stack(lambda b: torch.cat([b.cross_attn.k.bias, b.cross_attn.v.bias], 0)),
+            "co_w": stack(lambda b: b.cross_attn.o.weight), "co_b": stack(lambda b: b.cross_attn.o.bias),
+            "ffn0_w": stack(lambda b: b.ffn[0].weight), "ffn0_b": stack(lambda b: b.ffn[0].bias),
+            "ffn2_w": stack(lambda b: b.ffn[2].weight), "ffn2_b": stack(lambda b: b.ffn[2].bias),
+        }
         layers = (_abi.ActionLayer * dit.num_layers)()
-        for i, b in enumerate(dit.blocks):
-            sa, ca = b.self_attn, b.cross_attn
-            L = layers[i]
-            L.modulation = ptr(bfw(b.modulation.reshape(6, -1)))
-            L.qkv_w = ptr(bfw(torch.cat([sa.q.weight, sa.k.weight, sa.v.weight], 0)))
-            L.qkv_b = ptr(bfw(torch.cat([sa.q.bias, sa.k.bias, sa.v.bias], 0)))
-            L.norm_q, L.norm_k = ptr(bfw(sa.norm_q.weight)), ptr(bfw(sa.norm_k.weight))
-            L.o_w, L.o_b = ptr(bfw(sa.o.weight)), ptr(bfw(sa.o.bias))
-            L.norm3_w, L.norm3_b = ptr(bfw(b.norm3.weight)), ptr(bfw(b.norm3.bias))
-            L.cq_w, L.cq_b = ptr(bfw(ca.q.weight)), ptr(bfw(ca.q.bias))
-            L.cnorm_q, L.cnorm_k = ptr(bfw(ca.norm_q.weight)), ptr(bfw(ca.norm_k.weight))
-            L.ckv_w = ptr(bfw(torch.cat([ca.k.weight, ca.v.weight], 0)))
-            L.ckv_b = ptr(bfw(torch.cat([ca.k.bias, ca.v.bias], 0)))
-            L.co_w, L.co_b = ptr(bfw(ca.o.weight)), ptr(bfw(ca.o.bias))
-            L.ffn0_w, L.ffn0_b = ptr(bfw(b.ffn[0].weight)), ptr(bfw(b.ffn[0].bias))
-            L.ffn2_w, L.ffn2_b = ptr(bfw(b.ffn[2].weight)), ptr(bfw(b.ffn[2].bias))
+        for i in range(dit.num_layers):
+            for name, t in S.items():
+                setattr(layers[i], name, t[i].data_ptr())
+        stacks = _abi.ActionStacks()
+        for name, _ in _abi.ActionStacks._fields_:
+            setattr(stacks, name, S[name].data_ptr())
+        self._stacks = stacks
         w = _abi.ActionWeights()
         for name, mod in (("enc", dit.action_encoder), ("text0", dit.text_embedding[0]),
                           ("text2", dit.text_embedding[2]), ("time0", dit.time_embedding[0]),
@@ -197,6 +218,7 @@ class ActionExpertEngine:
         w.layers = layers
         w.rope = ptr(rope_table(dit.attn_head_dim).to(self.dev))
         w.rope_positions = 1024
+        w.stacks = C.pointer(stacks)
         cfg = _abi.ActionConfig(dit.hidden_dim, dit.action_dim, dit.ffn_dim, dit.text_dim,
                                 dit.freq_dim, dit.num_heads, dit.attn_head_dim, dit.num_layers,
                                 float(dit.eps))
@@ -262,6 +284,17 @@ class ActionExpertEngine:
         n = C.c_int32()
         check(lib().fam_action_launch_count(self.handle, C.byref(n)), "fam_action_launch_count")
         return n.value
+
+    MODES = {"auto": 0, "chain": 1, "fused": 2}
+
+    def set_mode(self, mode: str) -> None:
+        """'auto' (fused persistent kernel when the call qualifies), 'chain' or 'fused'."""
+        check(lib().fam_action_set_mode(self.handle, self.MODES[mode]), "fam_action_set_mode")
+
+    def last_path(self) -> str:
+        n = C.c_int32()
+        check(lib().fam_action_last_path(self.handle, C.byref(n)), "fam_action_last_path")
+        return {0: "none", 1: "chain", 2: "fused"}[n.value]
 
     def denoise_step(self, latents, timestep, context, context_mask=None, cache_k=None,
                      cache_v=None, attn_mask=None) -> torch.Tensor:

@@ -194,6 +194,21 @@ typedef struct fam_action_layer {
   const void* ffn2_w; const void* ffn2_b;  /* [D, F], [D]       ffn.2 */
 } fam_action_layer;
 
+/* Optional (no counterpart in the reference, whose blocks are separate
+ * modules): the same per-block tensors stacked over the blocks, contiguous
+ * (block l of a stack starts at l * rows).  When given, fam_action_chunk can
+ * run the fused persistent chunk kernel (batch 1, <= 32 action tokens,
+ * action_dim <= 16, head_dim 64, hidden a multiple of 256 and <= 1024, other
+ * widths multiples of 128, <= 256 context tokens, <= 2560 video + action
+ * keys); the layer pointers must point into these stacks. */
+typedef struct fam_action_stacks {
+  const void *qkv_w, *o_w, *cq_w, *co_w, *ffn0_w, *ffn2_w;   /* [L*N, K] */
+  const void *qkv_b, *o_b, *cq_b, *co_b, *ffn0_b, *ffn2_b;   /* [L*N] */
+  const void *norm_q, *norm_k, *cnorm_q;                     /* [L*HD] */
+  const void *norm3_w, *norm3_b;                             /* [L*D] */
+  const void *modulation;                                    /* [L*6*D] */
+} fam_action_stacks;
+
 typedef struct fam_action_weights {
   const void* enc_w; const void* enc_b;        /* [D, A]  action_encoder */
   const void* text0_w; const void* text0_b;    /* [D, T]  text_embedding.0 */
@@ -205,7 +220,15 @@ typedef struct fam_action_weights {
   const fam_action_layer* layers;              /* host array [L] */
   const void* rope;        /* f32 [rope_positions, d/2, 2] (cos, sin) of precompute_freqs_cis(d) */
   int32_t rope_positions;
+  const fam_action_stacks* stacks; /* NULL: launch-chain path only */
 } fam_action_weights;
+
+/* Execution path of fam_action_chunk: FAM_ACTION_AUTO picks the fused
+ * persistent kernel when the call qualifies, FAM_ACTION_CHAIN always runs the
+ * chain of per-op kernels, FAM_ACTION_FUSED requires the fused kernel. */
+#define FAM_ACTION_AUTO 0
+#define FAM_ACTION_CHAIN 1
+#define FAM_ACTION_FUSED 2
 
 typedef struct fam_action_expert fam_action_expert;
 
@@ -257,6 +280,11 @@ FAM_API int fam_action_denoise_step(fam_action_expert* e, const fam_action_io* i
 /* Number of kernels the last fam_action_chunk / fam_action_denoise_step call
  * enqueued (a graph replay launches the same set). */
 FAM_API int fam_action_launch_count(const fam_action_expert* e, int32_t* count);
+
+/* Selects the execution path (FAM_ACTION_AUTO / _CHAIN / _FUSED) and reports
+ * the path the last fam_action_chunk call took (1 chain, 2 fused). */
+FAM_API int fam_action_set_mode(fam_action_expert* e, int32_t mode);
+FAM_API int fam_action_last_path(const fam_action_expert* e, int32_t* path);
 
 /* ======================================================================
  * Video DiT prefill (WanVideoDiT backbone) — BASELINE config 2.

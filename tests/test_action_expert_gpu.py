@@ -90,6 +90,35 @@ def test_chunk_matches_oracle_and_is_deterministic():
     assert trace.shape == (4, B, Sa, 7)
 
 
+@pytest.mark.parametrize("Sa,Sv,C,tpf", [(32, 200, 16, 50), (8, 97, 5, 97), (20, 300, 64, 60)])
+def test_fused_kernel_matches_chain_and_oracle(Sa, Sv, C, tpf):
+    """The fused persistent chunk kernel (batch 1) against the launch chain and the oracle."""
+    dit, sd, cfg = _build(seed=11)
+    ctx, cm, ck, cv, noise, mask = _inputs(1, Sa, Sv, max(C, 1), cfg.text_dim, 256, cfg.num_layers, tpf)
+    ctx = ctx[:, :C] if C else ctx[:, :0]
+    cm = cm[:, :C] if C else cm[:, :0]
+    ts, ds = M.build_inference_schedule(3, 5.0)
+    ref = O.action_chunk_with_cache(sd, cfg, noise.float(), ctx.float(), cm, [k.float() for k in ck],
+                                    [v.float() for v in cv], mask, 3, 5.0)
+    eng = dit.engine()
+    args = (noise.cuda(), ts, ds, ctx.cuda(), cm.cuda(), [k.cuda() for k in ck], [v.cuda() for v in cv],
+            mask.cuda())
+    eng.set_mode("chain")
+    got_c = eng.chunk(*args).cpu().float()
+    assert eng.last_path() == "chain"
+    eng.set_mode("fused")
+    got_f, trace = eng.chunk(*args, return_trace=True)
+    got_f = got_f.cpu().float()
+    assert eng.last_path() == "fused" and eng.launch_count() < 100
+    got_f2 = eng.chunk(*args).cpu().float()  # graph replay of the fused chunk
+    eng.set_mode("auto")
+    for got in (got_c, got_f, got_f2):
+        err = (got - ref).abs().max().item()
+        assert err <= 2e-2 * max(1.0, ref.abs().max().item()) and _cos(got, ref) >= 0.999, err
+    assert (got_f - got_c).abs().max().item() <= 2e-2
+    assert trace.shape == (3, 1, Sa, 7)
+
+
 def test_full_config1_chunk():
     """BASELINE config 1 at full size: 1024 hidden, 16x64 heads, 28 blocks, 1760-token cache,
     10 steps, batch 1."""
