@@ -313,29 +313,63 @@ __device__ __forceinline__ void ln_load_row(const FusedArgs& a, int r, int lane,
   }
 }
 
+// Row statistics of a LayerNorm over D = 256 NCH columns (two passes over the
+// registers: mean, then the centred sum of squares).
 template <int NCH>
-__device__ __forceinline__ void ln_store_row(const FusedArgs& a, uint8_t* stg, int r, int lane, int mode,
-                                             const float (&f)[NCH * 8]) {
-  constexpr int D = NCH * 256;
-  if (r >= a.R) {
-#pragma unroll
-    for (int u = 0; u < NCH; ++u) {
-      const int ch = lane + 32 * u;
-      stage_chunk(stg, ch >> 3, r, ch & 7, make_uint4(0, 0, 0, 0));
-    }
-    return;
-  }
-  float sum = 0.f;
+__device__ __forceinline__ void ln_partial(const float (&f)[NCH * 8], float& sum) {
+  sum = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH * 8; ++i) sum += f[i];
-  const float mean = warp_sum(sum) / D;
+}
+template <int NCH>
+__device__ __forceinline__ float ln_centred(const float (&f)[NCH * 8], float mean) {
   float var = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH * 8; ++i) {
     const float d = f[i] - mean;
     var += d * d;
   }
-  const float rstd = rsqrtf(warp_sum(var) / D + a.eps);
+  return var;
+}
+
+// The warp's three rows r0 = w, r1 = w + 11, r2 = w + 22 of the 11 worker
+// warps, processed together so their loads, reductions and stores overlap
+// (independent instruction streams).  Rows >= R are staged as zeros; a row
+// >= 32 (the third row of the last warp) does not exist.
+template <int NCH>
+__device__ void stage_layernorm_t(const FusedArgs& a, uint8_t* stg, int mode) {
+  constexpr int D = NCH * 256;
+  const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
+  const int r0 = wid, r1 = wid + 11, r2 = wid + 22;
+  const bool has2 = r2 < kFusedRows;
+  float xa[NCH * 8], xb[NCH * 8], xc[NCH * 8];
+  ln_load_row<NCH>(a, r0, lane, xa);
+  ln_load_row<NCH>(a, r1, lane, xb);
+  ln_load_row<NCH>(a, has2 ? r2 : r1, lane, xc);
+  float sa, sb, sc;
+  ln_partial<NCH>(xa, sa);
+  ln_partial<NCH>(xb, sb);
+  ln_partial<NCH>(xc, sc);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    sc += __shfl_xor_sync(0xffffffffu, sc, o);
+  }
+  const float ma = sa / D, mb = sb / D, mc = sc / D;
+  float va = ln_centred<NCH>(xa, ma), vb = ln_centred<NCH>(xb, mb), vc = ln_centred<NCH>(xc, mc);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    va += __shfl_xor_sync(0xffffffffu, va, o);
+    vb += __shfl_xor_sync(0xffffffffu, vb, o);
+    vc += __shfl_xor_sync(0xffffffffu, vc, o);
+  }
+  // n = x * rstd - mean * rstd; a row >= R gets rstd = 0 (zeros, then the
+  // modulation is skipped for it below)
+  const float ra = r0 < a.R ? rsqrtf(va / D + a.eps) : 0.f;
+  const float rb = r1 < a.R ? rsqrtf(vb / D + a.eps) : 0.f;
+  const float rc = r2 < a.R ? rsqrtf(vc / D + a.eps) : 0.f;
+  const float ba = -ma * ra, bb = -mb * rb, bc = -mc * rc;
   const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst);
   const float4* ca = cm + D / 4;
 #pragma unroll
@@ -344,27 +378,19 @@ __device__ __forceinline__ void ln_store_row(const FusedArgs& a, uint8_t* stg, i
     const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = ca[2 * ch], a1 = ca[2 * ch + 1];
     const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
     const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    float o[8];
+    float oa[8], ob[8], oc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float n = (f[u * 8 + e] - mean) * rstd;
-      o[e] = mode == 0 ? rbf(n) * mv[e] + av[e] : n * mv[e] + av[e];
+      const float na = fmaf(xa[u * 8 + e], ra, ba), nb = fmaf(xb[u * 8 + e], rb, bb);
+      const float nc = fmaf(xc[u * 8 + e], rc, bc);
+      oa[e] = mode == 0 ? rbf(na) * mv[e] + av[e] : na * mv[e] + av[e];
+      ob[e] = mode == 0 ? rbf(nb) * mv[e] + av[e] : nb * mv[e] + av[e];
+      oc[e] = mode == 0 ? rbf(nc) * mv[e] + av[e] : nc * mv[e] + av[e];
     }
-    stage_chunk(stg, ch >> 3, r, ch & 7, pack8(o));
+    stage_chunk(stg, ch >> 3, r0, ch & 7, r0 < a.R ? pack8(oa) : make_uint4(0, 0, 0, 0));
+    stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? pack8(ob) : make_uint4(0, 0, 0, 0));
+    if (has2) stage_chunk(stg, ch >> 3, r2, ch & 7, r2 < a.R ? pack8(oc) : make_uint4(0, 0, 0, 0));
   }
-}
-
-template <int NCH>
-__device__ void stage_layernorm_t(const FusedArgs& a, uint8_t* stg, int mode) {
-  const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
-  const int r0 = wid, r1 = wid + 11, r2 = wid + 22;  // 11 worker warps over 32 rows
-  float xa[NCH * 8], xb[NCH * 8];
-  ln_load_row<NCH>(a, r0, lane, xa);
-  ln_load_row<NCH>(a, r1, lane, xb);
-  ln_store_row<NCH>(a, stg, r0, lane, mode, xa);
-  if (r2 < kFusedRows) ln_load_row<NCH>(a, r2, lane, xa);
-  ln_store_row<NCH>(a, stg, r1, lane, mode, xb);
-  if (r2 < kFusedRows) ln_store_row<NCH>(a, stg, r2, lane, mode, xa);
 }
 
 __device__ void stage_layernorm(const FusedArgs& a, uint8_t* stg, int mode) {
