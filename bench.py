@@ -20,6 +20,9 @@ larger than the 126 MB L2, so no L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fam|reference]
 
+(`--euler-steps N` shortens the chunk for ncu captures of the fused kernel; the
+reported workload name then no longer matches the metric's configuration.)
+
 `--impl reference` times the reference algorithm's CPU implementation (the
 CPU oracle restating FastWAM's PyTorch code, bf16 like the reference model)
 on this host's cores, rank 0 only.
@@ -48,6 +51,11 @@ METRIC = "action-chunk latency p50 ms (bs=1); chunks/sec at 1/2/4/8 B200 vs roof
 CFG = dict(hidden_dim=1024, action_dim=7, ffn_dim=4096, text_dim=4096, freq_dim=256, eps=1e-6,
            num_heads=16, attn_head_dim=64, num_layers=28)
 SA, SV, CTX, NSTEPS, SHIFT = 32, 1760, 64, 10, 1.0
+# DRAM read + write of fused_chunk_kernel per Euler step: one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of this workload at 2 Euler
+# steps, 2,079,377,664 B / 2.  Every step streams the same weights and K/V, so a
+# launch's traffic scales with the step count.
+FUSED_DRAM_BYTES_PER_STEP = 1_039_688_832
 
 
 def _peaks():
@@ -177,6 +185,27 @@ def time_dominant_kernel(M, dit, dev, reps=5):
     per = s.elapsed_time(e) / (reps * len(ws))
     alg = F * D * 2 + SA * F * 2 + SA * D * 2
     return per, alg
+
+
+def time_fused_kernel(eng, chunk, reps=5):
+    """The fused persistent chunk kernel alone: CUDA events recorded by the library
+    on the launching stream immediately around its launch (fam_action_set_kernel_events)
+    in plain (not graph-replayed) chunk calls, averaged over `reps` chunks.  Returns
+    ms per launch."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    e.record()
+    torch.cuda.synchronize()  # torch creates the CUDA events on first record
+    eng.set_kernel_events(s, e)
+    times = []
+    try:
+        for _ in range(reps + 1):
+            chunk()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+    finally:
+        eng.set_kernel_events(None, None)
+    return statistics.mean(times[1:])
 
 
 def cpu_reference_chunks_per_s(n_steps_timed: int, warmup: int = 1):
@@ -310,10 +339,22 @@ def run_fam(args):
     h2d = noise_h.numel() * 2 + ctx_h.numel() * 2 + cm_h.numel()
     d2h = out_h.numel() * 4
 
+    path = eng.last_path()
+    alg = algorithmic_bytes_per_chunk(dit)
+    if path == "fused":
+        def chunk_eager():
+            lat.copy_(noise_d)
+            eng.chunk(lat, ts, ds, ctx_d, cm_d, cks, cvs, mask_d, out=lat, use_graph=False)
+        k_ms = time_fused_kernel(eng, chunk_eager)
+        k_bytes = NSTEPS * (alg["per_eval_weights"] + alg["kv"])
+        k_name = "fused_chunk_kernel (persistent: every step and block of the chunk, 1 launch)"
+        k_traffic = FUSED_DRAM_BYTES_PER_STEP * NSTEPS
+    else:
+        k_ms, k_bytes = time_dominant_kernel(M, dit, dev)
+        k_name = "gemm_bf16_tc_kernel<32> (ffn.2 weight stream, split-K 16)"
+        k_traffic = None
     if rank == 0:
         hbm, tc, src = _peaks()
-        k_ms, k_bytes = time_dominant_kernel(M, dit, dev)
-        alg = algorithmic_bytes_per_chunk(dit)
         chunk_ms = elapsed_ms / K
         value = ws * K / (elapsed_ms / 1e3)
         line = {
@@ -322,13 +363,14 @@ def run_fam(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) inputs and K/V cache), random-init weights",
             "config": {"workload": "BASELINE configs[1]: action expert 1024h/16x64/28 blocks, "
-                                   "1760-token K/V cache, 64-token context, 10 Euler steps",
+                                   f"1760-token K/V cache, 64-token context, {NSTEPS} Euler steps",
                        "batch_per_gpu": 1, "action_tokens": SA, "video_tokens": SV,
                        "context_tokens": CTX, "euler_steps": NSTEPS, "parallelism": f"replicas x{ws}",
                        "l2": "working set per chunk (8.2 GB weights + 2 GB K/V streamed) >> 126 MB L2; no flush"},
-            "roofline": {"bound": "hbm", "kernel": "gemm_bf16_tc_kernel<32> (ffn.2 weight stream, split-K 16)",
+            "path": path,
+            "roofline": {"bound": "hbm", "kernel": k_name,
                          "achieved": k_bytes / (k_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
-                         "frac": k_bytes / (k_ms * 1e-3) / 1e9 / hbm, "traffic": None,
+                         "frac": k_bytes / (k_ms * 1e-3) / 1e9 / hbm, "traffic": k_traffic,
                          "peak_source": src, "avg_launch_us": k_ms * 1e3,
                          "bytes_per_launch": k_bytes},
             "chunk_roofline": {"bound": "hbm", "bytes_per_chunk": alg["bytes"],
@@ -363,7 +405,11 @@ def main():
     ap.add_argument("--impl", choices=["fam", "reference"], default="fam")
     ap.add_argument("--cpu-samples", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--euler-steps", type=int, default=NSTEPS,
+                    help="Euler steps per chunk (profiling captures only; the metric is quoted at 10)")
     args = ap.parse_args()
+    if args.euler_steps != NSTEPS:
+        globals()["NSTEPS"] = args.euler_steps
     if args.impl == "reference":
         run_reference(args)
     else:

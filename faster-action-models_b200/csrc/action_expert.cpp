@@ -134,6 +134,7 @@ struct fam_action_expert {
   int num_sms = 0;
   int mode = FAM_ACTION_AUTO;
   int last_path = 0;
+  cudaEvent_t kernel_start = nullptr, kernel_stop = nullptr;  // measurement hook
 };
 
 namespace {
@@ -562,7 +563,13 @@ int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float
   a.splits = (io.video_tokens + io.action_tokens + kFusedKeysPerSplit - 1) / kFusedKeysPerSplit;
   a.eps = g.eps;
   a.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(g.head_dim));
+  // measurement hook: plain (not captured) calls only
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  FAM_TRY(cudaStreamIsCapturing(c.st, &cap));
+  const bool timed = e->kernel_start != nullptr && cap == cudaStreamCaptureStatusNone;
+  if (timed) FAM_TRY(cudaEventRecord(e->kernel_start, c.st));
   FAM_LAUNCH(launch_fused_chunk(a, e->num_sms, c.st));
+  if (timed) FAM_TRY(cudaEventRecord(e->kernel_stop, c.st));
   return 0;
 }
 
@@ -580,6 +587,14 @@ int fam_action_set_mode(fam_action_expert* e, int32_t mode) {
 int fam_action_last_path(const fam_action_expert* e, int32_t* path) {
   if (e == nullptr || path == nullptr) return set_error("null argument");
   *path = e->last_path;
+  return FAM_OK;
+}
+
+int fam_action_set_kernel_events(fam_action_expert* e, void* start_event, void* stop_event) {
+  if (e == nullptr || (start_event == nullptr) != (stop_event == nullptr))
+    return set_error("fam_action_set_kernel_events: both events or neither");
+  e->kernel_start = static_cast<cudaEvent_t>(start_event);
+  e->kernel_stop = static_cast<cudaEvent_t>(stop_event);
   return FAM_OK;
 }
 

@@ -296,6 +296,14 @@ class ActionExpertEngine:
         check(lib().fam_action_last_path(self.handle, C.byref(n)), "fam_action_last_path")
         return {0: "none", 1: "chain", 2: "fused"}[n.value]
 
+    def set_kernel_events(self, start=None, stop=None) -> None:
+        """Record two torch.cuda.Event objects around the fused kernel of every
+        fused-path chunk called with use_graph=False (None, None clears).  The
+        events must have been recorded once (torch creates the CUDA event lazily)."""
+        hs = C.c_void_p(start.cuda_event) if start is not None else None
+        he = C.c_void_p(stop.cuda_event) if stop is not None else None
+        check(lib().fam_action_set_kernel_events(self.handle, hs, he), "fam_action_set_kernel_events")
+
     def denoise_step(self, latents, timestep, context, context_mask=None, cache_k=None,
                      cache_v=None, attn_mask=None) -> torch.Tensor:
         """One model evaluation (FastWAM._denoise_action_with_video_cache, fastwam.py:771-804)."""

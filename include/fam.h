@@ -286,6 +286,13 @@ FAM_API int fam_action_launch_count(const fam_action_expert* e, int32_t* count);
 FAM_API int fam_action_set_mode(fam_action_expert* e, int32_t mode);
 FAM_API int fam_action_last_path(const fam_action_expert* e, int32_t* path);
 
+/* Measurement hook (no counterpart in the reference): with two cudaEvent_t
+ * handles set, every fused-path fam_action_chunk called with use_graph = 0
+ * records start / stop on its stream immediately around the fused kernel
+ * launch, so a caller can time that kernel alone (graph replays record
+ * nothing).  NULL, NULL clears the hook. */
+FAM_API int fam_action_set_kernel_events(fam_action_expert* e, void* start_event, void* stop_event);
+
 /* ======================================================================
  * Video DiT prefill (WanVideoDiT backbone) — BASELINE config 2.
  *
