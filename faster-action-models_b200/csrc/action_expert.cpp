@@ -131,7 +131,7 @@ struct fam_action_expert {
   bool has_stacks = false;
   fam_action_stacks stacks = {};
   CUtensorMap tm[6];     // stacked weights for the fused kernel
-  int num_sms = 0;
+  int num_sms = 0;  // CTAs of the fused kernel's grid (2-CTA clusters, all co-resident)
   int mode = FAM_ACTION_AUTO;
   int last_path = 0;
   cudaEvent_t kernel_start = nullptr, kernel_stop = nullptr;  // measurement hook
@@ -483,9 +483,9 @@ bool fused_eligible(const fam_action_expert* e, const fam_action_io* io, int N) 
   const int HD = g.num_heads * g.head_dim;
   if (!e->has_stacks || e->num_sms < 64 || e->num_sms > kFusedMaxCtas) return false;
   if (io->batch != 1 || io->action_tokens > kFusedRows || g.head_dim != 64 || g.action_dim > 16) return false;
-  if (g.hidden_dim % 256 || HD % 128 || g.ffn_dim % 128 || g.hidden_dim > 1024) return false;
+  if (g.hidden_dim % 512 || HD % 128 || g.ffn_dim % 128 || g.hidden_dim > 1024) return false;
   if (g.num_layers > kFusedMaxLayers || io->context_tokens > 256 || N > kMaxSteps) return false;
-  if (3 * HD / 128 + HD / 128 + g.ffn_dim / 128 > e->num_sms) return false;
+  if (3 * HD / 128 + HD / 128 + g.ffn_dim / 128 > e->num_sms / 2) return false;  // one pair item per pair and phase
   const int skv = io->video_tokens + io->action_tokens;
   if ((skv + kFusedKeysPerSplit - 1) / kFusedKeysPerSplit > kFusedMaxSplits) return false;
   if (io->video_tokens > 0 && (io->video_token_stride % 8)) return false;
@@ -640,10 +640,7 @@ int fam_action_expert_create(const fam_action_config* cfg, const fam_action_weig
       e->has_stacks = true;
       rc = check_cuda(fused_init_attributes(), "fused kernel attributes");
       if (rc) return rc;
-      int dev = 0;
-      cudaGetDevice(&dev);
-      rc = check_cuda(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
-      if (rc) return rc;
+      e->num_sms = fused_max_ctas();  // co-resident CTAs in 2-CTA clusters (0: fused path off)
     } else {
       e->w.stacks = nullptr;
     }

@@ -36,6 +36,8 @@
 // fresh keys by s_k.  Reference numerics otherwise as the separate kernels:
 // DiTBlock.forward (wan_video_dit.py:248-267), MoT joint attention
 // (mot.py:528-578), scheduler step (scheduler_continuous.py:82-88).
+#include <cstddef>
+
 #include "action_fused.h"
 #include "fam_common.cuh"
 #include "fam_internal.h"
@@ -55,6 +57,10 @@ constexpr int kSplitStride = kFusedRows * 64 + kFusedRows * 2;  // floats per sp
 // (4 x 32 tokens x 16 pairs), then the LayerNorm constants (2 x D fp32).
 constexpr int kStgRope = 16 * kBBlock;
 constexpr int kStgLnConst = kStgRope + 4 * kFusedRows * 16 * 8;
+// pair items: the peer's partial accumulators of this CTA's output rows,
+// [32 tokens][64 rows] fp32, behind the half-width B operand (<= 8 K blocks)
+constexpr int kStgXacc = 8 * kBBlock;
+static_assert(kStgXacc + kFusedRows * 64 * 4 <= kStgRope, "pair exchange buffer");
 static_assert(kStgLnConst + 2 * 1024 * 4 <= kFusedStaging, "staging layout");
 
 struct FusedSmemTail {
@@ -66,7 +72,15 @@ struct FusedSmemTail {
   float stat[kFusedRows][2];
   float scale[2][kFusedRows];                 // per-row q scale, per-key scale
   int last;
+  // pair items: the peer CTA writes its half-row LayerNorm sums here and
+  // arrives on xstat_bar (one arrival per worker warp); its partial
+  // accumulators go to the staging (kStgXacc) with arrivals on xacc_bar
+  alignas(16) float xstat[kFusedRows][2];  // 8-byte (v2) remote stores and loads
+  uint64_t xstat_bar;
+  uint64_t xacc_bar;
 };
+
+static_assert(offsetof(FusedSmemTail, xstat) % 8 == 0, "xstat rows are accessed as float2");
 
 __host__ __device__ constexpr size_t fused_tail_offset() {
   return static_cast<size_t>(kFusedRing) * kATile + kFusedStaging;
@@ -86,13 +100,20 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 
 // ---------------------------------------------------------------- schedule
+// GEMM work items.  The LayerNorm GEMMs (qkv, cross-q, ffn.0: full K = D) run
+// as pair items on the two CTAs of a cluster: each CTA LayerNorms and stages
+// half of the K columns, runs half of the K blocks, and the pair exchanges the
+// row statistics and the partial accumulators through distributed shared
+// memory (each CTA then finishes half of the 128 output rows).  The residual
+// GEMMs (o, cross-o, ffn.2) are split-K items of one CTA.
 struct FItem {
   int n;       // 128-row tile of the output features
-  int sub;     // head (o, co), ffn.0 tile (ffn2), 0 otherwise
+  int sub;     // head group (o, co), ffn.0 tile group (ffn2), 0 otherwise
   int kb0;     // first 64-wide K block
   int nkb;     // K blocks
 };
 
+__device__ __forceinline__ bool f_pair(int p) { return p == kFQkv || p == kFCq || p == kFFfn0; }
 __device__ __forceinline__ int f_rows(const FusedArgs& a, int p) {
   switch (p) {
     case kFQkv: return 3 * a.HD;
@@ -118,18 +139,29 @@ __device__ __forceinline__ int f_count(const FusedArgs& a, int p) {
   if (p == kFFfn2) return nt * (a.F / 128 / f_ffn_group(a));
   return nt;
 }
-// CTA offsets spread the full-K tiles (qkv, cross-q, ffn.0) over distinct SMs.
+// Placement: pair items on pairs 0.. (qkv, then cross-q, then ffn.0); ffn.2 on
+// CTAs 0.. (the qkv / cross-q CTAs: their next LayerNorm GEMM is phases away,
+// so both items' tiles fit the ring in time); o and cross-o after the pair
+// CTAs (idle in the phase before the ffn.0 pairs take theirs).
 __device__ __forceinline__ int f_offset(const FusedArgs& a, int p) {
+  const int pq = 3 * a.HD / 128, pc = a.HD / 128, pf = a.F / 128;
   switch (p) {
     case kFQkv: return 0;
-    case kFCq: return 3 * a.HD / 128;
-    case kFFfn0: return 3 * a.HD / 128 + a.HD / 128;
-    default: return 3 * a.HD / 128 + a.HD / 128 + a.F / 128;
+    case kFCq: return pq;
+    case kFFfn0: return pq + pc;
+    case kFFfn2: return 0;
+    default: return 2 * (pq + pc + pf);  // o, cross-o (CTA units)
   }
 }
-__device__ __forceinline__ FItem f_item(const FusedArgs& a, int p, int i) {
+// the scheduling unit of a phase: a pair (cluster) or a CTA
+__device__ __forceinline__ int f_units(int p, int G) { return f_pair(p) ? G / 2 : G; }
+__device__ __forceinline__ int f_first(const FusedArgs& a, int p, int cta, int G) {
+  const int u = f_pair(p) ? cta / 2 : cta, n = f_units(p, G);
+  return ((u - f_offset(a, p)) % n + n) % n;
+}
+// item i of phase p; `half` = cluster rank for pair items
+__device__ __forceinline__ FItem f_item(const FusedArgs& a, int p, int i, int half) {
   FItem it;
-  const int kbs_full = a.D / 64;
   if (p == kFO || p == kFCo) {
     const int hg = f_head_group(a), groups = a.H / hg;
     it.n = i / groups;
@@ -143,15 +175,13 @@ __device__ __forceinline__ FItem f_item(const FusedArgs& a, int p, int i) {
     it.kb0 = it.sub * 2 * fg;
     it.nkb = 2 * fg;
   } else {
+    const int kh = a.D / 128;  // K blocks per half
     it.n = i;
     it.sub = 0;
-    it.kb0 = 0;
-    it.nkb = kbs_full;
+    it.kb0 = half * kh;
+    it.nkb = kh;
   }
   return it;
-}
-__device__ __forceinline__ int f_first(const FusedArgs& a, int p, int cta, int G) {
-  return ((cta - f_offset(a, p)) % G + G) % G;
 }
 
 // ----------------------------------------------------------- grid barrier
@@ -297,9 +327,12 @@ __device__ __forceinline__ float4 ld_cg_f4_early(const float* p) {
   return v;
 }
 
+// Half rows: this CTA's D / 2 columns [half * D / 2, ...) of residual row r,
+// lane chunks lane + 32u (u < NCH, D / 2 = 256 NCH).
 template <int NCH>
-__device__ __forceinline__ void ln_load_row(const FusedArgs& a, int r, int lane, float (&v)[NCH * 8]) {
-  const float* xr = a.x + static_cast<long long>(r) * (NCH * 256);
+__device__ __forceinline__ void ln_load_half(const FusedArgs& a, int r, int lane, int half,
+                                             float (&v)[NCH * 8]) {
+  const float* xr = a.x + static_cast<long long>(r) * a.D + half * (NCH * 256);
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
     const int ch = lane + 32 * u;
@@ -313,69 +346,93 @@ __device__ __forceinline__ void ln_load_row(const FusedArgs& a, int r, int lane,
   }
 }
 
-// Row statistics of a LayerNorm over D = 256 NCH columns (two passes over the
-// registers: mean, then the centred sum of squares).
+// Shifted sums of a half row: sum (x - c) and sum (x - c)^2 with c = x[r][0]
+// (the same shift in both halves keeps the one-pass variance well conditioned).
 template <int NCH>
-__device__ __forceinline__ void ln_partial(const float (&f)[NCH * 8], float& sum) {
-  sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < NCH * 8; ++i) sum += f[i];
-}
-template <int NCH>
-__device__ __forceinline__ float ln_centred(const float (&f)[NCH * 8], float mean) {
-  float var = 0.f;
+__device__ __forceinline__ void ln_half_sums(const float (&f)[NCH * 8], float c, float& s1, float& s2) {
+  s1 = 0.f;
+  s2 = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH * 8; ++i) {
-    const float d = f[i] - mean;
-    var += d * d;
+    const float d = f[i] - c;
+    s1 += d;
+    s2 += d * d;
   }
-  return var;
 }
 
-// The warp's three rows r0 = w, r1 = w + 11, r2 = w + 22 of the 11 worker
-// warps, processed together so their loads, reductions and stores overlap
-// (independent instruction streams).  Rows >= R are staged as zeros; a row
-// >= 32 (the third row of the last warp) does not exist.
+__device__ __forceinline__ bool mbar_wait_cl(const FusedArgs& a, uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(a.status, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// LayerNorm staging of a pair item.  mode 0: AdaLN (constants 1 + scale,
+// shift); mode 1: affine norm3.  The warp's three rows r0 = w, r1 = w + 11,
+// r2 = w + 22 are processed together (independent instruction streams).  The
+// two CTAs of the pair exchange their half-row sums: lane 0 of every worker
+// warp stores them into the peer's xstat and arrives on the peer's xstat_bar,
+// then waits for the peer's eleven arrivals on its own.  Rows >= R are staged
+// as zeros; a row >= 32 (the third row of the last warp) does not exist.
+// Returns false on a timed-out exchange.
 template <int NCH>
-__device__ void stage_layernorm_t(const FusedArgs& a, uint8_t* stg, int mode) {
-  constexpr int D = NCH * 256;
+__device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, int mode, int half,
+                                       uint32_t parity) {
+  constexpr int DH = NCH * 256;  // columns of this half
+  const int D = a.D;
   const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
   const int r0 = wid, r1 = wid + 11, r2 = wid + 22;
   const bool has2 = r2 < kFusedRows;
   float xa[NCH * 8], xb[NCH * 8], xc[NCH * 8];
-  ln_load_row<NCH>(a, r0, lane, xa);
-  ln_load_row<NCH>(a, r1, lane, xb);
-  ln_load_row<NCH>(a, has2 ? r2 : r1, lane, xc);
-  float sa, sb, sc;
-  ln_partial<NCH>(xa, sa);
-  ln_partial<NCH>(xb, sb);
-  ln_partial<NCH>(xc, sc);
+  ln_load_half<NCH>(a, r0, lane, half, xa);
+  ln_load_half<NCH>(a, r1, lane, half, xb);
+  ln_load_half<NCH>(a, has2 ? r2 : r1, lane, half, xc);
+  const float ca = r0 < a.R ? __ldcg(a.x + static_cast<long long>(r0) * D) : 0.f;
+  const float cb = r1 < a.R ? __ldcg(a.x + static_cast<long long>(r1) * D) : 0.f;
+  const float cc = (has2 && r2 < a.R) ? __ldcg(a.x + static_cast<long long>(r2) * D) : 0.f;
+  float s[6];
+  ln_half_sums<NCH>(xa, ca, s[0], s[1]);
+  ln_half_sums<NCH>(xb, cb, s[2], s[3]);
+  ln_half_sums<NCH>(xc, cc, s[4], s[5]);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    sa += __shfl_xor_sync(0xffffffffu, sa, o);
-    sb += __shfl_xor_sync(0xffffffffu, sb, o);
-    sc += __shfl_xor_sync(0xffffffffu, sc, o);
-  }
-  const float ma = sa / D, mb = sb / D, mc = sc / D;
-  float va = ln_centred<NCH>(xa, ma), vb = ln_centred<NCH>(xb, mb), vc = ln_centred<NCH>(xc, mc);
+  for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    va += __shfl_xor_sync(0xffffffffu, va, o);
-    vb += __shfl_xor_sync(0xffffffffu, vb, o);
-    vc += __shfl_xor_sync(0xffffffffu, vc, o);
+    for (int i = 0; i < 6; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
+  // exchange with the peer
+  const uint32_t peer = half ^ 1;
+  if (lane == 0) {
+    st_cluster_v2(cluster_map(&tl->xstat[r0][0], peer), s[0], s[1]);
+    st_cluster_v2(cluster_map(&tl->xstat[r1][0], peer), s[2], s[3]);
+    if (has2) st_cluster_v2(cluster_map(&tl->xstat[r2][0], peer), s[4], s[5]);
+    mbar_arrive_cluster(cluster_map(&tl->xstat_bar, peer));
   }
-  // n = x * rstd - mean * rstd; a row >= R gets rstd = 0 (zeros, then the
-  // modulation is skipped for it below)
-  const float ra = r0 < a.R ? rsqrtf(va / D + a.eps) : 0.f;
-  const float rb = r1 < a.R ? rsqrtf(vb / D + a.eps) : 0.f;
-  const float rc = r2 < a.R ? rsqrtf(vc / D + a.eps) : 0.f;
-  const float ba = -ma * ra, bb = -mb * rb, bc = -mc * rc;
-  const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst);
-  const float4* ca = cm + D / 4;
+  const bool ok = mbar_wait_cl(a, &tl->xstat_bar, parity, kErrWaitFull);
+  if (!ok) return false;
+  const float2 pa = *reinterpret_cast<const float2*>(&tl->xstat[r0][0]);
+  const float2 pb = *reinterpret_cast<const float2*>(&tl->xstat[r1][0]);
+  const float2 pc = has2 ? *reinterpret_cast<const float2*>(&tl->xstat[r2][0]) : make_float2(0.f, 0.f);
+  // mean = c + S1 / D, var = S2 / D - (S1 / D)^2; n = x * rstd - mean * rstd
+  auto stats = [&](float c, float s1, float s2, int r, float& rs, float& b) {
+    const float m1 = s1 / D;
+    const float var = fmaxf(s2 / D - m1 * m1, 0.f);
+    rs = r < a.R ? rsqrtf(var + a.eps) : 0.f;
+    b = -(c + m1) * rs;
+  };
+  float ra, ba, rb, bb, rc, bc;
+  stats(ca, s[0] + pa.x, s[1] + pa.y, r0, ra, ba);
+  stats(cb, s[2] + pb.x, s[3] + pb.y, r1, rb, bb);
+  stats(cc, s[4] + pc.x, s[5] + pc.y, has2 ? r2 : kFusedRows, rc, bc);
+  const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst) + half * (DH / 4);
+  const float4* cadd = reinterpret_cast<const float4*>(stg + kStgLnConst) + D / 4 + half * (DH / 4);
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
-    const int ch = lane + 32 * u;
-    const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = ca[2 * ch], a1 = ca[2 * ch + 1];
+    const int ch = lane + 32 * u;  // chunk within this half: local K block ch >> 3
+    const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = cadd[2 * ch], a1 = cadd[2 * ch + 1];
     const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
     const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     float oa[8], ob[8], oc[8];
@@ -391,15 +448,13 @@ __device__ void stage_layernorm_t(const FusedArgs& a, uint8_t* stg, int mode) {
     stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? pack8(ob) : make_uint4(0, 0, 0, 0));
     if (has2) stage_chunk(stg, ch >> 3, r2, ch & 7, r2 < a.R ? pack8(oc) : make_uint4(0, 0, 0, 0));
   }
+  return true;
 }
 
-__device__ void stage_layernorm(const FusedArgs& a, uint8_t* stg, int mode) {
-  switch (a.D >> 8) {
-    case 1: stage_layernorm_t<1>(a, stg, mode); break;
-    case 2: stage_layernorm_t<2>(a, stg, mode); break;
-    case 3: stage_layernorm_t<3>(a, stg, mode); break;
-    default: stage_layernorm_t<4>(a, stg, mode); break;
-  }
+__device__ bool stage_layernorm_pair(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, int mode, int half,
+                                     uint32_t parity) {
+  return (a.D >> 9) == 1 ? stage_layernorm_pair_t<1>(a, stg, tl, mode, half, parity)
+                         : stage_layernorm_pair_t<2>(a, stg, tl, mode, half, parity);
 }
 
 // Copy columns [col0, col0 + 64 * nkb) of a bf16 [R, ld] buffer into the
@@ -563,15 +618,25 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
 }
 
 // One GEMM work item on the workers (the weight tiles arrive through the ring).
+// Pair items (qkv, cross-q, ffn.0) run on both CTAs of a cluster (`half` =
+// cluster rank): each stages and multiplies its K half, then the epilogue
+// warps of the TMEM lane quarters the peer owns (rank 0 owns quarters 0-1 =
+// output rows 0-63 of the tile, rank 1 quarters 2-3) send their partial sums
+// to the peer (kStgXacc, [token][64] fp32) and the owners add them and finish.
 __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, FusedSmemTail* tl,
                           int p, int step, int l, const FItem& it, uint32_t& ring_it,
-                          uint32_t& items_done) {
+                          uint32_t& items_done, uint32_t& pair_done) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool pair = f_pair(p);
+  const int half = pair ? static_cast<int>(cluster_ctarank()) : 0;
+  const uint32_t pparity = pair_done & 1;
   // 1. B operand
   switch (p) {
-    case kFQkv: stage_layernorm(a, stg, 0); break;
-    case kFCq: stage_layernorm(a, stg, 1); break;
-    case kFFfn0: stage_layernorm(a, stg, 0); break;
+    case kFQkv:
+    case kFCq:
+    case kFFfn0:
+      if (!stage_layernorm_pair(a, stg, tl, p == kFCq ? 1 : 0, half, pparity)) tl->abort = 1;
+      break;
     case kFO: stage_copy(a, stg, a.ao, a.HD, it.kb0 * 64, it.nkb); break;
     case kFCo: stage_copy(a, stg, a.ci, a.HD, it.kb0 * 64, it.nkb); break;
     default: stage_copy(a, stg, a.fh, a.F, it.kb0 * 64, it.nkb); break;
@@ -612,8 +677,9 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
   if (warp >= 2 && warp <= 9) {
     const int q = warp & 3, t0 = warp >= 6 ? kEpiTokens : 0;
     const int f = it.n * 128 + q * 32 + lane;
+    const bool keep = !pair || ((q >> 1) == half);  // pair: this CTA finishes its half of the rows
     EpiConst c;
-    epi_load(a, stg, p, step, l, it, f, t0, c);
+    if (keep) epi_load(a, stg, p, step, l, it, f, t0, c);
     const bool ok = mbar_wait(&tl->accum, items_done & 1, a.status, kErrWaitAccum);
     tc_fence_after();
     if (!ok) tl->abort = 1;
@@ -634,10 +700,26 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
         v[i] = t;
       }
     }
-    if (ok && !tl->abort) gemm_epilogue(a, p, step, l, f, t0, c, v);
+    if (pair) {
+      float* xacc = reinterpret_cast<float*>(stg + kStgXacc);  // [token][64]
+      const int fl = (q & 1) * 32 + lane;
+      if (!keep) {
+        // partial sums of the peer's rows -> the peer's staging, then arrive
+        const uint32_t dst = cluster_map(xacc, half ^ 1);
+#pragma unroll
+        for (int jj = 0; jj < kEpiTokens; ++jj) st_cluster_f32(dst + ((t0 + jj) * 64 + fl) * 4, v[jj]);
+        mbar_arrive_cluster(cluster_map(&tl->xacc_bar, half ^ 1));
+      } else {
+        if (!mbar_wait_cl(a, &tl->xacc_bar, pparity, kErrWaitAccum)) tl->abort = 1;
+#pragma unroll
+        for (int jj = 0; jj < kEpiTokens; ++jj) v[jj] += xacc[(t0 + jj) * 64 + fl];
+      }
+    }
+    if (keep && ok && !tl->abort) gemm_epilogue(a, p, step, l, f, t0, c, v);
     tc_fence_before();
   }
   ++items_done;
+  if (pair) ++pair_done;
   bar_workers();
 }
 
@@ -1020,11 +1102,11 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
 // after the cross-q CTAs (cross), so that they are idle in the phase before
 // and can prefetch their constant K / V there.
 __device__ __forceinline__ int attn_joint_first(const FusedArgs& a, int cta, int G) {
-  const int off = 3 * a.HD / 128;
+  const int off = 2 * (3 * a.HD / 128);  // after the qkv pairs
   return ((cta - off) % G + G) % G;
 }
 __device__ __forceinline__ int attn_cross_first(const FusedArgs& a, int cta, int G) {
-  const int off = 3 * a.HD / 128 + a.HD / 128;
+  const int off = 2 * (3 * a.HD / 128 + a.HD / 128 + a.F / 128);  // after every pair CTA
   return ((cta - off) % G + G) % G;
 }
 
@@ -1105,6 +1187,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
       mbar_init(&tl->empty[s], 1);
     }
     mbar_init(&tl->accum, kFusedIssuers);
+    mbar_init(&tl->xstat_bar, kFusedWorkers / 32);  // one arrival per peer worker warp
+    mbar_init(&tl->xacc_bar, 4 * 32);               // every lane of the peer's 4 sending warps
     tl->abort = 0;
     fence_mbar_init();
     for (int p = 0; p < 6; ++p) tma_prefetch_desc(&a.tm[p]);
@@ -1126,8 +1210,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         for (int l = 0; l < a.L && !tl->abort; ++l)
           for (int p = 0; p < 6 && !tl->abort; ++p) {
             const int cnt = f_count(a, p), rows = f_rows(a, p);
-            for (int i = f_first(a, p, cta, G); i < cnt && !tl->abort; i += G) {
-              const FItem itm = f_item(a, p, i);
+            const int half = f_pair(p) ? static_cast<int>(cluster_ctarank()) : 0;
+            for (int i = f_first(a, p, cta, G); i < cnt && !tl->abort; i += f_units(p, G)) {
+              const FItem itm = f_item(a, p, i, half);
               for (int k = 0; k < itm.nkb; ++k) {
                 const int s = it % kFusedRing;
                 if (it >= kFusedRing &&
@@ -1149,7 +1234,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     }
   } else {
     // ------------------------------------------------------ workers
-    uint32_t ring_it = 0, items_done = 0, epoch = 0;
+    uint32_t ring_it = 0, items_done = 0, epoch = 0, pair_done = 0;
+    const int rank = static_cast<int>(cluster_ctarank());
     const int R = a.R, D = a.D;
     const bool has_qkv = f_first(a, kFQkv, cta, G) < f_count(a, kFQkv);
     const bool has_cq = f_first(a, kFCq, cta, G) < f_count(a, kFCq);
@@ -1169,8 +1255,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
       }
       for (int l = 0; l < a.L && !tl->abort; ++l) {
         // qkv
-        for (int i = f_first(a, kFQkv, cta, G); i < f_count(a, kFQkv); i += G)
-          gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i), ring_it, items_done);
+        for (int i = f_first(a, kFQkv, cta, G); i < f_count(a, kFQkv); i += f_units(kFQkv, G))
+          gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i, rank), ring_it, items_done, pair_done);
         if (attn_joint_first(a, cta, G) < a.H * a.splits)
           attn_stage_const(a, stg, joint_item(a, step, l, attn_joint_first(a, cta, G)));
         if (!grid_sync(a, epoch, tl)) break;
@@ -1179,12 +1265,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         for (int i = attn_joint_first(a, cta, G); i < a.H * a.splits; i += G)
           attention_item(a, stg, tl, joint_item(a, step, l, i), i == attn_joint_first(a, cta, G));
         if (!grid_sync(a, epoch, tl)) break;
-        for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += G)
-          gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i), ring_it, items_done);
+        for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += f_units(kFO, G))
+          gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i, rank), ring_it, items_done, pair_done);
         if (has_cq) ln_const_prefetch(a, stg, step, l, 1, 0);
         if (!grid_sync(a, epoch, tl)) break;
-        for (int i = f_first(a, kFCq, cta, G); i < f_count(a, kFCq); i += G)
-          gemm_item(a, ring, stg, tl, kFCq, step, l, f_item(a, kFCq, i), ring_it, items_done);
+        for (int i = f_first(a, kFCq, cta, G); i < f_count(a, kFCq); i += f_units(kFCq, G))
+          gemm_item(a, ring, stg, tl, kFCq, step, l, f_item(a, kFCq, i, rank), ring_it, items_done, pair_done);
         if (a.C > 0 && attn_cross_first(a, cta, G) < a.H)
           attn_stage_const(a, stg, cross_item(a, step, l, attn_cross_first(a, cta, G)));
         if (!grid_sync(a, epoch, tl)) break;
@@ -1193,15 +1279,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         for (int h = attn_cross_first(a, cta, G); h < a.H && a.C > 0; h += G)
           attention_item(a, stg, tl, cross_item(a, step, l, h), h == attn_cross_first(a, cta, G));
         if (!grid_sync(a, epoch, tl)) break;
-        for (int i = f_first(a, kFCo, cta, G); i < f_count(a, kFCo); i += G)
-          gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i), ring_it, items_done);
+        for (int i = f_first(a, kFCo, cta, G); i < f_count(a, kFCo); i += f_units(kFCo, G))
+          gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i, rank), ring_it, items_done, pair_done);
         if (has_ffn0) ln_const_prefetch(a, stg, step, l, 0, 3);
         if (!grid_sync(a, epoch, tl)) break;
-        for (int i = f_first(a, kFFfn0, cta, G); i < f_count(a, kFFfn0); i += G)
-          gemm_item(a, ring, stg, tl, kFFfn0, step, l, f_item(a, kFFfn0, i), ring_it, items_done);
+        for (int i = f_first(a, kFFfn0, cta, G); i < f_count(a, kFFfn0); i += f_units(kFFfn0, G))
+          gemm_item(a, ring, stg, tl, kFFfn0, step, l, f_item(a, kFFfn0, i, rank), ring_it, items_done, pair_done);
         if (!grid_sync(a, epoch, tl)) break;
-        for (int i = f_first(a, kFFfn2, cta, G); i < f_count(a, kFFfn2); i += G)
-          gemm_item(a, ring, stg, tl, kFFfn2, step, l, f_item(a, kFFfn2, i), ring_it, items_done);
+        for (int i = f_first(a, kFFfn2, cta, G); i < f_count(a, kFFfn2); i += f_units(kFFfn2, G))
+          gemm_item(a, ring, stg, tl, kFFfn2, step, l, f_item(a, kFFfn2, i, rank), ring_it, items_done, pair_done);
         if (has_qkv && l + 1 < a.L) ln_const_prefetch(a, stg, step, l + 1, 0, 0);
         if (!grid_sync(a, epoch, tl)) break;
       }
@@ -1261,6 +1347,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     tc_fence_after();
     tmem_dealloc(tl->tmem, kFusedIssuers * kFusedRows);
   }
+  // the peer CTA may still write into this CTA's shared memory (DSMEM) until
+  // it is done too
+  cluster_barrier();
 }
 
 cudaError_t fused_init_attributes() {
@@ -1274,12 +1363,36 @@ cudaError_t launch_fused_chunk(const FusedArgs& a, int grid, cudaStream_t st) {
   cfg.blockDim = dim3(kFusedThreads);
   cfg.dynamicSmemBytes = fused_smem_bytes();
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, fused_chunk_kernel, a);
+}
+
+int fused_max_ctas() {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kFusedThreads);
+  cfg.dynamicSmemBytes = fused_smem_bytes();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fused_chunk_kernel, a);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, fused_chunk_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return 2 * clusters;
 }
 
 }  // namespace fam

@@ -12,7 +12,7 @@ namespace fam {
 
 constexpr int kFusedMaxLayers = 32;
 constexpr int kFusedRows = 32;        // token rows of one sample (MMA N, zero padded)
-constexpr int kFusedThreads = 384;    // warp 0 weight producer, warps 1..11 workers
+constexpr int kFusedThreads = 384;    // warp 0 weight producer, warps 1..11 workers (clusters of 2 CTAs)
 constexpr int kFusedWorkers = 352;
 constexpr int kFusedRing = 8;         // 128 x 64 bf16 weight tiles in flight per CTA (128 KB)
 constexpr int kFusedStaging = 88 * 1024;
@@ -56,5 +56,7 @@ struct FusedArgs {
 size_t fused_smem_bytes();
 cudaError_t launch_fused_chunk(const FusedArgs& a, int grid, cudaStream_t st);
 cudaError_t fused_init_attributes();
+// CTAs of the largest co-resident grid of 2-CTA clusters (0 if unknown).
+int fused_max_ctas();
 
 }  // namespace fam

@@ -198,7 +198,7 @@ typedef struct fam_action_layer {
  * modules): the same per-block tensors stacked over the blocks, contiguous
  * (block l of a stack starts at l * rows).  When given, fam_action_chunk can
  * run the fused persistent chunk kernel (batch 1, <= 32 action tokens,
- * action_dim <= 16, head_dim 64, hidden a multiple of 256 and <= 1024, other
+ * action_dim <= 16, head_dim 64, hidden 512 or 1024, other
  * widths multiples of 128, <= 256 context tokens, <= 2560 video + action
  * keys); the layer pointers must point into these stacks. */
 typedef struct fam_action_stacks {

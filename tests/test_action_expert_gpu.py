@@ -92,9 +92,10 @@ def test_chunk_matches_oracle_and_is_deterministic():
 
 @pytest.mark.parametrize("Sa,Sv,C,tpf", [(32, 200, 16, 50), (8, 97, 5, 97), (20, 300, 64, 60)])
 def test_fused_kernel_matches_chain_and_oracle(Sa, Sv, C, tpf):
-    """The fused persistent chunk kernel (batch 1) against the launch chain and the oracle."""
-    dit, sd, cfg = _build(seed=11)
-    ctx, cm, ck, cv, noise, mask = _inputs(1, Sa, Sv, max(C, 1), cfg.text_dim, 256, cfg.num_layers, tpf)
+    """The fused persistent chunk kernel (batch 1) against the launch chain and the oracle
+    (hidden 512 = two 256-wide halves per CTA pair, 8 heads)."""
+    dit, sd, cfg = _build(D=512, H=8, F=1024, seed=11)
+    ctx, cm, ck, cv, noise, mask = _inputs(1, Sa, Sv, max(C, 1), cfg.text_dim, 512, cfg.num_layers, tpf)
     ctx = ctx[:, :C] if C else ctx[:, :0]
     cm = cm[:, :C] if C else cm[:, :0]
     ts, ds = M.build_inference_schedule(3, 5.0)
