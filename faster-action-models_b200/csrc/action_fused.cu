@@ -185,13 +185,16 @@ __device__ __forceinline__ FItem f_item(const FusedArgs& a, int p, int i, int ha
 }
 
 // ----------------------------------------------------------- grid barrier
-// Flag barrier (no contended atomic, one propagation hop): every CTA
-// release-stores the barrier index into its own 128-byte flag line, and worker
-// thread i of every CTA acquire-polls the line of CTA i.  Every wait is
-// bounded; a timeout or an abort raised elsewhere sets the abort word and
-// every CTA leaves its phase loop.
-__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Flag barrier (one propagation hop): every worker warp of a CTA adds 1 to the
+// CTA's own 128-byte flag line with a release reduction right after its own
+// writes of the phase (the warps' write-acknowledgement waits overlap instead
+// of one CTA-wide fence after the slowest warp), and worker thread i of every
+// CTA acquire-polls the line of CTA i until it reaches 11 x the barrier index.
+// Every wait is bounded; a timeout or an abort raised elsewhere sets the abort
+// word and every CTA leaves its phase loop.
+constexpr unsigned kFusedWorkerWarps = kFusedWorkers / 32;
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ bool poll_ge(const FusedArgs& a, const unsigned* p, unsigned target,
@@ -209,18 +212,14 @@ __device__ __forceinline__ bool poll_ge(const FusedArgs& a, const unsigned* p, u
 }
 
 __device__ __forceinline__ bool grid_sync(const FusedArgs& a, unsigned& epoch, FusedSmemTail* tl) {
-  // The CTA barrier orders the phase's writes of every worker before the
-  // flag thread's fence + release store (cumulative), as in a cooperative
-  // grid sync: one fence per CTA, not one per thread.
-  bar_workers();
+  // __syncwarp orders the warp's writes before lane 0's release reduction
+  // (cumulative at gpu scope)
+  __syncwarp();
   ++epoch;
   const int wt = threadIdx.x - 32;
-  if (wt == 0) {
-    __threadfence();
-    st_release(a.flags + blockIdx.x * 32, epoch);
-  }
-  // one hop: worker thread i of every CTA waits for CTA i's arrival
-  if (wt < static_cast<int>(gridDim.x)) poll_ge(a, a.flags + wt * 32, epoch, tl);
+  if ((threadIdx.x & 31) == 0) red_release_add(a.flags + blockIdx.x * 32, 1u);
+  // one hop: worker thread i of every CTA waits for CTA i's eleven arrivals
+  if (wt < static_cast<int>(gridDim.x)) poll_ge(a, a.flags + wt * 32, epoch * kFusedWorkerWarps, tl);
   bar_workers();
   return tl->abort == 0;
 }
@@ -1257,13 +1256,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         // qkv
         for (int i = f_first(a, kFQkv, cta, G); i < f_count(a, kFQkv); i += f_units(kFQkv, G))
           gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i, rank), ring_it, items_done, pair_done);
-        if (attn_joint_first(a, cta, G) < a.H * a.splits)
+        // constant K / V of the first joint item, on CTAs without a qkv item
+        // (one that has one would delay its barrier arrival)
+        if (!has_qkv && attn_joint_first(a, cta, G) < a.H * a.splits)
           attn_stage_const(a, stg, joint_item(a, step, l, attn_joint_first(a, cta, G)));
         if (!grid_sync(a, epoch, tl)) break;
         // joint attention: items (head, split); the first item's constant
         // K / V were prefetched at the end of the qkv phase
         for (int i = attn_joint_first(a, cta, G); i < a.H * a.splits; i += G)
-          attention_item(a, stg, tl, joint_item(a, step, l, i), i == attn_joint_first(a, cta, G));
+          attention_item(a, stg, tl, joint_item(a, step, l, i), !has_qkv && i == attn_joint_first(a, cta, G));
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += f_units(kFO, G))
           gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i, rank), ring_it, items_done, pair_done);
