@@ -965,12 +965,10 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
   }
   bar_workers();  // K/V staging no longer read: reuse it for the block merge
   // block partials: O [4][32][kCombRow] (padded rows: conflict-free stores),
-  // (m, l) [4][32][2], then per (block, row) weights and per row 1 / L
+  // (m, l) [4][32][2]
   constexpr int kCombRow = 64 + 4;
   float* comb = reinterpret_cast<float*>(stg);
   float* cml = comb + 4 * kFusedRows * kCombRow;
-  float* cw = cml + 4 * kFusedRows * 2;            // [4][32]
-  float* crow = cw + 4 * kFusedRows;               // [32][2]: M, L
   if (active) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -987,33 +985,29 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
   }
   bar_workers();
   const int nsplit = t.nsplit;
-  for (int r = threadIdx.x - 32; r < kFusedRows; r += kFusedWorkers) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) M = fmaxf(M, cml[(b * kFusedRows + r) * 2]);
-    const float base = M == -INFINITY ? 0.f : M;
-    float L = 0.f;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const float w = exp2f(cml[(b * kFusedRows + r) * 2] - base);
-      cw[b * kFusedRows + r] = w;
-      L += w * cml[(b * kFusedRows + r) * 2 + 1];
-    }
-    crow[r * 2] = M;
-    crow[r * 2 + 1] = L;
-  }
-  bar_workers();
-  // merge the 4 key blocks: the split's (O, m, l), four dims per thread.  A
-  // split partial is O [32][64] followed by (m, l) [32][2] (kSplitStride floats).
+  // merge the 4 key blocks: the split's (O, m, l), four dims per thread; every
+  // thread derives its row's block weights itself (no serial pass).  A split
+  // partial is O [32][64] followed by (m, l) [32][2] (kSplitStride floats).
   __nv_bfloat16* out = t.out;
   float* part = t.part;
   const long long ots = t.ots;
   for (int idx = threadIdx.x - 32; idx < kFusedRows * 16; idx += kFusedWorkers) {
     const int r = idx >> 4, d = (idx & 15) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float mb[4], lb[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const float w = cw[b * kFusedRows + r];
+      const float2 ml = *reinterpret_cast<const float2*>(cml + (b * kFusedRows + r) * 2);
+      mb[b] = ml.x;
+      lb[b] = ml.y;
+    }
+    const float M = fmaxf(fmaxf(mb[0], mb[1]), fmaxf(mb[2], mb[3]));
+    const float base = M == -INFINITY ? 0.f : M;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const float w = exp2f(mb[b] - base);
+      L += w * lb[b];
       const float4 ov = *reinterpret_cast<const float4*>(comb + (b * kFusedRows + r) * kCombRow + d);
       acc.x += w * ov.x;
       acc.y += w * ov.y;
@@ -1021,7 +1015,7 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
       acc.w += w * ov.w;
     }
     if (nsplit == 1) {
-      const float L = crow[r * 2 + 1], inv = L > 0.f ? 1.f / L : 0.f;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
       if (r < a.R) {
         uint2 pk;
         pk.x = pack_bf16(acc.x * inv, acc.y * inv);
@@ -1030,7 +1024,7 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
       }
     } else {
       *reinterpret_cast<float4*>(part + r * 64 + d) = acc;
-      if (d == 0) *reinterpret_cast<float2*>(part + kFusedRows * 64 + r * 2) = make_float2(crow[r * 2], crow[r * 2 + 1]);
+      if (d == 0) *reinterpret_cast<float2*>(part + kFusedRows * 64 + r * 2) = make_float2(M, L);
     }
   }
   if (nsplit == 1) {
@@ -1050,8 +1044,7 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
   bar_workers();
   if (tl->last) {
     // every split's partial -> shared memory in one cp.async group (L2 reads,
-    // kSplitStride floats each), then per (split, row) weights, then the
-    // output rows
+    // kSplitStride floats each), then the output rows
     float* sp_all = reinterpret_cast<float*>(stg);
     const float* part_head = t.part_head;
     const int nchunk = nsplit * kSplitStride / 4;
@@ -1060,32 +1053,31 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
     cp_async_commit();
     cp_async_wait<0>();
     bar_workers();
-    float* wts = sp_all + nsplit * kSplitStride;   // [nsplit][32], then 1 / L [32]
-    for (int r = threadIdx.x - 32; r < kFusedRows; r += kFusedWorkers) {
-      float M = -INFINITY;
-      for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2]);
-      const float base = M == -INFINITY ? 0.f : M;
-      float L = 0.f;
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float w = exp2f(sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2] - base);
-        wts[sp * kFusedRows + r] = w;
-        L += w * sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2 + 1];
-      }
-      wts[nsplit * kFusedRows + r] = L > 0.f ? 1.f / L : 0.f;
-    }
-    bar_workers();
+    // every output element: its row's split weights (recomputed per thread,
+    // no serial pass), then the weighted sum over the splits
     for (int idx = threadIdx.x - 32; idx < a.R * 16; idx += kFusedWorkers) {
       const int r = idx >> 4, d = (idx & 15) * 4;
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < kFusedMaxSplits; ++sp)
+        if (sp < nsplit) M = fmaxf(M, sp_all[sp * kSplitStride + kFusedRows * 64 + r * 2]);
+      const float base = M == -INFINITY ? 0.f : M;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float4 ov = *reinterpret_cast<const float4*>(sp_all + sp * kSplitStride + r * 64 + d);
-        const float w = wts[sp * kFusedRows + r];
-        acc.x += w * ov.x;
-        acc.y += w * ov.y;
-        acc.z += w * ov.z;
-        acc.w += w * ov.w;
+      float L = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < kFusedMaxSplits; ++sp) {
+        if (sp < nsplit) {
+          const float2 ml = *reinterpret_cast<const float2*>(sp_all + sp * kSplitStride + kFusedRows * 64 + r * 2);
+          const float w = exp2f(ml.x - base);
+          L += w * ml.y;
+          const float4 ov = *reinterpret_cast<const float4*>(sp_all + sp * kSplitStride + r * 64 + d);
+          acc.x += w * ov.x;
+          acc.y += w * ov.y;
+          acc.z += w * ov.z;
+          acc.w += w * ov.w;
+        }
       }
-      const float inv = wts[nsplit * kFusedRows + r];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
       uint2 pk;
       pk.x = pack_bf16(acc.x * inv, acc.y * inv);
       pk.y = pack_bf16(acc.z * inv, acc.w * inv);
