@@ -22,7 +22,8 @@ class ActionLayer(C.Structure):
 class ActionStacks(C.Structure):
     _fields_ = [(n, vp) for n in (
         "qkv_w", "o_w", "cq_w", "co_w", "ffn0_w", "ffn2_w", "qkv_b", "o_b", "cq_b", "co_b",
-        "ffn0_b", "ffn2_b", "norm_q", "norm_k", "cnorm_q", "norm3_w", "norm3_b", "modulation")]
+        "ffn0_b", "ffn2_b", "norm_q", "norm_k", "cnorm_q", "norm3_w", "norm3_b", "modulation",
+        "ckv_w", "ckv_b", "cnorm_k")]
 
 
 class ActionWeights(C.Structure):

@@ -228,21 +228,45 @@ int enqueue_prologue(const Ctx& c, const float* timesteps, int N) {
                     kActGeluTanh, wsp<void>(c, c.L.ch1), D, false));
     FAM_TRYI(gemm_w(c, w.text2_w, w.text2_b, D, D, wsp<void>(c, c.L.ch1), D, c.crow, 1, kActNone,
                     wsp<void>(c, c.L.cemb), D, false));
-    for (int l = 0; l < g.num_layers; ++l) {
-      const fam_action_layer& ly = c.e->layers[l];
-      __nv_bfloat16* ckv = wsp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.crow * 2 * HD;
-      FAM_TRYI(gemm_w(c, ly.ckv_w, ly.ckv_b, 2 * HD, D, wsp<void>(c, c.L.cemb), D, c.crow, 1,
-                      kActNone, ckv, 2 * HD, false));
+    // Cross K / V of every block, context-token major: ckv[row][l * 2HD + (K | V)]
+    // (row = b * C + t); the K half RMSNorm'd with block l's norm_k.
+    const int L = g.num_layers;
+    const long long ld = static_cast<long long>(L) * 2 * HD;
+    __nv_bfloat16* ckv_all = wsp<__nv_bfloat16>(c, c.L.ckv);
+    const fam_action_stacks& s = c.e->stacks;
+    if (c.e->has_stacks && s.ckv_w != nullptr && s.ckv_b != nullptr && s.cnorm_k != nullptr) {
+      // one GEMM over the stacked projections, one RMSNorm launch over (row, block)
+      FAM_TRYI(gemm_w(c, s.ckv_w, s.ckv_b, L * 2 * HD, D, wsp<void>(c, c.L.cemb), D, c.crow, 1,
+                      kActNone, ckv_all, ld, false));
       RmsRowsArgs r = {};
       r.nsplit = 0;
-      r.in = ckv;
-      r.in_stride = 2 * HD;
-      r.w = bf(ly.cnorm_k);
-      r.out = ckv;
+      r.in = ckv_all;
+      r.in_stride = 2 * HD;  // (row, block) slice rr = row * L + l starts at rr * 2HD
+      r.w = bf(s.cnorm_k);
+      r.w_period = L;
+      r.w_stride = HD;
+      r.out = ckv_all;
       r.out_stride = 2 * HD;
       r.N = HD;
       r.eps = g.eps;
-      FAM_LAUNCH(launch_rms_rows(r, c.crow, c.st, c.pdl));
+      FAM_LAUNCH(launch_rms_rows(r, c.crow * L, c.st, c.pdl));
+    } else {
+      for (int l = 0; l < L; ++l) {
+        const fam_action_layer& ly = c.e->layers[l];
+        __nv_bfloat16* ckv = ckv_all + static_cast<size_t>(l) * 2 * HD;
+        FAM_TRYI(gemm_w(c, ly.ckv_w, ly.ckv_b, 2 * HD, D, wsp<void>(c, c.L.cemb), D, c.crow, 1,
+                        kActNone, ckv, ld, false));
+        RmsRowsArgs r = {};
+        r.nsplit = 0;
+        r.in = ckv;
+        r.in_stride = ld;
+        r.w = bf(ly.cnorm_k);
+        r.out = ckv;
+        r.out_stride = ld;
+        r.N = HD;
+        r.eps = g.eps;
+        FAM_LAUNCH(launch_rms_rows(r, c.crow, c.st, c.pdl));
+      }
     }
   }
   return 0;
@@ -366,11 +390,13 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       ca.q = rq.out;
       ca.q_bs = static_cast<long long>(Sa) * HD;
       ca.q_ts = HD;
-      const __nv_bfloat16* ckv = wsp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.crow * 2 * HD;
+      // context-token-major cross K / V of every block (prologue layout)
+      const long long cld = static_cast<long long>(g.num_layers) * 2 * HD;
+      const __nv_bfloat16* ckv = wsp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * 2 * HD;
       ca.k1 = ckv;
       ca.v1 = ckv + HD;
-      ca.kv1_bs = static_cast<long long>(io.context_tokens) * 2 * HD;
-      ca.kv1_ts = 2 * HD;
+      ca.kv1_bs = static_cast<long long>(io.context_tokens) * cld;
+      ca.kv1_ts = cld;
       ca.S1 = io.context_tokens;
       ca.key_mask = io.context_mask;
       ca.key_mask_bs = io.context_tokens;

@@ -1133,11 +1133,11 @@ __device__ AttnItem joint_item(const FusedArgs& a, int step, int l, int i) {
 
 __device__ AttnItem cross_item(const FusedArgs& a, int step, int l, int h) {
   const float* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
-  const __nv_bfloat16* kv = a.ckv + static_cast<long long>(l) * a.C * 2 * a.HD;
+  const __nv_bfloat16* kv = a.ckv + static_cast<long long>(l) * 2 * a.HD;  // [C][L][2HD]
   AttnItem t;
   t.k1 = kv + h * a.hd;
   t.v1 = kv + a.HD + h * a.hd;
-  t.ts1 = 2 * a.HD;
+  t.ts1 = static_cast<long long>(a.L) * 2 * a.HD;
   t.S1 = a.C;
   t.k2 = nullptr;
   t.v2 = nullptr;

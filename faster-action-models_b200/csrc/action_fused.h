@@ -35,7 +35,7 @@ struct FusedArgs {
   long long v_ts;                    // cache token stride (elements)
   int Sv;
   const uint8_t* mask2d;             // [Sa, Sv + Sa] or null
-  const __nv_bfloat16* ckv;          // [L, C, 2HD]: RMSNorm'd K then V per context token
+  const __nv_bfloat16* ckv;          // [C, L, 2HD]: RMSNorm'd K then V per context token and block
   const uint8_t* ctx_mask;           // [C] or null
   int C;
   // workspace

@@ -79,6 +79,8 @@ struct RmsRowsArgs {
   long long out_stride;
   int N;
   float eps;
+  int w_period;        // > 0: row r uses the weight vector w + (r % w_period) * w_stride
+  long long w_stride;
 };
 
 struct EncodeArgs {

@@ -261,10 +261,11 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const RmsRowsArgs
     ss += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
   }
   const float r = rsqrtf(block_sum(ss, red) / a.N + a.eps);
+  const __nv_bfloat16* wr = a.w + (a.w_period > 0 ? static_cast<long long>(row % a.w_period) * a.w_stride : 0);
   for (int g = threadIdx.x; g < a.N / 4; g += blockDim.x) {
     const int f = 4 * g;
     const float4 y = *reinterpret_cast<const float4*>(sbuf + f);
-    const float4 w = ld_bf4(a.w + f);
+    const float4 w = ld_bf4(wr + f);
     st_bf4(a.out + static_cast<long long>(row) * a.out_stride + f,
            make_float4(rbf(y.x * r) * w.x, rbf(y.y * r) * w.y, rbf(y.z * r) * w.z, rbf(y.w * r) * w.w));
   }

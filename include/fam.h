@@ -207,6 +207,11 @@ typedef struct fam_action_stacks {
   const void *norm_q, *norm_k, *cnorm_q;                     /* [L*HD] */
   const void *norm3_w, *norm3_b;                             /* [L*D] */
   const void *modulation;                                    /* [L*6*D] */
+  /* optional (NULL: per-block prologue launches): cross-attention K/V
+   * projection and k RMSNorm weight stacked over the blocks, for one batched
+   * context K/V GEMM per chunk */
+  const void *ckv_w, *ckv_b;                                 /* [L*2HD, D], [L*2HD] */
+  const void *cnorm_k;                                       /* [L*HD] */
 } fam_action_stacks;
 
 typedef struct fam_action_weights {
