@@ -60,7 +60,9 @@ constexpr int kStgLnConst = kStgRope + 4 * kFusedRows * 16 * 8;
 // pair items: the peer's partial accumulators of this CTA's output rows,
 // [32 tokens][64 rows] fp32, behind the half-width B operand (<= 8 K blocks)
 constexpr int kStgXacc = 8 * kBBlock;
-static_assert(kStgXacc + kFusedRows * 64 * 4 <= kStgRope, "pair exchange buffer");
+constexpr int kStgXsend = kStgXacc + kFusedRows * 64 * 4;  // this CTA's outgoing partials
+constexpr uint32_t kXaccBytes = kFusedRows * 64 * 4;
+static_assert(kStgXsend + kXaccBytes <= kStgRope, "pair exchange buffers");
 static_assert(kStgLnConst + 2 * 1024 * 4 <= kFusedStaging, "staging layout");
 
 struct FusedSmemTail {
@@ -74,10 +76,13 @@ struct FusedSmemTail {
   int last;
   // pair items: the peer CTA writes its half-row LayerNorm sums here and
   // arrives on xstat_bar (one arrival per worker warp); its partial
-  // accumulators go to the staging (kStgXacc) with arrivals on xacc_bar
+  // accumulators arrive in the staging (kStgXacc) by one bulk copy that
+  // completes on xacc_bar (armed here with the expected bytes); xsend_bar
+  // gathers this CTA's four sending warps before it issues its own copy
   alignas(16) float xstat[kFusedRows][2];  // 8-byte (v2) remote stores and loads
   uint64_t xstat_bar;
   uint64_t xacc_bar;
+  uint64_t xsend_bar;
 };
 
 static_assert(offsetof(FusedSmemTail, xstat) % 8 == 0, "xstat rows are accessed as float2");
@@ -642,6 +647,8 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
   }
   fence_async_smem();
   bar_workers();
+  // pair: expect the peer's partial accumulators (8 KB bulk copy) on xacc_bar
+  if (pair && threadIdx.x == 32) mbar_arrive_expect_tx(&tl->xacc_bar, kXaccBytes);
   // 2. MMA: kFusedIssuers issuing threads (lane 0 of warps 1, 6, 7, 8; issuer
   // j takes the K blocks k = j mod kFusedIssuers) into separate TMEM
   // accumulators summed by the epilogue.  A single thread's tcgen05.mma issue
@@ -700,15 +707,28 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
       }
     }
     if (pair) {
-      float* xacc = reinterpret_cast<float*>(stg + kStgXacc);  // [token][64]
       const int fl = (q & 1) * 32 + lane;
       if (!keep) {
-        // partial sums of the peer's rows -> the peer's staging, then arrive
-        const uint32_t dst = cluster_map(xacc, half ^ 1);
+        // partial sums of the peer's rows -> this CTA's send buffer; the
+        // first sending warp then moves all 8 KB to the peer in one bulk copy
+        float* xsend = reinterpret_cast<float*>(stg + kStgXsend);  // [token][64]
 #pragma unroll
-        for (int jj = 0; jj < kEpiTokens; ++jj) st_cluster_f32(dst + ((t0 + jj) * 64 + fl) * 4, v[jj]);
-        mbar_arrive_cluster(cluster_map(&tl->xacc_bar, half ^ 1));
+        for (int jj = 0; jj < kEpiTokens; ++jj) xsend[(t0 + jj) * 64 + fl] = v[jj];
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tl->xsend_bar);
+        const int first_give = half == 0 ? 2 : 4;  // lowest warp of the sending quarters
+        if (warp == first_give && lane == 0) {
+          if (!mbar_wait(&tl->xsend_bar, pparity, a.status, kErrWaitAccum)) {
+            tl->abort = 1;
+          } else {
+            bulk_copy_to_peer(cluster_map(stg + kStgXacc, half ^ 1), xsend, kXaccBytes,
+                              cluster_map(&tl->xacc_bar, half ^ 1));
+            bulk_wait_read();  // the send buffer is reused by the next pair item
+          }
+        }
       } else {
+        const float* xacc = reinterpret_cast<const float*>(stg + kStgXacc);  // [token][64]
         if (!mbar_wait_cl(a, &tl->xacc_bar, pparity, kErrWaitAccum)) tl->abort = 1;
 #pragma unroll
         for (int jj = 0; jj < kEpiTokens; ++jj) v[jj] += xacc[(t0 + jj) * 64 + fl];
@@ -1179,7 +1199,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     }
     mbar_init(&tl->accum, kFusedIssuers);
     mbar_init(&tl->xstat_bar, kFusedWorkers / 32);  // one arrival per peer worker warp
-    mbar_init(&tl->xacc_bar, 4 * 32);               // every lane of the peer's 4 sending warps
+    mbar_init(&tl->xacc_bar, 1);                    // own expect_tx arrival + the peer's bulk copy
+    mbar_init(&tl->xsend_bar, 4);                   // lane 0 of this CTA's 4 sending warps
     tl->abort = 0;
     fence_mbar_init();
     for (int p = 0; p < 6; ++p) tma_prefetch_desc(&a.tm[p]);
