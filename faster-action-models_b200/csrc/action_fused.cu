@@ -311,12 +311,23 @@ __device__ void ln_const_prefetch(const FusedArgs& a, uint8_t* stg, int step, in
       ld_bf8(a.norm3_w + static_cast<long long>(l) * D + f0, m);
       ld_bf8(a.norm3_b + static_cast<long long>(l) * D + f0, ad);
     }
-    float* cm = reinterpret_cast<float*>(stg + kStgLnConst) + f0;
-    float* ca = cm + D;
-    reinterpret_cast<float4*>(cm)[0] = make_float4(m[0], m[1], m[2], m[3]);
-    reinterpret_cast<float4*>(cm)[1] = make_float4(m[4], m[5], m[6], m[7]);
-    reinterpret_cast<float4*>(ca)[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
-    reinterpret_cast<float4*>(ca)[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+    if (mode == 0) {
+      // AdaLN: bf16 (1 + scale) and shift pairs, [D / 2] bf16x2 each (the
+      // reference's modulate works on bf16 tensors; the staging applies them
+      // with one packed bf16 FMA per pair)
+      uint4* cm = reinterpret_cast<uint4*>(stg + kStgLnConst) + ch;
+      uint4* ca = reinterpret_cast<uint4*>(stg + kStgLnConst) + D / 8 + ch;
+      *cm = make_uint4(pack_bf16(m[0], m[1]), pack_bf16(m[2], m[3]), pack_bf16(m[4], m[5]), pack_bf16(m[6], m[7]));
+      *ca = make_uint4(pack_bf16(ad[0], ad[1]), pack_bf16(ad[2], ad[3]), pack_bf16(ad[4], ad[5]),
+                       pack_bf16(ad[6], ad[7]));
+    } else {
+      float* cm = reinterpret_cast<float*>(stg + kStgLnConst) + f0;
+      float* ca = cm + D;
+      reinterpret_cast<float4*>(cm)[0] = make_float4(m[0], m[1], m[2], m[3]);
+      reinterpret_cast<float4*>(cm)[1] = make_float4(m[4], m[5], m[6], m[7]);
+      reinterpret_cast<float4*>(ca)[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+      reinterpret_cast<float4*>(ca)[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+    }
   }
 }
 
@@ -431,26 +442,57 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
   stats(ca, s[0] + pa.x, s[1] + pa.y, r0, ra, ba);
   stats(cb, s[2] + pb.x, s[3] + pb.y, r1, rb, bb);
   stats(cc, s[4] + pc.x, s[5] + pc.y, has2 ? r2 : kFusedRows, rc, bc);
-  const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst) + half * (DH / 4);
-  const float4* cadd = reinterpret_cast<const float4*>(stg + kStgLnConst) + D / 4 + half * (DH / 4);
+  if (mode == 0) {
+    // AdaLN: bf16(n) * bf16(1 + scale) + bf16(shift), one packed bf16 FMA per pair
+    const uint4* cm = reinterpret_cast<const uint4*>(stg + kStgLnConst) + half * (DH / 8);
+    const uint4* cadd = reinterpret_cast<const uint4*>(stg + kStgLnConst) + D / 8 + half * (DH / 8);
 #pragma unroll
-  for (int u = 0; u < NCH; ++u) {
-    const int ch = lane + 32 * u;  // chunk within this half: local K block ch >> 3
-    const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = cadd[2 * ch], a1 = cadd[2 * ch + 1];
-    const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    float oa[8], ob[8], oc[8];
+    for (int u = 0; u < NCH; ++u) {
+      const int ch = lane + 32 * u;  // chunk within this half: local K block ch >> 3
+      const uint4 m4 = cm[ch], a4 = cadd[ch];
+      const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w}, aw[4] = {a4.x, a4.y, a4.z, a4.w};
+      uint32_t oa[4], ob[4], oc[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float na = fmaf(xa[u * 8 + e], ra, ba), nb = fmaf(xb[u * 8 + e], rb, bb);
-      const float nc = fmaf(xc[u * 8 + e], rc, bc);
-      oa[e] = mode == 0 ? rbf(na) * mv[e] + av[e] : na * mv[e] + av[e];
-      ob[e] = mode == 0 ? rbf(nb) * mv[e] + av[e] : nb * mv[e] + av[e];
-      oc[e] = mode == 0 ? rbf(nc) * mv[e] + av[e] : nc * mv[e] + av[e];
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 mv = *reinterpret_cast<const __nv_bfloat162*>(&mw[e]);
+        const __nv_bfloat162 av = *reinterpret_cast<const __nv_bfloat162*>(&aw[e]);
+        const int i0 = u * 8 + 2 * e;
+        __nv_bfloat162 na = __floats2bfloat162_rn(fmaf(xa[i0], ra, ba), fmaf(xa[i0 + 1], ra, ba));
+        __nv_bfloat162 nb = __floats2bfloat162_rn(fmaf(xb[i0], rb, bb), fmaf(xb[i0 + 1], rb, bb));
+        __nv_bfloat162 nc = __floats2bfloat162_rn(fmaf(xc[i0], rc, bc), fmaf(xc[i0 + 1], rc, bc));
+        na = __hfma2(na, mv, av);
+        nb = __hfma2(nb, mv, av);
+        nc = __hfma2(nc, mv, av);
+        oa[e] = *reinterpret_cast<uint32_t*>(&na);
+        ob[e] = *reinterpret_cast<uint32_t*>(&nb);
+        oc[e] = *reinterpret_cast<uint32_t*>(&nc);
+      }
+      stage_chunk(stg, ch >> 3, r0, ch & 7, r0 < a.R ? make_uint4(oa[0], oa[1], oa[2], oa[3]) : make_uint4(0, 0, 0, 0));
+      stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? make_uint4(ob[0], ob[1], ob[2], ob[3]) : make_uint4(0, 0, 0, 0));
+      if (has2)
+        stage_chunk(stg, ch >> 3, r2, ch & 7, r2 < a.R ? make_uint4(oc[0], oc[1], oc[2], oc[3]) : make_uint4(0, 0, 0, 0));
     }
-    stage_chunk(stg, ch >> 3, r0, ch & 7, r0 < a.R ? pack8(oa) : make_uint4(0, 0, 0, 0));
-    stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? pack8(ob) : make_uint4(0, 0, 0, 0));
-    if (has2) stage_chunk(stg, ch >> 3, r2, ch & 7, r2 < a.R ? pack8(oc) : make_uint4(0, 0, 0, 0));
+  } else {
+    // affine norm3 (fp32 weight and bias, one rounding at the store)
+    const float4* cm = reinterpret_cast<const float4*>(stg + kStgLnConst) + half * (DH / 4);
+    const float4* cadd = reinterpret_cast<const float4*>(stg + kStgLnConst) + D / 4 + half * (DH / 4);
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int ch = lane + 32 * u;
+      const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = cadd[2 * ch], a1 = cadd[2 * ch + 1];
+      const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float oa[8], ob[8], oc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        oa[e] = fmaf(xa[u * 8 + e], ra, ba) * mv[e] + av[e];
+        ob[e] = fmaf(xb[u * 8 + e], rb, bb) * mv[e] + av[e];
+        oc[e] = fmaf(xc[u * 8 + e], rc, bc) * mv[e] + av[e];
+      }
+      stage_chunk(stg, ch >> 3, r0, ch & 7, r0 < a.R ? pack8(oa) : make_uint4(0, 0, 0, 0));
+      stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? pack8(ob) : make_uint4(0, 0, 0, 0));
+      if (has2) stage_chunk(stg, ch >> 3, r2, ch & 7, r2 < a.R ? pack8(oc) : make_uint4(0, 0, 0, 0));
+    }
   }
   return true;
 }
