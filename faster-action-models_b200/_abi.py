@@ -68,6 +68,8 @@ def declare_counts(lib) -> None:
     lib.fam_action_set_mode.restype = C.c_int
     lib.fam_action_last_path.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
     lib.fam_action_last_path.restype = C.c_int
+    lib.fam_selftest_bounded_wait.argtypes = [C.c_void_p]
+    lib.fam_selftest_bounded_wait.restype = C.c_int
     lib.fam_action_set_kernel_events.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
     lib.fam_action_set_kernel_events.restype = C.c_int
 

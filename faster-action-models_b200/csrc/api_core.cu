@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "../../include/fam.h"
+#include "fam_common.cuh"
 #include "fam_internal.h"
 
 namespace fam {
@@ -107,6 +108,27 @@ int fam_device_status(int* code, int reset, void* stream) {
   }
   if (code) *code = v;
   return FAM_OK;
+}
+
+namespace fam {
+// One thread waits on an mbarrier that nothing will complete: the bounded wait
+// gives up after its %globaltimer limit, records kErrWaitFull in the status
+// word and the kernel returns normally.
+__global__ void selftest_wait_kernel(int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, status, kErrWaitFull);
+  }
+}
+}  // namespace fam
+
+int fam_selftest_bounded_wait(void* stream) {
+  int* w = device_status_word();
+  if (w == nullptr) return set_error("fam_selftest_bounded_wait: no device status word");
+  fam::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(w);
+  return check_cuda(cudaGetLastError(), "fam_selftest_bounded_wait launch");
 }
 
 int fam_gemm(const fam_gemm_desc* d, void* stream) {

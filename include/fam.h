@@ -63,6 +63,13 @@ FAM_API int fam_last_error(char* buf, size_t len);
  * Synchronizes `stream`.  reset != 0 clears the word afterwards. */
 FAM_API int fam_device_status(int* code, int reset, void* stream);
 
+/* Self-test of the failure path (no counterpart in the reference): launches
+ * one thread that waits on an mbarrier nothing completes.  The wait gives up
+ * after its 1 s %globaltimer limit, records code 1 (a consumer wait expired)
+ * in the device status word and the kernel returns: no fault, the context
+ * stays usable.  Read the outcome with fam_device_status after the stream. */
+FAM_API int fam_selftest_bounded_wait(void* stream);
+
 /* D[m][n] = sum_k A[m][k] * B[n][k]  on the tcgen05 tensor cores.
  * A: bf16 [m, k] row stride lda; B: bf16 [n, k] row stride ldb (both K-major,
  * 16-byte aligned, k and strides multiples of 8).  The output element for
