@@ -202,18 +202,21 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// The flag is re-read back to back; the abort word and the clock are checked
+// every 16th read only, so a poll iteration is one L2 round trip.
 __device__ __forceinline__ bool poll_ge(const FusedArgs& a, const unsigned* p, unsigned target,
                                         FusedSmemTail* tl) {
+  if (ld_acquire(p) >= target) return true;
   const unsigned long long t0 = globaltimer_ns();
-  while (ld_acquire(p) < target) {
-    if (ld_acquire(a.sync + 1) != 0 || globaltimer_ns() - t0 > kWaitLimitNs) {
+  for (unsigned it = 1;; ++it) {
+    if (ld_acquire(p) >= target) return true;
+    if ((it & 15) == 0 && (ld_acquire(a.sync + 1) != 0 || globaltimer_ns() - t0 > kWaitLimitNs)) {
       if (ld_acquire(a.sync + 1) == 0) record_error(a.status, kErrWaitFull);
       atomicExch(a.sync + 1, 1u);
       tl->abort = 1;
       return false;
     }
   }
-  return true;
 }
 
 __device__ __forceinline__ bool grid_sync(const FusedArgs& a, unsigned& epoch, FusedSmemTail* tl) {
