@@ -393,6 +393,8 @@ cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_cae_steps(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
+  CaeStepArgs staged = a;
+  if (cae_staged_plan(a, &staged.plan)) return launch_cae_steps_staged(staged, st, pdl);
   const size_t smem = sizeof(CaeSmem);
   cudaError_t e = cudaFuncSetAttribute(cae_steps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));

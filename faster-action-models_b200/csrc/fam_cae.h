@@ -37,8 +37,27 @@ struct CaeCtxArgs {
   float eps;
 };
 
+// Shared-memory plan of the staged step kernel (offsets in floats from the
+// dynamic shared-memory base; computed on the host by cae_staged_plan).
+constexpr int kCaeStagedTensors = 18;  // per-block tensors: 0..13 attention half, 14..17 FFN half
+constexpr int kCaeStagedHalfSplit = 14;
+struct CaeStagePlan {
+  int off[kCaeStagedTensors];      // offset inside its half
+  int rows[kCaeStagedTensors], cols[kCaeStagedTensors], stride[kCaeStagedTensors];
+  int a_floats, f_floats, kv_floats;
+  int kc;                          // context keys per K/V unit
+  int units_per_head;
+  int wpq;                         // warps per query row in cross attention
+  int tb;                          // t_mod rows per time-MLP batch
+  int hdp;                         // row stride of the q/k/v/attention rows
+  int o_abuf, o_fbuf, o_kv, o_x, o_h, o_q, o_k, o_v, o_att, o_qc, o_f, o_part, o_tm, o_tscr, o_lat,
+      o_rope, o_encw, o_encb, o_headw, o_headb;
+  int total_floats;
+};
+
 struct CaeStepArgs {
   CaeWeightsDev w;
+  CaeStagePlan plan;
   const float* rope;               // [positions, hd/2, 2]
   const float* ctx_k;              // [L, B*C, HD]
   const float* ctx_v;
@@ -55,6 +74,10 @@ struct CaeStepArgs {
 cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_cae_steps(const CaeStepArgs& a, cudaStream_t st, bool pdl);
 size_t cae_smem_bytes();
+// Staged step kernel (weights and context K/V streamed through shared memory).
+// Returns false when the shapes or pointers do not fit it; the plan is then unset.
+bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* plan);
+cudaError_t launch_cae_steps_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl);
 
 // ------------------------------------------------------------ action decoder
 constexpr int kDecMaxStages = 4;

@@ -89,3 +89,50 @@ def test_decoder_strides_and_suites(horizon, tokens, hidden, suites):
     got = ae.cuda().decode(z.cuda(), sid.cuda() if sid is not None else None)
     torch.cuda.synchronize()
     _close(got, ref)
+
+
+# (hidden, heads, head_dim, ffn, layers, tokens S, context C, batch, steps, masked)
+# covers: several key chunks per head with a ragged last chunk (C=600), query rows
+# that do not divide the 32 warps (S=6), head_dim 4/8/16, odd depth, a single
+# block, more Euler steps than one t_mod batch (10), per-sample context masks,
+# and a width that falls back to the unstaged kernel (hidden 64, ffn 256).
+CAE_SHAPES = [
+    (32, 4, 8, 128, 3, 6, 600, 2, 10, True),
+    (16, 4, 4, 64, 1, 8, 16, 3, 5, True),
+    (32, 2, 16, 64, 2, 32, 77, 1, 3, False),
+    (64, 4, 16, 256, 2, 8, 40, 2, 2, True),
+]
+
+
+@pytest.mark.parametrize("D,H,hd,F,L,S,C,B,N,masked", CAE_SHAPES)
+def test_cae_shapes_vs_oracle(D, H, hd, F, L, S, C, B, N, masked):
+    torch.manual_seed(D * 7 + L)
+    T, A = 64, 16
+    dit = M.ActionDiT(hidden_dim=D, action_dim=A, ffn_dim=F, text_dim=T, freq_dim=256, eps=1e-6,
+                      num_heads=H, attn_head_dim=hd, num_layers=L)
+    with torch.no_grad():
+        for p in dit.parameters():
+            p.add_(0.05 * torch.randn_like(p))  # non-zero AdaLN modulation / gates
+    assert dit.is_compact()
+    cfg = O.DiTConfig(hidden_dim=D, ffn_dim=F, num_heads=H, attn_head_dim=hd, num_layers=L,
+                      text_dim=T, action_dim=A)
+    g = torch.Generator().manual_seed(C + S)
+    ctx = torch.randn(B, C, T, generator=g)
+    noise = torch.randn(B, S, A, generator=g)
+    mask = None
+    if masked:
+        mask = torch.rand(B, C, generator=g) > 0.3
+        mask[:, 0] = True  # no fully masked sample (the reference softmax is undefined there)
+    sd = {k: v.float() for k, v in dit.state_dict().items()}
+    ts, ds = O.build_inference_schedule(N, 3.0, dtype=torch.float32)
+    x, vel = noise.clone(), []
+    for t, d in zip(ts, ds):
+        v = O.action_forward(sd, cfg, x, t.reshape(1), ctx, mask)
+        vel.append(v)
+        x = O.scheduler_step(v, d, x)
+    lat, trace = dit.cuda().engine().chunk(noise.cuda(), ts.tolist(), ds.tolist(), ctx.cuda(),
+                                           mask.cuda() if mask is not None else None,
+                                           return_trace=True)
+    torch.cuda.synchronize()
+    _close(trace, torch.stack(vel))
+    _close(lat, x)
