@@ -95,9 +95,6 @@ size_t fused_smem_bytes() { return fused_tail_offset() + sizeof(FusedSmemTail) +
 __device__ __forceinline__ void bar_workers() {
   asm volatile("barrier.sync 1, %0;" ::"r"(kFusedWorkers) : "memory");
 }
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -11,10 +11,28 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-size_t cae_ws(const fam_action_config& c, int B, int C) {
-  const size_t kv = static_cast<size_t>(c.num_layers) * B * C * c.num_heads * c.head_dim * sizeof(float);
-  return 2 * align256(kv);
+// Workspace: context K | context V | slice partial sums | packed block weights | status word.
+struct CaeWsLayout {
+  size_t k, v, part, wpack, status, total;
+};
+
+CaeWsLayout cae_ws_layout(const fam_action_config& c, int B, int C) {
+  CaeWsLayout w;
+  // rows of H*d + 8 floats cover both the plain and the padded (staged) layouts
+  const size_t kv = align256(static_cast<size_t>(c.num_layers) * B * C * (c.num_heads * c.head_dim + 8) * sizeof(float));
+  CaeStagePlan p;
+  memset(&p, 0, sizeof(p));
+  cae_tensor_table(c.hidden_dim, c.num_heads * c.head_dim, c.ffn_dim, &p);
+  w.k = 0;
+  w.v = kv;
+  w.part = 2 * kv;
+  w.wpack = w.part + align256(static_cast<size_t>(kCaeCtxSlices) * B * C * c.hidden_dim * sizeof(float));
+  w.status = w.wpack + align256(static_cast<size_t>(c.num_layers) * (p.a_floats + p.f_floats) * sizeof(float));
+  w.total = w.status + 256;
+  return w;
 }
+
+size_t cae_ws(const fam_action_config& c, int B, int C) { return cae_ws_layout(c, B, C).total; }
 
 int check_cae(const fam_action_config* c) {
   if (c == nullptr) return set_error("cae: null config");
@@ -58,9 +76,12 @@ int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_
   if (workspace == nullptr || workspace_bytes < need)
     return set_error("cae: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   const int HD = cfg->num_heads * cfg->head_dim;
-  const size_t kv_bytes = align256(static_cast<size_t>(cfg->num_layers) * batch * context_tokens * HD * sizeof(float));
-  float* ctx_k = static_cast<float*>(workspace);
-  float* ctx_v = reinterpret_cast<float*>(static_cast<char*>(workspace) + kv_bytes);
+  const CaeWsLayout wl = cae_ws_layout(*cfg, batch, context_tokens);
+  char* ws = static_cast<char*>(workspace);
+  float* ctx_k = reinterpret_cast<float*>(ws + wl.k);
+  float* ctx_v = reinterpret_cast<float*>(ws + wl.v);
+  float* wpack = reinterpret_cast<float*>(ws + wl.wpack);
+  int* status = reinterpret_cast<int*>(ws + wl.status);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   CaeCtxArgs ca;
@@ -82,8 +103,12 @@ int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_
   ca.ctx_k = ctx_k;
   ca.ctx_v = ctx_v;
   ca.eps = cfg->eps;
-  rc = check_cuda(launch_cae_context(ca, st, false), "cae context launch");
-  if (rc) return rc;
+  ca.B = batch;
+  ca.C = context_tokens;
+  ca.H = cfg->num_heads;
+  ca.hd = cfg->head_dim;
+  ca.part = reinterpret_cast<float*>(ws + wl.part);
+  ca.status = status;
 
   CaeStepArgs sa;
   memset(&sa, 0, sizeof(sa));
@@ -124,7 +149,33 @@ int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_
   sa.L = cfg->num_layers;
   sa.freq_dim = cfg->freq_dim;
   sa.eps = cfg->eps;
+  sa.status = status;
+  // staged step kernel when the split context path and the shared-memory plan
+  // both fit: the context launch then writes head-major K/V and packs weights
+  if (cae_ctx_split_setup(&ca) && cae_staged_plan(sa, &sa.plan)) {
+    ca.kv_packed = 1;
+    ca.wpack = wpack;
+    ca.plan = sa.plan;
+    sa.wpack = wpack;
+  }
+  rc = check_cuda(launch_cae_context(ca, st, false), "cae context launch");
+  if (rc) return rc;
   return check_cuda(launch_cae_steps(sa, st, true), "cae steps launch");
+}
+
+int fam_cae_status(const fam_action_config* cfg, int32_t batch, int32_t context_tokens, const void* workspace,
+                   int32_t* status, void* stream) {
+  int rc = check_cae(cfg);
+  if (rc) return rc;
+  if (workspace == nullptr || status == nullptr || batch <= 0 || context_tokens <= 0)
+    return set_error("cae: bad status arguments");
+  const CaeWsLayout wl = cae_ws_layout(*cfg, batch, context_tokens);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = check_cuda(cudaMemcpyAsync(status, static_cast<const char*>(workspace) + wl.status, sizeof(int32_t),
+                                  cudaMemcpyDeviceToHost, st),
+                  "cae status copy");
+  if (rc) return rc;
+  return check_cuda(cudaStreamSynchronize(st), "cae status sync");
 }
 
 int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_decoder_weights* w,

@@ -1,20 +1,21 @@
-// Compact Action Expert (hidden width <= 64): the whole Euler loop in one
-// persistent launch.  BASELINE config 0 (hidden 32, 4 heads x 8, 8 blocks,
-// 512-token context, 4 Euler steps) is launch-bound: every tensor of a step is
-// a few KB, so one CTA per sample keeps the token states in shared memory for
-// all steps x blocks and reads the (L2-resident) weights directly; the context
-// side is one multi-CTA launch before it.
+// Compact Action Expert (hidden width <= 64): the context side and the
+// unstaged Euler loop.  BASELINE config 0 (hidden 32, 4 heads x 8, 8 blocks,
+// 512-token context, 4 Euler steps) is launch- and latency-bound.
 //
-//   cae_context_kernel   text_embedding (Linear -> GELU(tanh) -> Linear) of every
-//                        context token and, per block, the cross-attention K
-//                        (RMSNorm over H*d) and V.  fp32, CUDA cores; each CTA
-//                        owns 4 context tokens.
-//   cae_steps_kernel     per sample: for every Euler step the time MLP
-//                        (sinusoid -> Linear -> SiLU -> Linear -> SiLU -> Linear
-//                        (6D)), action_encoder, every DiT block (AdaLN, q/k/v +
-//                        RMSNorm + RoPE, self attention, gated o-proj, norm3 +
-//                        cross attention, AdaLN FFN with GELU(tanh), gate), head,
-//                        and the Euler update x += v * delta.
+//   cae_ctx_slice_kernel  text_embedding.0 partial sums: CTA per (16 context
+//                         tokens, 1/8 of the text columns), both tiles brought
+//                         in by bulk copies; fp32 FMA.
+//   cae_ctx_kv_kernel     CTA per (16 context tokens, block): reduce the slices,
+//                         GELU(tanh), text_embedding.2, the block's cross K
+//                         (RMSNorm over H*d) and V, written [L, rows, H*d]
+//                         (rows padded to H*d + 4 / + 8 for the staged step
+//                         kernel); also packs the block's weights into the
+//                         staged kernel's shared-memory layout.
+//   cae_context_kernel    single-kernel context side (4 tokens per CTA) for
+//                         shapes the split path does not take.
+//   cae_steps_kernel      unstaged Euler loop (one CTA per sample, weights read
+//                         from L2) for shapes the staged kernel does not take;
+//                         the staged kernel lives in cae_staged.cu.
 //
 // Reference (FastWAM/src/fastwam/models/wan22/...): ActionDiT.prepare/forward
 // (action_dit.py:312-362), DiTBlock.forward (wan_video_dit.py:248-267),
@@ -23,6 +24,8 @@
 // the reference's fp32 CAE configuration.
 #include "fam_common.cuh"
 #include "fam_cae.h"
+
+#include <type_traits>
 
 namespace fam {
 
@@ -374,7 +377,248 @@ __global__ void __launch_bounds__(kCaeThreads) cae_steps_kernel(const __grid_con
   for (int i = threadIdx.x; i < S * A; i += blockDim.x) latent[i] = sm.lat[i];
 }
 
+
+// -------------------------------------------------------- split context path
+constexpr int kCtxThreads = 256;
+
+__device__ __forceinline__ const float* cae_layer_tensor(const CaeLayer& ly, int t) {
+  switch (t) {
+    case 0: return ly.modulation;
+    case 1: return ly.qkv_w;
+    case 2: return ly.qkv_b;
+    case 3: return ly.norm_q;
+    case 4: return ly.norm_k;
+    case 5: return ly.o_w;
+    case 6: return ly.o_b;
+    case 7: return ly.norm3_w;
+    case 8: return ly.norm3_b;
+    case 9: return ly.cq_w;
+    case 10: return ly.cq_b;
+    case 11: return ly.cnorm_q;
+    case 12: return ly.co_w;
+    case 13: return ly.co_b;
+    case 14: return ly.ffn0_w;
+    case 15: return ly.ffn0_b;
+    case 16: return ly.ffn2_w;
+    default: return ly.ffn2_b;
+  }
+}
+
+__device__ __forceinline__ void ctx_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ float4 ctx_load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ctx_load4(const __nv_bfloat16* p) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+  const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// part[ks][row][o] = sum over the slice's columns of text0_w[o][c] * ctx[row][c].
+// smem: ctx tile [16][tk] (input type) | W slice [D][tk + 4] fp32
+template <typename Tin>
+__global__ void __launch_bounds__(kCtxThreads) cae_ctx_slice_kernel(const __grid_constant__ CaeCtxArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ uint64_t bar;
+  const int r0 = blockIdx.x * kCaeCtxRows, nr = min(kCaeCtxRows, a.rows - r0);
+  const int T = a.T, D = a.D, tk = a.tk, ks = blockIdx.y;
+  const int k0 = ks * tk, nk = max(0, min(tk, T - k0));
+  Tin* sx = reinterpret_cast<Tin*>(sm);
+  float* sw = sm + (kCaeCtxRows * tk * static_cast<int>(sizeof(Tin))) / 4;
+  const Tin* src = std::is_same<Tin, float>::value ? reinterpret_cast<const Tin*>(a.ctx_f32)
+                                                   : reinterpret_cast<const Tin*>(a.ctx_bf16);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the context (and the previous call's readers of the workspace)
+  pdl_launch_dependents();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && a.status != nullptr) *a.status = 0;
+  if (nk > 0) {
+    if (threadIdx.x == 0)
+      mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(nr * nk * sizeof(Tin) + D * nk * 4));
+    const int t = threadIdx.x;
+    if (t < nr)
+      ctx_bulk(sx + t * tk, src + static_cast<long long>(r0 + t) * T + k0, static_cast<uint32_t>(nk * sizeof(Tin)),
+               &bar);
+    else if (t < nr + D)
+      ctx_bulk(sw + (t - nr) * (tk + 4), a.text0_w + static_cast<long long>(t - nr) * T + k0,
+               static_cast<uint32_t>(nk * 4), &bar);
+    mbar_wait(&bar, 0, a.status, 0x4343);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  const float* w0 = sw + lane * (tk + 4);
+  const float* w1 = sw + (lane + 32) * (tk + 4);
+  const bool has0 = lane < D, has1 = lane + 32 < D;
+  for (int c = 0; c < nk; c += 4) {
+    const float4 x0 = ctx_load4(sx + warp * tk + c);
+    const float4 x1 = ctx_load4(sx + (warp + 8) * tk + c);
+    if (has0) {
+      const float4 w = ctx_load4(w0 + c);
+      acc[0][0] = fmaf(w.x, x0.x, fmaf(w.y, x0.y, fmaf(w.z, x0.z, fmaf(w.w, x0.w, acc[0][0]))));
+      acc[1][0] = fmaf(w.x, x1.x, fmaf(w.y, x1.y, fmaf(w.z, x1.z, fmaf(w.w, x1.w, acc[1][0]))));
+    }
+    if (has1) {
+      const float4 w = ctx_load4(w1 + c);
+      acc[0][1] = fmaf(w.x, x0.x, fmaf(w.y, x0.y, fmaf(w.z, x0.z, fmaf(w.w, x0.w, acc[0][1]))));
+      acc[1][1] = fmaf(w.x, x1.x, fmaf(w.y, x1.y, fmaf(w.z, x1.z, fmaf(w.w, x1.w, acc[1][1]))));
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = warp + 8 * rr;
+    if (r >= nr) continue;
+    float* dst = a.part + (static_cast<long long>(ks) * a.rows + r0 + r) * D;
+    if (has0) dst[lane] = acc[rr][0];
+    if (has1) dst[lane + 32] = acc[rr][1];
+  }
+}
+
+// smem: e1 [16][D] | e [16][D] | ckv weights [2HD][D + 4]
+__global__ void __launch_bounds__(kCtxThreads) cae_ctx_kv_kernel(const __grid_constant__ CaeCtxArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int r0 = blockIdx.x * kCaeCtxRows, nr = min(kCaeCtxRows, a.rows - r0);
+  const int l = blockIdx.y, D = a.D, HD = a.HD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* e1 = sm;
+  float* e = e1 + kCaeCtxRows * D;
+  float* wkv = e + kCaeCtxRows * D;
+  const CaeLayer& ly = a.layers[l];
+  // constant inputs first (they overlap the slice launch): this block's K/V
+  // projection, and this CTA's share of the packed block weights
+  for (int i = threadIdx.x; i < 2 * HD * D; i += kCtxThreads) {
+    const int o = i / D, c = i - o * D;
+    wkv[o * (D + 4) + c] = ly.ckv_w[i];
+  }
+  if (a.wpack != nullptr) {
+    const CaeStagePlan& p = a.plan;
+    int ntasks = 0;
+    for (int t = 0; t < kCaeStagedTensors; ++t) ntasks += p.rows[t];
+    float* blk = a.wpack + static_cast<long long>(l) * (p.a_floats + p.f_floats);
+    for (int task = blockIdx.x * (kCtxThreads / 32) + warp; task < ntasks; task += gridDim.x * (kCtxThreads / 32)) {
+      int t = 0, r = task;
+      while (r >= p.rows[t]) {
+        r -= p.rows[t];
+        ++t;
+      }
+      const float* src = cae_layer_tensor(ly, t);
+      float* dst = blk + (t < kCaeStagedHalfSplit ? 0 : p.a_floats) + p.off[t] + r * p.stride[t];
+      const int cols = p.cols[t];
+      for (int c = lane; c < cols; c += 32) dst[c] = src != nullptr ? src[static_cast<long long>(r) * cols + c] : 0.f;
+    }
+  }
+  pdl_wait();  // slice partial sums
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < nr * D; i += kCtxThreads) {
+    const int r = i / D, o = i - r * D;
+    float s = a.text0_b[o];
+    for (int ks = 0; ks < kCaeCtxSlices; ++ks) s += a.part[(static_cast<long long>(ks) * a.rows + r0 + r) * D + o];
+    e1[r * D + o] = gelu_tanh(s);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nr * D; i += kCtxThreads) {
+    const int r = i / D, o = i - r * D;
+    float s = a.text2_b[o];
+    const float* wr = a.text2_w + static_cast<long long>(o) * D;
+    for (int c = 0; c < D; ++c) s += wr[c] * e1[r * D + c];
+    e[r * D + o] = s;
+  }
+  __syncthreads();
+  // K = RMSNorm(Wk e + bk) * norm_k over H*d, V = Wv e + bv: warp per token
+  for (int r = warp; r < nr; r += kCtxThreads / 32) {
+    float kv[2], vv[2], ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int o = lane + 32 * u;
+      kv[u] = vv[u] = 0.f;
+      if (o < HD) {
+        float sk = ly.ckv_b[o], sv = ly.ckv_b[HD + o];
+        const float* wk = wkv + o * (D + 4);
+        const float* wv = wkv + (HD + o) * (D + 4);
+        for (int c = 0; c < D; ++c) {
+          sk = fmaf(wk[c], e[r * D + c], sk);
+          sv = fmaf(wv[c], e[r * D + c], sv);
+        }
+        kv[u] = sk;
+        vv[u] = sv;
+        ss += sk * sk;
+      }
+    }
+    const float rr = rsqrtf(warp_sum(ss) / HD + a.eps);
+    const int R = r0 + r;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int o = lane + 32 * u;
+      if (o >= HD) continue;
+      const float kn = kv[u] * rr * ly.cnorm_k[o];
+      const long long row = static_cast<long long>(l) * a.rows + R;
+      if (a.kv_packed) {  // padded rows: conflict-free tensor-core fragment loads
+        a.ctx_k[row * (HD + 4) + o] = kn;
+        a.ctx_v[row * (HD + 8) + o] = vv[u];
+      } else {
+        a.ctx_k[row * HD + o] = kn;
+        a.ctx_v[row * HD + o] = vv[u];
+      }
+    }
+  }
+}
+
+static size_t ctx_slice_smem(const CaeCtxArgs& a) {
+  const size_t esz = a.ctx_bf16 != nullptr ? 2 : 4;
+  return kCaeCtxRows * a.tk * esz + static_cast<size_t>(a.D) * (a.tk + 4) * 4;
+}
+
+bool cae_ctx_split_setup(CaeCtxArgs* a) {
+  a->tk = 0;
+  const void* ctx = a->ctx_bf16 != nullptr ? static_cast<const void*>(a->ctx_bf16) : static_cast<const void*>(a->ctx_f32);
+  if (a->T % 8 != 0 || a->D % 4 != 0 || a->D > 64 || a->HD > 64) return false;
+  if ((reinterpret_cast<uintptr_t>(ctx) & 15) != 0 || (reinterpret_cast<uintptr_t>(a->text0_w) & 15) != 0) return false;
+  int tk = (a->T + kCaeCtxSlices - 1) / kCaeCtxSlices;
+  tk = (tk + 7) / 8 * 8;
+  a->tk = tk;
+  if (ctx_slice_smem(*a) > 227 * 1024) {
+    a->tk = 0;
+    return false;
+  }
+  return true;
+}
+
+template <typename Kern>
+static cudaError_t ctx_launch(Kern k, dim3 grid, size_t smem, cudaStream_t st, bool pdl, const CaeCtxArgs& a) {
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kCtxThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, a);
+}
+
 cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl) {
+  if (a.tk > 0) {
+    const int tiles = (a.rows + kCaeCtxRows - 1) / kCaeCtxRows;
+    cudaError_t e = a.ctx_bf16 != nullptr
+                        ? ctx_launch(cae_ctx_slice_kernel<__nv_bfloat16>, dim3(tiles, kCaeCtxSlices), ctx_slice_smem(a), st, pdl, a)
+                        : ctx_launch(cae_ctx_slice_kernel<float>, dim3(tiles, kCaeCtxSlices), ctx_slice_smem(a), st, pdl, a);
+    if (e != cudaSuccess) return e;
+    const size_t smem2 = sizeof(float) * (2 * kCaeCtxRows * a.D + 2 * a.HD * (a.D + 4));
+    return ctx_launch(cae_ctx_kv_kernel, dim3(tiles, a.L), smem2, st, true, a);
+  }
   const size_t smem = sizeof(float) * kCaeCtxTokens * (a.T + 2 * a.D);
   cudaError_t e = cudaFuncSetAttribute(cae_context_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
@@ -393,8 +637,7 @@ cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_cae_steps(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
-  CaeStepArgs staged = a;
-  if (cae_staged_plan(a, &staged.plan)) return launch_cae_steps_staged(staged, st, pdl);
+  if (a.wpack != nullptr) return launch_cae_steps_staged(a, st, pdl);
   const size_t smem = sizeof(CaeSmem);
   cudaError_t e = cudaFuncSetAttribute(cae_steps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));

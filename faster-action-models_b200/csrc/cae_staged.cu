@@ -1,27 +1,34 @@
 // Compact Action Expert, staged Euler loop: one CTA of 1024 threads per sample
 // runs every Euler step x every DiT block with all operands in shared memory.
 //
-// The per-block weights (~60 KB fp32 for BASELINE config 0) are staged one block
-// ahead with cp.async: the attention half (modulation, qkv, o, norm3, cross q,
-// cross o) double buffered, the FFN half (ffn0, ffn2) single buffered and
-// reloaded once the previous block's FFN is done.  The block's context K/V
-// (written by cae_context_kernel) streams through two buffers one (head, key
-// chunk) unit ahead.  Every per-token chain that only needs its own row
-// (projection -> residual -> LayerNorm -> next projection, the head, the Euler
-// update and the next step's encoder) runs inside one warp per token row, so a
-// block costs about ten CTA barriers.  Matrix rows sit in shared memory with a
-// stride of K + 4 floats, which makes the lane-per-output float4 reads
-// conflict-free.
+// Weights: the context launch packs every block's tensors into one global blob
+// in exactly the shared-memory layout (matrix rows padded to K + 4 floats, so
+// the lane-per-output float4 reads are conflict-free).  Each block's attention
+// half (modulation, qkv, o, norm3, cross q, cross o) is double buffered and
+// arrives one block ahead by a single bulk copy; the FFN half (ffn0, ffn2) is
+// single buffered and reloaded once the previous block's FFN is done.
+// Context K/V ([L, B*C, H*d] with rows padded to H*d + 4 / + 8, also written by
+// the context launch) streams through two buffers one key chunk ahead, two bulk
+// copies per chunk.  Every copy completes on an mbarrier with a bounded wait.
+//
+// Per block: warp-per-row chains for everything that only needs its own token
+// row (projection -> residual -> LayerNorm -> next projection, the head, the
+// Euler update, the next step's encoder).  Cross attention: each warp owns one
+// head and 16 keys of every chunk and keeps a running softmax over the chunks;
+// scores and P.V run on the tensor cores (mma.sync TF32, split into high and
+// low parts for fp32 accuracy); the key slices merge in the next row chain.
 //
 // Reference (FastWAM/src/fastwam/models/wan22/...): ActionDiT.prepare/forward
 // (action_dit.py:312-362), DiTBlock.forward (wan_video_dit.py:248-267), the
-// sinusoid (:30-34), RMSNorm (:146-157), rope_apply (:54-60), flash-free
-// attention (:105-124 semantics: softmax(q k^T / sqrt(d)) v), the scheduler step
+// sinusoid (:30-34), RMSNorm (:146-157), rope_apply (:54-60), attention
+// softmax(q k^T / sqrt(d)) v, the scheduler step
 // (schedulers/scheduler_continuous.py:82-88).  fp32 arithmetic like the
 // reference's fp32 CAE configuration.
 #include "fam_cae.h"
 #include "fam_common.cuh"
 #include "fam_mma.cuh"
+
+#include <cstring>
 
 namespace fam {
 
@@ -30,8 +37,9 @@ namespace {
 constexpr int kCsThreads = 1024;
 constexpr int kCsWarps = kCsThreads / 32;
 constexpr int kCsMaxTb = 8;       // t_mod rows per time-MLP batch
-constexpr int kCsMaxRows = 32;    // token rows (one warp each)
+constexpr int kCsMaxRows = 16;    // token rows (one 16-row tensor-core tile)
 constexpr int kCsSmemLimit = 227 * 1024;
+constexpr int kCsErrWait = 0x4341;  // a bulk copy did not complete within the wait limit
 
 __device__ __forceinline__ void cs_cp4(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -59,32 +67,13 @@ __device__ __forceinline__ void cs_stage(float* dst, const float* src, int rows,
   }
 }
 
-__device__ __forceinline__ const float* cs_src(const CaeLayer& ly, int t) {
-  switch (t) {
-    case 0: return ly.modulation;
-    case 1: return ly.qkv_w;
-    case 2: return ly.qkv_b;
-    case 3: return ly.norm_q;
-    case 4: return ly.norm_k;
-    case 5: return ly.o_w;
-    case 6: return ly.o_b;
-    case 7: return ly.norm3_w;
-    case 8: return ly.norm3_b;
-    case 9: return ly.cq_w;
-    case 10: return ly.cq_b;
-    case 11: return ly.cnorm_q;
-    case 12: return ly.co_w;
-    case 13: return ly.co_b;
-    case 14: return ly.ffn0_w;
-    case 15: return ly.ffn0_b;
-    case 16: return ly.ffn2_w;
-    default: return ly.ffn2_b;
-  }
-}
-
-__device__ __forceinline__ void cs_stage_half(float* base, const CaeLayer& ly, const CaeStagePlan& p, int t0,
-                                              int t1) {
-  for (int t = t0; t < t1; ++t) cs_stage(base + p.off[t], cs_src(ly, t), p.rows[t], p.cols[t], p.stride[t]);
+// One bulk copy global -> shared completing on `bar` (16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void cs_bulk(float* dst, const float* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // W[0:K] . v[0:K], both 16-byte aligned in shared memory, K % 4 == 0.
@@ -138,17 +127,19 @@ __device__ __forceinline__ void cs_adaln_row(const float (&xv)[2], float* hrow, 
   }
 }
 
-struct CsPtrs {
-  float *abuf0, *abuf1, *fbuf, *kv0, *kv1, *x, *h, *q, *k, *v, *att, *qc, *f, *part, *tm, *tscr, *lat, *rope, *encw,
-      *encb, *headw, *headb;
-};
+// Shared-memory regions: base + plan offset, evaluated at each use (the plan
+// lives in the kernel parameters, so no pointer stays live in registers).
+#define CS_SM(name) (csm + a.plan.o_##name)
+#define CS_ABUF(e) (csm + a.plan.o_abuf + (((e) & 1) ? a.plan.a_floats : 0))
+#define CS_KV(g) (csm + a.plan.o_kv + (((g) & 1) ? a.plan.kv_floats : 0))
+#define CS_BAR(i) (reinterpret_cast<uint64_t*>(csm + a.plan.o_bar) + (i))
 
 // t_mod rows of steps [step0, step0 + nb): sinusoid (fp64 then fp32) -> Linear ->
 // SiLU -> Linear -> SiLU -> Linear(6D).  Block-wide; ends with a barrier.
-__device__ void cs_time_batch(const CaeStepArgs& a, const CsPtrs& P, int step0, int nb) {
+__device__ __noinline__ void cs_time_batch(const CaeStepArgs& a, float* csm, int step0, int nb) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = a.D, fd = a.freq_dim, half = fd / 2;
-  float* t1 = P.tscr;                    // [tb][fd]
+  float* t1 = CS_SM(tscr);               // [tb][fd]
   float* t2 = t1 + a.plan.tb * fd;       // [tb][D]
   float* t3 = t2 + a.plan.tb * D;        // [tb][D]
   for (int i = threadIdx.x; i < nb * half; i += kCsThreads) {
@@ -172,95 +163,226 @@ __device__ void cs_time_batch(const CaeStepArgs& a, const CsPtrs& P, int step0, 
         for (int r = 0; r < kCsMaxTb; ++r)
           if (r < nb) acc[r] = fmaf(w, in[r * K + c], acc[r]);
       }
+      const float bo = bias != nullptr ? __ldg(bias + o) : 0.f;
 #pragma unroll
       for (int r = 0; r < kCsMaxTb; ++r) {
-        if (r >= nb) break;
-        const float s = warp_sum(acc[r]) + (bias != nullptr ? __ldg(bias + o) : 0.f);
-        if (lane == 0) out[r * O + o] = act ? silu(s) : s;
+        const float s = warp_sum(acc[r]) + bo;
+        if (lane == 0 && r < nb) out[r * O + o] = act ? silu(s) : s;
       }
     }
     __syncthreads();
   };
   mlp(a.w.time0_w, a.w.time0_b, t1, fd, t2, D, true);
   mlp(a.w.time2_w, a.w.time2_b, t2, D, t3, D, true);
-  mlp(a.w.tproj_w, a.w.tproj_b, t3, D, P.tm, 6 * D, false);
+  mlp(a.w.tproj_w, a.w.tproj_b, t3, D, CS_SM(tm), 6 * D, false);
 }
 
-// Cross attention of one (head, key chunk) unit for the warp's query row and key
-// slice; running softmax state (m, l, acc) persists across the head's chunks.
+// ------------------------------------------------ tensor-core cross attention
+// mma.sync m16n8k8 TF32 with each operand split into a high part (the fp32
+// value with its low 13 mantissa bits cleared: exactly a TF32 number) and the
+// exact remainder, which the tensor core reads to TF32 precision again:
+// a*b ~ al*bh + ah*bl + ah*bh keeps ~21 significant bits, fp32-level accuracy
+// for the fp32 reference.  The split is one AND and one subtraction.
+__device__ __forceinline__ uint32_t cs_tf32(float x) { return __float_as_uint(x) & 0xffffe000u; }
+__device__ __forceinline__ void cs_mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cs_mma_3xtf32(float (&c)[4], const float (&a)[4], float b0, float b1) {
+  uint32_t ah[4], al[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ah[i] = cs_tf32(a[i]);
+    al[i] = cs_tf32(a[i] - __uint_as_float(ah[i]));
+  }
+  const uint32_t bh0 = cs_tf32(b0), bh1 = cs_tf32(b1);
+  const uint32_t bl0 = cs_tf32(b0 - __uint_as_float(bh0)), bl1 = cs_tf32(b1 - __uint_as_float(bh1));
+  cs_mma_tf32(c, al, bh0, bh1);
+  cs_mma_tf32(c, ah, bl0, bl1);
+  cs_mma_tf32(c, ah, bh0, bh1);
+}
+
+// One warp's running softmax over its 16-key slice of every chunk of one head,
+// for the 16-row query tile (rows >= S are zero).  Fragment rows: g = lane / 4
+// (r0) and g + 8 (r1); score columns 2t, 2t+1 of each 8-key tile (t = lane % 4).
 template <int HDIM>
-__device__ __forceinline__ void cs_cross_unit(const float* kb, const float* vb, int nk, const float (&qv)[HDIM],
-                                              const uint8_t* kmask, int wpq, int qw, float scale, float& m, float& l,
-                                              float (&acc)[HDIM]) {
-  const int lane = threadIdx.x & 31;
-  const int per = (nk + wpq - 1) / wpq;
-  const int k_lo = qw * per, k_hi = min(nk, k_lo + per);
-  for (int j0 = k_lo; j0 < k_hi; j0 += 128) {
-    float sc[4];
-    float bm = -INFINITY;
+struct CsFlash {
+  static constexpr int KS = (HDIM + 7) / 8;  // 8-wide k steps over the head dims / 8-wide dim tiles
+  float m0, m1, l0, l1;
+  float o[KS][4];
+  __device__ __forceinline__ void init() {
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int j = j0 + lane + 32 * i;
-      sc[i] = -INFINITY;
-      if (j < k_hi && (kmask == nullptr || kmask[j] != 0)) {
-        const float* kr = kb + j * (HDIM + 4);
-        float d = 0.f;
-#pragma unroll
-        for (int c = 0; c < HDIM; c += 4) {
-          const float4 kk = *reinterpret_cast<const float4*>(kr + c);
-          d = fmaf(qv[c], kk.x, d);
-          d = fmaf(qv[c + 1], kk.y, d);
-          d = fmaf(qv[c + 2], kk.z, d);
-          d = fmaf(qv[c + 3], kk.w, d);
-        }
-        sc[i] = d * scale;
-        bm = fmaxf(bm, sc[i]);
-      }
-    }
-    bm = warp_max(bm);
-    const float mn = fmaxf(m, bm);
-    if (mn == -INFINITY) continue;  // every key so far masked (warp-uniform)
-    const float alpha = expf(m - mn);
-    l *= alpha;
-#pragma unroll
-    for (int d = 0; d < HDIM; ++d) acc[d] *= alpha;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (sc[i] == -INFINITY) continue;
-      const int j = j0 + lane + 32 * i;
-      const float pj = expf(sc[i] - mn);
-      l += pj;
-      const float* vr = vb + j * HDIM;
-#pragma unroll
-      for (int c = 0; c < HDIM; c += 4) {
-        const float4 vv = *reinterpret_cast<const float4*>(vr + c);
-        acc[c] = fmaf(pj, vv.x, acc[c]);
-        acc[c + 1] = fmaf(pj, vv.y, acc[c + 1]);
-        acc[c + 2] = fmaf(pj, vv.z, acc[c + 2]);
-        acc[c + 3] = fmaf(pj, vv.w, acc[c + 3]);
-      }
-    }
-    m = mn;
+    for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   }
+  // buf: K [kc][HD + 4] then V [kc][HD + 8]; keys [k0, k0 + 16) of the chunk (nk valid)
+  __device__ __forceinline__ void chunk(const float* buf, int kc, int HD, int nk, int k0, int hh, const float* qc,
+                                        int hdp, int S, const uint8_t* kmask, float scale) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float* kb = buf;
+    const float* vb = buf + kc * (HD + 4);
+    float qa[KS][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int d0 = ks * 8 + t;
+      const float* q0 = qc + g * hdp + hh * HDIM;
+      const float* q1 = qc + (g + 8) * hdp + hh * HDIM;
+      qa[ks][0] = (g < S && d0 < HDIM) ? q0[d0] : 0.f;
+      qa[ks][1] = (g + 8 < S && d0 < HDIM) ? q1[d0] : 0.f;
+      qa[ks][2] = (g < S && d0 + 4 < HDIM) ? q0[d0 + 4] : 0.f;
+      qa[ks][3] = (g + 8 < S && d0 + 4 < HDIM) ? q1[d0 + 4] : 0.f;
+    }
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int n0 = k0 + nt * 8;
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const float* kr = kb + (n0 + g) * (HD + 4) + hh * HDIM;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const int d0 = ks * 8 + t;
+        const float b0 = d0 < HDIM ? kr[d0] : 0.f;
+        const float b1 = d0 + 4 < HDIM ? kr[d0 + 4] : 0.f;
+        cs_mma_3xtf32(sc[nt], qa[ks], b0, b1);
+      }
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const int j = n0 + 2 * t + e2;
+        const bool valid = j < nk && (kmask == nullptr || kmask[j] != 0);
+        sc[nt][e2] = valid ? sc[nt][e2] * scale : -INFINITY;
+        sc[nt][2 + e2] = valid ? sc[nt][2 + e2] * scale : -INFINITY;
+      }
+    }
+    float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float al0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        sc[nt][e2] = sc[nt][e2] == -INFINITY ? 0.f : expf(sc[nt][e2] - mn0);
+        sc[nt][2 + e2] = sc[nt][2 + e2] == -INFINITY ? 0.f : expf(sc[nt][2 + e2] - mn1);
+      }
+    }
+    l0 = l0 * al0 + ((sc[0][0] + sc[0][1]) + (sc[1][0] + sc[1][1]));
+    l1 = l1 * al1 + ((sc[0][2] + sc[0][3]) + (sc[1][2] + sc[1][3]));
+#pragma unroll
+    for (int nd = 0; nd < KS; ++nd) {
+      o[nd][0] *= al0;
+      o[nd][1] *= al0;
+      o[nd][2] *= al1;
+      o[nd][3] *= al1;
+    }
+    m0 = mn0;
+    m1 = mn1;
+    // P.V: the score fragment of each 8-key tile becomes the A fragment
+    const int srcA = (lane & ~3) | (t >> 1), srcB = srcA + 2;
+    const bool odd = (t & 1) != 0;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      float pa[4];
+      {
+        const float x0 = __shfl_sync(0xffffffffu, sc[nt][0], srcA), x1 = __shfl_sync(0xffffffffu, sc[nt][1], srcA);
+        const float y0 = __shfl_sync(0xffffffffu, sc[nt][0], srcB), y1 = __shfl_sync(0xffffffffu, sc[nt][1], srcB);
+        const float z0 = __shfl_sync(0xffffffffu, sc[nt][2], srcA), z1 = __shfl_sync(0xffffffffu, sc[nt][3], srcA);
+        const float w0 = __shfl_sync(0xffffffffu, sc[nt][2], srcB), w1 = __shfl_sync(0xffffffffu, sc[nt][3], srcB);
+        pa[0] = odd ? x1 : x0;
+        pa[2] = odd ? y1 : y0;
+        pa[1] = odd ? z1 : z0;
+        pa[3] = odd ? w1 : w0;
+      }
+      const int n0 = k0 + nt * 8;
+      const float* vr0 = vb + (n0 + t) * (HD + 8) + hh * HDIM + g;
+      const float* vr1 = vr0 + 4 * (HD + 8);
+#pragma unroll
+      for (int nd = 0; nd < KS; ++nd) {
+        const bool dv = nd * 8 + g < HDIM;
+        cs_mma_3xtf32(o[nd], pa, dv ? vr0[nd * 8] : 0.f, dv ? vr1[nd * 8] : 0.f);
+      }
+    }
+  }
+  // Partial of this warp: rows < S of [m, l, O[HDIM]] with row stride HDIM + 2.
+  __device__ __forceinline__ void store(float* part, int S) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+    lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+    float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+    lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = g + 8 * half;
+      if (r >= S) continue;
+      float* pr = part + r * (HDIM + 2);
+      if (t == 0) {
+        pr[0] = half ? m1 : m0;
+        pr[1] = half ? lt1 : lt0;
+      }
+#pragma unroll
+      for (int nd = 0; nd < KS; ++nd)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int d = nd * 8 + 2 * t + e2;
+          if (d < HDIM) pr[2 + d] = o[nd][2 * half + e2];
+        }
+    }
+  }
+};
+
+// Bulk-copy issue (one thread) and waits (every thread).
+__device__ __forceinline__ void cs_issue_a(const CaeStepArgs& a, float* csm, int e) {
+  uint64_t* bar = CS_BAR(e & 1);
+  const int blk = a.plan.a_floats + a.plan.f_floats;
+  mbar_arrive_expect_tx(bar, a.plan.a_floats * 4);
+  cs_bulk(CS_ABUF(e), a.wpack + static_cast<long long>(e % a.L) * blk, a.plan.a_floats * 4, bar);
+}
+__device__ __forceinline__ void cs_issue_f(const CaeStepArgs& a, float* csm, int e) {
+  uint64_t* bar = CS_BAR(2);
+  const int blk = a.plan.a_floats + a.plan.f_floats;
+  mbar_arrive_expect_tx(bar, a.plan.f_floats * 4);
+  cs_bulk(CS_SM(fbuf), a.wpack + static_cast<long long>(e % a.L) * blk + a.plan.a_floats, a.plan.f_floats * 4, bar);
+}
+template <int HDIM>
+__device__ __forceinline__ void cs_issue_kv(const CaeStepArgs& a, float* csm, int g) {
+  const int U = a.plan.units, kc = a.plan.kc, HD = a.HD;
+  const int e = g / U, u = g - e * U, l = e % a.L;
+  const int j0 = u * kc, nk = min(kc, a.C - j0);
+  const long long row = (static_cast<long long>(l) * a.B + blockIdx.x) * a.C + j0;
+  const uint32_t kbytes = static_cast<uint32_t>(nk * (HD + 4) * 4), vbytes = static_cast<uint32_t>(nk * (HD + 8) * 4);
+  uint64_t* bar = CS_BAR(3 + (g & 1));
+  float* buf = CS_KV(g);
+  mbar_arrive_expect_tx(bar, kbytes + vbytes);
+  cs_bulk(buf, a.ctx_k + row * (HD + 4), kbytes, bar);
+  cs_bulk(buf + kc * (HD + 4), a.ctx_v + row * (HD + 8), vbytes, bar);
+}
+__device__ __forceinline__ void cs_wait(const CaeStepArgs& a, float* csm, int i, int parity) {
+  mbar_wait(CS_BAR(i), static_cast<uint32_t>(parity), a.status, kCsErrWait);
 }
 
-// Issue the K/V copies of unit u of block l (head u / uph, key chunk u % uph).
-__device__ __forceinline__ void cs_stage_kv(const CaeStepArgs& a, float* buf, int l, int u) {
-  const CaeStagePlan& p = a.plan;
-  const int hd = a.hd, HD = a.HD;
-  const int hh = u / p.units_per_head, ch = u - hh * p.units_per_head;
-  const int j0 = ch * p.kc, nk = min(p.kc, a.C - j0);
-  const long long row0 = (static_cast<long long>(l) * a.B + blockIdx.x) * a.C + j0;
-  const float* ck = a.ctx_k + row0 * HD + hh * hd;
-  const float* cv = a.ctx_v + row0 * HD + hh * hd;
-  float* kb = buf;
-  float* vb = buf + p.kc * (hd + 4);
-  const int c4 = hd >> 2;
-  for (int i = threadIdx.x; i < nk * c4; i += kCsThreads) {
-    const int r = i / c4, c = (i - r * c4) * 4;
-    cp_async16(kb + r * (hd + 4) + c, ck + static_cast<long long>(r) * HD + c, true);
-    cp_async16(vb + r * hd + c, cv + static_cast<long long>(r) * HD + c, true);
+// Block-0 entry of a step for token row s (one warp): encoder from the latent,
+// then AdaLN 1 with the attention half `abuf`.
+__device__ __forceinline__ void cs_step_entry_row(const CaeStepArgs& a, float* csm, int s, int step,
+                                                  const float* abuf) {
+  const int lane = threadIdx.x & 31, D = a.D, A = a.A;
+  const float* tmr = CS_SM(tm) + (step % a.plan.tb) * 6 * D;
+  float xv[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int o = lane + 32 * u;
+    xv[u] = 0.f;
+    if (o < D) {
+      xv[u] = CS_SM(encb)[o] + cs_dot(CS_SM(encw) + o * (A + 4), CS_SM(lat) + s * A, A);
+      CS_SM(x)[s * D + o] = xv[u];
+    }
   }
+  cs_adaln_row(xv, CS_SM(h) + s * D, abuf + a.plan.off[0], tmr, D, a.eps, 0, 1);
 }
 
 template <int HDIM>
@@ -268,88 +390,58 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
   extern __shared__ __align__(16) float csm[];
   const CaeStagePlan& p = a.plan;
   const int b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = a.S, D = a.D, A = a.A, HD = a.HD, H = HD / HDIM, F = a.F, L = a.L, N = a.num_steps;
-  const int hdp = p.hdp;
-  CsPtrs P;
-  P.abuf0 = csm + p.o_abuf;
-  P.abuf1 = P.abuf0 + p.a_floats;
-  P.fbuf = csm + p.o_fbuf;
-  P.kv0 = csm + p.o_kv;
-  P.kv1 = P.kv0 + p.kv_floats;
-  P.x = csm + p.o_x;
-  P.h = csm + p.o_h;
-  P.q = csm + p.o_q;
-  P.k = csm + p.o_k;
-  P.v = csm + p.o_v;
-  P.att = csm + p.o_att;
-  P.qc = csm + p.o_qc;
-  P.f = csm + p.o_f;
-  P.part = csm + p.o_part;
-  P.tm = csm + p.o_tm;
-  P.tscr = csm + p.o_tscr;
-  P.lat = csm + p.o_lat;
-  P.rope = csm + p.o_rope;
-  P.encw = csm + p.o_encw;
-  P.encb = csm + p.o_encb;
-  P.headw = csm + p.o_headw;
-  P.headb = csm + p.o_headb;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = a.S, D = a.D, A = a.A, HD = a.HD, H = HD / HDIM, F = a.F, L = a.L, N = a.num_steps, C = a.C;
+  const int hdp = p.hdp, kc = p.kc;
   const float scale = rsqrtf(static_cast<float>(HDIM));
-  const uint8_t* kmask = a.ctx_mask != nullptr ? a.ctx_mask + static_cast<long long>(b) * a.C : nullptr;
+  const uint8_t* kmask = a.ctx_mask != nullptr ? a.ctx_mask + static_cast<long long>(b) * C : nullptr;
   float* latent = a.latent + static_cast<long long>(b) * S * A;
+  const int U = p.units;
+  const int total = N * L;
+  const int blk_floats = p.a_floats + p.f_floats;
 
-  // ---- prologue: constant tensors, block 0 weights, the latent; first t_mod batch
-  cs_stage(P.encw, a.w.enc_w, D, A, A + 4);
-  cs_stage(P.encb, a.w.enc_b, 1, D, D);
-  cs_stage(P.headw, a.w.head_w, A, D, D + 4);
-  cs_stage(P.headb, a.w.head_b, 1, A, A);
-  cs_stage(P.rope, a.rope, 1, S * HDIM, S * HDIM);
-  cs_stage(P.lat, latent, 1, S * A, S * A);
-  cs_stage_half(P.abuf0, a.w.layers[0], p, 0, kCaeStagedHalfSplit);
-  cs_stage_half(P.fbuf, a.w.layers[0], p, kCaeStagedHalfSplit, kCaeStagedTensors);
+  // ---- prologue: barriers, constant tensors, first t_mod batch, block 0 weights
+  if (tid == 0) {
+    for (int i = 0; i < 5; ++i) mbar_init(CS_BAR(i), 1);
+    fence_mbar_init();
+  }
+  cs_stage(CS_SM(encw), a.w.enc_w, D, A, A + 4);
+  cs_stage(CS_SM(encb), a.w.enc_b, 1, D, D);
+  cs_stage(CS_SM(headw), a.w.head_w, A, D, D + 4);
+  cs_stage(CS_SM(headb), a.w.head_b, 1, A, A);
+  cs_stage(CS_SM(rope), a.rope, 1, S * HDIM, S * HDIM);
+  cs_stage(CS_SM(lat), latent, 1, S * A, S * A);
   cp_async_commit();
-  cs_time_batch(a, P, 0, min(p.tb, N));
-  pdl_wait();  // the context K/V come from the preceding launch
+  __syncthreads();
+  cs_time_batch(a, csm, 0, min(p.tb, N));
+  // K/V buffers start at zero: rows past a short last chunk are read by the
+  // tensor-core tiles (their scores are masked, and 0 * finite stays 0)
+  for (int i = tid; i < 2 * p.kv_floats; i += kCsThreads) CS_SM(kv)[i] = 0.f;
+  fence_async_smem();
+  __syncthreads();
+  pdl_wait();  // packed weights and context K/V come from the preceding launch
+  if (tid == 0) {
+    cs_issue_a(a, csm, 0);
+    cs_issue_f(a, csm, 0);
+    cs_issue_kv<HDIM>(a, csm, 0);
+  }
   pdl_launch_dependents();
   cp_async_wait<0>();
+  cs_wait(a, csm, 0, 0);
   __syncthreads();
 
-  // standalone block-0 AdaLN of a step: encoder from the latent, then AdaLN 1
-  auto step_entry_row = [&](int s, int step, const float* abuf) {
-    const float* tmr = P.tm + (step % p.tb) * 6 * D;
-    float xv[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int o = lane + 32 * u;
-      xv[u] = 0.f;
-      if (o < D) {
-        xv[u] = P.encb[o] + cs_dot(P.encw + o * (A + 4), P.lat + s * A, A);
-        P.x[s * D + o] = xv[u];
-      }
-    }
-    cs_adaln_row(xv, P.h + s * D, abuf + p.off[0], tmr, D, a.eps, 0, 1);
-  };
-  for (int s = warp; s < S; s += kCsWarps) step_entry_row(s, 0, P.abuf0);
+  for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, 0, CS_ABUF(0));
 
-  const int uph = p.units_per_head, U = H * uph;
-  const int total = N * L;
   for (int e = 0; e < total; ++e) {
     const int step = e / L, l = e - step * L;
-    const CaeLayer& ly = a.w.layers[l];
-    float* ab = (e & 1) ? P.abuf1 : P.abuf0;
+    float* ab = CS_ABUF(e);
     const float* mod = ab + p.off[0];
-    const float* tmr = P.tm + (step % p.tb) * 6 * D;
+    const float* tmr = CS_SM(tm) + (step % p.tb) * 6 * D;
     __syncthreads();  // AdaLN-1 rows of this block written; previous block's FFN done
-    // prefetch: K/V unit 0 of this block, then the next block's attention half
-    // and this block's FFN half (block 0's FFN half came with the prologue)
-    cs_stage_kv(a, P.kv0, l, 0);
-    cp_async_commit();
-    if (e + 1 < total) {
-      const int ln = (e + 1) % L;
-      cs_stage_half((e & 1) ? P.abuf0 : P.abuf1, a.w.layers[ln], p, 0, kCaeStagedHalfSplit);
+    if (tid == 0) {
+      if (e + 1 < total) cs_issue_a(a, csm, e + 1);
+      if (e > 0) cs_issue_f(a, csm, e);
     }
-    if (e > 0) cs_stage_half(P.fbuf, ly, p, kCaeStagedHalfSplit, kCaeStagedTensors);
-    cp_async_commit();
 
     // ---- q, k, v (+ RMSNorm over H*d, RoPE on q and k): warp per (row, part)
     for (int item = warp; item < 3 * S; item += kCsWarps) {
@@ -360,9 +452,9 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int o = lane + 32 * u;
-        y[u] = o < HD ? bias[o] + cs_dot(w + o * (D + 4), P.h + s * D, D) : 0.f;
+        y[u] = o < HD ? bias[o] + cs_dot(w + o * (D + 4), CS_SM(h) + s * D, D) : 0.f;
       }
-      float* dst = part == 0 ? P.q : (part == 1 ? P.k : P.v);
+      float* dst = part == 0 ? CS_SM(q) : (part == 1 ? CS_SM(k) : CS_SM(v));
       if (part < 2) {
         const float* nw = ab + p.off[part == 0 ? 3 : 4];
         const float r = rsqrtf(warp_sum(y[0] * y[0] + y[1] * y[1]) / HD + a.eps);
@@ -373,7 +465,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
           const float other = __shfl_xor_sync(0xffffffffu, yn, 1);
           if (o < HD) {
             const int pi = (o % HDIM) >> 1;
-            const float c = P.rope[(s * (HDIM / 2) + pi) * 2], sn = P.rope[(s * (HDIM / 2) + pi) * 2 + 1];
+            const float c = CS_SM(rope)[(s * (HDIM / 2) + pi) * 2], sn = CS_SM(rope)[(s * (HDIM / 2) + pi) * 2 + 1];
             dst[s * hdp + o] = (o & 1) == 0 ? yn * c - other * sn : other * sn + yn * c;
           }
         }
@@ -390,10 +482,10 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
     // ---- self attention over the S action tokens: warp per (row, head), lanes over keys
     for (int item = warp; item < S * H; item += kCsWarps) {
       const int s = item / H, hh = item - s * H;
-      float sc = -INFINITY;
+      float scv = -INFINITY;
       if (lane < S) {
-        const float* qr = P.q + s * hdp + hh * HDIM;
-        const float* kr = P.k + lane * hdp + hh * HDIM;
+        const float* qr = CS_SM(q) + s * hdp + hh * HDIM;
+        const float* kr = CS_SM(k) + lane * hdp + hh * HDIM;
         float d = 0.f;
 #pragma unroll
         for (int c = 0; c < HDIM; c += 4) {
@@ -404,18 +496,18 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
           d = fmaf(qq.z, kk.z, d);
           d = fmaf(qq.w, kk.w, d);
         }
-        sc = d * scale;
+        scv = d * scale;
       }
-      const float mx = warp_max(sc);
-      const float pj = lane < S ? expf(sc - mx) : 0.f;
+      const float mx = warp_max(scv);
+      const float pj = lane < S ? expf(scv - mx) : 0.f;
       const float den = warp_sum(pj);
       float acc = 0.f;
       const int d = lane % HDIM;
       for (int j = 0; j < S; ++j) {
         const float pp = __shfl_sync(0xffffffffu, pj, j);
-        acc = fmaf(pp, P.v[j * hdp + hh * HDIM + d], acc);
+        acc = fmaf(pp, CS_SM(v)[j * hdp + hh * HDIM + d], acc);
       }
-      if (lane < HDIM) P.att[s * hdp + hh * HDIM + lane] = acc / den;
+      if (lane < HDIM) CS_SM(att)[s * hdp + hh * HDIM + lane] = acc / den;
     }
     __syncthreads();
 
@@ -429,9 +521,9 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
         const int o = lane + 32 * u;
         xv[u] = 0.f;
         if (o < D) {
-          const float y = ob[o] + cs_dot(ow + o * (HD + 4), P.att + s * hdp, HD);
-          xv[u] = P.x[s * D + o] + (mod[2 * D + o] + tmr[2 * D + o]) * y;
-          P.x[s * D + o] = xv[u];
+          const float y = ob[o] + cs_dot(ow + o * (HD + 4), CS_SM(att) + s * hdp, HD);
+          xv[u] = CS_SM(x)[s * D + o] + (mod[2 * D + o] + tmr[2 * D + o]) * y;
+          CS_SM(x)[s * D + o] = xv[u];
         }
       }
       float mean, rstd;
@@ -441,7 +533,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int o = lane + 32 * u;
-        if (o < D) P.h[s * D + o] = (xv[u] - mean) * rstd * n3w[o] + n3b[o];
+        if (o < D) CS_SM(h)[s * D + o] = (xv[u] - mean) * rstd * n3w[o] + n3b[o];
       }
       __syncwarp();
       const float* cw = ab + p.off[9];
@@ -451,85 +543,60 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int o = lane + 32 * u;
-        y[u] = o < HD ? cb[o] + cs_dot(cw + o * (D + 4), P.h + s * D, D) : 0.f;
+        y[u] = o < HD ? cb[o] + cs_dot(cw + o * (D + 4), CS_SM(h) + s * D, D) : 0.f;
       }
       const float r = rsqrtf(warp_sum(y[0] * y[0] + y[1] * y[1]) / HD + a.eps);
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int o = lane + 32 * u;
-        if (o < HD) P.qc[s * hdp + o] = y[u] * r * cn[o];
+        if (o < HD) CS_SM(qc)[s * hdp + o] = y[u] * r * cn[o];
       }
     }
 
-    // ---- cross attention: (head, key chunk) units stream through two buffers
+    // ---- cross attention: key chunks of all heads; warp = (head, 16 keys of the
+    // chunk), tensor-core scores and P.V with a running softmax across chunks
     {
-      const int s = warp / p.wpq, qw = warp - s * p.wpq;
-      const bool active = s < S;
-      float m = -INFINITY, lsum = 0.f;
-      float acc[HDIM];
-      float qv[HDIM];
-#pragma unroll
-      for (int d = 0; d < HDIM; ++d) acc[d] = qv[d] = 0.f;
+      const int wh = p.wh, hh = warp / wh, slot = warp - hh * wh;
+      const bool act = hh < H;
+      CsFlash<HDIM> fl;
+      fl.init();
       for (int u = 0; u < U; ++u) {
-        if (u == 0)
-          cp_async_wait<1>();
-        else
-          cp_async_wait<0>();
-        __syncthreads();
-        if (u + 1 < U) cs_stage_kv(a, ((u + 1) & 1) ? P.kv1 : P.kv0, l, u + 1);
-        cp_async_commit();
-        const int hh = u / uph, ch = u - hh * uph;
-        if (!active) continue;
-        if (ch == 0) {
-          m = -INFINITY;
-          lsum = 0.f;
-#pragma unroll
-          for (int d = 0; d < HDIM; ++d) {
-            acc[d] = 0.f;
-            qv[d] = P.qc[s * hdp + hh * HDIM + d];
-          }
-        }
-        const float* buf = (u & 1) ? P.kv1 : P.kv0;
-        const int j0 = ch * p.kc, nk = min(p.kc, a.C - j0);
-        cs_cross_unit<HDIM>(buf, buf + p.kc * (HDIM + 4), nk, qv, kmask != nullptr ? kmask + j0 : nullptr, p.wpq,
-                            qw, scale, m, lsum, acc);
-        if (ch == uph - 1) {
-          const float lt = warp_sum(lsum);
-#pragma unroll
-          for (int d = 0; d < HDIM; ++d) acc[d] = warp_sum(acc[d]);
-          if (lane == 0) {
-            float* pp = P.part + ((s * H + hh) * p.wpq + qw) * (HDIM + 2);
-            pp[0] = m;
-            pp[1] = lt;
-#pragma unroll
-            for (int d = 0; d < HDIM; ++d) pp[2 + d] = acc[d];
-          }
+        const int g = e * U + u;
+        cs_wait(a, csm, 3 + (g & 1), (g >> 1) & 1);
+        __syncthreads();  // chunk g landed; every warp is done with chunk g - 1 (the other buffer)
+        if (tid == 0 && g + 1 < total * U) cs_issue_kv<HDIM>(a, csm, g + 1);
+        if (act) {
+          const int j0 = u * kc;
+          fl.chunk(CS_KV(g), kc, HD, min(kc, C - j0), slot * 16, hh, CS_SM(qc), hdp, S,
+                   kmask != nullptr ? kmask + j0 : nullptr, scale);
         }
       }
+      if (act) fl.store(CS_SM(part) + (hh * wh + slot) * S * (HDIM + 2), S);
     }
     __syncthreads();
 
-    // ---- row chain: merge the key slices; x += cross_o(attn); h = AdaLN 2(x)
+    // ---- row chain: merge the key chunks; x += cross_o(attn); h = AdaLN 2(x)
     for (int s = warp; s < S; s += kCsWarps) {
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int o = lane + 32 * u;
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int o = lane + 32 * u2;
         if (o < HD) {
           const int hh = o / HDIM, d = o - hh * HDIM;
-          const float* pp = P.part + (s * H + hh) * p.wpq * (HDIM + 2);
+          const float* pp = CS_SM(part) + (hh * p.wh * S + s) * (HDIM + 2);
+          const int pst = S * (HDIM + 2);  // next slot of the same head
           float mx = -INFINITY;
-          for (int q = 0; q < p.wpq; ++q) mx = fmaxf(mx, pp[q * (HDIM + 2)]);
+          for (int sl = 0; sl < p.wh; ++sl) mx = fmaxf(mx, pp[sl * pst]);
           float num = 0.f, den = 0.f;
           if (mx != -INFINITY) {
-            for (int q = 0; q < p.wpq; ++q) {
-              const float mq = pp[q * (HDIM + 2)];
-              if (mq == -INFINITY) continue;
-              const float f = expf(mq - mx);
-              den = fmaf(f, pp[q * (HDIM + 2) + 1], den);
-              num = fmaf(f, pp[q * (HDIM + 2) + 2 + d], num);
+            for (int sl = 0; sl < p.wh; ++sl) {
+              const float* q = pp + sl * pst;
+              if (q[0] == -INFINITY) continue;
+              const float fct = expf(q[0] - mx);
+              den = fmaf(fct, q[1], den);
+              num = fmaf(fct, q[2 + d], num);
             }
           }
-          P.att[s * hdp + o] = den > 0.f ? num / den : 0.f;
+          CS_SM(att)[s * hdp + o] = den > 0.f ? num / den : 0.f;
         }
       }
       __syncwarp();
@@ -537,27 +604,28 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
       const float* cb = ab + p.off[13];
       float xv[2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int o = lane + 32 * u;
-        xv[u] = 0.f;
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int o = lane + 32 * u2;
+        xv[u2] = 0.f;
         if (o < D) {
-          xv[u] = P.x[s * D + o] + (cb[o] + cs_dot(cw + o * (HD + 4), P.att + s * hdp, HD));
-          P.x[s * D + o] = xv[u];
+          xv[u2] = CS_SM(x)[s * D + o] + (cb[o] + cs_dot(cw + o * (HD + 4), CS_SM(att) + s * hdp, HD));
+          CS_SM(x)[s * D + o] = xv[u2];
         }
       }
-      cs_adaln_row(xv, P.h + s * D, mod, tmr, D, a.eps, 3, 4);
+      cs_adaln_row(xv, CS_SM(h) + s * D, mod, tmr, D, a.eps, 3, 4);
     }
-    cp_async_wait<0>();  // the FFN half of this block and the next block's attention half
+    cs_wait(a, csm, 2, e & 1);                                      // this block's FFN half
+    if (e + 1 < total) cs_wait(a, csm, (e + 1) & 1, ((e + 1) >> 1) & 1);  // next block's attention half
     __syncthreads();
 
     // ---- FFN 0 + GELU(tanh): warp per (row, 32 outputs)
     {
       const int ng = (F + 31) / 32;
-      const float* w = P.fbuf + p.off[14];
-      const float* bias = P.fbuf + p.off[15];
+      const float* w = CS_SM(fbuf) + p.off[14];
+      const float* bias = CS_SM(fbuf) + p.off[15];
       for (int item = warp; item < S * ng; item += kCsWarps) {
         const int s = item / ng, o = (item - s * ng) * 32 + lane;
-        if (o < F) P.f[s * F + o] = gelu_tanh(bias[o] + cs_dot(w + o * (D + 4), P.h + s * D, D));
+        if (o < F) CS_SM(f)[s * F + o] = gelu_tanh(bias[o] + cs_dot(w + o * (D + 4), CS_SM(h) + s * D, D));
       }
     }
     __syncthreads();
@@ -567,45 +635,45 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
     const bool last = l == L - 1;
     const bool more = e + 1 < total;
     const bool new_batch = last && more && ((step + 1) % p.tb) == 0;
-    const float* mod_next = (e & 1) ? P.abuf0 + p.off[0] : P.abuf1 + p.off[0];
+    const float* abn = CS_ABUF(e + 1);
     for (int s = warp; s < S; s += kCsWarps) {
-      const float* w = P.fbuf + p.off[16];
-      const float* bias = P.fbuf + p.off[17];
+      const float* w = CS_SM(fbuf) + p.off[16];
+      const float* bias = CS_SM(fbuf) + p.off[17];
       float xv[2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int o = lane + 32 * u;
-        xv[u] = 0.f;
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int o = lane + 32 * u2;
+        xv[u2] = 0.f;
         if (o < D) {
-          const float y = bias[o] + cs_dot(w + o * (F + 4), P.f + s * F, F);
-          xv[u] = P.x[s * D + o] + (mod[5 * D + o] + tmr[5 * D + o]) * y;
-          P.x[s * D + o] = xv[u];
+          const float y = bias[o] + cs_dot(w + o * (F + 4), CS_SM(f) + s * F, F);
+          xv[u2] = CS_SM(x)[s * D + o] + (mod[5 * D + o] + tmr[5 * D + o]) * y;
+          CS_SM(x)[s * D + o] = xv[u2];
         }
       }
       if (!last) {
-        cs_adaln_row(xv, P.h + s * D, mod_next, tmr, D, a.eps, 0, 1);
+        cs_adaln_row(xv, CS_SM(h) + s * D, abn + p.off[0], tmr, D, a.eps, 0, 1);
         continue;
       }
       __syncwarp();
       const float delta = a.deltas.t[step];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int o = lane + 32 * u;
+      for (int u2 = 0; u2 < 2; ++u2) {
+        const int o = lane + 32 * u2;
         if (o < A) {
-          const float vel = P.headb[o] + cs_dot(P.headw + o * (D + 4), P.x + s * D, D);
+          const float vel = CS_SM(headb)[o] + cs_dot(CS_SM(headw) + o * (D + 4), CS_SM(x) + s * D, D);
           if (a.trace != nullptr) a.trace[(static_cast<long long>(step) * a.B + b) * S * A + s * A + o] = vel;
-          const float nl = P.lat[s * A + o] + vel * delta;
-          P.lat[s * A + o] = nl;
+          const float nl = CS_SM(lat)[s * A + o] + vel * delta;
+          CS_SM(lat)[s * A + o] = nl;
           if (!more) latent[s * A + o] = nl;
         }
       }
       __syncwarp();
-      if (more && !new_batch) step_entry_row(s, step + 1, (e & 1) ? P.abuf0 : P.abuf1);
+      if (more && !new_batch) cs_step_entry_row(a, csm, s, step + 1, abn);
     }
     if (new_batch) {
       __syncthreads();
-      cs_time_batch(a, P, step + 1, min(p.tb, N - step - 1));
-      for (int s = warp; s < S; s += kCsWarps) step_entry_row(s, step + 1, (e & 1) ? P.abuf0 : P.abuf1);
+      cs_time_batch(a, csm, step + 1, min(p.tb, N - step - 1));
+      for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, step + 1, abn);
     }
   }
 }
@@ -633,86 +701,84 @@ int round4(int v) { return (v + 3) & ~3; }
 
 }  // namespace
 
-bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
-  const int S = a.S, D = a.D, A = a.A, HD = a.HD, hd = a.hd, F = a.F, C = a.C;
-  if (S < 1 || S > kCsMaxRows || D > 64 || HD > 64 || A > 64 || A < 1 || C < 1) return false;
-  if (hd != 4 && hd != 8 && hd != 16) return false;
-  if (HD % hd != 0 || D % 4 != 0 || HD % 4 != 0 || F % 4 != 0 || A % 4 != 0 || F < 4) return false;
-  if (a.freq_dim < 2 || a.freq_dim % 2 != 0 || a.num_steps < 1 || a.L < 1) return false;
-  // RoPE table rows for S positions, the latent rows, and the encoder/head
-  // weights are staged with 16-byte copies when aligned, 4-byte otherwise.
-  CaeStagePlan p;
-  memset(&p, 0, sizeof(p));
-  const int H = HD / hd;
+void cae_tensor_table(int D, int HD, int F, CaeStagePlan* p) {
   auto tensor = [&](int t, int rows, int cols, int stride, int& cursor) {
-    p.off[t] = cursor;
-    p.rows[t] = rows;
-    p.cols[t] = cols;
-    p.stride[t] = stride;
+    p->off[t] = cursor;
+    p->rows[t] = rows;
+    p->cols[t] = cols;
+    p->stride[t] = stride;
     cursor += round4(rows * stride);
   };
   int ca = 0;
-  tensor(0, 1, 6 * D, 6 * D, ca);
-  tensor(1, 3 * HD, D, D + 4, ca);
+  tensor(0, 1, 6 * D, 6 * D, ca);        // modulation
+  tensor(1, 3 * HD, D, D + 4, ca);       // qkv
   tensor(2, 1, 3 * HD, 3 * HD, ca);
-  tensor(3, 1, HD, HD, ca);
-  tensor(4, 1, HD, HD, ca);
-  tensor(5, D, HD, HD + 4, ca);
+  tensor(3, 1, HD, HD, ca);              // norm_q
+  tensor(4, 1, HD, HD, ca);              // norm_k
+  tensor(5, D, HD, HD + 4, ca);          // o
   tensor(6, 1, D, D, ca);
-  tensor(7, 1, D, D, ca);
+  tensor(7, 1, D, D, ca);                // norm3
   tensor(8, 1, D, D, ca);
-  tensor(9, HD, D, D + 4, ca);
+  tensor(9, HD, D, D + 4, ca);           // cross q
   tensor(10, 1, HD, HD, ca);
-  tensor(11, 1, HD, HD, ca);
-  tensor(12, D, HD, HD + 4, ca);
+  tensor(11, 1, HD, HD, ca);             // cross norm_q
+  tensor(12, D, HD, HD + 4, ca);         // cross o
   tensor(13, 1, D, D, ca);
   int cf = 0;
-  tensor(14, F, D, D + 4, cf);
+  tensor(14, F, D, D + 4, cf);           // ffn.0
   tensor(15, 1, F, F, cf);
-  tensor(16, D, F, F + 4, cf);
+  tensor(16, D, F, F + 4, cf);           // ffn.2
   tensor(17, 1, D, D, cf);
-  p.a_floats = ca;
-  p.f_floats = cf;
+  p->a_floats = ca;
+  p->f_floats = cf;
+}
+
+bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
+  const int S = a.S, D = a.D, A = a.A, HD = a.HD, hd = a.hd, F = a.F, C = a.C;
+  if (S < 1 || S > kCsMaxRows || D > 64 || HD > 64 || A > 64 || A < 1 || C < 1) return false;
+  if (HD / hd > kCsWarps) return false;
+  if (hd != 4 && hd != 8 && hd != 16) return false;
+  if (HD % hd != 0 || D % 4 != 0 || HD % 4 != 0 || F % 4 != 0 || A % 4 != 0 || F < 4) return false;
+  if (a.freq_dim < 2 || a.freq_dim % 2 != 0 || a.num_steps < 1 || a.L < 1) return false;
+  CaeStagePlan p;
+  memset(&p, 0, sizeof(p));
+  const int H = HD / hd;
+  cae_tensor_table(D, HD, F, &p);
   p.hdp = HD + 4;
-  p.wpq = kCsWarps / S;
   p.tb = a.num_steps < kCsMaxTb ? a.num_steps : kCsMaxTb;
-  auto layout = [&](int kc) {
-    int c = 0;
-    auto take = [&](int n) {
-      const int o = c;
-      c += round4(n);
-      return o;
-    };
-    p.kc = kc;
-    p.units_per_head = (C + kc - 1) / kc;
-    p.kv_floats = round4(kc * (hd + 4) + kc * hd);
-    p.o_abuf = take(2 * p.a_floats);
-    p.o_fbuf = take(p.f_floats);
-    p.o_kv = take(2 * p.kv_floats);
-    p.o_x = take(S * D);
-    p.o_h = take(S * D);
-    p.o_q = take(S * p.hdp);
-    p.o_k = take(S * p.hdp);
-    p.o_v = take(S * p.hdp);
-    p.o_att = take(S * p.hdp);
-    p.o_qc = take(S * p.hdp);
-    p.o_f = take(S * F);
-    p.o_part = take(S * H * p.wpq * (hd + 2));
-    p.o_tm = take(p.tb * 6 * D);
-    p.o_tscr = take(p.tb * (a.freq_dim + 2 * D));
-    p.o_lat = take(S * A);
-    p.o_rope = take(S * hd);
-    p.o_encw = take(D * (A + 4));
-    p.o_encb = take(D);
-    p.o_headw = take(A * (D + 4));
-    p.o_headb = take(A);
-    p.total_floats = c;
-    return static_cast<size_t>(c) * sizeof(float) <= static_cast<size_t>(kCsSmemLimit);
+  p.wh = kCsWarps / H;
+  p.kc = 16 * p.wh;
+  p.units = (C + p.kc - 1) / p.kc;
+  int c = 0;
+  auto take = [&](int n) {
+    const int o = c;
+    c += round4(n);
+    return o;
   };
-  // context keys per K/V unit: the largest of 512, 256, ..., 32 that fits
-  // (the whole context when it is shorter)
-  bool ok = false;
-  for (int kc0 = 512; kc0 >= 32 && !ok; kc0 >>= 1) ok = layout(kc0 < round4(C) ? kc0 : round4(C));
+  p.kv_floats = round4(p.kc * (2 * HD + 12));
+  p.o_abuf = take(2 * p.a_floats);
+  p.o_fbuf = take(p.f_floats);
+  p.o_kv = take(2 * p.kv_floats);
+  p.o_x = take(S * D);
+  p.o_h = take(S * D);
+  p.o_q = take(S * p.hdp);
+  p.o_k = take(S * p.hdp);
+  p.o_v = take(S * p.hdp);
+  p.o_att = take(S * p.hdp);
+  p.o_qc = take(S * p.hdp);
+  p.o_f = take(S * F);
+  p.o_part = take(H * p.wh * S * (hd + 2));
+  p.o_tm = take(p.tb * 6 * D);
+  p.o_tscr = take(p.tb * (a.freq_dim + 2 * D));
+  p.o_lat = take(S * A);
+  p.o_rope = take(S * hd);
+  p.o_encw = take(D * (A + 4));
+  p.o_encb = take(D);
+  p.o_headw = take(A * (D + 4));
+  p.o_headb = take(A);
+  p.o_bar = take(10);  // 5 mbarriers (8-byte aligned: every offset is a multiple of 4 floats)
+  p.total_floats = c;
+  const bool ok = static_cast<size_t>(c) * sizeof(float) <= static_cast<size_t>(kCsSmemLimit);
   if (!ok) return false;
   *out = p;
   return true;

@@ -26,41 +26,56 @@ struct CaeWeightsDev {
   CaeLayer layers[kCaeMaxLayers];
 };
 
+// Shared-memory plan of the staged step kernel (offsets in floats from the
+// dynamic shared-memory base; computed on the host by cae_staged_plan).
+constexpr int kCaeStagedTensors = 18;  // per-block tensors: 0..13 attention half, 14..17 FFN half
+constexpr int kCaeStagedHalfSplit = 14;
+struct CaeStagePlan {
+  int off[kCaeStagedTensors];      // offset inside its half (floats)
+  int rows[kCaeStagedTensors], cols[kCaeStagedTensors], stride[kCaeStagedTensors];
+  int a_floats, f_floats, kv_floats;
+  int kc;                          // context keys per K/V chunk (16 per warp of a head)
+  int units;                       // key chunks per block
+  int wh;                          // warps per head in cross attention
+  int tb;                          // t_mod rows per time-MLP batch
+  int hdp;                         // row stride of the q/k/v/attention rows
+  int o_abuf, o_fbuf, o_kv, o_x, o_h, o_q, o_k, o_v, o_att, o_qc, o_f, o_part, o_tm, o_tscr, o_lat,
+      o_rope, o_encw, o_encb, o_headw, o_headb, o_bar;
+  int total_floats;
+};
+
 struct CaeCtxArgs {
   const float* ctx_f32;            // [rows, T] (one of the two)
   const __nv_bfloat16* ctx_bf16;
   int rows, T, D, HD, L;
   const float *text0_w, *text0_b, *text2_w, *text2_b;
   CaeLayer layers[kCaeMaxLayers];
-  float* ctx_k;                    // [L, rows, HD]
-  float* ctx_v;
+  float* ctx_k;                    // [L, rows, HD], or [L, rows, HD + 4] when kv_packed
+  float* ctx_v;                    // [L, rows, HD], or [L, rows, HD + 8] when kv_packed
   float eps;
+  // split path (tk > 0): slice kernel + K/V kernel, optional weight packing
+  int B, C, H, hd;
+  int kv_packed;
+  int tk;                          // input columns per slice of text_embedding.0
+  float* part;                     // [kCaeCtxSlices, rows, D] partial sums
+  float* wpack;                    // [L, a_floats + f_floats] packed block weights, or null
+  CaeStagePlan plan;               // tensor table of the packed layout
+  int* status;                     // zeroed by the slice launch; bounded-wait failures
 };
 
-// Shared-memory plan of the staged step kernel (offsets in floats from the
-// dynamic shared-memory base; computed on the host by cae_staged_plan).
-constexpr int kCaeStagedTensors = 18;  // per-block tensors: 0..13 attention half, 14..17 FFN half
-constexpr int kCaeStagedHalfSplit = 14;
-struct CaeStagePlan {
-  int off[kCaeStagedTensors];      // offset inside its half
-  int rows[kCaeStagedTensors], cols[kCaeStagedTensors], stride[kCaeStagedTensors];
-  int a_floats, f_floats, kv_floats;
-  int kc;                          // context keys per K/V unit
-  int units_per_head;
-  int wpq;                         // warps per query row in cross attention
-  int tb;                          // t_mod rows per time-MLP batch
-  int hdp;                         // row stride of the q/k/v/attention rows
-  int o_abuf, o_fbuf, o_kv, o_x, o_h, o_q, o_k, o_v, o_att, o_qc, o_f, o_part, o_tm, o_tscr, o_lat,
-      o_rope, o_encw, o_encb, o_headw, o_headb;
-  int total_floats;
-};
+constexpr int kCaeCtxSlices = 8;    // input-column slices of text_embedding.0
+constexpr int kCaeCtxRows = 16;     // context tokens per CTA on the split path
+// Split context path eligibility (sets a.tk); false keeps the single-kernel path.
+bool cae_ctx_split_setup(CaeCtxArgs* a);
 
 struct CaeStepArgs {
   CaeWeightsDev w;
   CaeStagePlan plan;
+  const float* wpack;              // packed block weights: staged kernel when non-null
+  int* status;                     // bounded-wait failures (or null)
   const float* rope;               // [positions, hd/2, 2]
-  const float* ctx_k;              // [L, B*C, HD]
-  const float* ctx_v;
+  const float* ctx_k;              // [L, B*C, HD], or [L, B*C, HD + 4] with wpack
+  const float* ctx_v;              // [L, B*C, HD], or [L, B*C, HD + 8] with wpack
   const uint8_t* ctx_mask;         // [B, C] or null
   float* latent;                   // [B, S, A] in/out
   float* trace;                    // [N, B, S, A] or null
@@ -74,8 +89,10 @@ struct CaeStepArgs {
 cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_cae_steps(const CaeStepArgs& a, cudaStream_t st, bool pdl);
 size_t cae_smem_bytes();
-// Staged step kernel (weights and context K/V streamed through shared memory).
-// Returns false when the shapes or pointers do not fit it; the plan is then unset.
+// Packed per-block weight table (offsets, padded strides, half sizes) for D, H*d, F.
+void cae_tensor_table(int D, int HD, int F, CaeStagePlan* p);
+// Staged step kernel (packed weights and context K/V streamed through shared
+// memory by bulk copies).  Returns false when the shapes do not fit it.
 bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* plan);
 cudaError_t launch_cae_steps_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl);
 

@@ -642,7 +642,17 @@ class CAEEngine:
                                   self.ws.data_ptr(), self.ws.numel(), C.c_void_p(st)),
               "fam_cae_chunk")
         self._hold = (ctx, cm)
+        self._last = (B, C_)
         return (lat, trace) if return_trace else lat
+
+    def status(self) -> int:
+        """Status word of the last chunk (0 = every bounded device wait completed)."""
+        B, C_ = self._last
+        out = C.c_int32(0)
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        check(lib().fam_cae_status(C.byref(self.cfg), B, C_, self.ws.data_ptr(), C.byref(out), C.c_void_p(st)),
+              "fam_cae_status")
+        return out.value
 
     def denoise_step(self, latents, timestep, context, context_mask=None):
         """One model evaluation (ActionDiT.forward) -> velocity fp32 [B,S,A]."""

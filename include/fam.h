@@ -400,6 +400,12 @@ FAM_API int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w
                           float* velocity_trace, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* Status word of the last fam_cae_chunk on this workspace (synchronizes the
+ * stream): 0, or nonzero when a bounded device wait (a bulk copy that did not
+ * land within the wait limit) gave up and the outputs are not valid. */
+FAM_API int fam_cae_status(const fam_action_config* cfg, int32_t batch, int32_t context_tokens,
+                           const void* workspace, int32_t* status, void* stream);
+
 /* ======================================================================
  * Action-VAE decoder (ActionAE.decode / ActionDecoder.forward,
  * FastWAM/src/fastwam/models/action_ae.py:123-166, 184-187), fp32:

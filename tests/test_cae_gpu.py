@@ -92,15 +92,17 @@ def test_decoder_strides_and_suites(horizon, tokens, hidden, suites):
 
 
 # (hidden, heads, head_dim, ffn, layers, tokens S, context C, batch, steps, masked)
-# covers: several key chunks per head with a ragged last chunk (C=600), query rows
-# that do not divide the 32 warps (S=6), head_dim 4/8/16, odd depth, a single
-# block, more Euler steps than one t_mod batch (10), per-sample context masks,
-# and a width that falls back to the unstaged kernel (hidden 64, ffn 256).
+# covers: several key chunks with a ragged last chunk (C=600, C=77), query rows
+# that do not fill the 16-row tensor-core tile (S=6), head_dim 4/8/16, odd depth,
+# a single block, more Euler steps than one t_mod batch (10), per-sample context
+# masks, and shapes that take the unstaged kernel (hidden 64 with ffn 256, and
+# 32 action tokens).
 CAE_SHAPES = [
     (32, 4, 8, 128, 3, 6, 600, 2, 10, True),
     (16, 4, 4, 64, 1, 8, 16, 3, 5, True),
-    (32, 2, 16, 64, 2, 32, 77, 1, 3, False),
+    (32, 2, 16, 64, 2, 16, 77, 1, 3, False),
     (64, 4, 16, 256, 2, 8, 40, 2, 2, True),
+    (32, 4, 8, 128, 2, 32, 64, 1, 2, False),
 ]
 
 
@@ -130,9 +132,10 @@ def test_cae_shapes_vs_oracle(D, H, hd, F, L, S, C, B, N, masked):
         v = O.action_forward(sd, cfg, x, t.reshape(1), ctx, mask)
         vel.append(v)
         x = O.scheduler_step(v, d, x)
-    lat, trace = dit.cuda().engine().chunk(noise.cuda(), ts.tolist(), ds.tolist(), ctx.cuda(),
-                                           mask.cuda() if mask is not None else None,
-                                           return_trace=True)
+    eng = dit.cuda().engine()
+    lat, trace = eng.chunk(noise.cuda(), ts.tolist(), ds.tolist(), ctx.cuda(),
+                           mask.cuda() if mask is not None else None, return_trace=True)
     torch.cuda.synchronize()
+    assert eng.status() == 0
     _close(trace, torch.stack(vel))
     _close(lat, x)
