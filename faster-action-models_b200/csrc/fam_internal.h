@@ -46,6 +46,7 @@ struct GemmEpilogue {
   int first_frame_tokens;   // 0: a single gate row per batch
   long long gate_bstride;
   long long gate_gstride;
+  int vec;                  // set by gemm_plan: 16-feature vector path of the store / residual epilogue
 };
 
 struct GemmArgs {
@@ -63,6 +64,7 @@ struct GemmPlan {
   GemmArgs args;
   int bn;
   int splits;
+  int persist;              // persistent tile loop over min(tiles, SMs) CTAs
 };
 
 int gemm_pick_bn(int n);

@@ -50,6 +50,51 @@ __host__ __device__ constexpr uint32_t gemm_tmem_cols(int bn) {
 // b0..b0+15.
 __device__ __forceinline__ void gemm_epilogue_apply(const GemmArgs& args, const GemmEpilogue& e,
                                                     int a_row, int b0, int split, float* v) {
+  if (e.vec && e.kind == kEpiStore) {
+    // features contiguous in the output, N % 16 == 0: vector bias loads and stores
+    if (b0 >= args.N) return;
+    float bz[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) bz[j] = 0.f;
+    if (e.bias != nullptr) {
+      const uint4* bp = reinterpret_cast<const uint4*>(e.bias + b0);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 u = bp[h];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+          bz[8 * h + 2 * k] = f.x;
+          bz[8 * h + 2 * k + 1] = f.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float x = v[j] + bz[j];
+      if (e.act == kActGeluTanh) x = gelu_tanh(rbf(x));
+      else if (e.act == kActSilu) x = silu(rbf(x));
+      v[j] = x;
+    }
+    if (e.out_bf16) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(e.out) +
+                                            static_cast<long long>(a_row) * e.out_sa + b0);
+      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out) + static_cast<long long>(a_row) * e.out_sa + b0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    return;
+  }
   if (e.kind == kEpiPartial) {
     float* out = reinterpret_cast<float*>(e.out) + split * e.split_stride +
                  static_cast<long long>(a_row) * e.out_sa;
@@ -271,6 +316,285 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+
+// ------------------------------------------------------ persistent variant
+// Large problems (more output tiles than SMs, no split-K): one CTA per SM loops
+// over tiles (tile = blockIdx.x + i * gridDim.x, M-blocks fastest, so the CTAs
+// in flight share each weight n-block through L2).  Two TMEM accumulators: the
+// MMA warp fills one while the epilogue warps drain the other, so a tile's
+// epilogue overlaps the next tile's main loop; the operand ring runs on across
+// tile boundaries.
+template <int BN>
+__device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_t tacc, int a_row, int n0) {
+  const GemmEpilogue& e = args.epi;
+  const bool row_ok = a_row < args.M;
+  if (e.vec && e.kind == kEpiResidual) {
+    // out[row][f] += g[f] * act(acc + bias[f]); 16 features per TMEM load, the
+    // fp32 residual of 64 features prefetched at a time
+    float* orow = reinterpret_cast<float*>(e.out) + static_cast<long long>(row_ok ? a_row : 0) * e.out_sa;
+    const float* grow = nullptr;
+    if (e.gate_t != nullptr) {
+      const int tok = row_ok ? a_row : 0;
+      const int bi = tok / e.tokens_per_batch, within = tok - bi * e.tokens_per_batch;
+      const int grp = (e.first_frame_tokens > 0 && within >= e.first_frame_tokens) ? 1 : 0;
+      grow = e.gate_t + bi * e.gate_bstride + grp * e.gate_gstride;
+    }
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 64) {
+      float4 r[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = n0 + c0 + 4 * j;
+        r[j] = (row_ok && col < args.N) ? *reinterpret_cast<const float4*>(orow + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[16];
+        __syncwarp();
+        tmem_ld16(tacc + c0 + 16 * q, v);
+        const int b0 = n0 + c0 + 16 * q;
+        if (!row_ok || b0 >= args.N) continue;
+        float bz[16], gw[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) bz[j] = gw[j] = 0.f;
+        if (e.bias != nullptr) {
+          const uint4* bp = reinterpret_cast<const uint4*>(e.bias + b0);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint4 u = bp[h];
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+              bz[8 * h + 2 * k] = f.x;
+              bz[8 * h + 2 * k + 1] = f.y;
+            }
+          }
+        }
+        if (e.gate_w != nullptr) {
+          const uint4* gp = reinterpret_cast<const uint4*>(e.gate_w + b0);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint4 u = gp[h];
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+              gw[8 * h + 2 * k] = f.x;
+              gw[8 * h + 2 * k + 1] = f.y;
+            }
+          }
+        }
+        float g[16];
+        if (grow != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 t = *reinterpret_cast<const float4*>(grow + b0 + 4 * j);
+            g[4 * j] = t.x + gw[4 * j];
+            g[4 * j + 1] = t.y + gw[4 * j + 1];
+            g[4 * j + 2] = t.z + gw[4 * j + 2];
+            g[4 * j + 3] = t.w + gw[4 * j + 3];
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) g[j] = 1.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float x[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float t = v[4 * j + k] + bz[4 * j + k];
+            if (e.act == kActGeluTanh) t = gelu_tanh(rbf(t));
+            else if (e.act == kActSilu) t = silu(rbf(t));
+            x[k] = t;
+          }
+          const float4 rr = r[4 * q + j];
+          *reinterpret_cast<float4*>(orow + b0 + 4 * j) =
+              make_float4(rr.x + g[4 * j] * x[0], rr.y + g[4 * j + 1] * x[1], rr.z + g[4 * j + 2] * x[2],
+                          rr.w + g[4 * j + 3] * x[3]);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 16) {
+    float v[16];
+    __syncwarp();
+    tmem_ld16(tacc + c, v);
+    if (row_ok) gemm_epilogue_apply(args, e, a_row, n0 + c, 0, v);
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA,
+                                const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  constexpr int STAGES = gemm_stages(BN);
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_BYTES = BN * kBK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t ACC_COLS = gemm_tmem_cols(BN);
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;       // [2] accumulator drained (one arrival per epilogue warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (args.M + kBM - 1) / kBM;
+  const int ntiles = tiles_m * ((args.N + BN - 1) / BN);
+  const int nkb = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0 && nkb > 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      const uint64_t polA = args.a_is_const ? pol_w : pol_x;
+      const uint64_t polB = args.b_is_const ? pol_w : pol_x;
+      // first tile: constant operand of the first stages before the wait on the previous launch
+      int tile = blockIdx.x;
+      int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
+      const int pre = min(nkb, STAGES);
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* sa = smem + i * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
+        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], i * kBK, m0, polA);
+        if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], i * kBK, n0, polB);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* sa = smem + i * STAGE_BYTES;
+        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], i * kBK, m0, polA);
+        if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], i * kBK, n0, polB);
+      }
+      int kb = pre, issued = pre;
+      if (kb == nkb) {
+        kb = 0;
+        tile += gridDim.x;
+        m0 = (tile % tiles_m) * kBM;
+        n0 = (tile / tiles_m) * BN;
+      }
+      for (int it = pre; tile < ntiles; ++it) {
+        const int s = it % STAGES;
+        if (*abort_flag) break;
+        if (!mbar_wait(&empty[s], static_cast<uint32_t>(it / STAGES - 1) & 1, args.status, kErrWaitEmpty)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* sa = smem + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+        tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0, polA);
+        tma_load_2d(sa + A_BYTES, &tmB, &full[s], kb * kBK, n0, polB);
+        issued = it + 1;
+        if (++kb == nkb) {
+          kb = 0;
+          tile += gridDim.x;
+          m0 = (tile % tiles_m) * kBM;
+          n0 = (tile / tiles_m) * BN;
+        }
+      }
+      // every issued copy has landed before the CTA can exit
+      for (int j = max(0, issued - STAGES); j < issued; ++j)
+        mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1, args.status, kErrWaitFull);
+    } else if (lane == 0) {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < ntiles && nkb > 0; tile += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (*abort_flag) break;
+        if (lt >= 2 && !mbar_wait(&tempty[buf], static_cast<uint32_t>((lt >> 1) - 1) & 1, args.status,
+                                  kErrWaitAccum)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dacc = tmem_base + buf * ACC_COLS;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (*abort_flag || !mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, args.status,
+                                        kErrWaitFull)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem + s * STAGE_BYTES);
+          const uint64_t db = umma_desc_sw128(smem + s * STAGE_BYTES + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_ss(dacc, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int sp = warp & 3;  // TMEM lane quarter of this warp
+    pdl_wait();
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles && nkb > 0; tile += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      const bool ok = mbar_wait(&tfull[buf], static_cast<uint32_t>(lt >> 1) & 1, args.status, kErrWaitAccum);
+      tc_fence_after();
+      if (!ok) *abort_flag = 1;
+      if (*abort_flag) break;
+      const int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
+      gemm_tile_epilogue<BN>(args, tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16),
+                             m0 + sp * 32 + lane, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 template <int BN>
 static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
@@ -296,14 +620,55 @@ static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, 
   return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BN>, ta, tb, a);
 }
 
+template <int BN>
+static cudaError_t launch_gemm_persist_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                                          int grid, cudaStream_t stream, bool pdl) {
+  static bool attr_set = false;
+  constexpr int smem = gemm_smem_bytes(BN);
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_persist_kernel<BN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_persist_kernel<BN>, ta, tb, a);
+}
+
+static int gemm_num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
+}
+
 cudaError_t gemm_init_attributes() {
   cudaError_t e;
 #define FAM_SET(BN)                                                                          \
   e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                            gemm_smem_bytes(BN));                                             \
   if (e != cudaSuccess) return e;
-  FAM_SET(16) FAM_SET(32) FAM_SET(64) FAM_SET(128) FAM_SET(256)
+  FAM_SET(16) FAM_SET(32) FAM_SET(64) FAM_SET(128) FAM_SET(192) FAM_SET(256)
 #undef FAM_SET
+#define FAM_SETP(BN)                                                                              \
+  e = cudaFuncSetAttribute(gemm_bf16_tc_persist_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           gemm_smem_bytes(BN));                                                  \
+  if (e != cudaSuccess) return e;
+  FAM_SETP(64) FAM_SETP(128) FAM_SETP(192) FAM_SETP(256)
+#undef FAM_SETP
   return cudaSuccess;
 }
 
@@ -316,11 +681,21 @@ int gemm_pick_bn(int n) {
 }
 
 cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
+  if (p.persist > 0) {
+    switch (p.bn) {
+      case 64: return launch_gemm_persist_bn<64>(p.ta, p.tb, p.args, p.persist, stream, pdl);
+      case 128: return launch_gemm_persist_bn<128>(p.ta, p.tb, p.args, p.persist, stream, pdl);
+      case 192: return launch_gemm_persist_bn<192>(p.ta, p.tb, p.args, p.persist, stream, pdl);
+      case 256: return launch_gemm_persist_bn<256>(p.ta, p.tb, p.args, p.persist, stream, pdl);
+      default: break;
+    }
+  }
   switch (p.bn) {
     case 16: return launch_gemm_bn<16>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 32: return launch_gemm_bn<32>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 64: return launch_gemm_bn<64>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 128: return launch_gemm_bn<128>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 192: return launch_gemm_bn<192>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 256: return launch_gemm_bn<256>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
@@ -336,7 +711,25 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
     return set_error("gemm: K and row strides must be multiples of 8 elements (16 bytes)");
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return set_error("gemm: operand base addresses must be 16-byte aligned");
-  if (bn == 0) bn = gemm_pick_bn(N);
+  if (bn == 0) {
+    bn = gemm_pick_bn(N);
+    // many-tile problems: the tile width with the shortest estimated makespan
+    // (whole rounds over the SMs x tile width x relative per-column cost)
+    const int sms = gemm_num_sms(), mt = (M + kBM - 1) / kBM;
+    if (splits <= 1 && mt * ((N + 255) / 256) > sms) {
+      const int cand[3] = {256, 192, 128};
+      const double cost[3] = {1.0, 1.1, 1.3};
+      double best = 1e30;
+      for (int i = 0; i < 3; ++i) {
+        const int tiles = mt * ((N + cand[i] - 1) / cand[i]);
+        const double t = static_cast<double>((tiles + sms - 1) / sms) * cand[i] * cost[i];
+        if (t < best - 1e-9) {
+          best = t;
+          bn = cand[i];
+        }
+      }
+    }
+  }
   const int kb_total = (K + kBK - 1) / kBK;
   if (splits < 1) splits = 1;
   if (splits > kb_total) splits = kb_total;
@@ -354,6 +747,29 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
     return set_error("gemm: cuTensorMapEncodeTiled failed for B");
   p->bn = bn;
   p->splits = splits;
+  // persistent tile loop when the tiles outnumber the SMs (no split-K)
+  const int ntiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  const int sms = gemm_num_sms();
+  p->persist = (splits == 1 && bn >= 64 && ntiles > sms) ? sms : 0;
+  // 16-feature vector epilogue (residual): features contiguous in the output,
+  // 16-byte aligned rows, bias / gates / gate rows aligned for vector loads
+  {
+    GemmEpilogue& ve = p->args.epi;
+    ve = epi;
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool rows_ok = !epi.features_on_a && epi.out_sb == 1 && (N % 16) == 0 && al16(epi.out) &&
+                         (epi.bias == nullptr || al16(epi.bias));
+    if (epi.kind == kEpiResidual)
+      ve.vec = (rows_ok && (epi.out_sa % 4) == 0 && (epi.gate_w == nullptr || al16(epi.gate_w)) &&
+                (epi.gate_t == nullptr ||
+                 (al16(epi.gate_t) && (epi.gate_bstride % 4) == 0 && (epi.gate_gstride % 4) == 0)))
+                   ? 1
+                   : 0;
+    else if (epi.kind == kEpiStore)
+      ve.vec = (rows_ok && (epi.out_sa % (epi.out_bf16 ? 8 : 4)) == 0) ? 1 : 0;
+    else
+      ve.vec = 0;
+  }
   p->args.M = M;
   p->args.N = N;
   p->args.K = K;
@@ -361,7 +777,6 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
   p->args.a_is_const = a_is_const ? 1 : 0;
   p->args.b_is_const = b_is_const ? 1 : 0;
   p->args.status = status;
-  p->args.epi = epi;
   return 0;
 }
 

@@ -82,3 +82,27 @@ def test_residual_gate(fam_ops):
     tok = torch.arange(64, device="cuda")
     gate = gw.float()[None, :] + gt[tok // 32, 0]
     _close(r, r0[:64] + gate * _ref(x[:64], w, b))
+
+
+@pytest.mark.parametrize("tile_n", [0, 128, 192, 256])
+def test_persistent_residual_and_store(fam_ops, tile_n):
+    """Many-tile problems run the persistent kernel (two TMEM accumulators, vector
+    residual epilogue); tile widths 128 / 192 / 256 and the automatic choice."""
+    g = torch.Generator(device="cuda").manual_seed(11 + tile_n)
+    B, S, K, F, ff = 2, 880, 512, 3072, 352
+    x = torch.randn(B * S, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    b = torch.randn(F, device="cuda", generator=g).bfloat16()
+    gw = torch.randn(F, device="cuda", generator=g).bfloat16()
+    gt = torch.randn(B, 2, F, device="cuda", generator=g)
+    r0 = torch.randn(B * S, F, device="cuda", generator=g)
+    r = r0.clone()
+    fam_ops.gemm(x, w, bias=b, residual=r, gate_w=gw, gate_t=gt, tokens_per_batch=S,
+                 first_frame_tokens=ff, gate_batch_stride=2 * F, gate_group_stride=F, tile_n=tile_n)
+    y = fam_ops.gemm(x, w, bias=b, act="gelu_tanh", tile_n=tile_n)
+    torch.cuda.synchronize()
+    tok = torch.arange(B * S, device="cuda")
+    grp = ((tok % S) >= ff).long()
+    gate = gw.float()[None, :] + gt[tok // S, grp]
+    _close(r, r0 + gate * _ref(x, w, b))
+    _close(y, _ref(x, w, b, "gelu_tanh"))
