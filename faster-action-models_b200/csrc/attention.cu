@@ -182,41 +182,60 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
     const __nv_bfloat16* V = sV[cur];
     const uint8_t* M = sM[cur];
     const uint8_t* Km = sKm[cur];
-    // S = Q K^T for 64 keys: 8 tiles of 8 keys.
+    // S = Q K^T for 64 keys: 8 tiles of 8 keys; K fragments by ldmatrix (two
+    // 16-dim k steps per x4 load: matrices = dims +0, +8, +16, +24 of 8 keys)
     float s[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
-      const __nv_bfloat16* kr = K + (n * 8 + g) * Cfg::kRow;
+      const uint32_t kaddr = smem_u32(K + (n * 8 + (lane & 7)) * Cfg::kRow + (lane >> 3) * 8);
 #pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        uint32_t bf[2];
-        bf[0] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 2 * t);
-        bf[1] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 8 + 2 * t);
-        mma_bf16_16816(s[n], qf[kk], bf);
+      for (int kk = 0; kk < KS; kk += 2) {
+        uint32_t b4[4];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(b4[0]), "=r"(b4[1]), "=r"(b4[2]), "=r"(b4[3])
+                     : "r"(kaddr + kk * 32));
+        mma_bf16_16816(s[n], qf[kk], b4);
+        mma_bf16_16816(s[n], qf[kk + 1], b4 + 2);
       }
     }
-    // scale + mask, row max
+    // scale + mask, row max.  A block every row of the tile sees whole (no
+    // explicit or key mask, inside the key range, outside the first-frame rule)
+    // skips the per-element tests.
     float mx0 = -INFINITY, mx1 = -INFINITY;
     const int r0 = warp * 16 + g, r1 = r0 + 8;  // rows inside the tile
+    const bool whole = !use_m2 && !use_km && j0 + kAttnKB <= k_end && (ff == 0 || q0 >= ff || j0 + kAttnKB <= ff);
+    if (whole) {
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 8; ++n) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int jj = n * 8 + 2 * t + e;
-        const int j = j0 + jj;
-        bool kv_ok = j < k_end;
-        if (use_km) kv_ok = kv_ok && Km[jj] != 0;
-        bool ok0 = kv_ok && qr0 < a.Sq && (ff == 0 || qr0 >= ff || j < ff);
-        bool ok1 = kv_ok && qr1 < a.Sq && (ff == 0 || qr1 >= ff || j < ff);
-        if (use_m2) {
-          ok0 = ok0 && M[r0 * kAttnKB + jj] != 0;
-          ok1 = ok1 && M[r1 * kAttnKB + jj] != 0;
+        for (int e = 0; e < 2; ++e) {
+          s[n][e] *= a.scale_log2;
+          s[n][2 + e] *= a.scale_log2;
+          mx0 = fmaxf(mx0, s[n][e]);
+          mx1 = fmaxf(mx1, s[n][2 + e]);
         }
-        s[n][e] = ok0 ? s[n][e] * a.scale_log2 : -INFINITY;
-        s[n][2 + e] = ok1 ? s[n][2 + e] * a.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[n][e]);
-        mx1 = fmaxf(mx1, s[n][2 + e]);
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int jj = n * 8 + 2 * t + e;
+          const int j = j0 + jj;
+          bool kv_ok = j < k_end;
+          if (use_km) kv_ok = kv_ok && Km[jj] != 0;
+          bool ok0 = kv_ok && qr0 < a.Sq && (ff == 0 || qr0 >= ff || j < ff);
+          bool ok1 = kv_ok && qr1 < a.Sq && (ff == 0 || qr1 >= ff || j < ff);
+          if (use_m2) {
+            ok0 = ok0 && M[r0 * kAttnKB + jj] != 0;
+            ok1 = ok1 && M[r1 * kAttnKB + jj] != 0;
+          }
+          s[n][e] = ok0 ? s[n][e] * a.scale_log2 : -INFINITY;
+          s[n][2 + e] = ok1 ? s[n][2 + e] * a.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, s[n][e]);
+          mx1 = fmaxf(mx1, s[n][2 + e]);
+        }
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -360,7 +379,7 @@ __global__ void __launch_bounds__(WARPS * 32) attention_kernel(const AttnArgs a)
 
 // Query-tile width used for a launch: 32 queries for small query counts (the
 // action tokens), 64 otherwise.
-static int attn_warps(int Sq) { return Sq <= 32 ? 2 : 4; }
+static int attn_warps(int Sq) { return Sq <= 32 ? 2 : (Sq < 512 ? 4 : 8); }
 
 size_t attn_partial_bytes(int B, int H, int Sq, int head_dim, int nsplit) {
   if (nsplit <= 1) return 0;
@@ -413,7 +432,8 @@ cudaError_t attn_init_attributes() {
                                          AttnCfg<HD, W>::kBytes);                             \
     if (e != cudaSuccess) return e;                                                           \
   }
-  FAM_ATTN_ATTR(64, 2) FAM_ATTN_ATTR(64, 4) FAM_ATTN_ATTR(128, 2) FAM_ATTN_ATTR(128, 4)
+  FAM_ATTN_ATTR(64, 2) FAM_ATTN_ATTR(64, 4) FAM_ATTN_ATTR(64, 8) FAM_ATTN_ATTR(128, 2) FAM_ATTN_ATTR(128, 4)
+  FAM_ATTN_ATTR(128, 8)
 #undef FAM_ATTN_ATTR
   return cudaSuccess;
 }
@@ -425,9 +445,13 @@ cudaError_t launch_attention(const AttnArgs& a, int B, int head_dim, cudaStream_
     if (e != cudaSuccess) return e;
     attrs = true;
   }
-  const bool small = attn_warps(a.Sq) == 2;
-  if (head_dim == 64) return small ? launch_attn_cfg<64, 2>(a, B, st, pdl) : launch_attn_cfg<64, 4>(a, B, st, pdl);
-  if (head_dim == 128) return small ? launch_attn_cfg<128, 2>(a, B, st, pdl) : launch_attn_cfg<128, 4>(a, B, st, pdl);
+  const int w = attn_warps(a.Sq);
+  if (head_dim == 64)
+    return w == 2 ? launch_attn_cfg<64, 2>(a, B, st, pdl)
+                  : (w == 4 ? launch_attn_cfg<64, 4>(a, B, st, pdl) : launch_attn_cfg<64, 8>(a, B, st, pdl));
+  if (head_dim == 128)
+    return w == 2 ? launch_attn_cfg<128, 2>(a, B, st, pdl)
+                  : (w == 4 ? launch_attn_cfg<128, 4>(a, B, st, pdl) : launch_attn_cfg<128, 8>(a, B, st, pdl));
   return cudaErrorInvalidValue;
 }
 
