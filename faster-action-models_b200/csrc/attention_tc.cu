@@ -1,0 +1,394 @@
+// tcgen05 flash attention for long self attention (the backbone prefill:
+// SDPA with the first-frame-causal rule, FastWAM/src/fastwam/models/wan22/
+// wan_video_dit.py:13-22 and :514-518), head_dim 128.
+//
+// One CTA = 128 queries of one (batch, head).  Warp roles (256 threads):
+//   warp 0      TMA producer: the Q tile once, then 128-key blocks of K and of
+//               V^T into a two-stage ring (128-byte swizzle, K-major);
+//   warp 1      allocates TMEM and (lane 0) issues tcgen05.mma:
+//                 S_j = Q K_j^T  into TMEM columns [128 (j % 2), +128),
+//                 O  += P_j V_j  into TMEM columns [256, 384),
+//               S_{j+1} is issued before waiting for P_j, so the scores of the
+//               next block are computed while the softmax of this one runs;
+//   warps 4..7  softmax, one thread per query row (TMEM lane = row): load the
+//               row of S_j, mask, online max / sum in exp2 form, write P_j as
+//               bf16 into a swizzled shared tile (the A operand of the P.V
+//               MMA), rescale the O row in TMEM when the row max moved, and at
+//               the end divide by the row sum and store the output row.
+// V arrives transposed ([dims, keys], written by vt_transpose_kernel) so every
+// MMA operand is K-major.  Tiles wholly inside the first frame stop at the
+// first-frame keys; keys past the batch's tokens and the first-frame rule are
+// masked per element.  Every wait is bounded (status word, then the CTA
+// drains its copies and frees TMEM).
+#include "fam_common.cuh"
+#include "fam_internal.h"
+#include "fam_kernels.h"
+
+namespace fam {
+
+namespace {
+
+constexpr int kTcThreads = 256;
+constexpr int kTcRows = 128;                      // queries per CTA, keys per block, head dim
+constexpr int kTcChunk = kTcRows * 128;           // 128 rows x 128 bytes (64 bf16): one swizzle-atom column
+constexpr int kTcSmem = 12 * kTcChunk + 1024 + 256;  // Q 2 | K 2x2 | V^T 2x2 | P 2 chunks, align slack, barriers
+constexpr uint32_t kTcTmemCols = 512;
+constexpr int kErrTcWait = 0x4154;
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// V [B*S, ld] (head h at columns h*128..) -> V^T [(b*H + h)*128 + d, S_pad]; keys
+// in [S, S_pad) are written as zeros.  CTA = 64 keys of one (batch, head).
+__global__ void __launch_bounds__(256) vt_transpose_kernel(const __nv_bfloat16* __restrict__ v, long long ld,
+                                                           __nv_bfloat16* __restrict__ vt, int S, int S_pad, int H) {
+  __shared__ __nv_bfloat16 tile[64][kTcRows + 2];
+  const int t0 = blockIdx.x * 64, h = blockIdx.y, b = blockIdx.z;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int idx = threadIdx.x; idx < 64 * (kTcRows / 8); idx += 256) {
+    const int t = idx / (kTcRows / 8), c = idx % (kTcRows / 8);
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (t0 + t < S) u = *reinterpret_cast<const uint4*>(v + (static_cast<long long>(b) * S + t0 + t) * ld + h * kTcRows + c * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tile[t][c * 8 + i] = e[i];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < kTcRows * 8; idx += 256) {
+    const int d = idx / 8, c = idx % 8;
+    if (t0 + c * 8 >= S_pad) continue;
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 p;
+      p.x = tile[c * 8 + 2 * i][d];
+      p.y = tile[c * 8 + 2 * i + 1][d];
+      w[i] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(vt + (static_cast<long long>(b) * H + h) * kTcRows * S_pad + static_cast<long long>(d) * S_pad +
+                              t0 + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __grid_constant__ AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = sm;
+  uint8_t* sK = sm + 2 * kTcChunk;   // stage s at + 2 * s * kTcChunk
+  uint8_t* sV = sm + 6 * kTcChunk;
+  uint8_t* sP = sm + 10 * kTcChunk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 12 * kTcChunk);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // 4 softmax warps
+  uint64_t* pv_done = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = blockIdx.x * kTcRows;
+  const int S = a.S;
+  const int kend = (a.ff > 0 && q0 + kTcRows <= a.ff) ? a.ff : S;  // tiles inside the first frame
+  const int nb = (kend + kTcRows - 1) / kTcRows;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&a.tq);
+    tma_prefetch_desc(&a.tk);
+    tma_prefetch_desc(&a.tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();  // Q, K and V^T come from earlier launches
+      const uint64_t pol = policy_evict_last();
+      const int row_q = b * S + q0;
+      mbar_arrive_expect_tx(q_full, 2 * kTcChunk);
+      tma_load_2d(sQ, &a.tq, q_full, h * kTcRows, row_q, pol);
+      tma_load_2d(sQ + kTcChunk, &a.tq, q_full, h * kTcRows + 64, row_q, pol);
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j & 1;
+        if (*abort_flag) break;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], static_cast<uint32_t>((j >> 1) - 1) & 1, a.status, kErrTcWait)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], 4 * kTcChunk);
+        uint8_t* k_dst = sK + 2 * s * kTcChunk;
+        uint8_t* v_dst = sV + 2 * s * kTcChunk;
+        tma_load_2d(k_dst, &a.tk, &kv_full[s], h * kTcRows, b * S + j * kTcRows, pol);
+        tma_load_2d(k_dst + kTcChunk, &a.tk, &kv_full[s], h * kTcRows + 64, b * S + j * kTcRows, pol);
+        tma_load_2d(v_dst, &a.tv, &kv_full[s], j * kTcRows, (b * a.H + h) * kTcRows, pol);
+        tma_load_2d(v_dst + kTcChunk, &a.tv, &kv_full[s], j * kTcRows + 64, (b * a.H + h) * kTcRows, pol);
+        issued = j + 1;
+      }
+      // every issued copy has landed before the CTA can exit
+      mbar_wait(q_full, 0, a.status, kErrTcWait);
+      for (int j = max(0, issued - 2); j < issued; ++j)
+        mbar_wait(&kv_full[j & 1], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTcRows, kTcRows);
+      bool ok = mbar_wait(q_full, 0, a.status, kErrTcWait);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTcRows / 16; ++kk) {
+          const uint64_t da = umma_desc_sw128(sQ + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+          const uint64_t db = umma_desc_sw128(sK + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+          umma_bf16_ss(tmem_base + (j & 1) * kTcRows, da, db, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok && nb > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < nb; ++j) {
+        if (*abort_flag) break;
+        // S_{j+1} goes to the buffer of S_{j-1}, whose softmax published P_{j-1}
+        if (j + 1 < nb && !issue_s(j + 1)) break;
+        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1, a.status, kErrTcWait)) break;
+        tc_fence_after();
+        const int s = j & 1;
+#pragma unroll
+        for (int kk = 0; kk < kTcRows / 16; ++kk) {
+          const uint64_t da = umma_desc_sw128(sP + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+          const uint64_t db = umma_desc_sw128(sV + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+          umma_bf16_ss(tmem_base + 2 * kTcRows, da, db, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[s]);
+        umma_commit(pv_done);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp >= 4) {
+    pdl_wait();  // the output rows are read by the previous layer's launches
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const int qrow = q0 + r;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);
+    const bool first_frame_row = a.ff > 0 && qrow < a.ff;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb && ok; ++j) {
+      // warp-uniform outcome of every wait: the TMEM loads and stores below are warp-collective
+      const bool got = mbar_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait);
+      if (!__all_sync(0xffffffffu, got)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[kTcRows];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + (j & 1) * kTcRows + 32 * c, sv + 32 * c);
+      tmem_wait_ld();
+      const int j0 = j * kTcRows;
+      const int lim = first_frame_row ? min(kend, a.ff) : kend;  // keys this row may see
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTcRows; ++c) {
+        sv[c] = (j0 + c < lim) ? sv[c] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[c]);
+      }
+      const float mn = fmaxf(m, mx);
+      const float base = mn == -INFINITY ? 0.f : mn;
+      const float alpha = exp2f(m - base);
+      m = mn;
+      uint32_t pk[kTcRows / 2];
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < kTcRows; c += 2) {
+        const float p0 = exp2f(sv[c] - base), p1 = exp2f(sv[c + 1] - base);
+        ps += p0 + p1;
+        pk[c / 2] = pack2_bf16(p0, p1);
+      }
+      l = l * alpha + ps;
+      // P_{j-1} and O: the previous P.V must be complete before they change
+      if (j > 0) {
+        const bool done = mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1, a.status, kErrTcWait);
+        if (!__all_sync(0xffffffffu, done)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (!__all_sync(0xffffffffu, alpha == 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(lane_addr + 2 * kTcRows + 32 * c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(lane_addr + 2 * kTcRows + 32 * c, ov);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> the swizzled A tile: 16-byte unit u of row r sits at u ^ (r % 8)
+#pragma unroll
+      for (int u = 0; u < kTcRows / 8; ++u) {
+        const int chunk = u >> 3, uu = u & 7;
+        uint4* dst = reinterpret_cast<uint4*>(sP + chunk * kTcChunk + r * 128 + ((uu ^ (r & 7)) << 4));
+        *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool fin = ok && nb > 0 && mbar_wait(pv_done, static_cast<uint32_t>(nb - 1) & 1, a.status, kErrTcWait);
+    if (__all_sync(0xffffffffu, fin)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = a.out + (static_cast<long long>(b) * S + qrow) * a.out_ts + h * kTcRows;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(lane_addr + 2 * kTcRows + 32 * c, ov);
+        tmem_wait_ld();
+        if (qrow < S) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(orow + 32 * c)[i] =
+                make_uint4(pack2_bf16(ov[8 * i] * inv, ov[8 * i + 1] * inv), pack2_bf16(ov[8 * i + 2] * inv, ov[8 * i + 3] * inv),
+                           pack2_bf16(ov[8 * i + 4] * inv, ov[8 * i + 5] * inv), pack2_bf16(ov[8 * i + 6] * inv, ov[8 * i + 7] * inv));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+}
+
+}  // namespace
+
+size_t attention_tc_vt_bytes(int B, int H, int S) {
+  const size_t S_pad = static_cast<size_t>((S + 63) / 64 * 64);
+  return static_cast<size_t>(B) * H * kTcRows * S_pad * sizeof(__nv_bfloat16);
+}
+
+bool attention_tc_eligible(int head_dim, int Sq, int S1, int S2, bool masks, long long q_ts, long long kv_ts,
+                           long long out_ts) {
+  return head_dim == kTcRows && S2 == 0 && !masks && Sq == S1 && Sq >= 512 && (q_ts % 8) == 0 && (kv_ts % 8) == 0 &&
+         (out_ts % 8) == 0;
+}
+
+cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int H, int ff,
+                                float scale_log2, __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int S_pad = (S + 63) / 64 * 64;
+  cudaLaunchAttribute attr_l[1];
+  attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_l[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S_pad / 64, H, B);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cfg.attrs = attr_l;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v, kv_ts, vt, S, S_pad, H);
+    if (e != cudaSuccess) return e;
+  }
+  AttnTcArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!make_tmap_bf16_2d(&a.tq, q, static_cast<uint64_t>(B) * S, static_cast<uint64_t>(H) * kTcRows,
+                         static_cast<uint64_t>(q_ts), kTcRows) ||
+      !make_tmap_bf16_2d(&a.tk, k, static_cast<uint64_t>(B) * S, static_cast<uint64_t>(H) * kTcRows,
+                         static_cast<uint64_t>(kv_ts), kTcRows) ||
+      !make_tmap_bf16_2d(&a.tv, vt, static_cast<uint64_t>(B) * H * kTcRows, static_cast<uint64_t>(S_pad),
+                         static_cast<uint64_t>(S_pad), kTcRows))
+    return cudaErrorInvalidValue;
+  a.out = out;
+  a.out_ts = out_ts;
+  a.B = B;
+  a.S = S;
+  a.H = H;
+  a.ff = ff;
+  a.scale_log2 = scale_log2;
+  a.status = status;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((S + kTcRows - 1) / kTcRows, H, B);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = st;
+  cfg.attrs = attr_l;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel, a);
+}
+
+}  // namespace fam

@@ -67,6 +67,26 @@ struct GemmPlan {
   int persist;              // persistent tile loop over min(tiles, SMs) CTAs
 };
 
+// tcgen05 flash attention for long self attention (head_dim 128, one key source,
+// no explicit / key masks; the first-frame-causal rule is supported).
+struct AttnTcArgs {
+  CUtensorMap tq;             // Q  [B*S, H*128]
+  CUtensorMap tk;             // K  [B*S, H*128]
+  CUtensorMap tv;             // V^T [B*H*128, S_pad]
+  __nv_bfloat16* out;         // [B*S, out_ts]
+  long long out_ts;
+  int B, S, H, ff;
+  float scale_log2;
+  int* status;
+};
+bool attention_tc_eligible(int head_dim, int Sq, int S1, int S2, bool masks, long long q_ts, long long kv_ts,
+                           long long out_ts);
+size_t attention_tc_vt_bytes(int B, int H, int S);
+// Transposes V into `vt` (attention_tc_vt_bytes) and runs the attention.
+cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int H, int ff,
+                                float scale_log2, __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl);
+
 int gemm_pick_bn(int n);
 int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M, int N,
               int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,

@@ -32,7 +32,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
 
 struct VLayout {
-  size_t x, h, qkv, q, ao, qc, ci, fh, patch, tmod, sin, th1, th2, cemb, ch1, ckv, apart, ctr;
+  size_t x, h, qkv, q, ao, qc, ci, fh, patch, tmod, sin, th1, th2, cemb, ch1, ckv, apart, ctr, vt;
   size_t total;
 };
 
@@ -66,6 +66,7 @@ VLayout vlayout(const fam_video_config& c, int B, int S, int C) {
   // attention runs unsplit at these query counts; a small area for safety
   w.apart = take(attn_partial_bytes(B, c.num_heads, S, c.head_dim, 1));
   w.ctr = take(static_cast<size_t>(B) * c.num_heads * attn_query_tiles(S) * 4);
+  w.vt = take(attention_tc_vt_bytes(B, c.num_heads, S));  // V^T of the tcgen05 self attention
   w.total = off;
   return w;
 }
@@ -291,7 +292,14 @@ int enqueue_prefill(const VCtx& c) {
     aa.keys_per_split = S;
     aa.part = wp<float>(c, c.L.apart);
     aa.counters = wp<int>(c, c.L.ctr);
-    V_LAUNCH(launch_attention(aa, B, g.head_dim, c.st, c.pdl));
+    if (attention_tc_eligible(g.head_dim, S, S, 0, false, aa.q_ts, aa.kv1_ts, aa.out_ts)) {
+      V_LAUNCH(launch_attention_tc(aa.q, aa.q_ts, aa.k1, aa.v1, aa.kv1_ts, aa.out, aa.out_ts, B, S, g.num_heads,
+                                   aa.first_frame_tokens, aa.scale_log2, wp<__nv_bfloat16>(c, c.L.vt), c.e->status,
+                                   c.st, c.pdl));
+      ++c.e->launch_count;  // V^T transpose + attention
+    } else {
+      V_LAUNCH(launch_attention(aa, B, g.head_dim, c.st, c.pdl));
+    }
     V_TRYI(gemm_x(c, aa.out, HD, M, ly.o_w, ly.o_b, D, HD, kEpiResidual, kActNone, x, D, true,
                   ly.modulation, 2));
     // norm3 + cross attention (no gate)

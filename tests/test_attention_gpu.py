@@ -48,3 +48,23 @@ def test_first_frame_causal_and_key_mask(fam_ops):
     ref2 = torch.cat([_ref(q[:1], k[:1], v[:1], H), _ref(q[1:], k[1:, :250], v[1:, :250], H)])
     torch.cuda.synchronize()
     assert (out2.float() - ref2).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,S,H,ff", [(1, 1760, 4, 352), (2, 700, 3, 176), (1, 512, 2, 0), (2, 1000, 2, 0)])
+def test_tcgen05_self_attention(fam_ops, B, S, H, ff):
+    """Long self attention (one key source, head_dim 128) runs the tcgen05 kernel
+    (TMEM scores and output, V transposed once); ragged last tiles, several
+    batches and the first-frame-causal rule."""
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + S + ff)
+    HD = H * 128
+    q = torch.randn(B, S, HD, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, S, HD, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, S, HD, device="cuda", generator=g).bfloat16()
+    out = fam_ops.attention(q, k, v, H, first_frame_tokens=ff)
+    torch.cuda.synchronize()
+    mask = torch.ones(S, S, dtype=torch.bool, device="cuda")
+    if ff:
+        mask[:ff, ff:] = False
+    ref = _ref(q, k, v, H, mask)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
