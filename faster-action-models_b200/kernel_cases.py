@@ -1,12 +1,16 @@
 """Fixed single-GPU workloads of the library's kernels, for profilers.
 
-    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,attn_c2,cae_c0} [repeats]
+    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,attn_c2,cae_c0,prefill_c2,dit4dit_c3} [repeats]
 
 Each case runs its library call `repeats` times (default 3) on cuda:0 and
 synchronizes; under ncu, skip the warm-up launches with `-s`.
   gemm_qkv_c2  ops.gemm: [1760, 3072] x [9216, 3072]^T + bias (backbone qkv, config 2)
   attn_c2      ops.attention: 1760 tokens, 24 heads x 128, first-frame-causal (352)
   cae_c0       CAEEngine.chunk + ActionAE.decode of BASELINE config 0
+  prefill_c2   WanVideoDiT.prefill of BASELINE config 2 (30 blocks, 1,760 tokens, batch 1)
+  dit4dit_c3   DiT4DiTPipeline of BASELINE config 3 (backbone to block 18 of 28 at 3,520
+               tokens + 16-block action head, 4 Euler steps, batch 1); prints the
+               p50 chunk latency over the repeats
 """
 import importlib
 import sys
@@ -17,6 +21,7 @@ import torch
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 ops = importlib.import_module("faster-action-models_b200.ops")
 M = importlib.import_module("faster-action-models_b200.models")
+P = importlib.import_module("faster-action-models_b200.pipeline")
 
 
 def main(case: str, reps: int) -> None:
@@ -43,6 +48,43 @@ def main(case: str, reps: int) -> None:
         eng = dit.engine()
         for _ in range(reps):
             ae.decode(eng.chunk(noise, ts, ds, ctx))
+    elif case == "prefill_c2":
+        with torch.device(dev):
+            vid = M.WanVideoDiT(hidden_dim=3072, in_dim=48, ffn_dim=14336, out_dim=48, text_dim=4096, freq_dim=256,
+                                eps=1e-6, patch_size=(1, 2, 2), num_heads=24, attn_head_dim=128, num_layers=30,
+                                has_image_input=False, seperated_timestep=True,
+                                video_attention_mask_mode="first_frame_causal")
+        vid = vid.to(torch.bfloat16)
+        lat = torch.randn(1, 48, 5, 32, 44, device=dev).bfloat16()
+        ctx = torch.randn(1, 64, 4096, device=dev).bfloat16()
+        cm = torch.ones(1, 64, dtype=torch.bool, device=dev)
+        t = torch.full((1,), 500.0).bfloat16()
+        for _ in range(reps):
+            vid.prefill(lat, t, ctx, cm)
+    elif case == "dit4dit_c3":
+        with torch.device(dev):
+            vid = M.WanVideoDiT(hidden_dim=2048, in_dim=48, ffn_dim=8192, out_dim=48, text_dim=4096, freq_dim=256,
+                                eps=1e-6, patch_size=(1, 2, 2), num_heads=16, attn_head_dim=128, num_layers=28,
+                                has_image_input=False, seperated_timestep=True,
+                                video_attention_mask_mode="first_frame_causal")
+            head = M.ActionDiT(1024, 29, 4096, 2048, 256, 1e-6, 16, 64, 16)
+        vid, head = vid.to(torch.bfloat16), head.to(torch.bfloat16)
+        pipe = P.DiT4DiTPipeline(vid, head, extract_layer=17, num_steps=4, shift=1.0, micro_batch=1)
+        g = torch.Generator().manual_seed(0)
+        lat = torch.randn(1, 48, 4, 44, 80, generator=g).bfloat16().to(dev)
+        ctx = torch.randn(1, 64, 4096, generator=g).bfloat16().to(dev)
+        noise = torch.randn(1, 16, 29, generator=g).to(dev)
+        t = torch.full((1,), 500.0).bfloat16()
+        times = []
+        for _ in range(reps + 2):
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            pipe(lat, t, ctx, None, noise)
+            e0.record()
+            torch.cuda.synchronize()
+            times.append(s0.elapsed_time(e0))
+        times = sorted(times[2:])
+        print("dit4dit_c3 chunk ms p50", round(times[len(times) // 2], 3))
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()

@@ -13,12 +13,19 @@ CAEPipeline is BASELINE config 4: the video backbone forward once per chunk,
 the compact action expert cross-attending the backbone's final token states,
 and the Action-VAE decoder, over a batch of independent rollouts processed in
 micro-batches.
+
+DiT4DiTPipeline is BASELINE config 3 (the DiT4DiT world action model restated
+with the FastWAM classes): the backbone runs only up to its feature block (tail
+elision, `elide_backbone`) and a flow-matching action head cross-attends that
+block's token states.
 """
 from __future__ import annotations
 
+import copy
 from typing import Optional, Sequence
 
 import torch
+from torch import nn
 
 from .models import ActionAE, ActionDiT, WanVideoDiT, build_inference_schedule
 
@@ -130,4 +137,78 @@ class CAEPipeline:
             lat = self.expert.engine().chunk(noise[s:e].to(hidden.device, torch.float32),
                                              self.ts, self.ds, hidden)
             outs.append(self.ae.decode(lat))
+        return torch.cat(outs)
+
+
+def elide_backbone(video: WanVideoDiT, extract_layer: int) -> WanVideoDiT:
+    """A WanVideoDiT that shares `video`'s parameters but holds blocks 0..extract_layer
+    only: its prefill returns the token states after block `extract_layer` (the
+    feature hook of DiT4DiT, Cosmos25.py:152-171 with extract_layer 17 in
+    DiT4DiT/config/libero/dit4dit_libero.yaml:14), and the later blocks never run."""
+    if not 0 <= extract_layer < video.num_layers:
+        raise ValueError(f"extract_layer {extract_layer} outside 0..{video.num_layers - 1}")
+    el = copy.copy(video)
+    el._modules = dict(video._modules)
+    el._modules["blocks"] = nn.ModuleList(list(video.blocks)[:extract_layer + 1])
+    el._engine = None
+    return el
+
+
+class DiT4DiTPipeline:
+    """backbone features at `extract_layer` -> flow-matching action head
+    (ActionDiT cross-attending the features, no video cache) over `num_steps` Euler steps
+    -> optional Action-VAE decode, in micro-batches.
+
+    A compact head (hidden <= 64) runs the fp32 compact engine and denoises action
+    latents for the decoder; a wide head runs the bf16 action-expert engine and
+    returns the denoised chunk itself (decoded when `ae` is given)."""
+
+    def __init__(self, video: WanVideoDiT, head: ActionDiT, extract_layer: int,
+                 ae: Optional[ActionAE] = None, num_steps: int = 4, shift: float = 1.0,
+                 micro_batch: int = 16):
+        if head.text_dim != video.hidden_dim:
+            raise ValueError("the head's text_dim must equal the backbone hidden width")
+        self.backbone = elide_backbone(video, extract_layer)
+        self.head, self.ae = head, ae
+        self.ts, self.ds = build_inference_schedule(num_steps, shift, dtype=torch.float32)
+        self.micro_batch = micro_batch
+        self._bufs = {}
+
+    def _buffers(self, b: int, S: int, dev):
+        key = (b, S)
+        if key not in self._bufs:
+            v = self.backbone
+            HD = v.num_heads * v.attn_head_dim
+            ks = [torch.empty(b, S, HD, dtype=torch.bfloat16, device=dev) for _ in range(v.num_layers)]
+            vs = [torch.empty(b, S, HD, dtype=torch.bfloat16, device=dev) for _ in range(v.num_layers)]
+            hid = torch.empty(b, S, v.hidden_dim, dtype=torch.float32, device=dev)
+            self._bufs[key] = (ks, vs, hid)
+        return self._bufs[key]
+
+    @torch.no_grad()
+    def __call__(self, latents: torch.Tensor, timestep, context: torch.Tensor,
+                 context_mask: Optional[torch.Tensor], noise: torch.Tensor) -> torch.Tensor:
+        """latents [B, in, F, H, W], noise [B, Sa, A] -> fp32 [B, Sa, A] (or decoded actions)."""
+        B = latents.shape[0]
+        t = timestep if torch.is_tensor(timestep) else torch.full((B,), float(timestep))
+        t = t.reshape(-1)
+        if t.numel() == 1:
+            t = t.expand(B)
+        pt, ph, pw = self.backbone.patch_size
+        S = (latents.shape[2] // pt) * (latents.shape[3] // ph) * (latents.shape[4] // pw)
+        outs = []
+        for s in range(0, B, self.micro_batch):
+            e = min(B, s + self.micro_batch)
+            cm = context_mask[s:e] if context_mask is not None else None
+            ks, vs, hid = self._buffers(e - s, S, latents.device)
+            _, _, feats = self.backbone.engine().prefill(latents[s:e], t[s:e], context[s:e], cm,
+                                                         return_hidden=True, cache_k=ks, cache_v=vs,
+                                                         hidden=hid)
+            if self.head.is_compact():
+                lat = self.head.engine().chunk(noise[s:e].to(feats.device, torch.float32),
+                                               self.ts, self.ds, feats)
+            else:
+                lat = self.head.engine().chunk(noise[s:e].to(feats.device, torch.bfloat16),
+                                               self.ts, self.ds, feats).float()
+            outs.append(self.ae.decode(lat) if self.ae is not None else lat)
         return torch.cat(outs)

@@ -97,3 +97,24 @@ def test_library_loads_and_exports_every_declared_symbol():
         assert hasattr(lib, n), f"{n} declared in include/fam.h but not exported"
     fam = importlib.import_module("faster-action-models_b200")
     assert fam.version()[0] == 0
+
+
+def test_elide_backbone_shares_parameters():
+    """DiT4DiT tail elision: the elided backbone holds blocks 0..k of the original module
+    (the same parameter tensors) and leaves the original untouched."""
+    P = importlib.import_module("faster-action-models_b200.pipeline")
+    Mm = importlib.import_module("faster-action-models_b200.models")
+    vid = Mm.WanVideoDiT(hidden_dim=64, in_dim=4, ffn_dim=128, out_dim=4, text_dim=32, freq_dim=256, eps=1e-6,
+                         patch_size=(1, 2, 2), num_heads=2, attn_head_dim=32, num_layers=4,
+                         has_image_input=False)
+    el = P.elide_backbone(vid, 1)
+    assert el.num_layers == 2 and vid.num_layers == 4
+    full = dict(vid.named_parameters())
+    for name, p in el.named_parameters():
+        assert p is full[name]
+    names = {n for n, _ in el.named_parameters()}
+    assert not any(n.startswith(("blocks.2.", "blocks.3.")) for n in names)
+    assert any(n.startswith("blocks.1.") for n in names)
+    import pytest as _pt
+    with _pt.raises(ValueError):
+        P.elide_backbone(vid, 4)

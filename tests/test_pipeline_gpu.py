@@ -102,3 +102,54 @@ def test_cae_pipeline_microbatched():
     assert torch.equal(got, got2)
     err = (got - ref).abs().max().item()
     assert err <= 2e-2 * max(1.0, ref.abs().max().item()) and _cos(got, ref) >= 0.999, err
+
+
+@pytest.mark.parametrize("compact", [False, True])
+def test_dit4dit_pipeline(compact):
+    """BASELINE config 3 at reduced width: backbone features at block 1 of 3 (tail
+    elision), a flow-matching head cross-attending them (wide bf16 head returning
+    the chunk, or a compact fp32 head + Action-VAE decode), 4 Euler steps."""
+    D, H, hd, L, T, Cin, k = 256, 2, 128, 3, 64, 16, 1
+    vid = _video(D, H, hd, 512, T, L, Cin, 3).to(torch.bfloat16)
+    torch.manual_seed(7)
+    if compact:
+        head = M.ActionDiT(hidden_dim=32, action_dim=48, ffn_dim=128, text_dim=D, freq_dim=256, eps=1e-6,
+                           num_heads=4, attn_head_dim=8, num_layers=2)
+        ae = M.ActionAE(M.ActionAEConfig(action_dim=29, action_horizon=16, num_tokens=8, latent_dim=48,
+                                         decoder_hidden=64, video_cond_dim=0))
+        Sa, A = 8, 48
+    else:
+        head = M.ActionDiT(hidden_dim=128, action_dim=29, ffn_dim=256, text_dim=D, freq_dim=256, eps=1e-6,
+                           num_heads=2, attn_head_dim=64, num_layers=2).to(torch.bfloat16)
+        ae, Sa, A = None, 16, 29
+    B = 3
+    g = torch.Generator().manual_seed(8)
+    lat = torch.randn(B, Cin, 3, 8, 12, generator=g).bfloat16()
+    ctx = torch.randn(B, 6, T, generator=g).bfloat16()
+    cm = torch.ones(B, 6, dtype=torch.bool)
+    noise = torch.randn(B, Sa, A, generator=g)
+    t = torch.full((B,), 500.0).bfloat16()
+    vcfg = O.DiTConfig(hidden_dim=D, ffn_dim=512, num_heads=H, attn_head_dim=hd, num_layers=k + 1,
+                       text_dim=T, in_dim=Cin, out_dim=Cin)
+    hcfg = O.DiTConfig(hidden_dim=head.hidden_dim, ffn_dim=head.ffn_dim, num_heads=head.num_heads,
+                       attn_head_dim=head.attn_head_dim, num_layers=head.num_layers, text_dim=D, action_dim=A)
+    vsd = {kk: v.float() for kk, v in vid.state_dict().items()}
+    hsd = {kk: v.float() for kk, v in head.state_dict().items()}
+    tok, _, tmod, cemb, cmask, freqs, _, tpf = O.video_prepare(vsd, vcfg, lat.float(), t.float(),
+                                                               ctx.float(), cm)
+    _, _, feats = O.prefill_video_cache(vsd, vcfg, tok, freqs, tmod, cemb, cmask,
+                                        O.build_video_to_video_mask(tok.shape[1], tpf), return_hidden=True)
+    ts, ds = O.build_inference_schedule(4, 1.0, dtype=torch.float32)
+    x = noise.clone()
+    for tt, dd in zip(ts, ds):
+        x = O.scheduler_step(O.action_forward(hsd, hcfg, x, tt.reshape(1), feats), dd, x)
+    ref = x
+    if ae is not None:
+        ref = O.action_decode({kk: v.float() for kk, v in ae.state_dict().items()},
+                              O.DecoderConfig(29, 16, 8, 48, 64), x)
+    pipe = P.DiT4DiTPipeline(vid.cuda(), head.cuda(), extract_layer=k, ae=ae.cuda() if ae is not None else None,
+                             num_steps=4, shift=1.0, micro_batch=2)
+    got = pipe(lat.cuda(), t, ctx.cuda(), cm.cuda(), noise.cuda()).cpu()
+    assert got.shape == ref.shape
+    err = (got - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()) and _cos(got, ref) >= 0.999, err
