@@ -251,7 +251,7 @@ struct CsFlash {
       for (int e2 = 0; e2 < 2; ++e2) {
         const int j = n0 + 2 * t + e2;
         const bool valid = j < nk && (kmask == nullptr || kmask[j] != 0);
-        sc[nt][e2] = valid ? sc[nt][e2] * scale : -INFINITY;
+        sc[nt][e2] = valid ? sc[nt][e2] * scale : -INFINITY;  // scale includes log2(e): exp2 form
         sc[nt][2 + e2] = valid ? sc[nt][2 + e2] * scale : -INFINITY;
       }
     }
@@ -262,14 +262,14 @@ struct CsFlash {
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float al0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0);
-    const float al1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
+    const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
       for (int e2 = 0; e2 < 2; ++e2) {
-        sc[nt][e2] = sc[nt][e2] == -INFINITY ? 0.f : expf(sc[nt][e2] - mn0);
-        sc[nt][2 + e2] = sc[nt][2 + e2] == -INFINITY ? 0.f : expf(sc[nt][2 + e2] - mn1);
+        sc[nt][e2] = sc[nt][e2] == -INFINITY ? 0.f : exp2f(sc[nt][e2] - mn0);
+        sc[nt][2 + e2] = sc[nt][2 + e2] == -INFINITY ? 0.f : exp2f(sc[nt][2 + e2] - mn1);
       }
     }
     l0 = l0 * al0 + ((sc[0][0] + sc[0][1]) + (sc[1][0] + sc[1][1]));
@@ -369,8 +369,8 @@ __device__ __forceinline__ void cs_wait(const CaeStepArgs& a, float* csm, int i,
 // Block-0 entry of a step for token row s (one warp): encoder from the latent,
 // then AdaLN 1 with the attention half `abuf`.
 __device__ __forceinline__ void cs_step_entry_row(const CaeStepArgs& a, float* csm, int s, int step,
-                                                  const float* abuf) {
-  const int lane = threadIdx.x & 31, D = a.D, A = a.A;
+                                                  const float* abuf, int D, int A) {
+  const int lane = threadIdx.x & 31;
   const float* tmr = CS_SM(tm) + (step % a.plan.tb) * 6 * D;
   float xv[2];
 #pragma unroll
@@ -385,20 +385,24 @@ __device__ __forceinline__ void cs_step_entry_row(const CaeStepArgs& a, float* c
   cs_adaln_row(xv, CS_SM(h) + s * D, abuf + a.plan.off[0], tmr, D, a.eps, 0, 1);
 }
 
-template <int HDIM>
+// FD, FHD, FF, FA, FS: compile-time hidden width, H*d, FFN width, latent width and
+// token count of a specialised instance (0 = read from the arguments): with
+// constant widths every dot product and row reduction unrolls completely.
+template <int HDIM, int FD, int FHD, int FF, int FA, int FS>
 __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const __grid_constant__ CaeStepArgs a) {
   extern __shared__ __align__(16) float csm[];
   const CaeStagePlan& p = a.plan;
   const int b = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int S = a.S, D = a.D, A = a.A, HD = a.HD, H = HD / HDIM, F = a.F, L = a.L, N = a.num_steps, C = a.C;
-  const int hdp = p.hdp, kc = p.kc;
+  const int S = FS ? FS : a.S, D = FD ? FD : a.D, A = FA ? FA : a.A, HD = FHD ? FHD : a.HD, H = HD / HDIM;
+  const int F = FF ? FF : a.F, L = a.L, N = a.num_steps, C = a.C;
+  const int hdp = FHD ? FHD + 4 : p.hdp, kc = p.kc;
   const float scale = rsqrtf(static_cast<float>(HDIM));
+  const float scale_log2 = scale * 1.4426950408889634f;  // softmax in exp2 form
   const uint8_t* kmask = a.ctx_mask != nullptr ? a.ctx_mask + static_cast<long long>(b) * C : nullptr;
   float* latent = a.latent + static_cast<long long>(b) * S * A;
   const int U = p.units;
   const int total = N * L;
-  const int blk_floats = p.a_floats + p.f_floats;
 
   // ---- prologue: barriers, constant tensors, first t_mod batch, block 0 weights
   if (tid == 0) {
@@ -430,7 +434,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
   cs_wait(a, csm, 0, 0);
   __syncthreads();
 
-  for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, 0, CS_ABUF(0));
+  for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, 0, CS_ABUF(0), D, A);
 
   for (int e = 0; e < total; ++e) {
     const int step = e / L, l = e - step * L;
@@ -496,10 +500,10 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
           d = fmaf(qq.z, kk.z, d);
           d = fmaf(qq.w, kk.w, d);
         }
-        scv = d * scale;
+        scv = d * scale_log2;
       }
       const float mx = warp_max(scv);
-      const float pj = lane < S ? expf(scv - mx) : 0.f;
+      const float pj = lane < S ? exp2f(scv - mx) : 0.f;
       const float den = warp_sum(pj);
       float acc = 0.f;
       const int d = lane % HDIM;
@@ -568,7 +572,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
         if (act) {
           const int j0 = u * kc;
           fl.chunk(CS_KV(g), kc, HD, min(kc, C - j0), slot * 16, hh, CS_SM(qc), hdp, S,
-                   kmask != nullptr ? kmask + j0 : nullptr, scale);
+                   kmask != nullptr ? kmask + j0 : nullptr, scale_log2);
         }
       }
       if (act) fl.store(CS_SM(part) + (hh * wh + slot) * S * (HDIM + 2), S);
@@ -591,7 +595,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
             for (int sl = 0; sl < p.wh; ++sl) {
               const float* q = pp + sl * pst;
               if (q[0] == -INFINITY) continue;
-              const float fct = expf(q[0] - mx);
+              const float fct = exp2f(q[0] - mx);  // slice maxima are in the log2 domain
               den = fmaf(fct, q[1], den);
               num = fmaf(fct, q[2 + d], num);
             }
@@ -668,21 +672,21 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
         }
       }
       __syncwarp();
-      if (more && !new_batch) cs_step_entry_row(a, csm, s, step + 1, abn);
+      if (more && !new_batch) cs_step_entry_row(a, csm, s, step + 1, abn, D, A);
     }
     if (new_batch) {
       __syncthreads();
       cs_time_batch(a, csm, step + 1, min(p.tb, N - step - 1));
-      for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, step + 1, abn);
+      for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, step + 1, abn, D, A);
     }
   }
 }
 
-template <int HDIM>
+template <int HDIM, int FD, int FHD, int FF, int FA, int FS>
 cudaError_t launch_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
+  auto kern = cae_steps_staged_kernel<HDIM, FD, FHD, FF, FA, FS>;
   const size_t smem = static_cast<size_t>(a.plan.total_floats) * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(cae_steps_staged_kernel<HDIM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B);
@@ -694,7 +698,7 @@ cudaError_t launch_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, cae_steps_staged_kernel<HDIM>, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 int round4(int v) { return (v + 3) & ~3; }
@@ -785,10 +789,13 @@ bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
 }
 
 cudaError_t launch_cae_steps_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
+  // BASELINE config 0 shape (hidden 32, 4 x 8 heads, FFN 128, 16 latent dims, 8 tokens)
+  if (a.hd == 8 && a.D == 32 && a.HD == 32 && a.F == 128 && a.A == 16 && a.S == 8)
+    return launch_staged<8, 32, 32, 128, 16, 8>(a, st, pdl);
   switch (a.hd) {
-    case 4: return launch_staged<4>(a, st, pdl);
-    case 8: return launch_staged<8>(a, st, pdl);
-    default: return launch_staged<16>(a, st, pdl);
+    case 4: return launch_staged<4, 0, 0, 0, 0, 0>(a, st, pdl);
+    case 8: return launch_staged<8, 0, 0, 0, 0, 0>(a, st, pdl);
+    default: return launch_staged<16, 0, 0, 0, 0, 0>(a, st, pdl);
   }
 }
 
