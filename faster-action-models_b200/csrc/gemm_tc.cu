@@ -345,10 +345,12 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int col = n0 + c0 + 4 * j;
-        r[j] = (row_ok && col < args.N) ? *reinterpret_cast<const float4*>(orow + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+        r[j] = (row_ok && c0 + 4 * j < BN && col < args.N) ? *reinterpret_cast<const float4*>(orow + col)
+                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
+        if (c0 + 16 * q >= BN) break;  // tile widths that are not a multiple of 64
         float v[16];
         __syncwarp();
         tmem_ld16(tacc + c0 + 16 * q, v);
@@ -661,13 +663,13 @@ cudaError_t gemm_init_attributes() {
   e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                            gemm_smem_bytes(BN));                                             \
   if (e != cudaSuccess) return e;
-  FAM_SET(16) FAM_SET(32) FAM_SET(64) FAM_SET(128) FAM_SET(192) FAM_SET(256)
+  FAM_SET(16) FAM_SET(32) FAM_SET(64) FAM_SET(128) FAM_SET(160) FAM_SET(192) FAM_SET(256)
 #undef FAM_SET
 #define FAM_SETP(BN)                                                                              \
   e = cudaFuncSetAttribute(gemm_bf16_tc_persist_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                            gemm_smem_bytes(BN));                                                  \
   if (e != cudaSuccess) return e;
-  FAM_SETP(64) FAM_SETP(128) FAM_SETP(192) FAM_SETP(256)
+  FAM_SETP(64) FAM_SETP(128) FAM_SETP(160) FAM_SETP(192) FAM_SETP(256)
 #undef FAM_SETP
   return cudaSuccess;
 }
@@ -685,6 +687,7 @@ cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
     switch (p.bn) {
       case 64: return launch_gemm_persist_bn<64>(p.ta, p.tb, p.args, p.persist, stream, pdl);
       case 128: return launch_gemm_persist_bn<128>(p.ta, p.tb, p.args, p.persist, stream, pdl);
+      case 160: return launch_gemm_persist_bn<160>(p.ta, p.tb, p.args, p.persist, stream, pdl);
       case 192: return launch_gemm_persist_bn<192>(p.ta, p.tb, p.args, p.persist, stream, pdl);
       case 256: return launch_gemm_persist_bn<256>(p.ta, p.tb, p.args, p.persist, stream, pdl);
       default: break;
@@ -695,6 +698,7 @@ cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
     case 32: return launch_gemm_bn<32>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 64: return launch_gemm_bn<64>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 128: return launch_gemm_bn<128>(p.ta, p.tb, p.args, p.splits, stream, pdl);
+    case 160: return launch_gemm_bn<160>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 192: return launch_gemm_bn<192>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     case 256: return launch_gemm_bn<256>(p.ta, p.tb, p.args, p.splits, stream, pdl);
     default: return cudaErrorInvalidValue;
@@ -713,17 +717,18 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
     return set_error("gemm: operand base addresses must be 16-byte aligned");
   if (bn == 0) {
     bn = gemm_pick_bn(N);
-    // many-tile problems: the tile width with the shortest estimated makespan
-    // (whole rounds over the SMs x tile width x relative per-column cost)
+    // many-tile problems: the tile width with the shortest estimated makespan,
+    // whole rounds over the SMs x per-tile time; the per-tile time measured on
+    // B200 for 128-row tiles grows as (BN + 340) (operand rows streamed per
+    // k-block plus a fixed per-k-block cost, fitted over BN = 128..256)
     const int sms = gemm_num_sms(), mt = (M + kBM - 1) / kBM;
     if (splits <= 1 && mt * ((N + 255) / 256) > sms) {
-      const int cand[3] = {256, 192, 128};
-      const double cost[3] = {1.0, 1.1, 1.3};
-      double best = 1e30;
-      for (int i = 0; i < 3; ++i) {
-        const int tiles = mt * ((N + cand[i] - 1) / cand[i]);
-        const double t = static_cast<double>((tiles + sms - 1) / sms) * cand[i] * cost[i];
-        if (t < best - 1e-9) {
+      const int cand[4] = {256, 192, 160, 128};
+      long long best = -1;
+      for (int i = 0; i < 4; ++i) {
+        const long long tiles = static_cast<long long>(mt) * ((N + cand[i] - 1) / cand[i]);
+        const long long t = ((tiles + sms - 1) / sms) * (cand[i] + 340);
+        if (best < 0 || t < best) {
           best = t;
           bn = cand[i];
         }

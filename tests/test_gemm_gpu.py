@@ -84,10 +84,10 @@ def test_residual_gate(fam_ops):
     _close(r, r0[:64] + gate * _ref(x[:64], w, b))
 
 
-@pytest.mark.parametrize("tile_n", [0, 128, 192, 256])
+@pytest.mark.parametrize("tile_n", [0, 128, 160, 192, 256])
 def test_persistent_residual_and_store(fam_ops, tile_n):
     """Many-tile problems run the persistent kernel (two TMEM accumulators, vector
-    residual epilogue); tile widths 128 / 192 / 256 and the automatic choice."""
+    residual epilogue); tile widths 128 / 160 / 192 / 256 and the automatic choice."""
     g = torch.Generator(device="cuda").manual_seed(11 + tile_n)
     B, S, K, F, ff = 2, 880, 512, 3072, 352
     x = torch.randn(B * S, K, device="cuda", generator=g).bfloat16()
