@@ -40,6 +40,7 @@ constexpr int kCsMaxTb = 8;       // t_mod rows per time-MLP batch
 constexpr int kCsMaxRows = 16;    // token rows (one 16-row tensor-core tile)
 constexpr int kCsSmemLimit = 227 * 1024;
 constexpr int kCsErrWait = 0x4341;  // a bulk copy did not complete within the wait limit
+constexpr int kCsMaxCluster = 4;    // CTAs per sample sharing the cross-attention key chunks
 
 __device__ __forceinline__ void cs_cp4(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -349,12 +350,16 @@ __device__ __forceinline__ void cs_issue_f(const CaeStepArgs& a, float* csm, int
   mbar_arrive_expect_tx(bar, a.plan.f_floats * 4);
   cs_bulk(CS_SM(fbuf), a.wpack + static_cast<long long>(e % a.L) * blk + a.plan.a_floats, a.plan.f_floats * 4, bar);
 }
+// K/V chunk g of this CTA's sequence: block g / ur, its (g % ur)-th chunk, i.e.
+// key chunk rank + (g % ur) * nc of the block (chunks are dealt round-robin over
+// the nc CTAs of the sample's cluster).
 template <int HDIM>
-__device__ __forceinline__ void cs_issue_kv(const CaeStepArgs& a, float* csm, int g) {
-  const int U = a.plan.units, kc = a.plan.kc, HD = a.HD;
-  const int e = g / U, u = g - e * U, l = e % a.L;
+__device__ __forceinline__ void cs_issue_kv(const CaeStepArgs& a, float* csm, int g, int b, int rank, int ur) {
+  const int nc = a.plan.nc, kc = a.plan.kc, HD = a.HD;
+  const int e = g / ur, i = g - e * ur, l = e % a.L;
+  const int u = rank + i * nc;
   const int j0 = u * kc, nk = min(kc, a.C - j0);
-  const long long row = (static_cast<long long>(l) * a.B + blockIdx.x) * a.C + j0;
+  const long long row = (static_cast<long long>(l) * a.B + b) * a.C + j0;
   const uint32_t kbytes = static_cast<uint32_t>(nk * (HD + 4) * 4), vbytes = static_cast<uint32_t>(nk * (HD + 8) * 4);
   uint64_t* bar = CS_BAR(3 + (g & 1));
   float* buf = CS_KV(g);
@@ -392,7 +397,9 @@ template <int HDIM, int FD, int FHD, int FF, int FA, int FS>
 __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const __grid_constant__ CaeStepArgs a) {
   extern __shared__ __align__(16) float csm[];
   const CaeStagePlan& p = a.plan;
-  const int b = blockIdx.x;
+  const int nc = p.nc;                                     // CTAs of the sample's cluster
+  const int b = blockIdx.x / nc;
+  const int rank = nc > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = FS ? FS : a.S, D = FD ? FD : a.D, A = FA ? FA : a.A, HD = FHD ? FHD : a.HD, H = HD / HDIM;
   const int F = FF ? FF : a.F, L = a.L, N = a.num_steps, C = a.C;
@@ -402,11 +409,13 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
   const uint8_t* kmask = a.ctx_mask != nullptr ? a.ctx_mask + static_cast<long long>(b) * C : nullptr;
   float* latent = a.latent + static_cast<long long>(b) * S * A;
   const int U = p.units;
+  const int ur = (U - rank + nc - 1) / nc;  // key chunks of each block handled by this CTA
   const int total = N * L;
 
   // ---- prologue: barriers, constant tensors, first t_mod batch, block 0 weights
   if (tid == 0) {
     for (int i = 0; i < 5; ++i) mbar_init(CS_BAR(i), 1);
+    for (int i = 5; i < 7; ++i) mbar_init(CS_BAR(i), nc);  // slice exchange, one arrival per CTA
     fence_mbar_init();
   }
   cs_stage(CS_SM(encw), a.w.enc_w, D, A, A + 4);
@@ -417,6 +426,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
   cs_stage(CS_SM(lat), latent, 1, S * A, S * A);
   cp_async_commit();
   __syncthreads();
+  if (nc > 1) cluster_barrier();  // every CTA's exchange barriers are initialised before any peer arrives
   cs_time_batch(a, csm, 0, min(p.tb, N));
   // K/V buffers start at zero: rows past a short last chunk are read by the
   // tensor-core tiles (their scores are masked, and 0 * finite stays 0)
@@ -427,7 +437,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
   if (tid == 0) {
     cs_issue_a(a, csm, 0);
     cs_issue_f(a, csm, 0);
-    cs_issue_kv<HDIM>(a, csm, 0);
+    cs_issue_kv<HDIM>(a, csm, 0, b, rank, ur);
   }
   pdl_launch_dependents();
   cp_async_wait<0>();
@@ -558,24 +568,70 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
     }
 
     // ---- cross attention: key chunks of all heads; warp = (head, 16 keys of the
-    // chunk), tensor-core scores and P.V with a running softmax across chunks
+    // chunk), tensor-core scores and P.V with a running softmax across chunks.
+    // The chunks of a block are dealt over the nc CTAs of the sample's cluster.
     {
       const int wh = p.wh, hh = warp / wh, slot = warp - hh * wh;
       const bool act = hh < H;
       CsFlash<HDIM> fl;
       fl.init();
-      for (int u = 0; u < U; ++u) {
-        const int g = e * U + u;
+      for (int i = 0; i < ur; ++i) {
+        const int g = e * ur + i;
         cs_wait(a, csm, 3 + (g & 1), (g >> 1) & 1);
         __syncthreads();  // chunk g landed; every warp is done with chunk g - 1 (the other buffer)
-        if (tid == 0 && g + 1 < total * U) cs_issue_kv<HDIM>(a, csm, g + 1);
+        if (tid == 0 && g + 1 < total * ur) cs_issue_kv<HDIM>(a, csm, g + 1, b, rank, ur);
         if (act) {
-          const int j0 = u * kc;
+          const int j0 = (rank + i * nc) * kc;
           fl.chunk(CS_KV(g), kc, HD, min(kc, C - j0), slot * 16, hh, CS_SM(qc), hdp, S,
                    kmask != nullptr ? kmask + j0 : nullptr, scale_log2);
         }
       }
       if (act) fl.store(CS_SM(part) + (hh * wh + slot) * S * (HDIM + 2), S);
+    }
+    __syncthreads();
+    // merge the wh key slices of each (head, row) into one partial (m, l, o) and
+    // publish it to slot `rank` of every cluster CTA's exchange buffer
+    {
+      const int par = e & 1, row_f = HDIM + 2;
+      float* xp = CS_SM(xpart) + (par * nc + rank) * H * S * row_f;
+      for (int t = tid; t < H * S * row_f; t += kCsThreads) {
+        const int j = t % row_f, hs = t / row_f, hh = hs / S, s2 = hs - hh * S;
+        const float* pp = CS_SM(part) + (hh * p.wh * S + s2) * row_f;
+        const int pst = S * row_f;
+        float mx = -INFINITY;
+        for (int sl = 0; sl < p.wh; ++sl) mx = fmaxf(mx, pp[sl * pst]);
+        float v = mx;
+        if (j > 0) {
+          v = 0.f;
+          if (mx != -INFINITY)
+            for (int sl = 0; sl < p.wh; ++sl) {
+              const float* q = pp + sl * pst;
+              if (q[0] != -INFINITY) v = fmaf(exp2f(q[0] - mx), q[j], v);  // slice maxima: log2 domain
+            }
+        }
+        if (nc == 1) {
+          xp[t] = v;
+        } else {
+          for (int r2 = 0; r2 < nc; ++r2) st_cluster_f32(cluster_map(xp + t, r2), v);
+        }
+      }
+      if (nc > 1) {
+        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+        __syncthreads();
+        if (tid == 0)
+          for (int r2 = 0; r2 < nc; ++r2) mbar_arrive_cluster(cluster_map(CS_BAR(5 + par), r2));
+        // every CTA's slices of this block have landed (bounded wait)
+        const uint32_t want = static_cast<uint32_t>(e >> 1) & 1;
+        if (!mbar_try_wait_cluster(CS_BAR(5 + par), want)) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait_cluster(CS_BAR(5 + par), want)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              record_error(a.status, kCsErrWait);
+              break;
+            }
+          }
+        }
+      }
     }
     __syncthreads();
 
@@ -586,16 +642,17 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
         const int o = lane + 32 * u2;
         if (o < HD) {
           const int hh = o / HDIM, d = o - hh * HDIM;
-          const float* pp = CS_SM(part) + (hh * p.wh * S + s) * (HDIM + 2);
-          const int pst = S * (HDIM + 2);  // next slot of the same head
+          const int row_f = HDIM + 2;
+          const float* pp = CS_SM(xpart) + ((e & 1) * nc * H * S + hh * S + s) * row_f;
+          const int pst = H * S * row_f;  // next cluster rank
           float mx = -INFINITY;
-          for (int sl = 0; sl < p.wh; ++sl) mx = fmaxf(mx, pp[sl * pst]);
+          for (int r2 = 0; r2 < nc; ++r2) mx = fmaxf(mx, pp[r2 * pst]);
           float num = 0.f, den = 0.f;
           if (mx != -INFINITY) {
-            for (int sl = 0; sl < p.wh; ++sl) {
-              const float* q = pp + sl * pst;
+            for (int r2 = 0; r2 < nc; ++r2) {
+              const float* q = pp + r2 * pst;
               if (q[0] == -INFINITY) continue;
-              const float fct = exp2f(q[0] - mx);  // slice maxima are in the log2 domain
+              const float fct = exp2f(q[0] - mx);  // maxima in the log2 domain
               den = fmaf(fct, q[1], den);
               num = fmaf(fct, q[2 + d], num);
             }
@@ -665,10 +722,10 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
         const int o = lane + 32 * u2;
         if (o < A) {
           const float vel = CS_SM(headb)[o] + cs_dot(CS_SM(headw) + o * (D + 4), CS_SM(x) + s * D, D);
-          if (a.trace != nullptr) a.trace[(static_cast<long long>(step) * a.B + b) * S * A + s * A + o] = vel;
+          if (a.trace != nullptr && rank == 0) a.trace[(static_cast<long long>(step) * a.B + b) * S * A + s * A + o] = vel;
           const float nl = CS_SM(lat)[s * A + o] + vel * delta;
           CS_SM(lat)[s * A + o] = nl;
-          if (!more) latent[s * A + o] = nl;
+          if (!more && rank == 0) latent[s * A + o] = nl;
         }
       }
       __syncwarp();
@@ -680,6 +737,7 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
       for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, step + 1, abn, D, A);
     }
   }
+  if (nc > 1) cluster_barrier();  // no CTA leaves while a peer could still address its shared memory
 }
 
 template <int HDIM, int FD, int FHD, int FF, int FA, int FS>
@@ -689,15 +747,19 @@ cudaError_t launch_staged(const CaeStepArgs& a, cudaStream_t st, bool pdl) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.B);
+  cfg.gridDim = dim3(a.B * a.plan.nc);
   cfg.blockDim = dim3(kCsThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.plan.nc;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
@@ -753,6 +815,7 @@ bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
   p.wh = kCsWarps / H;
   p.kc = 16 * p.wh;
   p.units = (C + p.kc - 1) / p.kc;
+  p.nc = p.units < kCsMaxCluster ? p.units : kCsMaxCluster;
   int c = 0;
   auto take = [&](int n) {
     const int o = c;
@@ -772,6 +835,7 @@ bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
   p.o_qc = take(S * p.hdp);
   p.o_f = take(S * F);
   p.o_part = take(H * p.wh * S * (hd + 2));
+  p.o_xpart = take(2 * p.nc * H * S * (hd + 2));  // [block parity][cluster rank][H][S][m, l, o]
   p.o_tm = take(p.tb * 6 * D);
   p.o_tscr = take(p.tb * (a.freq_dim + 2 * D));
   p.o_lat = take(S * A);
@@ -780,7 +844,7 @@ bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {
   p.o_encb = take(D);
   p.o_headw = take(A * (D + 4));
   p.o_headb = take(A);
-  p.o_bar = take(10);  // 5 mbarriers (8-byte aligned: every offset is a multiple of 4 floats)
+  p.o_bar = take(14);  // 7 mbarriers (8-byte aligned: every offset is a multiple of 4 floats)
   p.total_floats = c;
   const bool ok = static_cast<size_t>(c) * sizeof(float) <= static_cast<size_t>(kCsSmemLimit);
   if (!ok) return false;

@@ -36,10 +36,11 @@ struct CaeStagePlan {
   int a_floats, f_floats, kv_floats;
   int kc;                          // context keys per K/V chunk (16 per warp of a head)
   int units;                       // key chunks per block
+  int nc;                          // CTAs per sample (a thread-block cluster): chunks dealt round-robin
   int wh;                          // warps per head in cross attention
   int tb;                          // t_mod rows per time-MLP batch
   int hdp;                         // row stride of the q/k/v/attention rows
-  int o_abuf, o_fbuf, o_kv, o_x, o_h, o_q, o_k, o_v, o_att, o_qc, o_f, o_part, o_tm, o_tscr, o_lat,
+  int o_abuf, o_fbuf, o_kv, o_x, o_h, o_q, o_k, o_v, o_att, o_qc, o_f, o_part, o_xpart, o_tm, o_tscr, o_lat,
       o_rope, o_encw, o_encb, o_headw, o_headb, o_bar;
   int total_floats;
 };
