@@ -176,13 +176,19 @@ __device__ void dl_build_input(const DecLayerArgs& a, float* x, float* stat) {
   const int b = blockIdx.y, h = a.h, Lin = a.Lin, n = h * Lin;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (a.in_mode == 0) {
+    // input_proj: the token rows of z first (shared), then one output per thread;
+    // the weight row of each output is read with independent loads
+    float* zs = stat + 16;  // [Lin][Z] (the stat area is followed by room for it)
+    for (int i = threadIdx.x; i < Lin * a.Z; i += kDlThreads) zs[i] = a.z[static_cast<long long>(b) * Lin * a.Z + i];
+    __syncthreads();
     const int sid = (a.suite_ids != nullptr && a.suite_embed != nullptr) ? a.suite_ids[b] : -1;
     for (int i = threadIdx.x; i < n; i += kDlThreads) {
       const int c = i / Lin, t = i - c * Lin;
       float acc = a.in_b[c];
-      const float* zr = a.z + (static_cast<long long>(b) * Lin + t) * a.Z;
+      const float* zr = zs + t * a.Z;
       const float* wr = a.in_w + static_cast<long long>(c) * a.Z;
-      for (int k = 0; k < a.Z; ++k) acc += wr[k] * zr[k];
+#pragma unroll 8
+      for (int k = 0; k < a.Z; ++k) acc += __ldg(wr + k) * zr[k];
       if (sid >= 0) acc += a.suite_embed[static_cast<long long>(sid) * h + c];
       x[i] = acc;
     }
@@ -190,13 +196,11 @@ __device__ void dl_build_input(const DecLayerArgs& a, float* x, float* stat) {
     return;
   }
   const float* src = a.src + static_cast<long long>(b) * n;
-  for (int i = threadIdx.x * 4; i < n; i += kDlThreads * 4) {
-    if (i + 4 <= n) {
-      *reinterpret_cast<float4*>(x + i) = *reinterpret_cast<const float4*>(src + i);
-    } else {
-      for (int j = i; j < n; ++j) x[j] = src[j];
-    }
-  }
+  const float* res = a.in_mode == 2 ? a.resid + static_cast<long long>(b) * n : nullptr;
+  // n % 4 == 0 (h % 4 == 0): independent float4 loads, all in flight at once
+#pragma unroll 8
+  for (int i = threadIdx.x * 4; i < n; i += kDlThreads * 4)
+    *reinterpret_cast<float4*>(x + i) = __ldg(reinterpret_cast<const float4*>(src + i));
   __syncthreads();
   // GroupNorm statistics: warp per group, two passes over shared memory
   const int gsz = (h / a.G) * Lin;
@@ -218,15 +222,19 @@ __device__ void dl_build_input(const DecLayerArgs& a, float* x, float* stat) {
   }
   __syncthreads();
   const int cg = h / a.G;
-  const float* res = a.in_mode == 2 ? a.resid + static_cast<long long>(b) * n : nullptr;
-  for (int i = threadIdx.x; i < n; i += kDlThreads) {
-    const int c = i / Lin, g = c / cg;
-    float y = (x[i] - stat[2 * g]) * stat[2 * g + 1] * a.gn_w[c] + a.gn_b[c];
-    if (a.in_mode == 1)
-      y = silu(y);
-    else
-      y += res[i];
-    x[i] = y;
+#pragma unroll 4
+  for (int i = threadIdx.x * 4; i < n; i += kDlThreads * 4) {
+    const int c = i / Lin, g = c / cg;  // Lin % 4 == 0: the four values share a channel
+    const float m = stat[2 * g], r = stat[2 * g + 1], w = a.gn_w[c], bb = a.gn_b[c];
+    float4 y = *reinterpret_cast<const float4*>(x + i);
+    y = make_float4((y.x - m) * r * w + bb, (y.y - m) * r * w + bb, (y.z - m) * r * w + bb, (y.w - m) * r * w + bb);
+    if (a.in_mode == 1) {
+      y = make_float4(silu(y.x), silu(y.y), silu(y.z), silu(y.w));
+    } else {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(res + i));
+      y = make_float4(y.x + q.x, y.y + q.y, y.z + q.z, y.w + q.w);
+    }
+    *reinterpret_cast<float4*>(x + i) = y;
   }
   __syncthreads();
   if (a.xsave != nullptr) {
@@ -236,7 +244,7 @@ __device__ void dl_build_input(const DecLayerArgs& a, float* x, float* stat) {
   }
 }
 
-// dynamic smem: x[h * Lin] | w[kDlCo][h][K] | part[kDlThreads] | stat[16]
+// dynamic smem: x[h * Lin] | w[kDlCo][h][K] | part[kDlThreads] | stat[16] | z rows
 __global__ void __launch_bounds__(kDlThreads) dec_layer_kernel(const __grid_constant__ DecLayerArgs a) {
   extern __shared__ __align__(16) float dsm[];
   const int h = a.h, Lin = a.Lin, Lout = a.Lout;
@@ -247,12 +255,29 @@ __global__ void __launch_bounds__(kDlThreads) dec_layer_kernel(const __grid_cons
   float* part = w + kDlCo * h * K;
   float* stat = part + kDlThreads;
   const int co0 = blockIdx.x * kDlCo;
-  // weight slice -> w[co_l][ci][k] (weights are never written by a launch)
-  for (int i = threadIdx.x; i < kDlCo * h * K; i += kDlThreads) {
-    const int col = i / (h * K), r = i - col * h * K, ci = r / K, k = r - ci * K;
-    const float* src = a.transposed ? a.w + (static_cast<long long>(ci) * h + co0 + col) * K + k
-                                    : a.w + (static_cast<long long>(co0 + col) * h + ci) * K + k;
-    dl_cp4(w + i, src);
+  // weight slice -> w[co_l][ci][k] (weights are never written by a launch):
+  // 16-byte copies when the runs are aligned (Conv1d: one run of h*3 per output
+  // channel; ConvTranspose1d: a run of K per (input, output channel))
+  const bool al16 = (reinterpret_cast<uintptr_t>(a.w) & 15) == 0;
+  if (al16 && !a.transposed && (h * K) % 4 == 0) {
+    const int per = h * K / 4;
+    for (int i = threadIdx.x; i < kDlCo * per; i += kDlThreads) {
+      const int col = i / per, r = i - col * per;
+      cp_async16(w + col * h * K + 4 * r, a.w + (static_cast<long long>(co0 + col) * h) * K + 4 * r, true);
+    }
+  } else if (al16 && a.transposed && K % 4 == 0) {
+    const int per = K / 4;
+    for (int i = threadIdx.x; i < kDlCo * h * per; i += kDlThreads) {
+      const int q = i % per, cc = i / per, col = cc % kDlCo, ci = cc / kDlCo;
+      cp_async16(w + (col * h + ci) * K + 4 * q, a.w + (static_cast<long long>(ci) * h + co0 + col) * K + 4 * q, true);
+    }
+  } else {
+    for (int i = threadIdx.x; i < kDlCo * h * K; i += kDlThreads) {
+      const int col = i / (h * K), r = i - col * h * K, ci = r / K, k = r - ci * K;
+      const float* src = a.transposed ? a.w + (static_cast<long long>(ci) * h + co0 + col) * K + k
+                                      : a.w + (static_cast<long long>(co0 + col) * h + ci) * K + k;
+      dl_cp4(w + i, src);
+    }
   }
   cp_async_commit();
   pdl_wait();
@@ -308,7 +333,7 @@ __global__ void __launch_bounds__(kDlThreads) dec_layer_kernel(const __grid_cons
 }
 
 // skip + GroupNorm of the last stage, crop / zero-pad to the horizon, output_proj.
-// dynamic smem: x[h * Lin] | out_w[A][h] | stat[16]
+// dynamic smem: x[h * Lin] | out_w[A][h] | stat[16] | z rows
 __global__ void __launch_bounds__(kDlThreads) dec_head_kernel(const __grid_constant__ DecLayerArgs a) {
   extern __shared__ __align__(16) float dsm[];
   const int h = a.h, Lin = a.Lin, A = a.A, Hz = a.horizon;
@@ -323,20 +348,29 @@ __global__ void __launch_bounds__(kDlThreads) dec_head_kernel(const __grid_const
   cp_async_wait<0>();
   __syncthreads();
   const int b = blockIdx.y;
-  for (int i = threadIdx.x; i < Hz * A; i += kDlThreads) {
-    const int p = i / A, c = i - p * A;
-    float acc = a.out_b[c];
-    if (p < Lin)
-      for (int k = 0; k < h; ++k) acc = fmaf(ow[c * h + k], x[k * Lin + p], acc);
-    a.final_out[(static_cast<long long>(b) * Hz + p) * A + c] = acc;
+  // warp per output feature, lanes over positions: x[k][p] reads are consecutive
+  // across the lanes, the weight row is a broadcast
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = warp; c < A; c += kDlThreads / 32) {
+    const float* wr = ow + c * h;
+    for (int p = lane; p < Hz; p += 32) {
+      float acc = a.out_b[c];
+      if (p < Lin) {
+#pragma unroll 8
+        for (int k = 0; k < h; ++k) acc = fmaf(wr[k], x[k * Lin + p], acc);
+      }
+      a.final_out[(static_cast<long long>(b) * Hz + p) * A + c] = acc;
+    }
   }
 }
 
+// stat[16] is followed by kDlZRows floats for the token rows of z (input_proj)
+constexpr int kDlZRows = 1024;
 static size_t dl_layer_smem(int h, int Lin, int K) {
-  return sizeof(float) * (((h * Lin + 3) & ~3) + kDlCo * h * K + kDlThreads + 16);
+  return sizeof(float) * (((h * Lin + 3) & ~3) + kDlCo * h * K + kDlThreads + 16 + kDlZRows);
 }
 static size_t dl_head_smem(int h, int Lin, int A) {
-  return sizeof(float) * (((h * Lin + 3) & ~3) + ((A * h + 3) & ~3) + 16);
+  return sizeof(float) * (((h * Lin + 3) & ~3) + ((A * h + 3) & ~3) + 16 + kDlZRows);
 }
 
 template <typename Kern>
@@ -375,8 +409,10 @@ static bool decoder_wide(const DecArgs& a, cudaStream_t st, cudaError_t* err) {
   if (h % kDlCo != 0 || h % G != 0) return false;
   const int kSmemMax = 227 * 1024;
   int L = a.cfg.num_tokens;
+  if (L % 4 != 0 || L * a.cfg.latent_dim > kDlZRows) return false;
   for (int i = 0; i < a.num_stages; ++i) {
     const int Lout = stage_out_len(L, a.stages[i].stride);
+    if (Lout % 4 != 0) return false;  // float4 rows of one channel
     if (dl_layer_smem(h, L, 2 * a.stages[i].stride) > kSmemMax || dl_layer_smem(h, Lout, 3) > kSmemMax) return false;
     L = Lout;
   }

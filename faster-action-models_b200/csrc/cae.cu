@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(kCtxThreads) cae_ctx_slice_kernel(const __grid
   }
 }
 
-// smem: e1 [16][D] | e [16][D] | ckv weights [2HD][D + 4]
+// smem: e1 [16][D] | e [16][D] | ckv weights [2HD][D + 4] | text_embedding.2 weight [D][D + 4]
 __global__ void __launch_bounds__(kCtxThreads) cae_ctx_kv_kernel(const __grid_constant__ CaeCtxArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int r0 = blockIdx.x * kCaeCtxRows, nr = min(kCaeCtxRows, a.rows - r0);
@@ -491,13 +491,28 @@ __global__ void __launch_bounds__(kCtxThreads) cae_ctx_kv_kernel(const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* e1 = sm;
   float* e = e1 + kCaeCtxRows * D;
-  float* wkv = e + kCaeCtxRows * D;
+  float* wkv = e + kCaeCtxRows * D;         // [2HD][D + 4]
+  float* w2 = wkv + 2 * HD * (D + 4);       // text_embedding.2 weight [D][D + 4]
   const CaeLayer& ly = a.layers[l];
   // constant inputs first (they overlap the slice launch): this block's K/V
-  // projection, and this CTA's share of the packed block weights
-  for (int i = threadIdx.x; i < 2 * HD * D; i += kCtxThreads) {
-    const int o = i / D, c = i - o * D;
-    wkv[o * (D + 4) + c] = ly.ckv_w[i];
+  // projection and text_embedding.2 (float4 loads when aligned, all issued
+  // before use), and this CTA's share of the packed block weights
+  const bool v4 = ((reinterpret_cast<uintptr_t>(ly.ckv_w) | reinterpret_cast<uintptr_t>(a.text2_w)) & 15) == 0;
+  if (v4) {
+    const int d4 = D / 4;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < 2 * HD * d4; i += kCtxThreads) {
+      const int o = i / d4, c = (i - o * d4) * 4;
+      *reinterpret_cast<float4*>(wkv + o * (D + 4) + c) = __ldg(reinterpret_cast<const float4*>(ly.ckv_w) + i);
+    }
+#pragma unroll 4
+    for (int i = threadIdx.x; i < D * d4; i += kCtxThreads) {
+      const int o = i / d4, c = (i - o * d4) * 4;
+      *reinterpret_cast<float4*>(w2 + o * (D + 4) + c) = __ldg(reinterpret_cast<const float4*>(a.text2_w) + i);
+    }
+  } else {
+    for (int i = threadIdx.x; i < 2 * HD * D; i += kCtxThreads) wkv[(i / D) * (D + 4) + i % D] = ly.ckv_w[i];
+    for (int i = threadIdx.x; i < D * D; i += kCtxThreads) w2[(i / D) * (D + 4) + i % D] = a.text2_w[i];
   }
   if (a.wpack != nullptr) {
     const CaeStagePlan& p = a.plan;
@@ -520,15 +535,19 @@ __global__ void __launch_bounds__(kCtxThreads) cae_ctx_kv_kernel(const __grid_co
   pdl_launch_dependents();
   for (int i = threadIdx.x; i < nr * D; i += kCtxThreads) {
     const int r = i / D, o = i - r * D;
+    float pv[kCaeCtxSlices];
+#pragma unroll
+    for (int ks = 0; ks < kCaeCtxSlices; ++ks) pv[ks] = a.part[(static_cast<long long>(ks) * a.rows + r0 + r) * D + o];
     float s = a.text0_b[o];
-    for (int ks = 0; ks < kCaeCtxSlices; ++ks) s += a.part[(static_cast<long long>(ks) * a.rows + r0 + r) * D + o];
+#pragma unroll
+    for (int ks = 0; ks < kCaeCtxSlices; ++ks) s += pv[ks];
     e1[r * D + o] = gelu_tanh(s);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < nr * D; i += kCtxThreads) {
     const int r = i / D, o = i - r * D;
     float s = a.text2_b[o];
-    const float* wr = a.text2_w + static_cast<long long>(o) * D;
+    const float* wr = w2 + o * (D + 4);
     for (int c = 0; c < D; ++c) s += wr[c] * e1[r * D + c];
     e[r * D + o] = s;
   }
@@ -616,7 +635,7 @@ cudaError_t launch_cae_context(const CaeCtxArgs& a, cudaStream_t st, bool pdl) {
                         ? ctx_launch(cae_ctx_slice_kernel<__nv_bfloat16>, dim3(tiles, kCaeCtxSlices), ctx_slice_smem(a), st, pdl, a)
                         : ctx_launch(cae_ctx_slice_kernel<float>, dim3(tiles, kCaeCtxSlices), ctx_slice_smem(a), st, pdl, a);
     if (e != cudaSuccess) return e;
-    const size_t smem2 = sizeof(float) * (2 * kCaeCtxRows * a.D + 2 * a.HD * (a.D + 4));
+    const size_t smem2 = sizeof(float) * (2 * kCaeCtxRows * a.D + (2 * a.HD + a.D) * (a.D + 4));
     return ctx_launch(cae_ctx_kv_kernel, dim3(tiles, a.L), smem2, st, true, a);
   }
   const size_t smem = sizeof(float) * kCaeCtxTokens * (a.T + 2 * a.D);
