@@ -41,6 +41,7 @@ class GemmDesc(C.Structure):
         ("bias", C.c_void_p), ("gate_w", C.c_void_p), ("gate_t", C.c_void_p),
         ("tokens_per_batch", C.c_int32), ("first_frame_tokens", C.c_int32),
         ("gate_batch_stride", C.c_int64), ("gate_group_stride", C.c_int64),
+        ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("split_round", C.c_int32),
     ]
 
 
@@ -53,7 +54,8 @@ def _declare(lib):
     lib.fam_last_error.argtypes = [C.c_char_p, C.c_size_t]
     lib.fam_device_status.argtypes = [C.POINTER(C.c_int), C.c_int, C.c_void_p]
     lib.fam_gemm.argtypes = [C.POINTER(GemmDesc), C.c_void_p]
-    for name in ("fam_version", "fam_last_error", "fam_device_status", "fam_gemm"):
+    lib.fam_gemm_split_round_scratch_bytes.argtypes = [C.POINTER(C.c_size_t)]
+    for name in ("fam_version", "fam_last_error", "fam_device_status", "fam_gemm", "fam_gemm_split_round_scratch_bytes"):
         getattr(lib, name).restype = C.c_int
     from . import _abi  # model-level entry points
     _abi.declare(lib)

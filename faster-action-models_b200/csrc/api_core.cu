@@ -155,10 +155,28 @@ int fam_gemm(const fam_gemm_desc* d, void* stream) {
     return set_error("fam_gemm: the residual epilogue accumulates into fp32");
   if (e.out == nullptr) return set_error("fam_gemm: null output");
   GemmPlan p;
+  float* skp = nullptr;
+  unsigned* skf = nullptr;
+  size_t skb = 0;
+  if (d->scratch != nullptr) {
+    const size_t part = gemm_sk_scratch_bytes();
+    if (d->scratch_bytes < part + gemm_num_sms() * sizeof(unsigned))
+      return set_error("fam_gemm: split-round scratch of %zu bytes needed", part + gemm_num_sms() * sizeof(unsigned));
+    skp = static_cast<float*>(d->scratch);
+    skf = reinterpret_cast<unsigned*>(static_cast<char*>(d->scratch) + part);
+    skb = part;
+  }
   int rc = gemm_plan(&p, d->a, d->lda, d->b, d->ldb, d->m, d->n, d->k, d->splits, d->tile_n, e,
-                     d->a_is_const != 0, d->b_is_const != 0, device_status_word());
+                     d->a_is_const != 0, d->b_is_const != 0, device_status_word(), skp, skf, skb,
+                     d->split_round != 0);
   if (rc) return rc;
   return check_cuda(gemm_launch(p, static_cast<cudaStream_t>(stream), d->pdl != 0), "fam_gemm launch");
+}
+
+int fam_gemm_split_round_scratch_bytes(size_t* bytes) {
+  if (bytes == nullptr) return set_error("fam_gemm_split_round_scratch_bytes: null bytes");
+  *bytes = gemm_sk_scratch_bytes() + gemm_num_sms() * sizeof(unsigned);
+  return FAM_OK;
 }
 
 }  // extern "C"

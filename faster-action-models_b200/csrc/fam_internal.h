@@ -56,6 +56,16 @@ struct GemmArgs {
   int b_is_const;
   int* status;
   GemmEpilogue epi;
+  // Split last round (persistent kernel with a scratch): whole tiles go round-
+  // robin for sk_full rounds; each of the remaining tiles is split into
+  // sk_pieces k-ranges on consecutive CTAs.  Pieces 1.. store their fp32 partial
+  // in sk_part[their CTA] and count their epilogue warps on sk_flag[piece 0's
+  // CTA]; piece 0 adds the partials in piece order before the epilogue and
+  // clears the flag.
+  int sk_full;              // whole-tile rounds before the split round
+  int sk_pieces;            // k-pieces per remaining tile (0: no split round)
+  float* sk_part;           // [CTAs][128][BN] fp32
+  unsigned* sk_flag;        // [CTAs], zero between launches
 };
 
 struct GemmPlan {
@@ -88,9 +98,17 @@ cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __
                                 float scale_log2, __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl);
 
 int gemm_pick_bn(int n);
+// sk_part / sk_flag (optional, sk_bytes of fp32 scratch and one zeroed word per
+// SM): a many-tile problem may then run 256-wide tiles and split the tiles of
+// the last, partial round over the idle CTAs (sk_force: whenever possible,
+// else when the tile-time model predicts a gain).
 int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M, int N,
               int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,
-              int* status);
+              int* status, float* sk_part = nullptr, unsigned* sk_flag = nullptr, size_t sk_bytes = 0,
+              bool sk_force = false);
+// Streaming-multiprocessor count of the current device, and the split-round scratch it needs.
+int gemm_num_sms();
+size_t gemm_sk_scratch_bytes();
 cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl);
 // Sets the dynamic shared-memory limits of every kernel instantiation (call
 // once per device before any stream capture).

@@ -9,6 +9,11 @@
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lane
 //               quarter w%4) and apply bias / GELU / gated residual / split-K
 //               partial stores.
+// The persistent variant (many-tile problems) loops over tiles with two TMEM
+// accumulators, so that the epilogue of one tile overlaps the main loop of the
+// next, and runs eight epilogue warps (warps 2..9, two per lane quarter, each
+// on half of the tile's columns): the epilogue of a K=3072 tile is otherwise
+// longer than its main loop.
 //
 // The same kernel serves both operand orientations used by the models:
 //   * small-M action GEMMs (8..256 tokens) run "weights as A": A = W[out,in]
@@ -31,6 +36,11 @@ namespace fam {
 constexpr int kGemmThreads = 192;
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle atom)
 constexpr int kBM = 128;         // MMA M
+constexpr int kSkMaxPieces = 4;  // k-pieces per tile of a split last round
+// Persistent kernel: producer warp, MMA warp and two epilogue warps per TMEM
+// lane quarter (each drains half of the tile's columns).
+constexpr int kPersistEpiWarps = 8;
+constexpr int kPersistThreads = 64 + 32 * kPersistEpiWarps;
 
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
 __host__ __device__ constexpr int gemm_stages(int bn) {
@@ -324,8 +334,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // MMA warp fills one while the epilogue warps drain the other, so a tile's
 // epilogue overlaps the next tile's main loop; the operand ring runs on across
 // tile boundaries.
+// A parked k-piece partial is a [BN/4][128 rows][4] fp32 block: the float4 of
+// columns c..c+3 of row r sits at ((c / 4) * 128 + r) * 4, so that the 32 rows
+// of a warp touch 512 contiguous bytes per access.
+__device__ __forceinline__ long long gemm_part_index(int r, int c) {
+  return (static_cast<long long>(c >> 2) * kBM + r) * 4;
+}
+
+// Adds columns c..c+15 of row r of the tile's later k-pieces, in piece order
+// (npart partials, pstride floats apart); every load is issued before the adds.
+__device__ __forceinline__ void gemm_add_partial(float* v, const float* padd, int r, int c, int npart,
+                                                 long long pstride) {
+  if (npart <= 0) return;
+  float4 t[kSkMaxPieces - 1][4];
+#pragma unroll
+  for (int q = 0; q < kSkMaxPieces - 1; ++q)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      t[q][j] = q < npart ? *reinterpret_cast<const float4*>(padd + q * pstride + gemm_part_index(r, c + 4 * j))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < kSkMaxPieces - 1; ++q)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[4 * j] += t[q][j].x;
+      v[4 * j + 1] += t[q][j].y;
+      v[4 * j + 2] += t[q][j].z;
+      v[4 * j + 3] += t[q][j].w;
+    }
+}
+
 template <int BN>
-__device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_t tacc, int a_row, int n0) {
+__device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_t tacc, int r, int a_row, int n0,
+                                                   int cb, int ce, const float* padd, int npart) {
   const GemmEpilogue& e = args.epi;
   const bool row_ok = a_row < args.M;
   if (e.vec && e.kind == kEpiResidual) {
@@ -340,20 +381,21 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
       grow = e.gate_t + bi * e.gate_bstride + grp * e.gate_gstride;
     }
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 64) {
-      float4 r[16];
+    for (int c0 = cb; c0 < ce; c0 += 64) {
+      float4 rs[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int col = n0 + c0 + 4 * j;
-        r[j] = (row_ok && c0 + 4 * j < BN && col < args.N) ? *reinterpret_cast<const float4*>(orow + col)
+        rs[j] = (row_ok && c0 + 4 * j < ce && col < args.N) ? *reinterpret_cast<const float4*>(orow + col)
                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        if (c0 + 16 * q >= BN) break;  // tile widths that are not a multiple of 64
+        if (c0 + 16 * q >= ce) break;  // column ranges that are not a multiple of 64
         float v[16];
         __syncwarp();
         tmem_ld16(tacc + c0 + 16 * q, v);
+        gemm_add_partial(v, padd, r, c0 + 16 * q, npart, static_cast<long long>(kBM) * BN);
         const int b0 = n0 + c0 + 16 * q;
         if (!row_ok || b0 >= args.N) continue;
         float bz[16], gw[16];
@@ -411,7 +453,7 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
             else if (e.act == kActSilu) t = silu(rbf(t));
             x[k] = t;
           }
-          const float4 rr = r[4 * q + j];
+          const float4 rr = rs[4 * q + j];
           *reinterpret_cast<float4*>(orow + b0 + 4 * j) =
               make_float4(rr.x + g[4 * j] * x[0], rr.y + g[4 * j + 1] * x[1], rr.z + g[4 * j + 2] * x[2],
                           rr.w + g[4 * j + 3] * x[3]);
@@ -421,16 +463,61 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
     return;
   }
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 16) {
+  for (int c = cb; c < ce; c += 16) {
     float v[16];
     __syncwarp();
     tmem_ld16(tacc + c, v);
+    gemm_add_partial(v, padd, r, c, npart, static_cast<long long>(kBM) * BN);
     if (row_ok) gemm_epilogue_apply(args, e, a_row, n0 + c, 0, v);
   }
 }
 
+// Segments of a persistent CTA: whole tiles blockIdx.x + i * gridDim.x; with a
+// split last round, sk_full whole rounds and then piece (blockIdx.x % P) of
+// remaining tile (blockIdx.x / P) (piece = -1 for a whole tile).
+struct GemmSegs {
+  int i, ntiles, nkb, full, P, stage;
+  __device__ __forceinline__ void init(const GemmArgs& args, int ntiles_, int nkb_) {
+    ntiles = ntiles_;
+    nkb = nkb_;
+    P = args.sk_pieces;
+    full = P > 0 ? args.sk_full : (ntiles + gridDim.x - 1) / gridDim.x;
+    i = 0;
+    stage = 0;
+  }
+  __device__ __forceinline__ bool next(int& t, int& kb0, int& kb1, int& piece) {
+    if (stage == 0) {
+      const int tt = blockIdx.x + i * gridDim.x;
+      if (i < full && tt < ntiles) {
+        ++i;
+        t = tt;
+        kb0 = 0;
+        kb1 = nkb;
+        piece = -1;
+        return true;
+      }
+      stage = 1;
+    }
+    if (stage == 1) {
+      stage = 2;
+      if (P > 0) {
+        const int j = blockIdx.x / P, p = blockIdx.x - j * P;
+        const int tt = full * gridDim.x + j;
+        if (tt < ntiles) {
+          t = tt;
+          kb0 = p * nkb / P;
+          kb1 = (p + 1) * nkb / P;
+          piece = p;
+          return true;
+        }
+      }
+    }
+    return false;
+  }
+};
+
 template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPersistThreads, 1)
     gemm_bf16_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA,
                                 const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   constexpr int STAGES = gemm_stages(BN);
@@ -463,7 +550,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kPersistEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -486,30 +573,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint64_t pol_x = policy_evict_last();
       const uint64_t polA = args.a_is_const ? pol_w : pol_x;
       const uint64_t polB = args.b_is_const ? pol_w : pol_x;
-      // first tile: constant operand of the first stages before the wait on the previous launch
-      int tile = blockIdx.x;
+      // first segment: constant operand of the first stages before the wait on the previous launch
+      GemmSegs sg;
+      sg.init(args, ntiles, nkb);
+      int tile = 0, kb0 = 0, kb1 = 0, piece = -1;
+      bool have = sg.next(tile, kb0, kb1, piece);
       int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
-      const int pre = min(nkb, STAGES);
+      const int pre = have ? min(kb1 - kb0, STAGES) : 0;
       for (int i = 0; i < pre; ++i) {
         uint8_t* sa = smem + i * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
-        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], i * kBK, m0, polA);
-        if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], i * kBK, n0, polB);
+        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], (kb0 + i) * kBK, m0, polA);
+        if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], (kb0 + i) * kBK, n0, polB);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
         uint8_t* sa = smem + i * STAGE_BYTES;
-        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], i * kBK, m0, polA);
-        if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], i * kBK, n0, polB);
+        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], (kb0 + i) * kBK, m0, polA);
+        if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], (kb0 + i) * kBK, n0, polB);
       }
-      int kb = pre, issued = pre;
-      if (kb == nkb) {
-        kb = 0;
-        tile += gridDim.x;
+      int kb = kb0 + pre, issued = pre;
+      if (have && kb == kb1) {
+        have = sg.next(tile, kb0, kb1, piece);
+        kb = kb0;
         m0 = (tile % tiles_m) * kBM;
         n0 = (tile / tiles_m) * BN;
       }
-      for (int it = pre; tile < ntiles; ++it) {
+      for (int it = pre; have; ++it) {
         const int s = it % STAGES;
         if (*abort_flag) break;
         if (!mbar_wait(&empty[s], static_cast<uint32_t>(it / STAGES - 1) & 1, args.status, kErrWaitEmpty)) {
@@ -521,9 +611,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0, polA);
         tma_load_2d(sa + A_BYTES, &tmB, &full[s], kb * kBK, n0, polB);
         issued = it + 1;
-        if (++kb == nkb) {
-          kb = 0;
-          tile += gridDim.x;
+        if (++kb == kb1) {
+          have = sg.next(tile, kb0, kb1, piece);
+          kb = kb0;
           m0 = (tile % tiles_m) * kBM;
           n0 = (tile / tiles_m) * BN;
         }
@@ -538,7 +628,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kBM, BN);
       int it = 0, lt = 0;
-      for (int tile = blockIdx.x; tile < ntiles && nkb > 0; tile += gridDim.x, ++lt) {
+      GemmSegs sg;
+      sg.init(args, ntiles, nkb);
+      int tile, kb0, kb1, piece;
+      for (; nkb > 0 && sg.next(tile, kb0, kb1, piece); ++lt) {
         const int buf = lt & 1;
         if (*abort_flag) break;
         if (lt >= 2 && !mbar_wait(&tempty[buf], static_cast<uint32_t>((lt >> 1) - 1) & 1, args.status,
@@ -549,7 +642,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t dacc = tmem_base + buf * ACC_COLS;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           if (*abort_flag || !mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, args.status,
                                         kErrWaitFull)) {
@@ -562,7 +655,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t db = umma_desc_sw128(smem + s * STAGE_BYTES + A_BYTES);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            umma_bf16_ss(dacc, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16_ss(dacc, da + 2 * k, db + 2 * k, idesc, (kb > kb0 || k != 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -570,18 +663,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
+    static_assert((BN / 2) % 16 == 0, "epilogue column halves are whole 16-column loads");
     const int sp = warp & 3;  // TMEM lane quarter of this warp
+    const int cb = ((warp - 2) >> 2) * (BN / 2), ce = cb + BN / 2;  // this warp's column half
     pdl_wait();
     int lt = 0;
-    for (int tile = blockIdx.x; tile < ntiles && nkb > 0; tile += gridDim.x, ++lt) {
+    GemmSegs sg;
+    sg.init(args, ntiles, nkb);
+    int tile, kb0, kb1, piece;
+    for (; nkb > 0 && sg.next(tile, kb0, kb1, piece); ++lt) {
       const int buf = lt & 1;
+      if (args.epi.vec && args.epi.kind == kEpiResidual && piece <= 0) {
+        // pull this row's residual segment into L2 while the tile's main loop runs
+        const int row = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN + cb;
+        const int ncols = min(ce, args.N - (tile / tiles_m) * BN) - cb;
+        if (row < args.M && ncols > 0)
+          bulk_prefetch_l2(reinterpret_cast<const float*>(args.epi.out) + static_cast<long long>(row) * args.epi.out_sa + col,
+                           static_cast<uint32_t>(ncols) * 4u);
+      }
       const bool ok = mbar_wait(&tfull[buf], static_cast<uint32_t>(lt >> 1) & 1, args.status, kErrWaitAccum);
       tc_fence_after();
       if (!ok) *abort_flag = 1;
       if (*abort_flag) break;
       const int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
-      gemm_tile_epilogue<BN>(args, tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16),
-                             m0 + sp * 32 + lane, n0);
+      const uint32_t tacc = tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16);
+      const int r = sp * 32 + lane;  // row inside the tile
+      if (piece > 0) {
+        // a later k-piece of a tile that piece 0's CTA finishes: park the fp32 partial
+        float* pt = args.sk_part + static_cast<long long>(blockIdx.x) * kBM * BN;
+#pragma unroll 1
+        for (int c = cb; c < ce; c += 16) {
+          float v[16];
+          __syncwarp();
+          tmem_ld16(tacc + c, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<float4*>(pt + gemm_part_index(r, c + 4 * j)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.sk_flag + blockIdx.x - piece, 1u);
+      } else if (piece == 0) {
+        // piece 0: wait for the other pieces' partials (every epilogue warp of each)
+        unsigned* fl = args.sk_flag + blockIdx.x;
+        const unsigned want = static_cast<unsigned>(kPersistEpiWarps * (args.sk_pieces - 1));
+        int got = 1;
+        if (lane == 0) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (atomicAdd(fl, 0u) < want) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              record_error(args.status, kErrWaitAccum);
+              got = 0;
+              break;
+            }
+          }
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        __threadfence();
+        const float* pt = args.sk_part + static_cast<long long>(blockIdx.x + 1) * kBM * BN;
+        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, cb, ce, pt, got ? args.sk_pieces - 1 : 0);
+        // every epilogue warp is done with the partials: clear the flag
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kPersistEpiWarps) : "memory");
+        if (warp == 2 && lane == 0) atomicExch(fl, 0u);
+      } else {
+        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, cb, ce, nullptr, 0);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -635,7 +782,7 @@ static cudaError_t launch_gemm_persist_bn(const CUtensorMap& ta, const CUtensorM
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(kPersistThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -646,7 +793,7 @@ static cudaError_t launch_gemm_persist_bn(const CUtensorMap& ta, const CUtensorM
   return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_persist_kernel<BN>, ta, tb, a);
 }
 
-static int gemm_num_sms() {
+int gemm_num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev = 0;
@@ -656,6 +803,8 @@ static int gemm_num_sms() {
   }
   return n;
 }
+
+size_t gemm_sk_scratch_bytes() { return static_cast<size_t>(gemm_num_sms()) * kBM * 256 * sizeof(float); }
 
 cudaError_t gemm_init_attributes() {
   cudaError_t e;
@@ -709,28 +858,51 @@ cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
 // with row stride ldb.  `splits` > 1 requires the partial epilogue.
 int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M,
               int N, int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const,
-              bool b_is_const, int* status) {
+              bool b_is_const, int* status, float* sk_part, unsigned* sk_flag, size_t sk_bytes,
+              bool sk_force) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error("gemm: empty problem");
   if ((K % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0)
     return set_error("gemm: K and row strides must be multiples of 8 elements (16 bytes)");
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return set_error("gemm: operand base addresses must be 16-byte aligned");
+  // Tile width for many-tile problems: the shortest estimated makespan.  The
+  // time of a 128-row tile measured on B200 grows as (BN + 340) per k-block
+  // (operand rows streamed per k-block plus a fixed per-k-block cost, fitted
+  // over BN = 128..256); whole rounds over the SMs cost that each.  With a
+  // scratch, 256-wide tiles may instead split the last, partial round into
+  // P <= 4 k-pieces, which costs 1/P of a round plus a fixed exchange
+  // (measured ~25 us, about 53 k-blocks of a 256-wide tile).
+  bool sk = false;
+  const int sms = gemm_num_sms(), mt = (M + kBM - 1) / kBM;
+  const long long nkb_all = (K + kBK - 1) / kBK;
+  int sk_pieces = 0, sk_full = 0;
   if (bn == 0) {
     bn = gemm_pick_bn(N);
-    // many-tile problems: the tile width with the shortest estimated makespan,
-    // whole rounds over the SMs x per-tile time; the per-tile time measured on
-    // B200 for 128-row tiles grows as (BN + 340) (operand rows streamed per
-    // k-block plus a fixed per-k-block cost, fitted over BN = 128..256)
-    const int sms = gemm_num_sms(), mt = (M + kBM - 1) / kBM;
     if (splits <= 1 && mt * ((N + 255) / 256) > sms) {
       const int cand[4] = {256, 192, 160, 128};
-      long long best = -1;
+      double best = -1.0;
       for (int i = 0; i < 4; ++i) {
         const long long tiles = static_cast<long long>(mt) * ((N + cand[i] - 1) / cand[i]);
-        const long long t = ((tiles + sms - 1) / sms) * (cand[i] + 340);
+        const double t = static_cast<double>((tiles + sms - 1) / sms) * (cand[i] + 340) * nkb_all;
         if (best < 0 || t < best) {
           best = t;
           bn = cand[i];
+        }
+      }
+      if (sk_part != nullptr && sk_flag != nullptr && sk_bytes >= gemm_sk_scratch_bytes()) {
+        const long long tiles = static_cast<long long>(mt) * ((N + 255) / 256);
+        const int full = static_cast<int>(tiles / sms), left = static_cast<int>(tiles - static_cast<long long>(full) * sms);
+        int P = left > 0 ? sms / left : 0;
+        if (P > kSkMaxPieces) P = kSkMaxPieces;
+        if (P > nkb_all) P = static_cast<int>(nkb_all);
+        if (P >= 2) {
+          const double t = (full + 1.0 / P) * (256 + 340) * nkb_all + 53.0 * (256 + 340);
+          if (sk_force || t < best) {
+            sk = true;
+            bn = 256;
+            sk_pieces = P;
+            sk_full = full;
+          }
         }
       }
     }
@@ -754,8 +926,17 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
   p->splits = splits;
   // persistent tile loop when the tiles outnumber the SMs (no split-K)
   const int ntiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
-  const int sms = gemm_num_sms();
   p->persist = (splits == 1 && bn >= 64 && ntiles > sms) ? sms : 0;
+  p->args.sk_full = 0;
+  p->args.sk_pieces = 0;
+  p->args.sk_part = nullptr;
+  p->args.sk_flag = nullptr;
+  if (sk && p->persist > 0) {
+    p->args.sk_full = sk_full;
+    p->args.sk_pieces = sk_pieces;
+    p->args.sk_part = sk_part;
+    p->args.sk_flag = sk_flag;
+  }
   // 16-feature vector epilogue (residual): features contiguous in the output,
   // 16-byte aligned rows, bias / gates / gate rows aligned for vector loads
   {

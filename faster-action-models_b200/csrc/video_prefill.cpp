@@ -32,7 +32,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
 
 struct VLayout {
-  size_t x, h, qkv, q, ao, qc, ci, fh, patch, tmod, sin, th1, th2, cemb, ch1, ckv, apart, ctr, vt;
+  size_t x, h, qkv, q, ao, qc, ci, fh, patch, tmod, sin, th1, th2, cemb, ch1, ckv, apart, ctr, vt, skp, skf;
   size_t total;
 };
 
@@ -67,6 +67,8 @@ VLayout vlayout(const fam_video_config& c, int B, int S, int C) {
   w.apart = take(attn_partial_bytes(B, c.num_heads, S, c.head_dim, 1));
   w.ctr = take(static_cast<size_t>(B) * c.num_heads * attn_query_tiles(S) * 4);
   w.vt = take(attention_tc_vt_bytes(B, c.num_heads, S));  // V^T of the tcgen05 self attention
+  w.skp = take(gemm_sk_scratch_bytes());                   // split-round partials of the GEMMs
+  w.skf = take(static_cast<size_t>(gemm_num_sms()) * sizeof(unsigned));
   w.total = off;
   return w;
 }
@@ -148,7 +150,8 @@ int gemm_x(const VCtx& c, const void* act, long long lda, int M, const void* W, 
     e.gate_gstride = 6LL * D;
   }
   GemmPlan p;
-  V_TRYI(gemm_plan(&p, act, lda, W, K, M, N, K, 1, 0, e, false, true, c.e->status));
+  V_TRYI(gemm_plan(&p, act, lda, W, K, M, N, K, 1, 0, e, false, true, c.e->status, wp<float>(c, c.L.skp),
+                   wp<unsigned>(c, c.L.skf), gemm_sk_scratch_bytes()));
   V_LAUNCH(gemm_launch(p, c.st, c.pdl));
   return 0;
 }
@@ -175,6 +178,7 @@ int enqueue_prefill(const VCtx& c) {
   c.e->launch_count = 0;
   const size_t ctr_bytes = static_cast<size_t>(B) * g.num_heads * attn_query_tiles(S) * 4;
   V_TRY(cudaMemsetAsync(wp<void>(c, c.L.ctr), 0, ctr_bytes, c.st));
+  V_TRY(cudaMemsetAsync(wp<void>(c, c.L.skf), 0, static_cast<size_t>(gemm_num_sms()) * sizeof(unsigned), c.st));
 
   // ---- time MLP on (first frame t=0, rest t) per sample
   StepTimes ts = {};

@@ -35,13 +35,16 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
          residual: Optional[torch.Tensor] = None, gate_w: Optional[torch.Tensor] = None,
          gate_t: Optional[torch.Tensor] = None, tokens_per_batch: int = 0,
          first_frame_tokens: int = 0, gate_batch_stride: int = 0, gate_group_stride: int = 0,
-         pdl: bool = False) -> torch.Tensor:
+         pdl: bool = False, split_round: str = "off") -> torch.Tensor:
     """Linear layer on the tensor cores.
 
     weights_as_a=False:  a = activations [T, K], b = weight [F, K] -> [T, F]
     weights_as_a=True:   a = weight [F, K], b = activations [T, K] -> [T, F]
     splits > 1 returns fp32 split-K partials [splits, T, F] (no bias).
     residual (fp32 [T, F]) is updated in place: residual += gate * (x W^T + bias).
+    split_round: "auto" / "always" let a many-tile problem run 256-wide tiles and split
+    each tile of the last, partial round into k-pieces on the idle SMs ("auto": only
+    where the tile-time model predicts a gain); a zeroed per-device scratch is kept for it.
     """
     _require(a, torch.bfloat16, "a")
     _require(b, torch.bfloat16, "b")
@@ -88,8 +91,26 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
     else:
         d.out_stride_a, d.out_stride_b = ld, 1
     d.out = out.data_ptr()
+    if split_round not in ("off", "auto", "always"):
+        raise ValueError(f"split_round {split_round!r}")
+    if split_round != "off":
+        sk = _split_scratch(a.device)
+        d.scratch, d.scratch_bytes = sk.data_ptr(), sk.numel()
+        d.split_round = 1 if split_round == "always" else 0
     check(lib().fam_gemm(C.byref(d), C.c_void_p(_stream())), "fam_gemm")
     return out
+
+
+_SK = {}
+
+
+def _split_scratch(dev) -> torch.Tensor:
+    """Zeroed split-round scratch of the device (every launch leaves it zeroed)."""
+    if dev not in _SK:
+        n = C.c_size_t()
+        check(lib().fam_gemm_split_round_scratch_bytes(C.byref(n)), "fam_gemm_split_round_scratch_bytes")
+        _SK[dev] = torch.zeros(n.value, dtype=torch.uint8, device=dev)
+    return _SK[dev]
 
 
 def attention_desc(q, k1, v1, heads, k2=None, v2=None, mask=None, key_mask=None,

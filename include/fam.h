@@ -107,9 +107,19 @@ typedef struct fam_gemm_desc {
   int32_t first_frame_tokens;
   int64_t gate_batch_stride;
   int64_t gate_group_stride;
+  /* Optional split-round scratch (NULL: none), fam_gemm_split_round_scratch_bytes
+   * bytes, zeroed once before its first use (every launch leaves it zeroed).
+   * With it a many-tile problem may run 256-wide tiles whole-round-robin and
+   * split each tile of the last, partial round into 2..4 k-pieces on the idle
+   * SMs, summed in a fixed order (deterministic).  split_round = 0: only when
+   * the tile-time model predicts a gain; 1: whenever the last round is partial. */
+  void* scratch;
+  size_t scratch_bytes;
+  int32_t split_round;
 } fam_gemm_desc;
 
 FAM_API int fam_gemm(const fam_gemm_desc* desc, void* stream);
+FAM_API int fam_gemm_split_round_scratch_bytes(size_t* bytes);
 
 /* Masked multi-head attention, softmax(q k^T / sqrt(d)) v with a bool mask,
  * over the concatenation of two key/value sources (source 2 may be empty).

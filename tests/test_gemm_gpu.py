@@ -106,3 +106,36 @@ def test_persistent_residual_and_store(fam_ops, tile_n):
     gate = gw.float()[None, :] + gt[tok // S, grp]
     _close(r, r0 + gate * _ref(x, w, b))
     _close(y, _ref(x, w, b, "gelu_tanh"))
+
+
+@pytest.mark.parametrize("F,K", [(3072, 512), (3072, 1344), (9216, 512), (14336, 256)])
+def test_split_round(fam_ops, F, K):
+    """Split last round: 256-wide tiles round-robin, each tile of the partial last
+    round cut into 4 / 2 / 3 k-pieces (F = 3072 / 9216 / 14336 at 1760 tokens) and
+    finished from the later pieces' fp32 partials; residual and GELU-store
+    epilogues, deterministic across launches; the model-chosen schedule agrees."""
+    g = torch.Generator(device="cuda").manual_seed(K)
+    B, S, ff = 2, 880, 352
+    x = torch.randn(B * S, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(F, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    b = torch.randn(F, device="cuda", generator=g).bfloat16()
+    gw = torch.randn(F, device="cuda", generator=g).bfloat16()
+    gt = torch.randn(B, 2, F, device="cuda", generator=g)
+    r0 = torch.randn(B * S, F, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        r = r0.clone()
+        fam_ops.gemm(x, w, bias=b, residual=r, gate_w=gw, gate_t=gt, tokens_per_batch=S,
+                     first_frame_tokens=ff, gate_batch_stride=2 * F, gate_group_stride=F,
+                     split_round="always")
+        y = fam_ops.gemm(x, w, bias=b, act="gelu_tanh", split_round="always")
+        torch.cuda.synchronize()
+        outs.append((r, y))
+    y_auto = fam_ops.gemm(x, w, bias=b, act="gelu_tanh", split_round="auto")
+    tok = torch.arange(B * S, device="cuda")
+    grp = ((tok % S) >= ff).long()
+    gate = gw.float()[None, :] + gt[tok // S, grp]
+    _close(outs[0][0], r0 + gate * _ref(x, w, b))
+    _close(outs[0][1], _ref(x, w, b, "gelu_tanh"))
+    _close(y_auto, _ref(x, w, b, "gelu_tanh"))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
