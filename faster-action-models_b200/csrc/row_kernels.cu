@@ -105,27 +105,32 @@ __device__ __forceinline__ float4 mod_value4(const ModRows& m, long long off, in
 
 // ---------------------------------------------------------------- resid_norm
 // Each thread owns column groups g = threadIdx.x + i * blockDim.x (4 columns
-// each, at most kMaxGroups); the updated row stays in registers.
+// each, NG = ceil(D / 1024) of them); the updated row stays in registers.
+// NG and the presence of the residual update are compile-time, so that the
+// registers (and the CTAs resident per SM) follow the row width: a norm-only
+// D = 3072 row keeps 3 groups of constants, not 4 groups of both sets.
 constexpr int kMaxGroups = 4;  // D <= 4 * 4 * 256 = 4096
+template <int NG, bool RESID>
 __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNormArgs a) {
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int D = a.D;
   const int G = D / 4;
   float* x = a.x + static_cast<long long>(row) * D;
-  const long long moff = a.mod.tmod != nullptr ? mod_row_offset(a.mod, row) : 0;
+  const long long moff = (RESID && a.mod.tmod != nullptr) ? mod_row_offset(a.mod, row) : 0;
   const long long noff = a.nmod.tmod != nullptr ? mod_row_offset(a.nmod, row) : 0;
   // Constants of the chain (bias, gate, norm affine / shift / scale) load before
   // the programmatic-launch wait; only x and the partials depend on it.
-  float4 cb[kMaxGroups], cg[kMaxGroups], c0[kMaxGroups], c1[kMaxGroups];
+  float4 cb[NG], cg[NG], c0[NG], c1[NG];
 #pragma unroll
-  for (int i = 0; i < kMaxGroups; ++i) {
+  for (int i = 0; i < NG; ++i) {
     const int g = threadIdx.x + i * blockDim.x;
     if (g >= G) break;
     const int f = 4 * g;
-    cb[i] = (a.partials != nullptr && a.bias != nullptr) ? ld_bf4(a.bias + f) : make_float4(0.f, 0.f, 0.f, 0.f);
-    cg[i] = (a.partials != nullptr && a.gate_chunk >= 0) ? mod_value4(a.mod, moff, a.gate_chunk, f, D)
-                                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+    if (RESID) {
+      cb[i] = a.bias != nullptr ? ld_bf4(a.bias + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+      cg[i] = a.gate_chunk >= 0 ? mod_value4(a.mod, moff, a.gate_chunk, f, D) : make_float4(1.f, 1.f, 1.f, 1.f);
+    }
     if (a.norm_mode == kNormAffine) {
       c0[i] = ld_bf4(a.norm_w + f);
       c1[i] = ld_bf4(a.norm_b + f);
@@ -136,15 +141,15 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
   }
   pdl_wait();
   pdl_launch_dependents();
-  float4 v[kMaxGroups];
+  float4 v[NG];
   float lsum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kMaxGroups; ++i) {
+  for (int i = 0; i < NG; ++i) {
     const int g = threadIdx.x + i * blockDim.x;
     if (g >= G) break;
     const int f = 4 * g;
     float4 xv = *reinterpret_cast<const float4*>(x + f);
-    if (a.partials != nullptr) {
+    if (RESID) {
       float4 y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * D + f);
       y = rbf4(f4add(y, cb[i]));  // the reference's Linear output is a bf16 tensor
       const float4 gt = cg[i];
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
   const float mean = block_sum(lsum, red) / D;
   float lvar = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kMaxGroups; ++i) {
+  for (int i = 0; i < NG; ++i) {
     const int g = threadIdx.x + i * blockDim.x;
     if (g >= G) break;
     const float4 d = make_float4(v[i].x - mean, v[i].y - mean, v[i].z - mean, v[i].w - mean);
@@ -168,7 +173,7 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
   const float rstd = rsqrtf(block_sum(lvar, red) / D + a.eps);
   __nv_bfloat16* h = a.h + static_cast<long long>(row) * a.h_stride;
 #pragma unroll
-  for (int i = 0; i < kMaxGroups; ++i) {
+  for (int i = 0; i < NG; ++i) {
     const int g = threadIdx.x + i * blockDim.x;
     if (g >= G) break;
     const int f = 4 * g;
@@ -376,9 +381,20 @@ static cudaError_t ensure_smem(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
 }
 
+template <bool RESID>
+static cudaError_t launch_resid_norm_t(const ResidNormArgs& a, int rows, cudaStream_t st, bool pdl) {
+  switch ((a.D + 4 * kRowThreads - 1) / (4 * kRowThreads)) {
+    case 1: return launch_pdl(resid_norm_kernel<1, RESID>, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
+    case 2: return launch_pdl(resid_norm_kernel<2, RESID>, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
+    case 3: return launch_pdl(resid_norm_kernel<3, RESID>, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
+    default: return launch_pdl(resid_norm_kernel<4, RESID>, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
+  }
+}
+
 cudaError_t launch_resid_norm(const ResidNormArgs& a, int rows, cudaStream_t st, bool pdl) {
   if (a.D % 4 != 0 || a.D > 4 * kMaxGroups * kRowThreads) return cudaErrorInvalidValue;
-  return launch_pdl(resid_norm_kernel, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
+  return a.partials != nullptr ? launch_resid_norm_t<true>(a, rows, st, pdl)
+                               : launch_resid_norm_t<false>(a, rows, st, pdl);
 }
 
 cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, bool pdl) {
