@@ -11,9 +11,10 @@
 //               partial stores.
 // The persistent variant (many-tile problems) loops over tiles with two TMEM
 // accumulators, so that the epilogue of one tile overlaps the main loop of the
-// next, and runs eight epilogue warps (warps 2..9, two per lane quarter, each
-// on half of the tile's columns): the epilogue of a K=3072 tile is otherwise
-// longer than its main loop.
+// next, and runs sixteen epilogue warps (warps 2..17, four per lane quarter,
+// 16-column chunks dealt round-robin): the epilogue is a latency-bound chain
+// of TMEM loads, conversions and scattered stores per warp, and with fewer
+// warps the epilogue of a K=3072 tile is longer than its main loop.
 //
 // The same kernel serves both operand orientations used by the models:
 //   * small-M action GEMMs (8..256 tokens) run "weights as A": A = W[out,in]
@@ -37,9 +38,10 @@ constexpr int kGemmThreads = 192;
 constexpr int kBK = 64;          // K elements per stage (128 bytes of bf16: one swizzle atom)
 constexpr int kBM = 128;         // MMA M
 constexpr int kSkMaxPieces = 4;  // k-pieces per tile of a split last round
-// Persistent kernel: producer warp, MMA warp and two epilogue warps per TMEM
-// lane quarter (each drains half of the tile's columns).
-constexpr int kPersistEpiWarps = 8;
+// Persistent kernel: producer warp, MMA warp and four epilogue warps per TMEM
+// lane quarter (16-column chunks dealt round-robin over the four).
+constexpr int kPersistEpiWarps = 16;
+constexpr int kEpiPerQuarter = kPersistEpiWarps / 4;
 constexpr int kPersistThreads = 64 + 32 * kPersistEpiWarps;
 
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kBM * kBK * 2 + bn * kBK * 2; }
@@ -364,14 +366,17 @@ __device__ __forceinline__ void gemm_add_partial(float* v, const float* padd, in
     }
 }
 
+// Epilogue of one epilogue warp: tile rows of its TMEM lane quarter (a row per
+// lane), 16-column chunks c0, c0 + cs, ... < BN.  npart parked partials of later
+// k-pieces (padd, pstride floats apart) are added in piece order first.
 template <int BN>
 __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_t tacc, int r, int a_row, int n0,
-                                                   int cb, int ce, const float* padd, int npart) {
+                                                   int c0, int cs, const float* padd, int npart) {
   const GemmEpilogue& e = args.epi;
   const bool row_ok = a_row < args.M;
   if (e.vec && e.kind == kEpiResidual) {
-    // out[row][f] += g[f] * act(acc + bias[f]); 16 features per TMEM load, the
-    // fp32 residual of 64 features prefetched at a time
+    // out[row][f] += g[f] * act(acc + bias[f]); the chunk's fp32 residual and
+    // gate row are loaded before its TMEM load so that the latencies overlap
     float* orow = reinterpret_cast<float*>(e.out) + static_cast<long long>(row_ok ? a_row : 0) * e.out_sa;
     const float* grow = nullptr;
     if (e.gate_t != nullptr) {
@@ -381,89 +386,56 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
       grow = e.gate_t + bi * e.gate_bstride + grp * e.gate_gstride;
     }
 #pragma unroll 1
-    for (int c0 = cb; c0 < ce; c0 += 64) {
-      float4 rs[16];
+    for (int c = c0; c < BN; c += cs) {
+      const int b0 = n0 + c;
+      const bool ok = row_ok && b0 < args.N;
+      float4 rr[4], gt[4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int col = n0 + c0 + 4 * j;
-        rs[j] = (row_ok && c0 + 4 * j < ce && col < args.N) ? *reinterpret_cast<const float4*>(orow + col)
-                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < 4; ++j) {
+        rr[j] = ok ? *reinterpret_cast<const float4*>(orow + b0 + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gt[j] = (ok && grow != nullptr) ? *reinterpret_cast<const float4*>(grow + b0 + 4 * j)
+                                        : make_float4(1.f, 1.f, 1.f, 1.f);
       }
+      float v[16];
+      __syncwarp();
+      tmem_ld16(tacc + c, v);
+      gemm_add_partial(v, padd, r, c, npart, static_cast<long long>(kBM) * BN);
+      if (!ok) continue;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (c0 + 16 * q >= ce) break;  // column ranges that are not a multiple of 64
-        float v[16];
-        __syncwarp();
-        tmem_ld16(tacc + c0 + 16 * q, v);
-        gemm_add_partial(v, padd, r, c0 + 16 * q, npart, static_cast<long long>(kBM) * BN);
-        const int b0 = n0 + c0 + 16 * q;
-        if (!row_ok || b0 >= args.N) continue;
-        float bz[16], gw[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) bz[j] = gw[j] = 0.f;
+      for (int j = 0; j < 4; ++j) {
+        // four columns at a time: bias and gate weight as 8-byte bf16 loads
+        float bz[4] = {0.f, 0.f, 0.f, 0.f}, gw[4] = {0.f, 0.f, 0.f, 0.f};
         if (e.bias != nullptr) {
-          const uint4* bp = reinterpret_cast<const uint4*>(e.bias + b0);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint4 u = bp[h];
-            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
-              bz[8 * h + 2 * k] = f.x;
-              bz[8 * h + 2 * k + 1] = f.y;
-            }
-          }
+          const uint2 u = *reinterpret_cast<const uint2*>(e.bias + b0 + 4 * j);
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          bz[0] = f0.x; bz[1] = f0.y; bz[2] = f1.x; bz[3] = f1.y;
         }
-        if (e.gate_w != nullptr) {
-          const uint4* gp = reinterpret_cast<const uint4*>(e.gate_w + b0);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint4 u = gp[h];
-            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
-              gw[8 * h + 2 * k] = f.x;
-              gw[8 * h + 2 * k + 1] = f.y;
-            }
-          }
+        if (grow != nullptr && e.gate_w != nullptr) {
+          const uint2 u = *reinterpret_cast<const uint2*>(e.gate_w + b0 + 4 * j);
+          const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          gw[0] = f0.x; gw[1] = f0.y; gw[2] = f1.x; gw[3] = f1.y;
         }
-        float g[16];
-        if (grow != nullptr) {
+        float x[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 t = *reinterpret_cast<const float4*>(grow + b0 + 4 * j);
-            g[4 * j] = t.x + gw[4 * j];
-            g[4 * j + 1] = t.y + gw[4 * j + 1];
-            g[4 * j + 2] = t.z + gw[4 * j + 2];
-            g[4 * j + 3] = t.w + gw[4 * j + 3];
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) g[j] = 1.f;
+        for (int k = 0; k < 4; ++k) {
+          float t = v[4 * j + k] + bz[k];
+          if (e.act == kActGeluTanh) t = gelu_tanh(rbf(t));
+          else if (e.act == kActSilu) t = silu(rbf(t));
+          x[k] = t;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float x[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            float t = v[4 * j + k] + bz[4 * j + k];
-            if (e.act == kActGeluTanh) t = gelu_tanh(rbf(t));
-            else if (e.act == kActSilu) t = silu(rbf(t));
-            x[k] = t;
-          }
-          const float4 rr = rs[4 * q + j];
-          *reinterpret_cast<float4*>(orow + b0 + 4 * j) =
-              make_float4(rr.x + g[4 * j] * x[0], rr.y + g[4 * j + 1] * x[1], rr.z + g[4 * j + 2] * x[2],
-                          rr.w + g[4 * j + 3] * x[3]);
-        }
+        const float4 g = gt[j];
+        const float4 q = rr[j];
+        *reinterpret_cast<float4*>(orow + b0 + 4 * j) =
+            make_float4(q.x + (g.x + gw[0]) * x[0], q.y + (g.y + gw[1]) * x[1], q.z + (g.z + gw[2]) * x[2],
+                        q.w + (g.w + gw[3]) * x[3]);
       }
     }
     return;
   }
 #pragma unroll 1
-  for (int c = cb; c < ce; c += 16) {
+  for (int c = c0; c < BN; c += cs) {
     float v[16];
     __syncwarp();
     tmem_ld16(tacc + c, v);
@@ -663,9 +635,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       }
     }
   } else {
-    static_assert((BN / 2) % 16 == 0, "epilogue column halves are whole 16-column loads");
-    const int sp = warp & 3;  // TMEM lane quarter of this warp
-    const int cb = ((warp - 2) >> 2) * (BN / 2), ce = cb + BN / 2;  // this warp's column half
+    static_assert(BN % 16 == 0, "epilogue chunks are whole 16-column loads");
+    const int sp = warp & 3;                       // TMEM lane quarter of this warp
+    const int wq = (warp - 2) >> 2;                // its rank among the quarter's warps
+    const int c0 = 16 * wq, cs = 16 * kEpiPerQuarter;  // its 16-column chunks
     pdl_wait();
     int lt = 0;
     GemmSegs sg;
@@ -673,10 +646,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     int tile, kb0, kb1, piece;
     for (; nkb > 0 && sg.next(tile, kb0, kb1, piece); ++lt) {
       const int buf = lt & 1;
-      if (args.epi.vec && args.epi.kind == kEpiResidual && piece <= 0) {
+      if (args.epi.vec && args.epi.kind == kEpiResidual && piece <= 0 && wq == 0) {
         // pull this row's residual segment into L2 while the tile's main loop runs
-        const int row = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN + cb;
-        const int ncols = min(ce, args.N - (tile / tiles_m) * BN) - cb;
+        const int row = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN;
+        const int ncols = min(BN, args.N - col);
         if (row < args.M && ncols > 0)
           bulk_prefetch_l2(reinterpret_cast<const float*>(args.epi.out) + static_cast<long long>(row) * args.epi.out_sa + col,
                            static_cast<uint32_t>(ncols) * 4u);
@@ -692,7 +665,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         // a later k-piece of a tile that piece 0's CTA finishes: park the fp32 partial
         float* pt = args.sk_part + static_cast<long long>(blockIdx.x) * kBM * BN;
 #pragma unroll 1
-        for (int c = cb; c < ce; c += 16) {
+        for (int c = c0; c < BN; c += cs) {
           float v[16];
           __syncwarp();
           tmem_ld16(tacc + c, v);
@@ -722,12 +695,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         got = __shfl_sync(0xffffffffu, got, 0);
         __threadfence();
         const float* pt = args.sk_part + static_cast<long long>(blockIdx.x + 1) * kBM * BN;
-        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, cb, ce, pt, got ? args.sk_pieces - 1 : 0);
+        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, c0, cs, pt, got ? args.sk_pieces - 1 : 0);
         // every epilogue warp is done with the partials: clear the flag
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kPersistEpiWarps) : "memory");
         if (warp == 2 && lane == 0) atomicExch(fl, 0u);
       } else {
-        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, cb, ce, nullptr, 0);
+        gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, c0, cs, nullptr, 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -905,6 +878,11 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
           }
         }
       }
+    } else if (splits <= 1 && !epi.features_on_a && mt <= 4) {
+      // few activation rows against a wide weight (context projections): halve
+      // the tile width while the tiles still fit one wave, so that the weight
+      // stream is spread over more SMs
+      while (bn > 32 && (bn & (bn - 1)) == 0 && mt * ((N + bn / 2 - 1) / (bn / 2)) <= sms) bn /= 2;
     }
   }
   const int kb_total = (K + kBK - 1) / kBK;
