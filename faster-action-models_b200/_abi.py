@@ -56,6 +56,7 @@ def declare(lib) -> None:
               "fam_action_chunk", "fam_action_denoise_step"):
         getattr(lib, n).restype = C.c_int
     declare_counts(lib)
+    declare_vae(lib)
     declare_ops(lib)
     declare_cae(lib)
     declare_video(lib)
@@ -175,4 +176,20 @@ def declare_video(lib) -> None:
     lib.fam_video_launch_count.argtypes = [vp, C.POINTER(C.c_int32)]
     for n in ("fam_video_expert_create", "fam_video_expert_destroy", "fam_video_workspace_size",
               "fam_video_prefill", "fam_video_launch_count"):
+        getattr(lib, n).restype = C.c_int
+
+
+def declare_vae(lib) -> None:
+    """Wan2.2 VAE encode pieces (include/fam.h, fam_vae_*)."""
+    i32, i64, f32 = C.c_int32, C.c_int64, C.c_float
+    fp = C.POINTER(C.c_float)
+    lib.fam_vae_patchify.argtypes = [vp, i32, i32, vp, vp]
+    lib.fam_vae_im2col.argtypes = [vp, i64, i32, i32, i32, i32, i32, i32, i32, vp, i64, vp]
+    lib.fam_vae_rms.argtypes = [vp, i64, i64, i32, vp, i32, vp, i64, vp, i64, vp]
+    lib.fam_vae_avg_down_add.argtypes = [vp, i64, i32, i32, i32, i32, i32, i32, vp, i64, vp]
+    lib.fam_vae_softmax.argtypes = [vp, i64, i32, i32, f32, vp, i64, vp]
+    lib.fam_vae_transpose.argtypes = [vp, i64, i32, i32, vp, i64, vp]
+    lib.fam_vae_latent.argtypes = [vp, i64, i64, i32, vp, vp, vp, vp]
+    for n in ("fam_vae_patchify", "fam_vae_im2col", "fam_vae_rms", "fam_vae_avg_down_add", "fam_vae_softmax",
+              "fam_vae_transpose", "fam_vae_latent"):
         getattr(lib, n).restype = C.c_int

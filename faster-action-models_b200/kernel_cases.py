@@ -11,6 +11,8 @@ synchronizes; under ncu, skip the warm-up launches with `-s`.
   dit4dit_c3   DiT4DiTPipeline of BASELINE config 3 (backbone to block 18 of 28 at 3,520
                tokens + 16-block action head, 4 Euler steps, batch 1); prints the
                p50 chunk latency over the repeats
+  vae_c1       WanVideoVAE38 encode of one 512 x 704 observation frame (dim 160, z 48,
+               the configs-1/2 latent grid 32 x 44); prints the p50 latency
 """
 import importlib
 import sys
@@ -22,6 +24,7 @@ sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 ops = importlib.import_module("faster-action-models_b200.ops")
 M = importlib.import_module("faster-action-models_b200.models")
 P = importlib.import_module("faster-action-models_b200.pipeline")
+VAE = importlib.import_module("faster-action-models_b200.vae")
 
 
 def main(case: str, reps: int) -> None:
@@ -85,6 +88,31 @@ def main(case: str, reps: int) -> None:
             times.append(s0.elapsed_time(e0))
         times = sorted(times[2:])
         print("dit4dit_c3 chunk ms p50", round(times[len(times) // 2], 3))
+    elif case == "vae_c1":
+        g = torch.Generator().manual_seed(0)
+        sd = {}
+        for name, shape in VAE.encoder_param_shapes(160, 48).items():
+            if name.endswith("gamma"):
+                sd[name] = (1.0 + 0.1 * torch.randn(shape, generator=g)).bfloat16()
+            elif name.endswith("bias"):
+                sd[name] = (0.05 * torch.randn(shape, generator=g)).bfloat16()
+            else:
+                fan_in = 1
+                for d in shape[1:]:
+                    fan_in *= d
+                sd[name] = (torch.randn(shape, generator=g) / fan_in ** 0.5).bfloat16()
+        vae = VAE.WanVideoVAE38(sd, torch.zeros(48), torch.ones(48), z_dim=48, dim=160)
+        img = (torch.rand(1, 3, 1, 512, 704, generator=g) * 2 - 1).bfloat16().to(dev)
+        times = []
+        for _ in range(reps + 2):
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            vae.model.encode(img, vae.scale)
+            e0.record()
+            torch.cuda.synchronize()
+            times.append(s0.elapsed_time(e0))
+        times = sorted(times[2:])
+        print("vae_c1 encode ms p50", round(times[len(times) // 2], 3))
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()

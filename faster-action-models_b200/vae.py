@@ -1,0 +1,345 @@
+"""Wan2.2 VAE encode of the observation frame on B200.
+
+Mirrors the reference interface used by the FastWAM prologue,
+``self.vae.model.encode(video, self.vae.scale)`` with video [1, 3, 1, H, W]
+(FastWAM/src/fastwam/models/wan22/fastwam.py:296-306; VideoVAE38_.encode,
+wan22/wan_video_vae.py:1285-1304), for the first frame (T = 1), which is all
+the action-chunk prologue encodes.  Parameters load from the reference's
+state dict names (``encoder.*``, ``conv1.*``).
+
+Every step runs in libfam (include/fam.h): 3x3 convolutions as
+``fam_vae_im2col`` + the tcgen05 GEMM (bias / residual epilogues), 1x1
+convolutions as GEMMs, RMS_norm(+SiLU), the AvgDown3D shortcut, the one-head
+attention (scores GEMM, row softmax, P V GEMM) and the latent normalisation
+as ``fam_vae_*`` kernels.  The sequence is captured once per frame size in a
+CUDA graph.  With T = 1 every CausalConv3d sees two zero frames in front
+(wan_video_vae.py:38-53), so its last temporal tap is packed; the temporal
+downsample convs of Resample38 only fill their cache on a first chunk
+(:177-190) and are not used.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import ops
+from ._lib import check, lib
+
+Params = Dict[str, torch.Tensor]
+
+
+def _ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream() -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class _Conv:
+    """Packed convolution: bf16 weight [Cout, taps * Cin_p] (K order dy, dx, c), bf16 bias."""
+
+    def __init__(self, w: torch.Tensor, b: Optional[torch.Tensor], cin_p: int, device):
+        if w.dim() == 5:                       # CausalConv3d: last temporal tap
+            w = w[:, :, -1]
+        cout, cin = w.shape[:2]
+        self.taps = w.shape[2] * w.shape[3] if w.dim() == 4 else 1
+        if w.dim() == 4:
+            w = w.permute(0, 2, 3, 1)           # [Cout, kh, kw, Cin]
+        w = w.reshape(cout, self.taps, cin)
+        wp = torch.zeros(cout, self.taps, cin_p, dtype=torch.float32)
+        wp[:, :, :cin] = w.float()
+        self.w = wp.reshape(cout, self.taps * cin_p).to(device=device, dtype=torch.bfloat16).contiguous()
+        self.b = None if b is None else b.reshape(-1).to(device=device, dtype=torch.bfloat16).contiguous()
+        self.cout, self.cin_p = cout, cin_p
+
+
+class VideoVAE38Encoder:
+    """VideoVAE38_ encoder side (Encoder3d_38 + conv1) for one frame."""
+
+    def __init__(self, state_dict: Params, dim: int = 160, z_dim: int = 48,
+                 dim_mult: Sequence[int] = (1, 2, 4, 4), num_res_blocks: int = 2,
+                 temperal_downsample: Sequence[bool] = (False, True, True), device="cuda"):
+        self.device = torch.device(device)
+        self.dim, self.z_dim = dim, z_dim
+        self.dim_mult, self.num_res_blocks = tuple(dim_mult), num_res_blocks
+        self.temperal_downsample = tuple(temperal_downsample)
+        sd = state_dict
+        dev = self.device
+
+        def g(name):  # RMS_norm gamma as bf16 [C]
+            return sd[name + ".gamma"].reshape(-1).to(device=dev, dtype=torch.bfloat16).contiguous()
+
+        def conv(name, cin_p):
+            return _Conv(sd[name + ".weight"], sd.get(name + ".bias"), cin_p, dev)
+
+        dims = [dim * u for u in (1,) + self.dim_mult]
+        for c in dims + [2 * z_dim]:
+            if c % 8:
+                raise ValueError(f"channel count {c} is not a multiple of 8")
+        self.conv_in = conv("encoder.conv1", 16)      # patchified 12 channels, padded to 16
+        self.blocks = []
+        n = len(self.dim_mult)
+        for i, (din, dout) in enumerate(zip(dims[:-1], dims[1:])):
+            pre = f"encoder.downsamples.{i}.downsamples"
+            rbs, cin = [], din
+            for j in range(num_res_blocks):
+                rbs.append(self._res_block(sd, f"{pre}.{j}", cin, dout, g, conv))
+                cin = dout
+            down = i != n - 1
+            t_down = self.temperal_downsample[i] if i < len(self.temperal_downsample) else False
+            self.blocks.append(dict(rbs=rbs, din=din, dout=dout, down=down, ft=2 if t_down else 1,
+                                    resample=conv(f"{pre}.{num_res_blocks}.resample.1", dout) if down else None))
+        c = dims[-1]
+        self.mid0 = self._res_block(sd, "encoder.middle.0", c, c, g, conv)
+        self.attn = dict(gamma=g("encoder.middle.1.norm"), qkv=conv("encoder.middle.1.to_qkv", c),
+                         proj=conv("encoder.middle.1.proj", c))
+        self.mid2 = self._res_block(sd, "encoder.middle.2", c, c, g, conv)
+        self.head_gamma = g("encoder.head.0")
+        self.head = conv("encoder.head.2", c)
+        self.conv1 = conv("conv1", 2 * z_dim)
+        self._bufs = {}
+        self._graphs = {}
+
+    @staticmethod
+    def _res_block(sd, pre, cin, cout, g, conv):
+        return dict(cin=cin, cout=cout, g0=g(pre + ".residual.0"), c1=conv(pre + ".residual.2", cin),
+                    g1=g(pre + ".residual.3"), c2=conv(pre + ".residual.6", cout),
+                    sc=conv(pre + ".shortcut", cin) if (pre + ".shortcut.weight") in sd else None)
+
+    # ------------------------------------------------------------- buffers
+    def _alloc(self, H: int, W: int):
+        key = (H, W)
+        if key in self._bufs:
+            return self._bufs[key]
+        if H % 16 or W % 16:
+            raise ValueError(f"frame {H}x{W}: height and width must be multiples of 16")
+        if ((H // 16) * (W // 16)) % 8:
+            raise ValueError(f"frame {H}x{W}: the latent grid must hold a multiple of 8 positions "
+                             "(the attention P V product runs over them as GEMM K)")
+        dims = [self.dim * u for u in (1,) + self.dim_mult]
+        h, w = H // 2, W // 2
+        pmax = h * w
+        cmax = max(dims + [2 * self.z_dim, 16])
+        # im2col of the widest convolution at each resolution
+        col, hh, ww = 9 * 16 * pmax, h, w
+        for i, blk in enumerate(self.blocks):
+            col = max(col, 9 * max(blk["din"], blk["dout"]) * hh * ww)
+            if blk["down"]:
+                hh, ww = hh // 2, ww // 2
+                col = max(col, 9 * blk["dout"] * hh * ww)
+        pl = hh * ww
+        dev = self.device
+        f32 = lambda n: torch.empty(n, device=dev, dtype=torch.float32)
+        b16 = lambda n: torch.empty(n, device=dev, dtype=torch.bfloat16)
+        c = dims[-1]
+        bufs = dict(
+            image=b16(3 * H * W), patch=b16(pmax * 16), col=b16(col),
+            x=[f32(pmax * cmax) for _ in range(3)], y=f32(pmax * cmax), xin=f32(pmax * cmax),
+            t=b16(pmax * cmax), raw=b16(pmax * cmax),
+            qkv=b16(pl * 3 * c), s=f32(pl * pl), pm=b16(pl * pl), vt=b16(c * pl), o=b16(pl * c),
+            z=f32(pl * 2 * self.z_dim), mu=f32(pl * 2 * self.z_dim),
+            mean=f32(self.z_dim), inv_std=f32(self.z_dim), out=f32(self.z_dim * pl),
+        )
+        self._bufs[key] = bufs
+        return bufs
+
+    # ----------------------------------------------------------- pieces
+    @staticmethod
+    def _m(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+        return buf[: rows * cols].view(rows, cols)
+
+    def _rms(self, x, P, Cc, gamma, silu, out=None, raw=None):
+        check(lib().fam_vae_rms(C.c_void_p(x.data_ptr()), Cc, P, Cc, C.c_void_p(_ptr(gamma)), 1 if silu else 0,
+                                C.c_void_p(_ptr(out)), Cc, C.c_void_p(_ptr(raw)), Cc, _stream()), "fam_vae_rms")
+
+    def _conv3(self, bufs, src, H, W, cv: _Conv, stride, Ho, Wo, out=None, residual=None):
+        cin = cv.cin_p
+        check(lib().fam_vae_im2col(C.c_void_p(src.data_ptr()), cin, H, W, cin, stride, 1 if stride == 1 else 0,
+                                   Ho, Wo, C.c_void_p(bufs["col"].data_ptr()), 9 * cin, _stream()),
+              "fam_vae_im2col")
+        col = self._m(bufs["col"], Ho * Wo, 9 * cin)
+        if residual is not None:
+            ops.gemm(col, cv.w, bias=cv.b, residual=residual)
+        else:
+            ops.gemm(col, cv.w, bias=cv.b, out=out, out_dtype=torch.float32)
+
+    def _res(self, bufs, rb, xi, H, W):
+        """ResidualBlock (wan_video_vae.py:267-302); returns the output stream index."""
+        P, cin, cout = H * W, rb["cin"], rb["cout"]
+        X = self._m(bufs["x"][xi], P, cin)
+        T = self._m(bufs["t"], P, cin)
+        raw = self._m(bufs["raw"], P, cin) if rb["sc"] is not None else None
+        self._rms(X, P, cin, rb["g0"], True, out=T, raw=raw)
+        Y = self._m(bufs["y"], P, cout)
+        self._conv3(bufs, T, H, W, rb["c1"], 1, H, W, out=Y)
+        T2 = self._m(bufs["t"], P, cout)
+        self._rms(Y, P, cout, rb["g1"], True, out=T2)
+        if rb["sc"] is None:
+            self._conv3(bufs, T2, H, W, rb["c2"], 1, H, W, residual=X)
+            return xi
+        xo = (xi + 1) % 3
+        XO = self._m(bufs["x"][xo], P, cout)
+        ops.gemm(raw, rb["sc"].w, bias=rb["sc"].b, out=XO, out_dtype=torch.float32)
+        self._conv3(bufs, T2, H, W, rb["c2"], 1, H, W, residual=XO)
+        return xo
+
+    def _attention(self, bufs, xi, H, W):
+        """AttentionBlock (wan_video_vae.py:304-342), one head over the frame's tokens."""
+        a, P, c = self.attn, H * W, self.dim * self.dim_mult[-1]
+        X = self._m(bufs["x"][xi], P, c)
+        T = self._m(bufs["t"], P, c)
+        self._rms(X, P, c, a["gamma"], False, out=T)
+        QKV = self._m(bufs["qkv"], P, 3 * c)
+        ops.gemm(T, a["qkv"].w, bias=a["qkv"].b, out=QKV)
+        S = self._m(bufs["s"], P, P)
+        ops.gemm(QKV[:, :c], QKV[:, c:2 * c], out=S, out_dtype=torch.float32)
+        PM = self._m(bufs["pm"], P, P)
+        check(lib().fam_vae_softmax(C.c_void_p(S.data_ptr()), P, P, P, 1.0 / math.sqrt(c),
+                                    C.c_void_p(PM.data_ptr()), P, _stream()), "fam_vae_softmax")
+        VT = self._m(bufs["vt"], c, P)
+        check(lib().fam_vae_transpose(C.c_void_p(QKV[:, 2 * c:].data_ptr()), 3 * c, P, c,
+                                      C.c_void_p(VT.data_ptr()), P, _stream()), "fam_vae_transpose")
+        O = self._m(bufs["o"], P, c)
+        ops.gemm(PM, VT, out=O)
+        ops.gemm(O, a["proj"].w, bias=a["proj"].b, residual=X)
+
+    def _run(self, bufs, H, W):
+        h, w = H // 2, W // 2
+        check(lib().fam_vae_patchify(C.c_void_p(bufs["image"].data_ptr()), H, W,
+                                     C.c_void_p(bufs["patch"].data_ptr()), _stream()), "fam_vae_patchify")
+        xi = 0
+        X = self._m(bufs["x"][xi], h * w, self.dim)
+        self._conv3(bufs, self._m(bufs["patch"], h * w, 16), h, w, self.conv_in, 1, h, w, out=X)
+        for blk in self.blocks:
+            P = h * w
+            XIN = self._m(bufs["xin"], P, blk["din"])
+            XIN.copy_(self._m(bufs["x"][xi], P, blk["din"]))
+            for rb in blk["rbs"]:
+                xi = self._res(bufs, rb, xi, h, w)
+            dout = blk["dout"]
+            if blk["down"]:
+                X = self._m(bufs["x"][xi], P, dout)
+                RAW = self._m(bufs["raw"], P, dout)
+                self._rms(X, P, dout, None, False, raw=RAW)
+                xd = (xi + 1) % 3
+                ho, wo = h // 2, w // 2
+                XD = self._m(bufs["x"][xd], ho * wo, dout)
+                # ZeroPad2d((0, 1, 0, 1)) + Conv2d(3, stride 2) (wan_video_vae.py:254-258)
+                self._conv3(bufs, RAW, h, w, blk["resample"], 2, ho, wo, out=XD)
+                check(lib().fam_vae_avg_down_add(C.c_void_p(XIN.data_ptr()), blk["din"], h, w, blk["din"], dout,
+                                                 blk["ft"], 2, C.c_void_p(XD.data_ptr()), dout, _stream()),
+                      "fam_vae_avg_down_add")
+                xi, h, w = xd, ho, wo
+            else:
+                X = self._m(bufs["x"][xi], P, dout)
+                check(lib().fam_vae_avg_down_add(C.c_void_p(XIN.data_ptr()), blk["din"], h, w, blk["din"], dout,
+                                                 blk["ft"], 1, C.c_void_p(X.data_ptr()), dout, _stream()),
+                      "fam_vae_avg_down_add")
+        xi = self._res(bufs, self.mid0, xi, h, w)
+        self._attention(bufs, xi, h, w)
+        xi = self._res(bufs, self.mid2, xi, h, w)
+        P, c, z2 = h * w, self.dim * self.dim_mult[-1], 2 * self.z_dim
+        X = self._m(bufs["x"][xi], P, c)
+        T = self._m(bufs["t"], P, c)
+        self._rms(X, P, c, self.head_gamma, True, out=T)
+        Z = self._m(bufs["z"], P, z2)
+        self._conv3(bufs, T, h, w, self.head, 1, h, w, out=Z)
+        RAW = self._m(bufs["raw"], P, z2)
+        self._rms(Z, P, z2, None, False, raw=RAW)
+        MU = self._m(bufs["mu"], P, z2)
+        ops.gemm(RAW, self.conv1.w, bias=self.conv1.b, out=MU, out_dtype=torch.float32)
+        check(lib().fam_vae_latent(C.c_void_p(MU.data_ptr()), z2, P, self.z_dim,
+                                   C.c_void_p(bufs["mean"].data_ptr()), C.c_void_p(bufs["inv_std"].data_ptr()),
+                                   C.c_void_p(bufs["out"].data_ptr()), _stream()), "fam_vae_latent")
+        return h, w
+
+    # -------------------------------------------------------------- API
+    def encode(self, x: torch.Tensor, scale: List[torch.Tensor], use_graph: bool = True) -> torch.Tensor:
+        """VideoVAE38_.encode(x, scale) for x [1, 3, 1, H, W] -> mu [1, z_dim, 1, H/16, W/16] (fp32)."""
+        if x.dim() != 5 or x.shape[0] != 1 or x.shape[1] != 3:
+            raise ValueError(f"x must be [1, 3, T, H, W], got {tuple(x.shape)}")
+        if x.shape[2] != 1:
+            raise NotImplementedError("only the first-frame encode (T = 1) of the action prologue is built")
+        H, W = int(x.shape[3]), int(x.shape[4])
+        bufs = self._alloc(H, W)
+        bufs["image"].copy_(x.reshape(-1).to(device=self.device, dtype=torch.bfloat16))
+        bufs["mean"].copy_(torch.as_tensor(scale[0]).reshape(-1).to(device=self.device, dtype=torch.float32))
+        bufs["inv_std"].copy_(torch.as_tensor(scale[1]).reshape(-1).to(device=self.device, dtype=torch.float32))
+        hl, wl = H // 16, W // 16
+        if not use_graph:
+            self._run(bufs, H, W)
+        else:
+            key = (H, W)
+            g = self._graphs.get(key)
+            if g is None:
+                s = torch.cuda.Stream(device=self.device)
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    self._run(bufs, H, W)        # warm-up outside the capture (attributes, scratch)
+                torch.cuda.current_stream().wait_stream(s)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._run(bufs, H, W)
+                self._graphs[key] = g
+            g.replay()
+        return bufs["out"][: self.z_dim * hl * wl].view(1, self.z_dim, 1, hl, wl).clone()
+
+
+def encoder_param_shapes(dim: int = 160, z_dim: int = 48, dim_mult: Sequence[int] = (1, 2, 4, 4),
+                         num_res_blocks: int = 2) -> Dict[str, tuple]:
+    """Names and shapes of the parameters VideoVAE38Encoder reads, as in the
+    reference's VideoVAE38_ state dict (Encoder3d_38 + conv1)."""
+    dims = [dim * u for u in (1,) + tuple(dim_mult)]
+    s: Dict[str, tuple] = {}
+
+    def conv(name, cout, cin, k, three_d=True):
+        s[name + ".weight"] = (cout, cin, k, k, k) if three_d else (cout, cin, k, k)
+        s[name + ".bias"] = (cout,)
+
+    def rb(pre, cin, cout):
+        s[pre + ".residual.0.gamma"] = (cin, 1, 1, 1)
+        conv(pre + ".residual.2", cout, cin, 3)
+        s[pre + ".residual.3.gamma"] = (cout, 1, 1, 1)
+        conv(pre + ".residual.6", cout, cout, 3)
+        if cin != cout:
+            conv(pre + ".shortcut", cout, cin, 1)
+
+    conv("encoder.conv1", dims[0], 12, 3)
+    for i, (din, dout) in enumerate(zip(dims[:-1], dims[1:])):
+        pre = f"encoder.downsamples.{i}.downsamples"
+        cin = din
+        for j in range(num_res_blocks):
+            rb(f"{pre}.{j}", cin, dout)
+            cin = dout
+        if i != len(dim_mult) - 1:
+            conv(f"{pre}.{num_res_blocks}.resample.1", dout, dout, 3, three_d=False)
+    c = dims[-1]
+    rb("encoder.middle.0", c, c)
+    s["encoder.middle.1.norm.gamma"] = (c, 1, 1)
+    conv("encoder.middle.1.to_qkv", 3 * c, c, 1, three_d=False)
+    conv("encoder.middle.1.proj", c, c, 1, three_d=False)
+    rb("encoder.middle.2", c, c)
+    s["encoder.head.0.gamma"] = (c, 1, 1, 1)
+    conv("encoder.head.2", 2 * z_dim, c, 3)
+    conv("conv1", 2 * z_dim, 2 * z_dim, 1)
+    return s
+
+
+class WanVideoVAE38:
+    """Holder with the reference's attributes: ``.model.encode(x, scale)``, ``.scale``,
+    ``.z_dim``, ``.upsampling_factor`` (wan_video_vae.py:1347-1375)."""
+
+    def __init__(self, state_dict: Params, mean: torch.Tensor, std: torch.Tensor, z_dim: int = 48,
+                 dim: int = 160, device="cuda", **kw):
+        self.model = VideoVAE38Encoder(state_dict, dim=dim, z_dim=z_dim, device=device, **kw)
+        dev = torch.device(device)
+        self.mean = torch.as_tensor(mean, dtype=torch.float32, device=dev)
+        self.inv_std = torch.as_tensor(std, dtype=torch.float32, device=dev).reciprocal()
+        self.scale = [self.mean, self.inv_std]
+        self.z_dim = z_dim
+        self.upsampling_factor = 16
+        self.temporal_downsample_factor = 4

@@ -452,6 +452,38 @@ FAM_API int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_w
                               int32_t batch, const float* z, const int32_t* suite_ids, float* out,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Wan2.2 VAE encode of one observation frame: the pieces around the GEMMs of
+ * VideoVAE38_.encode with T = 1 (FastWAM/src/fastwam/models/wan22/
+ * wan_video_vae.py:1285-1304 via Encoder3d_38.forward :678-733; called from
+ * fastwam.py:296-306).  Activations are channels-last [positions, channels];
+ * 3x3 convolutions are fam_vae_im2col + fam_gemm, 1x1 convolutions fam_gemm.
+ * -------------------------------------------------------------------------- */
+/* patchify(2) (wan_video_vae.py:199-212) of a bf16 [3, H, W] frame into
+ * out bf16 [(H/2)(W/2), 16], channel c*4 + r*2 + q (channels 12..15 zero). */
+FAM_API int fam_vae_patchify(const void* image, int H, int W, void* out, void* stream);
+/* 3x3 gather for a convolution of stride `stride` and top/left zero padding
+ * `pad` (bottom/right padding follows from Ho, Wo): dst [Ho*Wo, 9*C] bf16,
+ * K order (dy, dx, c).  C, row strides: multiples of 8. */
+FAM_API int fam_vae_im2col(const void* src, int64_t src_ld, int H, int W, int C, int stride, int pad,
+                           int Ho, int Wo, void* dst, int64_t dst_ld, void* stream);
+/* RMS_norm over channels (wan_video_vae.py:55-70; + SiLU when silu_on) of the
+ * fp32 stream x [P, C] into bf16 out (nullable), and/or bf16(x) into raw. */
+FAM_API int fam_vae_rms(const float* x, int64_t x_ld, int64_t P, int C, const void* gamma, int silu_on,
+                        void* out, int64_t out_ld, void* raw, int64_t raw_ld, void* stream);
+/* out += AvgDown3D(in) for a one-frame input (wan_video_vae.py:345-395). */
+FAM_API int fam_vae_avg_down_add(const float* in, int64_t in_ld, int H, int W, int Cin, int Cout,
+                                 int factor_t, int factor_s, float* out, int64_t out_ld, void* stream);
+/* Row softmax of fp32 scores * scale into bf16 (AttentionBlock, :321-342). */
+FAM_API int fam_vae_softmax(const float* s, int64_t s_ld, int rows, int cols, float scale, void* p,
+                            int64_t p_ld, void* stream);
+/* bf16 transpose dst[c][r] = src[r][c]. */
+FAM_API int fam_vae_transpose(const void* src, int64_t src_ld, int rows, int cols, void* dst,
+                              int64_t dst_ld, void* stream);
+/* out f32 [z, P] = (mu[:, :z] - mean) * inv_std (VideoVAE38_.encode, :1296-1303). */
+FAM_API int fam_vae_latent(const float* mu, int64_t mu_ld, int64_t P, int z, const float* mean,
+                           const float* inv_std, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,8 @@ Reference code paths exercised:
       plus the final hidden state through DiTBlock.forward (wan_video_dit.py:248-267)
   sched / masks / rope / sinusoid: scheduler_continuous.py:63-88, fastwam.py:429-451,
         wan_video_dit.py:30-60, 489-523
+  vae VideoVAE38_.encode of one observation frame (fp32 and bf16)
+        FastWAM/src/fastwam/models/wan22/wan_video_vae.py:1285-1304, 619-733
 """
 from __future__ import annotations
 
@@ -55,6 +57,7 @@ def _import_reference(ref_root: Path):
     from fastwam.models.wan22.schedulers.scheduler_continuous import \
         WanContinuousFlowMatchScheduler
     from fastwam.models.action_ae import ActionAE, ActionAEConfig
+    from fastwam.models.wan22.wan_video_vae import VideoVAE38_
     return SimpleNamespace(**locals())
 
 
@@ -219,14 +222,50 @@ def make_primitives(R):
     return out
 
 
+def make_vae(R):
+    """Wan2.2 VAE (VideoVAE38_) encode of a first frame at a small width.
+
+    Every parameter is re-drawn (the reference zero-initialises the attention
+    projection, which would hide the attention path) and rounded to bf16."""
+    torch.manual_seed(4)
+    cfg = dict(dim=8, z_dim=8, dec_dim=8)
+    m = R.VideoVAE38_(**cfg).eval()
+    g = torch.Generator().manual_seed(4)
+    with torch.no_grad():
+        for name, prm in m.named_parameters():
+            if name.endswith("gamma"):
+                prm.copy_(1.0 + 0.1 * torch.randn(prm.shape, generator=g))
+            elif name.endswith("bias"):
+                prm.copy_(0.05 * torch.randn(prm.shape, generator=g))
+            else:
+                fan_in = prm[0].numel()
+                prm.copy_(torch.randn(prm.shape, generator=g) / fan_in ** 0.5)
+    _round_params_bf16(m)
+    image = (torch.rand(1, 3, 1, 64, 96, generator=g) * 2 - 1).bfloat16()
+    mean = (0.2 * torch.randn(8, generator=g)).bfloat16().float()
+    inv_std = (1.0 + 0.5 * torch.rand(8, generator=g)).bfloat16().float()
+    out = {"kind": "vae", "cfg": cfg, "image": image, "mean": mean, "inv_std": inv_std,
+           # the temporal downsample convs never run on a first frame
+           "params": {k: v.detach().to(torch.bfloat16).clone() for k, v in m.state_dict().items()
+                      if (k.startswith("encoder.") or k.startswith("conv1.")) and ".time_conv." not in k}}
+    with torch.no_grad():
+        out["mu_f32"] = m.float().encode(image.float(), [mean, inv_std])
+        out["mu_bf16"] = m.bfloat16().encode(image, [mean.bfloat16(), inv_std.bfloat16()])
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", nargs="*", default=None, help="fixture names to (re)generate")
     args = ap.parse_args()
     R = _import_reference(Path(args.reference))
     torch.set_num_threads(4)
     for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
-                     ("c2_video_prefill", make_c2), ("primitives", make_primitives)):
+                     ("c2_video_prefill", make_c2), ("primitives", make_primitives),
+                     ("vae_encode", make_vae)):
+        if args.only is not None and name not in args.only:
+            continue
         fx = fn(R)
         path = OUT / f"{name}.pt"
         torch.save(fx, path)

@@ -109,3 +109,16 @@ def test_c2_video_prefill_matches_reference():
     _same(torch.stack(ks), fx["cache_k"])
     _same(torch.stack(vs), fx["cache_v"])
     _same(hidden, fx["hidden"])
+
+
+def test_vae_encode_matches_reference():
+    """VideoVAE38_.encode of one frame: bit-exact at bf16, fp32 to rounding."""
+    fx = _load("vae_encode")
+    c = fx["cfg"]
+    cfg = O.VaeConfig(dim=c["dim"], z_dim=c["z_dim"])
+    mu = O.vae_encode_first_frame(fx["params"], cfg, fx["image"], fx["mean"].bfloat16(),
+                                  fx["inv_std"].bfloat16())
+    assert torch.equal(mu, fx["mu_bf16"])
+    p32 = {k: v.float() for k, v in fx["params"].items()}
+    mu32 = O.vae_encode_first_frame(p32, cfg, fx["image"].float(), fx["mean"], fx["inv_std"])
+    assert (mu32 - fx["mu_f32"]).abs().max().item() < 1e-5
