@@ -190,6 +190,7 @@ def declare_vae(lib) -> None:
     lib.fam_vae_softmax.argtypes = [vp, i64, i32, i32, f32, vp, i64, vp]
     lib.fam_vae_transpose.argtypes = [vp, i64, i32, i32, vp, i64, vp]
     lib.fam_vae_latent.argtypes = [vp, i64, i64, i32, vp, vp, vp, vp]
+    lib.fam_vae_splitk_reduce.argtypes = [vp, i32, i64, i32, vp, vp, i64, i32, vp]
     for n in ("fam_vae_patchify", "fam_vae_im2col", "fam_vae_rms", "fam_vae_avg_down_add", "fam_vae_softmax",
-              "fam_vae_transpose", "fam_vae_latent"):
+              "fam_vae_transpose", "fam_vae_latent", "fam_vae_splitk_reduce"):
         getattr(lib, n).restype = C.c_int

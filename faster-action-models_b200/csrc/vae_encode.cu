@@ -17,6 +17,9 @@
 //   vae_softmax_kernel       row softmax of the one-head attention scores
 //   vae_transpose_kernel     V -> V^T for the P V product
 //   vae_latent_kernel        (mu - mean) * inv_std, channel-first output
+//   vae_splitk_kernel        sum of split-K GEMM partials + bias, stored or
+//                            added into the fp32 stream (the few-tile
+//                            low-resolution convolutions)
 #include "../../include/fam.h"
 #include "fam_common.cuh"
 #include "fam_internal.h"
@@ -197,6 +200,36 @@ __global__ void vae_latent_kernel(const float* __restrict__ mu, long long mu_ld,
   }
 }
 
+// out[m][n] (+)= bias[n] + sum_s part[s][m][n], four columns per thread.
+__global__ void vae_splitk_kernel(const float* __restrict__ part, int splits, long long M, int N,
+                                  const __nv_bfloat16* __restrict__ bias, float* __restrict__ out, long long out_ld,
+                                  int accumulate) {
+  const int nq = N / 4;
+  const long long total = M * nq;
+  const long long sstride = M * N;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long m = i / nq;
+    const int n = static_cast<int>(i % nq) * 4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (bias != nullptr) {
+      const float2 b0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + n));
+      const float2 b1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + n + 2));
+      a = make_float4(b0.x, b0.y, b1.x, b1.y);
+    }
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + sp * sstride + m * N + n));
+      a = make_float4(a.x + v.x, a.y + v.y, a.z + v.z, a.w + v.w);
+    }
+    float4* o = reinterpret_cast<float4*>(out + m * out_ld + n);
+    if (accumulate) {
+      const float4 r = *o;
+      a = make_float4(a.x + r.x, a.y + r.y, a.z + r.z, a.w + r.w);
+    }
+    *o = a;
+  }
+}
+
 int grid_for(long long work, int per_block) {
   long long g = (work + per_block - 1) / per_block;
   if (g > 148LL * 16) g = 148LL * 16;
@@ -285,6 +318,16 @@ int fam_vae_latent(const float* mu, int64_t mu_ld, int64_t P, int z, const float
   vae_latent_kernel<<<grid_for(P * z, kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       mu, mu_ld, P, z, mean, inv_std, out);
   return launched("vae_latent_kernel");
+}
+
+int fam_vae_splitk_reduce(const float* partials, int splits, int64_t M, int N, const void* bias, float* out,
+                          int64_t out_ld, int accumulate, void* stream) {
+  if (partials == nullptr || out == nullptr || splits < 1 || M <= 0 || N <= 0 || (N % 4) || (out_ld % 4) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(partials) & 15))
+    return set_error("fam_vae_splitk_reduce: bad arguments");
+  vae_splitk_kernel<<<grid_for(M * (N / 4), kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      partials, splits, M, N, static_cast<const __nv_bfloat16*>(bias), out, out_ld, accumulate);
+  return launched("vae_splitk_kernel");
 }
 
 }  // extern "C"

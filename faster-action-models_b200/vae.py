@@ -133,6 +133,11 @@ class VideoVAE38Encoder:
                 col = max(col, 9 * blk["dout"] * hh * ww)
         pl = hh * ww
         dev = self.device
+        # split-K partials of the few-tile GEMMs (every GEMM at the last two resolutions)
+        part = 0
+        for (m, n, k) in ((pl * 4, dims[-1], 9 * dims[-1]), (pl, dims[-1], 9 * dims[-1]), (pl, 3 * dims[-1], dims[-1]),
+                          (pl, 2 * self.z_dim, 9 * dims[-1]), (pl, 2 * self.z_dim, 2 * self.z_dim)):
+            part = max(part, self._splits(m, n, k) * m * n)
         f32 = lambda n: torch.empty(n, device=dev, dtype=torch.float32)
         b16 = lambda n: torch.empty(n, device=dev, dtype=torch.bfloat16)
         c = dims[-1]
@@ -142,7 +147,7 @@ class VideoVAE38Encoder:
             t=b16(pmax * cmax), raw=b16(pmax * cmax),
             qkv=b16(pl * 3 * c), s=f32(pl * pl), pm=b16(pl * pl), vt=b16(c * pl), o=b16(pl * c),
             z=f32(pl * 2 * self.z_dim), mu=f32(pl * 2 * self.z_dim),
-            mean=f32(self.z_dim), inv_std=f32(self.z_dim), out=f32(self.z_dim * pl),
+            mean=f32(self.z_dim), inv_std=f32(self.z_dim), out=f32(self.z_dim * pl), part=f32(max(part, 4)),
         )
         self._bufs[key] = bufs
         return bufs
@@ -151,6 +156,33 @@ class VideoVAE38Encoder:
     @staticmethod
     def _m(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
         return buf[: rows * cols].view(rows, cols)
+
+    @staticmethod
+    def _splits(M: int, N: int, K: int) -> int:
+        """Split-K factor for a convolution GEMM with fewer 128 x 256 tiles than
+        half the SMs (the low-resolution layers): fill about one wave."""
+        tiles = ((M + 127) // 128) * ((N + 255) // 256)
+        if tiles * 2 > 148:
+            return 1
+        return max(1, min(148 // tiles, (K + 63) // 64 // 4))
+
+    def _gemm(self, bufs, a, cv: "_Conv", out=None, residual=None):
+        """out = a W^T + b (fp32 store) or residual += a W^T + b."""
+        M, K = a.shape
+        N = cv.cout
+        sp = self._splits(M, N, K) if N % 4 == 0 else 1
+        if sp == 1:
+            if residual is not None:
+                ops.gemm(a, cv.w, bias=cv.b, residual=residual)
+            else:
+                ops.gemm(a, cv.w, bias=cv.b, out=out, out_dtype=torch.float32)
+            return
+        part = bufs["part"][: sp * M * N].view(sp, M, N)
+        ops.gemm(a, cv.w, splits=sp, out=part)
+        dst = residual if residual is not None else out
+        check(lib().fam_vae_splitk_reduce(C.c_void_p(part.data_ptr()), sp, M, N, C.c_void_p(_ptr(cv.b)),
+                                          C.c_void_p(dst.data_ptr()), dst.stride(0),
+                                          1 if residual is not None else 0, _stream()), "fam_vae_splitk_reduce")
 
     def _rms(self, x, P, Cc, gamma, silu, out=None, raw=None):
         check(lib().fam_vae_rms(C.c_void_p(x.data_ptr()), Cc, P, Cc, C.c_void_p(_ptr(gamma)), 1 if silu else 0,
@@ -162,10 +194,7 @@ class VideoVAE38Encoder:
                                    Ho, Wo, C.c_void_p(bufs["col"].data_ptr()), 9 * cin, _stream()),
               "fam_vae_im2col")
         col = self._m(bufs["col"], Ho * Wo, 9 * cin)
-        if residual is not None:
-            ops.gemm(col, cv.w, bias=cv.b, residual=residual)
-        else:
-            ops.gemm(col, cv.w, bias=cv.b, out=out, out_dtype=torch.float32)
+        self._gemm(bufs, col, cv, out=out, residual=residual)
 
     def _res(self, bufs, rb, xi, H, W):
         """ResidualBlock (wan_video_vae.py:267-302); returns the output stream index."""
@@ -183,7 +212,7 @@ class VideoVAE38Encoder:
             return xi
         xo = (xi + 1) % 3
         XO = self._m(bufs["x"][xo], P, cout)
-        ops.gemm(raw, rb["sc"].w, bias=rb["sc"].b, out=XO, out_dtype=torch.float32)
+        self._gemm(bufs, raw, rb["sc"], out=XO)
         self._conv3(bufs, T2, H, W, rb["c2"], 1, H, W, residual=XO)
         return xo
 
@@ -205,7 +234,7 @@ class VideoVAE38Encoder:
                                       C.c_void_p(VT.data_ptr()), P, _stream()), "fam_vae_transpose")
         O = self._m(bufs["o"], P, c)
         ops.gemm(PM, VT, out=O)
-        ops.gemm(O, a["proj"].w, bias=a["proj"].b, residual=X)
+        self._gemm(bufs, O, a["proj"], residual=X)
 
     def _run(self, bufs, H, W):
         h, w = H // 2, W // 2
@@ -251,7 +280,7 @@ class VideoVAE38Encoder:
         RAW = self._m(bufs["raw"], P, z2)
         self._rms(Z, P, z2, None, False, raw=RAW)
         MU = self._m(bufs["mu"], P, z2)
-        ops.gemm(RAW, self.conv1.w, bias=self.conv1.b, out=MU, out_dtype=torch.float32)
+        self._gemm(bufs, RAW, self.conv1, out=MU)
         check(lib().fam_vae_latent(C.c_void_p(MU.data_ptr()), z2, P, self.z_dim,
                                    C.c_void_p(bufs["mean"].data_ptr()), C.c_void_p(bufs["inv_std"].data_ptr()),
                                    C.c_void_p(bufs["out"].data_ptr()), _stream()), "fam_vae_latent")

@@ -480,6 +480,10 @@ FAM_API int fam_vae_softmax(const float* s, int64_t s_ld, int rows, int cols, fl
 /* bf16 transpose dst[c][r] = src[r][c]. */
 FAM_API int fam_vae_transpose(const void* src, int64_t src_ld, int rows, int cols, void* dst,
                               int64_t dst_ld, void* stream);
+/* out f32 [M, N] (+= when accumulate) bias + sum over splits of the split-K
+ * GEMM partials f32 [splits, M, N] (fam_gemm FAM_EPI_PARTIAL). */
+FAM_API int fam_vae_splitk_reduce(const float* partials, int splits, int64_t M, int N, const void* bias,
+                                  float* out, int64_t out_ld, int accumulate, void* stream);
 /* out f32 [z, P] = (mu[:, :z] - mean) * inv_std (VideoVAE38_.encode, :1296-1303). */
 FAM_API int fam_vae_latent(const float* mu, int64_t mu_ld, int64_t P, int z, const float* mean,
                            const float* inv_std, float* out, void* stream);
