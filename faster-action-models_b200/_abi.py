@@ -183,9 +183,9 @@ def declare_vae(lib) -> None:
     """Wan2.2 VAE encode pieces (include/fam.h, fam_vae_*)."""
     i32, i64, f32 = C.c_int32, C.c_int64, C.c_float
     fp = C.POINTER(C.c_float)
-    lib.fam_vae_patchify.argtypes = [vp, i32, i32, vp, vp]
+    lib.fam_vae_patchify.argtypes = [vp, i32, i32, vp, i64, i32, vp]
     lib.fam_vae_im2col.argtypes = [vp, i64, i32, i32, i32, i32, i32, i32, i32, vp, i64, vp]
-    lib.fam_vae_rms.argtypes = [vp, i64, i64, i32, vp, i32, vp, i64, vp, i64, vp]
+    lib.fam_vae_rms.argtypes = [vp, i64, i64, i32, vp, i32, vp, i64, i32, vp, i64, vp]
     lib.fam_vae_avg_down_add.argtypes = [vp, i64, i32, i32, i32, i32, i32, i32, vp, i64, vp]
     lib.fam_vae_softmax.argtypes = [vp, i64, i32, i32, f32, vp, i64, vp]
     lib.fam_vae_transpose.argtypes = [vp, i64, i32, i32, vp, i64, vp]

@@ -166,9 +166,17 @@ int fam_gemm(const fam_gemm_desc* d, void* stream) {
     skf = reinterpret_cast<unsigned*>(static_cast<char*>(d->scratch) + part);
     skb = part;
   }
-  int rc = gemm_plan(&p, d->a, d->lda, d->b, d->ldb, d->m, d->n, d->k, d->splits, d->tile_n, e,
-                     d->a_is_const != 0, d->b_is_const != 0, device_status_word(), skp, skf, skb,
-                     d->split_round != 0);
+  int rc;
+  if (d->conv_wp > 0) {
+    if (d->features_on_a || d->conv_cin <= 0 || d->k != 9 * ((d->conv_cin + 63) / 64) * 64 || d->tile_n != 0)
+      return set_error("fam_gemm: convolution needs features_on_a = 0, tile_n = 0 and k = 9 * ceil(cin / 64) * 64");
+    rc = gemm_plan_conv3(&p, d->a, d->lda, d->conv_a_rows, d->conv_cin, d->conv_wp, d->m, d->b, d->ldb, d->n,
+                         d->splits, e, device_status_word());
+  } else {
+    rc = gemm_plan(&p, d->a, d->lda, d->b, d->ldb, d->m, d->n, d->k, d->splits, d->tile_n, e,
+                   d->a_is_const != 0, d->b_is_const != 0, device_status_word(), skp, skf, skb,
+                   d->split_round != 0);
+  }
   if (rc) return rc;
   return check_cuda(gemm_launch(p, static_cast<cudaStream_t>(stream), d->pdl != 0), "fam_gemm launch");
 }

@@ -47,6 +47,9 @@ struct GemmEpilogue {
   long long gate_bstride;
   long long gate_gstride;
   int vec;                  // set by gemm_plan: 16-feature vector path of the store / residual epilogue
+  // > 0: A rows are the padded positions y * conv_wp + x of a 3x3 convolution
+  // (implicit GEMM); output row y * (conv_wp - 2) + x, none for x >= conv_wp - 2
+  int conv_wp;
 };
 
 struct GemmArgs {
@@ -66,6 +69,12 @@ struct GemmArgs {
   int sk_pieces;            // k-pieces per remaining tile (0: no split round)
   float* sk_part;           // [CTAs][128][BN] fp32
   unsigned* sk_flag;        // [CTAs], zero between launches
+  // Implicit 3x3 stride-1 convolution (taps = 9): K block kb reads channel
+  // block kb % tap_kpt of A row m + (t / 3) * tap_wp + t % 3, t = kb / tap_kpt,
+  // from a zero-bordered channels-last activation buffer; B is [N, 9 * tap_kpt * 64].
+  int taps;                 // 1: plain GEMM
+  int tap_wp;
+  int tap_kpt;
 };
 
 struct GemmPlan {
@@ -106,6 +115,12 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
               int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,
               int* status, float* sk_part = nullptr, unsigned* sk_flag = nullptr, size_t sk_bytes = 0,
               bool sk_force = false);
+// Implicit-GEMM 3x3 stride-1 convolution: A is a zero-bordered channels-last
+// buffer [a_rows, cin] (row stride lda) whose rows are the padded positions of
+// a frame of width wp - 2; M = H * wp output rows (epi.conv_wp = wp maps them
+// back); B the packed weight [N, 9 * ceil(cin / 64) * 64].
+int gemm_plan_conv3(GemmPlan* p, const void* A, long long lda, long long a_rows, int cin, int wp, int M,
+                    const void* B, long long ldb, int N, int splits, GemmEpilogue epi, int* status);
 // Streaming-multiprocessor count of the current device, and the split-round scratch it needs.
 int gemm_num_sms();
 size_t gemm_sk_scratch_bytes();

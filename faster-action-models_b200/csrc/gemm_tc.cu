@@ -58,6 +58,26 @@ __host__ __device__ constexpr uint32_t gemm_tmem_cols(int bn) {
   return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
 }
 
+// A operand coordinates (K element, row) of K block kb for output rows from m0
+// (an implicit 3x3 convolution shifts the rows per tap).
+__device__ __forceinline__ void gemm_a_coord(const GemmArgs& a, int kb, int m0, int& ax, int& ay) {
+  if (a.taps > 1) {
+    const int t = kb / a.tap_kpt;
+    ax = (kb - t * a.tap_kpt) * kBK;
+    ay = m0 + (t / 3) * a.tap_wp + (t - (t / 3) * 3);
+  } else {
+    ax = kb * kBK;
+    ay = m0;
+  }
+}
+
+// Output row of A row p (-1: a padding column of an implicit convolution).
+__device__ __forceinline__ int gemm_out_row(const GemmEpilogue& e, int p) {
+  if (e.conv_wp <= 0) return p;
+  const int y = p / e.conv_wp, x = p - y * e.conv_wp;
+  return x < e.conv_wp - 2 ? y * (e.conv_wp - 2) + x : -1;
+}
+
 // Apply the epilogue to 16 accumulator values of A-row `a_row`, B-rows
 // b0..b0+15.
 __device__ __forceinline__ void gemm_epilogue_apply(const GemmArgs& args, const GemmEpilogue& e,
@@ -239,16 +259,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Prologue: constant operand first (may run before the previous kernel ends).
       for (int i = 0; i < pre; ++i) {
         const int kc = (kb_begin + i) * kBK;
+        int ax, ay;
+        gemm_a_coord(args, kb_begin + i, m0, ax, ay);
         uint8_t* sa = smem + i * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
-        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], kc, m0, polA);
+        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], ax, ay, polA);
         if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], kc, n0, polB);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
         const int kc = (kb_begin + i) * kBK;
+        int ax, ay;
+        gemm_a_coord(args, kb_begin + i, m0, ax, ay);
         uint8_t* sa = smem + i * STAGE_BYTES;
-        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], kc, m0, polA);
+        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], ax, ay, polA);
         if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], kc, n0, polB);
       }
       int issued = pre;
@@ -261,9 +285,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         const int kc = (kb_begin + i) * kBK;
+        int ax, ay;
+        gemm_a_coord(args, kb_begin + i, m0, ax, ay);
         uint8_t* sa = smem + s * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-        tma_load_2d(sa, &tmA, &full[s], kc, m0, polA);
+        tma_load_2d(sa, &tmA, &full[s], ax, ay, polA);
         tma_load_2d(sa + A_BYTES, &tmB, &full[s], kc, n0, polB);
         issued = i + 1;
       }
@@ -314,7 +340,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[16];
         __syncwarp();
         tmem_ld16(tmem_base + (static_cast<uint32_t>(sp * 32) << 16) + c, v);
-        if (a_row < args.M) gemm_epilogue_apply(args, e, a_row, n0 + c, split, v);
+        const int orow = gemm_out_row(e, a_row);
+        if (a_row < args.M && orow >= 0) gemm_epilogue_apply(args, e, orow, n0 + c, split, v);
       }
     }
   }
@@ -373,7 +400,9 @@ template <int BN>
 __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_t tacc, int r, int a_row, int n0,
                                                    int c0, int cs, const float* padd, int npart) {
   const GemmEpilogue& e = args.epi;
-  const bool row_ok = a_row < args.M;
+  const int out_row = gemm_out_row(e, a_row);
+  const bool row_ok = a_row < args.M && out_row >= 0;
+  a_row = row_ok ? out_row : 0;  // from here on, the output row
   if (e.vec && e.kind == kEpiResidual) {
     // out[row][f] += g[f] * act(acc + bias[f]); the chunk's fp32 residual and
     // gate row are loaded before its TMEM load so that the latencies overlap
@@ -553,15 +582,19 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
       const int pre = have ? min(kb1 - kb0, STAGES) : 0;
       for (int i = 0; i < pre; ++i) {
+        int ax, ay;
+        gemm_a_coord(args, kb0 + i, m0, ax, ay);
         uint8_t* sa = smem + i * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
-        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], (kb0 + i) * kBK, m0, polA);
+        if (args.a_is_const) tma_load_2d(sa, &tmA, &full[i], ax, ay, polA);
         if (args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], (kb0 + i) * kBK, n0, polB);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
+        int ax, ay;
+        gemm_a_coord(args, kb0 + i, m0, ax, ay);
         uint8_t* sa = smem + i * STAGE_BYTES;
-        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], (kb0 + i) * kBK, m0, polA);
+        if (!args.a_is_const) tma_load_2d(sa, &tmA, &full[i], ax, ay, polA);
         if (!args.b_is_const) tma_load_2d(sa + A_BYTES, &tmB, &full[i], (kb0 + i) * kBK, n0, polB);
       }
       int kb = kb0 + pre, issued = pre;
@@ -579,8 +612,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
           break;
         }
         uint8_t* sa = smem + s * STAGE_BYTES;
+        int ax, ay;
+        gemm_a_coord(args, kb, m0, ax, ay);
         mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-        tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0, polA);
+        tma_load_2d(sa, &tmA, &full[s], ax, ay, polA);
         tma_load_2d(sa + A_BYTES, &tmB, &full[s], kb * kBK, n0, polB);
         issued = it + 1;
         if (++kb == kb1) {
@@ -648,9 +683,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       const int buf = lt & 1;
       if (args.epi.vec && args.epi.kind == kEpiResidual && piece <= 0 && wq == 0) {
         // pull this row's residual segment into L2 while the tile's main loop runs
-        const int row = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN;
+        const int prow = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN;
+        const int row = prow < args.M ? gemm_out_row(args.epi, prow) : -1;
         const int ncols = min(BN, args.N - col);
-        if (row < args.M && ncols > 0)
+        if (row >= 0 && ncols > 0)
           bulk_prefetch_l2(reinterpret_cast<const float*>(args.epi.out) + static_cast<long long>(row) * args.epi.out_sa + col,
                            static_cast<uint32_t>(ncols) * 4u);
       }
@@ -804,6 +840,25 @@ int gemm_pick_bn(int n) {
   return 256;
 }
 
+int gemm_plan_conv3(GemmPlan* p, const void* A, long long lda, long long a_rows, int cin, int wp, int M,
+                    const void* B, long long ldb, int N, int splits, GemmEpilogue epi, int* status) {
+  if (cin <= 0 || (cin % 8) || wp < 3 || a_rows <= 0 || M <= 0 || lda < cin)
+    return set_error("gemm_plan_conv3: bad convolution geometry");
+  const int kpt = (cin + kBK - 1) / kBK;
+  epi.conv_wp = wp;
+  // plan as a plain [M, 9 * kpt * 64] x [N, same]^T problem, then point the A
+  // map at the activation buffer and switch the producer to tap addressing
+  int rc = gemm_plan(p, A, 9LL * kpt * kBK, B, ldb, M, N, 9 * kpt * kBK, splits, 0, epi, false, true, status);
+  if (rc) return rc;
+  if (!make_tmap_bf16_2d(&p->ta, A, static_cast<uint64_t>(a_rows), static_cast<uint64_t>(cin),
+                         static_cast<uint64_t>(lda), kBM))
+    return set_error("gemm_plan_conv3: cuTensorMapEncodeTiled failed for A");
+  p->args.taps = 9;
+  p->args.tap_wp = wp;
+  p->args.tap_kpt = kpt;
+  return 0;
+}
+
 cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
   if (p.persist > 0) {
     switch (p.bn) {
@@ -909,6 +964,9 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
   p->args.sk_pieces = 0;
   p->args.sk_part = nullptr;
   p->args.sk_flag = nullptr;
+  p->args.taps = 1;
+  p->args.tap_wp = 0;
+  p->args.tap_kpt = 0;
   if (sk && p->persist > 0) {
     p->args.sk_full = sk_full;
     p->args.sk_pieces = sk_pieces;

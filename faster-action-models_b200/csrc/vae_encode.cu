@@ -2,9 +2,11 @@
 // FastWAM/src/fastwam/models/wan22/wan_video_vae.py:1285-1304, 619-733).
 //
 // Activations are channels-last [positions, channels] (one frame, batch 1);
-// the residual stream is fp32, GEMM operands bf16.  A 3x3 convolution is an
-// im2col gather into [positions, 9 * C] (K order: dy, dx, c) followed by the
-// tcgen05 GEMM of gemm_tc.cu with the bias / residual epilogue; 1x1
+// the residual stream is fp32, GEMM operands bf16.  A stride-1 3x3
+// convolution is the tcgen05 GEMM of gemm_tc.cu in its implicit-convolution
+// form (per tap the A rows of a zero-bordered buffer shift by dy * (W+2) + dx;
+// RMS_norm and patchify write that layout); a stride-2 one is an im2col
+// gather into [positions, 9 * C] (K order: dy, dx, c) + GEMM; 1x1
 // convolutions are plain GEMMs.  With T = 1 the causal 3-D convolutions see
 // two zero frames in front, so only the last temporal tap of their weights
 // contributes (the host packs that slice).  The kernels here are the
@@ -33,7 +35,7 @@ constexpr int kVaeThreads = 256;
 // output channel c * 4 + r * 2 + q of position (h, w) is image[c][2h + q][2w + r];
 // channels 12..15 are zero padding for the 16-byte GEMM rows.
 __global__ void vae_patchify_kernel(const __nv_bfloat16* __restrict__ img, int H, int W,
-                                    __nv_bfloat16* __restrict__ out) {
+                                    __nv_bfloat16* __restrict__ out, long long out_ld, int pad) {
   const int h2 = H / 2, w2 = W / 2;
   const long long P = static_cast<long long>(h2) * w2;
   for (long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; p < P;
@@ -49,7 +51,8 @@ __global__ void vae_patchify_kernel(const __nv_bfloat16* __restrict__ img, int H
           v[c * 4 + r * 2 + q] = img[(static_cast<long long>(c) * H + 2 * y + q) * W + 2 * x + r];
 #pragma unroll
     for (int c = 12; c < 16; ++c) v[c] = __float2bfloat16(0.f);
-    uint4* o = reinterpret_cast<uint4*>(out + p * 16);
+    const long long orow = pad ? static_cast<long long>(y + 1) * (w2 + 2) + x + 1 : p;
+    uint4* o = reinterpret_cast<uint4*>(out + orow * out_ld);
     o[0] = *reinterpret_cast<const uint4*>(&v[0]);
     o[1] = *reinterpret_cast<const uint4*>(&v[8]);
   }
@@ -79,10 +82,12 @@ __global__ void vae_im2col_kernel(const __nv_bfloat16* __restrict__ src, long lo
 
 // RMS_norm over the channels of each position (wan_video_vae.py:55-70):
 // x / max(||x||, 1e-12) * sqrt(C) * gamma, then SiLU when asked; one warp per
-// position.  raw (nullable) receives bf16(x).
+// position.  raw (nullable) receives bf16(x).  pad_w > 0: out is the
+// zero-bordered buffer of a frame pad_w wide (position p at row
+// (p / pad_w + 1) * (pad_w + 2) + p % pad_w + 1).
 __global__ void vae_rms_kernel(const float* __restrict__ x, long long x_ld, long long P, int C,
                                const __nv_bfloat16* __restrict__ gamma, int silu_on,
-                               __nv_bfloat16* __restrict__ out, long long out_ld,
+                               __nv_bfloat16* __restrict__ out, long long out_ld, int pad_w,
                                __nv_bfloat16* __restrict__ raw, long long raw_ld) {
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
@@ -101,6 +106,8 @@ __global__ void vae_rms_kernel(const float* __restrict__ x, long long x_ld, long
       }
     }
     if (out == nullptr) continue;
+    const int pi = static_cast<int>(p);  // positions < 2^31 (checked on the host)
+    const long long orow = pad_w > 0 ? static_cast<long long>(pi / pad_w + 1) * (pad_w + 2) + pi % pad_w + 1 : p;
     ss = warp_sum(ss);
     const float k = sqrtf(static_cast<float>(C)) / fmaxf(sqrtf(ss), 1e-12f);
     for (int c = 4 * lane; c < C; c += 128) {
@@ -115,7 +122,7 @@ __global__ void vae_rms_kernel(const float* __restrict__ x, long long x_ld, long
       uint2 u;
       u.x = *reinterpret_cast<uint32_t*>(&a);
       u.y = *reinterpret_cast<uint32_t*>(&b);
-      *reinterpret_cast<uint2*>(out + p * out_ld + c) = u;
+      *reinterpret_cast<uint2*>(out + orow * out_ld + c) = u;
     }
   }
 }
@@ -123,23 +130,23 @@ __global__ void vae_rms_kernel(const float* __restrict__ x, long long x_ld, long
 // AvgDown3D (wan_video_vae.py:345-395) of a one-frame input, added into out:
 // the (c, t, ph, pw) flattening of the input with factor_t - 1 zero frames in
 // front is averaged in groups of Cin * factor / Cout consecutive entries.
-__global__ void vae_avg_down_add_kernel(const float* __restrict__ in, long long in_ld, int H, int W, int Cin,
-                                        int Cout, int ft, int fs, float* __restrict__ out, long long out_ld) {
+// (32-bit index arithmetic: the host checks that every index fits.)
+__global__ void vae_avg_down_add_kernel(const float* __restrict__ in, int in_ld, int H, int W, int Cin,
+                                        int Cout, int ft, int fs, float* __restrict__ out, int out_ld) {
   const int Ho = H / fs, Wo = W / fs;
   const int factor = ft * fs * fs, grp = Cin * factor / Cout;
-  const long long total = static_cast<long long>(Ho) * Wo * Cout;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int o = static_cast<int>(i % Cout);
-    const long long p = i / Cout;
-    const int y = static_cast<int>(p / Wo), x = static_cast<int>(p % Wo);
+  const int total = Ho * Wo * Cout;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int o = i % Cout;
+    const int p = i / Cout;
+    const int y = p / Wo, x = p - y * Wo;
     float acc = 0.f;
     for (int j = 0; j < grp; ++j) {
       const int f = o * grp + j;
       const int c = f / factor, rem = f % factor;
       const int t = rem / (fs * fs), ph = (rem / fs) % fs, pw = rem % fs;
       if (t < ft - 1) continue;  // a zero frame of the temporal padding
-      acc += in[(static_cast<long long>(y * fs + ph) * W + x * fs + pw) * in_ld + c];
+      acc += __ldg(in + ((y * fs + ph) * W + x * fs + pw) * in_ld + c);
     }
     out[p * out_ld + o] += acc / static_cast<float>(grp);
   }
@@ -201,16 +208,15 @@ __global__ void vae_latent_kernel(const float* __restrict__ mu, long long mu_ld,
 }
 
 // out[m][n] (+)= bias[n] + sum_s part[s][m][n], four columns per thread.
-__global__ void vae_splitk_kernel(const float* __restrict__ part, int splits, long long M, int N,
-                                  const __nv_bfloat16* __restrict__ bias, float* __restrict__ out, long long out_ld,
+__global__ void vae_splitk_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                  const __nv_bfloat16* __restrict__ bias, float* __restrict__ out, int out_ld,
                                   int accumulate) {
   const int nq = N / 4;
-  const long long total = M * nq;
-  const long long sstride = M * N;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long m = i / nq;
-    const int n = static_cast<int>(i % nq) * 4;
+  const int total = M * nq;
+  const long long sstride = static_cast<long long>(M) * N;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int m = i / nq;
+    const int n = (i - m * nq) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     if (bias != nullptr) {
       const float2 b0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + n));
@@ -218,10 +224,10 @@ __global__ void vae_splitk_kernel(const float* __restrict__ part, int splits, lo
       a = make_float4(b0.x, b0.y, b1.x, b1.y);
     }
     for (int sp = 0; sp < splits; ++sp) {
-      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + sp * sstride + m * N + n));
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + sp * sstride + static_cast<long long>(m) * N + n));
       a = make_float4(a.x + v.x, a.y + v.y, a.z + v.z, a.w + v.w);
     }
-    float4* o = reinterpret_cast<float4*>(out + m * out_ld + n);
+    float4* o = reinterpret_cast<float4*>(out + static_cast<long long>(m) * out_ld + n);
     if (accumulate) {
       const float4 r = *o;
       a = make_float4(a.x + r.x, a.y + r.y, a.z + r.z, a.w + r.w);
@@ -245,13 +251,14 @@ using namespace fam;
 
 extern "C" {
 
-int fam_vae_patchify(const void* image, int H, int W, void* out, void* stream) {
-  if (image == nullptr || out == nullptr || H <= 0 || W <= 0 || (H % 2) || (W % 2))
+int fam_vae_patchify(const void* image, int H, int W, void* out, int64_t out_ld, int pad, void* stream) {
+  if (image == nullptr || out == nullptr || H <= 0 || W <= 0 || (H % 2) || (W % 2) || out_ld < 16)
     return set_error("fam_vae_patchify: bad arguments");
-  if (reinterpret_cast<uintptr_t>(out) & 15) return set_error("fam_vae_patchify: output must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (out_ld % 8))
+    return set_error("fam_vae_patchify: output rows must be 16-byte aligned");
   const long long P = static_cast<long long>(H / 2) * (W / 2);
   vae_patchify_kernel<<<grid_for(P, kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(image), H, W, static_cast<__nv_bfloat16*>(out));
+      static_cast<const __nv_bfloat16*>(image), H, W, static_cast<__nv_bfloat16*>(out), out_ld, pad);
   return launched("vae_patchify_kernel");
 }
 
@@ -270,16 +277,17 @@ int fam_vae_im2col(const void* src, int64_t src_ld, int H, int W, int C, int str
 }
 
 int fam_vae_rms(const float* x, int64_t x_ld, int64_t P, int C, const void* gamma, int silu_on, void* out,
-                int64_t out_ld, void* raw, int64_t raw_ld, void* stream) {
+                int64_t out_ld, int out_pad_w, void* raw, int64_t raw_ld, void* stream) {
   if (x == nullptr || P <= 0 || C <= 0 || (C % 4) || (x_ld % 4) || (out == nullptr && raw == nullptr) ||
       (out != nullptr && gamma == nullptr))
     return set_error("fam_vae_rms: bad arguments");
   if ((out != nullptr && (out_ld % 4)) || (raw != nullptr && (raw_ld % 4)))
     return set_error("fam_vae_rms: output row strides must be multiples of 4 elements");
+  if (P >= (1LL << 31)) return set_error("fam_vae_rms: too many positions");
   const long long warps = P;
   vae_rms_kernel<<<grid_for(warps * 32, kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       x, x_ld, P, C, static_cast<const __nv_bfloat16*>(gamma), silu_on, static_cast<__nv_bfloat16*>(out), out_ld,
-      static_cast<__nv_bfloat16*>(raw), raw_ld);
+      out_pad_w, static_cast<__nv_bfloat16*>(raw), raw_ld);
   return launched("vae_rms_kernel");
 }
 
@@ -289,8 +297,10 @@ int fam_vae_avg_down_add(const float* in, int64_t in_ld, int H, int W, int Cin, 
       factor_s < 1 || (H % factor_s) || (W % factor_s) || ((Cin * factor_t * factor_s * factor_s) % Cout))
     return set_error("fam_vae_avg_down_add: bad arguments");
   const long long total = static_cast<long long>(H / factor_s) * (W / factor_s) * Cout;
+  if (static_cast<long long>(H) * W * in_ld >= (1LL << 31) || total * out_ld / Cout >= (1LL << 31))
+    return set_error("fam_vae_avg_down_add: frame too large for 32-bit indexing");
   vae_avg_down_add_kernel<<<grid_for(total, kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      in, in_ld, H, W, Cin, Cout, factor_t, factor_s, out, out_ld);
+      in, static_cast<int>(in_ld), H, W, Cin, Cout, factor_t, factor_s, out, static_cast<int>(out_ld));
   return launched("vae_avg_down_add_kernel");
 }
 
@@ -325,8 +335,11 @@ int fam_vae_splitk_reduce(const float* partials, int splits, int64_t M, int N, c
   if (partials == nullptr || out == nullptr || splits < 1 || M <= 0 || N <= 0 || (N % 4) || (out_ld % 4) ||
       (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(partials) & 15))
     return set_error("fam_vae_splitk_reduce: bad arguments");
+  if (M * N >= (1LL << 31) || M * out_ld >= (1LL << 31))
+    return set_error("fam_vae_splitk_reduce: too large for 32-bit indexing");
   vae_splitk_kernel<<<grid_for(M * (N / 4), kVaeThreads), kVaeThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      partials, splits, M, N, static_cast<const __nv_bfloat16*>(bias), out, out_ld, accumulate);
+      partials, splits, static_cast<int>(M), N, static_cast<const __nv_bfloat16*>(bias), out,
+      static_cast<int>(out_ld), accumulate);
   return launched("vae_splitk_kernel");
 }
 

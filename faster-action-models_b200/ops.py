@@ -101,6 +101,45 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
     return out
 
 
+def conv3x3(act: torch.Tensor, cin: int, wp: int, H: int, w: torch.Tensor, *, out: torch.Tensor,
+            bias: Optional[torch.Tensor] = None, accumulate: bool = False, splits: int = 1) -> torch.Tensor:
+    """Implicit-GEMM 3x3 stride-1 convolution on the tensor cores.
+
+    act: bf16 zero-bordered channels-last buffer, row (y + 1) * wp + (x + 1) holds
+    position (y, x) of an H x (wp - 2) frame (cin channels, row stride act.stride(0));
+    w: bf16 [N, 9 * ceil(cin / 64) * 64], K order (dy, dx, c) with each tap's
+    channels zero-padded to whole 64-blocks.  out: fp32 [H * (wp - 2), N] stored, or
+    accumulated into when `accumulate`; with splits > 1, out is the fp32 partial
+    buffer [splits, H * (wp - 2), N] (no bias)."""
+    _require(act, torch.bfloat16, "act")
+    _require(w, torch.bfloat16, "w")
+    kpt = (cin + 63) // 64
+    N, K = w.shape
+    if K != 9 * kpt * 64 or act.stride(-1) != 1 or w.stride(1) != 1:
+        raise ValueError(f"conv3x3: weight {tuple(w.shape)} for {cin} channels")
+    M = H * wp
+    Mo = H * (wp - 2)
+    d = GemmDesc()
+    d.a, d.lda, d.b, d.ldb = act.data_ptr(), act.stride(0), w.data_ptr(), w.stride(0)
+    d.m, d.n, d.k = M, N, K
+    d.splits = splits
+    d.activation = _lib.FAM_ACT_NONE
+    d.b_is_const = 1
+    d.conv_wp, d.conv_cin, d.conv_a_rows = wp, cin, act.shape[0]
+    d.out_dtype = _lib.FAM_DTYPE_F32
+    if splits > 1:
+        d.epilogue = _lib.FAM_EPI_PARTIAL
+        d.out_stride_split = Mo * N
+    else:
+        d.epilogue = _lib.FAM_EPI_RESIDUAL if accumulate else _lib.FAM_EPI_STORE
+        d.bias = _ptr(bias)
+        d.tokens_per_batch = Mo
+    _require(out, torch.float32, "out")
+    d.out, d.out_stride_a, d.out_stride_b = out.data_ptr(), out.stride(-2), 1
+    check(lib().fam_gemm(C.byref(d), C.c_void_p(_stream())), "fam_gemm (conv3x3)")
+    return out
+
+
 _SK = {}
 
 

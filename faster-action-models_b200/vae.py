@@ -7,9 +7,10 @@ wan22/wan_video_vae.py:1285-1304), for the first frame (T = 1), which is all
 the action-chunk prologue encodes.  Parameters load from the reference's
 state dict names (``encoder.*``, ``conv1.*``).
 
-Every step runs in libfam (include/fam.h): 3x3 convolutions as
-``fam_vae_im2col`` + the tcgen05 GEMM (bias / residual epilogues), 1x1
-convolutions as GEMMs, RMS_norm(+SiLU), the AvgDown3D shortcut, the one-head
+Every step runs in libfam (include/fam.h): stride-1 3x3 convolutions as the
+tcgen05 GEMM's implicit convolution (``ops.conv3x3``: per tap the A rows of a
+zero-bordered channels-last buffer shift by dy * (W + 2) + dx), the stride-2
+ones as ``fam_vae_im2col`` + GEMM, 1x1 convolutions as GEMMs, RMS_norm(+SiLU), the AvgDown3D shortcut, the one-head
 attention (scores GEMM, row softmax, P V GEMM) and the latent normalisation
 as ``fam_vae_*`` kernels.  The sequence is captured once per frame size in a
 CUDA graph.  With T = 1 every CausalConv3d sees two zero frames in front
@@ -80,7 +81,10 @@ class VideoVAE38Encoder:
         for c in dims + [2 * z_dim]:
             if c % 8:
                 raise ValueError(f"channel count {c} is not a multiple of 8")
-        self.conv_in = conv("encoder.conv1", 16)      # patchified 12 channels, padded to 16
+        c64 = lambda c: (c + 63) // 64 * 64           # implicit convolutions: whole 64-channel K blocks per tap
+        self._c64 = c64
+        conv = lambda name, cin_p: _Conv(sd[name + ".weight"], sd.get(name + ".bias"), cin_p, dev)
+        self.conv_in = conv("encoder.conv1", 64)      # patchified 12 channels (16 in the buffer)
         self.blocks = []
         n = len(self.dim_mult)
         for i, (din, dout) in enumerate(zip(dims[:-1], dims[1:])):
@@ -99,15 +103,15 @@ class VideoVAE38Encoder:
                          proj=conv("encoder.middle.1.proj", c))
         self.mid2 = self._res_block(sd, "encoder.middle.2", c, c, g, conv)
         self.head_gamma = g("encoder.head.0")
-        self.head = conv("encoder.head.2", c)
+        self.head = conv("encoder.head.2", c64(c))
         self.conv1 = conv("conv1", 2 * z_dim)
         self._bufs = {}
         self._graphs = {}
 
-    @staticmethod
-    def _res_block(sd, pre, cin, cout, g, conv):
-        return dict(cin=cin, cout=cout, g0=g(pre + ".residual.0"), c1=conv(pre + ".residual.2", cin),
-                    g1=g(pre + ".residual.3"), c2=conv(pre + ".residual.6", cout),
+    def _res_block(self, sd, pre, cin, cout, g, conv):
+        c64 = self._c64
+        return dict(cin=cin, cout=cout, g0=g(pre + ".residual.0"), c1=conv(pre + ".residual.2", c64(cin)),
+                    g1=g(pre + ".residual.3"), c2=conv(pre + ".residual.6", c64(cout)),
                     sc=conv(pre + ".shortcut", cin) if (pre + ".shortcut.weight") in sd else None)
 
     # ------------------------------------------------------------- buffers
@@ -124,33 +128,62 @@ class VideoVAE38Encoder:
         h, w = H // 2, W // 2
         pmax = h * w
         cmax = max(dims + [2 * self.z_dim, 16])
-        # im2col of the widest convolution at each resolution
-        col, hh, ww = 9 * 16 * pmax, h, w
-        for i, blk in enumerate(self.blocks):
-            col = max(col, 9 * max(blk["din"], blk["dout"]) * hh * ww)
+        dev = self.device
+        # zero-bordered conv inputs, one per resolution, rows as wide as the
+        # widest input channel count there (the border is never written);
+        # im2col only for the stride-2 resample convolutions
+        tp, col, hh, ww, cins = {}, 8, h, w, [16]
+        for blk in self.blocks:
+            cins += [blk["din"], blk["dout"]]
             if blk["down"]:
+                tp[(hh, ww)] = max(cins)
                 hh, ww = hh // 2, ww // 2
                 col = max(col, 9 * blk["dout"] * hh * ww)
+                cins = [blk["dout"]]
+        tp[(hh, ww)] = max(cins + [dims[-1]])
+        tp = {k: torch.zeros(((k[0] + 2) * (k[1] + 2), c), device=dev, dtype=torch.bfloat16) for k, c in tp.items()}
         pl = hh * ww
-        dev = self.device
-        # split-K partials of the few-tile GEMMs (every GEMM at the last two resolutions)
-        part = 0
-        for (m, n, k) in ((pl * 4, dims[-1], 9 * dims[-1]), (pl, dims[-1], 9 * dims[-1]), (pl, 3 * dims[-1], dims[-1]),
-                          (pl, 2 * self.z_dim, 9 * dims[-1]), (pl, 2 * self.z_dim, 2 * self.z_dim)):
-            part = max(part, self._splits(m, n, k) * m * n)
+        # split-K partials: the largest of every GEMM the encode issues
+        part = 4
+        for (m, n, k, mo) in self._gemm_shapes(H, W):
+            if n % 4 == 0:
+                part = max(part, self._splits(m, n, k) * mo * n)
         f32 = lambda n: torch.empty(n, device=dev, dtype=torch.float32)
         b16 = lambda n: torch.empty(n, device=dev, dtype=torch.bfloat16)
         c = dims[-1]
         bufs = dict(
-            image=b16(3 * H * W), patch=b16(pmax * 16), col=b16(col),
+            image=b16(3 * H * W), col=b16(col), tp=tp, part=f32(part),
             x=[f32(pmax * cmax) for _ in range(3)], y=f32(pmax * cmax), xin=f32(pmax * cmax),
-            t=b16(pmax * cmax), raw=b16(pmax * cmax),
+            raw=b16(pmax * cmax), t=b16(pl * c),
             qkv=b16(pl * 3 * c), s=f32(pl * pl), pm=b16(pl * pl), vt=b16(c * pl), o=b16(pl * c),
             z=f32(pl * 2 * self.z_dim), mu=f32(pl * 2 * self.z_dim),
-            mean=f32(self.z_dim), inv_std=f32(self.z_dim), out=f32(self.z_dim * pl), part=f32(max(part, 4)),
+            mean=f32(self.z_dim), inv_std=f32(self.z_dim), out=f32(self.z_dim * pl),
         )
         self._bufs[key] = bufs
         return bufs
+
+    def _gemm_shapes(self, H: int, W: int):
+        """(M, N, K, output rows) of every split-capable GEMM of one encode, in order."""
+        c64 = self._c64
+        h, w = H // 2, W // 2
+        out = [(h * (w + 2), self.dim, 9 * 64, h * w)]                   # conv_in
+        def rb_shapes(cin, cout):
+            r = [(h * (w + 2), cout, 9 * c64(cin), h * w), (h * (w + 2), cout, 9 * c64(cout), h * w)]
+            if cin != cout:
+                r.append((h * w, cout, cin, h * w))                       # 1x1 shortcut
+            return r
+        for blk in self.blocks:
+            cin = blk["din"]
+            for _ in blk["rbs"]:
+                out += rb_shapes(cin, blk["dout"])
+                cin = blk["dout"]
+            if blk["down"]:
+                h, w = h // 2, w // 2
+                out.append((h * w, blk["dout"], 9 * blk["dout"], h * w))  # stride-2 resample (im2col)
+        c, z2 = self.dim * self.dim_mult[-1], 2 * self.z_dim
+        out += rb_shapes(c, c) + [(h * w, c, c, h * w)] + rb_shapes(c, c)  # middle, attention proj
+        out += [(h * (w + 2), z2, 9 * c64(c), h * w), (h * w, z2, z2, h * w)]  # head, conv1
+        return out
 
     # ----------------------------------------------------------- pieces
     @staticmethod
@@ -184,9 +217,28 @@ class VideoVAE38Encoder:
                                           C.c_void_p(dst.data_ptr()), dst.stride(0),
                                           1 if residual is not None else 0, _stream()), "fam_vae_splitk_reduce")
 
-    def _rms(self, x, P, Cc, gamma, silu, out=None, raw=None):
+    def _rms(self, x, P, Cc, gamma, silu, out=None, raw=None, pad_w=0):
+        out_ld = out.stride(0) if out is not None else Cc
         check(lib().fam_vae_rms(C.c_void_p(x.data_ptr()), Cc, P, Cc, C.c_void_p(_ptr(gamma)), 1 if silu else 0,
-                                C.c_void_p(_ptr(out)), Cc, C.c_void_p(_ptr(raw)), Cc, _stream()), "fam_vae_rms")
+                                C.c_void_p(_ptr(out)), out_ld, pad_w, C.c_void_p(_ptr(raw)), Cc, _stream()),
+              "fam_vae_rms")
+
+    def _conv1(self, bufs, H, W, cin, cv: _Conv, out=None, residual=None):
+        """Stride-1 3x3 convolution of the zero-bordered buffer of this resolution."""
+        tp = bufs["tp"][(H, W)]
+        M, N, K = H * (W + 2), cv.cout, cv.w.shape[1]
+        sp = self._splits(M, N, K) if N % 4 == 0 else 1
+        if sp == 1:
+            dst = residual if residual is not None else out
+            ops.conv3x3(tp, cin, W + 2, H, cv.w, out=dst, bias=cv.b, accumulate=residual is not None)
+            return
+        Mo = H * W
+        part = bufs["part"][: sp * Mo * N].view(sp, Mo, N)
+        ops.conv3x3(tp, cin, W + 2, H, cv.w, out=part, splits=sp)
+        dst = residual if residual is not None else out
+        check(lib().fam_vae_splitk_reduce(C.c_void_p(part.data_ptr()), sp, Mo, N, C.c_void_p(_ptr(cv.b)),
+                                          C.c_void_p(dst.data_ptr()), dst.stride(0),
+                                          1 if residual is not None else 0, _stream()), "fam_vae_splitk_reduce")
 
     def _conv3(self, bufs, src, H, W, cv: _Conv, stride, Ho, Wo, out=None, residual=None):
         cin = cv.cin_p
@@ -200,20 +252,19 @@ class VideoVAE38Encoder:
         """ResidualBlock (wan_video_vae.py:267-302); returns the output stream index."""
         P, cin, cout = H * W, rb["cin"], rb["cout"]
         X = self._m(bufs["x"][xi], P, cin)
-        T = self._m(bufs["t"], P, cin)
+        tp = bufs["tp"][(H, W)]
         raw = self._m(bufs["raw"], P, cin) if rb["sc"] is not None else None
-        self._rms(X, P, cin, rb["g0"], True, out=T, raw=raw)
+        self._rms(X, P, cin, rb["g0"], True, out=tp, raw=raw, pad_w=W)
         Y = self._m(bufs["y"], P, cout)
-        self._conv3(bufs, T, H, W, rb["c1"], 1, H, W, out=Y)
-        T2 = self._m(bufs["t"], P, cout)
-        self._rms(Y, P, cout, rb["g1"], True, out=T2)
+        self._conv1(bufs, H, W, cin, rb["c1"], out=Y)
+        self._rms(Y, P, cout, rb["g1"], True, out=tp, pad_w=W)
         if rb["sc"] is None:
-            self._conv3(bufs, T2, H, W, rb["c2"], 1, H, W, residual=X)
+            self._conv1(bufs, H, W, cout, rb["c2"], residual=X)
             return xi
         xo = (xi + 1) % 3
         XO = self._m(bufs["x"][xo], P, cout)
         self._gemm(bufs, raw, rb["sc"], out=XO)
-        self._conv3(bufs, T2, H, W, rb["c2"], 1, H, W, residual=XO)
+        self._conv1(bufs, H, W, cout, rb["c2"], residual=XO)
         return xo
 
     def _attention(self, bufs, xi, H, W):
@@ -238,11 +289,12 @@ class VideoVAE38Encoder:
 
     def _run(self, bufs, H, W):
         h, w = H // 2, W // 2
-        check(lib().fam_vae_patchify(C.c_void_p(bufs["image"].data_ptr()), H, W,
-                                     C.c_void_p(bufs["patch"].data_ptr()), _stream()), "fam_vae_patchify")
+        tp0 = bufs["tp"][(h, w)]
+        check(lib().fam_vae_patchify(C.c_void_p(bufs["image"].data_ptr()), H, W, C.c_void_p(tp0.data_ptr()),
+                                     tp0.stride(0), 1, _stream()), "fam_vae_patchify")
         xi = 0
         X = self._m(bufs["x"][xi], h * w, self.dim)
-        self._conv3(bufs, self._m(bufs["patch"], h * w, 16), h, w, self.conv_in, 1, h, w, out=X)
+        self._conv1(bufs, h, w, 16, self.conv_in, out=X)
         for blk in self.blocks:
             P = h * w
             XIN = self._m(bufs["xin"], P, blk["din"])
@@ -273,10 +325,9 @@ class VideoVAE38Encoder:
         xi = self._res(bufs, self.mid2, xi, h, w)
         P, c, z2 = h * w, self.dim * self.dim_mult[-1], 2 * self.z_dim
         X = self._m(bufs["x"][xi], P, c)
-        T = self._m(bufs["t"], P, c)
-        self._rms(X, P, c, self.head_gamma, True, out=T)
+        self._rms(X, P, c, self.head_gamma, True, out=bufs["tp"][(h, w)], pad_w=w)
         Z = self._m(bufs["z"], P, z2)
-        self._conv3(bufs, T, h, w, self.head, 1, h, w, out=Z)
+        self._conv1(bufs, h, w, c, self.head, out=Z)
         RAW = self._m(bufs["raw"], P, z2)
         self._rms(Z, P, z2, None, False, raw=RAW)
         MU = self._m(bufs["mu"], P, z2)

@@ -116,6 +116,15 @@ typedef struct fam_gemm_desc {
   void* scratch;
   size_t scratch_bytes;
   int32_t split_round;
+  /* Implicit 3x3 stride-1 convolution when conv_wp > 0: a is a zero-bordered
+   * channels-last activation buffer [conv_a_rows, conv_cin] (row stride lda)
+   * whose rows are the padded positions y * conv_wp + x of a frame of width
+   * conv_wp - 2; m = H * conv_wp; b is [n, k] with k = 9 * ceil(conv_cin / 64) * 64
+   * (per tap (dy, dx) a block of the input channels, zero-padded to 64);
+   * output row y * (conv_wp - 2) + x for x < conv_wp - 2. */
+  int32_t conv_wp;
+  int32_t conv_cin;
+  int64_t conv_a_rows;
 } fam_gemm_desc;
 
 FAM_API int fam_gemm(const fam_gemm_desc* desc, void* stream);
@@ -460,17 +469,21 @@ FAM_API int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_w
  * 3x3 convolutions are fam_vae_im2col + fam_gemm, 1x1 convolutions fam_gemm.
  * -------------------------------------------------------------------------- */
 /* patchify(2) (wan_video_vae.py:199-212) of a bf16 [3, H, W] frame into
- * out bf16 [(H/2)(W/2), 16], channel c*4 + r*2 + q (channels 12..15 zero). */
-FAM_API int fam_vae_patchify(const void* image, int H, int W, void* out, void* stream);
+ * out bf16 rows of 16 channels c*4 + r*2 + q (12..15 zero), row stride out_ld;
+ * pad = 1: the zero-bordered layout of fam_gemm's implicit convolution
+ * (position (y, x) at row (y + 1) * (W/2 + 2) + x + 1). */
+FAM_API int fam_vae_patchify(const void* image, int H, int W, void* out, int64_t out_ld, int pad,
+                             void* stream);
 /* 3x3 gather for a convolution of stride `stride` and top/left zero padding
  * `pad` (bottom/right padding follows from Ho, Wo): dst [Ho*Wo, 9*C] bf16,
  * K order (dy, dx, c).  C, row strides: multiples of 8. */
 FAM_API int fam_vae_im2col(const void* src, int64_t src_ld, int H, int W, int C, int stride, int pad,
                            int Ho, int Wo, void* dst, int64_t dst_ld, void* stream);
 /* RMS_norm over channels (wan_video_vae.py:55-70; + SiLU when silu_on) of the
- * fp32 stream x [P, C] into bf16 out (nullable), and/or bf16(x) into raw. */
+ * fp32 stream x [P, C] into bf16 out (nullable; out_pad_w > 0: the
+ * zero-bordered layout of a frame out_pad_w wide), and/or bf16(x) into raw. */
 FAM_API int fam_vae_rms(const float* x, int64_t x_ld, int64_t P, int C, const void* gamma, int silu_on,
-                        void* out, int64_t out_ld, void* raw, int64_t raw_ld, void* stream);
+                        void* out, int64_t out_ld, int out_pad_w, void* raw, int64_t raw_ld, void* stream);
 /* out += AvgDown3D(in) for a one-frame input (wan_video_vae.py:345-395). */
 FAM_API int fam_vae_avg_down_add(const float* in, int64_t in_ld, int H, int W, int Cin, int Cout,
                                  int factor_t, int factor_s, float* out, int64_t out_ld, void* stream);

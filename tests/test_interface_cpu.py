@@ -118,3 +118,20 @@ def test_elide_backbone_shares_parameters():
     import pytest as _pt
     with _pt.raises(ValueError):
         P.elide_backbone(vid, 4)
+
+
+def test_vae_encoder_param_table_matches_reference_state_dict():
+    """encoder_param_shapes lists exactly the reference VideoVAE38_ encoder parameters
+    (names and shapes of the state dict recorded from the reference in the fixture)."""
+    import importlib
+    from pathlib import Path
+    import torch
+    V = importlib.import_module("faster-action-models_b200.vae")
+    fx = torch.load(Path(__file__).resolve().parent / "golden" / "vae_encode.pt", weights_only=False)
+    want = {k: tuple(v.shape) for k, v in fx["params"].items()}
+    got = V.encoder_param_shapes(dim=fx["cfg"]["dim"], z_dim=fx["cfg"]["z_dim"])
+    assert got == want
+    # the host-side packing accepts them (no device work)
+    enc = V.VideoVAE38Encoder(fx["params"], dim=fx["cfg"]["dim"], z_dim=fx["cfg"]["z_dim"], device="cpu")
+    assert enc.conv_in.w.shape == (fx["cfg"]["dim"], 9 * 64)
+    assert all(s[0] > 0 and s[2] % 8 == 0 for s in enc._gemm_shapes(64, 96))
