@@ -163,7 +163,7 @@ class VideoIO(C.Structure):
                 ("timesteps", C.POINTER(C.c_float)), ("context", vp), ("context_mask", vp),
                 ("rope", vp), ("first_frame_causal", C.c_int32), ("cache_k", C.POINTER(vp)),
                 ("cache_v", C.POINTER(vp)), ("hidden_out", vp), ("workspace", vp),
-                ("workspace_bytes", C.c_size_t)]
+                ("workspace_bytes", C.c_size_t), ("t_out", vp)]
 
 
 def declare_video(lib) -> None:
@@ -174,8 +174,10 @@ def declare_video(lib) -> None:
     lib.fam_video_workspace_size.argtypes = [vp, i32, i32, i32, C.POINTER(sz)]
     lib.fam_video_prefill.argtypes = [vp, C.POINTER(VideoIO), i32, vp]
     lib.fam_video_launch_count.argtypes = [vp, C.POINTER(C.c_int32)]
+    lib.fam_video_head_norm.argtypes = [vp, vp, vp, i32, i32, i32, i32, C.c_float, vp, vp]
+    lib.fam_video_unpatchify.argtypes = [vp, i32, i32, i32, i32, i32, i32, i32, i32, vp, vp]
     for n in ("fam_video_expert_create", "fam_video_expert_destroy", "fam_video_workspace_size",
-              "fam_video_prefill", "fam_video_launch_count"):
+              "fam_video_prefill", "fam_video_launch_count", "fam_video_head_norm", "fam_video_unpatchify"):
         getattr(lib, n).restype = C.c_int
 
 

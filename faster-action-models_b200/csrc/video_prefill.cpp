@@ -210,6 +210,8 @@ int enqueue_prefill(const VCtx& c) {
                    wp<void>(c, c.L.th2), false));
   V_TRYI(gemm_rows(wp<void>(c, c.L.th2), 2 * B, D, w.tproj_w, w.tproj_b, 6 * D, kActNone,
                    wp<void>(c, c.L.tmod), true));
+  if (io.t_out != nullptr)  // t itself (before the SiLU of the projection input), for the output head
+    V_TRYI(gemm_rows(wp<void>(c, c.L.th1), 2 * B, D, w.time2_w, w.time2_b, D, kActNone, io.t_out, false));
   // ---- patch embedding: patchify + GEMM into the fp32 residual stream
   PatchArgs pa = {bf(io.latents), wp<__nv_bfloat16>(c, c.L.patch), B, g.in_dim, io.frames,
                   io.height, io.width, g.patch_t, g.patch_h, g.patch_w};
@@ -474,6 +476,7 @@ int fam_video_prefill(fam_video_expert* e, const fam_video_io* io, int32_t use_g
   key.ptrs = {reinterpret_cast<uintptr_t>(io->workspace), reinterpret_cast<uintptr_t>(io->latents),
               reinterpret_cast<uintptr_t>(io->context), reinterpret_cast<uintptr_t>(io->context_mask),
               reinterpret_cast<uintptr_t>(io->rope), reinterpret_cast<uintptr_t>(io->hidden_out),
+              reinterpret_cast<uintptr_t>(io->t_out),
               static_cast<uintptr_t>(io->batch), static_cast<uintptr_t>(io->frames),
               static_cast<uintptr_t>(io->height), static_cast<uintptr_t>(io->width),
               static_cast<uintptr_t>(io->context_tokens), static_cast<uintptr_t>(io->first_frame_causal)};

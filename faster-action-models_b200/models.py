@@ -23,7 +23,7 @@ from typing import List, Optional, Sequence
 import torch
 import torch.nn as nn
 
-from . import _abi
+from . import _abi, ops
 from ._lib import check, lib
 
 
@@ -441,6 +441,7 @@ class VideoPrefillEngine:
         self.dev = p.device
         self.dit = dit
         self.keep: List[torch.Tensor] = []
+        self._head = None
         bfw = lambda t: t.detach().to(device=self.dev, dtype=torch.bfloat16).contiguous()
 
         def ptr(t):
@@ -507,9 +508,10 @@ class VideoPrefillEngine:
         return self._rope[key]
 
     def prefill(self, latents, timestep, context, context_mask=None, return_hidden=False,
-                cache_k=None, cache_v=None, hidden=None, use_graph=True):
+                cache_k=None, cache_v=None, hidden=None, use_graph=True, t_out=None):
         """WanVideoDiT.prepare + MoT.prefill_video_cache_tensor: returns the per-block K and V
-        lists ([B, S, H*d] bf16) and, with return_hidden, the final token states (fp32)."""
+        lists ([B, S, H*d] bf16) and, with return_hidden, the final token states (fp32).
+        t_out (bf16 [B, 2, D], optional) receives the time embedding rows for post()."""
         d = self.dit
         lat = latents.to(device=self.dev, dtype=torch.bfloat16).contiguous()
         B, _, Fr, Hh, Ww = lat.shape
@@ -547,6 +549,7 @@ class VideoPrefillEngine:
         io.cache_k = C.cast(kp, C.POINTER(C.c_void_p))
         io.cache_v = C.cast(vpp, C.POINTER(C.c_void_p))
         io.hidden_out = hidden.data_ptr() if hidden is not None else None
+        io.t_out = t_out.data_ptr() if t_out is not None else None
         n = C.c_size_t()
         check(lib().fam_video_workspace_size(self.handle, B, S, Cc, C.byref(n)), "fam_video_workspace_size")
         if self.ws is None or self.ws.numel() < n.value:
@@ -557,6 +560,34 @@ class VideoPrefillEngine:
               "fam_video_prefill")
         self.last = (lat, ctx, cm, rope, kp, vpp, ts)  # keep inputs alive until the work is done
         return (cache_k, cache_v, hidden) if return_hidden else (cache_k, cache_v)
+
+    def post(self, hidden, t_rows, grid, first_frame_tokens, out=None):
+        """WanVideoDiT.post_dit (wan_video_dit.py:634-638): Head.forward with the per-token
+        time embedding, then unpatchify -> bf16 [B, out_dim, F, H, W].  hidden: fp32
+        [B, S, D] from prefill(return_hidden=True); t_rows: its t_out."""
+        d = self.dit
+        B, S, D = hidden.shape
+        f, h, w = grid
+        pt, ph, pw = d.patch_size
+        hw = d.head
+        if self._head is None:
+            self._head = (hw.head.weight.detach().to(self.dev, torch.bfloat16).contiguous(),
+                          hw.head.bias.detach().to(self.dev, torch.bfloat16).contiguous(),
+                          hw.modulation.detach().reshape(2, D).to(self.dev, torch.bfloat16).contiguous())
+        wgt, bias, mod = self._head
+        st = C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+        normed = torch.empty(B * S, D, dtype=torch.bfloat16, device=self.dev)
+        check(lib().fam_video_head_norm(C.c_void_p(hidden.data_ptr()), C.c_void_p(t_rows.data_ptr()),
+                                        C.c_void_p(mod.data_ptr()), B, S, first_frame_tokens, D, float(d.eps),
+                                        C.c_void_p(normed.data_ptr()), st), "fam_video_head_norm")
+        proj = ops.gemm(normed, wgt, bias=bias)
+        Cout = wgt.shape[0] // (pt * ph * pw)
+        if out is None:
+            out = torch.empty(B, Cout, f * pt, h * ph, w * pw, dtype=torch.bfloat16, device=self.dev)
+        check(lib().fam_video_unpatchify(C.c_void_p(proj.data_ptr()), B, f, h, w, pt, ph, pw, Cout,
+                                         C.c_void_p(out.data_ptr()), st), "fam_video_unpatchify")
+        self.last_post = (normed, proj)
+        return out
 
 
 # ---------------------------------------------------- compact expert engine

@@ -9,6 +9,13 @@ action expert over the cache, and the optional Action-VAE decode, returning
 the chunk as fp32 on the CPU.  The observation VAE encode that produces the
 first-frame latents, and prompt encoding, are outside this path.
 
+FastWAMJointPolicy.infer_joint follows FastWAM.infer_joint (fastwam.py:866-1078):
+video and action latents denoised together.  Under the MoT mask the video rows
+attend only to video keys, so each model evaluation (_joint_denoise_core,
+fastwam.py:492-554) is the video expert's own forward over the current noisy
+video latents -- whose per-block K/V is that step's cache -- plus its output
+head, and the action expert over that cache.
+
 CAEPipeline is BASELINE config 4: the video backbone forward once per chunk,
 the compact action expert cross-attending the backbone's final token states,
 and the Action-VAE decoder, over a batch of independent rollouts processed in
@@ -83,6 +90,69 @@ class FastWAMActionPolicy:
             out["action"] = lat[0].float().cpu()
         if return_action_latents:
             out["action_latents"] = lat[0].float().cpu()
+        return out
+
+
+class FastWAMJointPolicy(FastWAMActionPolicy):
+    """FastWAM.infer_joint from the first-frame latents on (video decode excluded)."""
+
+    def __init__(self, video_expert: WanVideoDiT, action_expert: ActionDiT,
+                 action_vae: Optional[ActionAE] = None, action_infer_shift: float = 5.0,
+                 video_infer_shift: float = 5.0, torch_dtype=torch.bfloat16):
+        super().__init__(video_expert, action_expert, action_vae, action_infer_shift, torch_dtype)
+        self.video_shift = float(video_infer_shift)
+
+    @torch.no_grad()
+    def joint_step(self, latents_video: torch.Tensor, latents_action: torch.Tensor, timestep_video,
+                   timestep_action, context: torch.Tensor, context_mask: torch.Tensor):
+        """FastWAM._joint_denoise_core -> (video prediction bf16 [B, C, F, H, W],
+        action prediction bf16 [B, Sa, A])."""
+        vid, act = self.video_expert, self.action_expert
+        eng = vid.engine()
+        B, _, Fr, Hh, Ww = latents_video.shape
+        pt, ph, pw = vid.patch_size
+        grid = (Fr // pt, Hh // ph, Ww // pw)
+        tpf = grid[1] * grid[2]
+        t_rows = torch.empty(B, 2, vid.hidden_dim, dtype=torch.bfloat16, device=self.device)
+        k, v, hidden = eng.prefill(latents_video, timestep_video, context, context_mask, return_hidden=True,
+                                   use_graph=False, t_out=t_rows)
+        pred_video = eng.post(hidden, t_rows, grid, tpf)
+        mask = mot_action_mask(k[0].shape[1], latents_action.shape[1], tpf, device=self.device)
+        pred_action = act.engine().denoise_step(latents_action, timestep_action, context, context_mask, k, v, mask)
+        return pred_video, pred_action
+
+    @torch.no_grad()
+    def infer_joint(self, first_frame_latents: torch.Tensor, num_latent_frames: int, context: torch.Tensor,
+                    context_mask: torch.Tensor, action_horizon: int, num_inference_steps: int = 20,
+                    sigma_shift: Optional[float] = None, seed: Optional[int] = None) -> dict:
+        """Seeded CPU noise for both latents (fastwam.py:945-965), the first latent frame
+        pinned to the observation after every step (:1063), both Euler updates in bf16
+        (scheduler_continuous.py:82-88).  Returns {"video_latents", "action"}."""
+        act = self.action_expert
+        B, zc, _, lh, lw = first_frame_latents.shape
+        gv = None if seed is None else torch.Generator(device="cpu").manual_seed(seed)
+        ga = None if seed is None else torch.Generator(device="cpu").manual_seed(seed)
+        lat_v = torch.randn((1, zc, num_latent_frames, lh, lw), generator=gv, dtype=torch.float32).to(
+            device=self.device, dtype=self.torch_dtype)
+        latent_horizon = self.action_vae.cfg.num_tokens if self.action_vae is not None else action_horizon
+        lat_a = torch.randn((1, latent_horizon, act.action_dim), generator=ga, dtype=torch.float32).to(
+            device=self.device, dtype=self.torch_dtype)
+        first = first_frame_latents.to(device=self.device, dtype=self.torch_dtype)
+        lat_v[:, :, 0:1] = first
+        ts_v, ds_v = build_inference_schedule(num_inference_steps, self.video_shift if sigma_shift is None
+                                              else float(sigma_shift), dtype=self.torch_dtype)
+        ts_a, ds_a = build_inference_schedule(num_inference_steps, self.shift if sigma_shift is None
+                                              else float(sigma_shift), dtype=self.torch_dtype)
+        for tv, dv, ta, da in zip(ts_v, ds_v, ts_a, ds_a):
+            pv, pa = self.joint_step(lat_v, lat_a, torch.tensor([tv]), torch.tensor([ta]), context, context_mask)
+            lat_v = lat_v + pv * torch.tensor(dv, dtype=self.torch_dtype, device=self.device)
+            lat_a = lat_a + pa * torch.tensor(da, dtype=self.torch_dtype, device=self.device)
+            lat_v[:, :, 0:1] = first
+        out = {"video_latents": lat_v}
+        if self.action_vae is not None:
+            out["action"] = self.action_vae.decode(lat_a.float())[0].to(dtype=self.torch_dtype).float().cpu()
+        else:
+            out["action"] = lat_a[0].float().cpu()
         return out
 
 

@@ -366,6 +366,8 @@ typedef struct fam_video_io {
   float* hidden_out;          /* f32 [B, S, D] or NULL */
   void* workspace;
   size_t workspace_bytes;
+  void* t_out;                /* bf16 [B, 2, D] time embedding t (first-frame t = 0 row, then the
+                               * other frames' row) for the output head, or NULL */
 } fam_video_io;
 
 FAM_API int fam_video_expert_create(const fam_video_config* cfg, const fam_video_weights* w,
@@ -460,6 +462,19 @@ FAM_API int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_
 FAM_API int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_weights* w,
                               int32_t batch, const float* z, const int32_t* suite_ids, float* out,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Video output head (WanVideoDiT.post_dit -> Head.forward + unpatchify,
+ * wan_video_dit.py:290-306, 426-431, 634-638), the video half of a joint
+ * denoising step.  fam_video_head_norm: out bf16 [B*S, D] =
+ * LayerNorm(hidden) * (1 + scale) + shift with (shift, scale) = bf16(modulation
+ * [2, D] + t) of the token's row of t_rows bf16 [B, 2, D] (row 0 for the first
+ * first_frame_tokens tokens of a sample); then fam_gemm with head.head gives
+ * [B*S, pt*ph*pw*C]; fam_video_unpatchify rearranges it to bf16 [B, C, F*pt, H*ph, W*pw]. */
+FAM_API int fam_video_head_norm(const float* hidden, const void* t_rows, const void* modulation, int32_t batch,
+                                int32_t tokens, int32_t first_frame_tokens, int32_t dim, float eps, void* out,
+                                void* stream);
+FAM_API int fam_video_unpatchify(const void* x, int32_t batch, int32_t f, int32_t h, int32_t w, int32_t pt,
+                                 int32_t ph, int32_t pw, int32_t channels, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Wan2.2 VAE encode of one observation frame: the pieces around the GEMMs of

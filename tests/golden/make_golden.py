@@ -24,6 +24,8 @@ Reference code paths exercised:
       plus the final hidden state through DiTBlock.forward (wan_video_dit.py:248-267)
   sched / masks / rope / sinusoid: scheduler_continuous.py:63-88, fastwam.py:429-451,
         wan_video_dit.py:30-60, 489-523
+  joint FastWAM._joint_denoise_core: both experts, MoT joint attention   (bf16)
+        FastWAM/src/fastwam/models/wan22/fastwam.py:492-554, mot.py:580-708
   vae VideoVAE38_.encode of one observation frame (fp32 and bf16)
         FastWAM/src/fastwam/models/wan22/wan_video_vae.py:1285-1304, 619-733
 """
@@ -222,6 +224,47 @@ def make_primitives(R):
     return out
 
 
+def make_joint(R):
+    """One joint video + action model evaluation (infer_joint's step), bf16."""
+    torch.manual_seed(5)
+    # head_dim 128: the 3-D RoPE splits it into (44, 42, 42) as at full size
+    vcfg = dict(hidden_dim=128, in_dim=16, ffn_dim=256, out_dim=16, text_dim=96, freq_dim=256,
+                eps=1e-6, patch_size=(1, 2, 2), num_heads=2, attn_head_dim=128, num_layers=2,
+                has_image_input=False, seperated_timestep=True,
+                video_attention_mask_mode="first_frame_causal")
+    acfg = dict(hidden_dim=64, action_dim=7, ffn_dim=128, text_dim=96, freq_dim=256, eps=1e-6,
+                num_heads=2, attn_head_dim=128, num_layers=2)
+    video = R.WanVideoDiT(**vcfg).to(torch.bfloat16).eval()
+    action = R.ActionDiT(**acfg).to(torch.bfloat16).eval()
+    mot = R.MoT({"video": video, "action": action}).eval()
+    g = torch.Generator().manual_seed(5)
+    latents_video = torch.randn(1, 16, 3, 4, 6, generator=g).bfloat16()
+    latents_action = torch.randn(1, 8, 7, generator=g).bfloat16()
+    C = 12
+    ctx = torch.randn(1, C, 96, generator=g).bfloat16()
+    ctx_mask = torch.ones(1, C, dtype=torch.bool)
+    ctx_mask[0, -3:] = False
+    tv = torch.tensor([700.0]).bfloat16()
+    ta = torch.tensor([700.0]).bfloat16()
+    host = SimpleNamespace(video_expert=SimpleNamespace(
+        build_video_to_video_mask=lambda video_seq_len, video_tokens_per_frame, device:
+        R.WanVideoDiT.build_video_to_video_mask(
+            SimpleNamespace(video_attention_mask_mode="first_frame_causal"), video_seq_len,
+            video_tokens_per_frame, device)))
+    tpf, Sv, Sa = 6, 18, 8
+    mask = R.FastWAM._build_mot_attention_mask(host, Sv, Sa, tpf, torch.device("cpu"))
+    core_host = SimpleNamespace(video_expert=video, action_expert=action, mot=mot)
+    with torch.no_grad():
+        pv, pa = R.FastWAM._joint_denoise_core(
+            core_host, latents_video=latents_video, latents_action=latents_action, timestep_video=tv,
+            timestep_action=ta, context=ctx, context_mask=ctx_mask, attention_mask=mask,
+            fuse_vae_embedding_in_latents=True)
+    return {"kind": "joint", "video_cfg": vcfg, "action_cfg": acfg, "video": _sd(video, torch.bfloat16),
+            "action": _sd(action, torch.bfloat16), "latents_video": latents_video,
+            "latents_action": latents_action, "timestep_video": tv, "timestep_action": ta,
+            "context": ctx, "context_mask": ctx_mask, "mask": mask, "pred_video": pv, "pred_action": pa}
+
+
 def make_vae(R):
     """Wan2.2 VAE (VideoVAE38_) encode of a first frame at a small width.
 
@@ -263,7 +306,7 @@ def main():
     torch.set_num_threads(4)
     for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
                      ("c2_video_prefill", make_c2), ("primitives", make_primitives),
-                     ("vae_encode", make_vae)):
+                     ("vae_encode", make_vae), ("joint_step", make_joint)):
         if args.only is not None and name not in args.only:
             continue
         fx = fn(R)

@@ -122,3 +122,22 @@ def test_vae_encode_matches_reference():
     p32 = {k: v.float() for k, v in fx["params"].items()}
     mu32 = O.vae_encode_first_frame(p32, cfg, fx["image"].float(), fx["mean"], fx["inv_std"])
     assert (mu32 - fx["mu_f32"]).abs().max().item() < 1e-5
+
+
+def test_joint_step_matches_reference():
+    """FastWAM._joint_denoise_core (both experts under the MoT mask): bit-exact at bf16."""
+    fx = _load("joint_step")
+    vc, ac = fx["video_cfg"], fx["action_cfg"]
+    vcfg = O.DiTConfig(hidden_dim=vc["hidden_dim"], ffn_dim=vc["ffn_dim"], num_heads=vc["num_heads"],
+                       attn_head_dim=vc["attn_head_dim"], num_layers=vc["num_layers"], text_dim=vc["text_dim"],
+                       freq_dim=vc["freq_dim"], eps=vc["eps"], in_dim=vc["in_dim"], out_dim=vc["out_dim"],
+                       patch_size=tuple(vc["patch_size"]))
+    acfg = O.DiTConfig(hidden_dim=ac["hidden_dim"], ffn_dim=ac["ffn_dim"], num_heads=ac["num_heads"],
+                       attn_head_dim=ac["attn_head_dim"], num_layers=ac["num_layers"], text_dim=ac["text_dim"],
+                       freq_dim=ac["freq_dim"], eps=ac["eps"], action_dim=ac["action_dim"])
+    pv, pa = O.joint_denoise_core(fx["video"], vcfg, fx["action"], acfg, fx["latents_video"],
+                                  fx["latents_action"], fx["timestep_video"], fx["timestep_action"],
+                                  fx["context"], fx["context_mask"])
+    _same(pv, fx["pred_video"])
+    _same(pa, fx["pred_action"])
+    assert torch.equal(O.build_mot_attention_mask(pv.shape[2] * 6, pa.shape[1], 6), fx["mask"])
