@@ -1,6 +1,6 @@
 """Fixed single-GPU workloads of the library's kernels, for profilers.
 
-    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,attn_c2,cae_c0,prefill_c2,dit4dit_c3} [repeats]
+    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,attn_c2,cae_c0,prefill_c2,dit4dit_c3,joint_c2,vae_c1} [repeats]
 
 Each case runs its library call `repeats` times (default 3) on cuda:0 and
 synchronizes; under ncu, skip the warm-up launches with `-s`.
@@ -11,6 +11,9 @@ synchronizes; under ncu, skip the warm-up launches with `-s`.
   dit4dit_c3   DiT4DiTPipeline of BASELINE config 3 (backbone to block 18 of 28 at 3,520
                tokens + 16-block action head, 4 Euler steps, batch 1); prints the
                p50 chunk latency over the repeats
+  joint_c2     FastWAMJointPolicy.joint_step at config-2 scale: the 30-layer backbone over
+               1,760 noisy video tokens + its output head, and a 30-layer action expert
+               (hidden 1024, 24 x 128 heads) over that step's K/V; prints the p50 latency
   vae_c1       WanVideoVAE38 encode of one 512 x 704 observation frame (dim 160, z 48,
                the configs-1/2 latent grid 32 x 44); prints the p50 latency
 """
@@ -88,6 +91,30 @@ def main(case: str, reps: int) -> None:
             times.append(s0.elapsed_time(e0))
         times = sorted(times[2:])
         print("dit4dit_c3 chunk ms p50", round(times[len(times) // 2], 3))
+    elif case == "joint_c2":
+        with torch.device(dev):
+            vid = M.WanVideoDiT(hidden_dim=3072, in_dim=48, ffn_dim=14336, out_dim=48, text_dim=4096, freq_dim=256,
+                                eps=1e-6, patch_size=(1, 2, 2), num_heads=24, attn_head_dim=128, num_layers=30,
+                                has_image_input=False, seperated_timestep=True,
+                                video_attention_mask_mode="first_frame_causal")
+            act = M.ActionDiT(1024, 7, 4096, 4096, 256, 1e-6, 24, 128, 30)
+        vid, act = vid.to(torch.bfloat16), act.to(torch.bfloat16)
+        pol = P.FastWAMJointPolicy(vid, act)
+        g = torch.Generator().manual_seed(0)
+        lat_v = torch.randn(1, 48, 5, 32, 44, generator=g).bfloat16().to(dev)
+        lat_a = torch.randn(1, 32, 7, generator=g).bfloat16().to(dev)
+        ctx = torch.randn(1, 64, 4096, generator=g).bfloat16().to(dev)
+        cm = torch.ones(1, 64, dtype=torch.bool, device=dev)
+        times = []
+        for _ in range(reps + 2):
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            pol.joint_step(lat_v, lat_a, torch.tensor([700.0]), torch.tensor([700.0]), ctx, cm)
+            e0.record()
+            torch.cuda.synchronize()
+            times.append(s0.elapsed_time(e0))
+        times = sorted(times[2:])
+        print("joint_c2 step ms p50", round(times[len(times) // 2], 3))
     elif case == "vae_c1":
         g = torch.Generator().manual_seed(0)
         sd = {}
