@@ -586,7 +586,18 @@ int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float
   a.hd = g.head_dim;
   a.F = g.ffn_dim;
   a.A = g.action_dim;
-  a.splits = (io.video_tokens + io.action_tokens + kFusedKeysPerSplit - 1) / kFusedKeysPerSplit;
+  {
+    // joint-attention splits: as many per head as one wave of CTAs holds
+    // (at most kFusedMaxSplits), each a whole number of 32-key steps and at
+    // most kFusedKeysPerSplit keys -- a short key list (a visible prefix of
+    // the cache) then spreads over more, smaller splits
+    const int skv = io.video_tokens + io.action_tokens;
+    const int cap = std::min(kFusedMaxSplits, std::max(1, e->num_sms / g.num_heads));
+    int kps = ((skv + cap - 1) / cap + 31) / 32 * 32;
+    kps = std::min(kFusedKeysPerSplit, std::max(32, kps));
+    a.kps = kps;
+    a.splits = (skv + kps - 1) / kps;
+  }
   a.eps = g.eps;
   a.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(g.head_dim));
   // measurement hook: plain (not captured) calls only

@@ -1182,8 +1182,8 @@ __device__ AttnItem joint_item(const FusedArgs& a, int step, int l, int i) {
   t.mask2d = a.mask2d;
   t.mrs = a.Sv + a.Sa;
   t.key_mask = nullptr;
-  t.k0 = sp * kFusedKeysPerSplit;
-  t.k1end = min(a.Sv + a.Sa, t.k0 + kFusedKeysPerSplit);
+  t.k0 = sp * a.kps;
+  t.k1end = min(a.Sv + a.Sa, t.k0 + a.kps);
   t.out = a.ao + h * a.hd;
   t.ots = a.HD;
   t.part_head = a.apart + static_cast<long long>(h) * a.splits * kSplitStride;

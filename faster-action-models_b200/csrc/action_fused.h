@@ -50,6 +50,7 @@ struct FusedArgs {
   __nv_bfloat16* trace;              // [N, R, A] or null
   StepTimes deltas;
   int N, L, R, Sa, D, HD, H, hd, F, A, splits;
+  int kps;                           // joint-attention keys per split (<= kFusedKeysPerSplit, a multiple of 32)
   float eps, scale_log2;
 };
 

@@ -37,6 +37,15 @@ from torch import nn
 from .models import ActionAE, ActionDiT, WanVideoDiT, build_inference_schedule
 
 
+def visible_video_prefix(cache_k, cache_v, tokens_per_frame: int):
+    """The cache rows the action tokens can see under the MoT mask: the first video
+    frame only (fastwam.py:429-451).  The keys after it are masked for every action row,
+    so the action expert attends over this prefix (strided views, no copy) with an
+    all-attend mask and gets the same result without streaming the masked keys."""
+    vis = min(tokens_per_frame, cache_k[0].shape[1])
+    return [t[:, :vis] for t in cache_k], [t[:, :vis] for t in cache_v], vis
+
+
 def mot_action_mask(video_seq_len: int, action_seq_len: int, tokens_per_frame: int,
                     device=None) -> torch.Tensor:
     """Action rows [Sa, Sv + Sa] of FastWAM._build_mot_attention_mask (fastwam.py:429-451):
@@ -77,7 +86,7 @@ class FastWAMActionPolicy:
                            context_mask)
         pt, ph, pw = vid.patch_size
         tpf = (first_frame_latents.shape[3] // ph) * (first_frame_latents.shape[4] // pw)
-        Sv = k[0].shape[1]
+        k, v, Sv = visible_video_prefix(k, v, tpf)
         mask = mot_action_mask(Sv, latent_horizon, tpf, device=self.device)
         ts, ds = build_inference_schedule(num_inference_steps,
                                           self.shift if sigma_shift is None else float(sigma_shift),
@@ -117,8 +126,9 @@ class FastWAMJointPolicy(FastWAMActionPolicy):
         k, v, hidden = eng.prefill(latents_video, timestep_video, context, context_mask, return_hidden=True,
                                    use_graph=False, t_out=t_rows)
         pred_video = eng.post(hidden, t_rows, grid, tpf)
-        mask = mot_action_mask(k[0].shape[1], latents_action.shape[1], tpf, device=self.device)
-        pred_action = act.engine().denoise_step(latents_action, timestep_action, context, context_mask, k, v, mask)
+        kv, vv, Sv = visible_video_prefix(k, v, tpf)
+        mask = mot_action_mask(Sv, latents_action.shape[1], tpf, device=self.device)
+        pred_action = act.engine().denoise_step(latents_action, timestep_action, context, context_mask, kv, vv, mask)
         return pred_video, pred_action
 
     @torch.no_grad()
