@@ -42,7 +42,7 @@ class GemmDesc(C.Structure):
         ("tokens_per_batch", C.c_int32), ("first_frame_tokens", C.c_int32),
         ("gate_batch_stride", C.c_int64), ("gate_group_stride", C.c_int64),
         ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("split_round", C.c_int32),
-        ("conv_wp", C.c_int32), ("conv_cin", C.c_int32), ("conv_a_rows", C.c_int64),
+        ("conv_wp", C.c_int32), ("conv_cin", C.c_int32), ("conv_a_rows", C.c_int64), ("pair", C.c_int32),
     ]
 
 

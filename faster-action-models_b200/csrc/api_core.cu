@@ -175,7 +175,7 @@ int fam_gemm(const fam_gemm_desc* d, void* stream) {
   } else {
     rc = gemm_plan(&p, d->a, d->lda, d->b, d->ldb, d->m, d->n, d->k, d->splits, d->tile_n, e,
                    d->a_is_const != 0, d->b_is_const != 0, device_status_word(), skp, skf, skb,
-                   d->split_round != 0);
+                   d->split_round != 0, d->pair != 0);
   }
   if (rc) return rc;
   return check_cuda(gemm_launch(p, static_cast<cudaStream_t>(stream), d->pdl != 0), "fam_gemm launch");

@@ -84,6 +84,7 @@ struct GemmPlan {
   int bn;
   int splits;
   int persist;              // persistent tile loop over min(tiles, SMs) CTAs
+  int pair;                 // > 0: CTA-pair kernel (256 x 256 tiles) over this many pairs
 };
 
 // tcgen05 flash attention for long self attention (head_dim 128, one key source,
@@ -114,7 +115,7 @@ int gemm_pick_bn(int n);
 int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M, int N,
               int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const, bool b_is_const,
               int* status, float* sk_part = nullptr, unsigned* sk_flag = nullptr, size_t sk_bytes = 0,
-              bool sk_force = false);
+              bool sk_force = false, bool allow_pair = false);
 // Implicit-GEMM 3x3 stride-1 convolution: A is a zero-bordered channels-last
 // buffer [a_rows, cin] (row stride lda) whose rows are the padded positions of
 // a frame of width wp - 2; M = H * wp output rows (epi.conv_wp = wp maps them

@@ -753,6 +753,174 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   }
 }
 
+// ------------------------------------------------------- CTA-pair variant
+// Many-tile problems with 256-wide N tiles: a cluster of two CTAs computes
+// 256 x 256 output tiles with tcgen05.mma.cta_group::2.  Each CTA loads its
+// own 128 rows of A and its half (128 rows) of the B tile, so a CTA streams
+// 32 KB per 64-deep k-block for 128 x 256 outputs instead of 48 KB.  The even
+// CTA (rank 0) issues the MMAs; its `full` barriers count both CTAs' TMA bytes,
+// its commits arrive on both CTAs' `empty` and `tfull` barriers, and both CTAs'
+// epilogue warps arrive on its `tempty`.  Each CTA drains its 128 TMEM lanes
+// with the persistent kernel's epilogue.  Every wait is bounded.
+constexpr int kPairBN = 256;
+__host__ __device__ constexpr int gemm_pair_stage_bytes() { return kBM * kBK * 2 + (kPairBN / 2) * kBK * 2; }
+constexpr int kPairStages = 6;
+__host__ __device__ constexpr int gemm_pair_smem_bytes() {
+  return kPairStages * gemm_pair_stage_bytes() + 1024 + 256;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const GemmArgs args) {
+  constexpr int BN = kPairBN;
+  constexpr int STAGES = kPairStages;
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int STAGE_BYTES = gemm_pair_stage_bytes();
+  constexpr uint32_t ACC_COLS = 256;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_m = (args.M + 2 * kBM - 1) / (2 * kBM);
+  const int ntiles = tiles_m * ((args.N + BN - 1) / BN);
+  const int nkb = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kPersistEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_barrier();  // both CTAs' barriers initialised before any remote arrival or TMA
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0 && nkb > 0) {
+      const uint64_t polA = policy_evict_last();
+      const uint64_t polB = policy_evict_first();
+      pdl_wait();
+      int it = 0;
+      for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
+        const int m0 = (tile % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (tile / tiles_m) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES &&
+              !mbar_wait(&empty[s], static_cast<uint32_t>(it / STAGES - 1) & 1, args.status, kErrWaitEmpty)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          const uint32_t bar0 = cluster_map(&full[s], 0);  // the even CTA's barrier
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, bar0, kb * kBK, m0, polA);
+          tma_load_2d_pair(sa + A_BYTES, &tmB, bar0, kb * kBK, n0, polB);
+        }
+      }
+      // the even CTA's full barriers count every copy of both CTAs: wait for
+      // the last ones before the pair can exit
+      if (rank == 0)
+        for (int j = max(0, it - STAGES); j < it; ++j)
+          mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1, args.status, kErrWaitFull);
+    } else if (lane == 0) {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
+      int it = 0, lt = 0;
+      for (int tile = pair; tile < ntiles && nkb > 0; tile += npairs, ++lt) {
+        const int buf = lt & 1;
+        if (*abort_flag) break;
+        if (lt >= 2 && !mbar_wait_cl_bounded(&tempty[buf], static_cast<uint32_t>((lt >> 1) - 1) & 1, args.status,
+                                             kErrWaitAccum)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dacc = tmem_base + buf * ACC_COLS;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (*abort_flag || !mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, args.status, kErrWaitFull)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem + s * STAGE_BYTES);
+          const uint64_t db = umma_desc_sw128(smem + s * STAGE_BYTES + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_bf16_ss_pair(dacc, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair_both(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair_both(&tfull[buf]);
+      }
+    }
+  } else {
+    const int sp = warp & 3;
+    const int wq = (warp - 2) >> 2;
+    const int c0 = 16 * wq, cs = 16 * kEpiPerQuarter;
+    const uint32_t tempty0 = cluster_map(&tempty[0], 0), tempty1 = cluster_map(&tempty[1], 0);
+    pdl_wait();
+    int lt = 0;
+    for (int tile = pair; tile < ntiles && nkb > 0; tile += npairs, ++lt) {
+      const int buf = lt & 1;
+      const bool ok = mbar_wait_cl_bounded(&tfull[buf], static_cast<uint32_t>(lt >> 1) & 1, args.status,
+                                           kErrWaitAccum);
+      tc_fence_after();
+      if (!ok) *abort_flag = 1;
+      if (*abort_flag) break;
+      const int m0 = (tile % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int n0 = (tile / tiles_m) * BN;
+      const uint32_t tacc = tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16);
+      const int r = sp * 32 + lane;
+      gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, c0, cs, nullptr, 0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(buf ? tempty1 : tempty0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_barrier();  // the pair is done with each other's barriers and TMEM
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 template <int BN>
 static cudaError_t launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
@@ -856,10 +1024,31 @@ int gemm_plan_conv3(GemmPlan* p, const void* A, long long lda, long long a_rows,
   p->args.taps = 9;
   p->args.tap_wp = wp;
   p->args.tap_kpt = kpt;
+  p->pair = 0;
   return 0;
 }
 
 cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
+  if (p.pair > 0) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemm_pair_smem_bytes());
+      if (e != cudaSuccess) return e;
+      attr_set = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * p.pair);
+    cfg.blockDim = dim3(kPersistThreads);
+    cfg.dynamicSmemBytes = gemm_pair_smem_bytes();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_bf16_tc_pair_kernel, p.ta, p.tb, p.args);
+  }
   if (p.persist > 0) {
     switch (p.bn) {
       case 64: return launch_gemm_persist_bn<64>(p.ta, p.tb, p.args, p.persist, stream, pdl);
@@ -887,7 +1076,7 @@ cudaError_t gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
 int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long long ldb, int M,
               int N, int K, int splits, int bn, const GemmEpilogue& epi, bool a_is_const,
               bool b_is_const, int* status, float* sk_part, unsigned* sk_flag, size_t sk_bytes,
-              bool sk_force) {
+              bool sk_force, bool allow_pair) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error("gemm: empty problem");
   if ((K % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0)
     return set_error("gemm: K and row strides must be multiples of 8 elements (16 bytes)");
@@ -967,6 +1156,17 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
   p->args.taps = 1;
   p->args.tap_wp = 0;
   p->args.tap_kpt = 0;
+  // CTA pairs (256 x 256 tiles, half of B per CTA) for many-tile problems that
+  // would run 256-wide tiles anyway
+  p->pair = 0;
+  if (allow_pair && splits == 1 && bn == 256 && !sk && !epi.features_on_a && M > kBM) {
+    const int pt = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
+    // each CTA of a pair loads a 128-row half of the B tile
+    if (!make_tmap_bf16_2d(&p->tb, B, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                           static_cast<uint64_t>(ldb), static_cast<uint32_t>(kPairBN / 2)))
+      return set_error("gemm: cuTensorMapEncodeTiled failed for the pair B half tile");
+    p->pair = std::min(pt, gemm_num_sms() / 2);
+  }
   if (sk && p->persist > 0) {
     p->args.sk_full = sk_full;
     p->args.sk_pieces = sk_pieces;

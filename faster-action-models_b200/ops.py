@@ -35,7 +35,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
          residual: Optional[torch.Tensor] = None, gate_w: Optional[torch.Tensor] = None,
          gate_t: Optional[torch.Tensor] = None, tokens_per_batch: int = 0,
          first_frame_tokens: int = 0, gate_batch_stride: int = 0, gate_group_stride: int = 0,
-         pdl: bool = False, split_round: str = "off") -> torch.Tensor:
+         pdl: bool = False, split_round: str = "off", pair: bool = False) -> torch.Tensor:
     """Linear layer on the tensor cores.
 
     weights_as_a=False:  a = activations [T, K], b = weight [F, K] -> [T, F]
@@ -64,6 +64,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None
     d.a_is_const = 1 if weights_as_a else 0
     d.b_is_const = 0 if weights_as_a else 1
     d.pdl = 1 if pdl else 0
+    d.pair = 1 if pair else 0
     d.bias = _ptr(bias)
     if residual is not None:
         _require(residual, torch.float32, "residual")

@@ -125,6 +125,9 @@ typedef struct fam_gemm_desc {
   int32_t conv_wp;
   int32_t conv_cin;
   int64_t conv_a_rows;
+  /* 1: a many-tile problem that would run 256-wide tiles may run them on CTA
+   * pairs (tcgen05 cta_group::2, 256 x 256 tiles, half of B per CTA); 0: off. */
+  int32_t pair;
 } fam_gemm_desc;
 
 FAM_API int fam_gemm(const fam_gemm_desc* desc, void* stream);

@@ -139,3 +139,28 @@ def test_split_round(fam_ops, F, K):
     _close(outs[0][1], _ref(x, w, b, "gelu_tanh"))
     _close(y_auto, _ref(x, w, b, "gelu_tanh"))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("M,K,N", [(1760, 512, 3072), (600, 1344, 1024), (1024, 3072, 9216)])
+def test_cta_pair(fam_ops, M, K, N):
+    """CTA-pair kernel (tcgen05 cta_group::2, 256 x 256 tiles, half of B per CTA):
+    store, GELU-store and gated-residual epilogues, ragged M, deterministic."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda", generator=g).bfloat16()
+    gt = torch.randn(1, N, device="cuda", generator=g)
+    r0 = torch.randn(M, N, device="cuda", generator=g)
+    outs = []
+    for _ in range(2):
+        y = fam_ops.gemm(x, w, bias=b, pair=True, tile_n=256)
+        yg = fam_ops.gemm(x, w, bias=b, act="gelu_tanh", pair=True, tile_n=256)
+        r = r0.clone()
+        fam_ops.gemm(x, w, bias=b, residual=r, gate_t=gt, tokens_per_batch=M, pair=True, tile_n=256)
+        torch.cuda.synchronize()
+        outs.append((y, yg, r))
+    _close(outs[0][0], _ref(x, w, b))
+    _close(outs[0][1], _ref(x, w, b, "gelu_tanh"))
+    _close(outs[0][2], r0 + gt[0][None, :] * _ref(x, w, b))
+    for a, c in zip(outs[0], outs[1]):
+        assert torch.equal(a, c)
