@@ -823,14 +823,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
 
   if (warp == 0) {
     if (lane == 0 && nkb > 0) {
-      const uint64_t polA = policy_evict_last();
-      const uint64_t polB = policy_evict_first();
-      pdl_wait();
+      const uint64_t polA = args.a_is_const ? policy_evict_first() : policy_evict_last();
+      const uint64_t polB = args.b_is_const ? policy_evict_first() : policy_evict_last();
+      // first tile: the operand that is constant for the launch chain (the
+      // weights) for the first stages before the wait on the previous launch
+      int pre = 0;
+      if (pair < ntiles) {
+        const int m0 = (pair % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (pair / tiles_m) * BN + static_cast<int>(rank) * (BN / 2);
+        pre = min(nkb, STAGES);
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* sa = smem + i * STAGE_BYTES;
+          const uint32_t bar0 = cluster_map(&full[i], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * STAGE_BYTES);
+          if (args.a_is_const) tma_load_2d_pair(sa, &tmA, bar0, i * kBK, m0, polA);
+          if (args.b_is_const) tma_load_2d_pair(sa + A_BYTES, &tmB, bar0, i * kBK, n0, polB);
+        }
+        pdl_wait();
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* sa = smem + i * STAGE_BYTES;
+          const uint32_t bar0 = cluster_map(&full[i], 0);
+          if (!args.a_is_const) tma_load_2d_pair(sa, &tmA, bar0, i * kBK, m0, polA);
+          if (!args.b_is_const) tma_load_2d_pair(sa + A_BYTES, &tmB, bar0, i * kBK, n0, polB);
+        }
+      } else {
+        pdl_wait();
+      }
       int it = 0;
       for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
         const int m0 = (tile % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
         const int n0 = (tile / tiles_m) * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
+          if (it < pre) continue;  // issued above
           const int s = it % STAGES;
           if (it >= STAGES &&
               !mbar_wait(&empty[s], static_cast<uint32_t>(it / STAGES - 1) & 1, args.status, kErrWaitEmpty)) {

@@ -151,7 +151,7 @@ int gemm_x(const VCtx& c, const void* act, long long lda, int M, const void* W, 
   }
   GemmPlan p;
   V_TRYI(gemm_plan(&p, act, lda, W, K, M, N, K, 1, 0, e, false, true, c.e->status, wp<float>(c, c.L.skp),
-                   wp<unsigned>(c, c.L.skf), gemm_sk_scratch_bytes()));
+                   wp<unsigned>(c, c.L.skf), gemm_sk_scratch_bytes(), false, /*allow_pair=*/true));
   V_LAUNCH(gemm_launch(p, c.st, c.pdl));
   return 0;
 }
