@@ -1,10 +1,11 @@
 """Fixed single-GPU workloads of the library's kernels, for profilers.
 
-    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,attn_c2,cae_c0,prefill_c2,dit4dit_c3,joint_c2,vae_c1} [repeats]
+    python faster-action-models_b200/kernel_cases.py {gemm_qkv_c2,gemm_qkv_pair_c2,attn_c2,cae_c0,prefill_c2,dit4dit_c3,joint_c2,vae_c1} [repeats]
 
 Each case runs its library call `repeats` times (default 3) on cuda:0 and
 synchronizes; under ncu, skip the warm-up launches with `-s`.
   gemm_qkv_c2  ops.gemm: [1760, 3072] x [9216, 3072]^T + bias (backbone qkv, config 2)
+  gemm_qkv_pair_c2  the same on CTA pairs (ops.gemm(pair=True, tile_n=256)), as the prefill runs it
   attn_c2      ops.attention: 1760 tokens, 24 heads x 128, first-frame-causal (352)
   cae_c0       CAEEngine.chunk + ActionAE.decode of BASELINE config 0
   prefill_c2   WanVideoDiT.prefill of BASELINE config 2 (30 blocks, 1,760 tokens, batch 1)
@@ -39,6 +40,12 @@ def main(case: str, reps: int) -> None:
         b = torch.randn(9216, device=dev).bfloat16()
         for _ in range(reps):
             ops.gemm(a, w, bias=b)
+    elif case == "gemm_qkv_pair_c2":
+        a = torch.randn(1760, 3072, device=dev).bfloat16()
+        w = (torch.randn(9216, 3072, device=dev) * 0.02).bfloat16()
+        b = torch.randn(9216, device=dev).bfloat16()
+        for _ in range(reps):
+            ops.gemm(a, w, bias=b, pair=True, tile_n=256)
     elif case == "attn_c2":
         q, k, v = (torch.randn(1, 1760, 24 * 128, device=dev).bfloat16() for _ in range(3))
         for _ in range(reps):
