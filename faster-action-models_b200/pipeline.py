@@ -16,6 +16,14 @@ fastwam.py:492-554) is the video expert's own forward over the current noisy
 video latents -- whose per-block K/V is that step's cache -- plus its output
 head, and the action expert over that cache.
 
+FastWAMJointPolicy(action_sees_full_video=True) is FastWAMJoint
+(fastwam_joint.py:29-49): the action rows attend to the whole video.
+FastWAMIDMPolicy.infer_action follows FastWAMIDM.infer_action
+(fastwam_idm.py:365-589): the video is denoised alone first (_denoise_video,
+:283-313: the video expert and its head, first frame pinned), then prefilled at
+timestep 0 into the K/V cache, and the action Euler loop runs over that cache
+with the FastWAMJoint mask.
+
 CAEPipeline is BASELINE config 4: the video backbone forward once per chunk,
 the compact action expert cross-attending the backbone's final token states,
 and the Action-VAE decoder, over a batch of independent rollouts processed in
@@ -103,13 +111,41 @@ class FastWAMActionPolicy:
 
 
 class FastWAMJointPolicy(FastWAMActionPolicy):
-    """FastWAM.infer_joint from the first-frame latents on (video decode excluded)."""
+    """FastWAM.infer_joint from the first-frame latents on (video decode excluded).
+    action_sees_full_video: the FastWAMJoint mask (action rows attend to every video
+    token) instead of FastWAM's (the first frame only)."""
 
     def __init__(self, video_expert: WanVideoDiT, action_expert: ActionDiT,
                  action_vae: Optional[ActionAE] = None, action_infer_shift: float = 5.0,
-                 video_infer_shift: float = 5.0, torch_dtype=torch.bfloat16):
+                 video_infer_shift: float = 5.0, torch_dtype=torch.bfloat16,
+                 action_sees_full_video: bool = False):
         super().__init__(video_expert, action_expert, action_vae, action_infer_shift, torch_dtype)
         self.video_shift = float(video_infer_shift)
+        self.full_video = bool(action_sees_full_video)
+
+    def _action_view(self, k, v, Sa: int, tpf: int):
+        """The cache rows and action mask of the action half of a step."""
+        if self.full_video:
+            Sv = k[0].shape[1]
+            return k, v, torch.ones(Sa, Sv + Sa, dtype=torch.uint8, device=self.device)
+        kv, vv, Sv = visible_video_prefix(k, v, tpf)
+        return kv, vv, mot_action_mask(Sv, Sa, tpf, device=self.device)
+
+    @torch.no_grad()
+    def video_step(self, latents_video: torch.Tensor, timestep_video, context: torch.Tensor,
+                   context_mask: torch.Tensor, return_cache: bool = False):
+        """The video expert alone over the current latents plus its output head
+        (FastWAMIDM._denoise_video) -> bf16 [B, C, F, H, W] (and the step's K/V)."""
+        vid = self.video_expert
+        eng = vid.engine()
+        B, _, Fr, Hh, Ww = latents_video.shape
+        pt, ph, pw = vid.patch_size
+        grid = (Fr // pt, Hh // ph, Ww // pw)
+        t_rows = torch.empty(B, 2, vid.hidden_dim, dtype=torch.bfloat16, device=self.device)
+        k, v, hidden = eng.prefill(latents_video, timestep_video, context, context_mask, return_hidden=True,
+                                   use_graph=False, t_out=t_rows)
+        pred = eng.post(hidden, t_rows, grid, grid[1] * grid[2])
+        return (pred, k, v) if return_cache else pred
 
     @torch.no_grad()
     def joint_step(self, latents_video: torch.Tensor, latents_action: torch.Tensor, timestep_video,
@@ -117,17 +153,10 @@ class FastWAMJointPolicy(FastWAMActionPolicy):
         """FastWAM._joint_denoise_core -> (video prediction bf16 [B, C, F, H, W],
         action prediction bf16 [B, Sa, A])."""
         vid, act = self.video_expert, self.action_expert
-        eng = vid.engine()
-        B, _, Fr, Hh, Ww = latents_video.shape
         pt, ph, pw = vid.patch_size
-        grid = (Fr // pt, Hh // ph, Ww // pw)
-        tpf = grid[1] * grid[2]
-        t_rows = torch.empty(B, 2, vid.hidden_dim, dtype=torch.bfloat16, device=self.device)
-        k, v, hidden = eng.prefill(latents_video, timestep_video, context, context_mask, return_hidden=True,
-                                   use_graph=False, t_out=t_rows)
-        pred_video = eng.post(hidden, t_rows, grid, tpf)
-        kv, vv, Sv = visible_video_prefix(k, v, tpf)
-        mask = mot_action_mask(Sv, latents_action.shape[1], tpf, device=self.device)
+        tpf = (latents_video.shape[3] // ph) * (latents_video.shape[4] // pw)
+        pred_video, k, v = self.video_step(latents_video, timestep_video, context, context_mask, return_cache=True)
+        kv, vv, mask = self._action_view(k, v, latents_action.shape[1], tpf)
         pred_action = act.engine().denoise_step(latents_action, timestep_action, context, context_mask, kv, vv, mask)
         return pred_video, pred_action
 
@@ -164,6 +193,68 @@ class FastWAMJointPolicy(FastWAMActionPolicy):
         else:
             out["action"] = lat_a[0].float().cpu()
         return out
+
+
+class FastWAMIDMPolicy(FastWAMJointPolicy):
+    """FastWAMIDM.infer_action from the first-frame latents on: the video denoised
+    alone, then the actions over its timestep-0 cache (the action rows see the whole
+    video, FastWAMJoint's mask)."""
+
+    def __init__(self, video_expert: WanVideoDiT, action_expert: ActionDiT,
+                 action_vae: Optional[ActionAE] = None, action_infer_shift: float = 5.0,
+                 video_infer_shift: float = 5.0, torch_dtype=torch.bfloat16):
+        super().__init__(video_expert, action_expert, action_vae, action_infer_shift, video_infer_shift,
+                         torch_dtype, action_sees_full_video=True)
+
+    @torch.no_grad()
+    def infer_action(self, first_frame_latents: torch.Tensor, num_latent_frames: int, context: torch.Tensor,
+                     context_mask: torch.Tensor, action_horizon: int, num_inference_steps: int = 20,
+                     sigma_shift: Optional[float] = None, seed: Optional[int] = None) -> dict:
+        """Returns {"video_latents", "action"} (fastwam_idm.py:365-589; the reference's
+        action latents are the action horizon itself: no Action-VAE in this model)."""
+        vid, act = self.video_expert, self.action_expert
+        B, zc, _, lh, lw = first_frame_latents.shape
+        gv = None if seed is None else torch.Generator(device="cpu").manual_seed(seed)
+        ga = None if seed is None else torch.Generator(device="cpu").manual_seed(seed)
+        lat_v = torch.randn((1, zc, num_latent_frames, lh, lw), generator=gv, dtype=torch.float32).to(
+            device=self.device, dtype=self.torch_dtype)
+        lat_a = torch.randn((1, action_horizon, act.action_dim), generator=ga, dtype=torch.float32).to(
+            device=self.device, dtype=self.torch_dtype)
+        first = first_frame_latents.to(device=self.device, dtype=self.torch_dtype)
+        lat_v[:, :, 0:1] = first
+        ts_v, ds_v = build_inference_schedule(num_inference_steps, self.video_shift if sigma_shift is None
+                                              else float(sigma_shift), dtype=self.torch_dtype)
+        for tv, dv in zip(ts_v, ds_v):
+            pv = self.video_step(lat_v, torch.tensor([tv]), context, context_mask)
+            lat_v = lat_v + pv * torch.tensor(dv, dtype=self.torch_dtype, device=self.device)
+            lat_v[:, :, 0:1] = first
+        k, v = vid.prefill(lat_v, torch.zeros(lat_v.shape[0]), context, context_mask)
+        Sv = k[0].shape[1]
+        mask = torch.ones(action_horizon, Sv + action_horizon, dtype=torch.uint8, device=self.device)
+        ts_a, ds_a = build_inference_schedule(num_inference_steps, self.shift if sigma_shift is None
+                                              else float(sigma_shift), dtype=self.torch_dtype)
+        lat_a = act.engine().chunk(lat_a, ts_a, ds_a, context, context_mask, k, v, mask)
+        return {"video_latents": lat_v, "action": lat_a[0].float().cpu()}
+
+
+class FastWAMOptionalIDMPolicy(FastWAMIDMPolicy):
+    """FastWAMOptionalIDM.infer_action (fastwam_optional_idm.py:60-120): "idm" runs the
+    IDM path, "first_frame" FastWAM's (the actions over the first frame's cache)."""
+
+    @torch.no_grad()
+    def infer_action(self, first_frame_latents: torch.Tensor, context: torch.Tensor, context_mask: torch.Tensor,
+                     action_horizon: int, num_inference_steps: int = 20, sigma_shift: Optional[float] = None,
+                     seed: Optional[int] = None, num_latent_frames: Optional[int] = None,
+                     action_infer_mode: str = "idm") -> dict:
+        if action_infer_mode == "idm":
+            if num_latent_frames is None:
+                raise ValueError("num_latent_frames is required for action_infer_mode='idm'")
+            return FastWAMIDMPolicy.infer_action(self, first_frame_latents, num_latent_frames, context, context_mask,
+                                                 action_horizon, num_inference_steps, sigma_shift, seed)
+        if action_infer_mode == "first_frame":
+            return FastWAMActionPolicy.infer_action(self, first_frame_latents, context, context_mask, action_horizon,
+                                                    num_inference_steps, sigma_shift, seed)
+        raise ValueError("action_infer_mode must be one of: idm, first_frame")
 
 
 class CAEPipeline:

@@ -26,6 +26,8 @@ Reference code paths exercised:
         wan_video_dit.py:30-60, 489-523
   joint FastWAM._joint_denoise_core: both experts, MoT joint attention   (bf16)
         FastWAM/src/fastwam/models/wan22/fastwam.py:492-554, mot.py:580-708
+  idm   FastWAMIDM._denoise_video (one video-only step) and FastWAMJoint's mask (bf16)
+        FastWAM/src/fastwam/models/wan22/fastwam_idm.py:283-313, fastwam_joint.py:29-49
   vae VideoVAE38_.encode of one observation frame (fp32 and bf16)
         FastWAM/src/fastwam/models/wan22/wan_video_vae.py:1285-1304, 619-733
 """
@@ -60,6 +62,8 @@ def _import_reference(ref_root: Path):
         WanContinuousFlowMatchScheduler
     from fastwam.models.action_ae import ActionAE, ActionAEConfig
     from fastwam.models.wan22.wan_video_vae import VideoVAE38_
+    from fastwam.models.wan22.fastwam_idm import FastWAMIDM
+    from fastwam.models.wan22.fastwam_joint import FastWAMJoint
     return SimpleNamespace(**locals())
 
 
@@ -265,6 +269,34 @@ def make_joint(R):
             "context": ctx, "context_mask": ctx_mask, "mask": mask, "pred_video": pv, "pred_action": pa}
 
 
+def make_idm(R):
+    """One video-only denoising step of FastWAMIDM and the FastWAMJoint MoT mask
+    (action rows see the whole video), bf16; weights of the joint fixture's shape."""
+    torch.manual_seed(6)
+    vcfg = dict(hidden_dim=128, in_dim=16, ffn_dim=256, out_dim=16, text_dim=96, freq_dim=256,
+                eps=1e-6, patch_size=(1, 2, 2), num_heads=2, attn_head_dim=128, num_layers=2,
+                has_image_input=False, seperated_timestep=True,
+                video_attention_mask_mode="first_frame_causal")
+    video = R.WanVideoDiT(**vcfg).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(6)
+    latents_video = torch.randn(1, 16, 3, 4, 6, generator=g).bfloat16()
+    C = 12
+    ctx = torch.randn(1, C, 96, generator=g).bfloat16()
+    ctx_mask = torch.ones(1, C, dtype=torch.bool)
+    ctx_mask[0, -2:] = False
+    tv = torch.tensor([600.0]).bfloat16()
+    tpf, Sv, Sa = 6, 18, 8
+    vmask = video.build_video_to_video_mask(Sv, tpf, torch.device("cpu"))
+    host = SimpleNamespace(video_expert=video)
+    with torch.no_grad():
+        pred = R.FastWAMIDM._denoise_video(host, latents_video=latents_video, timestep_video=tv, context=ctx,
+                                           context_mask=ctx_mask, video_self_attn_mask=vmask,
+                                           fuse_vae_embedding_in_latents=True)
+        mask = R.FastWAMJoint._build_mot_attention_mask(host, Sv, Sa, tpf, torch.device("cpu"))
+    return {"kind": "idm", "video_cfg": vcfg, "video": _sd(video, torch.bfloat16), "latents_video": latents_video,
+            "timestep_video": tv, "context": ctx, "context_mask": ctx_mask, "pred_video": pred, "joint_mask": mask}
+
+
 def make_vae(R):
     """Wan2.2 VAE (VideoVAE38_) encode of a first frame at a small width.
 
@@ -306,7 +338,7 @@ def main():
     torch.set_num_threads(4)
     for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
                      ("c2_video_prefill", make_c2), ("primitives", make_primitives),
-                     ("vae_encode", make_vae), ("joint_step", make_joint)):
+                     ("vae_encode", make_vae), ("joint_step", make_joint), ("idm_step", make_idm)):
         if args.only is not None and name not in args.only:
             continue
         fx = fn(R)

@@ -85,3 +85,68 @@ def test_infer_joint_against_oracle_loop():
         lat_v[:, :, 0:1] = first.float()
     _check(out["video_latents"], lat_v, "video latents")
     _check(out["action"], lat_a[0], "action latents")
+
+
+def test_joint_step_full_video_mask():
+    """FastWAMJoint: the action rows attend to every video token."""
+    fx = torch.load(GOLDEN / "joint_step.pt", weights_only=False)
+    pol, vc, ac = _policy(fx)
+    pol = P.FastWAMJointPolicy(pol.video_expert, pol.action_expert, action_sees_full_video=True)
+    vcfg, acfg = _cfgs(vc, ac)
+    pv, pa = pol.joint_step(fx["latents_video"].cuda(), fx["latents_action"].cuda(), fx["timestep_video"],
+                            fx["timestep_action"], fx["context"].cuda(), fx["context_mask"].cuda())
+    torch.cuda.synchronize()
+    f32 = lambda sd: {k: v.float() for k, v in sd.items()}
+    rv, ra = O.joint_denoise_core(f32(fx["video"]), vcfg, f32(fx["action"]), acfg, fx["latents_video"].float(),
+                                  fx["latents_action"].float(), fx["timestep_video"].float(),
+                                  fx["timestep_action"].float(), fx["context"].float(), fx["context_mask"],
+                                  full_video=True)
+    _check(pv, rv, "video prediction")
+    _check(pa, ra, "action prediction (full video)")
+
+
+def test_idm_video_step_golden():
+    """FastWAMIDM._denoise_video against the reference's recorded output."""
+    fx = torch.load(GOLDEN / "idm_step.pt", weights_only=False)
+    vid = M.WanVideoDiT(**dict(fx["video_cfg"]))
+    vid.load_state_dict({k: v.float() for k, v in fx["video"].items()})
+    act = M.ActionDiT(64, 7, 128, 96, 256, 1e-6, 2, 128, 2)
+    pol = P.FastWAMIDMPolicy(vid.to("cuda", torch.bfloat16), act.to("cuda", torch.bfloat16))
+    pv = pol.video_step(fx["latents_video"].cuda(), fx["timestep_video"], fx["context"].cuda(),
+                        fx["context_mask"].cuda())
+    torch.cuda.synchronize()
+    _check(pv, fx["pred_video"], "IDM video step")
+
+
+def test_idm_infer_action_against_oracle_loop():
+    """Two video-only steps (first frame pinned), the timestep-0 cache, then two action
+    steps over it with every video token visible."""
+    fx = torch.load(GOLDEN / "joint_step.pt", weights_only=False)
+    pol, vc, ac = _policy(fx)
+    pol = P.FastWAMIDMPolicy(pol.video_expert, pol.action_expert)
+    vcfg, acfg = _cfgs(vc, ac)
+    first = fx["latents_video"][:, :, :1].clone()
+    ctx, cm = fx["context"], fx["context_mask"]
+    out = pol.infer_action(first.cuda(), 3, ctx.cuda(), cm.cuda(), action_horizon=8, num_inference_steps=2, seed=3)
+    torch.cuda.synchronize()
+    pv32 = {k: v.float() for k, v in fx["video"].items()}
+    pa32 = {k: v.float() for k, v in fx["action"].items()}
+    gv = torch.Generator().manual_seed(3)
+    ga = torch.Generator().manual_seed(3)
+    lat_v = torch.randn((1, 16, 3, 4, 6), generator=gv).bfloat16().float()
+    lat_a = torch.randn((1, 8, 7), generator=ga).bfloat16().float()
+    lat_v[:, :, 0:1] = first.float()
+    ts, ds = O.build_inference_schedule(2, 5.0, dtype=torch.bfloat16)
+    for t, d in zip(ts, ds):
+        pv = O.video_denoise_step(pv32, vcfg, lat_v, t.reshape(1).float(), ctx.float(), cm)
+        lat_v = O.scheduler_step(pv, d.float(), lat_v)
+        lat_v[:, :, 0:1] = first.float()
+    tokens, _t, t_mod, cemb, cmask, freqs, grid, tpf = O.video_prepare(pv32, vcfg, lat_v, torch.zeros(1), ctx.float(), cm)
+    vmask = O.build_video_to_video_mask(tokens.shape[1], tpf)
+    ks, vs = O.prefill_video_cache(pv32, vcfg, tokens, freqs, t_mod, cemb, cmask, vmask)
+    amask = O.build_joint_model_mask(tokens.shape[1], 8, tpf)[tokens.shape[1]:]
+    for t, d in zip(ts, ds):
+        pa = O.denoise_action_with_video_cache(pa32, acfg, lat_a, t.reshape(1).float(), ctx.float(), cm, ks, vs, amask)
+        lat_a = O.scheduler_step(pa, d.float(), lat_a)
+    _check(out["video_latents"], lat_v, "IDM video latents")
+    _check(out["action"], lat_a[0], "IDM action")

@@ -141,3 +141,18 @@ def test_joint_step_matches_reference():
     _same(pv, fx["pred_video"])
     _same(pa, fx["pred_action"])
     assert torch.equal(O.build_mot_attention_mask(pv.shape[2] * 6, pa.shape[1], 6), fx["mask"])
+
+
+def test_idm_video_step_and_joint_mask_match_reference():
+    """FastWAMIDM._denoise_video (video expert alone + head) and FastWAMJoint's MoT
+    mask (action rows see the whole video): bit-exact at bf16."""
+    fx = _load("idm_step")
+    vc = fx["video_cfg"]
+    vcfg = O.DiTConfig(hidden_dim=vc["hidden_dim"], ffn_dim=vc["ffn_dim"], num_heads=vc["num_heads"],
+                       attn_head_dim=vc["attn_head_dim"], num_layers=vc["num_layers"], text_dim=vc["text_dim"],
+                       freq_dim=vc["freq_dim"], eps=vc["eps"], in_dim=vc["in_dim"], out_dim=vc["out_dim"],
+                       patch_size=tuple(vc["patch_size"]))
+    pv = O.video_denoise_step(fx["video"], vcfg, fx["latents_video"], fx["timestep_video"], fx["context"],
+                              fx["context_mask"])
+    _same(pv, fx["pred_video"])
+    assert torch.equal(O.build_joint_model_mask(18, 8, 6), fx["joint_mask"])
