@@ -224,20 +224,51 @@ int enqueue_prefill(const VCtx& c) {
                   kActGeluTanh, wp<void>(c, c.L.ch1), D, false));
     V_TRYI(gemm_x(c, wp<void>(c, c.L.ch1), D, c.BC, w.text2_w, w.text2_b, D, D, kEpiStore, kActNone,
                   wp<void>(c, c.L.cemb), D, false));
-    for (int l = 0; l < Lyr; ++l) {
+    // Cross K / V of every block, context-token major: ckv[row][l * 2HD + (K | V)]
+    // (row = b * C + t); the K half RMSNorm'd with block l's norm_k.
+    const long long ld = static_cast<long long>(Lyr) * 2 * HD;
+    __nv_bfloat16* ckv_all = wp<__nv_bfloat16>(c, c.L.ckv);
+    // projections stored block-major in one allocation (as the Python packer lays
+    // them out): one GEMM over all blocks, one RMSNorm launch over (row, block)
+    bool stacked = true;
+    for (int l = 1; l < Lyr && stacked; ++l) {
+      const fam_action_layer& l0 = c.e->layers[0];
       const fam_action_layer& ly = c.e->layers[l];
-      __nv_bfloat16* ckv = wp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.BC * 2 * HD;
-      V_TRYI(gemm_x(c, wp<void>(c, c.L.cemb), D, c.BC, ly.ckv_w, ly.ckv_b, 2 * HD, D, kEpiStore,
-                    kActNone, ckv, 2 * HD, false));
+      stacked = bf(ly.ckv_w) == bf(l0.ckv_w) + static_cast<size_t>(l) * 2 * HD * D &&
+                bf(ly.ckv_b) == bf(l0.ckv_b) + static_cast<size_t>(l) * 2 * HD &&
+                bf(ly.cnorm_k) == bf(l0.cnorm_k) + static_cast<size_t>(l) * HD;
+    }
+    if (stacked) {
+      const fam_action_layer& l0 = c.e->layers[0];
+      V_TRYI(gemm_x(c, wp<void>(c, c.L.cemb), D, c.BC, l0.ckv_w, l0.ckv_b, static_cast<int>(ld), D,
+                    kEpiStore, kActNone, ckv_all, ld, false));
       RmsRowsArgs r = {};
-      r.in = ckv;
-      r.in_stride = 2 * HD;
-      r.w = bf(ly.cnorm_k);
-      r.out = ckv;
+      r.in = ckv_all;
+      r.in_stride = 2 * HD;  // (row, block) slice rr = row * L + l starts at rr * 2HD
+      r.w = bf(l0.cnorm_k);
+      r.w_period = Lyr;
+      r.w_stride = HD;
+      r.out = ckv_all;
       r.out_stride = 2 * HD;
       r.N = HD;
       r.eps = g.eps;
-      V_LAUNCH(launch_rms_rows(r, c.BC, c.st, c.pdl));
+      V_LAUNCH(launch_rms_rows(r, c.BC * Lyr, c.st, c.pdl));
+    } else {
+      for (int l = 0; l < Lyr; ++l) {
+        const fam_action_layer& ly = c.e->layers[l];
+        __nv_bfloat16* ckv = ckv_all + static_cast<size_t>(l) * 2 * HD;
+        V_TRYI(gemm_x(c, wp<void>(c, c.L.cemb), D, c.BC, ly.ckv_w, ly.ckv_b, 2 * HD, D, kEpiStore,
+                      kActNone, ckv, ld, false));
+        RmsRowsArgs r = {};
+        r.in = ckv;
+        r.in_stride = ld;
+        r.w = bf(ly.cnorm_k);
+        r.out = ckv;
+        r.out_stride = ld;
+        r.N = HD;
+        r.eps = g.eps;
+        V_LAUNCH(launch_rms_rows(r, c.BC, c.st, c.pdl));
+      }
     }
   }
 
@@ -336,11 +367,11 @@ int enqueue_prefill(const VCtx& c) {
       ca.q = rq.out;
       ca.q_bs = static_cast<long long>(S) * HD;
       ca.q_ts = HD;
-      const __nv_bfloat16* ckv = wp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * c.BC * 2 * HD;
+      const __nv_bfloat16* ckv = wp<__nv_bfloat16>(c, c.L.ckv) + static_cast<size_t>(l) * 2 * HD;
       ca.k1 = ckv;
       ca.v1 = ckv + HD;
-      ca.kv1_bs = static_cast<long long>(io.context_tokens) * 2 * HD;
-      ca.kv1_ts = 2 * HD;
+      ca.kv1_bs = static_cast<long long>(io.context_tokens) * Lyr * 2 * HD;
+      ca.kv1_ts = static_cast<long long>(Lyr) * 2 * HD;
       ca.S1 = io.context_tokens;
       ca.key_mask = io.context_mask;
       ca.key_mask_bs = io.context_tokens;

@@ -449,6 +449,12 @@ class VideoPrefillEngine:
             return t.data_ptr()
 
         layers = (_abi.ActionLayer * dit.num_layers)()
+        # every block's cross K/V projection and norm_k stacked block-major, so the
+        # prefill projects the (step-invariant) context for all blocks in one GEMM
+        ckv_w = bfw(torch.stack([torch.cat([b.cross_attn.k.weight, b.cross_attn.v.weight], 0) for b in dit.blocks]))
+        ckv_b = bfw(torch.stack([torch.cat([b.cross_attn.k.bias, b.cross_attn.v.bias], 0) for b in dit.blocks]))
+        cnorm_k = bfw(torch.stack([b.cross_attn.norm_k.weight for b in dit.blocks]))
+        self.keep += [ckv_w, ckv_b, cnorm_k]
         for i, b in enumerate(dit.blocks):
             sa, ca, L = b.self_attn, b.cross_attn, layers[i]
             L.modulation = ptr(bfw(b.modulation.reshape(6, -1)))
@@ -458,9 +464,8 @@ class VideoPrefillEngine:
             L.o_w, L.o_b = ptr(bfw(sa.o.weight)), ptr(bfw(sa.o.bias))
             L.norm3_w, L.norm3_b = ptr(bfw(b.norm3.weight)), ptr(bfw(b.norm3.bias))
             L.cq_w, L.cq_b = ptr(bfw(ca.q.weight)), ptr(bfw(ca.q.bias))
-            L.cnorm_q, L.cnorm_k = ptr(bfw(ca.norm_q.weight)), ptr(bfw(ca.norm_k.weight))
-            L.ckv_w = ptr(bfw(torch.cat([ca.k.weight, ca.v.weight], 0)))
-            L.ckv_b = ptr(bfw(torch.cat([ca.k.bias, ca.v.bias], 0)))
+            L.cnorm_q, L.cnorm_k = ptr(bfw(ca.norm_q.weight)), cnorm_k[i].data_ptr()
+            L.ckv_w, L.ckv_b = ckv_w[i].data_ptr(), ckv_b[i].data_ptr()
             L.co_w, L.co_b = ptr(bfw(ca.o.weight)), ptr(bfw(ca.o.bias))
             L.ffn0_w, L.ffn0_b = ptr(bfw(b.ffn[0].weight)), ptr(bfw(b.ffn[0].bias))
             L.ffn2_w, L.ffn2_b = ptr(bfw(b.ffn[2].weight)), ptr(bfw(b.ffn[2].bias))
