@@ -243,6 +243,130 @@ __global__ void __launch_bounds__(kRowThreads) qkv_post_kernel(const QkvPostArgs
   }
 }
 
+// qkv_post over a bf16 [rows, 3HD] input that already holds the bias (the
+// GEMM epilogue adds it), in 16-byte groups (HD and head_dim multiples of 8,
+// 16-byte aligned rows).  Each thread issues every load of its
+// part of the row before using any, so one memory latency covers the row; the
+// RoPE table and the norm weights load before the programmatic-launch wait, and
+// the q and k sums of squares share one block reduction.  Per element the
+// arithmetic is the one of qkv_post_kernel.
+constexpr int kQkvLoads = 5;  // 8-column groups per thread: 3HD <= 5 * 8 * kRowThreads
+constexpr int kQkvNorm = 3;   // q and k groups per thread: 2HD <= 3 * 8 * kRowThreads
+
+__device__ __forceinline__ void unpack_bf8(const uint4 u, float* o) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 t = __bfloat1622float2(h[k]);
+    o[2 * k] = t.x;
+    o[2 * k + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf8(const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+  return u;
+}
+
+__device__ __forceinline__ float2 block_sum2(float2 v, float2* red) {
+  v.x = warp_sum(v.x);
+  v.y = warp_sum(v.y);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float2 t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : make_float2(0.0f, 0.0f);
+  if (w == 0) {
+    t.x = warp_sum(t.x);
+    t.y = warp_sum(t.y);
+  }
+  if (threadIdx.x == 0) red[32] = t;
+  __syncthreads();
+  return red[32];
+}
+
+__global__ void __launch_bounds__(kRowThreads, 3) qkv_post_wide_kernel(const QkvPostArgs a) {
+  extern __shared__ float sbuf[];
+  __shared__ float2 red[33];
+  const int row = blockIdx.x;
+  const int HD = a.HD, G = 3 * HD / 8, GQ = HD / 4, GK = HD / 8;
+  const int half = a.head_dim / 2;
+  const float2* tab = a.rope + static_cast<long long>(row % a.rows_per_batch) * half;
+  uint4 wv[kQkvNorm];
+  float4 c0[kQkvNorm], c1[kQkvNorm];
+#pragma unroll
+  for (int j = 0; j < kQkvNorm; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < GQ) {
+      const bool is_k = g >= GK;
+      const int f = 8 * (is_k ? g - GK : g);
+      wv[j] = *reinterpret_cast<const uint4*>((is_k ? a.norm_k : a.norm_q) + f);
+      const int i = (f % a.head_dim) / 2;  // first pair index inside the head (multiple of 4)
+      c0[j] = *reinterpret_cast<const float4*>(tab + i);
+      c1[j] = *reinterpret_cast<const float4*>(tab + i + 2);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const __nv_bfloat16* in = a.qkv_bf16 + static_cast<long long>(row) * 3 * HD;
+  uint4 raw[kQkvLoads];
+#pragma unroll
+  for (int j = 0; j < kQkvLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) raw[j] = *reinterpret_cast<const uint4*>(in + 8 * g);
+  }
+  float* sq = sbuf;  // [0, HD) q, [HD, 2HD) k
+  float ssq = 0.0f, ssk = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kQkvLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) {
+      const int f = 8 * g;
+      float y[8];
+      unpack_bf8(raw[j], y);
+      if (f < 2 * HD) {
+        float s2 = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s2 += y[e] * y[e];
+        if (f < HD) ssq += s2; else ssk += s2;
+        *reinterpret_cast<float4*>(sq + f) = make_float4(y[0], y[1], y[2], y[3]);
+        *reinterpret_cast<float4*>(sq + f + 4) = make_float4(y[4], y[5], y[6], y[7]);
+      } else {
+        *reinterpret_cast<uint4*>(a.v_out + static_cast<long long>(row) * a.out_stride + (f - 2 * HD)) =
+            pack_bf8(y);
+      }
+    }
+  }
+  const float2 ss = block_sum2(make_float2(ssq, ssk), red);
+  const float rq = rsqrtf(ss.x / HD + a.eps);
+  const float rk = rsqrtf(ss.y / HD + a.eps);
+#pragma unroll
+  for (int j = 0; j < kQkvNorm; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < GQ) {  // the same thread wrote these columns to shared memory above
+      const bool is_k = g >= GK;
+      const int f = 8 * (is_k ? g - GK : g);
+      const float r = is_k ? rk : rq;
+      const float* src = sq + (is_k ? HD : 0) + f;
+      float w[8], x[8], o[8];
+      unpack_bf8(wv[j], w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = rbf(rbf(src[e] * r) * w[e]);
+      const float cs[8] = {c0[j].x, c0[j].y, c0[j].z, c0[j].w, c1[j].x, c1[j].y, c1[j].z, c1[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // (cos, sin) of pair q
+        o[2 * q] = x[2 * q] * cs[2 * q] - x[2 * q + 1] * cs[2 * q + 1];
+        o[2 * q + 1] = x[2 * q] * cs[2 * q + 1] + x[2 * q + 1] * cs[2 * q];
+      }
+      *reinterpret_cast<uint4*>((is_k ? a.k_out : a.q_out) + static_cast<long long>(row) * a.out_stride + f) =
+          pack_bf8(o);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ rms_rows
 // out = RMSNorm(sum partials + bias) * w, one CTA per row.  With nsplit == 0
 // the input is a bf16 matrix (in place allowed).  dynamic smem: N floats.
@@ -399,6 +523,17 @@ cudaError_t launch_resid_norm(const ResidNormArgs& a, int rows, cudaStream_t st,
 
 cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, bool pdl) {
   const size_t smem = sizeof(float) * 2 * a.HD;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool wide = a.nsplit == 0 && a.qkv_bf16 != nullptr && a.bias == nullptr && a.HD % 8 == 0 &&
+                    a.head_dim % 8 == 0 && 3 * a.HD <= kQkvLoads * 8 * kRowThreads &&
+                    2 * a.HD <= kQkvNorm * 8 * kRowThreads && a.out_stride % 8 == 0 && al16(a.qkv_bf16) &&
+                    al16(a.norm_q) && al16(a.norm_k) && al16(a.rope) && al16(a.q_out) && al16(a.k_out) &&
+                    al16(a.v_out);
+  if (wide) {
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(qkv_post_wide_kernel), smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(qkv_post_wide_kernel, dim3(rows), dim3(kRowThreads), smem, st, pdl, a);
+  }
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(qkv_post_kernel), smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(qkv_post_kernel, dim3(rows), dim3(kRowThreads), smem, st, pdl, a);
