@@ -432,7 +432,10 @@ class WanVideoDiT(nn.Module):
 class VideoPrefillEngine:
     """Packed bf16 weights + fam_video_expert handle + workspace of one WanVideoDiT."""
 
-    def __init__(self, dit: WanVideoDiT):
+    def __init__(self, dit: WanVideoDiT, stack_cross_kv: bool = True):
+        """stack_cross_kv: store every block's cross K/V projection in one block-major
+        allocation (one context GEMM per prefill); False keeps one allocation per block
+        (one GEMM per block, the same result)."""
         p = next(dit.parameters())
         if not p.is_cuda:
             raise RuntimeError("WanVideoDiT must be on a CUDA device for the libfam path")
@@ -464,8 +467,12 @@ class VideoPrefillEngine:
             L.o_w, L.o_b = ptr(bfw(sa.o.weight)), ptr(bfw(sa.o.bias))
             L.norm3_w, L.norm3_b = ptr(bfw(b.norm3.weight)), ptr(bfw(b.norm3.bias))
             L.cq_w, L.cq_b = ptr(bfw(ca.q.weight)), ptr(bfw(ca.q.bias))
-            L.cnorm_q, L.cnorm_k = ptr(bfw(ca.norm_q.weight)), cnorm_k[i].data_ptr()
-            L.ckv_w, L.ckv_b = ckv_w[i].data_ptr(), ckv_b[i].data_ptr()
+            if stack_cross_kv:
+                L.cnorm_k, L.ckv_w, L.ckv_b = cnorm_k[i].data_ptr(), ckv_w[i].data_ptr(), ckv_b[i].data_ptr()
+            else:
+                L.cnorm_k, L.ckv_w, L.ckv_b = (ptr(cnorm_k[i].clone()), ptr(ckv_w[i].clone()),
+                                               ptr(ckv_b[i].clone()))
+            L.cnorm_q = ptr(bfw(ca.norm_q.weight))
             L.co_w, L.co_b = ptr(bfw(ca.o.weight)), ptr(bfw(ca.o.bias))
             L.ffn0_w, L.ffn0_b = ptr(bfw(b.ffn[0].weight)), ptr(bfw(b.ffn[0].bias))
             L.ffn2_w, L.ffn2_b = ptr(bfw(b.ffn[2].weight)), ptr(bfw(b.ffn[2].bias))

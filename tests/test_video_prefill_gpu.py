@@ -73,3 +73,24 @@ def test_config2_width_two_blocks():
     torch.backends.cudnn.allow_tf32 = False
     _run(D=3072, H=24, hd=128, F=14336, T=4096, L=2, Cin=48, B=1, Fr=5, Hh=32, Ww=44, C=64,
          ref_device="cuda")
+
+
+def test_per_block_cross_kv_layout_matches_stacked():
+    """Blocks whose cross K/V projections are separate allocations take the per-block
+    context GEMMs; the caches equal those of the stacked (one GEMM) layout."""
+    dit = _run(D=256, H=2, hd=128, F=512, T=64, L=3, Cin=16, B=2, Fr=3, Hh=8, Ww=12, C=10, ref_device="cpu",
+               seed=5)
+    g = torch.Generator().manual_seed(9)
+    lat = torch.randn(2, 16, 3, 8, 12, generator=g).bfloat16().cuda()
+    ctx = torch.randn(2, 10, 64, generator=g).bfloat16().cuda()
+    cm = torch.ones(2, 10, dtype=torch.bool, device="cuda")
+    t = torch.full((2,), 300.0).bfloat16()
+    ks, vs = dit.prefill(lat, t, ctx, cm)
+    ks = [k.clone() for k in ks]
+    vs = [v.clone() for v in vs]
+    eng = M.VideoPrefillEngine(dit, stack_cross_kv=False)
+    ks2, vs2 = eng.prefill(lat, t, ctx, cm)
+    torch.cuda.synchronize()
+    for l in range(3):
+        _check(ks2[l], ks[l], f"K[{l}] per-block")
+        _check(vs2[l], vs[l], f"V[{l}] per-block")
