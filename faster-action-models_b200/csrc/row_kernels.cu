@@ -400,6 +400,59 @@ __global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const RmsRowsArgs
   }
 }
 
+// rms_rows over a bias-free bf16 input in 16-byte groups: the weights load
+// before the programmatic-launch wait, every load of a thread's part of the row
+// is in flight at once and the row stays in registers (in place allowed: each
+// thread writes only the columns it read).  Per element the arithmetic is the
+// one of rms_rows_kernel.
+constexpr int kRmsLoads = 2;  // 8-column groups per thread: N <= 2 * 8 * kRowThreads
+
+__global__ void __launch_bounds__(kRowThreads) rms_rows_wide_kernel(const RmsRowsArgs a) {
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const int G = a.N / 8;
+  const __nv_bfloat16* wr = a.w + (a.w_period > 0 ? static_cast<long long>(row % a.w_period) * a.w_stride : 0);
+  uint4 wv[kRmsLoads];
+#pragma unroll
+  for (int j = 0; j < kRmsLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) wv[j] = *reinterpret_cast<const uint4*>(wr + 8 * g);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const __nv_bfloat16* in = a.in + static_cast<long long>(row) * a.in_stride;
+  uint4 raw[kRmsLoads];
+#pragma unroll
+  for (int j = 0; j < kRmsLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) raw[j] = *reinterpret_cast<const uint4*>(in + 8 * g);
+  }
+  float y[kRmsLoads][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kRmsLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) {
+      unpack_bf8(raw[j], y[j]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += y[j][e] * y[j][e];
+    }
+  }
+  const float r = rsqrtf(block_sum(ss, red) / a.N + a.eps);
+  __nv_bfloat16* out = a.out + static_cast<long long>(row) * a.out_stride;
+#pragma unroll
+  for (int j = 0; j < kRmsLoads; ++j) {
+    const int g = threadIdx.x + j * kRowThreads;
+    if (g < G) {
+      float w[8], o[8];
+      unpack_bf8(wv[j], w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = rbf(y[j][e] * r) * w[e];
+      *reinterpret_cast<uint4*>(out + 8 * g) = pack_bf8(o);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ sinusoid
 // out[r][i] = cos(t_r * 10000^(-i/half)), out[r][half+i] = sin(...), computed
 // in fp64 and rounded to bf16 (the timestep dtype of a bf16 model).
@@ -540,6 +593,11 @@ cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, boo
 }
 
 cudaError_t launch_rms_rows(const RmsRowsArgs& a, int rows, cudaStream_t st, bool pdl) {
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (a.nsplit == 0 && a.in != nullptr && a.bias == nullptr && a.N % 8 == 0 &&
+      a.N <= kRmsLoads * 8 * kRowThreads && a.in_stride % 8 == 0 && a.out_stride % 8 == 0 &&
+      (a.w_period <= 0 || a.w_stride % 8 == 0) && al16(a.in) && al16(a.out) && al16(a.w))
+    return launch_pdl(rms_rows_wide_kernel, dim3(rows), dim3(kRowThreads), 0, st, pdl, a);
   const size_t smem = sizeof(float) * a.N;
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(rms_rows_kernel), smem);
   if (e != cudaSuccess) return e;
