@@ -80,6 +80,16 @@ class FastWAMActionPolicy:
         self.device = next(action_expert.parameters()).device
 
     @torch.no_grad()
+    def _denoise_action_with_video_cache(self, latents_action: torch.Tensor, timestep_action,
+                                         context: torch.Tensor, context_mask, video_cache_k, video_cache_v,
+                                         action_attention_mask) -> torch.Tensor:
+        """FastWAM._denoise_action_with_video_cache (fastwam.py:771-804): one model evaluation of
+        the action expert over the video K/V cache; the velocity [B, Sa, A].  An instance may
+        replace this attribute; infer_action then runs its Euler loop through the replacement."""
+        return self.action_expert.engine().denoise_step(latents_action, timestep_action, context, context_mask,
+                                                        video_cache_k, video_cache_v, action_attention_mask)
+
+    @torch.no_grad()
     def infer_action(self, first_frame_latents: torch.Tensor, context: torch.Tensor,
                      context_mask: torch.Tensor, action_horizon: int, num_inference_steps: int = 20,
                      sigma_shift: Optional[float] = None, seed: Optional[int] = None,
@@ -99,7 +109,15 @@ class FastWAMActionPolicy:
         ts, ds = build_inference_schedule(num_inference_steps,
                                           self.shift if sigma_shift is None else float(sigma_shift),
                                           dtype=self.torch_dtype)
-        lat = act.engine().chunk(lat, ts, ds, context, context_mask, k, v, mask)
+        if "_denoise_action_with_video_cache" in self.__dict__:
+            # the step was replaced on this instance (as the reference's perf / oracle
+            # harnesses do): run the Euler loop through it, one model evaluation per step
+            for t, d in zip(ts, ds):
+                tt = torch.full((lat.shape[0],), float(t), dtype=self.torch_dtype)
+                vel = self._denoise_action_with_video_cache(lat, tt, context, context_mask, k, v, mask)
+                lat = (lat + vel * float(d)).to(self.torch_dtype)
+        else:
+            lat = act.engine().chunk(lat, ts, ds, context, context_mask, k, v, mask)
         out = {}
         if self.action_vae is not None:
             out["action"] = self.action_vae.decode(lat.float())[0].to(dtype=self.torch_dtype).float().cpu()
