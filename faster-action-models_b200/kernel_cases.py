@@ -17,6 +17,10 @@ synchronizes; under ncu, skip the warm-up launches with `-s`.
                (hidden 1024, 24 x 128 heads) over that step's K/V; prints the p50 latency
   vae_c1       WanVideoVAE38 encode of one 512 x 704 observation frame (dim 160, z 48,
                the configs-1/2 latent grid 32 x 44); prints the p50 latency
+  cae_c4       CAEPipeline of BASELINE config 4 on one GPU: the config-2 backbone (final
+               token states), the config-0 compact expert (4 Euler steps, text_dim 3072)
+               and the Action-VAE decode, for B = 1, 16, 128 independent observations in
+               micro-batches of 16; prints chunks/s per B (p50 over the repeats)
 """
 import importlib
 import sys
@@ -147,6 +151,39 @@ def main(case: str, reps: int) -> None:
             times.append(s0.elapsed_time(e0))
         times = sorted(times[2:])
         print("vae_c1 encode ms p50", round(times[len(times) // 2], 3))
+    elif case == "cae_c4":
+        torch.manual_seed(0)
+        with torch.device(dev):
+            vid = M.WanVideoDiT(hidden_dim=3072, in_dim=48, ffn_dim=14336, out_dim=48, text_dim=4096, freq_dim=256,
+                                eps=1e-6, patch_size=(1, 2, 2), num_heads=24, attn_head_dim=128, num_layers=30,
+                                has_image_input=False, seperated_timestep=True,
+                                video_attention_mask_mode="first_frame_causal")
+            dit = M.ActionDiT(hidden_dim=32, action_dim=16, ffn_dim=128, text_dim=3072, freq_dim=256, eps=1e-6,
+                              num_heads=4, attn_head_dim=8, num_layers=8)
+            ae = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16,
+                                             decoder_hidden=256, video_cond_dim=0, variational=True))
+        pipe = P.CAEPipeline(vid.to(torch.bfloat16), dit.to(torch.bfloat16), ae, num_steps=4, shift=1.0,
+                             micro_batch=16)
+        g = torch.Generator().manual_seed(0)
+        for B in (1, 16, 128):
+            lat = torch.randn(B, 48, 5, 32, 44, generator=g).bfloat16().to(dev)
+            ctx = torch.randn(B, 64, 4096, generator=g).bfloat16().to(dev)
+            cm = torch.ones(B, 64, dtype=torch.bool, device=dev)
+            noise = torch.randn(B, 8, 16, generator=g).to(dev)
+            pipe(lat, 500.0, ctx, cm, noise)
+            torch.cuda.synchronize()
+            ms = []
+            for _ in range(reps):
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                out = pipe(lat, 500.0, ctx, cm, noise)
+                s1.record()
+                torch.cuda.synchronize()
+                ms.append(s0.elapsed_time(s1))
+            assert out.shape == (B, 32, 7) and bool(torch.isfinite(out).all())
+            p50 = sorted(ms)[len(ms) // 2]
+            print(f"cae_c4 B={B} p50 {p50:.2f} ms  {B / (p50 * 1e-3):.1f} chunks/s")
+            del lat, ctx, cm, noise
     else:
         raise SystemExit(f"unknown case {case!r}")
     torch.cuda.synchronize()
