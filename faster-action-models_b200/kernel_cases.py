@@ -17,6 +17,9 @@ synchronizes; under ncu, skip the warm-up launches with `-s`.
                (hidden 1024, 24 x 128 heads) over that step's K/V; prints the p50 latency
   vae_c1       WanVideoVAE38 encode of one 512 x 704 observation frame (dim 160, z 48,
                the configs-1/2 latent grid 32 x 44); prints the p50 latency
+  xattn_c2     ops.attention as the backbone's cross attention: 1,760 query tokens, 24 heads
+               x 128, over 64 context tokens with a key mask (K and V halves of one
+               [64, 6144] row)
   cae_c4       CAEPipeline of BASELINE config 4 on one GPU: the config-2 backbone (final
                token states), the config-0 compact expert (4 Euler steps, text_dim 3072)
                and the Action-VAE decode, for B = 1, 16, 128 independent observations in
@@ -151,6 +154,13 @@ def main(case: str, reps: int) -> None:
             times.append(s0.elapsed_time(e0))
         times = sorted(times[2:])
         print("vae_c1 encode ms p50", round(times[len(times) // 2], 3))
+    elif case == "xattn_c2":
+        q = torch.randn(1, 1760, 3072, device=dev).bfloat16()
+        kv = torch.randn(1, 64, 6144, device=dev).bfloat16()
+        km = torch.ones(1, 64, dtype=torch.uint8, device=dev)
+        out = torch.empty_like(q)
+        for _ in range(reps):
+            ops.attention(q, kv[:, :, :3072], kv[:, :, 3072:], 24, key_mask=km, kv_splits=1, out=out)
     elif case == "cae_c4":
         torch.manual_seed(0)
         with torch.device(dev):
