@@ -150,3 +150,23 @@ def test_idm_infer_action_against_oracle_loop():
         lat_a = O.scheduler_step(pa, d.float(), lat_a)
     _check(out["video_latents"], lat_v, "IDM video latents")
     _check(out["action"], lat_a[0], "IDM action")
+
+
+def test_optional_idm_modes_match_their_policies():
+    """FastWAMOptionalIDM.infer_action: "first_frame" is FastWAM's path, "idm" the IDM path."""
+    fx = torch.load(GOLDEN / "joint_step.pt", weights_only=False)
+    pol, _, _ = _policy(fx)
+    opt = P.FastWAMOptionalIDMPolicy(pol.video_expert, pol.action_expert)
+    first = fx["latents_video"][:, :, :1].clone().cuda()
+    ctx, cm = fx["context"].cuda(), fx["context_mask"].cuda()
+    a = opt.infer_action(first, ctx, cm, action_horizon=8, num_inference_steps=2, seed=5,
+                         action_infer_mode="first_frame")
+    b = P.FastWAMActionPolicy(pol.video_expert, pol.action_expert).infer_action(
+        first, ctx, cm, action_horizon=8, num_inference_steps=2, seed=5)
+    _check(a["action"], b["action"], "first_frame mode")
+    c = opt.infer_action(first, ctx, cm, action_horizon=8, num_inference_steps=2, seed=5, num_latent_frames=3,
+                         action_infer_mode="idm")
+    d = P.FastWAMIDMPolicy(pol.video_expert, pol.action_expert).infer_action(
+        first, 3, ctx, cm, action_horizon=8, num_inference_steps=2, seed=5)
+    _check(c["action"], d["action"], "idm mode")
+    _check(c["video_latents"], d["video_latents"], "idm mode video")
