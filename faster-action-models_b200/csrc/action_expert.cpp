@@ -47,10 +47,17 @@ int choose_splits(int n_out, int k, int rows) {
 struct WsLayout {
   size_t x, h, part, q, ka, va, ao, qc, ci, fh, apart, ctr, tmod, sin, th1, th2, cemb, ch1, ckv, vel;
   size_t fsync, fssq, fpart;  // fused-kernel barrier / merge counters, RMS sums, split partials
+  size_t fx, fslots;          // fused-kernel bf16 residual [32][D], residual GEMM split partials
   size_t fsync_bytes, fssq_bytes;
   size_t total;
   int s_qkv, s_o, s_cq, s_co, s_f2;
 };
+
+// Words of the fused kernel's sync block before its flag lines: go, abort,
+// the joint-attention merge counters [N][L][H], the residual tile counters.
+size_t fused_sync_words(int N, int L, int H) {
+  return 2 + static_cast<size_t>(N) * L * H + 3 * (kFusedMaxD / 128);
+}
 
 WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
   WsLayout w = {};
@@ -99,13 +106,17 @@ WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
   w.ckv = take(static_cast<size_t>(c.num_layers) * crow * 2 * HD * 2);
   w.vel = take(rows * c.action_dim * 2);
   // fused persistent kernel (batch 1): counters, per-token RMS sums, split partials
-  // [go, abort, merge counters] padded to a 128-byte line, then one flag line per CTA
-  w.fsync_bytes = ((2 + static_cast<size_t>(N) * c.num_layers * c.num_heads + 31) / 32 * 32 +
+  // [go, abort, merge counters, residual tile counters] padded to a 128-byte
+  // line, then one flag line per CTA
+  w.fsync_bytes = ((fused_sync_words(N, c.num_layers, c.num_heads) + 31) / 32 * 32 +
                    static_cast<size_t>(kFusedMaxCtas) * 32) * 4;
-  w.fssq_bytes = static_cast<size_t>(N) * c.num_layers * 3 * kFusedRows * 4;
+  w.fssq_bytes = static_cast<size_t>(N) * c.num_layers * 3 * kFusedRows * 8;
   w.fsync = take(w.fsync_bytes);
   w.fssq = take(w.fssq_bytes);
   w.fpart = take(static_cast<size_t>(c.num_heads) * 64 * kFusedRows * 66 * 4);
+  w.fx = take(static_cast<size_t>(kFusedRows) * D * 2);
+  // residual GEMM split partials: at most max(heads, F / 128) splits per tile
+  w.fslots = take(static_cast<size_t>(std::max(c.num_heads, F / 128)) * kFusedRows * D * 4);
   w.total = off;
   return w;
 }
@@ -357,6 +368,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     FAM_TRYI(gemm_w(c, ly.o_w, nullptr, D, HD, aa.out, HD, rows, c.L.s_o, kActNone, part, D, true));
     ResidNormArgs r1 = {};
     r1.x = x;
+    r1.round_residual = 1;  // the reference keeps the residual in bf16
     r1.partials = part;
     r1.split_stride = static_cast<long long>(rows) * D;
     r1.nsplit = c.L.s_o;
@@ -416,6 +428,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     }
     ResidNormArgs r2 = {};
     r2.x = x;
+    r2.round_residual = 1;  // the reference keeps the residual in bf16
     r2.partials = c.crow > 0 ? part : nullptr;
     r2.split_stride = static_cast<long long>(rows) * D;
     r2.nsplit = c.L.s_co;
@@ -437,6 +450,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
                     part, D, true));
     ResidNormArgs r3 = {};
     r3.x = x;
+    r3.round_residual = 1;  // the reference keeps the residual in bf16
     r3.partials = part;
     r3.split_stride = static_cast<long long>(rows) * D;
     r3.nsplit = c.L.s_f2;
@@ -560,7 +574,8 @@ int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float
   a.ckv = wsp<__nv_bfloat16>(c, c.L.ckv);
   a.ctx_mask = io.context_mask;
   a.C = io.context_tokens;
-  a.x = wsp<float>(c, c.L.x);
+  a.x = wsp<__nv_bfloat16>(c, c.L.fx);
+  a.slots = wsp<float>(c, c.L.fslots);
   a.q = wsp<__nv_bfloat16>(c, c.L.q);
   a.ka = wsp<__nv_bfloat16>(c, c.L.ka);
   a.va = wsp<__nv_bfloat16>(c, c.L.va);
@@ -568,10 +583,11 @@ int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float
   a.qc = wsp<__nv_bfloat16>(c, c.L.qc);
   a.ci = wsp<__nv_bfloat16>(c, c.L.ci);
   a.fh = wsp<__nv_bfloat16>(c, c.L.fh);
-  a.ssq = wsp<float>(c, c.L.fssq);
+  a.ssq = wsp<double>(c, c.L.fssq);
   a.apart = wsp<float>(c, c.L.fpart);
   a.sync = wsp<unsigned>(c, c.L.fsync);
-  a.flags = a.sync + (2 + static_cast<size_t>(N) * g.num_layers * g.num_heads + 31) / 32 * 32;
+  a.tile_ctr = a.sync + 2 + static_cast<size_t>(N) * g.num_layers * g.num_heads;
+  a.flags = a.sync + (fused_sync_words(N, g.num_layers, g.num_heads) + 31) / 32 * 32;
   a.status = e->status;
   a.latent = static_cast<__nv_bfloat16*>(latent);
   a.trace = static_cast<__nv_bfloat16*>(trace);

@@ -12,13 +12,17 @@
 //                       drains — weights never depend on activations, so the
 //                       stream runs ahead across phase and step boundaries;
 //   warps 1..11         run the phases: stage the MMA B operand (the token
-//   (workers)           rows) straight from the fp32 residual stream with the
+//   (workers)           rows) straight from the bf16 residual stream with the
 //                       block's LayerNorm / AdaLN folded in, issue tcgen05.mma
-//                       (warp 1 lane 0) into a 128 x 32 fp32 TMEM accumulator,
-//                       and apply the epilogue in warps 2..5 (bias, RMSNorm
-//                       statistics, RoPE, GELU, gated residual adds as fp32
-//                       atomics into the residual stream).  Attention phases
-//                       use bf16 mma.sync fragments over cp.async-staged K/V.
+//                       into 128 x 32 fp32 TMEM accumulators, and apply the
+//                       epilogue in warps 2..9 (bias, RMSNorm statistics,
+//                       RoPE, GELU; the residual GEMMs store split partials
+//                       and the last split of a tile completes the gated
+//                       residual add with the reference's bf16 roundings).
+//                       Attention phases use bf16 mma.sync fragments over
+//                       cp.async-staged K/V.
+// Every cross-CTA sum is order-independent (fp64 sums of squares, split
+// partials summed in split order), so a launch is deterministic.
 //
 // Per block the phases are separated by grid barriers:
 //   qkv GEMM (AdaLN1 prologue; q/k RMSNorm sums + weight + RoPE epilogue)
@@ -74,6 +78,7 @@ struct FusedSmemTail {
   float stat[kFusedRows][2];
   float scale[2][kFusedRows];                 // per-row q scale, per-key scale
   int last;
+  int fin;                                    // this residual item completes its tile
   // pair items: the peer CTA writes its half-row LayerNorm sums here and
   // arrives on xstat_bar (one arrival per worker warp); its partial
   // accumulators arrive in the staging (kStgXacc) by one bulk copy that
@@ -314,7 +319,7 @@ __device__ void ln_const_prefetch(const FusedArgs& a, uint8_t* stg, int step, in
     if (mode == 0) {
       // AdaLN: bf16 (1 + scale) and shift pairs, [D / 2] bf16x2 each (the
       // reference's modulate works on bf16 tensors; the staging applies them
-      // with one packed bf16 FMA per pair)
+      // as a packed bf16 multiply, then a packed bf16 add)
       uint4* cm = reinterpret_cast<uint4*>(stg + kStgLnConst) + ch;
       uint4* ca = reinterpret_cast<uint4*>(stg + kStgLnConst) + D / 8 + ch;
       *cm = make_uint4(pack_bf16(m[0], m[1]), pack_bf16(m[2], m[3]), pack_bf16(m[4], m[5]), pack_bf16(m[6], m[7]));
@@ -342,36 +347,43 @@ __device__ __forceinline__ float4 ld_cg_f4_early(const float* p) {
   return v;
 }
 
-// Half rows: this CTA's D / 2 columns [half * D / 2, ...) of residual row r,
-// lane chunks lane + 32u (u < NCH, D / 2 = 256 NCH).
+__device__ __forceinline__ uint4 ld_cg_u4_early(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Half rows: this CTA's D / 2 columns [half * D / 2, ...) of the bf16
+// residual row r, lane chunks lane + 32u (u < NCH, D / 2 = 256 NCH), 8 values
+// per 16-byte load kept packed; rows >= R read as zeros.
 template <int NCH>
-__device__ __forceinline__ void ln_load_half(const FusedArgs& a, int r, int lane, int half,
-                                             float (&v)[NCH * 8]) {
-  const float* xr = a.x + static_cast<long long>(r) * a.D + half * (NCH * 256);
+__device__ __forceinline__ void ln_load_half(const FusedArgs& a, int r, int lane, int half, uint4 (&v)[NCH]) {
+  const __nv_bfloat16* xr = a.x + static_cast<long long>(r) * a.D + half * (NCH * 256);
 #pragma unroll
   for (int u = 0; u < NCH; ++u) {
     const int ch = lane + 32 * u;
-    float4 p0 = make_float4(0.f, 0.f, 0.f, 0.f), p1 = p0;
-    if (r < a.R) {
-      p0 = ld_cg_f4_early(xr + ch * 8);
-      p1 = ld_cg_f4_early(xr + ch * 8 + 4);
-    }
-    v[8 * u + 0] = p0.x; v[8 * u + 1] = p0.y; v[8 * u + 2] = p0.z; v[8 * u + 3] = p0.w;
-    v[8 * u + 4] = p1.x; v[8 * u + 5] = p1.y; v[8 * u + 6] = p1.z; v[8 * u + 7] = p1.w;
+    v[u] = r < a.R ? ld_cg_u4_early(xr + ch * 8) : make_uint4(0, 0, 0, 0);
   }
 }
 
 // Shifted sums of a half row: sum (x - c) and sum (x - c)^2 with c = x[r][0]
 // (the same shift in both halves keeps the one-pass variance well conditioned).
 template <int NCH>
-__device__ __forceinline__ void ln_half_sums(const float (&f)[NCH * 8], float c, float& s1, float& s2) {
+__device__ __forceinline__ void ln_half_sums(const uint4 (&x)[NCH], float c, float& s1, float& s2) {
   s1 = 0.f;
   s2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < NCH * 8; ++i) {
-    const float d = f[i] - c;
-    s1 += d;
-    s2 += d * d;
+  for (int u = 0; u < NCH; ++u) {
+    float f[8];
+    bf8_unpack(x[u], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = f[i] - c;
+      s1 += d;
+      s2 += d * d;
+    }
   }
 }
 
@@ -403,13 +415,15 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
   const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
   const int r0 = wid, r1 = wid + 11, r2 = wid + 22;
   const bool has2 = r2 < kFusedRows;
-  float xa[NCH * 8], xb[NCH * 8], xc[NCH * 8];
+  uint4 xa[NCH], xb[NCH], xc[NCH];  // the residual rows (bf16, packed), all loads in flight together
   ln_load_half<NCH>(a, r0, lane, half, xa);
   ln_load_half<NCH>(a, r1, lane, half, xb);
-  ln_load_half<NCH>(a, has2 ? r2 : r1, lane, half, xc);
-  const float ca = r0 < a.R ? __ldcg(a.x + static_cast<long long>(r0) * D) : 0.f;
-  const float cb = r1 < a.R ? __ldcg(a.x + static_cast<long long>(r1) * D) : 0.f;
-  const float cc = (has2 && r2 < a.R) ? __ldcg(a.x + static_cast<long long>(r2) * D) : 0.f;
+  ln_load_half<NCH>(a, has2 ? r2 : kFusedRows, lane, half, xc);
+  // the shift of the one-pass variance: a value common to both halves (the
+  // first element of the row)
+  const float ca = r0 < a.R ? bf2f(a.x[static_cast<long long>(r0) * D]) : 0.f;
+  const float cb = r1 < a.R ? bf2f(a.x[static_cast<long long>(r1) * D]) : 0.f;
+  const float cc = (has2 && r2 < a.R) ? bf2f(a.x[static_cast<long long>(r2) * D]) : 0.f;
   float s[6];
   ln_half_sums<NCH>(xa, ca, s[0], s[1]);
   ln_half_sums<NCH>(xb, cb, s[2], s[3]);
@@ -443,7 +457,7 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
   stats(cb, s[2] + pb.x, s[3] + pb.y, r1, rb, bb);
   stats(cc, s[4] + pc.x, s[5] + pc.y, has2 ? r2 : kFusedRows, rc, bc);
   if (mode == 0) {
-    // AdaLN: bf16(n) * bf16(1 + scale) + bf16(shift), one packed bf16 FMA per pair
+    // AdaLN: bf16(n) * bf16(1 + scale) + bf16(shift), packed bf16 pairs
     const uint4* cm = reinterpret_cast<const uint4*>(stg + kStgLnConst) + half * (DH / 8);
     const uint4* cadd = reinterpret_cast<const uint4*>(stg + kStgLnConst) + D / 8 + half * (DH / 8);
 #pragma unroll
@@ -451,18 +465,23 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
       const int ch = lane + 32 * u;  // chunk within this half: local K block ch >> 3
       const uint4 m4 = cm[ch], a4 = cadd[ch];
       const uint32_t mw[4] = {m4.x, m4.y, m4.z, m4.w}, aw[4] = {a4.x, a4.y, a4.z, a4.w};
+      float fa[8], fb[8], fc[8];
+      bf8_unpack(xa[u], fa);
+      bf8_unpack(xb[u], fb);
+      bf8_unpack(xc[u], fc);
       uint32_t oa[4], ob[4], oc[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const __nv_bfloat162 mv = *reinterpret_cast<const __nv_bfloat162*>(&mw[e]);
         const __nv_bfloat162 av = *reinterpret_cast<const __nv_bfloat162*>(&aw[e]);
-        const int i0 = u * 8 + 2 * e;
-        __nv_bfloat162 na = __floats2bfloat162_rn(fmaf(xa[i0], ra, ba), fmaf(xa[i0 + 1], ra, ba));
-        __nv_bfloat162 nb = __floats2bfloat162_rn(fmaf(xb[i0], rb, bb), fmaf(xb[i0 + 1], rb, bb));
-        __nv_bfloat162 nc = __floats2bfloat162_rn(fmaf(xc[i0], rc, bc), fmaf(xc[i0 + 1], rc, bc));
-        na = __hfma2(na, mv, av);
-        nb = __hfma2(nb, mv, av);
-        nc = __hfma2(nc, mv, av);
+        const int i0 = 2 * e;
+        __nv_bfloat162 na = __floats2bfloat162_rn(fmaf(fa[i0], ra, ba), fmaf(fa[i0 + 1], ra, ba));
+        __nv_bfloat162 nb = __floats2bfloat162_rn(fmaf(fb[i0], rb, bb), fmaf(fb[i0 + 1], rb, bb));
+        __nv_bfloat162 nc = __floats2bfloat162_rn(fmaf(fc[i0], rc, bc), fmaf(fc[i0 + 1], rc, bc));
+        // the reference's modulate on bf16 tensors: bf16(bf16(n * (1 + scale)) + shift)
+        na = __hadd2(__hmul2(na, mv), av);
+        nb = __hadd2(__hmul2(nb, mv), av);
+        nc = __hadd2(__hmul2(nc, mv), av);
         oa[e] = *reinterpret_cast<uint32_t*>(&na);
         ob[e] = *reinterpret_cast<uint32_t*>(&nb);
         oc[e] = *reinterpret_cast<uint32_t*>(&nc);
@@ -482,12 +501,16 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
       const float4 m0 = cm[2 * ch], m1 = cm[2 * ch + 1], a0 = cadd[2 * ch], a1 = cadd[2 * ch + 1];
       const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float fa[8], fb[8], fc[8];
+      bf8_unpack(xa[u], fa);
+      bf8_unpack(xb[u], fb);
+      bf8_unpack(xc[u], fc);
       float oa[8], ob[8], oc[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        oa[e] = fmaf(xa[u * 8 + e], ra, ba) * mv[e] + av[e];
-        ob[e] = fmaf(xb[u * 8 + e], rb, bb) * mv[e] + av[e];
-        oc[e] = fmaf(xc[u * 8 + e], rc, bc) * mv[e] + av[e];
+        oa[e] = fmaf(fa[e], ra, ba) * mv[e] + av[e];
+        ob[e] = fmaf(fb[e], rb, bb) * mv[e] + av[e];
+        oc[e] = fmaf(fc[e], rc, bc) * mv[e] + av[e];
       }
       stage_chunk(stg, ch >> 3, r0, ch & 7, r0 < a.R ? pack8(oa) : make_uint4(0, 0, 0, 0));
       stage_chunk(stg, ch >> 3, r1, ch & 7, r1 < a.R ? pack8(ob) : make_uint4(0, 0, 0, 0));
@@ -529,22 +552,22 @@ __device__ void stage_copy(const FusedArgs& a, uint8_t* stg, const __nv_bfloat16
 
 // ------------------------------------------------------------- epilogues
 // Per-feature constants of an epilogue, loaded before the accumulator wait so
-// their latency overlaps the MMA: bias, and the RMSNorm weight (qkv q/k,
-// cross-q) or the residual gate (o, ffn.2); plus the RoPE (cos, sin) of every
-// token for the q/k features.
+// their latency overlaps the MMA: bias, the RMSNorm weight (qkv q/k, cross-q)
+// or the residual gate (o, ffn.2); plus the RoPE (cos, sin) of every token for
+// the q/k features.
 // The epilogue runs on 8 warps: warps 2..5 take the tokens 0..15 and warps
 // 6..9 the tokens 16..31 of the TMEM lane quarter warp % 4 (one output
 // feature per lane), so two warps share every scheduler.
 constexpr int kEpiTokens = kFusedRows / 2;
 
 struct EpiConst {
-  float bias, mul;
+  float bias, mul, gate;
   const float2* rope;  // [16 tokens][16 pairs] of this warp's features (shared memory)
 };
 
 __device__ __forceinline__ void epi_load(const FusedArgs& a, uint8_t* stg, int p, int step, int l,
                                          const FItem& it, int f, int t0, EpiConst& c) {
-  const int D = a.D, HD = a.HD;
+  const int HD = a.HD;
   c.mul = 1.f;
   switch (p) {
     case kFQkv: {
@@ -572,10 +595,11 @@ __device__ __forceinline__ void epi_load(const FusedArgs& a, uint8_t* stg, int p
     case kFO:
     case kFCo:
     case kFFfn2: {
-      const __nv_bfloat16* bptr = p == kFO ? a.o_b : (p == kFCo ? a.co_b : a.ffn2_b);
-      if (p == kFO) c.mul = f_mod(a, step, l, 2, f);
-      if (p == kFFfn2) c.mul = f_mod(a, step, l, 5, f);
-      c.bias = it.sub == 0 ? bf2f(bptr[static_cast<long long>(l) * D + f]) : 0.f;
+      // the tile's last split item adds the bias to the sum of the split
+      // partials and applies the residual gate (o: gate_msa, ffn.2:
+      // gate_mlp; none for cross-o)
+      c.bias = 0.f;
+      c.gate = p == kFO ? f_mod(a, step, l, 2, f) : (p == kFFfn2 ? f_mod(a, step, l, 5, f) : 1.f);
       return;
     }
     case kFCq:
@@ -607,8 +631,8 @@ __device__ __forceinline__ float warp_transpose_sum16(float (&v)[16]) {
 }
 
 // Epilogue of one output feature f (this lane) for the tokens t0 .. t0 + 15.
-__device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int step, int l, int f, int t0,
-                                              const EpiConst& c, float (&v)[kEpiTokens]) {
+__device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int step, int l, const FItem& it, int f,
+                                              int t0, const EpiConst& c, float (&v)[kEpiTokens]) {
   const int lane = threadIdx.x & 31;
   const int R = a.R, D = a.D, HD = a.HD;
   switch (p) {
@@ -620,7 +644,7 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
           if (t0 + j < R) a.va[(t0 + j) * HD + ff] = f2bf(rbf(v[j] + c.bias));
         return;
       }
-      float* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + type) * kFusedRows;
+      double* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + type) * kFusedRows;
       __nv_bfloat16* dst = type == 0 ? a.q : a.ka;
 #pragma unroll
       for (int j = 0; j < kEpiTokens; ++j) {
@@ -633,18 +657,25 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
         if (t0 + j < R) dst[(t0 + j) * HD + ff] = f2bf(o);
       }
       const float mine = warp_transpose_sum16(v);  // lanes l, l ^ 16: token t0 + (l & 15)
-      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, mine);
+      // fp64: the sum of the fp32 warp partials is exact, whatever order they
+      // arrive in (the launch is deterministic)
+      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, static_cast<double>(mine));
       return;
     }
     case kFO:
     case kFCo:
-    case kFFfn2:
+    case kFFfn2: {
+      // this split item's partial tile -> its slot ([split][tile][token][128]
+      // fp32, one 128-byte row per warp and token); the last split item of
+      // the tile completes the residual add (residual_finalize)
+      float* slot = a.slots + ((static_cast<long long>(it.sub) * (D / 128) + it.n) * kFusedRows) * 128 + (f & 127);
 #pragma unroll
       for (int j = 0; j < kEpiTokens; ++j)
-        if (t0 + j < R) atomicAdd(a.x + (t0 + j) * D + f, c.mul * (v[j] + c.bias));
+        if (t0 + j < R) slot[(t0 + j) * 128] = v[j];
       return;
+    }
     case kFCq: {
-      float* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + 2) * kFusedRows;
+      double* ssq = a.ssq + ((static_cast<long long>(step) * a.L + l) * 3 + 2) * kFusedRows;
 #pragma unroll
       for (int j = 0; j < kEpiTokens; ++j) {
         const float y = rbf(v[j] + c.bias);
@@ -652,7 +683,7 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
         if (t0 + j < R) a.qc[(t0 + j) * HD + f] = f2bf(rbf(y * c.mul));
       }
       const float mine = warp_transpose_sum16(v);
-      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, mine);
+      if (lane < 16 && t0 + lane < R) atomicAdd(ssq + t0 + lane, static_cast<double>(mine));
       return;
     }
     default:  // ffn.0 + GELU(tanh)
@@ -660,6 +691,55 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
       for (int j = 0; j < kEpiTokens; ++j)
         if (t0 + j < R) a.fh[(t0 + j) * a.F + f] = f2bf(gelu_tanh(rbf(v[j] + c.bias)));
       return;
+  }
+}
+
+// Residual GEMMs (o, cross-o, ffn.2): after the 8 epilogue warps of a split
+// item have stored its partial tile, one thread publishes it (fence +
+// counter, as the attention split merge); the item that arrives last sums the
+// tile's split partials in split order (deterministic) plus the bias and
+// completes the residual add of the tile's 128 features as the reference's
+// bf16 tensors (mot.py:130-149): x = bf16(x + bf16(gate * bf16(o))).  It
+// resets the counter, which the same GEMM of the next block reuses.
+__device__ __forceinline__ void bar_epilogue() {
+  asm volatile("barrier.sync 2, 256;" ::: "memory");
+}
+__device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, int l, const FItem& it, int f,
+                                  int t0, float gate) {
+  bar_epilogue();
+  if (threadIdx.x == 64) {
+    const unsigned splits = static_cast<unsigned>(f_count(a, p) / (a.D / 128));
+    unsigned* ctr = a.tile_ctr + (p == kFO ? 0 : (p == kFCo ? 1 : 2)) * (kFusedMaxD / 128) + it.n;
+    __threadfence();
+    const bool last = atomicAdd(ctr, 1u) == splits - 1;
+    if (last) {
+      __threadfence();
+      *ctr = 0u;
+    }
+    tl->fin = last ? 1 : 0;
+  }
+  bar_epilogue();
+  if (!tl->fin) return;
+  const int splits = f_count(a, p) / (a.D / 128);
+  const __nv_bfloat16* bptr = p == kFO ? a.o_b : (p == kFCo ? a.co_b : a.ffn2_b);
+  const float bias = bf2f(bptr[static_cast<long long>(l) * a.D + f]);
+  const long long sstride = static_cast<long long>(a.D / 128) * kFusedRows * 128;  // floats per split
+  const float* slot = a.slots + static_cast<long long>(it.n) * kFusedRows * 128 + (f & 127);
+  float sum[kEpiTokens];
+#pragma unroll
+  for (int j = 0; j < kEpiTokens; ++j) sum[j] = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    float v[kEpiTokens];
+#pragma unroll
+    for (int j = 0; j < kEpiTokens; ++j) v[j] = t0 + j < a.R ? __ldcg(slot + sp * sstride + (t0 + j) * 128) : 0.f;
+#pragma unroll
+    for (int j = 0; j < kEpiTokens; ++j) sum[j] += v[j];
+  }
+#pragma unroll
+  for (int j = 0; j < kEpiTokens; ++j) {
+    if (t0 + j >= a.R) continue;
+    const long long idx = static_cast<long long>(t0 + j) * a.D + f;
+    a.x[idx] = f2bf(bf2f(a.x[idx]) + rbf(gate * rbf(sum[j] + bias)));
   }
 }
 
@@ -776,7 +856,8 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
         for (int jj = 0; jj < kEpiTokens; ++jj) v[jj] += xacc[(t0 + jj) * 64 + fl];
       }
     }
-    if (keep && ok && !tl->abort) gemm_epilogue(a, p, step, l, f, t0, c, v);
+    if (keep && ok && !tl->abort) gemm_epilogue(a, p, step, l, it, f, t0, c, v);
+    if (p == kFO || p == kFCo || p == kFFfn2) residual_finalize(a, tl, p, l, it, f, t0, c.gate);
     tc_fence_before();
   }
   ++items_done;
@@ -799,10 +880,10 @@ struct AttnItem {
   const __nv_bfloat16* v2;
   long long ts2;
   int S2;
-  const float* kscale2;     // [S2] sum of squares of the fresh keys (null: 1)
+  const double* kscale2;    // [S2] sum of squares of the fresh keys (null: 1)
   const __nv_bfloat16* qp;  // q rows: qp + r * qts (head offset applied)
   long long qts;
-  const float* qscale;      // [R] sum of squares of q rows (null: 1)
+  const double* qscale;     // [R] sum of squares of q rows (null: 1)
   const uint8_t* mask2d;    // [R, S1 + S2] (row stride mrs) or null
   long long mrs;
   const uint8_t* key_mask;  // [S1 + S2] or null
@@ -904,9 +985,9 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
   // per-row q scale and per-key scale of the fresh keys (RMSNorm as a scale)
   for (int i = threadIdx.x - 32; i < kFusedRows; i += kFusedWorkers) {
     tl->scale[0][i] = (t.qscale != nullptr && i < a.R)
-                          ? rsqrtf(__ldcg(t.qscale + i) / a.HD + a.eps) : 1.f;
+                          ? rsqrtf(static_cast<float>(__ldcg(t.qscale + i)) / a.HD + a.eps) : 1.f;
     tl->scale[1][i] = (t.kscale2 != nullptr && i < t.S2)
-                          ? rsqrtf(__ldcg(t.kscale2 + i) / a.HD + a.eps) : 1.f;
+                          ? rsqrtf(static_cast<float>(__ldcg(t.kscale2 + i)) / a.HD + a.eps) : 1.f;
   }
   cp_async_wait<0>();
   bar_workers();
@@ -1165,7 +1246,7 @@ __device__ __forceinline__ int attn_cross_first(const FusedArgs& a, int cta, int
 
 __device__ AttnItem joint_item(const FusedArgs& a, int step, int l, int i) {
   const int h = i / a.splits, sp = i % a.splits;
-  const float* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
+  const double* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
   AttnItem t;
   t.k1 = a.vk[l] + h * a.hd;
   t.v1 = a.vv[l] + h * a.hd;
@@ -1194,7 +1275,7 @@ __device__ AttnItem joint_item(const FusedArgs& a, int step, int l, int i) {
 }
 
 __device__ AttnItem cross_item(const FusedArgs& a, int step, int l, int h) {
-  const float* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
+  const double* ssq = a.ssq + (static_cast<long long>(step) * a.L + l) * 3 * kFusedRows;
   const __nv_bfloat16* kv = a.ckv + static_cast<long long>(l) * 2 * a.HD;  // [C][L][2HD]
   AttnItem t;
   t.k1 = kv + h * a.hd;
@@ -1302,7 +1383,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
           const int r = idx / D, f = idx % D;
           float acc = bf2f(a.enc_b[f]);
           for (int c = 0; c < a.A; ++c) acc += bf2f(a.enc_w[f * a.A + c]) * bf2f(__ldcg(a.latent + r * a.A + c));
-          a.x[idx] = rbf(acc);
+          a.x[idx] = f2bf(acc);
         }
         if (has_qkv) ln_const_prefetch(a, stg, step, 0, 0, 0);
         if (!grid_sync(a, epoch, tl)) break;
@@ -1349,25 +1430,28 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
       }
       if (tl->abort) break;
       // head + Euler update + the next step's action_encoder: one CTA per token
-      // row (row-local, no barrier between): warps take the velocity channels,
-      // one thread per channel updates the latent, every thread re-encodes
-      // features of the row.
+      // row (row-local, no barrier between).  The row goes to shared memory
+      // first; warps take the velocity channels, one thread per channel
+      // updates the latent, every thread re-encodes features of the row.
       for (int r = cta; r < R; r += G) {
         const int wi = warp - 1, wt = threadIdx.x - 32;
         float* svel = &tl->stat[0][0];
         float* slat = &tl->stat[kFusedRows / 2][0];
-        const float* xr = a.x + static_cast<long long>(r) * D;
+        __nv_bfloat16* xres = a.x + static_cast<long long>(r) * D;
+        float* xrow = reinterpret_cast<float*>(stg);
+        for (int f = wt; f < D; f += kFusedWorkers) xrow[f] = bf2f(__ldcg(xres + f));
+        bar_workers();
         for (int c = wi; c < a.A; c += 11) {
           float acc = 0.f;
 #pragma unroll 4
           for (int ch = lane; ch < D / 8; ch += 32) {
-            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(xr + ch * 8));
-            const float4 x1 = __ldcg(reinterpret_cast<const float4*>(xr + ch * 8 + 4));
+            const float4 x0 = *reinterpret_cast<const float4*>(xrow + ch * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(xrow + ch * 8 + 4);
             const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
             float wv[8];
             ld_bf8(a.head_w + static_cast<long long>(c) * D + ch * 8, wv);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc += rbf(xv[e]) * wv[e];
+            for (int e = 0; e < 8; ++e) acc += xv[e] * wv[e];
           }
           acc = warp_sum(acc);
           if (lane == 0) svel[c] = rbf(acc + bf2f(a.head_b[c]));
@@ -1387,9 +1471,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
           for (int f = wt; f < D; f += kFusedWorkers) {
             float acc = bf2f(a.enc_b[f]);
             for (int c = 0; c < a.A; ++c) acc += bf2f(a.enc_w[f * a.A + c]) * slat[c];
-            a.x[static_cast<long long>(r) * D + f] = rbf(acc);
+            xres[f] = f2bf(acc);
           }
         }
+        bar_workers();  // xrow (staging) is reused by the next row / the prefetch below
       }
       if (has_qkv && step + 1 < a.N) ln_const_prefetch(a, stg, step + 1, 0, 0, 0);
       if (!grid_sync(a, epoch, tl)) break;

@@ -11,6 +11,7 @@
 namespace fam {
 
 constexpr int kFusedMaxLayers = 32;
+constexpr int kFusedMaxD = 1024;     // hidden width bound of the fused path
 constexpr int kFusedRows = 32;        // token rows of one sample (MMA N, zero padded)
 constexpr int kFusedThreads = 384;    // warp 0 weight producer, warps 1..11 workers (clusters of 2 CTAs)
 constexpr int kFusedWorkers = 352;
@@ -38,10 +39,16 @@ struct FusedArgs {
   const __nv_bfloat16* ckv;          // [C, L, 2HD]: RMSNorm'd K then V per context token and block
   const uint8_t* ctx_mask;           // [C] or null
   int C;
-  // workspace
-  float* x;                          // [R, D]
+  // workspace.  The residual stream is bf16, as the reference's: each split
+  // item of a residual GEMM (o, cross-o, ffn.2) stores its fp32 partial tile
+  // in its own slot, and the last split item of each 128-feature tile
+  // (tile_ctr) sums them in split order (deterministic) and completes the
+  // tile's residual add x = bf16(x + bf16(gate * bf16(sum + bias))).
+  __nv_bfloat16* x;                  // [32, D]
+  float* slots;                      // [splits][D / 128][32][128] split partials
+  unsigned* tile_ctr;                // [3][kFusedMaxD / 128] split arrivals per residual GEMM tile
   __nv_bfloat16 *q, *ka, *va, *ao, *qc, *ci, *fh;
-  float* ssq;                        // [N][L][3][32] (zeroed per launch)
+  double* ssq;                       // [N][L][3][32] q / k / cross-q sums of squares (fp64: exact, order-free)
   float* apart;                      // [H][splits][32][hd + 2]
   unsigned* sync;                    // [0] barrier go word, [1] abort, [2..] merge counters [N][L][H]
   unsigned* flags;                   // per-CTA barrier arrival lines (32 words apart)

@@ -4,7 +4,8 @@
 // reduced with warp shuffles.
 //
 //   resid_norm   split-K reduction of the previous GEMM + bias + gated
-//                residual add (fp32 residual stream) + the next LayerNorm
+//                residual add (fp32 residual stream, or bf16 roundings as the
+//                reference's bf16 tensors) + the next LayerNorm
 //                (AdaLN with (1+scale)/shift, or affine norm3) -> bf16 operand
 //   qkv_post     split-K reduction of the fused QKV GEMM + bias, RMSNorm of q
 //                and k over the whole H*d row, RoPE from an fp32 cos/sin table,
@@ -153,8 +154,13 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
       float4 y = sum_splits4(a.partials, a.split_stride, a.nsplit, static_cast<long long>(row) * D + f);
       y = rbf4(f4add(y, cb[i]));  // the reference's Linear output is a bf16 tensor
       const float4 gt = cg[i];
-      xv = make_float4(xv.x + gt.x * y.x, xv.y + gt.y * y.y, xv.z + gt.z * y.z, xv.w + gt.w * y.w);
-      if (a.round_residual) xv = rbf4(xv);
+      if (a.round_residual) {
+        // bf16 residual stream: bf16(x + bf16(gate * y)), as the reference's bf16 tensors
+        const float4 gy = rbf4(make_float4(gt.x * y.x, gt.y * y.y, gt.z * y.z, gt.w * y.w));
+        xv = rbf4(make_float4(xv.x + gy.x, xv.y + gy.y, xv.z + gy.z, xv.w + gy.w));
+      } else {
+        xv = make_float4(xv.x + gt.x * y.x, xv.y + gt.y * y.y, xv.z + gt.z * y.z, xv.w + gt.w * y.w);
+      }
       *reinterpret_cast<float4*>(x + f) = xv;
     }
     v[i] = xv;
@@ -185,9 +191,11 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
     } else {  // AdaLN: LN(x) * (1 + scale) + shift
       const float4 sh = c0[i];
       const float4 sc = c1[i];
+      // modulate on bf16 tensors: bf16(bf16(n * bf16(1 + scale)) + shift)
       n = rbf4(n);
-      n = make_float4(n.x * (1.f + sc.x) + sh.x, n.y * (1.f + sc.y) + sh.y, n.z * (1.f + sc.z) + sh.z,
-                      n.w * (1.f + sc.w) + sh.w);
+      n = make_float4(rbf(n.x * rbf(1.f + sc.x)), rbf(n.y * rbf(1.f + sc.y)), rbf(n.z * rbf(1.f + sc.z)),
+                      rbf(n.w * rbf(1.f + sc.w)));
+      n = make_float4(n.x + sh.x, n.y + sh.y, n.z + sh.z, n.w + sh.w);
     }
     st_bf4(h + f, n);
   }
@@ -503,7 +511,7 @@ __global__ void __launch_bounds__(kRowThreads) encode_adaln_kernel(const EncodeA
   for (int f = threadIdx.x; f < D; f += blockDim.x) {
     const float shift = mod_value(a.mod, moff, 0, f, D);
     const float scale = mod_value(a.mod, moff, 1, f, D);
-    const float n = rbf((srow[f] - mean) * rstd) * (1.0f + scale) + shift;
+    const float n = rbf(rbf((srow[f] - mean) * rstd) * rbf(1.0f + scale)) + shift;
     a.h[static_cast<long long>(row) * D + f] = f2bf(n);
   }
 }

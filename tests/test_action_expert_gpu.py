@@ -1,11 +1,16 @@
 """Action expert (ActionDiT over a video K/V cache) through the C ABI vs the CPU oracle.
 
 Tolerances: per model evaluation, max|d| <= 2e-2 * max(1, max|ref|) and cosine >= 0.999
-against the fp32 oracle on the same bf16 weights.  For a whole multi-step chunk the
-reference's own bf16 arithmetic drifts from fp32 (measured 5.7e-2 max|d| at full BASELINE
-config 1 size), so the chunk gate is cosine >= 0.999 and max|d| within 2 x the oracle's
-bf16-vs-fp32 disagreement on the same inputs (the calibration rule of the reference's
-numerics oracle, geak/task/scripts/episode_oracle.py:145-199), and never above 0.1.
+against the fp32 oracle on the same bf16 weights.  Whole chunks at the BASELINE config-1
+size are held to the north-star gate against the reference's own bf16 arithmetic (the
+oracle run in bf16, which reproduces the reference bit for bit): cosine >= 0.999 and
+max|d| <= 2e-2, or at most the reference's own bf16-vs-bf16 floor where that is larger.
+The floor is measured in the test: the bf16 reference with only the summation order of
+its Linear layers changed (K summed in 2 or 4 fp32 pieces) against itself.  At this
+size (280 sequential evaluations, outputs up to ~3.5 where a bf16 ulp is 0.0156) that
+floor is 1-2 bf16 ulps, so 2e-2 alone is a coin flip for any correct bf16
+implementation that does not reproduce the CPU's exact summation order.  The distance
+to the fp32 oracle is printed beside it.
 """
 import importlib
 
@@ -120,28 +125,91 @@ def test_fused_kernel_matches_chain_and_oracle(Sa, Sv, C, tpf):
     assert trace.shape == (3, 1, Sa, 7)
 
 
-def test_full_config1_chunk():
-    """BASELINE config 1 at full size: 1024 hidden, 16x64 heads, 28 blocks, 1760-token cache,
-    10 steps, batch 1."""
+def _config1(B, seed=7):
     D, H, hd, F, T, L = 1024, 16, 64, 4096, 4096, 28
-    dit, sd, cfg = _build(D=D, H=H, hd=hd, F=F, T=T, L=L, seed=7)
-    B, Sa, Sv, C = 1, 32, 1760, 64
+    dit, sd, cfg = _build(D=D, H=H, hd=hd, F=F, T=T, L=L, seed=seed)
+    Sa, Sv, C = 32, 1760, 64
     ctx, cm, ck, cv, noise, _ = _inputs(B, Sa, Sv, C, T, D, L, 1760)
     cm[:] = True
     mask = torch.ones(Sa, Sv + Sa, dtype=torch.bool)  # BASELINE config 1: all-True joint mask
-    ts, ds = M.build_inference_schedule(10, 1.0)
-    torch.set_num_threads(max(1, torch.get_num_threads()))
-    ck32, cv32 = [k.float() for k in ck], [v.float() for v in cv]
-    ref32 = O.action_chunk_with_cache(sd, cfg, noise.float(), ctx.float(), cm, ck32, cv32, mask, 10, 1.0)
+    return dit, sd, cfg, (noise, ctx, cm, ck, cv, mask)
+
+
+def _linear_k_pieces(pieces):
+    """The oracle's Linear with its K dimension summed in `pieces` fp32 parts: the same
+    bf16 arithmetic in another summation order."""
+    def lin(p, name, x):
+        w, b = p[name + ".weight"], p.get(name + ".bias")
+        step = (w.shape[1] + pieces - 1) // pieces
+        acc = None
+        for k0 in range(0, w.shape[1], step):
+            part = x[..., k0:k0 + step].float() @ w[:, k0:k0 + step].float().t()
+            acc = part if acc is None else acc + part
+        return (acc if b is None else acc + b.float()).to(x.dtype)
+    return lin
+
+
+def _config1_refs(sd, cfg, inputs):
+    """fp32 oracle, bf16 reference, and the reference's bf16-vs-bf16 floor."""
+    noise, ctx, cm, ck, cv, mask = inputs
+    ref32 = O.action_chunk_with_cache(sd, cfg, noise.float(), ctx.float(), cm, [k.float() for k in ck],
+                                      [v.float() for v in cv], mask, 10, 1.0)
     sd16 = {k: v.bfloat16() for k, v in sd.items()}
     ref16 = O.action_chunk_with_cache(sd16, cfg, noise, ctx, cm, ck, cv, mask, 10, 1.0).float()
-    floor = (ref16 - ref32).abs().max().item()
-    got = dit.engine().chunk(noise.cuda(), ts, ds, ctx.cuda(), cm.cuda(), [k.cuda() for k in ck],
-                             [v.cuda() for v in cv], mask.cuda()).cpu().float()
+    floor16 = 0.0
+    linear = O.linear
+    try:
+        for pieces in (2, 4):
+            O.linear = _linear_k_pieces(pieces)
+            alt = O.action_chunk_with_cache(sd16, cfg, noise, ctx, cm, ck, cv, mask, 10, 1.0).float()
+            floor16 = max(floor16, (alt - ref16).abs().max().item())
+    finally:
+        O.linear = linear
+    return ref32, ref16, floor16
+
+
+def _config1_check(name, got, ref32, ref16, floor16):
     err32 = (got - ref32).abs().max().item()
-    err16 = (got - ref16).abs().max().item()
-    print(f"config1 chunk: max|gpu-fp32|={err32:.4f} max|gpu-bf16ref|={err16:.4f} "
-          f"bf16-vs-fp32 floor={floor:.4f} cos={_cos(got, ref32):.6f}")
-    assert _cos(got, ref32) >= 0.999 and _cos(got, ref16) >= 0.999
-    assert err32 <= min(0.1, max(2e-2, 2 * floor))
-    assert err16 <= min(0.1, max(2e-2, 2 * floor))
+    d16 = (got - ref16).abs()
+    err16 = d16.max().item()
+    c32, c16 = _cos(got, ref32), _cos(got, ref16)
+    print(f"PARITY {name}: max|d| vs bf16 reference {err16:.4f} (cos {c16:.6f}, "
+          f"{int((d16 > 2e-2).sum())} of {d16.numel()} beyond 2e-2); reference bf16-vs-bf16 floor "
+          f"{floor16:.4f}; vs fp32 oracle {err32:.4f} (cos {c32:.6f}); max|ref| {ref16.abs().max():.3f}")
+    assert err16 <= max(2e-2, floor16) and c16 >= 0.999, f"{name}: {err16} / {c16}"
+    assert c32 >= 0.999
+
+
+def test_full_config1_chunk():
+    """BASELINE config 1 at full size: 1024 hidden, 16x64 heads, 28 blocks, 1760-token cache,
+    10 steps, batch 1, on the fused persistent kernel (twice: a launch is deterministic)
+    and on the launch chain."""
+    dit, sd, cfg, inputs = _config1(1)
+    ref32, ref16, floor16 = _config1_refs(sd, cfg, inputs)
+    noise, ctx, cm, ck, cv, mask = inputs
+    ts, ds = M.build_inference_schedule(10, 1.0)
+    eng = dit.engine()
+    args = (noise.cuda(), ts, ds, ctx.cuda(), cm.cuda(), [k.cuda() for k in ck], [v.cuda() for v in cv],
+            mask.cuda())
+    for mode in ("fused", "chain"):
+        eng.set_mode(mode)
+        got = eng.chunk(*args).cpu().float()
+        assert eng.last_path() == mode
+        _config1_check(f"config1 B=1 {mode}", got, ref32, ref16, floor16)
+        if mode == "fused":
+            again = eng.chunk(*args, use_graph=False).cpu().float()
+            assert torch.equal(got, again), "fused chunk is not deterministic"
+    eng.set_mode("auto")
+
+
+def test_full_config1_chunk_batch8():
+    """BASELINE config 1 at batch 8 (the launch chain: per-step weights shared by 8 samples)."""
+    dit, sd, cfg, inputs = _config1(8, seed=8)
+    ref32, ref16, floor16 = _config1_refs(sd, cfg, inputs)
+    noise, ctx, cm, ck, cv, mask = inputs
+    ts, ds = M.build_inference_schedule(10, 1.0)
+    eng = dit.engine()
+    got = eng.chunk(noise.cuda(), ts, ds, ctx.cuda(), cm.cuda(), [k.cuda() for k in ck],
+                    [v.cuda() for v in cv], mask.cuda()).cpu().float()
+    assert eng.last_path() == "chain"
+    _config1_check("config1 B=8 chain", got, ref32, ref16, floor16)
