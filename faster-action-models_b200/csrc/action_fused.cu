@@ -561,7 +561,7 @@ __device__ void stage_copy(const FusedArgs& a, uint8_t* stg, const __nv_bfloat16
 constexpr int kEpiTokens = kFusedRows / 2;
 
 struct EpiConst {
-  float bias, mul, gate;
+  float bias, mul;
   const float2* rope;  // [16 tokens][16 pairs] of this warp's features (shared memory)
 };
 
@@ -596,10 +596,8 @@ __device__ __forceinline__ void epi_load(const FusedArgs& a, uint8_t* stg, int p
     case kFCo:
     case kFFfn2: {
       // the tile's last split item adds the bias to the sum of the split
-      // partials and applies the residual gate (o: gate_msa, ffn.2:
-      // gate_mlp; none for cross-o)
+      // partials and applies the residual gate (residual_finalize)
       c.bias = 0.f;
-      c.gate = p == kFO ? f_mod(a, step, l, 2, f) : (p == kFFfn2 ? f_mod(a, step, l, 5, f) : 1.f);
       return;
     }
     case kFCq:
@@ -695,51 +693,79 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
 }
 
 // Residual GEMMs (o, cross-o, ffn.2): after the 8 epilogue warps of a split
-// item have stored its partial tile, one thread publishes it (fence +
-// counter, as the attention split merge); the item that arrives last sums the
-// tile's split partials in split order (deterministic) plus the bias and
-// completes the residual add of the tile's 128 features as the reference's
-// bf16 tensors (mot.py:130-149): x = bf16(x + bf16(gate * bf16(o))).  It
-// resets the counter, which the same GEMM of the next block reuses.
+// item have stored its partial tile, one thread publishes it (release
+// increment of the tile's counter, cumulative over the CTA's stores through
+// the barrier) and waits (bounded) until every split item of the tile has;
+// the counters only grow within a launch (target = splits x uses so far).
+// Then each split item completes its share of the tile's tokens: the split
+// partials summed in split order (deterministic) plus the bias, and the
+// residual add as the reference's bf16 tensors (mot.py:130-149):
+// x = bf16(x + bf16(gate * bf16(o))).
 __device__ __forceinline__ void bar_epilogue() {
   asm volatile("barrier.sync 2, 256;" ::: "memory");
 }
-__device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, int l, const FItem& it, int f,
-                                  int t0, float gate) {
+constexpr int kFinMaxSplits = 8;  // split partials held in flight per thread
+__device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, int step, int l, const FItem& it) {
+  const int splits = f_count(a, p) / (a.D / 128);
   bar_epilogue();
   if (threadIdx.x == 64) {
-    const unsigned splits = static_cast<unsigned>(f_count(a, p) / (a.D / 128));
     unsigned* ctr = a.tile_ctr + (p == kFO ? 0 : (p == kFCo ? 1 : 2)) * (kFusedMaxD / 128) + it.n;
-    __threadfence();
-    const bool last = atomicAdd(ctr, 1u) == splits - 1;
-    if (last) {
-      __threadfence();
-      *ctr = 0u;
-    }
-    tl->fin = last ? 1 : 0;
+    red_release_add(ctr, 1u);
+    const unsigned target = static_cast<unsigned>(splits) * static_cast<unsigned>(step * a.L + l + 1);
+    tl->fin = poll_ge(a, ctr, target, tl) ? 1 : 0;
   }
   bar_epilogue();
   if (!tl->fin) return;
-  const int splits = f_count(a, p) / (a.D / 128);
-  const __nv_bfloat16* bptr = p == kFO ? a.o_b : (p == kFCo ? a.co_b : a.ffn2_b);
-  const float bias = bf2f(bptr[static_cast<long long>(l) * a.D + f]);
+  // this item's tokens, 4 consecutive features per thread and step
+  const int tb = it.sub * kFusedRows / splits, te = min(a.R, (it.sub + 1) * kFusedRows / splits);
   const long long sstride = static_cast<long long>(a.D / 128) * kFusedRows * 128;  // floats per split
-  const float* slot = a.slots + static_cast<long long>(it.n) * kFusedRows * 128 + (f & 127);
-  float sum[kEpiTokens];
+  const __nv_bfloat16* bptr = (p == kFO ? a.o_b : (p == kFCo ? a.co_b : a.ffn2_b)) + static_cast<long long>(l) * a.D;
+  const int cg = p == kFO ? 2 : 5;  // gate_msa (o) / gate_mlp (ffn.2); cross-o has no gate
+  for (int idx = threadIdx.x - 64; idx < (te - tb) * 32; idx += 256) {
+    const int tok = tb + (idx >> 5), fl = (idx & 31) * 4, f0 = it.n * 128 + fl;
+    const long long xoff = static_cast<long long>(tok) * a.D + f0;
+    const float* slot = a.slots + (static_cast<long long>(it.n) * kFusedRows + tok) * 128 + fl;
+    // every load in flight before the first use
+    const uint2 xr = __ldcg(reinterpret_cast<const uint2*>(a.x + xoff));
+    float4 part[kFinMaxSplits];
 #pragma unroll
-  for (int j = 0; j < kEpiTokens; ++j) sum[j] = 0.f;
-  for (int sp = 0; sp < splits; ++sp) {
-    float v[kEpiTokens];
+    for (int sp = 0; sp < kFinMaxSplits; ++sp)
+      part[sp] = sp < splits ? __ldcg(reinterpret_cast<const float4*>(slot + sp * sstride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = kFinMaxSplits; sp < splits; ++sp) {  // more splits than held in flight (F > 4096)
+      const float4 q = __ldcg(reinterpret_cast<const float4*>(slot + sp * sstride));
+      part[kFinMaxSplits - 1] = make_float4(part[kFinMaxSplits - 1].x + q.x, part[kFinMaxSplits - 1].y + q.y,
+                                            part[kFinMaxSplits - 1].z + q.z, part[kFinMaxSplits - 1].w + q.w);
+    }
+    const uint2 br = *reinterpret_cast<const uint2*>(bptr + f0);
+    float g[4] = {1.f, 1.f, 1.f, 1.f};
+    if (p != kFCo) {
+      const float4 tm = *reinterpret_cast<const float4*>(a.tmod + static_cast<long long>(step) * 6 * a.D + cg * a.D + f0);
+      const uint2 mr = *reinterpret_cast<const uint2*>(a.modulation + (static_cast<long long>(l) * 6 + cg) * a.D + f0);
+      const float tv[4] = {tm.x, tm.y, tm.z, tm.w};
+      const __nv_bfloat162 m0 = *reinterpret_cast<const __nv_bfloat162*>(&mr.x);
+      const __nv_bfloat162 m1 = *reinterpret_cast<const __nv_bfloat162*>(&mr.y);
+      const float mv[4] = {__low2float(m0), __high2float(m0), __low2float(m1), __high2float(m1)};
 #pragma unroll
-    for (int j = 0; j < kEpiTokens; ++j) v[j] = t0 + j < a.R ? __ldcg(slot + sp * sstride + (t0 + j) * 128) : 0.f;
+      for (int e = 0; e < 4; ++e) g[e] = rbf(rbf(tv[e]) + mv[e]);
+    }
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < kEpiTokens; ++j) sum[j] += v[j];
-  }
+    for (int sp = 0; sp < kFinMaxSplits; ++sp) {  // split order
+      sum[0] += part[sp].x;
+      sum[1] += part[sp].y;
+      sum[2] += part[sp].z;
+      sum[3] += part[sp].w;
+    }
+    const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162*>(&xr.x);
+    const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162*>(&xr.y);
+    const __nv_bfloat162 b0 = *reinterpret_cast<const __nv_bfloat162*>(&br.x);
+    const __nv_bfloat162 b1 = *reinterpret_cast<const __nv_bfloat162*>(&br.y);
+    const float xv[4] = {__low2float(x0), __high2float(x0), __low2float(x1), __high2float(x1)};
+    const float bv[4] = {__low2float(b0), __high2float(b0), __low2float(b1), __high2float(b1)};
+    float o[4];
 #pragma unroll
-  for (int j = 0; j < kEpiTokens; ++j) {
-    if (t0 + j >= a.R) continue;
-    const long long idx = static_cast<long long>(t0 + j) * a.D + f;
-    a.x[idx] = f2bf(bf2f(a.x[idx]) + rbf(gate * rbf(sum[j] + bias)));
+    for (int e = 0; e < 4; ++e) o[e] = xv[e] + rbf(g[e] * rbf(sum[e] + bv[e]));
+    *reinterpret_cast<uint2*>(a.x + xoff) = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
   }
 }
 
@@ -857,7 +883,7 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
       }
     }
     if (keep && ok && !tl->abort) gemm_epilogue(a, p, step, l, it, f, t0, c, v);
-    if (p == kFO || p == kFCo || p == kFFfn2) residual_finalize(a, tl, p, l, it, f, t0, c.gate);
+    if (p == kFO || p == kFCo || p == kFFfn2) residual_finalize(a, tl, p, step, l, it);
     tc_fence_before();
   }
   ++items_done;
