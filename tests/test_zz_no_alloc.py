@@ -33,6 +33,15 @@ def _case(B, seed):
     return q, k1, v1, H, k2, v2, mask
 
 
+def _sdpa_fp32(q, k1, v1, H, k2, v2, mask):
+    B, Sq, HD = q.shape
+    k = torch.cat([k1, k2], 1).float().view(B, -1, H, HD // H).transpose(1, 2)
+    v = torch.cat([v1, v2], 1).float().view(B, -1, H, HD // H).transpose(1, 2)
+    qh = q.float().view(B, Sq, H, HD // H).transpose(1, 2)
+    o = torch.nn.functional.scaled_dot_product_attention(qh, k, v, attn_mask=mask.bool())
+    return o.transpose(1, 2).reshape(B, Sq, HD)
+
+
 def test_static_scratch_matches_workspace_entry_point_twice():
     lib = _lib.lib()
     for call, seed in ((0, 11), (1, 12)):
@@ -48,6 +57,12 @@ def test_static_scratch_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         err = (out.float() - ref.float()).abs().max().item()
         assert err <= 2e-2, f"call {call}: max|d| {err}"
+        # and against plain fp32 attention of the same inputs (masked SDPA over the
+        # concatenated keys), independent of the library's own kernels
+        sd = _sdpa_fp32(q, k1, v1, H, k2, v2, mask)
+        err_sd = (out.float() - sd).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(out.float().flatten(), sd.flatten(), dim=0).item()
+        assert err_sd <= 2e-2 and cos >= 0.999, f"call {call}: vs fp32 SDPA max|d| {err_sd} cos {cos}"
 
 
 def test_static_scratch_rejects_oversized_problem():
