@@ -331,7 +331,8 @@ def make_vae(R):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the reference project checkout (holds FastWAM/src)")
     ap.add_argument("--only", nargs="*", default=None, help="fixture names to (re)generate")
     args = ap.parse_args()
     R = _import_reference(Path(args.reference))
