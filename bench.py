@@ -650,6 +650,8 @@ def run_case(case: str, reps: int) -> None:
     """Fixed single-GPU workloads of the library's kernels, for profilers: each runs its
     library call `reps` times on cuda:0 and synchronizes (under ncu, skip the warm-up
     launches with -s).
+      gemm_ffn0_c4      the headline roofline's kernel: backbone ffn.0 at the config-4 micro-batch
+                        ([28160, 3072] x [14336, 3072]^T, GELU, CTA pairs, automatic split round)
       gemm_qkv_c2       ops.gemm [1760, 3072] x [9216, 3072]^T + bias (backbone qkv)
       gemm_qkv_pair_c2  the same on CTA pairs, as the prefill runs it
       attn_c2           ops.attention: 1760 tokens, 24 x 128 heads, first-frame-causal (352)
@@ -663,7 +665,15 @@ def run_case(case: str, reps: int) -> None:
     M = importlib.import_module("faster-action-models_b200.models")
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
-    if case in ("gemm_qkv_c2", "gemm_qkv_pair_c2"):
+    if case == "gemm_ffn0_c4":
+        M_ = MICRO_BATCH * 1760
+        h = torch.randn(M_, 3072, device=dev).bfloat16()
+        w = (torch.randn(14336, 3072, device=dev) * 0.02).bfloat16()
+        b = torch.randn(14336, device=dev).bfloat16()
+        out = torch.empty(M_, 14336, device=dev, dtype=torch.bfloat16)
+        for _ in range(reps):
+            ops.gemm(h, w, bias=b, act="gelu_tanh", out=out, pair=True, tile_n=256, split_round="auto")
+    elif case in ("gemm_qkv_c2", "gemm_qkv_pair_c2"):
         a = torch.randn(1760, 3072, device=dev).bfloat16()
         w = (torch.randn(9216, 3072, device=dev) * 0.02).bfloat16()
         b = torch.randn(9216, device=dev).bfloat16()
