@@ -75,6 +75,11 @@ struct GemmArgs {
   int taps;                 // 1: plain GEMM
   int tap_wp;
   int tap_kpt;
+  // Tile raster of the persistent kernels: M-blocks fastest inside bands of
+  // band_m M-blocks, the bands one after another (0 or >= the M-blocks: one
+  // band).  A band's A rows stay in L2 while the weight n-blocks stream past
+  // them once per band instead of once per wave.
+  int band_m;
 };
 
 struct GemmPlan {

@@ -473,6 +473,15 @@ __device__ __forceinline__ void gemm_tile_epilogue(const GemmArgs& args, uint32_
   }
 }
 
+// (M-block, N-block) of persistent tile `tile` (GemmArgs::band_m).
+__device__ __forceinline__ int2 tile_mn(int tile, int tiles_m, int tiles_n, int band) {
+  if (band <= 0 || band >= tiles_m) return make_int2(tile % tiles_m, tile / tiles_m);
+  const int per_band = band * tiles_n;
+  const int b = tile / per_band, r = tile - b * per_band;
+  const int bm = min(band, tiles_m - b * band);
+  return make_int2(b * band + r % bm, r / bm);
+}
+
 // Segments of a persistent CTA: whole tiles blockIdx.x + i * gridDim.x; with a
 // split last round, sk_full whole rounds and then piece (blockIdx.x % P) of
 // remaining tile (blockIdx.x / P) (piece = -1 for a whole tile).
@@ -540,8 +549,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tiles_m = (args.M + kBM - 1) / kBM;
-  const int ntiles = tiles_m * ((args.N + BN - 1) / BN);
+  const int tiles_m = (args.M + kBM - 1) / kBM, tiles_n = (args.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n;
   const int nkb = (args.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -579,7 +588,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       sg.init(args, ntiles, nkb);
       int tile = 0, kb0 = 0, kb1 = 0, piece = -1;
       bool have = sg.next(tile, kb0, kb1, piece);
-      int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
+      int2 tmn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+      int m0 = tmn.x * kBM, n0 = tmn.y * BN;
       const int pre = have ? min(kb1 - kb0, STAGES) : 0;
       for (int i = 0; i < pre; ++i) {
         int ax, ay;
@@ -601,8 +611,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       if (have && kb == kb1) {
         have = sg.next(tile, kb0, kb1, piece);
         kb = kb0;
-        m0 = (tile % tiles_m) * kBM;
-        n0 = (tile / tiles_m) * BN;
+        tmn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+        m0 = tmn.x * kBM;
+        n0 = tmn.y * BN;
       }
       for (int it = pre; have; ++it) {
         const int s = it % STAGES;
@@ -621,8 +632,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         if (++kb == kb1) {
           have = sg.next(tile, kb0, kb1, piece);
           kb = kb0;
-          m0 = (tile % tiles_m) * kBM;
-          n0 = (tile / tiles_m) * BN;
+          tmn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+          m0 = tmn.x * kBM;
+          n0 = tmn.y * BN;
         }
       }
       // every issued copy has landed before the CTA can exit
@@ -683,7 +695,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       const int buf = lt & 1;
       if (args.epi.vec && args.epi.kind == kEpiResidual && piece <= 0 && wq == 0) {
         // pull this row's residual segment into L2 while the tile's main loop runs
-        const int prow = (tile % tiles_m) * kBM + sp * 32 + lane, col = (tile / tiles_m) * BN;
+        const int2 pmn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+        const int prow = pmn.x * kBM + sp * 32 + lane, col = pmn.y * BN;
         const int row = prow < args.M ? gemm_out_row(args.epi, prow) : -1;
         const int ncols = min(BN, args.N - col);
         if (row >= 0 && ncols > 0)
@@ -694,7 +707,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       tc_fence_after();
       if (!ok) *abort_flag = 1;
       if (*abort_flag) break;
-      const int m0 = (tile % tiles_m) * kBM, n0 = (tile / tiles_m) * BN;
+      const int2 emn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+      const int m0 = emn.x * kBM, n0 = emn.y * BN;
       const uint32_t tacc = tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16);
       const int r = sp * 32 + lane;  // row inside the tile
       if (piece > 0) {
@@ -793,8 +807,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int tiles_m = (args.M + 2 * kBM - 1) / (2 * kBM);
-  const int ntiles = tiles_m * ((args.N + BN - 1) / BN);
+  const int tiles_m = (args.M + 2 * kBM - 1) / (2 * kBM), tiles_n = (args.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n;
   const int nkb = (args.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -829,8 +843,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
       // weights) for the first stages before the wait on the previous launch
       int pre = 0;
       if (pair < ntiles) {
-        const int m0 = (pair % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = (pair / tiles_m) * BN + static_cast<int>(rank) * (BN / 2);
+        const int2 fmn = tile_mn(pair, tiles_m, tiles_n, args.band_m);
+        const int m0 = fmn.x * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = fmn.y * BN + static_cast<int>(rank) * (BN / 2);
         pre = min(nkb, STAGES);
         for (int i = 0; i < pre; ++i) {
           uint8_t* sa = smem + i * STAGE_BYTES;
@@ -851,8 +866,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
       }
       int it = 0;
       for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
-        const int m0 = (tile % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = (tile / tiles_m) * BN + static_cast<int>(rank) * (BN / 2);
+        const int2 tmn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+        const int m0 = tmn.x * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = tmn.y * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           if (it < pre) continue;  // issued above
           const int s = it % STAGES;
@@ -924,8 +940,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistThreads, 1)
       tc_fence_after();
       if (!ok) *abort_flag = 1;
       if (*abort_flag) break;
-      const int m0 = (tile % tiles_m) * 2 * kBM + static_cast<int>(rank) * kBM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int2 emn = tile_mn(tile, tiles_m, tiles_n, args.band_m);
+      const int m0 = emn.x * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int n0 = emn.y * BN;
       const uint32_t tacc = tmem_base + buf * ACC_COLS + (static_cast<uint32_t>(sp * 32) << 16);
       const int r = sp * 32 + lane;
       gemm_tile_epilogue<BN>(args, tacc, r, m0 + r, n0, c0, cs, nullptr, 0);
@@ -1190,6 +1207,12 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
                            static_cast<uint64_t>(ldb), static_cast<uint32_t>(kPairBN / 2)))
       return set_error("gemm: cuTensorMapEncodeTiled failed for the pair B half tile");
     p->pair = std::min(pt, gemm_num_sms() / 2);
+  }
+  // raster bands of ~24 MB of A rows (see GemmArgs::band_m)
+  {
+    const long long rows = p->pair > 0 ? 2 * kBM : kBM;
+    const long long block_bytes = rows * static_cast<long long>(K) * 2;
+    p->args.band_m = static_cast<int>(std::max(1LL, (24LL << 20) / block_bytes));
   }
   if (sk && p->persist > 0) {
     p->args.sk_full = sk_full;
