@@ -18,9 +18,17 @@
 //   * Nothing is allocated: no cudaMalloc, cudaFree or allocating library
 //     routine is called.  The arrival counters are cleared with
 //     cudaMemsetAsync on the caller's stream at every call.
-//   * Set-up: the first call on each device (with that device current)
-//     looks up the array's device address with cudaGetSymbolAddress.  Make
-//     that first call before any stream capture on the device.
+//   * Set-up: every call made while its stream is not capturing looks up the
+//     array's device address (cudaGetSymbolAddress, with the call's device
+//     current), so a context that was reset and reloaded is picked up; a
+//     call inside a stream capture reuses the address of the last such call
+//     on that device, so make one call on each device before any capture.
+//     Under CUDA's lazy module loading (the default) that first call also
+//     loads the library's device image, this array included: make it at
+//     start-up, before the part of the program that must not allocate.
+//   * Kernel: the split-KV mma.sync attention of fam_attention.  The tcgen05
+//     long-self-attention kernel that fam_attention picks for one key source
+//     of head_dim 128 needs a transposed-V workspace, so it is not used here.
 //   * Every call on a device shares the one array and leaves its contents
 //     behind.  Calls that may overlap on the GPU (different streams, or
 //     concurrent graphs) race on it: serialize them.
@@ -41,21 +49,29 @@ static constexpr int kMaxDev = 64;
 static void* g_scratch_addr[kMaxDev] = {nullptr};
 static std::mutex g_scratch_mu;
 
-// Device address of g_attention_scratch on the current device (set up once
-// per device).  The host-side symbol itself is only a stand-in and must never
-// be passed to a kernel.
-static int static_scratch(void** out) {
+// Device address of g_attention_scratch on the current device.  The host-side
+// symbol itself is only a stand-in and must never be passed to a kernel.  It is
+// looked up again on every call outside a stream capture (cheap), so that a
+// context reset that reloaded the module is followed; inside a capture the
+// last looked-up address of the device is used.
+static int static_scratch(cudaStream_t st, void** out) {
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "attention_static_scratch: cudaGetDevice");
   if (rc) return rc;
   if (dev < 0 || dev >= kMaxDev) return set_error("attention_static_scratch: device %d out of range", dev);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  rc = check_cuda(cudaStreamIsCapturing(st, &cap), "attention_static_scratch: cudaStreamIsCapturing");
+  if (rc) return rc;
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  if (cap == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     rc = check_cuda(cudaGetSymbolAddress(&p, g_attention_scratch),
                     "attention_static_scratch: cudaGetSymbolAddress");
     if (rc) return rc;
     g_scratch_addr[dev] = p;
+  } else if (g_scratch_addr[dev] == nullptr) {
+    return set_error("attention_static_scratch: the first call on device %d must come before any stream "
+                     "capture (it looks up the static scratch)", dev);
   }
   *out = g_scratch_addr[dev];
   return 0;
@@ -78,7 +94,7 @@ extern "C" int fam_attention_static_scratch(const fam_attention_desc* d, void* s
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a.nsplit > 1) {
     void* scratch = nullptr;
-    rc = static_scratch(&scratch);
+    rc = static_scratch(st, &scratch);
     if (rc) return rc;
     rc = check_cuda(attention_bind_scratch(&a, s, scratch, st), "attention_static_scratch counters");
     if (rc) return rc;

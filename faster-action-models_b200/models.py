@@ -94,6 +94,50 @@ def rope_table(head_dim: int, positions: int = 1024, theta: float = 10000.0) -> 
     return torch.stack([ang.cos(), ang.sin()], dim=-1).float().contiguous()
 
 
+class PreparedVideo:
+    """The token stage of WanVideoDiT.prepare (wan_video_dit.py:640-720) as this library
+    runs it: patch embedding, the per-token time MLPs and the text embedding are fused
+    into the prefill kernels, so prepare() hands the prefill its inputs (the latent grid,
+    per-sample timesteps, the raw context) in this record.  It stands in the reference's
+    `tokens` / `t` / `t_mod` slots; `.shape` is the token tensor's [B, S, D]."""
+
+    def __init__(self, latents, timestep, context, context_mask, grid, hidden_dim):
+        self.latents, self.timestep = latents, timestep
+        self.context, self.context_mask = context, context_mask
+        self.grid = grid
+        self.shape = torch.Size((latents.shape[0], grid[0] * grid[1] * grid[2], hidden_dim))
+
+
+class PreparedAction:
+    """The token stage of ActionDiT.prepare (action_dit.py:312-327): the action encoder,
+    the time MLP and the text embedding run inside the action-expert kernels, so
+    prepare() hands them the noisy latents, the timestep (a host value) and the raw
+    context.  `.shape` is the token tensor's [B, Sa, D]."""
+
+    def __init__(self, latents, timestep, context, context_mask, hidden_dim):
+        self.latents, self.timestep = latents, timestep
+        self.context, self.context_mask = context, context_mask
+        self.shape = torch.Size((latents.shape[0], latents.shape[1], hidden_dim))
+
+
+class ActionStepOut:
+    """MoT.forward_action_with_video_cache_tensor's output as this library runs it: the
+    step kernels end with the head (ActionDiT.post), so the record carries the velocity."""
+
+    def __init__(self, velocity):
+        self.velocity = velocity
+        self.shape = velocity.shape
+
+
+def _host_timestep(timestep):
+    """A timestep as host floats (a tensor on the GPU is read back once)."""
+    if torch.is_tensor(timestep):
+        return [float(x) for x in timestep.reshape(-1).float().tolist()]
+    if isinstance(timestep, (list, tuple)):
+        return [float(x) for x in timestep]
+    return [float(timestep)]
+
+
 class ActionDiT(nn.Module):
     """Action expert (action_dit.py:44-100): same constructor and state_dict."""
 
@@ -150,6 +194,23 @@ class ActionDiT(nn.Module):
     def forward(self, action_tokens, timestep, context, context_mask=None):
         """ActionDiT.forward (action_dit.py:333-362): the expert alone, no video cache."""
         return self.engine().denoise_step(action_tokens, timestep, context, context_mask)
+
+    def prepare(self, action_tokens, timestep, context, context_mask=None):
+        """ActionDiT.prepare (action_dit.py:312-327) -> (tokens, t, t_mod, context,
+        context_mask, freqs) in the reference's order; tokens / t / t_mod are one
+        PreparedAction record (the stage runs inside the step kernels) and freqs the RoPE
+        table of the action positions."""
+        prep = PreparedAction(action_tokens, _host_timestep(timestep)[0], context, context_mask,
+                              self.hidden_dim)
+        freqs = rope_table(self.attn_head_dim, action_tokens.shape[1])
+        return prep, prep, prep, context, context_mask, freqs
+
+    def post(self, x):
+        """ActionDiT.post (action_dit.py:329-331): the head, already applied by the step
+        kernels; returns the velocity of an ActionStepOut."""
+        if not isinstance(x, ActionStepOut):
+            raise TypeError("ActionDiT.post takes the output of MoT.forward_action_with_video_cache_tensor")
+        return x.velocity
 
 
 # ------------------------------------------------------------------ engine
@@ -306,7 +367,10 @@ class ActionExpertEngine:
 
     def denoise_step(self, latents, timestep, context, context_mask=None, cache_k=None,
                      cache_v=None, attn_mask=None) -> torch.Tensor:
-        """One model evaluation (FastWAM._denoise_action_with_video_cache, fastwam.py:771-804)."""
+        """One model evaluation (FastWAM._denoise_action_with_video_cache, fastwam.py:771-804).
+        timestep: a float, or a one-value tensor; the kernels take it as a launch argument,
+        so a tensor on the GPU costs a device-to-host read (a stream synchronisation) that a
+        host value does not."""
         lat = latents.to(device=self.dev, dtype=torch.bfloat16).contiguous()
         B, Sa, _ = lat.shape
         io = self._io(B, Sa, context, context_mask, cache_k, cache_v, attn_mask, 1)
@@ -428,6 +492,37 @@ class WanVideoDiT(nn.Module):
     def prefill(self, latents, timestep, context, context_mask=None, return_hidden=False):
         return self.engine().prefill(latents, timestep, context, context_mask, return_hidden)
 
+    def prepare(self, x, timestep, context, context_mask=None, action=None, fuse_vae_embedding_in_latents=True):
+        """WanVideoDiT.prepare (wan_video_dit.py:640-720) -> (tokens, t, t_mod, context,
+        context_mask, freqs, f, h, w, tokens_per_frame) in the reference's order; tokens /
+        t / t_mod are one PreparedVideo record (patch embedding, time MLPs and text
+        embedding run inside the prefill kernels), freqs the 3-D RoPE table."""
+        if action is not None:
+            raise ValueError("action-conditioned prepare is not on this path")
+        if not fuse_vae_embedding_in_latents:
+            raise ValueError("only fuse_vae_embedding_in_latents=True exists (as in the reference)")
+        pt, ph, pw = self.patch_size
+        f, h, w = x.shape[2] // pt, x.shape[3] // ph, x.shape[4] // pw
+        prep = PreparedVideo(x, _host_timestep(timestep), context, context_mask, (f, h, w), self.hidden_dim)
+        freqs = rope_table_3d(self.attn_head_dim, f, h, w)
+        return prep, prep, prep, context, context_mask, freqs, f, h, w, h * w
+
+    def build_video_to_video_mask(self, video_seq_len: int, video_tokens_per_frame: int, device=None):
+        """WanVideoDiT.build_video_to_video_mask (wan_video_dit.py:489-523), bool."""
+        mode = self.video_attention_mask_mode
+        if mode == "bidirectional":
+            return torch.ones((video_seq_len, video_seq_len), dtype=torch.bool, device=device)
+        if mode == "first_frame_causal":
+            m = torch.ones((video_seq_len, video_seq_len), dtype=torch.bool, device=device)
+            ff = min(video_tokens_per_frame, video_seq_len)
+            m[:ff, ff:] = False
+            return m
+        if mode == "per_frame_causal":
+            nf = video_seq_len // video_tokens_per_frame
+            fc = torch.tril(torch.ones((nf, nf), dtype=torch.bool, device=device))
+            return fc.repeat_interleave(video_tokens_per_frame, 0).repeat_interleave(video_tokens_per_frame, 1)
+        raise ValueError(f"unknown video_attention_mask_mode {mode!r}")
+
 
 class VideoPrefillEngine:
     """Packed bf16 weights + fam_video_expert handle + workspace of one WanVideoDiT."""
@@ -523,6 +618,8 @@ class VideoPrefillEngine:
                 cache_k=None, cache_v=None, hidden=None, use_graph=True, t_out=None):
         """WanVideoDiT.prepare + MoT.prefill_video_cache_tensor: returns the per-block K and V
         lists ([B, S, H*d] bf16) and, with return_hidden, the final token states (fp32).
+        timestep: a float, a list of floats (one per sample) or a tensor; the kernels take the
+        values as launch arguments, so a tensor on the GPU costs a device-to-host read.
         t_out (bf16 [B, 2, D], optional) receives the time embedding rows for post()."""
         d = self.dit
         lat = latents.to(device=self.dev, dtype=torch.bfloat16).contiguous()
@@ -541,7 +638,12 @@ class VideoPrefillEngine:
         cm = None
         if context_mask is not None:
             cm = context_mask.to(device=self.dev, dtype=torch.uint8).expand(B, Cc).contiguous()
-        tsv = timestep.reshape(-1).float().tolist() if torch.is_tensor(timestep) else [float(timestep)]
+        if torch.is_tensor(timestep):
+            tsv = timestep.reshape(-1).float().tolist()
+        elif isinstance(timestep, (list, tuple)):
+            tsv = [float(x) for x in timestep]
+        else:
+            tsv = [float(timestep)]
         if len(tsv) == 1:
             tsv = tsv * B
         io = _abi.VideoIO()
@@ -687,6 +789,51 @@ class CAEEngine:
         self._hold = (ctx, cm)
         self._last = (B, C_)
         return (lat, trace) if return_trace else lat
+
+    def chunk_decode(self, latents, timesteps: Sequence[float], deltas: Sequence[float], context, ae: "ActionAE",
+                     context_mask=None, suite_ids=None):
+        """The Euler loop and ActionAE.decode of the final latents (fam_cae_chunk_decode): the
+        decode runs in the step kernel's epilogue when the decoder qualifies (one upsampling
+        stage), else its own kernels follow.  Returns (fp32 latents [B, S, A], fp32 actions
+        [B, horizon, action_dim]); self.decode_fused tells which way the decode ran."""
+        lat = latents.to(device=self.dev, dtype=torch.float32).clone()
+        B, S, A = lat.shape
+        ctx = context if context.is_cuda and context.dtype in (torch.bfloat16, torch.float32) \
+            else context.to(self.dev, torch.float32)
+        ctx = ctx.contiguous()
+        C_ = ctx.shape[1]
+        cm = None
+        if context_mask is not None:
+            cm = context_mask.to(device=self.dev, dtype=torch.uint8).expand(B, C_).contiguous()
+        dec = ae.decoder
+        if dec._packed is None:
+            dec._pack()
+        dcfg, dw, _, _ = dec._packed
+        n = C.c_size_t()
+        check(lib().fam_cae_decode_workspace_size(C.byref(self.cfg), C.byref(dcfg), C.byref(dw), B, C_,
+                                                  C.byref(n)), "fam_cae_decode_workspace_size")
+        if self.ws is None or self.ws.numel() < n.value:
+            self.ws = torch.empty(n.value, dtype=torch.uint8, device=self.dev)
+        N = len(timesteps)
+        ts = (C.c_float * N)(*[float(t) for t in timesteps])
+        ds = (C.c_float * N)(*[float(d) for d in deltas])
+        out = torch.empty((B, ae.cfg.action_horizon, ae.cfg.action_dim), dtype=torch.float32, device=self.dev)
+        sid = None
+        if suite_ids is not None and dec.suite_embed is not None:
+            sid = suite_ids.to(device=self.dev, dtype=torch.int32).contiguous()
+        fused = C.c_int32(0)
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        check(lib().fam_cae_chunk_decode(C.byref(self.cfg), C.byref(self._w), B, S, ctx.data_ptr(),
+                                         1 if ctx.dtype == torch.bfloat16 else 0, C_,
+                                         cm.data_ptr() if cm is not None else None, lat.data_ptr(), ts, ds, N,
+                                         None, C.byref(dcfg), C.byref(dw),
+                                         sid.data_ptr() if sid is not None else None, out.data_ptr(),
+                                         C.byref(fused), self.ws.data_ptr(), self.ws.numel(), C.c_void_p(st)),
+              "fam_cae_chunk_decode")
+        self.decode_fused = bool(fused.value)
+        self._hold = (ctx, cm, sid)
+        self._last = (B, C_)
+        return lat, out
 
     def status(self) -> int:
         """Status word of the last chunk (0 = every bounded device wait completed)."""

@@ -14,10 +14,13 @@ boundary over this library:
   fam::action_decode                    ActionAE.decode (action_ae.py:184-187)
 
 A module holding packed weights is registered once (`register`) and named by an
-integer handle, so the operators take tensors and scalars only.  Every output is a
-new tensor (no aliasing of inputs); the fake implementations give shapes, dtypes and
-devices from the registered module's configuration, so the operators trace under
-FakeTensorMode / torch.compile without running a kernel.
+integer handle, so the operators take tensors and scalars only.  Timesteps are host
+scalars (float / List[float], already the values the reference computes in its
+dtype): the kernels take them as launch arguments, so no operator reads a device
+tensor back to the host, and a call never synchronises the stream.  Every output is
+a new tensor (no aliasing of inputs); the fake implementations give shapes, dtypes
+and devices from the registered module's configuration, so the operators trace under
+FakeTensorMode / torch.compile(fullgraph=True) without running a kernel.
 """
 import itertools
 from typing import Dict, List, Optional
@@ -56,11 +59,12 @@ def _or_none(ts: List[torch.Tensor]) -> Optional[List[torch.Tensor]]:
 
 # ------------------------------------------------------------ video prefill
 @torch.library.custom_op("fam::prefill_video_cache", mutates_args=())
-def prefill_video_cache(handle: int, latents: torch.Tensor, timestep: torch.Tensor, context: torch.Tensor,
+def prefill_video_cache(handle: int, latents: torch.Tensor, timestep: List[float], context: torch.Tensor,
                         context_mask: Optional[torch.Tensor]) -> List[torch.Tensor]:
-    """Per-block K then per-block V ([B, S, H*d] bf16 each, 2 x num_layers tensors)."""
+    """Per-block K then per-block V ([B, S, H*d] bf16 each, 2 x num_layers tensors);
+    timestep: one value per sample, or one for the batch."""
     vid = _get(handle, WanVideoDiT)
-    k, v = vid.engine().prefill(latents, timestep, context, context_mask)
+    k, v = vid.engine().prefill(latents, list(timestep), context, context_mask)
     return list(k) + list(v)
 
 
@@ -76,13 +80,13 @@ def _(handle, latents, timestep, context, context_mask):
 
 # ------------------------------------------------------------ action expert
 @torch.library.custom_op("fam::denoise_action_with_video_cache", mutates_args=())
-def denoise_action_with_video_cache(handle: int, latents: torch.Tensor, timestep: torch.Tensor,
+def denoise_action_with_video_cache(handle: int, latents: torch.Tensor, timestep: float,
                                     context: torch.Tensor, context_mask: Optional[torch.Tensor],
                                     cache_k: List[torch.Tensor], cache_v: List[torch.Tensor],
                                     attn_mask: Optional[torch.Tensor]) -> torch.Tensor:
     """One model evaluation: the velocity [B, Sa, A] (bf16).  Empty cache lists: no video K/V."""
     act = _get(handle, ActionDiT)
-    return act.engine().denoise_step(latents, timestep, context, context_mask, _or_none(cache_k),
+    return act.engine().denoise_step(latents, float(timestep), context, context_mask, _or_none(cache_k),
                                      _or_none(cache_v), attn_mask)
 
 

@@ -30,6 +30,9 @@ Reference code paths exercised:
         FastWAM/src/fastwam/models/wan22/fastwam_idm.py:283-313, fastwam_joint.py:29-49
   vae VideoVAE38_.encode of one observation frame (fp32 and bf16)
         FastWAM/src/fastwam/models/wan22/wan_video_vae.py:1285-1304, 619-733
+  fastwam_infer_action  FastWAM.infer_action end to end (VAE encode, proprio token, prefill,
+        action Euler loop, Action-VAE decode) and its checkpoint payload, small shapes, bf16
+        FastWAM/src/fastwam/models/wan22/fastwam.py:257-306, 1080-1274, 1300-1345
 """
 from __future__ import annotations
 
@@ -329,6 +332,76 @@ def make_vae(R):
     return out
 
 
+class _VaeHolder:
+    """The attributes FastWAM reads from its `vae`: .model.encode(x, scale), .scale, .to()."""
+
+    def __init__(self, model, mean, inv_std):
+        self.model, self.scale = model, [mean, inv_std]
+
+    def to(self, *args, **kwargs):
+        self.model.to(*args, **kwargs)
+        return self
+
+
+def make_fastwam(R):
+    """FastWAM.infer_action end to end at small shapes (fastwam.py:1080-1274): VAE encode of
+    the observation, proprio token appended to the context, video prefill at t = 0, the MoT
+    action Euler loop over the K/V cache, Action-VAE decode.  bf16 experts, VAE and proprio
+    encoder (the reference's torch_dtype), fp32 Action-VAE; the checkpoint payload is saved in
+    the reference's own format ({"mot": mot.state_dict(), "proprio_encoder": ...})."""
+    torch.manual_seed(9)
+    vcfg = dict(hidden_dim=128, in_dim=8, ffn_dim=256, out_dim=8, text_dim=96, freq_dim=256, eps=1e-6,
+                patch_size=(1, 2, 2), num_heads=2, attn_head_dim=128, num_layers=2, has_image_input=False,
+                seperated_timestep=True, video_attention_mask_mode="first_frame_causal")
+    acfg = dict(hidden_dim=64, action_dim=16, ffn_dim=128, text_dim=96, freq_dim=256, eps=1e-6,
+                num_heads=2, attn_head_dim=128, num_layers=2)
+    ae_cfg = dict(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16, decoder_hidden=64,
+                  video_cond_dim=0, variational=True)
+    vae_cfg = dict(dim=8, z_dim=8, dec_dim=8)
+    video = R.WanVideoDiT(**vcfg).to(torch.bfloat16).eval()
+    action = R.ActionDiT(**acfg).to(torch.bfloat16).eval()
+    mot = R.MoT({"video": video, "action": action}).eval()
+    vmodel = R.VideoVAE38_(**vae_cfg).eval()
+    g = torch.Generator().manual_seed(9)
+    with torch.no_grad():
+        for name, prm in vmodel.named_parameters():
+            if name.endswith("gamma"):
+                prm.copy_(1.0 + 0.1 * torch.randn(prm.shape, generator=g))
+            elif name.endswith("bias"):
+                prm.copy_(0.05 * torch.randn(prm.shape, generator=g))
+            else:
+                prm.copy_(torch.randn(prm.shape, generator=g) / prm[0].numel() ** 0.5)
+    vmodel = vmodel.bfloat16()
+    mean = (0.2 * torch.randn(8, generator=g)).bfloat16()
+    inv_std = (1.0 + 0.5 * torch.rand(8, generator=g)).bfloat16()
+    ae = R.ActionAE(R.ActionAEConfig(**ae_cfg)).eval()
+    model = R.FastWAM(video_expert=video, action_expert=action, mot=mot, vae=_VaeHolder(vmodel, mean, inv_std),
+                      text_dim=96, proprio_dim=8, action_vae=ae, device="cpu", torch_dtype=torch.bfloat16,
+                      action_infer_shift=5.0)
+    image = (torch.rand(1, 3, 64, 96, generator=g) * 2 - 1).bfloat16()
+    C = 12
+    ctx = torch.randn(1, C, 96, generator=g).bfloat16()
+    ctx_mask = torch.ones(1, C, dtype=torch.bool)
+    ctx_mask[0, -3:] = False
+    proprio = torch.randn(1, 8, generator=g).bfloat16()
+    with torch.no_grad():
+        out = model.infer_action(prompt=None, input_image=image, action_horizon=32, proprio=proprio,
+                                 context=ctx, context_mask=ctx_mask, num_inference_steps=4, seed=42,
+                                 rand_device="cpu", return_action_latents=True)
+    payload = {"mot": {k: v.detach().clone() for k, v in mot.state_dict().items()}, "step": None,
+               "torch_dtype": str(torch.bfloat16),
+               "proprio_encoder": {k: v.detach().clone() for k, v in model.proprio_encoder.state_dict().items()}}
+    return {"kind": "fastwam", "video_cfg": vcfg, "action_cfg": acfg, "ae_cfg": ae_cfg, "vae_cfg": vae_cfg,
+            "checkpoint": payload,
+            "vae_params": {k: v.detach().clone() for k, v in vmodel.state_dict().items()
+                           if (k.startswith("encoder.") or k.startswith("conv1.")) and ".time_conv." not in k},
+            "vae_mean": mean, "vae_inv_std": inv_std,
+            "action_vae": {"config": ae_cfg, "model": {k: v.detach().clone() for k, v in ae.state_dict().items()}},
+            "input_image": image, "context": ctx, "context_mask": ctx_mask, "proprio": proprio,
+            "num_inference_steps": 4, "seed": 42, "action_horizon": 32, "action_infer_shift": 5.0,
+            "action": out["action"], "action_latents": out["action_latents"]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True,
@@ -339,7 +412,8 @@ def main():
     torch.set_num_threads(4)
     for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
                      ("c2_video_prefill", make_c2), ("primitives", make_primitives),
-                     ("vae_encode", make_vae), ("joint_step", make_joint), ("idm_step", make_idm)):
+                     ("vae_encode", make_vae), ("joint_step", make_joint), ("idm_step", make_idm),
+                     ("fastwam_infer_action", make_fastwam)):
         if args.only is not None and name not in args.only:
             continue
         fx = fn(R)

@@ -135,3 +135,32 @@ def test_vae_encoder_param_table_matches_reference_state_dict():
     enc = V.VideoVAE38Encoder(fx["params"], dim=fx["cfg"]["dim"], z_dim=fx["cfg"]["z_dim"], device="cpu")
     assert enc.conv_in.w.shape == (fx["cfg"]["dim"], 9 * 64)
     assert all(s[0] > 0 and s[2] % 8 == 0 for s in enc._gemm_shapes(64, 96))
+
+
+def test_fastwam_checkpoint_layout_and_mot_checks():
+    """The MoT holder's state_dict keys are the reference checkpoint's (`mixtures.video.` /
+    `mixtures.action.`), load_checkpoint takes the reference payload unchanged, and the
+    expert-compatibility checks of mot.py:33-52 hold."""
+    import torch
+    FW = importlib.import_module("faster-action-models_b200.fastwam")
+    M = importlib.import_module("faster-action-models_b200.models")
+    fx = torch.load(Path(__file__).resolve().parent / "golden" / "fastwam_infer_action.pt")
+    video = M.WanVideoDiT(**fx["video_cfg"]).to(torch.bfloat16)
+    action = M.ActionDiT(**fx["action_cfg"]).to(torch.bfloat16)
+    mot = FW.MoT({"video": video, "action": action})
+    assert set(mot.state_dict().keys()) == set(fx["checkpoint"]["mot"].keys())
+    model = FW.FastWAM(video, action, mot, vae=None, text_dim=96, proprio_dim=8, device="cpu")
+    model.load_checkpoint(fx["checkpoint"])
+    for k, v in fx["checkpoint"]["mot"].items():
+        assert torch.equal(mot.state_dict()[k], v), k
+    assert torch.equal(model.proprio_encoder.weight, fx["checkpoint"]["proprio_encoder"]["weight"])
+    bad = M.ActionDiT(**{**fx["action_cfg"], "num_layers": 3})
+    with pytest.raises(ValueError, match="same number of layers"):
+        FW.MoT({"video": video, "action": bad})
+    with pytest.raises(ValueError, match="must include both"):
+        FW.MoT({"video": video})
+    with pytest.raises(ValueError, match="multiples of 16"):
+        model.infer_action(None, torch.zeros(1, 3, 60, 96), 32, context=torch.zeros(1, 4, 96),
+                           context_mask=torch.ones(1, 4, dtype=torch.bool))
+    with pytest.raises(ValueError, match="last dim must be 8"):
+        model.infer_action(None, torch.zeros(1, 3, 64, 96), 32, proprio=torch.zeros(1, 5))

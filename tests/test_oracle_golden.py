@@ -156,3 +156,28 @@ def test_idm_video_step_and_joint_mask_match_reference():
                               fx["context_mask"])
     _same(pv, fx["pred_video"])
     assert torch.equal(O.build_joint_model_mask(18, 8, 6), fx["joint_mask"])
+
+
+def test_oracle_infer_action_matches_reference_fastwam():
+    """The oracle's restatement of FastWAM.infer_action (VAE encode, proprio token, video
+    prefill at t = 0, MoT action Euler loop, Action-VAE decode) reproduces the reference run
+    recorded in fastwam_infer_action.pt (bf16 experts)."""
+    fx = torch.load(GOLDEN / "fastwam_infer_action.pt")
+    vc, ac = fx["video_cfg"], fx["action_cfg"]
+    vcfg = O.DiTConfig(hidden_dim=vc["hidden_dim"], ffn_dim=vc["ffn_dim"], num_heads=vc["num_heads"],
+                       attn_head_dim=vc["attn_head_dim"], num_layers=vc["num_layers"], text_dim=vc["text_dim"],
+                       in_dim=vc["in_dim"], out_dim=vc["out_dim"])
+    acfg = O.DiTConfig(hidden_dim=ac["hidden_dim"], ffn_dim=ac["ffn_dim"], num_heads=ac["num_heads"],
+                       attn_head_dim=ac["attn_head_dim"], num_layers=ac["num_layers"], text_dim=ac["text_dim"],
+                       action_dim=ac["action_dim"])
+    e = fx["ae_cfg"]
+    dcfg = O.DecoderConfig(e["action_dim"], e["action_horizon"], e["num_tokens"], e["latent_dim"],
+                           e["decoder_hidden"])
+    vae_cfg = O.VaeConfig(dim=fx["vae_cfg"]["dim"], z_dim=fx["vae_cfg"]["z_dim"])
+    act, lat = O.infer_action(fx["checkpoint"]["mot"], vcfg, acfg, fx["vae_params"], vae_cfg, fx["vae_mean"],
+                              fx["vae_inv_std"], fx["action_vae"]["model"], dcfg,
+                              fx["checkpoint"]["proprio_encoder"], fx["input_image"], fx["context"],
+                              fx["context_mask"], fx["proprio"], fx["action_horizon"], fx["num_inference_steps"],
+                              fx["action_infer_shift"], fx["seed"])
+    assert torch.equal(lat, fx["action_latents"])
+    assert torch.equal(act, fx["action"])

@@ -29,11 +29,11 @@ def test_fake_shapes():
         with FakeTensorMode():
             lat_v = torch.empty(1, 16, 3, 8, 12, dtype=torch.bfloat16)
             ctx = torch.empty(1, 10, 96, dtype=torch.bfloat16)
-            kv = torch.ops.fam.prefill_video_cache(hv, lat_v, torch.zeros(1), ctx, None)
+            kv = torch.ops.fam.prefill_video_cache(hv, lat_v, [0.0], ctx, None)
             assert len(kv) == 4 and all(t.shape == (1, 72, 64) and t.dtype == torch.bfloat16 for t in kv)
             lat_a = torch.empty(1, 8, 7, dtype=torch.bfloat16)
             mask = torch.ones(8, 80, dtype=torch.bool)
-            vel = torch.ops.fam.denoise_action_with_video_cache(ha, lat_a, torch.full((1,), 500.0), ctx, None,
+            vel = torch.ops.fam.denoise_action_with_video_cache(ha, lat_a, 500.0, ctx, None,
                                                                 kv[:2], kv[2:], mask)
             assert vel.shape == (1, 8, 7) and vel.dtype == torch.bfloat16
             out = torch.ops.fam.action_chunk(ha, lat_a, [1000.0, 500.0], [-0.5, -0.5], ctx, None, [], [], None)

@@ -39,14 +39,14 @@ def test_operators_match_engine_calls():
         ctx = torch.randn(1, 10, 96, generator=g).bfloat16().cuda()
         cm = torch.ones(1, 10, dtype=torch.bool, device="cuda")
         t0 = torch.zeros(1)
-        kv = torch.ops.fam.prefill_video_cache(hv, lat_v, t0, ctx, cm)
+        kv = torch.ops.fam.prefill_video_cache(hv, lat_v, [0.0], ctx, cm)
         k_ref, v_ref = vid.prefill(lat_v, t0, ctx, cm)
         assert all(torch.equal(a, b) for a, b in zip(kv, list(k_ref) + list(v_ref)))
         ck, cv = [k.clone() for k in kv[:2]], [v.clone() for v in kv[2:]]
         Sv = ck[0].shape[1]
         lat_a = torch.randn(1, 8, 7, generator=g).bfloat16().cuda()
         mask = torch.ones(8, Sv + 8, dtype=torch.bool, device="cuda")
-        t = torch.full((1,), 750.0).bfloat16()
+        t = 750.0  # a host scalar: the operators never read the device back
         vel = torch.ops.fam.denoise_action_with_video_cache(ha, lat_a, t, ctx, cm, ck, cv, mask)
         ref = act.engine().denoise_step(lat_a, t, ctx, cm, ck, cv, mask)
         assert vel.shape == (1, 8, 7) and vel.dtype == torch.bfloat16
