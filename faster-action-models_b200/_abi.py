@@ -140,8 +140,14 @@ def declare_cae(lib) -> None:
                                                i32, C.POINTER(sz)]
     lib.fam_action_decode.argtypes = [C.POINTER(DecoderConfig), C.POINTER(DecoderWeights), i32,
                                       vp, vp, vp, vp, sz, vp]
+    lib.fam_cae_decode_workspace_size.argtypes = [C.POINTER(ActionConfig), C.POINTER(DecoderConfig),
+                                                  C.POINTER(DecoderWeights), i32, i32, C.POINTER(sz)]
+    lib.fam_cae_chunk_decode.argtypes = [C.POINTER(ActionConfig), C.POINTER(CaeWeights), i32, i32, vp,
+                                         i32, i32, vp, vp, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                         i32, vp, C.POINTER(DecoderConfig), C.POINTER(DecoderWeights), vp, vp,
+                                         C.POINTER(i32), vp, sz, vp]
     for n in ("fam_cae_workspace_size", "fam_cae_chunk", "fam_cae_status", "fam_decoder_workspace_size",
-              "fam_action_decode"):
+              "fam_action_decode", "fam_cae_decode_workspace_size", "fam_cae_chunk_decode"):
         getattr(lib, n).restype = C.c_int
 
 

@@ -58,11 +58,35 @@ int fam_cae_workspace_size(const fam_action_config* cfg, int32_t batch, int32_t 
   return FAM_OK;
 }
 
-int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch,
-                  int32_t tokens, const void* context, int32_t context_bf16, int32_t context_tokens,
-                  const uint8_t* context_mask, float* latent, const float* timesteps,
-                  const float* deltas, int32_t num_steps, float* velocity_trace, void* workspace,
-                  size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Whether the decode can run in the staged step kernel's epilogue: one
+// upsampling stage of even stride, the sample's latents as the decoder input,
+// whole GroupNorm groups per CTA of the cluster, at most two outputs per
+// thread per layer, and the activations in the step kernel's dead buffers.
+bool cae_decode_fusable(const CaeStepArgs& sa, const fam_decoder_config& dc, const fam_decoder_weights& dw) {
+  if (sa.wpack == nullptr || dw.num_stages != 1 || dw.stages == nullptr) return false;
+  const int s = dw.stages[0].stride, h = dc.hidden, nc = sa.plan.nc;
+  if (s < 2 || s % 2 || dc.num_tokens != sa.S || dc.latent_dim != sa.A || h % 4 || h % nc) return false;
+  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc, Lo = dc.num_tokens * s;
+  if (ch % cg || ch / cg > 32 || ch * Lo > 2 * 1024 || ch * 2 * s > 8192 || ch * 3 * 4 > 8192) return false;
+  if (dc.action_horizon <= 0 || dc.action_dim <= 0) return false;
+  CaeDecode d;
+  memset(&d, 0, sizeof(d));
+  d.hidden = h;
+  d.tokens = dc.num_tokens;
+  d.stride = s;
+  return cae_decode_floats(d, nc) <= sa.plan.o_x;
+}
+
+int cae_chunk_impl(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch, int32_t tokens,
+                   const void* context, int32_t context_bf16, int32_t context_tokens, const uint8_t* context_mask,
+                   float* latent, const float* timesteps, const float* deltas, int32_t num_steps,
+                   float* velocity_trace, void* workspace, size_t workspace_bytes, void* stream,
+                   const fam_decoder_config* dcfg, const fam_decoder_weights* dw, const int32_t* suite_ids,
+                   float* actions, int32_t* decode_fused) {
   int rc = check_cae(cfg);
   if (rc) return rc;
   if (w == nullptr || w->layers == nullptr || latent == nullptr || timesteps == nullptr ||
@@ -158,9 +182,92 @@ int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_
     ca.plan = sa.plan;
     sa.wpack = wpack;
   }
+  const bool fuse = dcfg != nullptr && cae_decode_fusable(sa, *dcfg, *dw);
+  if (fuse) {
+    const fam_decoder_stage& g = dw->stages[0];
+    CaeDecode& d = sa.dec;
+    d.enabled = 1;
+    d.hidden = dcfg->hidden;
+    d.latent = dcfg->latent_dim;
+    d.tokens = dcfg->num_tokens;
+    d.stride = g.stride;
+    d.horizon = dcfg->action_horizon;
+    d.action_dim = dcfg->action_dim;
+    d.in_w = dw->in_w;
+    d.in_b = dw->in_b;
+    d.out_w = dw->out_w;
+    d.out_b = dw->out_b;
+    d.suite_embed = dw->suite_embed;
+    d.suite_ids = suite_ids;
+    d.convt_w = g.convt_w;
+    d.convt_b = g.convt_b;
+    d.gn0_w = g.gn0_w;
+    d.gn0_b = g.gn0_b;
+    d.c1_w = g.c1_w;
+    d.c1_b = g.c1_b;
+    d.gn1_w = g.gn1_w;
+    d.gn1_b = g.gn1_b;
+    d.c2_w = g.c2_w;
+    d.c2_b = g.c2_b;
+    d.gn2_w = g.gn2_w;
+    d.gn2_b = g.gn2_b;
+    d.out = actions;
+  }
+  if (decode_fused != nullptr) *decode_fused = fuse ? 1 : 0;
   rc = check_cuda(launch_cae_context(ca, st, false), "cae context launch");
   if (rc) return rc;
-  return check_cuda(launch_cae_steps(sa, st, true), "cae steps launch");
+  rc = check_cuda(launch_cae_steps(sa, st, true), "cae steps launch");
+  if (rc || dcfg == nullptr || fuse) return rc;
+  // the separate decoder after the chunk (its scratch behind the expert's workspace)
+  const size_t cae_need = cae_ws(*cfg, batch, context_tokens);
+  return fam_action_decode(dcfg, dw, batch, latent, suite_ids, actions, static_cast<char*>(workspace) + cae_need,
+                           workspace_bytes - cae_need, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch,
+                  int32_t tokens, const void* context, int32_t context_bf16, int32_t context_tokens,
+                  const uint8_t* context_mask, float* latent, const float* timesteps,
+                  const float* deltas, int32_t num_steps, float* velocity_trace, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  return cae_chunk_impl(cfg, w, batch, tokens, context, context_bf16, context_tokens, context_mask, latent,
+                        timesteps, deltas, num_steps, velocity_trace, workspace, workspace_bytes, stream, nullptr,
+                        nullptr, nullptr, nullptr, nullptr);
+}
+
+int fam_cae_decode_workspace_size(const fam_action_config* cfg, const fam_decoder_config* dcfg,
+                                  const fam_decoder_weights* dw, int32_t batch, int32_t context_tokens,
+                                  size_t* bytes) {
+  size_t a = 0, d = 0;
+  int rc = fam_cae_workspace_size(cfg, batch, context_tokens, &a);
+  if (rc) return rc;
+  rc = fam_decoder_workspace_size(dcfg, dw, batch, &d);
+  if (rc) return rc;
+  *bytes = a + d;
+  return FAM_OK;
+}
+
+int fam_cae_chunk_decode(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch, int32_t tokens,
+                         const void* context, int32_t context_bf16, int32_t context_tokens,
+                         const uint8_t* context_mask, float* latent, const float* timesteps, const float* deltas,
+                         int32_t num_steps, float* velocity_trace, const fam_decoder_config* dcfg,
+                         const fam_decoder_weights* dw, const int32_t* suite_ids, float* actions,
+                         int32_t* decode_fused, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dcfg == nullptr || dw == nullptr || actions == nullptr) return set_error("cae decode: null decoder argument");
+  size_t need = 0;
+  int rc = fam_cae_decode_workspace_size(cfg, dcfg, dw, batch, context_tokens, &need);
+  if (rc) return rc;
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error("cae decode: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (dcfg->num_tokens != tokens || dcfg->latent_dim != cfg->action_dim)
+    return set_error("cae decode: the decoder takes %d x %d latents, the chunk has %d x %d", dcfg->num_tokens,
+                     dcfg->latent_dim, tokens, cfg->action_dim);
+  return cae_chunk_impl(cfg, w, batch, tokens, context, context_bf16, context_tokens, context_mask, latent,
+                        timesteps, deltas, num_steps, velocity_trace, workspace, workspace_bytes, stream, dcfg, dw,
+                        suite_ids, actions, decode_fused);
 }
 
 int fam_cae_status(const fam_action_config* cfg, int32_t batch, int32_t context_tokens, const void* workspace,

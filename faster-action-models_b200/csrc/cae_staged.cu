@@ -393,6 +393,231 @@ __device__ __forceinline__ void cs_step_entry_row(const CaeStepArgs& a, float* c
 // FD, FHD, FF, FA, FS: compile-time hidden width, H*d, FFN width, latent width and
 // token count of a specialised instance (0 = read from the arguments): with
 // constant widths every dot product and row reduction unrolls completely.
+// ------------------------------------------------- epilogue: Action-VAE decode
+// The sample's final latents [T, Z] (every CTA of the cluster holds them) ->
+// the action chunk: input_proj (+ suite embedding), ConvTranspose1d(h, h, 2s,
+// s, s/2) -> GroupNorm -> SiLU, residual [Conv1d k3 -> GN -> SiLU -> Conv1d k3
+// -> GN] + skip, crop / zero-pad to the horizon, output_proj; fp32 like the
+// reference's Action-VAE.  CTA `rank` of the nc-CTA cluster owns the channels
+// [rank h / nc, (rank + 1) h / nc) -- whole GroupNorm groups -- and writes each
+// stage's activations of its channels into every CTA's copy of the full
+// activation (st.shared::cluster), one cluster barrier per exchange.  Weights
+// stream from global (L2) through a double-buffered cp.async staging area.
+constexpr int kDecChunk = 8192;   // floats per weight staging buffer
+constexpr float kDecGnEps = 1e-5f;
+
+__device__ __forceinline__ int dec_r4(int n) { return (n + 3) & ~3; }
+
+__host__ __device__ int dec_layout(const CaeDecode& d, int nc, int* o_xa, int* o_xb, int* o_loc, int* o_w,
+                                   int* o_st) {
+  const int h = d.hidden, Lo = d.tokens * d.stride, ch = h / nc;
+  int c = (h * d.tokens + 3) & ~3;
+  *o_xa = c;
+  c += h * Lo;
+  *o_xb = c;
+  c += h * Lo;
+  *o_loc = c;
+  c += (ch * Lo + 3) & ~3;
+  *o_w = c;
+  c += 2 * kDecChunk;
+  *o_st = c;                        // GroupNorm (mean, rstd) per local group
+  c += 16;
+  return c;
+}
+
+// Stage rows [r0, r0 + nr) of a weight whose row r is the `len` floats at
+// src + r * rstride (16-byte aligned, len % 4 == 0) into dst (rows packed).
+__device__ __forceinline__ void dec_stage(float* dst, const float* src, long long rstride, int r0, int nr, int len) {
+  const int l4 = len >> 2;
+  for (int i = threadIdx.x; i < nr * l4; i += kCsThreads) {
+    const int r = i / l4, c = (i - r * l4) * 4;
+    cp_async16(dst + r * len + c, src + static_cast<long long>(r0 + r) * rstride + c, true);
+  }
+  cp_async_commit();
+}
+
+// GroupNorm statistics of this CTA's groups of loc [ch][Lo] (warp g: group g),
+// then y = GN(loc) (* SiLU) written to rows [c0, c0 + ch) of `full` in every
+// CTA of the cluster (skip: add skip[c][p] after the norm).
+__device__ void dec_norm_exchange(float* loc, float* full, const float* skip, const float* gw, const float* gb,
+                                  int ch, int c0, int Lo, int cg, bool act, float* st, int nc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ng = ch / cg, n = cg * Lo;
+  if (warp < ng) {
+    const float* v = loc + warp * n;
+    float s = 0.f;
+    for (int i = lane; i < n; i += 32) s += v[i];
+    const float mean = warp_sum(s) / n;
+    float q = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float d = v[i] - mean;
+      q += d * d;
+    }
+    const float var = warp_sum(q) / n;
+    if (lane == 0) {
+      st[2 * warp] = mean;
+      st[2 * warp + 1] = rsqrtf(var + kDecGnEps);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ch * Lo; i += kCsThreads) {
+    const int cl = i / Lo, pp = i - cl * Lo, c = c0 + cl, g = cl / cg;
+    float y = (loc[i] - st[2 * g]) * st[2 * g + 1] * gw[c] + gb[c];
+    if (act) y = silu(y);
+    if (skip != nullptr) y += skip[c * Lo + pp];
+    full[c * Lo + pp] = y;
+    for (int r = 0; r < nc; ++r)
+      if (r != static_cast<int>(cluster_ctarank())) st_cluster_f32(cluster_map(full + c * Lo + pp, r), y);
+  }
+  if (nc > 1) cluster_barrier(); else __syncthreads();
+}
+
+// Conv1d(h, h, 3, padding 1) of the full activation `in` [h][Lo] for this CTA's
+// output channels -> loc [ch][Lo] (+ bias); weight [h][h][3].
+__device__ void dec_conv3(const float* in, float* loc, float* wbuf, const float* w, const float* bias, int h, int c0,
+                          int ch, int Lo) {
+  const int cc = kDecChunk / (ch * 3) >= h ? h : (kDecChunk / (ch * 3)) & ~3;  // input channels per chunk
+  const int nchunk = (h + cc - 1) / cc;
+  float acc[2] = {0.f, 0.f};
+  // chunk k: rows co of the slice, columns [ci0 * 3, (ci0 + cc) * 3)
+  auto stage = [&](int k) {
+    const int ci0 = k * cc, n = min(cc, h - ci0);
+    float* dst = wbuf + (k & 1) * kDecChunk;
+    const int l4 = n * 3 / 4;
+    for (int i = threadIdx.x; i < ch * l4; i += kCsThreads) {
+      const int r = i / l4, c = (i - r * l4) * 4;
+      cp_async16(dst + r * n * 3 + c, w + (static_cast<long long>(c0 + r) * h + ci0) * 3 + c, true);
+    }
+    cp_async_commit();
+  };
+  stage(0);
+  for (int k = 0; k < nchunk; ++k) {
+    if (k + 1 < nchunk) stage(k + 1);
+    if (k + 1 < nchunk) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();
+    const int ci0 = k * cc, n = min(cc, h - ci0);
+    const float* wk = wbuf + (k & 1) * kDecChunk;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = threadIdx.x + u * kCsThreads;
+      if (i >= ch * Lo) break;
+      const int cl = i / Lo, pp = i - cl * Lo;
+      const float* wr = wk + cl * n * 3;
+      float a0 = 0.f;
+      for (int ci = 0; ci < n; ++ci) {
+        const float* xr = in + (ci0 + ci) * Lo;
+        const float xm = pp > 0 ? xr[pp - 1] : 0.f, x0 = xr[pp], xp = pp + 1 < Lo ? xr[pp + 1] : 0.f;
+        a0 = fmaf(wr[ci * 3 + 0], xm, a0);
+        a0 = fmaf(wr[ci * 3 + 1], x0, a0);
+        a0 = fmaf(wr[ci * 3 + 2], xp, a0);
+      }
+      acc[u] += a0;
+    }
+    __syncthreads();  // the buffer is refilled two chunks on
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = threadIdx.x + u * kCsThreads;
+    if (i < ch * Lo) loc[i] = acc[u] + bias[c0 + i / Lo];
+  }
+  __syncthreads();
+}
+
+__device__ void cs_decode_epilogue(const CaeStepArgs& a, float* csm, int b, int nc) {
+  const CaeDecode& d = a.dec;
+  const int h = d.hidden, T = d.tokens, Z = d.latent, sdn = d.stride, K = 2 * sdn, pad = sdn / 2, Lo = T * sdn;
+  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc;
+  const int rank = nc > 1 ? static_cast<int>(cluster_ctarank()) : 0, c0 = rank * ch;
+  int o_xa, o_xb, o_loc, o_w, o_st;
+  dec_layout(d, nc, &o_xa, &o_xb, &o_loc, &o_w, &o_st);
+  float* h0 = csm;
+  float* xa = csm + o_xa;
+  float* xb = csm + o_xb;
+  float* loc = csm + o_loc;
+  float* wbuf = csm + o_w;
+  float* st = csm + o_st;
+  const float* lat = CS_SM(lat);  // [T][Z]: the final latents of the sample
+  // 1. input_proj (+ suite embedding), every channel on every CTA: h0 [h][T]
+  const int sid = (d.suite_ids != nullptr && d.suite_embed != nullptr) ? d.suite_ids[b] : -1;
+  for (int i = threadIdx.x; i < h * T; i += kCsThreads) {
+    const int c = i / T, t = i - c * T;
+    float acc = d.in_b[c];
+    for (int k = 0; k < Z; ++k) acc = fmaf(d.in_w[c * Z + k], lat[t * Z + k], acc);
+    if (sid >= 0) acc += d.suite_embed[static_cast<long long>(sid) * h + c];
+    h0[c * T + t] = acc;
+  }
+  // 2. ConvTranspose1d for this CTA's channels: out[co][p] = b[co] + sum over
+  //    ci and the two taps k = (p + pad) mod s, + s of w[ci][co][k] h0[ci][j],
+  //    j = (p + pad - k) / s; weight rows ci staged [cc][ch][K]
+  {
+    const int cc = kDecChunk / (ch * K) >= h ? h : kDecChunk / (ch * K);
+    const int nchunk = (h + cc - 1) / cc;
+    float acc[2] = {0.f, 0.f};
+    auto stage = [&](int k) {
+      const int ci0 = k * cc, n = min(cc, h - ci0);
+      float* dst = wbuf + (k & 1) * kDecChunk;
+      const int l4 = ch * K / 4;
+      for (int i = threadIdx.x; i < n * l4; i += kCsThreads) {
+        const int r = i / l4, c = (i - r * l4) * 4;
+        cp_async16(dst + r * ch * K + c, d.convt_w + (static_cast<long long>(ci0 + r) * h + c0) * K + c, true);
+      }
+      cp_async_commit();
+    };
+    stage(0);
+    for (int k = 0; k < nchunk; ++k) {
+      if (k + 1 < nchunk) stage(k + 1);
+      if (k + 1 < nchunk) cp_async_wait<1>(); else cp_async_wait<0>();
+      __syncthreads();
+      const int ci0 = k * cc, n = min(cc, h - ci0);
+      const float* wk = wbuf + (k & 1) * kDecChunk;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = threadIdx.x + u * kCsThreads;
+        if (i >= ch * Lo) break;
+        const int cl = i / Lo, pp = i - cl * Lo;
+        const int k1 = (pp + pad) % sdn, k2 = k1 + sdn;
+        const int j1 = (pp + pad - k1) / sdn, j2 = j1 - 1;
+        const bool v1 = j1 < T, v2 = j2 >= 0 && j2 < T;
+        float a0 = 0.f;
+        for (int ci = 0; ci < n; ++ci) {
+          const float* wr = wk + (ci * ch + cl) * K;
+          const float* hr = h0 + (ci0 + ci) * T;
+          if (v1) a0 = fmaf(wr[k1], hr[j1], a0);
+          if (v2) a0 = fmaf(wr[k2], hr[j2], a0);
+        }
+        acc[u] += a0;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = threadIdx.x + u * kCsThreads;
+      if (i < ch * Lo) loc[i] = acc[u] + d.convt_b[c0 + i / Lo];
+    }
+    __syncthreads();
+  }
+  // 3. GroupNorm + SiLU -> xa (the skip of the residual block), all CTAs
+  dec_norm_exchange(loc, xa, nullptr, d.gn0_w, d.gn0_b, ch, c0, Lo, cg, true, st, nc);
+  // 4. residual block: Conv1d -> GN -> SiLU -> xb; Conv1d -> GN, + skip -> xa'
+  dec_conv3(xa, loc, wbuf, d.c1_w, d.c1_b, h, c0, ch, Lo);
+  dec_norm_exchange(loc, xb, nullptr, d.gn1_w, d.gn1_b, ch, c0, Lo, cg, true, st, nc);
+  dec_conv3(xb, loc, wbuf, d.c2_w, d.c2_b, h, c0, ch, Lo);
+  // the block output overwrites xb (no CTA reads xb any more once conv2 is done:
+  // dec_conv3 ends with a CTA barrier and the exchange below with a cluster one)
+  if (nc > 1) cluster_barrier();
+  dec_norm_exchange(loc, xb, xa, d.gn2_w, d.gn2_b, ch, c0, Lo, cg, false, st, nc);
+  // 5. crop / zero-pad to the horizon, output_proj (rank 0 writes the chunk)
+  if (rank == 0) {
+    float* out = d.out + static_cast<long long>(b) * d.horizon * d.action_dim;
+    for (int i = threadIdx.x; i < d.horizon * d.action_dim; i += kCsThreads) {
+      const int pp = i / d.action_dim, o = i - pp * d.action_dim;
+      float acc = d.out_b[o];
+      if (pp < Lo)
+        for (int c = 0; c < h; ++c) acc = fmaf(d.out_w[o * h + c], xb[c * Lo + pp], acc);
+      out[i] = acc;
+    }
+  }
+}
+
 template <int HDIM, int FD, int FHD, int FF, int FA, int FS>
 __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const __grid_constant__ CaeStepArgs a) {
   extern __shared__ __align__(16) float csm[];
@@ -737,6 +962,12 @@ __global__ void __launch_bounds__(kCsThreads, 1) cae_steps_staged_kernel(const _
       for (int s = warp; s < S; s += kCsWarps) cs_step_entry_row(a, csm, s, step + 1, abn, D, A);
     }
   }
+  if (a.dec.enabled) {
+    // every CTA of the cluster is past its last block before any peer writes
+    // decode activations into the (now dead) weight buffers
+    if (nc > 1) cluster_barrier(); else __syncthreads();
+    cs_decode_epilogue(a, csm, b, nc);
+  }
   if (nc > 1) cluster_barrier();  // no CTA leaves while a peer could still address its shared memory
 }
 
@@ -797,6 +1028,11 @@ void cae_tensor_table(int D, int HD, int F, CaeStagePlan* p) {
   tensor(17, 1, D, D, cf);
   p->a_floats = ca;
   p->f_floats = cf;
+}
+
+int cae_decode_floats(const CaeDecode& d, int nc) {
+  int a, b, l, w, st;
+  return dec_layout(d, nc, &a, &b, &l, &w, &st);
 }
 
 bool cae_staged_plan(const CaeStepArgs& a, CaeStagePlan* out) {

@@ -69,8 +69,25 @@ constexpr int kCaeCtxRows = 16;     // context tokens per CTA on the split path
 // Split context path eligibility (sets a.tk); false keeps the single-kernel path.
 bool cae_ctx_split_setup(CaeCtxArgs* a);
 
+// Action-VAE decode of the final latents in the staged step kernel's epilogue
+// (ActionDecoder.forward, action_ae.py:123-166, one upsampling stage): the
+// CTAs of a sample's cluster split the hidden channels in whole GroupNorm
+// groups and exchange activations through distributed shared memory.
+struct CaeDecode {
+  int enabled;
+  int hidden, latent, tokens, stride, horizon, action_dim;
+  const float *in_w, *in_b, *out_w, *out_b, *suite_embed;
+  const int32_t* suite_ids;        // [B] or null
+  const float *convt_w, *convt_b, *gn0_w, *gn0_b, *c1_w, *c1_b, *gn1_w, *gn1_b, *c2_w, *c2_b, *gn2_w, *gn2_b;
+  float* out;                      // [B, horizon, action_dim]
+};
+// Shared-memory floats the epilogue decode needs (it uses the region before
+// the step kernel's row buffers, dead after the last block).
+int cae_decode_floats(const CaeDecode& d, int nc);
+
 struct CaeStepArgs {
   CaeWeightsDev w;
+  CaeDecode dec;
   CaeStagePlan plan;
   const float* wpack;              // packed block weights: staged kernel when non-null
   int* status;                     // bounded-wait failures (or null)

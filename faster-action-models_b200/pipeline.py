@@ -323,9 +323,10 @@ class CAEPipeline:
             _, _, hidden = self.video.engine().prefill(latents[s:e], t[s:e], context[s:e], cm,
                                                        return_hidden=True, cache_k=ks, cache_v=vs,
                                                        hidden=hid)
-            lat = self.expert.engine().chunk(noise[s:e].to(hidden.device, torch.float32),
-                                             self.ts, self.ds, hidden)
-            outs.append(self.ae.decode(lat))
+            # Euler loop + Action-VAE decode (the decode in the step kernel's epilogue)
+            _, actions = self.expert.engine().chunk_decode(noise[s:e].to(hidden.device, torch.float32),
+                                                           self.ts, self.ds, hidden, self.ae)
+            outs.append(actions)
         return torch.cat(outs)
 
 
@@ -393,6 +394,11 @@ class DiT4DiTPipeline:
             _, _, feats = self.backbone.engine().prefill(latents[s:e], t[s:e], context[s:e], cm,
                                                          return_hidden=True, cache_k=ks, cache_v=vs,
                                                          hidden=hid)
+            if self.head.is_compact() and self.ae is not None:
+                _, actions = self.head.engine().chunk_decode(noise[s:e].to(feats.device, torch.float32),
+                                                             self.ts, self.ds, feats, self.ae)
+                outs.append(actions)
+                continue
             if self.head.is_compact():
                 lat = self.head.engine().chunk(noise[s:e].to(feats.device, torch.float32),
                                                self.ts, self.ds, feats)

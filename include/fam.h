@@ -178,8 +178,12 @@ FAM_API int fam_attention(const fam_attention_desc* desc, void* workspace, size_
  * allocator).  No counterpart in the reference: its PyTorch path allocates
  * freely.  The split partials live in a static device array of 8 MiB per GPU
  * (held by every GPU that loads the library until exit); calls needing more
- * are rejected with FAM_ERR_INVALID.  Allocates nothing.  The first call on a
- * device looks the array up and should precede any stream capture there.
+ * are rejected with FAM_ERR_INVALID.  Allocates nothing.  Every call outside a
+ * stream capture looks the array's address up (a reset context is followed);
+ * make one call on each device before any capture there, and at start-up:
+ * under CUDA's lazy module loading that first call loads the library's device
+ * image, this array included.  Runs the split-KV mma.sync kernel (not the
+ * tcgen05 long-self-attention kernel, which needs a transposed-V workspace).
  * All calls on a device share the array: calls that overlap on the GPU race. */
 FAM_API int fam_attention_static_scratch(const fam_attention_desc* desc, void* stream);
 
@@ -423,6 +427,27 @@ FAM_API int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w
                           const float* timesteps, const float* deltas, int32_t num_steps,
                           float* velocity_trace, void* workspace, size_t workspace_bytes,
                           void* stream);
+
+/* fam_cae_chunk followed by the Action-VAE decode of the final latents
+ * (FastWAM.decode_action_latents -> ActionAE.decode, fastwam.py:855-863,
+ * action_ae.py:154-187): actions f32 [B, horizon, A], suite_ids int32 [B] or
+ * NULL.  When the decoder has one upsampling stage of even stride and its
+ * hidden channels split into whole GroupNorm groups over the CTAs of a
+ * sample's cluster, the decode runs in the epilogue of the staged step kernel
+ * (no further launch); otherwise the decoder's own kernels follow.
+ * *decode_fused (may be NULL) reports which.  `latent` receives the final
+ * latents either way.  Workspace: fam_cae_decode_workspace_size. */
+FAM_API int fam_cae_decode_workspace_size(const fam_action_config* cfg, const struct fam_decoder_config* dcfg,
+                                          const struct fam_decoder_weights* dw, int32_t batch,
+                                          int32_t context_tokens, size_t* bytes);
+FAM_API int fam_cae_chunk_decode(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch,
+                                 int32_t tokens, const void* context, int32_t context_bf16,
+                                 int32_t context_tokens, const uint8_t* context_mask, float* latent,
+                                 const float* timesteps, const float* deltas, int32_t num_steps,
+                                 float* velocity_trace, const struct fam_decoder_config* dcfg,
+                                 const struct fam_decoder_weights* dw, const int32_t* suite_ids,
+                                 float* actions, int32_t* decode_fused, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* Status word of the last fam_cae_chunk on this workspace (synchronizes the
  * stream): 0, or nonzero when a bounded device wait (a bulk copy that did not

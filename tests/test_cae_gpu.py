@@ -139,3 +139,58 @@ def test_cae_shapes_vs_oracle(D, H, hd, F, L, S, C, B, N, masked):
     assert eng.status() == 0
     _close(trace, torch.stack(vel))
     _close(lat, x)
+
+
+def test_chunk_decode_in_step_kernel_epilogue():
+    """fam_cae_chunk_decode: the Action-VAE decode in the staged step kernel's epilogue.
+    The config-0 golden (one-CTA cluster) and full config 0 (512-key context: a 4-CTA
+    cluster splitting the 256 decoder channels) give the reference's / the oracle's chunk
+    and the same chunk as the separate decoder launches; a decoder with two upsampling
+    stages takes the separate launches (decode_fused False) with the same result."""
+    fx = torch.load(GOLDEN / "c0_cae_expert.pt", weights_only=False)
+    dit = M.ActionDiT(**fx["dit_cfg"])
+    dit.load_state_dict({k: v.float() for k, v in fx["dit"].items()})
+    dit = dit.cuda()
+    c = fx["dec_cfg"]
+    ae = M.ActionAE(M.ActionAEConfig(action_dim=c["action_dim"], action_horizon=c["action_horizon"],
+                                     num_tokens=c["num_tokens"], latent_dim=c["latent_dim"],
+                                     decoder_hidden=c["decoder_hidden"], video_cond_dim=0, variational=True))
+    ae.load_state_dict({k: v.float() for k, v in fx["ae"].items()})
+    ae = ae.cuda()
+    eng = dit.engine()
+    ts, ds = fx["timesteps"].tolist(), fx["deltas"].tolist()
+    lat, chunk = eng.chunk_decode(fx["noise"].cuda(), ts, ds, fx["context"].float().cuda(), ae)
+    torch.cuda.synchronize()
+    assert eng.decode_fused
+    _close(lat, fx["latent"])
+    _close(chunk, fx["chunk"])
+
+    torch.manual_seed(0)
+    dit = M.ActionDiT(hidden_dim=32, action_dim=16, ffn_dim=128, text_dim=3072, freq_dim=256,
+                      eps=1e-6, num_heads=4, attn_head_dim=8, num_layers=8)
+    cfg = O.DiTConfig(hidden_dim=32, ffn_dim=128, num_heads=4, attn_head_dim=8, num_layers=8,
+                      text_dim=3072, action_dim=16)
+    ae = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16,
+                                     decoder_hidden=256, video_cond_dim=0, variational=True))
+    g = torch.Generator().manual_seed(0)
+    ctx = torch.randn(2, 512, 3072, generator=g)
+    noise = torch.randn(2, 8, 16, generator=g)
+    sd = {k: v.float() for k, v in dit.state_dict().items()}
+    dsd = {k: v.float() for k, v in ae.state_dict().items()}
+    ref_chunk = O.cae_chunk(sd, cfg, dsd, O.DecoderConfig(7, 32, 8, 16, 256), noise, ctx, num_steps=4, shift=1.0)
+    dit, ae = dit.cuda(), ae.cuda()
+    ts, ds = M.build_inference_schedule(4, 1.0, dtype=torch.float32)
+    eng = dit.engine()
+    for _ in range(2):  # a second call finds the first one's leftovers in the staging buffers
+        lat, chunk = eng.chunk_decode(noise.cuda(), ts, ds, ctx.cuda(), ae)
+        torch.cuda.synchronize()
+        assert eng.decode_fused
+        _close(chunk, ref_chunk)
+        _close(chunk, ae.decode(lat))
+
+    ae2 = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=64, num_tokens=8, latent_dim=16,
+                                      decoder_hidden=64, video_cond_dim=0, variational=True)).cuda()
+    lat2, chunk2 = eng.chunk_decode(noise.cuda(), ts, ds, ctx.cuda(), ae2)
+    torch.cuda.synchronize()
+    assert not eng.decode_fused  # 64 / 8 = strides 4 and 2, two upsampling stages: separate launches
+    _close(chunk2, ae2.decode(lat2))
