@@ -126,7 +126,8 @@ class DecoderStage(C.Structure):
 
 class DecoderWeights(C.Structure):
     _fields_ = [("in_w", fp), ("in_b", fp), ("out_w", fp), ("out_b", fp), ("suite_embed", fp),
-                ("stages", C.POINTER(DecoderStage)), ("num_stages", C.c_int32)]
+                ("stages", C.POINTER(DecoderStage)), ("num_stages", C.c_int32),
+                ("latent_std", fp), ("latent_mean", fp)]
 
 
 def declare_cae(lib) -> None:
@@ -145,7 +146,7 @@ def declare_cae(lib) -> None:
     lib.fam_cae_chunk_decode.argtypes = [C.POINTER(ActionConfig), C.POINTER(CaeWeights), i32, i32, vp,
                                          i32, i32, vp, vp, C.POINTER(C.c_float), C.POINTER(C.c_float),
                                          i32, vp, C.POINTER(DecoderConfig), C.POINTER(DecoderWeights), vp, vp,
-                                         C.POINTER(i32), vp, sz, vp]
+                                         i32, C.POINTER(i32), vp, sz, vp]
     for n in ("fam_cae_workspace_size", "fam_cae_chunk", "fam_cae_status", "fam_decoder_workspace_size",
               "fam_action_decode", "fam_cae_decode_workspace_size", "fam_cae_chunk_decode"):
         getattr(lib, n).restype = C.c_int

@@ -38,7 +38,12 @@ __global__ void dec_input_kernel(const __grid_constant__ DecArgs a, float* x) {
     const int c = i / T, t = i % T;
     float acc = a.in_b[c];
     const float* zr = a.z + (static_cast<long long>(b) * T + t) * Z;
-    for (int k = 0; k < Z; ++k) acc += a.in_w[c * Z + k] * zr[k];
+    if (a.lat_std != nullptr) {
+      for (int k = 0; k < Z; ++k)
+        acc += a.in_w[c * Z + k] * __fadd_rn(__fmul_rn(zr[k], a.lat_std[t * Z + k]), a.lat_mean[t * Z + k]);
+    } else {
+      for (int k = 0; k < Z; ++k) acc += a.in_w[c * Z + k] * zr[k];
+    }
     if (sid >= 0) acc += a.suite_embed[static_cast<long long>(sid) * h + c];
     x[(static_cast<long long>(b) * h + c) * T + t] = acc;
   }
@@ -154,6 +159,7 @@ struct DecLayerArgs {
   const float *gn_w, *gn_b;
   float* xsave;           // mode 1: the built input of this CTA's channels (the block's skip), or null
   const float *z, *in_w, *in_b, *suite_embed;
+  const float *lat_std, *lat_mean;  // [Lin, Z] or null: z * std + mean is decoded
   const int32_t* suite_ids;
   int Z;
   const float *w, *bias;  // convT: [h, h, 2s]; conv3: [h, h, 3]
@@ -179,7 +185,10 @@ __device__ void dl_build_input(const DecLayerArgs& a, float* x, float* stat) {
     // input_proj: the token rows of z first (shared), then one output per thread;
     // the weight row of each output is read with independent loads
     float* zs = stat + 16;  // [Lin][Z] (the stat area is followed by room for it)
-    for (int i = threadIdx.x; i < Lin * a.Z; i += kDlThreads) zs[i] = a.z[static_cast<long long>(b) * Lin * a.Z + i];
+    for (int i = threadIdx.x; i < Lin * a.Z; i += kDlThreads) {
+      const float zv = a.z[static_cast<long long>(b) * Lin * a.Z + i];
+      zs[i] = a.lat_std != nullptr ? __fadd_rn(__fmul_rn(zv, a.lat_std[i]), a.lat_mean[i]) : zv;
+    }
     __syncthreads();
     const int sid = (a.suite_ids != nullptr && a.suite_embed != nullptr) ? a.suite_ids[b] : -1;
     for (int i = threadIdx.x; i < n; i += kDlThreads) {
@@ -424,6 +433,8 @@ static bool decoder_wide(const DecArgs& a, cudaStream_t st, cudaError_t* err) {
   c.h = h;
   c.G = G;
   c.z = a.z;
+  c.lat_std = a.lat_std;
+  c.lat_mean = a.lat_mean;
   c.in_w = a.in_w;
   c.in_b = a.in_b;
   c.suite_embed = a.suite_embed;

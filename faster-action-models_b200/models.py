@@ -790,12 +790,18 @@ class CAEEngine:
         self._last = (B, C_)
         return (lat, trace) if return_trace else lat
 
+    DECODE_MODES = {"auto": 0, "fused": 1, "separate": 2}
+
     def chunk_decode(self, latents, timesteps: Sequence[float], deltas: Sequence[float], context, ae: "ActionAE",
-                     context_mask=None, suite_ids=None):
-        """The Euler loop and ActionAE.decode of the final latents (fam_cae_chunk_decode): the
-        decode runs in the step kernel's epilogue when the decoder qualifies (one upsampling
-        stage), else its own kernels follow.  Returns (fp32 latents [B, S, A], fp32 actions
-        [B, horizon, action_dim]); self.decode_fused tells which way the decode ran."""
+                     context_mask=None, suite_ids=None, decode: str = "auto"):
+        """The Euler loop and ActionAE.decode of the final latents (fam_cae_chunk_decode).  The
+        decode can run in the step kernel's epilogue when the decoder qualifies (one upsampling
+        stage of stride 2 or 4); decode="auto" takes it at batch >= 4 (where it beats the
+        separate launches), "fused" whenever it qualifies, "separate" never.
+        Returns (fp32 latents [B, S, A], fp32 actions [B, horizon, action_dim]);
+        self.decode_fused tells which way the decode ran."""
+        if decode not in self.DECODE_MODES:
+            raise ValueError(f"decode must be one of {sorted(self.DECODE_MODES)}")
         lat = latents.to(device=self.dev, dtype=torch.float32).clone()
         B, S, A = lat.shape
         ctx = context if context.is_cuda and context.dtype in (torch.bfloat16, torch.float32) \
@@ -806,6 +812,7 @@ class CAEEngine:
         if context_mask is not None:
             cm = context_mask.to(device=self.dev, dtype=torch.uint8).expand(B, C_).contiguous()
         dec = ae.decoder
+        dec.check_ids(suite_ids)
         if dec._packed is None:
             dec._pack()
         dcfg, dw, _, _ = dec._packed
@@ -828,7 +835,8 @@ class CAEEngine:
                                          cm.data_ptr() if cm is not None else None, lat.data_ptr(), ts, ds, N,
                                          None, C.byref(dcfg), C.byref(dw),
                                          sid.data_ptr() if sid is not None else None, out.data_ptr(),
-                                         C.byref(fused), self.ws.data_ptr(), self.ws.numel(), C.c_void_p(st)),
+                                         self.DECODE_MODES[decode], C.byref(fused), self.ws.data_ptr(),
+                                         self.ws.numel(), C.c_void_p(st)),
               "fam_cae_chunk_decode")
         self.decode_fused = bool(fused.value)
         self._hold = (ctx, cm, sid)
@@ -947,6 +955,11 @@ class ActionDecoder(nn.Module):
         if cfg.num_suites > 0:
             self.suite_embed = nn.Embedding(cfg.num_suites, cfg.decoder_hidden)
             nn.init.zeros_(self.suite_embed.weight)
+        # DiT4DiT's decoder (ActionAE.from_dit4dit): latent statistics applied inside the
+        # kernels, and task ids required when the decoder holds a task embedding
+        self.register_buffer("latent_std", None, persistent=False)
+        self.register_buffer("latent_mean", None, persistent=False)
+        self.require_suite_ids = False
         self._packed = None
         self.register_load_state_dict_post_hook(lambda m, k: setattr(m, "_packed", None))
 
@@ -980,14 +993,23 @@ class ActionDecoder(nn.Module):
         w.suite_embed = ptr(self.suite_embed.weight) if self.suite_embed is not None else None
         w.stages = stages
         w.num_stages = len(self.strides)
+        if self.latent_std is not None:
+            w.latent_std, w.latent_mean = ptr(self.latent_std), ptr(self.latent_mean)
         c = self.cfg
         cfg = _abi.DecoderConfig(c.action_dim, c.action_horizon, c.num_tokens, c.latent_dim,
                                  c.decoder_hidden, c.num_suites)
         self._packed = (cfg, w, stages, keep)
 
+    def check_ids(self, suite_ids) -> None:
+        """DiT4DiT's decoder refuses to run without task ids when it holds a task
+        embedding (action_vae.py:168-172); FastWAM's skips the embedding instead."""
+        if self.require_suite_ids and suite_ids is None:
+            raise ValueError("task_ids are required for a task-conditioned ActionVAE")
+
     def forward(self, z: torch.Tensor, suite_ids: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not z.is_cuda:
             raise RuntimeError("ActionDecoder runs on CUDA through libfam")
+        self.check_ids(suite_ids)
         if self._packed is None:
             self._pack()
         cfg, w, _, _ = self._packed
@@ -1020,6 +1042,62 @@ class ActionAE(nn.Module):
 
     def decode(self, z: torch.Tensor, suite_ids: Optional[torch.Tensor] = None) -> torch.Tensor:
         return self.decoder(z, suite_ids=suite_ids)
+
+    @classmethod
+    def from_dit4dit(cls, checkpoint, map_location="cpu") -> "ActionAE":
+        """DiT4DiT's ActionVAE as a decoder (DiT4DiT/model/modules/action_model/action_vae.py:
+        136-197), from the checkpoint that load_action_vae reads (action_vae.py:276-283):
+        {"config": ActionVAEConfig fields, "model": state_dict}, or a path to one.
+
+        The decoder's task embedding (conditioning_mode "encoder_decoder") loads as the suite
+        embedding and task ids become required at decode time, as in DiT4DiT.  When the
+        checkpoint sets apply_latent_normalization, its latent_mean / latent_std
+        ([num_tokens, latent_dim], std clamped at 1e-4, DiT4DiT/model/framework/DiT4DiT.py:
+        256-269) are applied to the latents inside the decode kernels, which is the
+        un-normalisation of DiT4DiT._decode_action_predictions (DiT4DiT.py:403-406).
+        DiT4DiT runs its encoder only to make training targets, so the returned model has
+        encoder None."""
+        import os
+        if isinstance(checkpoint, (str, os.PathLike)):
+            checkpoint = torch.load(checkpoint, map_location=map_location, weights_only=False)
+        c = dict(checkpoint["config"])
+        num_tasks = int(c.get("num_tasks", 0))
+        mode = c.get("conditioning_mode") or ("encoder_decoder" if num_tasks > 0 else "none")
+        if mode not in ("none", "encoder_only", "encoder_decoder"):
+            raise ValueError(f"conditioning_mode must be one of none, encoder_only, encoder_decoder; got {mode!r}")
+        if mode != "none" and num_tasks <= 0:
+            raise ValueError(f"conditioning_mode={mode!r} requires num_tasks > 0")
+        horizon, tokens = int(c.get("action_horizon", 16)), int(c.get("num_tokens", 4))
+        if horizon % tokens:
+            raise ValueError(f"action_horizon must be divisible by num_tokens, got {horizon} and {tokens}")
+        cfg = ActionAEConfig(action_dim=int(c.get("action_dim", 29)), action_horizon=horizon, num_tokens=tokens,
+                             latent_dim=int(c.get("latent_dim", 64)), encoder_hidden=int(c.get("encoder_hidden", 128)),
+                             decoder_hidden=int(c.get("decoder_hidden", 128)), video_cond_dim=0,
+                             variational=bool(c.get("variational", True)),
+                             num_suites=num_tasks if mode == "encoder_decoder" else 0)
+        ae = cls.__new__(cls)
+        nn.Module.__init__(ae)
+        ae.cfg = cfg
+        ae.encoder = None
+        ae.decoder = ActionDecoder(cfg)
+        sd = {}
+        for k, v in checkpoint["model"].items():
+            if k.startswith("decoder."):
+                k = k[len("decoder."):]
+                sd["suite_embed.weight" if k == "task_embedding.weight" else k] = v.float()
+        ae.decoder.load_state_dict(sd, strict=True)
+        ae.decoder.require_suite_ids = cfg.num_suites > 0
+        if checkpoint.get("apply_latent_normalization", False):
+            shape = (cfg.num_tokens, cfg.latent_dim)
+            mean = checkpoint.get("latent_mean", torch.zeros(shape)).float()
+            std = checkpoint.get("latent_std", torch.ones(shape)).float().clamp_min(1e-4)
+            while mean.dim() > 2 and mean.shape[0] == 1:
+                mean = mean[0]
+            while std.dim() > 2 and std.shape[0] == 1:
+                std = std[0]
+            ae.decoder.latent_mean = torch.broadcast_to(mean, shape).contiguous()
+            ae.decoder.latent_std = torch.broadcast_to(std, shape).contiguous()
+        return ae
 
 
 # ---------------------------------------------------------------- schedule

@@ -431,12 +431,20 @@ FAM_API int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w
 /* fam_cae_chunk followed by the Action-VAE decode of the final latents
  * (FastWAM.decode_action_latents -> ActionAE.decode, fastwam.py:855-863,
  * action_ae.py:154-187): actions f32 [B, horizon, A], suite_ids int32 [B] or
- * NULL.  When the decoder has one upsampling stage of even stride and its
- * hidden channels split into whole GroupNorm groups over the CTAs of a
- * sample's cluster, the decode runs in the epilogue of the staged step kernel
- * (no further launch); otherwise the decoder's own kernels follow.
- * *decode_fused (may be NULL) reports which.  `latent` receives the final
+ * NULL.  The decode can run in the epilogue of the staged step kernel (no
+ * further launch) when the decoder has one upsampling stage of stride 2 or 4
+ * and its hidden channels split into whole GroupNorm groups over the CTAs of a
+ * sample's cluster; otherwise the decoder's own kernels follow.  decode_mode:
+ * FAM_DECODE_AUTO takes the epilogue when it qualifies and batch >= 4 (each
+ * sample decodes on its own cluster of at most 4 SMs, flat in the batch,
+ * while the separate launches grow with it: they are as fast or faster at
+ * batch 1, the epilogue is faster at batch 16), FAM_DECODE_FUSED whenever it
+ * qualifies, FAM_DECODE_SEPARATE never.
+ * *decode_fused (may be NULL) reports which ran.  `latent` receives the final
  * latents either way.  Workspace: fam_cae_decode_workspace_size. */
+#define FAM_DECODE_AUTO 0
+#define FAM_DECODE_FUSED 1
+#define FAM_DECODE_SEPARATE 2
 FAM_API int fam_cae_decode_workspace_size(const fam_action_config* cfg, const struct fam_decoder_config* dcfg,
                                           const struct fam_decoder_weights* dw, int32_t batch,
                                           int32_t context_tokens, size_t* bytes);
@@ -446,7 +454,7 @@ FAM_API int fam_cae_chunk_decode(const fam_action_config* cfg, const fam_cae_wei
                                  const float* timesteps, const float* deltas, int32_t num_steps,
                                  float* velocity_trace, const struct fam_decoder_config* dcfg,
                                  const struct fam_decoder_weights* dw, const int32_t* suite_ids,
-                                 float* actions, int32_t* decode_fused, void* workspace,
+                                 float* actions, int32_t decode_mode, int32_t* decode_fused, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
 /* Status word of the last fam_cae_chunk on this workspace (synchronizes the
@@ -482,6 +490,12 @@ typedef struct fam_decoder_weights {
   const float* suite_embed;       /* [num_suites, h] or NULL */
   const fam_decoder_stage* stages;/* host array */
   int32_t num_stages;
+  /* Latent un-normalisation of DiT4DiT._decode_action_predictions
+   * (DiT4DiT/model/framework/DiT4DiT.py:403-406): when both are non-NULL the
+   * decoder reads z * latent_std + latent_mean (f32 [num_tokens, latent]; the
+   * product and the sum each rounded to f32) in place of z.  NULL for FastWAM's
+   * ActionAE, which decodes z as it is. */
+  const float *latent_std, *latent_mean;
 } fam_decoder_weights;
 
 FAM_API int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_decoder_weights* w,

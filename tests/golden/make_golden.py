@@ -33,6 +33,10 @@ Reference code paths exercised:
   fastwam_infer_action  FastWAM.infer_action end to end (VAE encode, proprio token, prefill,
         action Euler loop, Action-VAE decode) and its checkpoint payload, small shapes, bf16
         FastWAM/src/fastwam/models/wan22/fastwam.py:257-306, 1080-1274, 1300-1345
+  dit4dit_action_vae  DiT4DiT's ActionVAE.decode (task-conditioned, crop, two stages) and
+        the latent un-normalisation of DiT4DiT._decode_action_predictions           (fp32)
+        DiT4DiT/DiT4DiT/model/modules/action_model/action_vae.py:136-197, 276-283
+        DiT4DiT/DiT4DiT/model/framework/DiT4DiT.py:393-410
 """
 from __future__ import annotations
 
@@ -402,18 +406,92 @@ def make_fastwam(R):
             "action": out["action"], "action_latents": out["action_latents"]}
 
 
+def _import_dit4dit_action_vae(ref_root: Path):
+    """DiT4DiT's ActionVAE module, loaded from its file alone (its package __init__ files pull
+    in the VLM stack, which the decode never touches)."""
+    import importlib.util
+    path = ref_root / "DiT4DiT" / "DiT4DiT" / "model" / "modules" / "action_model" / "action_vae.py"
+    spec = importlib.util.spec_from_file_location("dit4dit_action_vae", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # dataclass resolution needs the module registered
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def make_dit4dit_vae(ref_root: Path):
+    """DiT4DiT ActionVAE.decode (DiT4DiT/model/modules/action_model/action_vae.py:136-197), fp32,
+    in the shapes that exercise every branch of the decoder: the config-3 compact chunk
+    (8 x 48 latents -> 16 x 29) with the decoder's task embedding (conditioning_mode
+    "encoder_decoder"), an "encoder_only" model whose decoder ignores task ids, a stride-3
+    ConvTranspose1d whose 3L + 1 output is cropped, and two upsampling stages (3, 3) with a
+    crop.  (The zero-pad branch of decode is unreachable through ActionVAE, whose encoder
+    requires the horizon to be a multiple of num_tokens.)  Each case saves the reference's
+    checkpoint layout ({"config": ActionVAEConfig.to_dict(), "model": state_dict}, as
+    load_action_vae reads it, action_vae.py:276-283).  The config-3 case also records
+    DiT4DiT._decode_action_predictions' latent un-normalisation followed by the decode
+    (DiT4DiT/model/framework/DiT4DiT.py:403-407)."""
+    V = _import_dit4dit_action_vae(ref_root)
+    cases = {
+        "c3_task_conditioned": dict(action_dim=29, action_horizon=16, num_tokens=8, latent_dim=48,
+                                    encoder_hidden=32, decoder_hidden=64, num_tasks=3,
+                                    conditioning_mode="encoder_decoder", batch=3),
+        "encoder_only": dict(action_dim=7, action_horizon=32, num_tokens=8, latent_dim=16, encoder_hidden=32,
+                             decoder_hidden=32, num_tasks=2, conditioning_mode="encoder_only", batch=2),
+        "stride3_crop": dict(action_dim=5, action_horizon=12, num_tokens=4, latent_dim=8, encoder_hidden=32,
+                             decoder_hidden=32, batch=2),
+        "two_stage_crop": dict(action_dim=6, action_horizon=18, num_tokens=2, latent_dim=8, encoder_hidden=32,
+                               decoder_hidden=32, batch=2),
+    }
+    out = {"kind": "dit4dit_action_vae", "cases": {}}
+    for i, (name, kw) in enumerate(cases.items()):
+        kw = dict(kw)
+        B = kw.pop("batch")
+        torch.manual_seed(100 + i)
+        cfg = V.ActionVAEConfig(**kw)
+        vae = V.ActionVAE(cfg).eval()
+        g = torch.Generator().manual_seed(200 + i)
+        with torch.no_grad():
+            # GroupNorm affines and the (zero-initialised) task embeddings get values, so
+            # every parameter changes the output
+            for mod in vae.modules():
+                if isinstance(mod, torch.nn.GroupNorm):
+                    mod.weight.copy_(1.0 + 0.2 * torch.randn(mod.weight.shape, generator=g))
+                    mod.bias.copy_(0.2 * torch.randn(mod.bias.shape, generator=g))
+                elif isinstance(mod, torch.nn.Embedding):
+                    mod.weight.copy_(0.5 * torch.randn(mod.weight.shape, generator=g))
+        _round_params_bf16(vae)
+        z = torch.randn(B, cfg.num_tokens, cfg.latent_dim, generator=g)
+        task_ids = torch.randint(0, max(1, cfg.num_tasks), (B,), generator=g) if cfg.num_tasks > 0 else None
+        with torch.no_grad():
+            actions = vae.decode(z, task_ids=task_ids)
+        rec = {"checkpoint": {"config": cfg.to_dict(),
+                              "model": {k: v.detach().clone() for k, v in vae.state_dict().items()}},
+               "latent": z, "task_ids": task_ids, "actions": actions}
+        if name == "c3_task_conditioned":
+            # per token and channel, as DiT4DiT registers them (DiT4DiT.py:256-266)
+            mean = 0.3 * torch.randn(cfg.num_tokens, cfg.latent_dim, generator=g)
+            std = 0.5 + torch.rand(cfg.num_tokens, cfg.latent_dim, generator=g)
+            with torch.no_grad():
+                rec["actions_denorm"] = vae.decode(z * std + mean, task_ids=task_ids)
+            rec["checkpoint"].update(latent_mean=mean, latent_std=std, apply_latent_normalization=True)
+        out["cases"][name] = rec
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True,
                     help="root of the reference project checkout (holds FastWAM/src)")
     ap.add_argument("--only", nargs="*", default=None, help="fixture names to (re)generate")
     args = ap.parse_args()
-    R = _import_reference(Path(args.reference))
+    ref_root = Path(args.reference)
+    R = _import_reference(ref_root)
     torch.set_num_threads(4)
     for name, fn in (("c0_cae_expert", make_c0), ("c1_action_cache", make_c1),
                      ("c2_video_prefill", make_c2), ("primitives", make_primitives),
                      ("vae_encode", make_vae), ("joint_step", make_joint), ("idm_step", make_idm),
-                     ("fastwam_infer_action", make_fastwam)):
+                     ("fastwam_infer_action", make_fastwam),
+                     ("dit4dit_action_vae", lambda _: make_dit4dit_vae(ref_root))):
         if args.only is not None and name not in args.only:
             continue
         fx = fn(R)

@@ -164,3 +164,27 @@ def test_fastwam_checkpoint_layout_and_mot_checks():
                            context_mask=torch.ones(1, 4, dtype=torch.bool))
     with pytest.raises(ValueError, match="last dim must be 8"):
         model.infer_action(None, torch.zeros(1, 3, 64, 96), 32, proprio=torch.zeros(1, 5))
+
+
+def test_dit4dit_action_vae_loader():
+    """ActionAE.from_dit4dit reads DiT4DiT's ActionVAE checkpoint layout: decoder weights with
+    the task embedding as the suite embedding, task ids required when the decoder holds one,
+    the latent statistics held for the kernels, and DiT4DiT's config checks."""
+    fx = torch.load(GOLDEN / "dit4dit_action_vae.pt", weights_only=False)["cases"]
+    ck = fx["c3_task_conditioned"]["checkpoint"]
+    ae = M.ActionAE.from_dit4dit(ck)
+    assert ae.encoder is None and ae.decoder.require_suite_ids
+    assert (ae.cfg.action_dim, ae.cfg.action_horizon, ae.cfg.num_tokens, ae.cfg.latent_dim) == (29, 16, 8, 48)
+    assert torch.equal(ae.decoder.suite_embed.weight, ck["model"]["decoder.task_embedding.weight"])
+    assert torch.equal(ae.decoder.latent_std, ck["latent_std"].clamp_min(1e-4))
+    assert torch.equal(ae.decoder.latent_mean, ck["latent_mean"])
+    assert "latent_std" not in ae.decoder.state_dict()
+    with pytest.raises(ValueError, match="task_ids are required"):
+        ae.decoder.check_ids(None)
+    eo = M.ActionAE.from_dit4dit(fx["encoder_only"]["checkpoint"])
+    assert eo.decoder.suite_embed is None and not eo.decoder.require_suite_ids and eo.decoder.latent_std is None
+    bad = {"config": dict(ck["config"], action_horizon=18), "model": ck["model"]}
+    with pytest.raises(ValueError, match="divisible"):
+        M.ActionAE.from_dit4dit(bad)
+    with pytest.raises(ValueError, match="requires num_tasks"):
+        M.ActionAE.from_dit4dit({"config": dict(ck["config"], num_tasks=0), "model": ck["model"]})

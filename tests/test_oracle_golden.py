@@ -181,3 +181,33 @@ def test_oracle_infer_action_matches_reference_fastwam():
                               fx["action_infer_shift"], fx["seed"])
     assert torch.equal(lat, fx["action_latents"])
     assert torch.equal(act, fx["action"])
+
+
+def dit4dit_decoder_params(ckpt):
+    """DiT4DiT ActionVAE checkpoint -> (oracle decoder params, DecoderConfig, whether the decoder
+    takes task ids): the decoder's task_embedding is the oracle's suite embedding."""
+    c = ckpt["config"]
+    cond = c["conditioning_mode"] == "encoder_decoder"
+    p = {}
+    for k, v in ckpt["model"].items():
+        if k.startswith("decoder."):
+            p[k.replace("decoder.task_embedding.", "decoder.suite_embed.")] = v.float()
+    cfg = O.DecoderConfig(c["action_dim"], c["action_horizon"], c["num_tokens"], c["latent_dim"],
+                          c["decoder_hidden"], c["num_tasks"] if cond else 0)
+    return p, cfg, cond
+
+
+@pytest.mark.parametrize("case", ["c3_task_conditioned", "encoder_only", "stride3_crop", "two_stage_crop"])
+def test_dit4dit_action_vae_decode_matches_reference(case):
+    """The oracle's decoder reproduces DiT4DiT's ActionVAE.decode (action_vae.py:136-197) on
+    the fixture made from the reference module: task-conditioned, task ids ignored by an
+    "encoder_only" decoder, a stride-3 crop and two upsampling stages; and the latent
+    un-normalisation of DiT4DiT._decode_action_predictions (DiT4DiT.py:403-406)."""
+    fx = _load("dit4dit_action_vae")["cases"][case]
+    p, cfg, cond = dit4dit_decoder_params(fx["checkpoint"])
+    ids = fx["task_ids"] if cond else None
+    _same(O.action_decode(p, cfg, fx["latent"], suite_ids=ids), fx["actions"], atol=1e-6)
+    if "actions_denorm" in fx:
+        ck = fx["checkpoint"]
+        z = fx["latent"] * ck["latent_std"].clamp_min(1e-4) + ck["latent_mean"]
+        _same(O.action_decode(p, cfg, z, suite_ids=ids), fx["actions_denorm"], atol=1e-6)
