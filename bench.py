@@ -403,12 +403,16 @@ def sub_c0(dev, peaks):
     noise = torch.randn(1, 8, 16, generator=g).to(dev)
     ts, ds = M.build_inference_schedule(CAE_STEPS, CAE_SHIFT, dtype=torch.float32)
     eng = exp.engine()
-    ms = time_calls(lambda: ae.decode(eng.chunk(noise, ts, ds, ctx)), 50, warmup=5)
+    ms = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae), 50, warmup=5)
+    fused = eng.decode_fused
+    ms_fused = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae, decode="fused"), 50, warmup=5)
     cpu_ms, cores, n = cpu_c0_ms()
     by = c0_bytes()
     return {"workload": "BASELINE configs[0]: CAE expert (hidden 32, 4 x 8 heads, 8 blocks) over a 512 x 3072 "
                         "context, 4 Euler steps + Action-VAE decode (hidden 256) -> 32 x 7, batch 1, fp32",
+            "decode": "step-kernel epilogue" if fused else "separate launches (decode=auto)",
             "latency_p50_ms": p50(ms), "chunks_per_s": 1e3 / p50(ms), "reps": len(ms),
+            "epilogue_decode_p50_ms": p50(ms_fused),
             "roofline": {"bound": "latency (HBM floor shown)", "bytes_per_chunk": by,
                          "floor_ms": by / (peaks["hbm"] * 1e9) * 1e3,
                          "achieved_gbs": by / (p50(ms) * 1e-3) / 1e9,
@@ -547,7 +551,10 @@ def run_fam(args):
         out = step()
     torch.cuda.synchronize()
     assert out.shape == (B, 32, 7) and bool(torch.isfinite(out).all())
-    launches = (vid.engine().launch_count() + 3 + 4) * ((B + MICRO_BATCH - 1) // MICRO_BATCH)
+    # per micro-batch: the backbone's launches, the CAE context (2) and step (1) launches, and
+    # the decoder's input, 3 per upsampling stage and output launches unless it ran fused
+    dec_launches = 0 if exp.engine().decode_fused else 2 + 3 * len(ae.decoder.strides)
+    launches = (vid.engine().launch_count() + 3 + dec_launches) * ((B + MICRO_BATCH - 1) // MICRO_BATCH)
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -555,12 +562,14 @@ def run_fam(args):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed_steps")
         t0.record()
         for s, e in ev:
             s.record()
             step()
             e.record()
         t1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
@@ -656,7 +665,7 @@ def run_case(case: str, reps: int) -> None:
       gemm_qkv_pair_c2  the same on CTA pairs, as the prefill runs it
       attn_c2           ops.attention: 1760 tokens, 24 x 128 heads, first-frame-causal (352)
       xattn_c2          the backbone's cross attention: 1760 queries over 64 context keys
-      cae_c0            config 0: compact expert chunk + Action-VAE decode
+      cae_c0            config 0: compact expert chunk with the Action-VAE decode in its epilogue
       fused_c1          config 1: the fused chunk kernel (plain launches), `--euler-steps`
       prefill_c2        config 2: the 30-block backbone prefill, batch 1
       vae_c1            VideoVAE38 encode of one 512 x 704 observation frame (p50 printed)
@@ -702,7 +711,7 @@ def run_case(case: str, reps: int) -> None:
         ts, ds = M.build_inference_schedule(CAE_STEPS, CAE_SHIFT, dtype=torch.float32)
         eng = exp.engine()
         for _ in range(reps):
-            ae.decode(eng.chunk(noise, ts, ds, ctx))
+            eng.chunk_decode(noise, ts, ds, ctx, ae, decode="fused")
     elif case == "fused_c1":
         M_, dit, ck, cv, ctx, cm, noise, mask = build_c1(dev)
         eng = dit.engine()

@@ -63,30 +63,46 @@ int fam_cae_workspace_size(const fam_action_config* cfg, int32_t batch, int32_t 
 namespace {
 
 // Whether the decode can run in the staged step kernel's epilogue: one
-// upsampling stage of even stride, the sample's latents as the decoder input,
-// whole GroupNorm groups per CTA of the cluster, at most two outputs per
-// thread per layer, and the activations in the step kernel's dead buffers.
+// upsampling stage of stride 2 or 4, the sample's latents as the decoder input,
+// whole GroupNorm groups per CTA of the cluster, register-tiled conv tasks of
+// 32 channels x 16 positions that divide the 32 warps, the staged weights within a staging
+// buffer, and the decode's buffers in the step kernel's dead ones (everything
+// below the latent rows).
 bool cae_decode_fusable(const CaeStepArgs& sa, const fam_decoder_config& dc, const fam_decoder_weights& dw) {
   if (sa.wpack == nullptr || dw.num_stages != 1 || dw.stages == nullptr) return false;
-  const int s = dw.stages[0].stride, h = dc.hidden, nc = sa.plan.nc;
-  if (s < 2 || s % 2 || dc.num_tokens != sa.S || dc.latent_dim != sa.A || h % 4 || h % nc) return false;
-  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc, Lo = dc.num_tokens * s;
-  if (ch % cg || ch / cg > 32 || ch * Lo > 2 * 1024 || ch * 2 * s > 8192 || ch * 3 * 4 > 8192) return false;
-  if (dc.action_horizon <= 0 || dc.action_dim <= 0) return false;
+  const int s = dw.stages[0].stride, h = dc.hidden, nc = sa.plan.nc, T = dc.num_tokens, Z = dc.latent_dim;
+  if ((s != 2 && s != 4) || T != sa.S || Z != sa.A || h % 4 || h % nc) return false;
+  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc, Lo = T * s, K = 2 * s;
+  if (ch % cg || ch / cg > 32 || ch % 32 || Lo % 16) return false;
+  const int nt = (ch / 32) * (Lo / 16);                                    // conv tasks (DecTask)
+  if (nt > 32 || 32 % nt) return false;
+  if (ch * (4 * 3 + 4) > kDecChunk || ch * K > kDecChunk) return false;    // one staged chunk fits
+  if (32 / nt * 16 * 33 * nt > kDecStages * kDecChunk) return false;       // split partials
+  if (Z % 4 || h * Z > kDecChunk || T * Z > ch * Lo) return false;         // input_proj staging
+  if (dc.action_horizon <= 0 || dc.action_dim <= 0 || dc.action_dim * h > 2 * kDecChunk) return false;
   CaeDecode d;
   memset(&d, 0, sizeof(d));
   d.hidden = h;
-  d.tokens = dc.num_tokens;
+  d.tokens = T;
   d.stride = s;
-  return cae_decode_floats(d, nc) <= sa.plan.o_x;
+  return cae_decode_floats(d, nc) <= sa.plan.o_lat;
 }
+
+// FAM_DECODE_AUTO's rule.  The epilogue decodes each sample on its own
+// cluster (at most 4 SMs), so its time is flat in the batch; the separate
+// launches spread over h / 4 CTAs per sample and grow with it.  Measured on
+// B200 (config-0 expert, 4 Euler steps, 1760 x 3072 features): batch 1,
+// hidden 256: 747.8 us epilogue against 718.2 us separate (hidden 128: 708.2
+// against 708.0); batch 16, hidden 256: 1486.0 against 1578.2 us (hidden 128:
+// 1437.5 against 1482.0).  The crossover at hidden 256 is near batch 4.
+bool cae_decode_auto_fuses(int batch) { return batch >= 4; }
 
 int cae_chunk_impl(const fam_action_config* cfg, const fam_cae_weights* w, int32_t batch, int32_t tokens,
                    const void* context, int32_t context_bf16, int32_t context_tokens, const uint8_t* context_mask,
                    float* latent, const float* timesteps, const float* deltas, int32_t num_steps,
                    float* velocity_trace, void* workspace, size_t workspace_bytes, void* stream,
                    const fam_decoder_config* dcfg, const fam_decoder_weights* dw, const int32_t* suite_ids,
-                   float* actions, int32_t* decode_fused) {
+                   float* actions, int decode_mode, int32_t* decode_fused) {
   int rc = check_cae(cfg);
   if (rc) return rc;
   if (w == nullptr || w->layers == nullptr || latent == nullptr || timesteps == nullptr ||
@@ -182,7 +198,8 @@ int cae_chunk_impl(const fam_action_config* cfg, const fam_cae_weights* w, int32
     ca.plan = sa.plan;
     sa.wpack = wpack;
   }
-  const bool fuse = dcfg != nullptr && cae_decode_fusable(sa, *dcfg, *dw);
+  const bool fuse = dcfg != nullptr && decode_mode != FAM_DECODE_SEPARATE && cae_decode_fusable(sa, *dcfg, *dw) &&
+                    (decode_mode == FAM_DECODE_FUSED || cae_decode_auto_fuses(batch));
   if (fuse) {
     const fam_decoder_stage& g = dw->stages[0];
     CaeDecode& d = sa.dec;
@@ -211,6 +228,8 @@ int cae_chunk_impl(const fam_action_config* cfg, const fam_cae_weights* w, int32
     d.c2_b = g.c2_b;
     d.gn2_w = g.gn2_w;
     d.gn2_b = g.gn2_b;
+    d.lat_std = dw->latent_std;
+    d.lat_mean = dw->latent_mean;
     d.out = actions;
   }
   if (decode_fused != nullptr) *decode_fused = fuse ? 1 : 0;
@@ -235,7 +254,7 @@ int fam_cae_chunk(const fam_action_config* cfg, const fam_cae_weights* w, int32_
                   size_t workspace_bytes, void* stream) {
   return cae_chunk_impl(cfg, w, batch, tokens, context, context_bf16, context_tokens, context_mask, latent,
                         timesteps, deltas, num_steps, velocity_trace, workspace, workspace_bytes, stream, nullptr,
-                        nullptr, nullptr, nullptr, nullptr);
+                        nullptr, nullptr, nullptr, FAM_DECODE_SEPARATE, nullptr);
 }
 
 int fam_cae_decode_workspace_size(const fam_action_config* cfg, const fam_decoder_config* dcfg,
@@ -255,8 +274,11 @@ int fam_cae_chunk_decode(const fam_action_config* cfg, const fam_cae_weights* w,
                          const uint8_t* context_mask, float* latent, const float* timesteps, const float* deltas,
                          int32_t num_steps, float* velocity_trace, const fam_decoder_config* dcfg,
                          const fam_decoder_weights* dw, const int32_t* suite_ids, float* actions,
-                         int32_t* decode_fused, void* workspace, size_t workspace_bytes, void* stream) {
+                         int32_t decode_mode, int32_t* decode_fused, void* workspace, size_t workspace_bytes,
+                         void* stream) {
   if (dcfg == nullptr || dw == nullptr || actions == nullptr) return set_error("cae decode: null decoder argument");
+  if (decode_mode < FAM_DECODE_AUTO || decode_mode > FAM_DECODE_SEPARATE)
+    return set_error("cae decode: decode_mode must be FAM_DECODE_AUTO, _FUSED or _SEPARATE");
   size_t need = 0;
   int rc = fam_cae_decode_workspace_size(cfg, dcfg, dw, batch, context_tokens, &need);
   if (rc) return rc;
@@ -267,7 +289,7 @@ int fam_cae_chunk_decode(const fam_action_config* cfg, const fam_cae_weights* w,
                      dcfg->latent_dim, tokens, cfg->action_dim);
   return cae_chunk_impl(cfg, w, batch, tokens, context, context_bf16, context_tokens, context_mask, latent,
                         timesteps, deltas, num_steps, velocity_trace, workspace, workspace_bytes, stream, dcfg, dw,
-                        suite_ids, actions, decode_fused);
+                        suite_ids, actions, decode_mode, decode_fused);
 }
 
 int fam_cae_status(const fam_action_config* cfg, int32_t batch, int32_t context_tokens, const void* workspace,
@@ -289,6 +311,8 @@ int fam_decoder_workspace_size(const fam_decoder_config* cfg, const fam_decoder_
                                int32_t batch, size_t* bytes) {
   if (cfg == nullptr || w == nullptr || bytes == nullptr || batch <= 0) return set_error("decoder: bad argument");
   if (w->num_stages > kDecMaxStages) return set_error("decoder: at most %d stages", kDecMaxStages);
+  if ((w->latent_std == nullptr) != (w->latent_mean == nullptr))
+    return set_error("decoder: latent_std and latent_mean are given together or not at all");
   *bytes = 3 * align256(decoder_scratch_floats(*cfg, w->stages, w->num_stages, batch) * sizeof(float));
   return FAM_OK;
 }
@@ -313,6 +337,8 @@ int fam_action_decode(const fam_decoder_config* cfg, const fam_decoder_weights* 
   for (int i = 0; i < w->num_stages; ++i) a.stages[i] = w->stages[i];
   a.num_stages = w->num_stages;
   a.z = z;
+  a.lat_std = w->latent_std;
+  a.lat_mean = w->latent_mean;
   a.suite_ids = suite_ids;
   a.out = out;
   const size_t part = need / 3;

@@ -402,45 +402,53 @@ __device__ __forceinline__ void cs_step_entry_row(const CaeStepArgs& a, float* c
 // [rank h / nc, (rank + 1) h / nc) -- whole GroupNorm groups -- and writes each
 // stage's activations of its channels into every CTA's copy of the full
 // activation (st.shared::cluster), one cluster barrier per exchange.  Weights
-// stream from global (L2) through a double-buffered cp.async staging area.
-constexpr int kDecChunk = 8192;   // floats per weight staging buffer
+// stream from global (L2) through a ring of kDecStages cp.async staging
+// buffers, two chunks in flight while the third is used.  Every stage call
+// commits one group (empty past the last chunk), so "wait_group 2" always
+// means "chunk k has landed".  The decode's buffers end below the step
+// kernel's latent rows, which the input projection reads first.
+//
+// Both convolutions are register-tiled (DecTask): each weight value a lane
+// loads serves 16 positions; the input-channel splits are summed in a fixed
+// order, so the result does not depend on timing.
 constexpr float kDecGnEps = 1e-5f;
 
-__device__ __forceinline__ int dec_r4(int n) { return (n + 3) & ~3; }
+// Row strides of the input_proj output h0 [h][ht] and of the stage activations
+// xa / xb [h][xs]: the rows of 8 consecutive input channels (the 8 lane phases)
+// start in distinct shared-memory banks (ht odd; xs / 4 odd).
+__host__ __device__ inline int dec_ht(int T) { return T | 1; }
+__host__ __device__ inline int dec_xs(int Lo) { return (((Lo + 4) >> 2) & 1) ? Lo + 4 : Lo + 8; }
 
 __host__ __device__ int dec_layout(const CaeDecode& d, int nc, int* o_xa, int* o_xb, int* o_loc, int* o_w,
                                    int* o_st) {
-  const int h = d.hidden, Lo = d.tokens * d.stride, ch = h / nc;
-  int c = (h * d.tokens + 3) & ~3;
+  const int h = d.hidden, Lo = d.tokens * d.stride, ch = h / nc, xs = dec_xs(Lo);
+  int c = (h * dec_ht(d.tokens) + 3) & ~3;  // h0
   *o_xa = c;
-  c += h * Lo;
+  c += h * xs;
   *o_xb = c;
-  c += h * Lo;
+  c += h * xs;
   *o_loc = c;
   c += (ch * Lo + 3) & ~3;
   *o_w = c;
-  c += 2 * kDecChunk;
+  c += kDecStages * kDecChunk;
   *o_st = c;                        // GroupNorm (mean, rstd) per local group
   c += 16;
   return c;
 }
 
-// Stage rows [r0, r0 + nr) of a weight whose row r is the `len` floats at
-// src + r * rstride (16-byte aligned, len % 4 == 0) into dst (rows packed).
-__device__ __forceinline__ void dec_stage(float* dst, const float* src, long long rstride, int r0, int nr, int len) {
-  const int l4 = len >> 2;
-  for (int i = threadIdx.x; i < nr * l4; i += kCsThreads) {
-    const int r = i / l4, c = (i - r * l4) * 4;
-    cp_async16(dst + r * len + c, src + static_cast<long long>(r0 + r) * rstride + c, true);
-  }
+// Copy `n` contiguous floats (n % 4 == 0, both ends 16-byte aligned) into
+// shared memory with cp.async, as one commit group.
+__device__ __forceinline__ void dec_copy(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x * 4; i < n; i += kCsThreads * 4) cp_async16(dst + i, src + i, true);
   cp_async_commit();
 }
 
 // GroupNorm statistics of this CTA's groups of loc [ch][Lo] (warp g: group g),
-// then y = GN(loc) (* SiLU) written to rows [c0, c0 + ch) of `full` in every
-// CTA of the cluster (skip: add skip[c][p] after the norm).
+// then y = GN(loc) (* SiLU) written to rows [c0, c0 + ch) of `full` [h][xs] in
+// every CTA of the cluster (skip: add skip[c][p] after the norm), 4 positions
+// per store.
 __device__ void dec_norm_exchange(float* loc, float* full, const float* skip, const float* gw, const float* gb,
-                                  int ch, int c0, int Lo, int cg, bool act, float* st, int nc) {
+                                  int ch, int c0, int Lo, int xs, int cg, bool act, float* st, int nc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, ng = ch / cg, n = cg * Lo;
   if (warp < ng) {
     const float* v = loc + warp * n;
@@ -459,73 +467,209 @@ __device__ void dec_norm_exchange(float* loc, float* full, const float* skip, co
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ch * Lo; i += kCsThreads) {
-    const int cl = i / Lo, pp = i - cl * Lo, c = c0 + cl, g = cl / cg;
-    float y = (loc[i] - st[2 * g]) * st[2 * g + 1] * gw[c] + gb[c];
-    if (act) y = silu(y);
-    if (skip != nullptr) y += skip[c * Lo + pp];
-    full[c * Lo + pp] = y;
-    for (int r = 0; r < nc; ++r)
-      if (r != static_cast<int>(cluster_ctarank())) st_cluster_f32(cluster_map(full + c * Lo + pp, r), y);
+  const int me = nc > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  for (int i = threadIdx.x * 4; i < ch * Lo; i += kCsThreads * 4) {
+    const int cl = i / Lo, pp = i - cl * Lo, c = c0 + cl, g = cl / cg;  // Lo % 4 == 0: one channel
+    const float m = st[2 * g], r = st[2 * g + 1], w = gw[c], bb = gb[c];
+    const float4 x = *reinterpret_cast<const float4*>(loc + i);
+    float4 y = make_float4((x.x - m) * r * w + bb, (x.y - m) * r * w + bb, (x.z - m) * r * w + bb,
+                           (x.w - m) * r * w + bb);
+    if (act) y = make_float4(silu(y.x), silu(y.y), silu(y.z), silu(y.w));
+    if (skip != nullptr) {
+      const float4 k = *reinterpret_cast<const float4*>(skip + c * xs + pp);
+      y = make_float4(y.x + k.x, y.y + k.y, y.z + k.z, y.w + k.w);
+    }
+    float* dst = full + c * xs + pp;
+    *reinterpret_cast<float4*>(dst) = y;
+    for (int r2 = 0; r2 < nc; ++r2)
+      if (r2 != me) st_cluster_v4(cluster_map(dst, r2), y);
   }
   if (nc > 1) cluster_barrier(); else __syncthreads();
 }
 
-// Conv1d(h, h, 3, padding 1) of the full activation `in` [h][Lo] for this CTA's
-// output channels -> loc [ch][Lo] (+ bias); weight [h][h][3].
-__device__ void dec_conv3(const float* in, float* loc, float* wbuf, const float* w, const float* bias, int h, int c0,
-                          int ch, int Lo) {
-  const int cc = kDecChunk / (ch * 3) >= h ? h : (kDecChunk / (ch * 3)) & ~3;  // input channels per chunk
-  const int nchunk = (h + cc - 1) / cc;
-  float acc[2] = {0.f, 0.f};
-  // chunk k: rows co of the slice, columns [ci0 * 3, (ci0 + cc) * 3)
-  auto stage = [&](int k) {
-    const int ci0 = k * cc, n = min(cc, h - ci0);
-    float* dst = wbuf + (k & 1) * kDecChunk;
-    const int l4 = n * 3 / 4;
-    for (int i = threadIdx.x; i < ch * l4; i += kCsThreads) {
-      const int r = i / l4, c = (i - r * l4) * 4;
-      cp_async16(dst + r * n * 3 + c, w + (static_cast<long long>(c0 + r) * h + ci0) * 3 + c, true);
-    }
-    cp_async_commit();
-  };
-  stage(0);
-  for (int k = 0; k < nchunk; ++k) {
-    if (k + 1 < nchunk) stage(k + 1);
-    if (k + 1 < nchunk) cp_async_wait<1>(); else cp_async_wait<0>();
-    __syncthreads();
-    const int ci0 = k * cc, n = min(cc, h - ci0);
-    const float* wk = wbuf + (k & 1) * kDecChunk;
+// A conv task: lane = one output channel, 16 positions; warp w = task t = w mod
+// nt (a block of 32 channels x a tile of 16 positions) x input-channel split
+// s = w / nt (ns = 32 / nt splits).  Weight loads are then one row per lane
+// (128-bit, conflict-free) and activation loads broadcasts; the splits'
+// partials meet in `part` and are summed in split order.
+struct DecTask {
+  int nt, ns, t, s, cl, p0;
+};
+__device__ __forceinline__ DecTask dec_task(int ch, int Lo) {
+  DecTask k;
+  const int nb = ch / 32, warp = threadIdx.x >> 5;
+  k.nt = nb * (Lo / 16);
+  k.ns = kCsWarps / k.nt;
+  k.t = warp % k.nt;
+  k.s = warp / k.nt;
+  k.cl = (k.t % nb) * 32 + (threadIdx.x & 31);
+  k.p0 = (k.t / nb) * 16;
+  return k;
+}
+
+// The splits' partials -> loc [ch][Lo] (+ bias).  part [ns][nt][16][33] (rows of
+// 32 lanes padded to 33) is the staging ring, free once the last chunk is used.
+__device__ void dec_split_sum(const float (&acc)[16], const DecTask& k, float* part, float* loc, const float* bias,
+                              int c0, int ch, int Lo) {
+  float* my = part + (k.s * k.nt + k.t) * 16 * 33 + (threadIdx.x & 31);
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = threadIdx.x + u * kCsThreads;
-      if (i >= ch * Lo) break;
-      const int cl = i / Lo, pp = i - cl * Lo;
-      const float* wr = wk + cl * n * 3;
-      float a0 = 0.f;
-      for (int ci = 0; ci < n; ++ci) {
-        const float* xr = in + (ci0 + ci) * Lo;
-        const float xm = pp > 0 ? xr[pp - 1] : 0.f, x0 = xr[pp], xp = pp + 1 < Lo ? xr[pp + 1] : 0.f;
-        a0 = fmaf(wr[ci * 3 + 0], xm, a0);
-        a0 = fmaf(wr[ci * 3 + 1], x0, a0);
-        a0 = fmaf(wr[ci * 3 + 2], xp, a0);
-      }
-      acc[u] += a0;
-    }
-    __syncthreads();  // the buffer is refilled two chunks on
-  }
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int i = threadIdx.x + u * kCsThreads;
-    if (i < ch * Lo) loc[i] = acc[u] + bias[c0 + i / Lo];
+  for (int i = 0; i < 16; ++i) my[i * 33] = acc[i];
+  __syncthreads();
+  const int nb = ch / 32;
+  for (int j = threadIdx.x; j < ch * Lo; j += kCsThreads) {
+    const int cl = j / Lo, p = j - cl * Lo, t = (cl >> 5) + (p >> 4) * nb;
+    const float* src = part + (t * 16 + (p & 15)) * 33 + (cl & 31);
+    float v = 0.f;
+    for (int s = 0; s < k.ns; ++s) v += src[s * k.nt * 16 * 33];
+    loc[j] = v + bias[c0 + cl];
   }
   __syncthreads();
 }
 
+// Row stride of a staged Conv1d chunk [ch][n * 3] (n % 4 == 0): a multiple of 4
+// floats whose quarter is odd, so 8 consecutive lanes' rows are conflict-free.
+__device__ __forceinline__ int dec_r3(int n) { return ((n * 3 / 4) & 1) ? n * 3 : n * 3 + 4; }
+
+// Conv1d(h, h, 3, padding 1) of the full activation `in` [h][xs] for this CTA's
+// output channels -> loc [ch][Lo] (+ bias); weight [h][h][3], staged per chunk
+// of cc input channels as [ch][n * 3] rows.  A split takes groups of 4 input
+// channels (one lane loads 12 weights as three 128-bit loads).
+__device__ void dec_conv3(const float* in, float* loc, float* wbuf, const float* w, const float* bias, int h, int c0,
+                          int ch, int Lo, int xs) {
+  const DecTask k = dec_task(ch, Lo);
+  int cmax = 4;
+  while (ch * dec_r3(cmax + 4) <= kDecChunk && cmax + 4 <= h) cmax += 4;
+  const int cc = cmax >= 4 * k.ns ? cmax / (4 * k.ns) * (4 * k.ns) : cmax;  // equal groups per split
+  const int nchunk = (h + cc - 1) / cc;
+  float acc[16] = {};
+  auto stage = [&](int kk) {
+    if (kk < nchunk) {
+      const int ci0 = kk * cc, n = min(cc, h - ci0), r3 = dec_r3(n), l4 = n * 3 / 4;
+      float* dst = wbuf + (kk % kDecStages) * kDecChunk;
+      for (int i = threadIdx.x; i < ch * l4; i += kCsThreads) {
+        const int r = i / l4, c = (i - r * l4) * 4;
+        cp_async16(dst + r * r3 + c, w + (static_cast<long long>(c0 + r) * h + ci0) * 3 + c, true);
+      }
+    }
+    cp_async_commit();
+  };
+  stage(0);
+  stage(1);
+  for (int kk = 0; kk < nchunk; ++kk) {
+    stage(kk + 2);
+    cp_async_wait<2>();
+    __syncthreads();
+    const int ci0 = kk * cc, n = min(cc, h - ci0);
+    const float* wr = wbuf + (kk % kDecStages) * kDecChunk + k.cl * dec_r3(n);
+    for (int g = k.s; g < n / 4; g += k.ns) {
+      float wv[12];
+#pragma unroll
+      for (int f = 0; f < 3; ++f) {
+        const float4 t4 = *reinterpret_cast<const float4*>(wr + g * 12 + 4 * f);
+        wv[4 * f] = t4.x;
+        wv[4 * f + 1] = t4.y;
+        wv[4 * f + 2] = t4.z;
+        wv[4 * f + 3] = t4.w;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float* xr = in + (ci0 + 4 * g + c) * xs + k.p0;
+        float xv[18];
+        xv[0] = k.p0 > 0 ? xr[-1] : 0.f;
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+          const float4 t4 = *reinterpret_cast<const float4*>(xr + 4 * f);
+          xv[1 + 4 * f] = t4.x;
+          xv[2 + 4 * f] = t4.y;
+          xv[3 + 4 * f] = t4.z;
+          xv[4 + 4 * f] = t4.w;
+        }
+        xv[17] = k.p0 + 16 < Lo ? xr[16] : 0.f;
+        const float w0 = wv[3 * c], w1 = wv[3 * c + 1], w2 = wv[3 * c + 2];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(w2, xv[i + 2], fmaf(w1, xv[i + 1], fmaf(w0, xv[i], acc[i])));
+      }
+    }
+    __syncthreads();  // the buffer is refilled three chunks on
+  }
+  dec_split_sum(acc, k, wbuf, loc, bias, c0, ch, Lo);
+}
+
+// Stage ConvTranspose1d chunk kk (input channels [kk cc, kk cc + n)) as rows
+// [ci][ch * K] into ring buffer kk mod kDecStages; channel c's taps are K / 4
+// 16-byte units at 4-float unit c K / 4 (+ half ^ bit 2 of c when K = 8, so 8
+// consecutive lanes' loads are conflict-free).  One commit group, empty past
+// the last chunk.
+__device__ __forceinline__ int dec_tunit(int c, int half, int K) {
+  return K == 8 ? 2 * c + (half ^ ((c >> 2) & 1)) : c * (K / 4) + half;
+}
+__device__ __forceinline__ int dec_convt_cc(int h, int ch, int K) {
+  return kDecChunk / (ch * K) >= h ? h : kDecChunk / (ch * K);
+}
+__device__ __forceinline__ void dec_convt_stage(float* wbuf, const float* w, int h, int c0, int ch, int K, int kk) {
+  const int cc = dec_convt_cc(h, ch, K);
+  if (kk * cc < h) {
+    const int ci0 = kk * cc, n = min(cc, h - ci0), u = ch * K / 4;
+    float* dst = wbuf + (kk % kDecStages) * kDecChunk;
+    for (int i = threadIdx.x; i < n * u; i += kCsThreads) {
+      const int r = i / u, e = i - r * u, c = e / (K / 4), half = e - c * (K / 4);
+      cp_async16(dst + r * ch * K + 4 * dec_tunit(c, half, K),
+                 w + (static_cast<long long>(ci0 + r) * h + c0 + c) * K + 4 * half, true);
+    }
+  }
+  cp_async_commit();
+}
+
+// ConvTranspose1d(h, h, 2S, S, S/2) of h0 [h][ht] (T positions) for this CTA's
+// output channels -> loc [ch][Lo = T S] (+ bias); weight [h][h][2S].  Output p
+// takes tap k1 = (p + S/2) mod S at input j1 = (p + S/2) div S and tap k1 + S
+// at j1 - 1; a lane's 16 positions start at a multiple of 16 (S divides 16), so
+// its taps and input offsets are compile-time constants.  The caller has issued
+// the staging of chunks 0 and 1 (dec_convt_stage).
+template <int S>
+__device__ void dec_convt(const float* h0, float* loc, float* wbuf, const float* w, const float* bias, int h, int c0,
+                          int ch, int T, int ht) {
+  constexpr int K = 2 * S, pad = S / 2, NJ = 16 / S + 2;  // input positions a lane reads
+  const int Lo = T * S, cc = dec_convt_cc(h, ch, K);
+  const int nchunk = (h + cc - 1) / cc;
+  const DecTask k = dec_task(ch, Lo);
+  const int jb = k.p0 / S - 1;  // first input position the lane reads
+  float acc[16] = {};
+  for (int kk = 0; kk < nchunk; ++kk) {
+    dec_convt_stage(wbuf, w, h, c0, ch, K, kk + 2);
+    cp_async_wait<2>();
+    __syncthreads();
+    const int ci0 = kk * cc, n = min(cc, h - ci0);
+    const float* wk = wbuf + (kk % kDecStages) * kDecChunk;
+    for (int cil = k.s; cil < n; cil += k.ns) {
+      const float* hr = h0 + (ci0 + cil) * ht;
+      float hv[NJ];
+#pragma unroll
+      for (int m = 0; m < NJ; ++m) hv[m] = (jb + m >= 0 && jb + m < T) ? hr[jb + m] : 0.f;
+      float tv[K];
+#pragma unroll
+      for (int f = 0; f < K / 4; ++f) {
+        const float4 t4 = *reinterpret_cast<const float4*>(wk + cil * ch * K + 4 * dec_tunit(k.cl, f, K));
+        tv[4 * f] = t4.x;
+        tv[4 * f + 1] = t4.y;
+        tv[4 * f + 2] = t4.z;
+        tv[4 * f + 3] = t4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int k1 = (pad + i) % S, jo = (pad + i) / S;  // constants after unrolling
+        acc[i] = fmaf(tv[k1 + S], hv[jo], fmaf(tv[k1], hv[jo + 1], acc[i]));
+      }
+    }
+    __syncthreads();  // the buffer is refilled three chunks on
+  }
+  dec_split_sum(acc, k, wbuf, loc, bias, c0, ch, Lo);
+}
+
 __device__ void cs_decode_epilogue(const CaeStepArgs& a, float* csm, int b, int nc) {
   const CaeDecode& d = a.dec;
-  const int h = d.hidden, T = d.tokens, Z = d.latent, sdn = d.stride, K = 2 * sdn, pad = sdn / 2, Lo = T * sdn;
-  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc;
+  const int h = d.hidden, T = d.tokens, Z = d.latent, sdn = d.stride, K = 2 * sdn, Lo = T * sdn;
+  const int G = h < 8 ? h : 8, cg = h / G, ch = h / nc, ht = dec_ht(T), xs = dec_xs(Lo);
   const int rank = nc > 1 ? static_cast<int>(cluster_ctarank()) : 0, c0 = rank * ch;
   int o_xa, o_xb, o_loc, o_w, o_st;
   dec_layout(d, nc, &o_xa, &o_xb, &o_loc, &o_w, &o_st);
@@ -536,85 +680,61 @@ __device__ void cs_decode_epilogue(const CaeStepArgs& a, float* csm, int b, int 
   float* wbuf = csm + o_w;
   float* st = csm + o_st;
   const float* lat = CS_SM(lat);  // [T][Z]: the final latents of the sample
-  // 1. input_proj (+ suite embedding), every channel on every CTA: h0 [h][T]
+  // 1. stage input_proj's weight (buffer 2) and the first two ConvTranspose1d
+  //    chunks (buffers 0, 1); the latents (DiT4DiT-un-normalised when statistics
+  //    are given) go to loc while they land
+  dec_copy(wbuf + 2 * kDecChunk, d.in_w, h * Z);
+  dec_convt_stage(wbuf, d.convt_w, h, c0, ch, K, 0);
+  dec_convt_stage(wbuf, d.convt_w, h, c0, ch, K, 1);
+  for (int i = threadIdx.x; i < T * Z; i += kCsThreads)
+    loc[i] = d.lat_std != nullptr ? __fadd_rn(__fmul_rn(lat[i], d.lat_std[i]), d.lat_mean[i]) : lat[i];
+  cp_async_wait<2>();
+  __syncthreads();
+  // input_proj (+ suite embedding), every channel on every CTA: h0 [h][ht]
+  const float* win = wbuf + 2 * kDecChunk;
   const int sid = (d.suite_ids != nullptr && d.suite_embed != nullptr) ? d.suite_ids[b] : -1;
   for (int i = threadIdx.x; i < h * T; i += kCsThreads) {
     const int c = i / T, t = i - c * T;
     float acc = d.in_b[c];
-    for (int k = 0; k < Z; ++k) acc = fmaf(d.in_w[c * Z + k], lat[t * Z + k], acc);
+    for (int k = 0; k < Z; ++k) acc = fmaf(win[c * Z + k], loc[t * Z + k], acc);
     if (sid >= 0) acc += d.suite_embed[static_cast<long long>(sid) * h + c];
-    h0[c * T + t] = acc;
+    h0[c * ht + t] = acc;
   }
-  // 2. ConvTranspose1d for this CTA's channels: out[co][p] = b[co] + sum over
-  //    ci and the two taps k = (p + pad) mod s, + s of w[ci][co][k] h0[ci][j],
-  //    j = (p + pad - k) / s; weight rows ci staged [cc][ch][K]
-  {
-    const int cc = kDecChunk / (ch * K) >= h ? h : kDecChunk / (ch * K);
-    const int nchunk = (h + cc - 1) / cc;
-    float acc[2] = {0.f, 0.f};
-    auto stage = [&](int k) {
-      const int ci0 = k * cc, n = min(cc, h - ci0);
-      float* dst = wbuf + (k & 1) * kDecChunk;
-      const int l4 = ch * K / 4;
-      for (int i = threadIdx.x; i < n * l4; i += kCsThreads) {
-        const int r = i / l4, c = (i - r * l4) * 4;
-        cp_async16(dst + r * ch * K + c, d.convt_w + (static_cast<long long>(ci0 + r) * h + c0) * K + c, true);
-      }
-      cp_async_commit();
-    };
-    stage(0);
-    for (int k = 0; k < nchunk; ++k) {
-      if (k + 1 < nchunk) stage(k + 1);
-      if (k + 1 < nchunk) cp_async_wait<1>(); else cp_async_wait<0>();
-      __syncthreads();
-      const int ci0 = k * cc, n = min(cc, h - ci0);
-      const float* wk = wbuf + (k & 1) * kDecChunk;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int i = threadIdx.x + u * kCsThreads;
-        if (i >= ch * Lo) break;
-        const int cl = i / Lo, pp = i - cl * Lo;
-        const int k1 = (pp + pad) % sdn, k2 = k1 + sdn;
-        const int j1 = (pp + pad - k1) / sdn, j2 = j1 - 1;
-        const bool v1 = j1 < T, v2 = j2 >= 0 && j2 < T;
-        float a0 = 0.f;
-        for (int ci = 0; ci < n; ++ci) {
-          const float* wr = wk + (ci * ch + cl) * K;
-          const float* hr = h0 + (ci0 + ci) * T;
-          if (v1) a0 = fmaf(wr[k1], hr[j1], a0);
-          if (v2) a0 = fmaf(wr[k2], hr[j2], a0);
-        }
-        acc[u] += a0;
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = threadIdx.x + u * kCsThreads;
-      if (i < ch * Lo) loc[i] = acc[u] + d.convt_b[c0 + i / Lo];
-    }
-    __syncthreads();
-  }
-  // 3. GroupNorm + SiLU -> xa (the skip of the residual block), all CTAs
-  dec_norm_exchange(loc, xa, nullptr, d.gn0_w, d.gn0_b, ch, c0, Lo, cg, true, st, nc);
-  // 4. residual block: Conv1d -> GN -> SiLU -> xb; Conv1d -> GN, + skip -> xa'
-  dec_conv3(xa, loc, wbuf, d.c1_w, d.c1_b, h, c0, ch, Lo);
-  dec_norm_exchange(loc, xb, nullptr, d.gn1_w, d.gn1_b, ch, c0, Lo, cg, true, st, nc);
-  dec_conv3(xb, loc, wbuf, d.c2_w, d.c2_b, h, c0, ch, Lo);
-  // the block output overwrites xb (no CTA reads xb any more once conv2 is done:
+  __syncthreads();  // h0 complete; buffer 2 free for chunk 2
+  // 2. ConvTranspose1d for this CTA's channels, then GroupNorm + SiLU -> xa
+  //    (the skip of the residual block), all CTAs
+  if (sdn == 2)
+    dec_convt<2>(h0, loc, wbuf, d.convt_w, d.convt_b, h, c0, ch, T, ht);
+  else
+    dec_convt<4>(h0, loc, wbuf, d.convt_w, d.convt_b, h, c0, ch, T, ht);
+  dec_norm_exchange(loc, xa, nullptr, d.gn0_w, d.gn0_b, ch, c0, Lo, xs, cg, true, st, nc);
+  // 3. residual block: Conv1d -> GN -> SiLU -> xb; Conv1d -> GN, + skip -> xb
+  dec_conv3(xa, loc, wbuf, d.c1_w, d.c1_b, h, c0, ch, Lo, xs);
+  dec_norm_exchange(loc, xb, nullptr, d.gn1_w, d.gn1_b, ch, c0, Lo, xs, cg, true, st, nc);
+  dec_conv3(xb, loc, wbuf, d.c2_w, d.c2_b, h, c0, ch, Lo, xs);
+  // output_proj's weight streams in while the last exchange runs; the block
+  // output overwrites xb (no CTA reads xb any more once conv2 is done:
   // dec_conv3 ends with a CTA barrier and the exchange below with a cluster one)
+  dec_copy(wbuf, d.out_w, d.action_dim * h);
   if (nc > 1) cluster_barrier();
-  dec_norm_exchange(loc, xb, xa, d.gn2_w, d.gn2_b, ch, c0, Lo, cg, false, st, nc);
-  // 5. crop / zero-pad to the horizon, output_proj (rank 0 writes the chunk)
-  if (rank == 0) {
-    float* out = d.out + static_cast<long long>(b) * d.horizon * d.action_dim;
-    for (int i = threadIdx.x; i < d.horizon * d.action_dim; i += kCsThreads) {
-      const int pp = i / d.action_dim, o = i - pp * d.action_dim;
-      float acc = d.out_b[o];
-      if (pp < Lo)
-        for (int c = 0; c < h; ++c) acc = fmaf(d.out_w[o * h + c], xb[c * Lo + pp], acc);
-      out[i] = acc;
-    }
+  dec_norm_exchange(loc, xb, xa, d.gn2_w, d.gn2_b, ch, c0, Lo, xs, cg, false, st, nc);
+  cp_async_wait<0>();
+  __syncthreads();
+  // 4. crop / zero-pad to the horizon, output_proj: CTA `rank` writes the rows
+  //    [rank, rank + nc, ...) of the chunk, 4 threads per output
+  const float* wo = wbuf;
+  float* out = d.out + static_cast<long long>(b) * d.horizon * d.action_dim;
+  const int A = d.action_dim, nout = ((d.horizon - rank + nc - 1) / nc) * A;
+  for (int i0 = 0; i0 < nout * 4; i0 += kCsThreads) {
+    const int i = i0 + threadIdx.x, e = i >> 2, part = i & 3;
+    const bool live = i < nout * 4;
+    const int pp = rank + (e / A) * nc, o = e - (e / A) * A;
+    float acc = 0.f;
+    if (live && pp < Lo)
+      for (int c = part; c < h; c += 4) acc = fmaf(wo[o * h + c], xb[c * xs + pp], acc);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (live && part == 0) out[pp * A + o] = acc + d.out_b[o];
   }
 }
 

@@ -79,11 +79,15 @@ struct CaeDecode {
   const float *in_w, *in_b, *out_w, *out_b, *suite_embed;
   const int32_t* suite_ids;        // [B] or null
   const float *convt_w, *convt_b, *gn0_w, *gn0_b, *c1_w, *c1_b, *gn1_w, *gn1_b, *c2_w, *c2_b, *gn2_w, *gn2_b;
+  const float *lat_std, *lat_mean; // [tokens, latent] or null: z * std + mean is decoded
   float* out;                      // [B, horizon, action_dim]
 };
 // Shared-memory floats the epilogue decode needs (it uses the region before
 // the step kernel's row buffers, dead after the last block).
 int cae_decode_floats(const CaeDecode& d, int nc);
+constexpr int kDecChunk = 8192;   // floats per weight staging buffer of the epilogue decode
+constexpr int kDecStages = 3;     // staging buffers: two chunks in flight while one is used
+
 
 struct CaeStepArgs {
   CaeWeightsDev w;
@@ -123,6 +127,7 @@ struct DecArgs {
   fam_decoder_stage stages[kDecMaxStages];
   int num_stages;
   const float* z;                  // [B, num_tokens, latent]
+  const float *lat_std, *lat_mean; // [num_tokens, latent] or null: z * std + mean is decoded
   const int32_t* suite_ids;        // [B] or null
   float* out;                      // [B, horizon, action_dim]
   float* buf0;                     // [B, hidden, max_len] scratch

@@ -120,6 +120,10 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
 __device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
   asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
 // Arrive (release at cluster scope: this thread's earlier stores, remote ones
 // included, are visible to a thread that observes the phase) on an mbarrier of
 // a peer CTA, given by its shared::cluster address.

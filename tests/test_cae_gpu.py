@@ -144,9 +144,10 @@ def test_cae_shapes_vs_oracle(D, H, hd, F, L, S, C, B, N, masked):
 def test_chunk_decode_in_step_kernel_epilogue():
     """fam_cae_chunk_decode: the Action-VAE decode in the staged step kernel's epilogue.
     The config-0 golden (one-CTA cluster) and full config 0 (512-key context: a 4-CTA
-    cluster splitting the 256 decoder channels) give the reference's / the oracle's chunk
-    and the same chunk as the separate decoder launches; a decoder with two upsampling
-    stages takes the separate launches (decode_fused False) with the same result."""
+    cluster splitting the 256 decoder channels, decode="fused") give the reference's / the
+    oracle's chunk and the same chunk as the separate decoder launches; decode="auto"
+    leaves batch 2 to the separate launches; a decoder with two upsampling stages
+    takes the separate launches (decode_fused False) with the same result."""
     fx = torch.load(GOLDEN / "c0_cae_expert.pt", weights_only=False)
     dit = M.ActionDiT(**fx["dit_cfg"])
     dit.load_state_dict({k: v.float() for k, v in fx["dit"].items()})
@@ -159,7 +160,7 @@ def test_chunk_decode_in_step_kernel_epilogue():
     ae = ae.cuda()
     eng = dit.engine()
     ts, ds = fx["timesteps"].tolist(), fx["deltas"].tolist()
-    lat, chunk = eng.chunk_decode(fx["noise"].cuda(), ts, ds, fx["context"].float().cuda(), ae)
+    lat, chunk = eng.chunk_decode(fx["noise"].cuda(), ts, ds, fx["context"].float().cuda(), ae, decode="fused")
     torch.cuda.synchronize()
     assert eng.decode_fused
     _close(lat, fx["latent"])
@@ -182,11 +183,27 @@ def test_chunk_decode_in_step_kernel_epilogue():
     ts, ds = M.build_inference_schedule(4, 1.0, dtype=torch.float32)
     eng = dit.engine()
     for _ in range(2):  # a second call finds the first one's leftovers in the staging buffers
-        lat, chunk = eng.chunk_decode(noise.cuda(), ts, ds, ctx.cuda(), ae)
+        lat, chunk = eng.chunk_decode(noise.cuda(), ts, ds, ctx.cuda(), ae, decode="fused")
         torch.cuda.synchronize()
         assert eng.decode_fused
         _close(chunk, ref_chunk)
         _close(chunk, ae.decode(lat))
+    # batch 2: decode="auto" leaves the decode to the separate launches
+    lat_a, chunk_a = eng.chunk_decode(noise.cuda(), ts, ds, ctx.cuda(), ae)
+    torch.cuda.synchronize()
+    assert not eng.decode_fused
+    _close(chunk_a, ref_chunk)
+    # batch 4: decode="auto" decodes in the epilogue, same chunks as the separate launches
+    g4 = torch.Generator().manual_seed(4)
+    ctx4, noise4 = torch.randn(4, 512, 3072, generator=g4).cuda(), torch.randn(4, 8, 16, generator=g4).cuda()
+    lat4, chunk4 = eng.chunk_decode(noise4, ts, ds, ctx4, ae)
+    torch.cuda.synchronize()
+    assert eng.decode_fused
+    _, chunk4s = eng.chunk_decode(noise4, ts, ds, ctx4, ae, decode="separate")
+    torch.cuda.synchronize()
+    assert not eng.decode_fused
+    _close(chunk4, chunk4s)
+    _close(chunk4, ae.decode(lat4))
 
     ae2 = M.ActionAE(M.ActionAEConfig(action_dim=7, action_horizon=64, num_tokens=8, latent_dim=16,
                                       decoder_hidden=64, video_cond_dim=0, variational=True)).cuda()
