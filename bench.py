@@ -73,6 +73,12 @@ BATCH_PER_GPU = 16
 MICRO_BATCH = 16
 C0_CTX = 512
 
+# DRAM traffic of the headline roofline's launch (ffn.0 at the config-4 micro-batch), from one ncu
+# capture of `bench.py --case gemm_ffn0_c4` (read 1,842,168,064 B + write 755,133,184 B), and its
+# algorithmic bytes (A 28,160 x 3,072, weights 14,336 x 3,072, output 28,160 x 14,336 bf16, bias)
+FFN0_C4_DRAM_BYTES = 1842168064 + 755133184
+FFN0_C4_ALG_BYTES = 2 * (MICRO_BATCH * 1760 * 3072 + 14336 * 3072 + MICRO_BATCH * 1760 * 14336 + 14336)
+
 C1_CFG = dict(hidden_dim=1024, action_dim=7, ffn_dim=4096, text_dim=4096, freq_dim=256, eps=1e-6,
               num_heads=16, attn_head_dim=64, num_layers=28)
 C1_SA, C1_SV, C1_CTX, C1_STEPS, C1_SHIFT = 32, 1760, 64, 10, 1.0
@@ -627,8 +633,10 @@ def run_fam(args):
                          "kernel": f"backbone ffn.0 GEMM ({MICRO_BATCH * 1760} x 14336 x 3072, GELU epilogue, "
                                    "tcgen05 CTA pairs) as the prefill launches it, timed alone",
                          "achieved": g_tf, "peak": peaks["tc"], "unit": "TFLOP/s", "frac": g_tf / peaks["tc"],
-                         "traffic": None, "avg_launch_us": g_ms * 1e3, "flops_per_launch": g_flops,
-                         "peak_source": peaks["source"]},
+                         "traffic": FFN0_C4_DRAM_BYTES, "algorithmic_bytes": FFN0_C4_ALG_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch "
+                                           "(bench.py --case gemm_ffn0_c4, one capture)",
+                         "avg_launch_us": g_ms * 1e3, "flops_per_launch": g_flops, "peak_source": peaks["source"]},
             "pipeline_roofline": {"bound": "tensor", "flops_per_chunk": flops_chunk, "achieved": pipe_tf,
                                   "peak": peaks["tc_sustained"], "unit": "TFLOP/s",
                                   "frac": pipe_tf / peaks["tc_sustained"],
