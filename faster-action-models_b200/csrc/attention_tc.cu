@@ -28,10 +28,9 @@ namespace fam {
 
 namespace {
 
-constexpr int kTcThreads = 256;
 constexpr int kTcRows = 128;                      // queries per CTA, keys per block, head dim
 constexpr int kTcChunk = kTcRows * 128;           // 128 rows x 128 bytes (64 bf16): one swizzle-atom column
-constexpr int kTcSmem = 12 * kTcChunk + 1024 + 256;  // Q 2 | K 2x2 | V^T 2x2 | P 2 chunks, align slack, barriers
+constexpr int kTcSmem = 12 * kTcChunk + 1024 + 256;  // Q 2x2 | K 2x2 | V^T 2x2 chunks, align slack, barriers
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kErrTcWait = 0x4154;
 
@@ -107,28 +106,74 @@ __global__ void __launch_bounds__(256) vt_transpose_kernel(const __nv_bfloat16* 
   }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __grid_constant__ AttnTcArgs a) {
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// Two query tiles per CTA in ping-pong.  One CTA = 256 queries (tiles t = 0, 1)
+// of one (batch, head); every 128-key block of K and V^T is loaded once for
+// both tiles.  Warp roles (384 threads):
+//   warp 0      TMA producer: both Q tiles once, then K / V^T blocks into a
+//               two-stage ring;
+//   warp 1      allocates TMEM (512 columns: tile t's S at [256 t, +128), its O
+//               at [256 t + 128, +128)) and (lane 0) issues, per block j,
+//               PV_0(j-1), S_0(j), PV_1(j-1), S_1(j): each tile's P.V and next
+//               scores run back to back while the other tile's softmax runs;
+//   warps 4..7  softmax of tile 0, warps 8..11 of tile 1: one thread per query
+//               row (TMEM lane).  Pass 1 loads the row of S for its maximum,
+//               pass 2 loads it again, takes exp2 against the running maximum
+//               and writes P as bf16 pairs over the S columns already read,
+//               the A operand of the P.V MMA (tcgen05.mma with A in TMEM).
+// The running maximum moves only when a new score exceeds it by more than
+// kTcLazy (log2 units): probabilities stay <= 2^kTcLazy, and the O rows are
+// rescaled only on those moves.  P.V(j) of a tile is issued before S(j+1) of
+// that tile by the same thread, so the MMAs read P before S overwrites it,
+// and the commit that signals S(j+1) also covers P.V(j), after which the
+// softmax may rescale O.
+constexpr int kTcPpThreads = 384;
+constexpr float kTcLazy = 8.f;
+// Per-element softmax work decides the loop's speed (the XU pipe runs exp2 and
+// the bf16 packing): full key blocks skip the mask, the row maximum is taken
+// on raw scores and scaled once, x = s * scale - max is one FMA.  Measured at
+// config 4 (16 x 1,760 tokens, 24 x 128 heads, one launch): single query tile
+// 1,216 us; two tiles in ping-pong 1,253 us; + the trims 915 us.  Moving part
+// of the packing to integer rounding or part of exp2 onto the FMA pipe (a
+// polynomial) measured slower once the trims were in.
+__global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __grid_constant__ AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = sm;
-  uint8_t* sK = sm + 2 * kTcChunk;   // stage s at + 2 * s * kTcChunk
-  uint8_t* sV = sm + 6 * kTcChunk;
-  uint8_t* sP = sm + 10 * kTcChunk;
+  uint8_t* sQ = sm;                  // tile t at + 2 t kTcChunk
+  uint8_t* sK = sm + 4 * kTcChunk;   // stage s at + 2 s kTcChunk
+  uint8_t* sV = sm + 8 * kTcChunk;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 12 * kTcChunk);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;    // 4 softmax warps
-  uint64_t* pv_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* s_full = bars + 5;    // [2 tiles]
+  uint64_t* p_full = bars + 7;    // [2 tiles], 4 softmax warps each
+  uint64_t* o_full = bars + 9;    // [2 tiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * kTcRows;
+  const int q0 = blockIdx.x * 2 * kTcRows;
   const int S = a.S;
-  const int kend = (a.ff > 0 && q0 + kTcRows <= a.ff) ? a.ff : S;  // tiles inside the first frame
+  const int kend = (a.ff > 0 && q0 + 2 * kTcRows <= a.ff) ? a.ff : S;  // CTAs inside the first frame
   const int nb = (kend + kTcRows - 1) / kTcRows;
 
   if (threadIdx.x == 0) {
@@ -137,9 +182,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&a.tq);
@@ -160,10 +205,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
     if (lane == 0) {
       pdl_wait();  // Q, K and V^T come from earlier launches
       const uint64_t pol = policy_evict_last();
-      const int row_q = b * S + q0;
-      mbar_arrive_expect_tx(q_full, 2 * kTcChunk);
-      tma_load_2d(sQ, &a.tq, q_full, h * kTcRows, row_q, pol);
-      tma_load_2d(sQ + kTcChunk, &a.tq, q_full, h * kTcRows + 64, row_q, pol);
+      mbar_arrive_expect_tx(q_full, 4 * kTcChunk);
+      for (int t = 0; t < 2; ++t) {
+        const int row_q = b * S + q0 + t * kTcRows;
+        tma_load_2d(sQ + 2 * t * kTcChunk, &a.tq, q_full, h * kTcRows, row_q, pol);
+        tma_load_2d(sQ + (2 * t + 1) * kTcChunk, &a.tq, q_full, h * kTcRows + 64, row_q, pol);
+      }
       int issued = 0;
       for (int j = 0; j < nb; ++j) {
         const int s = j & 1;
@@ -190,123 +237,141 @@ __global__ void __launch_bounds__(kTcThreads, 1) attention_tc_kernel(const __gri
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(kTcRows, kTcRows);
       bool ok = mbar_wait(q_full, 0, a.status, kErrTcWait);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait)) return false;
+      // P_t(j) . V_j into O_t; A = the bf16 P pairs in tile t's S columns
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(&p_full[t], static_cast<uint32_t>(j) & 1, a.status, kErrTcWait)) return false;
         tc_fence_after();
+        const int s = j & 1;
 #pragma unroll
         for (int kk = 0; kk < kTcRows / 16; ++kk) {
-          const uint64_t da = umma_desc_sw128(sQ + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
-          const uint64_t db = umma_desc_sw128(sK + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
-          umma_bf16_ss(tmem_base + (j & 1) * kTcRows, da, db, idesc, kk > 0 ? 1u : 0u);
+          const uint64_t db = umma_desc_sw128(sV + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+          umma_bf16_ts(tmem_base + 256 * t + 128, tmem_base + 256 * t + 8 * kk, db, idesc,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
         return true;
       };
-      if (ok && nb > 0) ok = issue_s(0);
       for (int j = 0; ok && j < nb; ++j) {
         if (*abort_flag) break;
-        // S_{j+1} goes to the buffer of S_{j-1}, whose softmax published P_{j-1}
-        if (j + 1 < nb && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1, a.status, kErrTcWait)) break;
-        tc_fence_after();
         const int s = j & 1;
-#pragma unroll
-        for (int kk = 0; kk < kTcRows / 16; ++kk) {
-          const uint64_t da = umma_desc_sw128(sP + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
-          const uint64_t db = umma_desc_sw128(sV + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
-          umma_bf16_ss(tmem_base + 2 * kTcRows, da, db, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(&kv_full[s], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait)) {
+          ok = false;
+          break;
         }
-        umma_commit(&kv_empty[s]);
-        umma_commit(pv_done);
+        tc_fence_after();
+        for (int t = 0; ok && t < 2; ++t) {
+          if (j > 0 && !issue_pv(t, j - 1)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int kk = 0; kk < kTcRows / 16; ++kk) {
+            const uint64_t da = umma_desc_sw128(sQ + (2 * t + (kk >> 2)) * kTcChunk) + 2 * (kk & 3);
+            const uint64_t db = umma_desc_sw128(sK + 2 * s * kTcChunk + (kk >> 2) * kTcChunk) + 2 * (kk & 3);
+            umma_bf16_ss(tmem_base + 256 * t, da, db, idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+        }
+        if (ok && j > 0) umma_commit(&kv_empty[(j - 1) & 1]);  // K_{j-1}, V_{j-1} consumed
+      }
+      for (int t = 0; ok && t < 2 && nb > 0; ++t) {
+        if (!issue_pv(t, nb - 1)) {
+          ok = false;
+          break;
+        }
+        umma_commit(&o_full[t]);
       }
       if (!ok) *abort_flag = 1;
     }
   } else if (warp >= 4) {
     pdl_wait();  // the output rows are read by the previous layer's launches
-    const int wq = warp & 3;
+    const int t = (warp - 4) >> 2, wq = warp & 3;
     const int r = wq * 32 + lane;
-    const int qrow = q0 + r;
-    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16);
+    const int qrow = q0 + t * kTcRows + r;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + 256 * t;
     const bool first_frame_row = a.ff > 0 && qrow < a.ff;
+    const int lim = first_frame_row ? min(kend, a.ff) : kend;  // keys this row may see
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
       // warp-uniform outcome of every wait: the TMEM loads and stores below are warp-collective
-      const bool got = mbar_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrTcWait);
+      const bool got = mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1, a.status, kErrTcWait);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[kTcRows];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(lane_addr + (j & 1) * kTcRows + 32 * c, sv + 32 * c);
-      tmem_wait_ld();
       const int j0 = j * kTcRows;
-      const int lim = first_frame_row ? min(kend, a.ff) : kend;  // keys this row may see
+      const bool full = j0 + kTcRows <= lim;  // no key of the block is masked for this row
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld32(lane_addr + 32 * c, sv);
+        tmem_wait_ld();
+        if (full) {
 #pragma unroll
-      for (int c = 0; c < kTcRows; ++c) {
-        sv[c] = (j0 + c < lim) ? sv[c] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[c]);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (j0 + 32 * c + i < lim) mx = fmaxf(mx, sv[i]);
+        }
       }
-      const float mn = fmaxf(m, mx);
-      const float base = mn == -INFINITY ? 0.f : mn;
-      const float alpha = exp2f(m - base);
-      m = mn;
-      uint32_t pk[kTcRows / 2];
+      mx = mx == -INFINITY ? mx : mx * a.scale_log2;  // scale_log2 > 0
+      float alpha = 1.f;
+      if (mx > m + kTcLazy || (m == -INFINITY && mx > -INFINITY)) {
+        alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
+        m = mx;
+      }
+      const float base = m == -INFINITY ? 0.f : m;
+      l *= alpha;
+      if (j > 0 && !__all_sync(0xffffffffu, alpha == 1.f)) {
+        // P.V(j-1) is complete: the commit that signalled S(j) covers it
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(lane_addr + 128 + 32 * c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(lane_addr + 128 + 32 * c, ov);
+        }
+      }
       float ps = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32];
+        tmem_ld32(lane_addr + 32 * c, sv);
+        tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < kTcRows; c += 2) {
-        const float p0 = exp2f(sv[c] - base), p1 = exp2f(sv[c + 1] - base);
-        ps += p0 + p1;
-        pk[c / 2] = pack2_bf16(p0, p1);
-      }
-      l = l * alpha + ps;
-      // P_{j-1} and O: the previous P.V must be complete before they change
-      if (j > 0) {
-        const bool done = mbar_wait(pv_done, static_cast<uint32_t>(j - 1) & 1, a.status, kErrTcWait);
-        if (!__all_sync(0xffffffffu, done)) {
-          ok = false;
-          break;
+        for (int i = 0; i < 32; i += 2) {
+          const float e0 = exp2f(fmaf(sv[i], a.scale_log2, -base));
+          const float e1 = exp2f(fmaf(sv[i + 1], a.scale_log2, -base));
+          const float p0 = (full || j0 + 32 * c + i < lim) ? e0 : 0.f;
+          const float p1 = (full || j0 + 32 * c + i + 1 < lim) ? e1 : 0.f;
+          ps += p0 + p1;
+          pk[i / 2] = pack2_bf16(p0, p1);
         }
-        tc_fence_after();
-        if (!__all_sync(0xffffffffu, alpha == 1.f)) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            tmem_ld32(lane_addr + 2 * kTcRows + 32 * c, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(lane_addr + 2 * kTcRows + 32 * c, ov);
-          }
-          tmem_wait_st();
-        }
+        // P columns [16 c, 16 c + 16) overlap S columns already loaded
+        tmem_st16(lane_addr + 16 * c, pk);
       }
-      // P row -> the swizzled A tile: 16-byte unit u of row r sits at u ^ (r % 8)
-#pragma unroll
-      for (int u = 0; u < kTcRows / 8; ++u) {
-        const int chunk = u >> 3, uu = u & 7;
-        uint4* dst = reinterpret_cast<uint4*>(sP + chunk * kTcChunk + r * 128 + ((uu ^ (r & 7)) << 4));
-        *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-      }
-      fence_async_smem();
+      l += ps;
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     if (!ok) *abort_flag = 1;
-    const bool fin = ok && nb > 0 && mbar_wait(pv_done, static_cast<uint32_t>(nb - 1) & 1, a.status, kErrTcWait);
+    const bool fin = ok && nb > 0 && mbar_wait(&o_full[t], 0, a.status, kErrTcWait);
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = a.out + (static_cast<long long>(b) * S + qrow) * a.out_ts + h * kTcRows;
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float ov[32];
-        tmem_ld32(lane_addr + 2 * kTcRows + 32 * c, ov);
+        tmem_ld32(lane_addr + 128 + 32 * c, ov);
         tmem_wait_ld();
         if (qrow < S) {
 #pragma unroll
@@ -382,8 +447,8 @@ cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __
   a.scale_log2 = scale_log2;
   a.status = status;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((S + kTcRows - 1) / kTcRows, H, B);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.gridDim = dim3((S + 2 * kTcRows - 1) / (2 * kTcRows), H, B);
+  cfg.blockDim = dim3(kTcPpThreads);
   cfg.dynamicSmemBytes = kTcSmem;
   cfg.stream = st;
   cfg.attrs = attr_l;
