@@ -92,7 +92,7 @@ static bool attention_use_tc(const fam_attention_desc* d, const AttnArgs& a) {
   return d->kv_splits <= 1 && d->kv1_batch_stride == static_cast<long long>(d->kv1_tokens) * d->kv1_token_stride &&
          d->q_batch_stride == static_cast<long long>(d->q_tokens) * d->q_token_stride &&
          d->out_batch_stride == static_cast<long long>(d->q_tokens) * d->out_token_stride &&
-         attention_tc_eligible(d->head_dim, a.Sq, a.S1, a.S2, a.mask2d != nullptr || a.key_mask != nullptr,
+         attention_tc_eligible(d->head_dim, d->batch, a.H, a.Sq, a.S1, a.S2, a.mask2d != nullptr, a.first_frame_tokens,
                                a.q_ts, a.kv1_ts, a.out_ts);
 }
 
@@ -103,7 +103,7 @@ int fam_attention_workspace_size(const fam_attention_desc* d, size_t* bytes) {
   const int rc = attention_prepare(d, &a, &s);
   if (rc) return rc;
   *bytes = s.total;
-  if (attention_use_tc(d, a)) *bytes = (s.total + 255) / 256 * 256 + attention_tc_vt_bytes(d->batch, d->heads, d->q_tokens);
+  if (attention_use_tc(d, a)) *bytes = (s.total + 255) / 256 * 256 + attention_tc_vt_bytes(d->batch, d->heads, a.S1);
   return FAM_OK;
 }
 
@@ -118,11 +118,11 @@ int fam_attention(const fam_attention_desc* d, void* workspace, size_t workspace
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (attention_use_tc(d, a)) {
     const size_t off = (s.total + 255) / 256 * 256;
-    const size_t need = off + attention_tc_vt_bytes(d->batch, d->heads, d->q_tokens);
+    const size_t need = off + attention_tc_vt_bytes(d->batch, d->heads, a.S1);
     if (workspace == nullptr || workspace_bytes < need)
       return set_error("attention: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    return check_cuda(launch_attention_tc(a.q, a.q_ts, a.k1, a.v1, a.kv1_ts, a.out, a.out_ts, d->batch, a.Sq, a.H,
-                                          a.first_frame_tokens, a.scale_log2,
+    return check_cuda(launch_attention_tc(a.q, a.q_ts, a.k1, a.v1, a.kv1_ts, a.out, a.out_ts, d->batch, a.Sq, a.S1,
+                                          a.H, a.first_frame_tokens, a.key_mask, a.key_mask_bs, a.scale_log2,
                                           reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + off), nullptr,
                                           st, false),
                       "attention launch");

@@ -146,6 +146,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
 // softmax may rescale O.
 constexpr int kTcPpThreads = 384;
 constexpr float kTcLazy = 8.f;
+// Keys [k0, k0 + 32) this thread's row may see, as bits: below the row's own
+// limit lim (which differs between the lanes of a warp that straddles the first
+// frame) and, with a key mask, unmasked.  The mask is row-independent: lane i
+// reads key k0 + i's byte (keys below kend, the CTA's key count) and the warp
+// shares them by one ballot, so call with the whole warp (km, kend uniform).
+__device__ __forceinline__ uint32_t key_bits(const uint8_t* km, int k0, int kend, int lim, int lane) {
+  uint32_t bits = lim <= k0 ? 0u : (lim - k0 >= 32 ? 0xffffffffu : (1u << (lim - k0)) - 1u);
+  if (km != nullptr) {
+    const int k = k0 + lane;
+    bits &= __ballot_sync(0xffffffffu, k < kend && km[k] != 0);
+  }
+  return bits;
+}
+
 // Per-element softmax work decides the loop's speed (the XU pipe runs exp2 and
 // the bf16 packing): full key blocks skip the mask, the row maximum is taken
 // on raw scores and scaled once, x = s * scale - max is one FMA.  Measured at
@@ -172,8 +186,8 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   const int q0 = blockIdx.x * 2 * kTcRows;
-  const int S = a.S;
-  const int kend = (a.ff > 0 && q0 + 2 * kTcRows <= a.ff) ? a.ff : S;  // CTAs inside the first frame
+  const int S = a.S, Skv = a.Skv;
+  const int kend = (a.ff > 0 && q0 + 2 * kTcRows <= a.ff) ? a.ff : Skv;  // CTAs inside the first frame
   const int nb = (kend + kTcRows - 1) / kTcRows;
 
   if (threadIdx.x == 0) {
@@ -222,8 +236,8 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
         mbar_arrive_expect_tx(&kv_full[s], 4 * kTcChunk);
         uint8_t* k_dst = sK + 2 * s * kTcChunk;
         uint8_t* v_dst = sV + 2 * s * kTcChunk;
-        tma_load_2d(k_dst, &a.tk, &kv_full[s], h * kTcRows, b * S + j * kTcRows, pol);
-        tma_load_2d(k_dst + kTcChunk, &a.tk, &kv_full[s], h * kTcRows + 64, b * S + j * kTcRows, pol);
+        tma_load_2d(k_dst, &a.tk, &kv_full[s], h * kTcRows, b * Skv + j * kTcRows, pol);
+        tma_load_2d(k_dst + kTcChunk, &a.tk, &kv_full[s], h * kTcRows + 64, b * Skv + j * kTcRows, pol);
         tma_load_2d(v_dst, &a.tv, &kv_full[s], j * kTcRows, (b * a.H + h) * kTcRows, pol);
         tma_load_2d(v_dst + kTcChunk, &a.tv, &kv_full[s], j * kTcRows + 64, (b * a.H + h) * kTcRows, pol);
         issued = j + 1;
@@ -290,6 +304,7 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + 256 * t;
     const bool first_frame_row = a.ff > 0 && qrow < a.ff;
     const int lim = first_frame_row ? min(kend, a.ff) : kend;  // keys this row may see
+    const uint8_t* km = a.kmask != nullptr ? a.kmask + static_cast<long long>(b) * a.kmask_bs : nullptr;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
@@ -301,12 +316,14 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
       }
       tc_fence_after();
       const int j0 = j * kTcRows;
-      const bool full = j0 + kTcRows <= lim;  // no key of the block is masked for this row
+      const bool full = j0 + kTcRows <= lim && km == nullptr;  // no key of the block is masked for this row
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float sv[32];
         tmem_ld32(lane_addr + 32 * c, sv);
+        // bit i: key j0 + 32 c + i may be seen (the key mask, one ballot per 32 keys)
+        const uint32_t mw = key_bits(km, j0 + 32 * c, kend, lim, lane);
         tmem_wait_ld();
         if (full) {
 #pragma unroll
@@ -314,7 +331,7 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (j0 + 32 * c + i < lim) mx = fmaxf(mx, sv[i]);
+            if ((mw >> i) & 1u) mx = fmaxf(mx, sv[i]);
         }
       }
       mx = mx == -INFINITY ? mx : mx * a.scale_log2;  // scale_log2 > 0
@@ -342,14 +359,17 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
       for (int c = 0; c < 4; ++c) {
         float sv[32];
         tmem_ld32(lane_addr + 32 * c, sv);
+        // every lane takes part in the ballot (lanes of a warp can differ in `full`)
+        const uint32_t bits = key_bits(km, j0 + 32 * c, kend, lim, lane);
+        const uint32_t mw = full ? 0xffffffffu : bits;
         tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const float e0 = exp2f(fmaf(sv[i], a.scale_log2, -base));
           const float e1 = exp2f(fmaf(sv[i + 1], a.scale_log2, -base));
-          const float p0 = (full || j0 + 32 * c + i < lim) ? e0 : 0.f;
-          const float p1 = (full || j0 + 32 * c + i + 1 < lim) ? e1 : 0.f;
+          const float p0 = ((mw >> i) & 1u) ? e0 : 0.f;
+          const float p1 = ((mw >> (i + 1)) & 1u) ? e1 : 0.f;
           ps += p0 + p1;
           pk[i / 2] = pack2_bf16(p0, p1);
         }
@@ -395,27 +415,33 @@ __global__ void __launch_bounds__(kTcPpThreads, 1) attention_tc_kernel(const __g
 
 }  // namespace
 
-size_t attention_tc_vt_bytes(int B, int H, int S) {
-  const size_t S_pad = static_cast<size_t>((S + 63) / 64 * 64);
+size_t attention_tc_vt_bytes(int B, int H, int Skv) {
+  const size_t S_pad = static_cast<size_t>((Skv + 63) / 64 * 64);
   return static_cast<size_t>(B) * H * kTcRows * S_pad * sizeof(__nv_bfloat16);
 }
 
-bool attention_tc_eligible(int head_dim, int Sq, int S1, int S2, bool masks, long long q_ts, long long kv_ts,
-                           long long out_ts) {
-  return head_dim == kTcRows && S2 == 0 && !masks && Sq == S1 && Sq >= 512 && (q_ts % 8) == 0 && (kv_ts % 8) == 0 &&
-         (out_ts % 8) == 0;
+bool attention_tc_eligible(int head_dim, int B, int H, int Sq, int S1, int S2, bool mask2d, int ff, long long q_ts,
+                           long long kv_ts, long long out_ts) {
+  if (head_dim != kTcRows || S2 != 0 || mask2d || S1 < 1 || (ff != 0 && S1 != Sq) || Sq < 512) return false;
+  if ((q_ts % 8) != 0 || (kv_ts % 8) != 0 || (out_ts % 8) != 0) return false;
+  // a second key source: measured (1,760 queries x 24 heads over 64 keys) 51 us
+  // against 46 us for attention_kernel at batch 1 (168 CTAs), 232 against 291 us
+  // at batch 16 (2,688 CTAs)
+  const long long ctas = static_cast<long long>(B) * H * ((Sq + 2 * kTcRows - 1) / (2 * kTcRows));
+  return S1 == Sq || ctas >= 4 * 148;
 }
 
 cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int H, int ff,
-                                float scale_log2, __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl) {
+                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int Skv, int H,
+                                int ff, const uint8_t* kmask, long long kmask_bs, float scale_log2,
+                                __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl) {
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int S_pad = (S + 63) / 64 * 64;
+  const int S_pad = (Skv + 63) / 64 * 64;
   cudaLaunchAttribute attr_l[1];
   attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr_l[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -426,22 +452,25 @@ cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __
     cfg.stream = st;
     cfg.attrs = attr_l;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v, kv_ts, vt, S, S_pad, H);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, vt_transpose_kernel, v, kv_ts, vt, Skv, S_pad, H);
     if (e != cudaSuccess) return e;
   }
   AttnTcArgs a;
   memset(&a, 0, sizeof(a));
   if (!make_tmap_bf16_2d(&a.tq, q, static_cast<uint64_t>(B) * S, static_cast<uint64_t>(H) * kTcRows,
                          static_cast<uint64_t>(q_ts), kTcRows) ||
-      !make_tmap_bf16_2d(&a.tk, k, static_cast<uint64_t>(B) * S, static_cast<uint64_t>(H) * kTcRows,
+      !make_tmap_bf16_2d(&a.tk, k, static_cast<uint64_t>(B) * Skv, static_cast<uint64_t>(H) * kTcRows,
                          static_cast<uint64_t>(kv_ts), kTcRows) ||
       !make_tmap_bf16_2d(&a.tv, vt, static_cast<uint64_t>(B) * H * kTcRows, static_cast<uint64_t>(S_pad),
                          static_cast<uint64_t>(S_pad), kTcRows))
     return cudaErrorInvalidValue;
   a.out = out;
   a.out_ts = out_ts;
+  a.kmask = kmask;
+  a.kmask_bs = kmask_bs;
   a.B = B;
   a.S = S;
+  a.Skv = Skv;
   a.H = H;
   a.ff = ff;
   a.scale_log2 = scale_log2;

@@ -96,21 +96,27 @@ struct GemmPlan {
 // no explicit / key masks; the first-frame-causal rule is supported).
 struct AttnTcArgs {
   CUtensorMap tq;             // Q  [B*S, H*128]
-  CUtensorMap tk;             // K  [B*S, H*128]
-  CUtensorMap tv;             // V^T [B*H*128, S_pad]
+  CUtensorMap tk;             // K  [B*Skv, H*128]
+  CUtensorMap tv;             // V^T [B*H*128, Skv_pad]
   __nv_bfloat16* out;         // [B*S, out_ts]
-  long long out_ts;
-  int B, S, H, ff;
+  const uint8_t* kmask;       // [B, kmask_bs] key mask (nonzero = attend) or null
+  long long out_ts, kmask_bs;
+  int B, S, Skv, H, ff;
   float scale_log2;
   int* status;
 };
-bool attention_tc_eligible(int head_dim, int Sq, int S1, int S2, bool masks, long long q_ts, long long kv_ts,
-                           long long out_ts);
-size_t attention_tc_vt_bytes(int B, int H, int S);
+// Self attention (Skv == Sq, optional first-frame rule) or attention over a
+// second key source (Skv keys, optional per-batch key mask, ff == 0; taken
+// only when the launch has at least 4 waves of CTAs: short key sources make
+// each CTA a short latency chain, which pays only with many CTAs in flight).
+bool attention_tc_eligible(int head_dim, int B, int H, int Sq, int S1, int S2, bool mask2d, int ff, long long q_ts,
+                           long long kv_ts, long long out_ts);
+size_t attention_tc_vt_bytes(int B, int H, int Skv);
 // Transposes V into `vt` (attention_tc_vt_bytes) and runs the attention.
 cudaError_t launch_attention_tc(const __nv_bfloat16* q, long long q_ts, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int H, int ff,
-                                float scale_log2, __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl);
+                                long long kv_ts, __nv_bfloat16* out, long long out_ts, int B, int S, int Skv, int H,
+                                int ff, const uint8_t* kmask, long long kmask_bs, float scale_log2,
+                                __nv_bfloat16* vt, int* status, cudaStream_t st, bool pdl);
 
 int gemm_pick_bn(int n);
 // sk_part / sk_flag (optional, sk_bytes of fp32 scratch and one zeroed word per

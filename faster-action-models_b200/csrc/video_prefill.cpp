@@ -329,10 +329,11 @@ int enqueue_prefill(const VCtx& c) {
     aa.keys_per_split = S;
     aa.part = wp<float>(c, c.L.apart);
     aa.counters = wp<int>(c, c.L.ctr);
-    if (attention_tc_eligible(g.head_dim, S, S, 0, false, aa.q_ts, aa.kv1_ts, aa.out_ts)) {
-      V_LAUNCH(launch_attention_tc(aa.q, aa.q_ts, aa.k1, aa.v1, aa.kv1_ts, aa.out, aa.out_ts, B, S, g.num_heads,
-                                   aa.first_frame_tokens, aa.scale_log2, wp<__nv_bfloat16>(c, c.L.vt), c.e->status,
-                                   c.st, c.pdl));
+    if (attention_tc_eligible(g.head_dim, B, g.num_heads, S, S, 0, false, aa.first_frame_tokens, aa.q_ts, aa.kv1_ts,
+                              aa.out_ts)) {
+      V_LAUNCH(launch_attention_tc(aa.q, aa.q_ts, aa.k1, aa.v1, aa.kv1_ts, aa.out, aa.out_ts, B, S, S, g.num_heads,
+                                   aa.first_frame_tokens, nullptr, 0, aa.scale_log2, wp<__nv_bfloat16>(c, c.L.vt),
+                                   c.e->status, c.st, c.pdl));
       ++c.e->launch_count;  // V^T transpose + attention
     } else {
       V_LAUNCH(launch_attention(aa, B, g.head_dim, c.st, c.pdl));
@@ -385,7 +386,18 @@ int enqueue_prefill(const VCtx& c) {
       ca.keys_per_split = io.context_tokens;
       ca.part = wp<float>(c, c.L.apart);
       ca.counters = wp<int>(c, c.L.ctr);
-      V_LAUNCH(launch_attention(ca, B, g.head_dim, c.st, c.pdl));
+      // the tcgen05 kernel with the context as the key source (its V^T fits the
+      // self attention's buffer while the context is no longer than the video)
+      if (io.context_tokens <= S &&
+          attention_tc_eligible(g.head_dim, B, g.num_heads, S, io.context_tokens, 0, false, 0, ca.q_ts, ca.kv1_ts,
+                                ca.out_ts)) {
+        V_LAUNCH(launch_attention_tc(ca.q, ca.q_ts, ca.k1, ca.v1, ca.kv1_ts, ca.out, ca.out_ts, B, S,
+                                     io.context_tokens, g.num_heads, 0, io.context_mask, io.context_tokens,
+                                     ca.scale_log2, wp<__nv_bfloat16>(c, c.L.vt), c.e->status, c.st, c.pdl));
+        ++c.e->launch_count;  // V^T transpose + attention
+      } else {
+        V_LAUNCH(launch_attention(ca, B, g.head_dim, c.st, c.pdl));
+      }
       V_TRYI(gemm_x(c, ca.out, HD, M, ly.co_w, ly.co_b, D, HD, kEpiResidual, kActNone, x, D, true));
     }
     // AdaLN (shift_mlp, scale_mlp) + FFN + gate_mlp

@@ -87,3 +87,25 @@ def test_tcgen05_self_attention_sharp_rising_logits(fam_ops):
     err = (out.float() - ref).abs().max().item()
     cos = torch.nn.functional.cosine_similarity(out.double().flatten(), ref.double().flatten(), dim=0).item()
     assert err < 2e-2 and cos >= 0.999, (err, cos)
+
+
+@pytest.mark.parametrize("B,S,C,H", [(4, 1760, 64, 24), (4, 600, 300, 64), (1, 600, 300, 2)])
+def test_tcgen05_attention_over_second_key_source(fam_ops, B, S, C, H):
+    """Queries over a separate key source (the backbone's cross attention over the context
+    tokens): C keys padded to 128-key blocks, a per-batch key mask.  The first two shapes
+    launch >= 4 waves of CTAs and run the tcgen05 kernel, the last the split-KV kernel."""
+    g = torch.Generator(device="cuda").manual_seed(S + C)
+    HD = H * 128
+    q = torch.randn(B, S, HD, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, C, HD, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, C, HD, device="cuda", generator=g).bfloat16()
+    km = torch.ones(B, C, dtype=torch.uint8, device="cuda")
+    km[-1, C - 7:] = 0
+    km[0, 3] = 0
+    out = fam_ops.attention(q, k, v, H, key_mask=km)
+    torch.cuda.synchronize()
+    ref = torch.cat([_ref(q[i:i + 1], k[i:i + 1], v[i:i + 1], H,
+                          km[i].bool().view(1, C).expand(S, C).contiguous()) for i in range(B)])
+    err = (out.float() - ref).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(out.double().flatten(), ref.double().flatten(), dim=0).item()
+    assert err < 2e-2 and cos >= 0.999, (err, cos)
