@@ -201,6 +201,98 @@ __global__ void __launch_bounds__(kRowThreads) resid_norm_kernel(const ResidNorm
   }
 }
 
+// --------------------------------------------------------- norm rows (4 per CTA)
+// The norm-only form of resid_norm (the residual already updated by a GEMM
+// epilogue, as in the backbone prefill).  A CTA normalises kNrRows rows, 64
+// threads (two warps) per row, D / 256 float4 groups per thread in registers,
+// so each thread has 4x the bytes of the CTA-per-row form in flight and the
+// two CTA barriers (mean, variance) serve 4 rows.  The norm constants -- the
+// affine weight and bias, or the AdaLN shift and scale of the rows' modulation
+// row when the CTA's rows share it -- are built once per CTA in shared memory
+// before the programmatic-launch wait (rows with different modulation rows
+// read theirs directly).
+constexpr int kNrRows = 4;
+constexpr int kNrMaxD = 4096;
+struct NormRowsArgs {
+  ResidNormArgs a;
+  int rows;
+};
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads) norm_rows_kernel(const NormRowsArgs na) {
+  __shared__ __align__(16) float cst[2 * kNrMaxD];  // weight / shift, then bias / scale
+  __shared__ float red[kNrRows][2][2];              // [row][warp][sum, sum of squares]
+  const ResidNormArgs& a = na.a;
+  const int D = a.D;
+  const int r = threadIdx.x >> 6, t = threadIdx.x & 63, w = (threadIdx.x >> 5) & 1, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kNrRows, row = row0 + r;
+  const int last = min(row0 + kNrRows, na.rows) - 1;
+  const bool ada = a.norm_mode == kNormAdaLN;
+  const long long off0 = ada ? mod_row_offset(a.nmod, row0) : 0;
+  const bool shared_c = !ada || mod_row_offset(a.nmod, last) == off0;
+  if (shared_c) {
+    for (int g = threadIdx.x; g < D / 4; g += kRowThreads) {
+      const int f = 4 * g;
+      float4 c0, c1;
+      if (ada) {
+        c0 = mod_value4(a.nmod, off0, a.shift_chunk, f, D);
+        c1 = mod_value4(a.nmod, off0, a.shift_chunk + 1, f, D);
+      } else {
+        c0 = ld_bf4(a.norm_w + f);
+        c1 = ld_bf4(a.norm_b + f);
+      }
+      *reinterpret_cast<float4*>(cst + f) = c0;
+      *reinterpret_cast<float4*>(cst + kNrMaxD + f) = c1;
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const bool live = row < na.rows;
+  float4 v[NV];
+  float s = 0.f;
+  const float* x = a.x + static_cast<long long>(live ? row : 0) * D;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = live ? *reinterpret_cast<const float4*>(x + 4 * (t + 64 * i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[r][w][0] = s;
+  __syncthreads();  // also publishes the constants
+  const float mean = (red[r][0][0] + red[r][1][0]) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 d = make_float4(v[i].x - mean, v[i].y - mean, v[i].z - mean, v[i].w - mean);
+    q += (d.x * d.x + d.y * d.y) + (d.z * d.z + d.w * d.w);
+  }
+  q = warp_sum(q);
+  if (lane == 0) red[r][w][1] = q;
+  __syncthreads();
+  if (!live) return;
+  const float rstd = rsqrtf((red[r][0][1] + red[r][1][1]) / D + a.eps);
+  const long long noff = ada && !shared_c ? mod_row_offset(a.nmod, row) : off0;
+  __nv_bfloat16* h = a.h + static_cast<long long>(row) * a.h_stride;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int f = 4 * (t + 64 * i);
+    float4 n = make_float4((v[i].x - mean) * rstd, (v[i].y - mean) * rstd, (v[i].z - mean) * rstd,
+                           (v[i].w - mean) * rstd);
+    if (ada) {  // bf16(bf16(LN(x) * bf16(1 + scale)) + shift), the reference's bf16 steps
+      const float4 sh = shared_c ? *reinterpret_cast<const float4*>(cst + f) : mod_value4(a.nmod, noff, a.shift_chunk, f, D);
+      const float4 sc = shared_c ? *reinterpret_cast<const float4*>(cst + kNrMaxD + f)
+                                 : mod_value4(a.nmod, noff, a.shift_chunk + 1, f, D);
+      n = rbf4(n);
+      n = make_float4(rbf(n.x * rbf(1.f + sc.x)), rbf(n.y * rbf(1.f + sc.y)), rbf(n.z * rbf(1.f + sc.z)),
+                      rbf(n.w * rbf(1.f + sc.w)));
+      n = make_float4(n.x + sh.x, n.y + sh.y, n.z + sh.z, n.w + sh.w);
+    } else {
+      const float4 wt = *reinterpret_cast<const float4*>(cst + f), b = *reinterpret_cast<const float4*>(cst + kNrMaxD + f);
+      n = make_float4(n.x * wt.x + b.x, n.y * wt.y + b.y, n.z * wt.z + b.z, n.w * wt.w + b.w);
+    }
+    st_bf4(h + f, n);
+  }
+}
+
 // ------------------------------------------------------------------ qkv_post
 // One CTA per token row; dynamic smem: 2*HD floats (q and k before the norm).
 __global__ void __launch_bounds__(kRowThreads) qkv_post_kernel(const QkvPostArgs a) {
@@ -578,6 +670,18 @@ static cudaError_t launch_resid_norm_t(const ResidNormArgs& a, int rows, cudaStr
 
 cudaError_t launch_resid_norm(const ResidNormArgs& a, int rows, cudaStream_t st, bool pdl) {
   if (a.D % 4 != 0 || a.D > 4 * kMaxGroups * kRowThreads) return cudaErrorInvalidValue;
+  if (a.partials == nullptr && (a.norm_mode == kNormAffine || a.norm_mode == kNormAdaLN) && a.D % 256 == 0 &&
+      a.D <= kNrMaxD && a.h_stride % 4 == 0) {
+    const dim3 grid((rows + kNrRows - 1) / kNrRows);
+    const NormRowsArgs na = {a, rows};
+    switch (a.D / 256) {
+      case 4: return launch_pdl(norm_rows_kernel<4>, grid, dim3(kRowThreads), 0, st, pdl, na);
+      case 8: return launch_pdl(norm_rows_kernel<8>, grid, dim3(kRowThreads), 0, st, pdl, na);
+      case 12: return launch_pdl(norm_rows_kernel<12>, grid, dim3(kRowThreads), 0, st, pdl, na);
+      case 16: return launch_pdl(norm_rows_kernel<16>, grid, dim3(kRowThreads), 0, st, pdl, na);
+      default: break;
+    }
+  }
   return a.partials != nullptr ? launch_resid_norm_t<true>(a, rows, st, pdl)
                                : launch_resid_norm_t<false>(a, rows, st, pdl);
 }
