@@ -467,6 +467,100 @@ __global__ void __launch_bounds__(kRowThreads, 3) qkv_post_wide_kernel(const Qkv
   }
 }
 
+// ------------------------------------------------------ qkv_post (2 rows per CTA)
+// The wide form for the backbone's row counts: 2 rows per CTA, 128 threads per
+// row, the row's 8-column groups g = t, t + 128, ... (9 per thread at HD =
+// 3072) loaded at once into registers; V is stored on arrival, q and k stay in
+// registers until their row's sums of squares are reduced (warp shuffles, one
+// CTA barrier), and the q / k norm weights and the rows' RoPE tables are staged
+// in shared memory before the launch wait.  Each SM keeps 4x the rows of the
+// CTA-per-row form in flight.  Per element the arithmetic is qkv_post_kernel's.
+constexpr int kQpRows = 2;
+constexpr int kQpThreads = kRowThreads / kQpRows;
+constexpr int kQpLoads = 9;      // 3 HD <= 9 * 8 * kQpThreads
+constexpr int kQpMaxHD = 3072;
+constexpr int kQpMaxHalf = 128;  // head_dim / 2
+struct QkvRowsArgs {
+  QkvPostArgs a;
+  int rows;
+};
+__global__ void __launch_bounds__(kRowThreads) qkv_post_rows_kernel(const QkvRowsArgs na) {
+  __shared__ __align__(16) __nv_bfloat16 wq[kQpMaxHD];
+  __shared__ __align__(16) __nv_bfloat16 wk[kQpMaxHD];
+  __shared__ __align__(16) float2 rope_s[kQpRows][kQpMaxHalf];
+  __shared__ float2 red[kQpRows][kQpThreads / 32];
+  const QkvPostArgs& a = na.a;
+  const int rows = na.rows, HD = a.HD, G = 3 * HD / 8, GQ = HD / 8, half = a.head_dim / 2;
+  const int r = threadIdx.x / kQpThreads, t = threadIdx.x % kQpThreads, wr = t >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kQpRows, row = row0 + r;
+  const bool live = row < rows;
+  for (int i = threadIdx.x; i < GQ; i += kRowThreads) {
+    reinterpret_cast<uint4*>(wq)[i] = reinterpret_cast<const uint4*>(a.norm_q)[i];
+    reinterpret_cast<uint4*>(wk)[i] = reinterpret_cast<const uint4*>(a.norm_k)[i];
+  }
+  for (int i = threadIdx.x; i < kQpRows * half; i += kRowThreads) {
+    const int rr = i / half, p = i - rr * half, rw = min(row0 + rr, rows - 1);
+    rope_s[rr][p] = a.rope[static_cast<long long>(rw % a.rows_per_batch) * half + p];
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  const __nv_bfloat16* in = a.qkv_bf16 + static_cast<long long>(live ? row : 0) * 3 * HD;
+  uint4 raw[kQpLoads];
+#pragma unroll
+  for (int j = 0; j < kQpLoads; ++j) {
+    const int g = t + j * kQpThreads;
+    if (live && g < G) raw[j] = *reinterpret_cast<const uint4*>(in + 8 * g);
+  }
+  float ssq = 0.0f, ssk = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kQpLoads; ++j) {
+    const int g = t + j * kQpThreads;
+    if (!live || g >= G) continue;
+    if (g >= 2 * GQ) {
+      *reinterpret_cast<uint4*>(a.v_out + static_cast<long long>(row) * a.out_stride + 8 * (g - 2 * GQ)) = raw[j];
+    } else {
+      float y[8];
+      unpack_bf8(raw[j], y);
+      float s2 = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s2 += y[e] * y[e];
+      if (g < GQ) ssq += s2; else ssk += s2;
+    }
+  }
+  ssq = warp_sum(ssq);
+  ssk = warp_sum(ssk);
+  if (lane == 0) red[r][wr] = make_float2(ssq, ssk);
+  __syncthreads();  // also publishes the staged constants
+  if (!live) return;
+  float2 tot = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kQpThreads / 32; ++i) tot = make_float2(tot.x + red[r][i].x, tot.y + red[r][i].y);
+  const float rq = rsqrtf(tot.x / HD + a.eps);
+  const float rk = rsqrtf(tot.y / HD + a.eps);
+#pragma unroll
+  for (int j = 0; j < kQpLoads; ++j) {
+    const int g = t + j * kQpThreads;
+    if (g >= 2 * GQ) continue;
+    const bool is_k = g >= GQ;
+    const int f = 8 * (is_k ? g - GQ : g);
+    const float rs = is_k ? rk : rq;
+    float y[8], w[8], x[8], o[8];
+    unpack_bf8(raw[j], y);
+    unpack_bf8(*reinterpret_cast<const uint4*>((is_k ? wk : wq) + f), w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = rbf(rbf(y[e] * rs) * w[e]);
+    const float2* cs = &rope_s[r][(f % a.head_dim) / 2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // (cos, sin) of pair q
+      const float2 c = cs[q];
+      o[2 * q] = x[2 * q] * c.x - x[2 * q + 1] * c.y;
+      o[2 * q + 1] = x[2 * q] * c.y + x[2 * q + 1] * c.x;
+    }
+    *reinterpret_cast<uint4*>((is_k ? a.k_out : a.q_out) + static_cast<long long>(row) * a.out_stride + f) =
+        pack_bf8(o);
+  }
+}
+
 // ------------------------------------------------------------------ rms_rows
 // out = RMSNorm(sum partials + bias) * w, one CTA per row.  With nsplit == 0
 // the input is a bf16 matrix (in place allowed).  dynamic smem: N floats.
@@ -694,6 +788,11 @@ cudaError_t launch_qkv_post(const QkvPostArgs& a, int rows, cudaStream_t st, boo
                     2 * a.HD <= kQkvNorm * 8 * kRowThreads && a.out_stride % 8 == 0 && al16(a.qkv_bf16) &&
                     al16(a.norm_q) && al16(a.norm_k) && al16(a.rope) && al16(a.q_out) && al16(a.k_out) &&
                     al16(a.v_out);
+  if (wide && a.HD <= kQpMaxHD && 3 * a.HD <= kQpLoads * 8 * kQpThreads && a.head_dim / 2 <= kQpMaxHalf) {
+    const QkvRowsArgs na = {a, rows};
+    return launch_pdl(qkv_post_rows_kernel, dim3((rows + kQpRows - 1) / kQpRows), dim3(kRowThreads), 0, st, pdl,
+                      na);
+  }
   if (wide) {
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(qkv_post_wide_kernel), smem);
     if (e != cudaSuccess) return e;
