@@ -110,7 +110,8 @@ WsLayout layout(const fam_action_config& c, int B, int Sa, int C, int N) {
   // line, then one flag line per CTA
   w.fsync_bytes = ((fused_sync_words(N, c.num_layers, c.num_heads) + 31) / 32 * 32 +
                    static_cast<size_t>(kFusedMaxCtas) * 32) * 4;
-  w.fssq_bytes = static_cast<size_t>(N) * c.num_layers * 3 * kFusedRows * 8;
+  // RMS sums of squares [N][L][3][32], then the LayerNorm row sums [N][L][3][32][2]
+  w.fssq_bytes = static_cast<size_t>(N) * c.num_layers * 3 * kFusedRows * 8 * 3;
   w.fsync = take(w.fsync_bytes);
   w.fssq = take(w.fssq_bytes);
   w.fpart = take(static_cast<size_t>(c.num_heads) * 64 * kFusedRows * 66 * 4);
@@ -584,6 +585,7 @@ int enqueue_chunk_fused(const Ctx& c, void* latent, const float* ts, const float
   a.ci = wsp<__nv_bfloat16>(c, c.L.ci);
   a.fh = wsp<__nv_bfloat16>(c, c.L.fh);
   a.ssq = wsp<double>(c, c.L.fssq);
+  a.lnstat = a.ssq + static_cast<size_t>(N) * g.num_layers * 3 * kFusedRows;
   a.apart = wsp<float>(c, c.L.fpart);
   a.sync = wsp<unsigned>(c, c.L.fsync);
   a.tile_ctr = a.sync + 2 + static_cast<size_t>(N) * g.num_layers * g.num_heads;

@@ -404,12 +404,13 @@ __device__ __forceinline__ bool mbar_wait_cl(const FusedArgs& a, uint64_t* bar, 
 // r2 = w + 22 are processed together (independent instruction streams).  The
 // two CTAs of the pair exchange their half-row sums: lane 0 of every worker
 // warp stores them into the peer's xstat and arrives on the peer's xstat_bar,
-// then waits for the peer's eleven arrivals on its own.  Rows >= R are staged
-// as zeros; a row >= 32 (the third row of the last warp) does not exist.
-// Returns false on a timed-out exchange.
+// then waits for the peer's eleven arrivals on its own.  With `st` (the row
+// sums the residual GEMM before wrote, [32][2] fp64) the sums and the exchange
+// are skipped.  Rows >= R are staged as zeros; a row >= 32 (the third row of
+// the last warp) does not exist.  Returns false on a timed-out exchange.
 template <int NCH>
 __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, int mode, int half,
-                                       uint32_t parity) {
+                                       uint32_t parity, const double* st) {
   constexpr int DH = NCH * 256;  // columns of this half
   const int D = a.D;
   const int wid = (threadIdx.x >> 5) - 1, lane = threadIdx.x & 31;
@@ -419,43 +420,56 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
   ln_load_half<NCH>(a, r0, lane, half, xa);
   ln_load_half<NCH>(a, r1, lane, half, xb);
   ln_load_half<NCH>(a, has2 ? r2 : kFusedRows, lane, half, xc);
-  // the shift of the one-pass variance: a value common to both halves (the
-  // first element of the row)
-  const float ca = r0 < a.R ? bf2f(a.x[static_cast<long long>(r0) * D]) : 0.f;
-  const float cb = r1 < a.R ? bf2f(a.x[static_cast<long long>(r1) * D]) : 0.f;
-  const float cc = (has2 && r2 < a.R) ? bf2f(a.x[static_cast<long long>(r2) * D]) : 0.f;
-  float s[6];
-  ln_half_sums<NCH>(xa, ca, s[0], s[1]);
-  ln_half_sums<NCH>(xb, cb, s[2], s[3]);
-  ln_half_sums<NCH>(xc, cc, s[4], s[5]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int i = 0; i < 6; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
-  // exchange with the peer
-  const uint32_t peer = half ^ 1;
-  if (lane == 0) {
-    st_cluster_v2(cluster_map(&tl->xstat[r0][0], peer), s[0], s[1]);
-    st_cluster_v2(cluster_map(&tl->xstat[r1][0], peer), s[2], s[3]);
-    if (has2) st_cluster_v2(cluster_map(&tl->xstat[r2][0], peer), s[4], s[5]);
-    mbar_arrive_cluster(cluster_map(&tl->xstat_bar, peer));
-  }
-  const bool ok = mbar_wait_cl(a, &tl->xstat_bar, parity, kErrWaitFull);
-  if (!ok) return false;
-  const float2 pa = *reinterpret_cast<const float2*>(&tl->xstat[r0][0]);
-  const float2 pb = *reinterpret_cast<const float2*>(&tl->xstat[r1][0]);
-  const float2 pc = has2 ? *reinterpret_cast<const float2*>(&tl->xstat[r2][0]) : make_float2(0.f, 0.f);
-  // mean = c + S1 / D, var = S2 / D - (S1 / D)^2; n = x * rstd - mean * rstd
-  auto stats = [&](float c, float s1, float s2, int r, float& rs, float& b) {
-    const float m1 = s1 / D;
-    const float var = fmaxf(s2 / D - m1 * m1, 0.f);
-    rs = r < a.R ? rsqrtf(var + a.eps) : 0.f;
-    b = -(c + m1) * rs;
-  };
   float ra, ba, rb, bb, rc, bc;
-  stats(ca, s[0] + pa.x, s[1] + pa.y, r0, ra, ba);
-  stats(cb, s[2] + pb.x, s[3] + pb.y, r1, rb, bb);
-  stats(cc, s[4] + pc.x, s[5] + pc.y, has2 ? r2 : kFusedRows, rc, bc);
+  // mean = S1 / D, var = S2 / D - mean^2 (fp64); n = x * rstd - mean * rstd
+  auto stats64 = [&](const double* s, int r, float& rs, float& b) {
+    const double m = __ldcg(s) / D;
+    const double var = fmax(__ldcg(s + 1) / D - m * m, 0.0);
+    rs = r < a.R ? rsqrtf(static_cast<float>(var) + a.eps) : 0.f;
+    b = -static_cast<float>(m) * rs;
+  };
+  if (st != nullptr) {
+    stats64(st + 2 * r0, r0, ra, ba);
+    stats64(st + 2 * r1, r1, rb, bb);
+    if (has2) stats64(st + 2 * r2, r2, rc, bc); else rc = bc = 0.f;
+  } else {
+    // the shift of the one-pass variance: a value common to both halves (the
+    // first element of the row)
+    const float ca = r0 < a.R ? bf2f(a.x[static_cast<long long>(r0) * D]) : 0.f;
+    const float cb = r1 < a.R ? bf2f(a.x[static_cast<long long>(r1) * D]) : 0.f;
+    const float cc = (has2 && r2 < a.R) ? bf2f(a.x[static_cast<long long>(r2) * D]) : 0.f;
+    float s[6];
+    ln_half_sums<NCH>(xa, ca, s[0], s[1]);
+    ln_half_sums<NCH>(xb, cb, s[2], s[3]);
+    ln_half_sums<NCH>(xc, cc, s[4], s[5]);
+  #pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+  #pragma unroll
+      for (int i = 0; i < 6; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
+    // exchange with the peer
+    const uint32_t peer = half ^ 1;
+    if (lane == 0) {
+      st_cluster_v2(cluster_map(&tl->xstat[r0][0], peer), s[0], s[1]);
+      st_cluster_v2(cluster_map(&tl->xstat[r1][0], peer), s[2], s[3]);
+      if (has2) st_cluster_v2(cluster_map(&tl->xstat[r2][0], peer), s[4], s[5]);
+      mbar_arrive_cluster(cluster_map(&tl->xstat_bar, peer));
+    }
+    const bool ok = mbar_wait_cl(a, &tl->xstat_bar, parity, kErrWaitFull);
+    if (!ok) return false;
+    const float2 pa = *reinterpret_cast<const float2*>(&tl->xstat[r0][0]);
+    const float2 pb = *reinterpret_cast<const float2*>(&tl->xstat[r1][0]);
+    const float2 pc = has2 ? *reinterpret_cast<const float2*>(&tl->xstat[r2][0]) : make_float2(0.f, 0.f);
+    // mean = c + S1 / D, var = S2 / D - (S1 / D)^2; n = x * rstd - mean * rstd
+    auto stats = [&](float c, float s1, float s2, int r, float& rs, float& b) {
+      const float m1 = s1 / D;
+      const float var = fmaxf(s2 / D - m1 * m1, 0.f);
+      rs = r < a.R ? rsqrtf(var + a.eps) : 0.f;
+      b = -(c + m1) * rs;
+    };
+    stats(ca, s[0] + pa.x, s[1] + pa.y, r0, ra, ba);
+    stats(cb, s[2] + pb.x, s[3] + pb.y, r1, rb, bb);
+    stats(cc, s[4] + pc.x, s[5] + pc.y, has2 ? r2 : kFusedRows, rc, bc);
+  }
   if (mode == 0) {
     // AdaLN: bf16(n) * bf16(1 + scale) + bf16(shift), packed bf16 pairs
     const uint4* cm = reinterpret_cast<const uint4*>(stg + kStgLnConst) + half * (DH / 8);
@@ -521,9 +535,9 @@ __device__ bool stage_layernorm_pair_t(const FusedArgs& a, uint8_t* stg, FusedSm
 }
 
 __device__ bool stage_layernorm_pair(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, int mode, int half,
-                                     uint32_t parity) {
-  return (a.D >> 9) == 1 ? stage_layernorm_pair_t<1>(a, stg, tl, mode, half, parity)
-                         : stage_layernorm_pair_t<2>(a, stg, tl, mode, half, parity);
+                                     uint32_t parity, const double* st) {
+  return (a.D >> 9) == 1 ? stage_layernorm_pair_t<1>(a, stg, tl, mode, half, parity, st)
+                         : stage_layernorm_pair_t<2>(a, stg, tl, mode, half, parity, st);
 }
 
 // Copy columns [col0, col0 + 64 * nkb) of a bf16 [R, ld] buffer into the
@@ -704,9 +718,17 @@ __device__ __forceinline__ void gemm_epilogue(const FusedArgs& a, int p, int ste
 __device__ __forceinline__ void bar_epilogue() {
   asm volatile("barrier.sync 2, 256;" ::: "memory");
 }
+// The [32][2] row sums written by residual GEMM p of (step, block l).
+__device__ __forceinline__ double* ln_stat_slot(const FusedArgs& a, int p, int step, int l) {
+  const int k = p == kFO ? 0 : (p == kFCo ? 1 : 2);
+  return a.lnstat + ((static_cast<long long>(step) * a.L + l) * 3 + k) * kFusedRows * 2;
+}
 constexpr int kFinMaxSplits = 8;  // split partials held in flight per thread
 __device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, int step, int l, const FItem& it) {
   const int splits = f_count(a, p) / (a.D / 128);
+  // row sums for the LayerNorm that follows (cross-q after o, ffn.0 after
+  // cross-o, the next block's qkv after ffn.2; none after the last block)
+  double* st = (p == kFFfn2 && l == a.L - 1) ? nullptr : ln_stat_slot(a, p, step, l);
   bar_epilogue();
   if (threadIdx.x == 64) {
     unsigned* ctr = a.tile_ctr + (p == kFO ? 0 : (p == kFCo ? 1 : 2)) * (kFusedMaxD / 128) + it.n;
@@ -766,6 +788,27 @@ __device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, 
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = xv[e] + rbf(g[e] * rbf(sum[e] + bv[e]));
     *reinterpret_cast<uint2*>(a.x + xoff) = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+    if (st != nullptr) {
+      // the next LayerNorm's row sums: this warp holds the token's 128 features of
+      // the tile (lane = 4 features), summed in a fixed shuffle order, then one
+      // fp64 add per tile (sums of fp32 values: exact in fp64, order-free)
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float xb = rbf(o[e]);
+        s1 += xb;
+        s2 += xb * xb;
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, m);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, m);
+      }
+      if ((threadIdx.x & 31) == 0) {
+        atomicAdd(st + 2 * tok, static_cast<double>(s1));
+        atomicAdd(st + 2 * tok + 1, static_cast<double>(s2));
+      }
+    }
   }
 }
 
@@ -777,7 +820,7 @@ __device__ void residual_finalize(const FusedArgs& a, FusedSmemTail* tl, int p, 
 // to the peer (kStgXacc, [token][64] fp32) and the owners add them and finish.
 __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, FusedSmemTail* tl,
                           int p, int step, int l, const FItem& it, uint32_t& ring_it,
-                          uint32_t& items_done, uint32_t& pair_done) {
+                          uint32_t& items_done, uint32_t& pair_done, uint32_t& xstat_done) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool pair = f_pair(p);
   const int half = pair ? static_cast<int>(cluster_ctarank()) : 0;
@@ -786,9 +829,16 @@ __device__ void gemm_item(const FusedArgs& a, uint8_t* ring, uint8_t* stg, Fused
   switch (p) {
     case kFQkv:
     case kFCq:
-    case kFFfn0:
-      if (!stage_layernorm_pair(a, stg, tl, p == kFCq ? 1 : 0, half, pparity)) tl->abort = 1;
+    case kFFfn0: {
+      // the row sums of the residual GEMM before (none for block 0's qkv: the
+      // step's encoder wrote its rows), else the pair exchanges half-row sums
+      const double* st = p == kFCq ? ln_stat_slot(a, kFO, step, l)
+                                   : (p == kFFfn0 ? ln_stat_slot(a, kFCo, step, l)
+                                                  : (l > 0 ? ln_stat_slot(a, kFFfn2, step, l - 1) : nullptr));
+      if (!stage_layernorm_pair(a, stg, tl, p == kFCq ? 1 : 0, half, xstat_done & 1, st)) tl->abort = 1;
+      if (st == nullptr) ++xstat_done;
       break;
+    }
     case kFO: stage_copy(a, stg, a.ao, a.HD, it.kb0 * 64, it.nkb); break;
     case kFCo: stage_copy(a, stg, a.ci, a.HD, it.kb0 * 64, it.nkb); break;
     default: stage_copy(a, stg, a.fh, a.F, it.kb0 * 64, it.nkb); break;
@@ -1395,7 +1445,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     }
   } else {
     // ------------------------------------------------------ workers
-    uint32_t ring_it = 0, items_done = 0, epoch = 0, pair_done = 0;
+    uint32_t ring_it = 0, items_done = 0, epoch = 0, pair_done = 0, xstat_done = 0;
     const int rank = static_cast<int>(cluster_ctarank());
     const int R = a.R, D = a.D;
     const bool has_qkv = f_first(a, kFQkv, cta, G) < f_count(a, kFQkv);
@@ -1417,7 +1467,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
       for (int l = 0; l < a.L && !tl->abort; ++l) {
         // qkv
         for (int i = f_first(a, kFQkv, cta, G); i < f_count(a, kFQkv); i += f_units(kFQkv, G))
-          gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFQkv, step, l, f_item(a, kFQkv, i, rank), ring_it, items_done, pair_done, xstat_done);
         // constant K / V of the first joint item, on CTAs without a qkv item
         // (one that has one would delay its barrier arrival)
         if (!has_qkv && attn_joint_first(a, cta, G) < a.H * a.splits)
@@ -1429,11 +1479,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
           attention_item(a, stg, tl, joint_item(a, step, l, i), !has_qkv && i == attn_joint_first(a, cta, G));
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += f_units(kFO, G))
-          gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i, rank), ring_it, items_done, pair_done, xstat_done);
         if (has_cq) ln_const_prefetch(a, stg, step, l, 1, 0);
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFCq, cta, G); i < f_count(a, kFCq); i += f_units(kFCq, G))
-          gemm_item(a, ring, stg, tl, kFCq, step, l, f_item(a, kFCq, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFCq, step, l, f_item(a, kFCq, i, rank), ring_it, items_done, pair_done, xstat_done);
         if (a.C > 0 && attn_cross_first(a, cta, G) < a.H)
           attn_stage_const(a, stg, cross_item(a, step, l, attn_cross_first(a, cta, G)));
         if (!grid_sync(a, epoch, tl)) break;
@@ -1443,14 +1493,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
           attention_item(a, stg, tl, cross_item(a, step, l, h), h == attn_cross_first(a, cta, G));
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFCo, cta, G); i < f_count(a, kFCo); i += f_units(kFCo, G))
-          gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i, rank), ring_it, items_done, pair_done, xstat_done);
         if (has_ffn0) ln_const_prefetch(a, stg, step, l, 0, 3);
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFFfn0, cta, G); i < f_count(a, kFFfn0); i += f_units(kFFfn0, G))
-          gemm_item(a, ring, stg, tl, kFFfn0, step, l, f_item(a, kFFfn0, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFFfn0, step, l, f_item(a, kFFfn0, i, rank), ring_it, items_done, pair_done, xstat_done);
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFFfn2, cta, G); i < f_count(a, kFFfn2); i += f_units(kFFfn2, G))
-          gemm_item(a, ring, stg, tl, kFFfn2, step, l, f_item(a, kFFfn2, i, rank), ring_it, items_done, pair_done);
+          gemm_item(a, ring, stg, tl, kFFfn2, step, l, f_item(a, kFFfn2, i, rank), ring_it, items_done, pair_done, xstat_done);
         if (has_qkv && l + 1 < a.L) ln_const_prefetch(a, stg, step, l + 1, 0, 0);
         if (!grid_sync(a, epoch, tl)) break;
       }

@@ -49,6 +49,8 @@ struct FusedArgs {
   unsigned* tile_ctr;                // [3][kFusedMaxD / 128] split arrivals per residual GEMM tile
   __nv_bfloat16 *q, *ka, *va, *ao, *qc, *ci, *fh;
   double* ssq;                       // [N][L][3][32] q / k / cross-q sums of squares (fp64: exact, order-free)
+  double* lnstat;                    // [N][L][3][32][2] per-token sum x, sum x^2 of the bf16 residual after the
+                                     // o, cross-o and ffn.2 adds (fp64 sums of fp32 partials: order-free)
   float* apart;                      // [H][splits][32][hd + 2]
   unsigned* sync;                    // [0] barrier go word, [1] abort, [2..] merge counters [N][L][H]
   unsigned* flags;                   // per-CTA barrier arrival lines (32 words apart)
