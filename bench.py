@@ -409,16 +409,17 @@ def sub_c0(dev, peaks):
     noise = torch.randn(1, 8, 16, generator=g).to(dev)
     ts, ds = M.build_inference_schedule(CAE_STEPS, CAE_SHIFT, dtype=torch.float32)
     eng = exp.engine()
-    ms = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae), 50, warmup=5)
-    fused = eng.decode_fused
-    ms_fused = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae, decode="fused"), 50, warmup=5)
+    with ClockSampler(dev.index or 0) as clk:
+        ms = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae), 50, warmup=5)
+        fused = eng.decode_fused
+        ms_fused = time_calls(lambda: eng.chunk_decode(noise, ts, ds, ctx, ae, decode="fused"), 50, warmup=5)
     cpu_ms, cores, n = cpu_c0_ms()
     by = c0_bytes()
     return {"workload": "BASELINE configs[0]: CAE expert (hidden 32, 4 x 8 heads, 8 blocks) over a 512 x 3072 "
                         "context, 4 Euler steps + Action-VAE decode (hidden 256) -> 32 x 7, batch 1, fp32",
             "decode": "step-kernel epilogue" if fused else "separate launches (decode=auto)",
             "latency_p50_ms": p50(ms), "chunks_per_s": 1e3 / p50(ms), "reps": len(ms),
-            "epilogue_decode_p50_ms": p50(ms_fused),
+            "epilogue_decode_p50_ms": p50(ms_fused), "clocks": clk.summary(),
             "roofline": {"bound": "latency (HBM floor shown)", "bytes_per_chunk": by,
                          "floor_ms": by / (peaks["hbm"] * 1e9) * 1e3,
                          "achieved_gbs": by / (p50(ms) * 1e-3) / 1e9,
@@ -440,13 +441,14 @@ def sub_c1(dev, peaks):
         lat.copy_(noise_d)
         eng.chunk(lat, ts, ds, ctx_d, cm_d, cks, cvs, mask_d, out=lat, use_graph=use_graph)
 
-    ms = time_calls(chunk, 20, warmup=3)
-    path = eng.last_path()
+    with ClockSampler(dev.index or 0) as clk:
+        ms = time_calls(chunk, 20, warmup=3)
+        path = eng.last_path()
+        k_ms = time_fused_kernel(eng, lambda: chunk(False)) if path == "fused" else None
     work = c1_work()
-    k_ms = time_fused_kernel(eng, lambda: chunk(False)) if path == "fused" else None
     rec = {"workload": "BASELINE configs[1]: action expert 1024h/16x64/28 blocks, 1760-token K/V cache, "
                        "64-token context, 10 Euler steps, batch 1",
-           "path": path, "latency_p50_ms": p50(ms), "chunks_per_s": 1e3 / p50(ms),
+           "path": path, "latency_p50_ms": p50(ms), "chunks_per_s": 1e3 / p50(ms), "clocks": clk.summary(),
            "chunk_roofline": {"bound": "hbm", "bytes_per_chunk": work["bytes"],
                               "floor_ms": work["bytes"] / (peaks["hbm"] * 1e9) * 1e3,
                               "frac": work["bytes"] / (peaks["hbm"] * 1e9) * 1e3 / p50(ms)}}
@@ -474,8 +476,10 @@ def sub_c1(dev, peaks):
         lat8.copy_(n8)
         eng.chunk(lat8, ts, ds, ctx8, cm8, ck8, cv8, mask_d, out=lat8)
 
-    ms8 = time_calls(chunk8, 10, warmup=3)
-    rec["batch8"] = {"path": eng.last_path(), "latency_p50_ms": p50(ms8), "chunks_per_s": B * 1e3 / p50(ms8)}
+    with ClockSampler(dev.index or 0) as clk8:
+        ms8 = time_calls(chunk8, 10, warmup=3)
+    rec["batch8"] = {"path": eng.last_path(), "latency_p50_ms": p50(ms8), "chunks_per_s": B * 1e3 / p50(ms8),
+                     "clocks": clk8.summary()}
     cps, cores, n, per_eval = cpu_c1_chunks_per_s()
     rec["cpu_baseline"] = {"value": cps, "unit": "chunks/s", "cores": cores, "kind": "port",
                            "sample": f"{n} model evaluations (10 per chunk) by the CPU oracle in bf16; "
@@ -488,12 +492,13 @@ def sub_c2(vid, dev, peaks, cpu):
     lat, ctx, cm = lat.to(dev), ctx.to(dev), cm.to(dev)
     t = torch.full((1,), VIDEO_T).bfloat16()
     eng = vid.engine()
-    ms = time_calls(lambda: eng.prefill(lat, t, ctx, cm), 10, warmup=3)
+    with ClockSampler(dev.index or 0) as clk:
+        ms = time_calls(lambda: eng.prefill(lat, t, ctx, cm), 10, warmup=3)
     fl = backbone_flops(1760, 352, VIDEO_CTX)
     ach = fl / (p50(ms) * 1e-3) / 1e12
     return {"workload": "BASELINE configs[2]: Wan2.2-5B-shaped backbone forward (30 blocks, 1760 tokens, 64 "
                         "context tokens), per-layer K/V cache out, batch 1",
-            "latency_p50_ms": p50(ms),
+            "latency_p50_ms": p50(ms), "clocks": clk.summary(),
             "roofline": {"bound": "tensor", "flops": fl, "achieved": ach, "peak": peaks["tc_sustained"],
                          "unit": "TFLOP/s", "frac": ach / peaks["tc_sustained"],
                          "frac_of_burst": ach / peaks["tc"], "peak_source": peaks["source"]},
