@@ -1168,6 +1168,12 @@ int gemm_plan(GemmPlan* p, const void* A, long long lda, const void* B, long lon
       // the tile width while the tiles still fit one wave, so that the weight
       // stream is spread over more SMs
       while (bn > 32 && (bn & (bn - 1)) == 0 && mt * ((N + bn / 2 - 1) / (bn / 2)) <= sms) bn /= 2;
+    } else if (splits <= 1 && epi.features_on_a) {
+      // weights as A with a few hundred token columns and no split-K (the
+      // action expert's ffn.0 at batch 8: 32 feature tiles x one 256-token
+      // tile): narrower token tiles while they fit one wave spread the weight
+      // stream (re-read from L2 per token tile) over more SMs
+      while (bn > 64 && (bn & (bn - 1)) == 0 && mt * ((N + bn / 2 - 1) / (bn / 2)) <= sms) bn /= 2;
     }
   }
   const int kb_total = (K + kBK - 1) / kBK;
