@@ -364,7 +364,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
     aa.nsplit = attn_auto_splits(io.batch * g.num_heads * attn_query_tiles(Sa), skv,
                                  &aa.keys_per_split);
     aa.status = c.e->status;
-    FAM_LAUNCH(launch_attention(aa, io.batch, g.head_dim, c.st, c.pdl));
+    FAM_LAUNCH(launch_attention_auto(aa, io.batch, g.head_dim, c.st, c.pdl));
 
     FAM_TRYI(gemm_w(c, ly.o_w, nullptr, D, HD, aa.out, HD, rows, c.L.s_o, kActNone, part, D, true));
     ResidNormArgs r1 = {};
@@ -424,7 +424,7 @@ int enqueue_step(const Ctx& c, int step, const void* latent, void* vel, float de
       ca.counters = wsp<int>(c, c.L.ctr);
       ca.part = wsp<float>(c, c.L.apart);
       ca.status = c.e->status;
-      FAM_LAUNCH(launch_attention(ca, io.batch, g.head_dim, c.st, c.pdl));
+      FAM_LAUNCH(launch_attention_auto(ca, io.batch, g.head_dim, c.st, c.pdl));
       FAM_TRYI(gemm_w(c, ly.co_w, nullptr, D, HD, ca.out, HD, rows, c.L.s_co, kActNone, part, D, true));
     }
     ResidNormArgs r2 = {};

@@ -103,7 +103,8 @@ int fam_attention_workspace_size(const fam_attention_desc* d, size_t* bytes) {
   const int rc = attention_prepare(d, &a, &s);
   if (rc) return rc;
   *bytes = s.total;
-  if (attention_use_tc(d, a)) *bytes = (s.total + 255) / 256 * 256 + attention_tc_vt_bytes(d->batch, d->heads, a.S1);
+  if (d->kv_splits <= 0 && attention_short_tc_taken(a, d->batch, d->head_dim)) *bytes = 0;  // one CTA per (batch, head)
+  else if (attention_use_tc(d, a)) *bytes = (s.total + 255) / 256 * 256 + attention_tc_vt_bytes(d->batch, d->heads, a.S1);
   return FAM_OK;
 }
 
@@ -113,9 +114,14 @@ int fam_attention(const fam_attention_desc* d, void* workspace, size_t workspace
   AttnScratch s;
   int rc = attention_prepare(d, &a, &s);
   if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d->kv_splits <= 0 && attention_short_tc_taken(a, d->batch, d->head_dim)) {
+    // short query sets on tcgen05: one CTA per (batch, head), no split scratch
+    a.status = device_status_word();
+    return check_cuda(launch_attention_auto(a, d->batch, d->head_dim, st, false), "attention launch");
+  }
   if (a.nsplit > 1 && (workspace == nullptr || workspace_bytes < s.total))
     return set_error("attention: workspace of %zu bytes needed, %zu given", s.total, workspace_bytes);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (attention_use_tc(d, a)) {
     const size_t off = (s.total + 255) / 256 * 256;
     const size_t need = off + attention_tc_vt_bytes(d->batch, d->heads, a.S1);

@@ -50,8 +50,7 @@ int* device_status_word() {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
-bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                       uint64_t row_stride, uint32_t box_rows) {
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   std::call_once(g_encode_once, []() {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -60,7 +59,12 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
         q == cudaDriverEntryPointSuccess)
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
-  if (g_encode == nullptr) return false;
+  return g_encode;
+}
+
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                       uint64_t row_stride, uint32_t box_rows) {
+  if (tmap_encoder() == nullptr) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
   cuuint32_t box[2] = {64u, box_rows};
@@ -69,6 +73,23 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 3-D bf16 tensor map over [batch, rows, cols] with row stride `row_stride` and
+// batch stride `batch_stride` elements; box = 64 columns x box_rows rows x 1,
+// 128-byte swizzle, out-of-bounds elements (past a batch's rows) read as zero.
+bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t batch, uint64_t rows, uint64_t cols,
+                       uint64_t row_stride, uint64_t batch_stride, uint32_t box_rows) {
+  if (tmap_encoder() == nullptr) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * 2), static_cast<cuuint64_t>(batch_stride * 2)};
+  cuuint32_t box[3] = {64u, box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

@@ -24,6 +24,12 @@ int* device_status_word();
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                        uint64_t row_stride, uint32_t box_rows);
 
+// 3-D bf16 tensor map over [batch, rows, cols] (row / batch strides in elements);
+// box = 64 columns x box_rows rows x 1 batch, 128-byte swizzle, rows past a
+// batch's end read as zero.
+bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t batch, uint64_t rows, uint64_t cols,
+                       uint64_t row_stride, uint64_t batch_stride, uint32_t box_rows);
+
 // ------------------------------------------------------------------ GEMM
 enum EpiKind : int { kEpiStore = 0, kEpiPartial = 1, kEpiResidual = 2 };
 enum ActKind : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };

@@ -163,5 +163,10 @@ int attn_query_tiles(int Sq);
 // Key splits that fill about two waves of the GPU with >= 128 keys each.
 int attn_auto_splits(int units, int skv, int* keys_per_split);
 cudaError_t launch_attention(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl);
+// The short-query attention on tcgen05 (attention_short_tc.cu: head dim 64, at
+// most 32 queries, no first-frame rule, batch x heads >= 128, TMA-compatible
+// strides) when the launch qualifies, attention_kernel otherwise.
+cudaError_t launch_attention_auto(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl);
+bool attention_short_tc_taken(const AttnArgs& a, int B, int head_dim);
 
 }  // namespace fam

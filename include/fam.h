@@ -168,6 +168,10 @@ typedef struct fam_attention_desc {
   int64_t out_batch_stride, out_token_stride;
 } fam_attention_desc;
 
+/* Bytes of device workspace fam_attention needs for this descriptor: 0 when
+ * the call runs without split partials (one CTA per batch and head, e.g. the
+ * tcgen05 short-query kernel that a descriptor with kv_splits = 0, head_dim
+ * 64, q_tokens <= 32 and batch x heads >= 128 selects). */
 FAM_API int fam_attention_workspace_size(const fam_attention_desc* desc, size_t* bytes);
 FAM_API int fam_attention(const fam_attention_desc* desc, void* workspace, size_t workspace_bytes,
                           void* stream);

@@ -109,3 +109,89 @@ def test_tcgen05_attention_over_second_key_source(fam_ops, B, S, C, H):
     err = (out.float() - ref).abs().max().item()
     cos = torch.nn.functional.cosine_similarity(out.double().flatten(), ref.double().flatten(), dim=0).item()
     assert err < 2e-2 and cos >= 0.999, (err, cos)
+
+
+def _workspace_bytes(fam_ops, q, k1, v1, H, k2=None, v2=None, mask=None, key_mask=None):
+    import ctypes as C
+    from importlib import import_module
+    d, _ = fam_ops.attention_desc(q, k1, v1, H, k2, v2, mask, key_mask)
+    n = C.c_size_t()
+    lib = import_module("faster-action-models_b200._lib").lib()
+    assert lib.fam_attention_workspace_size(C.byref(d), C.byref(n)) == 0
+    return n.value
+
+
+@pytest.mark.parametrize("B,H,Sq,S1,S2,use_mask,use_km", [
+    (8, 16, 32, 1760, 32, True, False),   # the action expert's joint attention at batch 8
+    (8, 16, 32, 64, 0, False, True),      # its cross attention over the context tokens
+    (4, 32, 20, 300, 17, True, True),     # ragged: 20 queries, sources not multiples of 128 keys
+    (2, 64, 32, 129, 0, False, False),
+    (128, 1, 1, 5, 3, True, False)])
+def test_tcgen05_short_query_attention(fam_ops, B, H, Sq, S1, S2, use_mask, use_km):
+    """At most 32 queries per (batch, head), head dim 64, >= 128 (batch, head) pairs: the
+    tcgen05 kernel with the queries replicated over the four TMEM lane quarters (each
+    softmax warp owns a quarter of every key block), V as an MN-major operand, two key
+    sources read through 3-D tensor maps, masks per query row and per batch key.  It needs
+    no split workspace, which is how the test knows it ran; one query row is fully masked
+    (output zero, as in the split-KV kernel)."""
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + Sq + S1 + S2)
+    HD = H * 64
+    q = torch.randn(B, Sq, HD, device="cuda", generator=g).bfloat16()
+    k1 = torch.randn(B, S1, HD, device="cuda", generator=g).bfloat16()
+    v1 = torch.randn(B, S1, HD, device="cuda", generator=g).bfloat16()
+    k2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16() if S2 else None
+    v2 = torch.randn(B, S2, HD, device="cuda", generator=g).bfloat16() if S2 else None
+    S = S1 + S2
+    mask = torch.ones(Sq, S, dtype=torch.bool, device="cuda")
+    if use_mask:
+        mask = torch.rand(Sq, S, device="cuda", generator=g) > 0.3
+        mask[:, -1] = True
+        if Sq > 1:
+            mask[Sq // 2] = False  # a fully masked query row
+    km = None
+    if use_km:
+        km = (torch.rand(B, S, device="cuda", generator=g) > 0.2).to(torch.uint8)
+        km[:, -1] = 1
+    m8 = mask.to(torch.uint8) if use_mask else None
+    assert _workspace_bytes(fam_ops, q, k1, v1, H, k2, v2, m8, km) == 0
+    out = fam_ops.attention(q, k1, v1, H, k2, v2, mask=m8, key_mask=km)
+    torch.cuda.synchronize()
+    kk = torch.cat([k1, k2], 1) if S2 else k1
+    vv = torch.cat([v1, v2], 1) if S2 else v1
+    refs = []
+    for i in range(B):
+        mi = mask & km[i].bool().view(1, S) if km is not None else mask
+        refs.append(_ref(q[i:i + 1], kk[i:i + 1], vv[i:i + 1], H, mi.contiguous()))
+    ref = torch.cat(refs)
+    live = mask.any(1) if km is None else torch.ones(Sq, dtype=torch.bool, device="cuda")
+    if use_mask and Sq > 1:
+        assert torch.all(out[:, Sq // 2] == 0)
+        live = live.clone()
+        live[Sq // 2] = False
+    o, r = out.float()[:, live], ref[:, live]
+    err = (o - r).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(o.double().flatten(), r.double().flatten(), dim=0).item()
+    assert err < 2e-2 and cos >= 0.999, (err, cos)
+    # the same call with explicit splits takes the split-KV kernel: both agree
+    alt = fam_ops.attention(q, k1, v1, H, k2, v2, mask=m8, key_mask=km, kv_splits=2)
+    torch.cuda.synchronize()
+    assert (alt.float()[:, live] - o).abs().max().item() < 2e-2
+
+
+def test_tcgen05_short_query_attention_sharp_rising_logits(fam_ops):
+    """Scores that grow along the keys move each quarter's running maximum by more than
+    the lazy-rescale margin again and again (O rows rescaled in TMEM)."""
+    B, H, Sq, S = 8, 16, 32, 1792
+    g = torch.Generator(device="cuda").manual_seed(11)
+    HD = H * 64
+    q = (3.0 * torch.randn(B, Sq, HD, device="cuda", generator=g)).bfloat16()
+    ramp = torch.linspace(0.2, 3.0, S, device="cuda").view(1, S, 1)
+    k = (torch.randn(B, S, HD, device="cuda", generator=g) * ramp).bfloat16()
+    v = torch.randn(B, S, HD, device="cuda", generator=g).bfloat16()
+    assert _workspace_bytes(fam_ops, q, k, v, H) == 0
+    out = fam_ops.attention(q, k, v, H)
+    torch.cuda.synchronize()
+    ref = _ref(q, k, v, H, torch.ones(Sq, S, dtype=torch.bool, device="cuda"))
+    err = (out.float() - ref).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(out.double().flatten(), ref.double().flatten(), dim=0).item()
+    assert err < 2e-2 and cos >= 0.999, (err, cos)
