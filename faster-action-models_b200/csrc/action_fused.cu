@@ -19,8 +19,11 @@
 //                       RoPE, GELU; the residual GEMMs store split partials
 //                       and the last split of a tile completes the gated
 //                       residual add with the reference's bf16 roundings).
-//                       Attention phases use bf16 mma.sync fragments over
-//                       cp.async-staged K/V.
+//                       Attention phases stage K / V with cp.async in the
+//                       128-byte-swizzled layout and run S = Q K^T and P.V on
+//                       tcgen05 (S, P and O in TMEM; the 32 queries replicated
+//                       over the four TMEM lane quarters, each softmax warp
+//                       owning a quarter of the item's keys).
 // Every cross-CTA sum is order-independent (fp64 sums of squares, split
 // partials summed in split order), so a launch is deterministic.
 //
@@ -51,7 +54,6 @@ namespace fam {
 
 constexpr int kATile = 128 * 64 * 2;          // one weight tile (16 KB)
 constexpr int kBBlock = kFusedRows * 128;     // one B k-block: 32 rows x 128 B (4 KB)
-constexpr int kKvRow = 64 + 8;                // padded K/V row (head_dim 64)
 constexpr int kFusedIssuers = 4;               // MMA-issuing threads per GEMM item
 constexpr int kFusedIssuer1 = 6;               // warps kFusedIssuer1.. host issuers 1..
 static_assert(kFusedIssuer1 + kFusedIssuers - 1 <= kFusedThreads / 32 && kFusedIssuers % 2 == 0, "issuer warps");
@@ -76,7 +78,6 @@ struct FusedSmemTail {
   uint32_t tmem;
   volatile int abort;
   float stat[kFusedRows][2];
-  float scale[2][kFusedRows];                 // per-row q scale, per-key scale
   int last;
   int fin;                                    // this residual item completes its tile
   // pair items: the peer CTA writes its half-row LayerNorm sums here and
@@ -88,6 +89,8 @@ struct FusedSmemTail {
   uint64_t xstat_bar;
   uint64_t xacc_bar;
   uint64_t xsend_bar;
+  uint64_t attn_s;     // S = Q K^T of the attention item complete
+  uint64_t attn_o[4];  // softmax warp w's P.V complete
 };
 
 static_assert(offsetof(FusedSmemTail, xstat) % 8 == 0, "xstat rows are accessed as float2");
@@ -972,24 +975,39 @@ struct AttnItem {
   int nsplit;
 };
 
-// Staging of an attention item: K / V [256][kKvRow] each, the attend bytes
-// [32][256], the key mask [256] and the q rows [32][kKvRow].
+// Staging of an attention item (1024-byte aligned): V / K [256 keys][64] each
+// and the q rows replicated four times [4 x 32][64], all in the 128-byte
+// swizzle the tcgen05 descriptors read (16-byte chunk c of row r at r * 128 +
+// (c ^ (r & 7)) * 16), then the attend bytes [32][256], the key mask [256] and
+// the per-key logit factors [256] fp32.
 struct AttnSmem {
-  __nv_bfloat16 *sK, *sV, *sQ;
+  uint8_t *sK, *sV, *sQ;
   uint8_t *sM, *sKm;
+  float* sKsc;
 };
 __device__ __forceinline__ AttnSmem attn_smem(uint8_t* stg) {
   AttnSmem m;
-  m.sK = reinterpret_cast<__nv_bfloat16*>(stg);
-  m.sV = m.sK + 256 * kKvRow;
-  m.sM = reinterpret_cast<uint8_t*>(m.sV + 256 * kKvRow);
+  m.sV = stg;
+  m.sK = stg + 256 * 128;
+  m.sQ = stg + 2 * 256 * 128;
+  m.sM = m.sQ + 4 * kFusedRows * 128;
   m.sKm = m.sM + kFusedRows * 256;
-  m.sQ = reinterpret_cast<__nv_bfloat16*>(m.sKm + 256);
+  m.sKsc = reinterpret_cast<float*>(m.sKm + 256);
   return m;
 }
-static_assert(2 * 256 * (64 + 8) * 2 + kFusedRows * 256 + 256 + kFusedRows * (64 + 8) * 2 + 256 * 4 <=
-                  kFusedStaging,
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+static_assert(2 * 256 * 128 + 4 * kFusedRows * 128 + kFusedRows * 256 + 256 + 256 * 4 <= kFusedStaging,
               "attention staging");
+static_assert(kFusedRing * kATile + kFusedStaging + sizeof(FusedSmemTail) + 1024 <= 232448,
+              "fused shared memory within the 227 KB per-CTA limit");
+// TMEM of the attention items: S [128 lanes][256 keys] fp32, then softmax warp
+// w's O partial [128][64] fp32 over its own S columns [64 w, 64 w + 64); P
+// [128][256] as bf16 pairs (the GEMM accumulators use columns [0, 128) in
+// their own phases)
+constexpr uint32_t kAttnColS = 0, kAttnColP = 256;
+constexpr uint32_t kFusedTmemCols = 512;
 static_assert(kFusedMaxSplits * (kFusedRows * 64 + kFusedRows * 2) * 4 + (kFusedMaxSplits + 1) * kFusedRows * 4 <=
                   kFusedStaging,
               "split partials of a head fit the staging");
@@ -1005,9 +1023,9 @@ __device__ void attn_stage_const(const FusedArgs& a, uint8_t* stg, const AttnIte
     const int r = idx >> 3, c = idx & 7;
     const int j = t.k0 + r;
     if (r < nkeys && j >= t.S1) continue;  // a fresh key: staged after the barrier
-    const bool valid = r < nkeys;
-    cp_async16(m.sK + r * kKvRow + c * 8, valid ? t.k1 + j * t.ts1 + c * 8 : a.q, valid);
-    cp_async16(m.sV + r * kKvRow + c * 8, valid ? t.v1 + j * t.ts1 + c * 8 : a.q, valid);
+    const bool valid = r < nkeys;            // keys past the split read as zeros
+    cp_async16(m.sK + sw128_off(r, c), valid ? t.k1 + j * t.ts1 + c * 8 : a.q, valid);
+    cp_async16(m.sV + sw128_off(r, c), valid ? t.v1 + j * t.ts1 + c * 8 : a.q, valid);
   }
   if (t.mask2d != nullptr) {
     if (t.mrs % 16 == 0 && (reinterpret_cast<uintptr_t>(t.mask2d) & 15) == 0 && t.k0 % 16 == 0) {
@@ -1035,172 +1053,192 @@ __device__ void attn_stage_const(const FusedArgs& a, uint8_t* stg, const AttnIte
 }
 
 __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* tl, const AttnItem& t,
-                               bool prefetched) {
+                               bool prefetched, uint32_t& attn_it, uint32_t& pv_it) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tq = lane & 3;
   const AttnSmem m = attn_smem(stg);
-  __nv_bfloat16* sK = m.sK;
-  __nv_bfloat16* sV = m.sV;
-  const uint8_t* sM = m.sM;
-  const uint8_t* sKm = m.sKm;
   const int nkeys = t.k1end - t.k0;
+  // the q chunk and the q-row scale of this thread, loaded first so their L2
+  // latency overlaps the staging below (rows >= R stay zero)
+  const int qi = threadIdx.x - 32, qr = qi >> 3, qc = qi & 7;
+  const bool qthread = qi < kFusedRows * 8;
+  uint4 qraw = make_uint4(0u, 0u, 0u, 0u);
+  double qss = 0.0;
+  if (qthread && qr < a.R) {
+    qraw = __ldcg(reinterpret_cast<const uint4*>(t.qp + qr * t.qts + qc * 8));
+    if (t.qscale != nullptr) qss = __ldcg(t.qscale + qr);
+  }
   if (!prefetched) attn_stage_const(a, stg, t);
-  // fresh keys (source 2) and the q rows: written by the phase before
+  // fresh keys (source 2): written by the phase before
   for (int idx = threadIdx.x - 32; idx < 256 * 8; idx += kFusedWorkers) {
     const int r = idx >> 3, c = idx & 7;
     const int j = t.k0 + r;
     if (r >= nkeys || j < t.S1) continue;
-    cp_async16(sK + r * kKvRow + c * 8, t.k2 + (j - t.S1) * t.ts2 + c * 8, true);
-    cp_async16(sV + r * kKvRow + c * 8, t.v2 + (j - t.S1) * t.ts2 + c * 8, true);
-  }
-  for (int idx = threadIdx.x - 32; idx < kFusedRows * 8; idx += kFusedWorkers) {
-    const int r = idx >> 3, c = idx & 7;
-    cp_async16(m.sQ + r * kKvRow + c * 8, r < a.R ? t.qp + r * t.qts + c * 8 : a.q, r < a.R);
+    cp_async16(m.sK + sw128_off(r, c), t.k2 + (j - t.S1) * t.ts2 + c * 8, true);
+    cp_async16(m.sV + sw128_off(r, c), t.v2 + (j - t.S1) * t.ts2 + c * 8, true);
   }
   cp_async_commit();
-  // per-row q scale and per-key scale of the fresh keys (RMSNorm as a scale)
-  for (int i = threadIdx.x - 32; i < kFusedRows; i += kFusedWorkers) {
-    tl->scale[0][i] = (t.qscale != nullptr && i < a.R)
-                          ? rsqrtf(static_cast<float>(__ldcg(t.qscale + i)) / a.HD + a.eps) : 1.f;
-    tl->scale[1][i] = (t.kscale2 != nullptr && i < t.S2)
-                          ? rsqrtf(static_cast<float>(__ldcg(t.kscale2 + i)) / a.HD + a.eps) : 1.f;
+  // q rows scaled by their RMSNorm scale and rounded to bf16, written four times
+  // (TMEM lane quarter w of S reads rows 32 w .. 32 w + 31)
+  if (qthread) {
+    const float sc = (t.qscale != nullptr && qr < a.R) ? rsqrtf(static_cast<float>(qss) / a.HD + a.eps) : 1.f;
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&qraw);
+    const uint4 u = make_uint4(pack_bf16(__low2float(h2[0]) * sc, __high2float(h2[0]) * sc),
+                               pack_bf16(__low2float(h2[1]) * sc, __high2float(h2[1]) * sc),
+                               pack_bf16(__low2float(h2[2]) * sc, __high2float(h2[2]) * sc),
+                               pack_bf16(__low2float(h2[3]) * sc, __high2float(h2[3]) * sc));
+#pragma unroll
+    for (int rep = 0; rep < 4; ++rep) *reinterpret_cast<uint4*>(m.sQ + sw128_off(rep * kFusedRows + qr, qc)) = u;
   }
   cp_async_wait<0>();
+  fence_async_smem();  // the staged K / V / Q (generic-proxy writes) before the MMAs read them
+  tc_fence_before();
   bar_workers();
-  // per-key logit factor: scale_log2 x the RMSNorm scale of a fresh key, 0
-  // for a key outside the split or masked out by the key mask
-  const int k0 = t.k0, S1 = t.S1;
-  float* sKsc = reinterpret_cast<float*>(m.sQ + kFusedRows * kKvRow);
-  for (int jj = threadIdx.x - 32; jj < 256; jj += kFusedWorkers) {
-    const int j = k0 + jj;
-    const float ks = j >= S1 && jj < nkeys ? tl->scale[1][j - S1] : 1.f;
-    sKsc[jj] = (jj < nkeys && sKm[jj] != 0) ? ks * a.scale_log2 : 0.f;
-  }
-  bar_workers();
+  tc_fence_after();
 
-  const int wi = warp - 1;                 // 0..10
-  const bool active = wi < 8;
-  const int qg = wi & 1, kq = wi >> 1;     // query group, key block
-  float o[8][4];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const int r0 = qg * 16 + g, r1 = r0 + 8;
-  if (active) {
-    // Q fragments, scaled per row
-    uint32_t qf[4][4];
-    const float s0 = tl->scale[0][r0], s1 = tl->scale[0][r1];
-    const bool v0 = r0 < a.R, v1 = r1 < a.R;
+  // S = Q K^T: M = 128 (four copies of the 32 queries), N = the item's keys
+  // rounded up to 16, K = 64
+  const uint32_t par = attn_it & 1;
+  ++attn_it;
+  const int nk16 = (nkeys + 15) & ~15;
+  if (threadIdx.x == 32) {
+    const uint32_t idesc = umma_idesc_bf16(128, nk16);
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int col = kk * 16 + hh * 8 + 2 * tq;
-        float x0 = 0.f, x1 = 0.f, y0 = 0.f, y1 = 0.f;
-        if (v0) {
-          const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(m.sQ + r0 * kKvRow + col);
-          x0 = __low2float(p) * s0;
-          x1 = __high2float(p) * s0;
-        }
-        if (v1) {
-          const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(m.sQ + r1 * kKvRow + col);
-          y0 = __low2float(p) * s1;
-          y1 = __high2float(p) * s1;
-        }
-        qf[kk][hh * 2 + 0] = pack_bf16(x0, x1);
-        qf[kk][hh * 2 + 1] = pack_bf16(y0, y1);
-      }
-    }
-    float s[8][4];
-    const int kb = kq * 64;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-      const __nv_bfloat16* kr = sK + (kb + n * 8 + g) * kKvRow;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t bfr[2];
-        bfr[0] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 2 * tq);
-        bfr[1] = *reinterpret_cast<const uint32_t*>(kr + kk * 16 + 8 + 2 * tq);
-        mma_bf16_16816(s[n], qf[kk], bfr);
-      }
-    }
-    // masks: the key factor (2 per n, one 8-byte load) and the attend bytes of
-    // rows r0 / r1 (2 per n, one 2-byte load each)
-    const bool m2 = t.mask2d != nullptr;
-    const uint8_t* mr0 = sM + r0 * 256;
-    const uint8_t* mr1 = sM + r1 * 256;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const int jj = kb + n * 8 + 2 * tq;
-      const float2 kf = *reinterpret_cast<const float2*>(sKsc + jj);
-      const unsigned a0 = m2 ? *reinterpret_cast<const uint16_t*>(mr0 + jj) : 0x0101u;
-      const unsigned a1 = m2 ? *reinterpret_cast<const uint16_t*>(mr1 + jj) : 0x0101u;
-      const bool ok00 = v0 && kf.x != 0.f && (a0 & 0xffu), ok01 = v0 && kf.y != 0.f && (a0 >> 8);
-      const bool ok10 = v1 && kf.x != 0.f && (a1 & 0xffu), ok11 = v1 && kf.y != 0.f && (a1 >> 8);
-      s[n][0] = ok00 ? s[n][0] * kf.x : -INFINITY;
-      s[n][1] = ok01 ? s[n][1] * kf.y : -INFINITY;
-      s[n][2] = ok10 ? s[n][2] * kf.x : -INFINITY;
-      s[n][3] = ok11 ? s[n][3] * kf.y : -INFINITY;
-      mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    m0 = mx0;
-    m1 = mx1;
-    const float b0 = m0 == -INFINITY ? 0.f : m0, b1 = m1 == -INFINITY ? 0.f : m1;
-    uint32_t pf[4][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float p0 = exp2f(s[n][0] - b0), p1 = exp2f(s[n][1] - b0);
-      const float p2 = exp2f(s[n][2] - b1), p3 = exp2f(s[n][3] - b1);
-      l0 += p0 + p1;
-      l1 += p2 + p3;
-      const int ks2 = n >> 1, hi = n & 1;
-      pf[ks2][hi ? 2 : 0] = pack_bf16(p0, p1);
-      pf[ks2][hi ? 3 : 1] = pack_bf16(p2, p3);
-    }
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-#pragma unroll
-    for (int ks2 = 0; ks2 < 4; ++ks2) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t bfr[2];
-        const int r = kb + ks2 * 16 + (lane & 15);
-        const uint32_t addr = smem_u32(sV + r * kKvRow + i * 8);
-        asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
-                     : "=r"(bfr[0]), "=r"(bfr[1])
-                     : "r"(addr));
-        mma_bf16_16816(o[i], pf[ks2], bfr);
-      }
-    }
+    for (int kk = 0; kk < 4; ++kk)
+      umma_bf16_ss(tl->tmem + kAttnColS, umma_desc_sw128(m.sQ) + 2 * kk, umma_desc_sw128(m.sK) + 2 * kk, idesc,
+                   kk > 0 ? 1u : 0u);
+    umma_commit(&tl->attn_s);
   }
-  bar_workers();  // K/V staging no longer read: reuse it for the block merge
-  // block partials: O [4][32][kCombRow] (padded rows: conflict-free stores),
-  // (m, l) [4][32][2]
+  // softmax warps 4..7: warp w owns keys [64 w, 64 w + 64) of the item for every
+  // query (its TMEM lane quarter holds all 32 query rows).  It writes its P
+  // columns [32 w, 32 w + 32), issues P.V over its own keys into its own S
+  // columns (no other warp reads them) and reads back its lanes' O rows: the
+  // four warps never wait for one another.  Rows of the other lane quarters in
+  // that product are zero or stale and are not read.
+  // quarter partials O [4][32][kCombRow] (padded rows: conflict-free stores) and
+  // (m, l) [4][32][2] over K and Q, which only the S MMA reads: a warp writes
+  // them after S is complete (V stays: other warps' P.V may still read it)
   constexpr int kCombRow = 64 + 4;
-  float* comb = reinterpret_cast<float*>(stg);
+  static_assert(4 * kFusedRows * (kCombRow + 2) * 4 <= 256 * 128 + 4 * kFusedRows * 128, "quarter partials");
+  float* comb = reinterpret_cast<float*>(m.sK);
   float* cml = comb + 4 * kFusedRows * kCombRow;
-  if (active) {
+  const bool smx = warp >= 4 && warp < 8;
+  const int wq = warp - 4, q = lane;
+  const uint32_t lane_addr = tl->tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  bool ok = true;
+  if (smx && 64 * wq < nkeys) {
+    // per-key logit factor of the warp's keys: scale_log2 x the RMSNorm scale of
+    // a fresh key, 0 for a key outside the split or masked out by the key mask
+    float* kfw = m.sKsc + 64 * wq;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int d = i * 8 + 2 * tq;
-      *reinterpret_cast<float2*>(comb + (kq * kFusedRows + r0) * kCombRow + d) = make_float2(o[i][0], o[i][1]);
-      *reinterpret_cast<float2*>(comb + (kq * kFusedRows + r1) * kCombRow + d) = make_float2(o[i][2], o[i][3]);
+    for (int h = 0; h < 2; ++h) {
+      const int jj = 64 * wq + 32 * h + lane, j = t.k0 + jj;
+      float ks = 1.f;
+      if (t.kscale2 != nullptr && j >= t.S1 && jj < nkeys)
+        ks = rsqrtf(static_cast<float>(__ldcg(t.kscale2 + (j - t.S1))) / a.HD + a.eps);
+      kfw[32 * h + lane] = (jj < nkeys && m.sKm[jj] != 0) ? ks * a.scale_log2 : 0.f;
     }
-    if (tq == 0) {
-      cml[(kq * kFusedRows + r0) * 2] = m0;
-      cml[(kq * kFusedRows + r0) * 2 + 1] = l0;
-      cml[(kq * kFusedRows + r1) * 2] = m1;
-      cml[(kq * kFusedRows + r1) * 2 + 1] = l1;
+    __syncwarp();
+    bool got = mbar_wait(&tl->attn_s, par, a.status, kErrWaitAccum);
+    ok = __all_sync(0xffffffffu, got);
+    float mq = -INFINITY, lq = 0.f;
+    if (ok) {
+      tc_fence_after();
+      float sv[64];
+      tmem_ld32(lane_addr + kAttnColS + 64 * wq, sv);
+      tmem_ld32(lane_addr + kAttnColS + 64 * wq + 32, sv + 32);
+      const bool v0 = q < a.R;
+      // attend bits of row q for the warp's 64 keys
+      uint32_t mb0 = 0xffffffffu, mb1 = 0xffffffffu;
+      if (t.mask2d != nullptr) {
+        uint32_t w[16];
+        const uint4* src = reinterpret_cast<const uint4*>(m.sM + q * 256 + 64 * wq);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 u = src[i];
+          w[4 * i] = u.x;
+          w[4 * i + 1] = u.y;
+          w[4 * i + 2] = u.z;
+          w[4 * i + 3] = u.w;
+        }
+        mb0 = mb1 = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            mb0 |= (((w[i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
+            mb1 |= (((w[8 + i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
+          }
+      }
+      tmem_wait_ld();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float kf = m.sKsc[64 * wq + i];
+        const bool bit = ((i < 32 ? mb0 >> i : mb1 >> (i - 32)) & 1u) != 0u;
+        sv[i] = (v0 && kf != 0.f && bit) ? sv[i] * kf : -INFINITY;
+        mx = fmaxf(mx, sv[i]);
+      }
+      const float base = mx == -INFINITY ? 0.f : mx;
+      uint32_t pk[32];
+      float ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = exp2f(sv[i] - base), p1 = exp2f(sv[i + 1] - base);
+        ps += p0 + p1;
+        pk[i / 2] = pack_bf16(p0, p1);
+      }
+      tmem_st16(lane_addr + kAttnColP + 32 * wq, pk);
+      tmem_st16(lane_addr + kAttnColP + 32 * wq + 16, pk + 16);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      mq = mx;
+      lq = ps;
+      // P.V over this warp's keys < nkeys (16 per step): A = its P columns, B =
+      // the V rows as staged ([keys, dims]: MN-major), D = its S columns
+      if (lane == 0) {
+        tc_fence_after();
+        const uint32_t idesc = umma_idesc_bf16_bmn(128, 64);
+        const int steps = (min(64, nkeys - 64 * wq) + 15) / 16;
+        for (int kk = 0; kk < steps; ++kk)
+          umma_bf16_ts(lane_addr - (static_cast<uint32_t>(wq * 32) << 16) + kAttnColS + 64 * wq,
+                       tl->tmem + kAttnColP + 32 * wq + 8 * kk, umma_desc_sw128_mn(m.sV + (4 * wq + kk) * 2048),
+                       idesc, kk > 0 ? 1u : 0u);
+        umma_commit(&tl->attn_o[wq]);
+      }
+      __syncwarp();
+      // attn_o[w] completes only on items with keys for warp w: its own count
+      got = mbar_wait(&tl->attn_o[wq], pv_it & 1, a.status, kErrWaitAccum);
+      ++pv_it;
+      ok = __all_sync(0xffffffffu, got);
     }
+    if (ok) {
+      tc_fence_after();
+      float* orow = comb + (wq * kFusedRows + q) * kCombRow;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float ov[32];
+        tmem_ld32(lane_addr + kAttnColS + 64 * wq + 32 * c, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(orow + 32 * c)[i] = make_float4(ov[4 * i], ov[4 * i + 1], ov[4 * i + 2], ov[4 * i + 3]);
+      }
+      cml[(wq * kFusedRows + q) * 2] = mq;
+      cml[(wq * kFusedRows + q) * 2 + 1] = lq;
+    } else if (lane == 0) {
+      tl->abort = 1;
+    }
+  } else if (smx) {
+    // no keys of this item: a zero partial, written once S (which reads K and
+    // Q) is complete
+    const bool got = mbar_wait(&tl->attn_s, par, a.status, kErrWaitAccum);
+    if (!__all_sync(0xffffffffu, got) && lane == 0) tl->abort = 1;
+    float* orow = comb + (wq * kFusedRows + q) * kCombRow;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) reinterpret_cast<float4*>(orow)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    cml[(wq * kFusedRows + q) * 2] = -INFINITY;
+    cml[(wq * kFusedRows + q) * 2 + 1] = 0.f;
   }
   bar_workers();
   const int nsplit = t.nsplit;
@@ -1400,17 +1438,28 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     mbar_init(&tl->xstat_bar, kFusedWorkers / 32);  // one arrival per peer worker warp
     mbar_init(&tl->xacc_bar, 1);                    // own expect_tx arrival + the peer's bulk copy
     mbar_init(&tl->xsend_bar, 4);                   // lane 0 of this CTA's 4 sending warps
+    mbar_init(&tl->attn_s, 1);
+    for (int w = 0; w < 4; ++w) mbar_init(&tl->attn_o[w], 1);
     tl->abort = 0;
     fence_mbar_init();
     for (int p = 0; p < 6; ++p) tma_prefetch_desc(&a.tm[p]);
   }
   if (warp == 1) {
-    tmem_alloc(&tl->tmem, kFusedIssuers * kFusedRows);
+    tmem_alloc(&tl->tmem, kFusedTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (warp >= 4 && warp < 8) {
+    // the attention items' P columns outside a softmax warp's own quarter of
+    // the keys stay zero for the whole launch
+    const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    const uint32_t pbase = tl->tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + kAttnColP;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) tmem_st16(pbase + 16 * c, z);
+    tmem_wait_st();
+  }
 
   if (warp == 0) {
     // ------------------------------------------------ weight producer
@@ -1445,7 +1494,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
     }
   } else {
     // ------------------------------------------------------ workers
-    uint32_t ring_it = 0, items_done = 0, epoch = 0, pair_done = 0, xstat_done = 0;
+    uint32_t ring_it = 0, items_done = 0, epoch = 0, pair_done = 0, xstat_done = 0, attn_it = 0, pv_it = 0;
     const int rank = static_cast<int>(cluster_ctarank());
     const int R = a.R, D = a.D;
     const bool has_qkv = f_first(a, kFQkv, cta, G) < f_count(a, kFQkv);
@@ -1476,7 +1525,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         // joint attention: items (head, split); the first item's constant
         // K / V were prefetched at the end of the qkv phase
         for (int i = attn_joint_first(a, cta, G); i < a.H * a.splits; i += G)
-          attention_item(a, stg, tl, joint_item(a, step, l, i), !has_qkv && i == attn_joint_first(a, cta, G));
+          attention_item(a, stg, tl, joint_item(a, step, l, i), !has_qkv && i == attn_joint_first(a, cta, G),
+                         attn_it, pv_it);
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFO, cta, G); i < f_count(a, kFO); i += f_units(kFO, G))
           gemm_item(a, ring, stg, tl, kFO, step, l, f_item(a, kFO, i, rank), ring_it, items_done, pair_done, xstat_done);
@@ -1490,7 +1540,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
         // cross attention: one item per head over the context (constant K / V
         // prefetched at the end of the cross-q phase)
         for (int h = attn_cross_first(a, cta, G); h < a.H && a.C > 0; h += G)
-          attention_item(a, stg, tl, cross_item(a, step, l, h), h == attn_cross_first(a, cta, G));
+          attention_item(a, stg, tl, cross_item(a, step, l, h), h == attn_cross_first(a, cta, G), attn_it,
+                         pv_it);
         if (!grid_sync(a, epoch, tl)) break;
         for (int i = f_first(a, kFCo, cta, G); i < f_count(a, kFCo); i += f_units(kFCo, G))
           gemm_item(a, ring, stg, tl, kFCo, step, l, f_item(a, kFCo, i, rank), ring_it, items_done, pair_done, xstat_done);
@@ -1562,7 +1613,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_chunk_kernel(const __g
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tl->tmem, kFusedIssuers * kFusedRows);
+    tmem_dealloc(tl->tmem, kFusedTmemCols);
   }
   // the peer CTA may still write into this CTA's shared memory (DSMEM) until
   // it is done too

@@ -16,7 +16,7 @@ constexpr int kFusedRows = 32;        // token rows of one sample (MMA N, zero p
 constexpr int kFusedThreads = 384;    // warp 0 weight producer, warps 1..11 workers (clusters of 2 CTAs)
 constexpr int kFusedWorkers = 352;
 constexpr int kFusedRing = 8;         // 128 x 64 bf16 weight tiles in flight per CTA (128 KB)
-constexpr int kFusedStaging = 88 * 1024;
+constexpr int kFusedStaging = 92 * 1024;
 constexpr int kFusedKeysPerSplit = 256;
 constexpr int kFusedMaxSplits = 10;   // joint-attention key splits per head (partials merged in shared memory)
 constexpr int kFusedMaxCtas = 256;  // barrier flag lines reserved
