@@ -93,6 +93,22 @@ bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t batch, uint6
   return r == CUDA_SUCCESS;
 }
 
+// 2-D uint8 tensor map over a row-major [rows, cols] byte matrix (row stride in
+// bytes), box = box_cols x box_rows, no swizzle, out-of-bounds bytes read as
+// zero.
+bool make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                     uint32_t box_cols, uint32_t box_rows) {
+  if (tmap_encoder() == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace fam
 
 using namespace fam;

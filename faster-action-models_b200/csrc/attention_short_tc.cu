@@ -14,12 +14,14 @@
 // Four online softmaxes over disjoint key subsets run side by side and are
 // merged once at the end through shared memory.  Warp roles (256 threads):
 //   warp 0      TMA producer: the Q copies, then 128-key blocks of K and V from
-//               source 1 (the cache) and source 2 (fresh keys) into a 4-stage
+//               source 1 (the cache) and source 2 (fresh keys) into a 5-stage
 //               ring; 3-D tensor maps whose boxes are min(128, keys) rows, so
 //               a block that runs past a source's keys reads zeros there (a
 //               source shorter than 128 keys leaves the rest of the stage as
 //               it was: zeroed at the start, or an earlier block's finite keys,
-//               all masked);
+//               all masked); with an attend mask whose rows and offsets
+//               suit TMA, the block's [queries, 128 keys] attend bytes land in
+//               the same stage;
 //   warp 1      TMEM (S double buffer at columns [0, 256), P double buffer
 //               [256, 384), O [384, 448)) and MMA issue: S two blocks ahead of
 //               the softmax, P(j).V(j) with A = P in TMEM and B = the V tile as
@@ -44,10 +46,12 @@ constexpr int kShRows = 128;                 // Q tile rows (4 copies of <= 32 q
 constexpr int kShQ = 32;                     // queries per (batch, head)
 constexpr int kShHd = 64;                    // head dim: one 128-byte swizzle row
 constexpr int kShTile = kShRows * 128;       // one [128 rows, 64 bf16] tile
-constexpr int kShStages = 4;
+constexpr int kShStages = 5;
+constexpr int kShMaskTile = kShQ * kShRows;     // attend bytes of one block [32][128]
 constexpr int kShMergeRow = 68;              // floats per merged O row (pad: conflict-free float4 stores)
 constexpr int kShMergeBytes = 4 * kShQ * kShMergeRow * 4 + 4 * kShQ * 2 * 4;
-constexpr int kShBarOff = (1 + 2 * kShStages) * kShTile + kShMergeBytes;
+constexpr int kShBarOff = (1 + 2 * kShStages) * kShTile + kShStages * kShMaskTile;
+static_assert(kShMergeBytes <= kShStages * kShTile, "the merge overlays the K ring");
 constexpr int kShSmem = kShBarOff + 256 + 1024;  // + barriers, + alignment slack
 constexpr uint32_t kShTmemCols = 512;
 constexpr uint32_t kShColS = 0, kShColP = 256, kShColO = 384;
@@ -60,6 +64,7 @@ struct AttnShortArgs {
   CUtensorMap tv1;
   CUtensorMap tk2;   // K2  [B, S2, H*64], box 64 x min(128, S2)
   CUtensorMap tv2;
+  CUtensorMap tm;    // attend bytes [Sq, S1+S2], box 128 x Sq (mask_tma)
   const uint8_t* mask2d;
   long long mask_rs;
   const uint8_t* key_mask;
@@ -68,6 +73,7 @@ struct AttnShortArgs {
   long long out_bs, out_ts;
   int Sq, S1, S2;
   int box1, box2;    // rows per K / V box of each source
+  int mask_tma;      // attend tiles arrive with the K / V stages
   int kv1_const;
   float scale_log2;
   int* status;
@@ -97,7 +103,10 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
   uint8_t* sQ = sm;
   uint8_t* sK = sm + kShTile;                      // stage s at + s kShTile
   uint8_t* sV = sm + (1 + kShStages) * kShTile;
-  float* so = reinterpret_cast<float*>(sm + (1 + 2 * kShStages) * kShTile);  // [4][32][kShMergeRow]
+  uint8_t* sMk = sm + (1 + 2 * kShStages) * kShTile;  // stage s at + s kShMaskTile
+  // the quarter merge overlays the K ring: no copy is in flight and no MMA reads
+  // it once the last P.V is complete
+  float* so = reinterpret_cast<float*>(sK);                                    // [4][32][kShMergeRow]
   float* sml = so + 4 * kShQ * kShMergeRow;                                     // [4][32] (m, l)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kShBarOff);
   uint64_t* q_full = bars;
@@ -138,6 +147,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       tma_prefetch_desc(&a.tk2);
       tma_prefetch_desc(&a.tv2);
     }
+    if (a.mask_tma) tma_prefetch_desc(&a.tm);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kShTmemCols);
@@ -173,7 +183,10 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       const uint64_t pol_q = policy_evict_last();
       auto load_block = [&](int j) {
         const int s = j % kShStages;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * 128 * (j < nb1 ? a.box1 : a.box2));
+        mbar_arrive_expect_tx(&kv_full[s], 2 * 128 * (j < nb1 ? a.box1 : a.box2) + (a.mask_tma ? a.Sq * kShRows : 0));
+        if (a.mask_tma)
+          tma_load_2d(sMk + s * kShMaskTile, &a.tm, &kv_full[s], j < nb1 ? j * kShRows : a.S1 + (j - nb1) * kShRows,
+                      0, pol_q);
         if (j < nb1) {
           tma_load_3d(sK + s * kShTile, &a.tk1, &kv_full[s], h * kShHd, j * kShRows, b, pol_kv);
           tma_load_3d(sV + s * kShTile, &a.tv1, &kv_full[s], h * kShHd, j * kShRows, b, pol_kv);
@@ -270,7 +283,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
     auto prefetch = [&](int j) {
       int kg0, nv;
       block_keys(j, kg0, nv);
-      if (mrow != nullptr && nv >= 32 && (reinterpret_cast<uintptr_t>(mrow + kg0) & 15) == 0) {
+      if (mrow != nullptr && !a.mask_tma && nv >= 32 && (reinterpret_cast<uintptr_t>(mrow + kg0) & 15) == 0) {
         mw0 = __ldg(reinterpret_cast<const uint4*>(mrow + kg0));
         mw1 = __ldg(reinterpret_cast<const uint4*>(mrow + kg0 + 16));
       }
@@ -295,16 +308,36 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       if (km != nullptr) bits &= __ballot_sync(0xffffffffu, kmv != 0);
       if (!row_ok) {
         bits = 0u;
+      } else if (a.mask_tma) {
+        // the block's attend tile landed with its K / V (kv_full of the stage)
+        const int s = j % kShStages;
+        got = mbar_wait(&kv_full[s], static_cast<uint32_t>(j / kShStages) & 1, a.status, kErrShortWait);
+        const uint4* t4 = reinterpret_cast<const uint4*>(sMk + s * kShMaskTile + q * kShRows + 32 * wq);
+        bits = got ? bits & word_bits(t4[0], t4[1]) : 0u;
       } else if (mrow != nullptr) {
         bits &= (nv >= 32 && (reinterpret_cast<uintptr_t>(mrow + kg0) & 15) == 0) ? word_bits(mw0, mw1)
                                                                                 : attend_bits(mrow + kg0, nv);
       }
       if (j + 1 < nb) prefetch(j + 1);
       tmem_wait_ld();
-      float mx = -INFINITY;
+      // one warp per SM sub-partition runs this: keep the dependency chains short
+      // (tree maximum, four partial sums) and skip the per-key selects when every
+      // key of the slice is visible to every row of the warp (a second softmax
+      // warp per quarter sharing the running maximum measured slower: the
+      // per-block exchange cost more than the halved element work)
+      const bool full = __all_sync(0xffffffffu, bits == 0xffffffffu);
+      if (!full) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if ((bits >> i) & 1u) mx = fmaxf(mx, sv[i]);
+        for (int i = 0; i < 32; ++i) sv[i] = ((bits >> i) & 1u) ? sv[i] : -INFINITY;
+      }
+      float t16[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) t16[i] = fmaxf(sv[i], sv[i + 16]);
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) t16[i] = fmaxf(t16[i], t16[i + w]);
+      float mx = t16[0];
       mx = mx == -INFINITY ? mx : mx * a.scale_log2;  // scale_log2 > 0
       float alpha = 1.f;
       if (mx > m + kShLazy || (m == -INFINITY && mx > -INFINITY)) {
@@ -312,15 +345,16 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
         m = mx;
       }
       const float base = m == -INFINITY ? 0.f : m;
-      float ps = 0.f;
+      float psa[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const float p0 = ((bits >> i) & 1u) ? exp2f(fmaf(sv[i], a.scale_log2, -base)) : 0.f;
-        const float p1 = ((bits >> (i + 1)) & 1u) ? exp2f(fmaf(sv[i + 1], a.scale_log2, -base)) : 0.f;
-        ps += p0 + p1;
+        const float p0 = exp2f(fmaf(sv[i], a.scale_log2, -base));  // exp2(-inf) = 0 for hidden keys
+        const float p1 = exp2f(fmaf(sv[i + 1], a.scale_log2, -base));
+        psa[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack2_bf16(p0, p1);
       }
+      const float ps = (psa[0] + psa[1]) + (psa[2] + psa[3]);
       // P buffer j & 1 was last read by P(j-2).V(j-2)
       got = j < 2 || mbar_wait(&pv_done[j & 1], static_cast<uint32_t>((j >> 1) - 1) & 1, a.status, kErrShortWait);
       if (!__all_sync(0xffffffffu, got)) {
@@ -460,6 +494,9 @@ static bool prepare_attention_short_tc(const AttnArgs& a, int B, int head_dim, A
         !make_tmap_bf16_3d(&s->tv2, a.v2, B, a.S2, cols, a.kv2_ts, a.kv2_bs, s->box2))
       return false;
   }
+  // attend tiles by TMA: 16-byte rows and block offsets (source 2 starts at S1)
+  s->mask_tma = a.mask2d != nullptr && aligned16(a.mask2d) && a.mask_rs % 16 == 0 && (a.S2 == 0 || a.S1 % 16 == 0) &&
+                make_tmap_u8_2d(&s->tm, a.mask2d, a.Sq, a.S1 + a.S2, a.mask_rs, kShRows, a.Sq);
   s->mask2d = a.mask2d;
   s->mask_rs = a.mask_rs;
   s->key_mask = a.key_mask;

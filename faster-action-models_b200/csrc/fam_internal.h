@@ -30,6 +30,11 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64
 bool make_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t batch, uint64_t rows, uint64_t cols,
                        uint64_t row_stride, uint64_t batch_stride, uint32_t box_rows);
 
+// 2-D uint8 tensor map over [rows, cols] bytes (row stride in bytes, a multiple of
+// 16); box = box_cols x box_rows, no swizzle, out-of-bounds bytes read as zero.
+bool make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                     uint32_t box_cols, uint32_t box_rows);
+
 // ------------------------------------------------------------------ GEMM
 enum EpiKind : int { kEpiStore = 0, kEpiPartial = 1, kEpiResidual = 2 };
 enum ActKind : int { kActNone = 0, kActGeluTanh = 1, kActSilu = 2 };
