@@ -680,6 +680,8 @@ def run_case(case: str, reps: int) -> None:
       xattn_c2          the backbone's cross attention: 1760 queries over 64 context keys
       cae_c0            config 0: compact expert chunk with the Action-VAE decode in its epilogue
       fused_c1          config 1: the fused chunk kernel (plain launches), `--euler-steps`
+      chain_c1_b8       config 1 at batch 8: the launch chain (plain launches), the last
+                        repetition inside the NVTX range "chain_c1_b8"
       prefill_c2        config 2: the 30-block backbone prefill, batch 1
       vae_c1            VideoVAE38 encode of one 512 x 704 observation frame (p50 printed)
     """
@@ -732,6 +734,27 @@ def run_case(case: str, reps: int) -> None:
         lat = noise.to(dev).clone()
         for _ in range(reps):
             eng.chunk(lat, ts, ds, ctx.to(dev), cm.to(dev), list(ck), list(cv), mask.to(dev), use_graph=False)
+    elif case == "chain_c1_b8":
+        M_, dit, ck, cv, ctx, cm, noise, mask = build_c1(dev)
+        eng = dit.engine()
+        ts, ds = M.build_inference_schedule(C1_STEPS, C1_SHIFT)
+        B = 8
+        g = torch.Generator().manual_seed(8)
+        HD = C1_CFG["num_heads"] * C1_CFG["attn_head_dim"]
+        ck8 = [torch.randn(B, C1_SV, HD, generator=g).bfloat16().to(dev) for _ in range(C1_CFG["num_layers"])]
+        cv8 = [torch.randn(B, C1_SV, HD, generator=g).bfloat16().to(dev) for _ in range(C1_CFG["num_layers"])]
+        ctx8 = torch.randn(B, C1_CTX, C1_CFG["text_dim"], generator=g).bfloat16().to(dev)
+        cm8 = torch.ones(B, C1_CTX, dtype=torch.uint8, device=dev)
+        n8 = torch.randn(B, C1_SA, C1_CFG["action_dim"], generator=g).bfloat16().to(dev)
+        lat8 = n8.clone()
+        for r in range(reps):
+            if r == reps - 1:
+                torch.cuda.synchronize()
+                torch.cuda.nvtx.range_push("chain_c1_b8")
+            lat8.copy_(n8)
+            eng.chunk(lat8, ts, ds, ctx8, cm8, ck8, cv8, mask.to(dev), out=lat8, use_graph=False)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     elif case == "prefill_c2":
         with torch.device(dev):
             vid = M.WanVideoDiT(**VIDEO_CFG)
