@@ -480,6 +480,26 @@ def sub_c1(dev, peaks):
         ms8 = time_calls(chunk8, 10, warmup=3)
     rec["batch8"] = {"path": eng.last_path(), "latency_p50_ms": p50(ms8), "chunks_per_s": B * 1e3 / p50(ms8),
                      "clocks": clk8.summary()}
+    del ck8, cv8
+    # batch 64 (BASELINE config 1's largest batch): inputs made on the device (12.9 GB of K/V)
+    B = 64
+    gd = torch.Generator(device=dev).manual_seed(64)
+    ck64 = [torch.randn(B, C1_SV, HD, device=dev, generator=gd).bfloat16() for _ in range(C1_CFG["num_layers"])]
+    cv64 = [torch.randn(B, C1_SV, HD, device=dev, generator=gd).bfloat16() for _ in range(C1_CFG["num_layers"])]
+    ctx64 = torch.randn(B, C1_CTX, C1_CFG["text_dim"], device=dev, generator=gd).bfloat16()
+    cm64 = torch.ones(B, C1_CTX, dtype=torch.uint8, device=dev)
+    n64 = torch.randn(B, C1_SA, C1_CFG["action_dim"], device=dev, generator=gd).bfloat16()
+    lat64 = n64.clone()
+
+    def chunk64():
+        lat64.copy_(n64)
+        eng.chunk(lat64, ts, ds, ctx64, cm64, ck64, cv64, mask_d, out=lat64)
+
+    with ClockSampler(dev.index or 0) as clk64:
+        ms64 = time_calls(chunk64, 5, warmup=3)
+    rec["batch64"] = {"path": eng.last_path(), "latency_p50_ms": p50(ms64), "chunks_per_s": B * 1e3 / p50(ms64),
+                      "clocks": clk64.summary()}
+    del ck64, cv64
     cps, cores, n, per_eval = cpu_c1_chunks_per_s()
     rec["cpu_baseline"] = {"value": cps, "unit": "chunks/s", "cores": cores, "kind": "port",
                            "sample": f"{n} model evaluations (10 per chunk) by the CPU oracle in bf16; "

@@ -26,9 +26,12 @@
 //     Under CUDA's lazy module loading (the default) that first call also
 //     loads the library's device image, this array included: make it at
 //     start-up, before the part of the program that must not allocate.
-//   * Kernel: the split-KV mma.sync attention of fam_attention.  The tcgen05
-//     long-self-attention kernel that fam_attention picks for one key source
-//     of head_dim 128 needs a transposed-V workspace, so it is not used here.
+//   * Kernel: the tcgen05 short-query kernel when the descriptor qualifies
+//     (kv_splits = 0, head_dim 64, <= 32 queries, batch x heads >= 128: one CTA
+//     per (batch, head), no scratch), else the split-KV mma.sync attention of
+//     fam_attention.  The tcgen05 long-self-attention kernel that fam_attention
+//     picks for one key source of head_dim 128 needs a transposed-V workspace,
+//     so it is not used here.
 //   * Every call on a device shares the one array and leaves its contents
 //     behind.  Calls that may overlap on the GPU (different streams, or
 //     concurrent graphs) race on it: serialize them.
@@ -86,12 +89,14 @@ extern "C" int fam_attention_static_scratch(const fam_attention_desc* d, void* s
   AttnScratch s;
   int rc = attention_prepare(d, &a, &s);
   if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d->kv_splits <= 0 && attention_short_tc_taken(a, d->batch, d->head_dim))
+    return check_cuda(launch_attention_auto(a, d->batch, d->head_dim, st, false), "attention_static_scratch launch");
   if (s.total > kStaticScratchBytes)
     return set_error(
         "attention_static_scratch: this call needs %zu bytes of scratch, the static array holds "
         "%zu; use fam_attention with a workspace or fewer kv_splits",
         s.total, kStaticScratchBytes);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a.nsplit > 1) {
     void* scratch = nullptr;
     rc = static_scratch(st, &scratch);

@@ -186,9 +186,12 @@ FAM_API int fam_attention(const fam_attention_desc* desc, void* workspace, size_
  * stream capture looks the array's address up (a reset context is followed);
  * make one call on each device before any capture there, and at start-up:
  * under CUDA's lazy module loading that first call loads the library's device
- * image, this array included.  Runs the split-KV mma.sync kernel (not the
- * tcgen05 long-self-attention kernel, which needs a transposed-V workspace).
- * All calls on a device share the array: calls that overlap on the GPU race. */
+ * image, this array included.  A descriptor with kv_splits = 0 that the
+ * tcgen05 short-query kernel takes (head_dim 64, q_tokens <= 32, batch x heads
+ * >= 128) runs that kernel, which needs no scratch; every other descriptor
+ * runs the split-KV mma.sync kernel (not the tcgen05 long-self-attention
+ * kernel, which needs a transposed-V workspace).  All calls on a device share
+ * the array: calls that overlap on the GPU race. */
 FAM_API int fam_attention_static_scratch(const fam_attention_desc* desc, void* stream);
 
 /* ======================================================================

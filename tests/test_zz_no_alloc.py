@@ -65,6 +65,25 @@ def test_static_scratch_matches_workspace_entry_point_twice():
         assert err_sd <= 2e-2 and cos >= 0.999, f"call {call}: vs fp32 SDPA max|d| {err_sd} cos {cos}"
 
 
+def test_static_scratch_short_query_shape_runs_tcgen05_without_scratch():
+    """Batch 8 x 16 heads of 32 queries: the descriptor the tcgen05 short-query kernel
+    takes (no split workspace), through the allocation-free entry point, twice."""
+    lib = _lib.lib()
+    for call, seed in ((0, 21), (1, 22)):
+        q, k1, v1, H, k2, v2, mask = _case(8, seed)
+        d, out = ops.attention_desc(q, k1, v1, H, k2, v2, mask=mask)
+        n = C.c_size_t()
+        _lib.check(lib.fam_attention_workspace_size(C.byref(d), C.byref(n)), "workspace size")
+        assert n.value == 0, "the case must take the scratch-free tcgen05 kernel"
+        _lib.check(lib.fam_attention_static_scratch(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                   "fam_attention_static_scratch")
+        torch.cuda.synchronize()
+        sd = _sdpa_fp32(q, k1, v1, H, k2, v2, mask)
+        err = (out.float() - sd).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(out.float().flatten(), sd.flatten(), dim=0).item()
+        assert err <= 2e-2 and cos >= 0.999, f"call {call}: vs fp32 SDPA max|d| {err} cos {cos}"
+
+
 def test_static_scratch_rejects_oversized_problem():
     lib = _lib.lib()
     q, k1, v1, H, k2, v2, mask = _case(4, 13)
