@@ -1160,14 +1160,19 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
           w[4 * i + 2] = u.z;
           w[4 * i + 3] = u.w;
         }
-        mb0 = mb1 = 0u;
+        uint32_t all1 = 0x01010101u;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 16; ++i) all1 &= w[i];
+        if (all1 != 0x01010101u) {  // not every byte 1: byte by byte
+          mb0 = mb1 = 0u;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            mb0 |= (((w[i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
-            mb1 |= (((w[8 + i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
-          }
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              mb0 |= (((w[i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
+              mb1 |= (((w[8 + i] >> (8 * k)) & 0xffu) != 0u ? 1u : 0u) << (4 * i + k);
+            }
+        }
       }
       tmem_wait_ld();
       float mx = -INFINITY;

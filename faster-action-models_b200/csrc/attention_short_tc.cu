@@ -79,9 +79,11 @@ struct AttnShortArgs {
   int* status;
 };
 
-// Bit i: byte i of the 32 attend bytes in (u0, u1) is nonzero.
+// Bit i: byte i of the 32 attend bytes in (u0, u1) is nonzero.  All-ones bytes
+// (a bool mask that hides nothing here) take one AND chain.
 __device__ __forceinline__ uint32_t word_bits(const uint4& u0, const uint4& u1) {
   const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  if ((w[0] & w[1] & w[2] & w[3] & w[4] & w[5] & w[6] & w[7] & 0x01010101u) == 0x01010101u) return 0xffffffffu;
   uint32_t bits = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
