@@ -46,15 +46,29 @@ constexpr int kShRows = 128;                 // Q tile rows (4 copies of <= 32 q
 constexpr int kShQ = 32;                     // queries per (batch, head)
 constexpr int kShHd = 64;                    // head dim: one 128-byte swizzle row
 constexpr int kShTile = kShRows * 128;       // one [128 rows, 64 bf16] tile
-constexpr int kShStages = 5;
 constexpr int kShMaskTile = kShQ * kShRows;     // attend bytes of one block [32][128]
 constexpr int kShMergeRow = 68;              // floats per merged O row (pad: conflict-free float4 stores)
 constexpr int kShMergeBytes = 4 * kShQ * kShMergeRow * 4 + 4 * kShQ * 2 * 4;
-constexpr int kShBarOff = (1 + 2 * kShStages) * kShTile + kShStages * kShMaskTile;
-static_assert(kShMergeBytes <= kShStages * kShTile, "the merge overlays the K ring");
-constexpr int kShSmem = kShBarOff + 256 + 1024;  // + barriers, + alignment slack
-constexpr uint32_t kShTmemCols = 512;
-constexpr uint32_t kShColS = 0, kShColP = 256, kShColO = 384;
+
+// Two shapes of the kernel.  The full one (one CTA per SM: S and P
+// double-buffered, 512 TMEM columns, a 5-stage ring) serves launches of up to
+// two waves; the compact one (two CTAs per SM: one S and one P buffer, 256
+// TMEM columns, a 2-stage ring) serves larger launches, where the second
+// CTA's softmax fills the gaps in the first one's chain.
+template <bool kCompact>
+struct ShCfg {
+  static constexpr int kStages = kCompact ? 2 : 5;
+  static constexpr int kSB = kCompact ? 1 : 2;  // S buffers
+  static constexpr int kPB = kCompact ? 1 : 2;  // P buffers
+  static constexpr uint32_t kColS = 0;
+  static constexpr uint32_t kColP = 128 * kSB;
+  static constexpr uint32_t kColO = kColP + 64 * kPB;
+  static constexpr uint32_t kTmemCols = kCompact ? 256 : 512;
+  static constexpr int kBarOff = (1 + 2 * kStages) * kShTile + kStages * kShMaskTile;
+  static constexpr int kSmem = kBarOff + 256 + 1024;  // + barriers, + alignment slack
+  static_assert(kShMergeBytes <= 2 * kStages * kShTile, "the merge overlays the K and V rings");
+  static_assert(kColO + 64 <= kTmemCols, "TMEM columns");
+};
 constexpr float kShLazy = 8.f;
 constexpr int kErrShortWait = 0x4155;
 
@@ -99,25 +113,28 @@ __device__ __forceinline__ uint32_t attend_bits(const uint8_t* p, int nv) {
   return bits;
 }
 
-__global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid_constant__ AttnShortArgs a) {
+template <bool kCompact>
+__global__ void __launch_bounds__(256, kCompact ? 2 : 1) attention_short_tc_kernel(const __grid_constant__ AttnShortArgs a) {
+  using Cfg = ShCfg<kCompact>;
+  constexpr int kSB = Cfg::kSB, kPB = Cfg::kPB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = sm;
   uint8_t* sK = sm + kShTile;                      // stage s at + s kShTile
-  uint8_t* sV = sm + (1 + kShStages) * kShTile;
-  uint8_t* sMk = sm + (1 + 2 * kShStages) * kShTile;  // stage s at + s kShMaskTile
-  // the quarter merge overlays the K ring: no copy is in flight and no MMA reads
-  // it once the last P.V is complete
+  uint8_t* sV = sm + (1 + Cfg::kStages) * kShTile;
+  uint8_t* sMk = sm + (1 + 2 * Cfg::kStages) * kShTile;  // stage s at + s kShMaskTile
+  // the quarter merge overlays the K and V rings: no copy is in flight and no
+  // MMA reads them once the last P.V is complete
   float* so = reinterpret_cast<float*>(sK);                                    // [4][32][kShMergeRow]
   float* sml = so + 4 * kShQ * kShMergeRow;                                     // [4][32] (m, l)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kShBarOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Cfg::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                    // [kShStages]
-  uint64_t* kv_empty = bars + 1 + kShStages;       // [kShStages]
-  uint64_t* s_full = bars + 1 + 2 * kShStages;     // [2] S buffer
-  uint64_t* p_full = bars + 3 + 2 * kShStages;     // [2] P buffer, 4 softmax warps each
-  uint64_t* pv_done = bars + 5 + 2 * kShStages;    // [2] P buffer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * kShStages);
+  uint64_t* kv_full = bars + 1;                    // [Cfg::kStages]
+  uint64_t* kv_empty = bars + 1 + Cfg::kStages;       // [Cfg::kStages]
+  uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;     // [kSB] S buffer
+  uint64_t* p_full = bars + 3 + 2 * Cfg::kStages;     // [kPB] P buffer, 4 softmax warps each
+  uint64_t* pv_done = bars + 5 + 2 * Cfg::kStages;    // [kPB] P buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * Cfg::kStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* fail_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -128,7 +145,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kShStages; ++i) {
+    for (int i = 0; i < Cfg::kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -152,7 +169,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
     if (a.mask_tma) tma_prefetch_desc(&a.tm);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kShTmemCols);
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
   // Rows a box does not cover are read by the MMAs too: zero the Q copies when
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
     const int first_short[2] = {a.box1 < kShRows && nb1 > 0 ? 0 : -1, a.box2 < kShRows && nb > nb1 ? nb1 : -1};
     for (int f = 0; f < 2; ++f) {
       const int j = first_short[f];
-      if (j < 0 || j >= kShStages) continue;
+      if (j < 0 || j >= Cfg::kStages) continue;
       for (int i = threadIdx.x; i < kShTile / 16; i += blockDim.x) {
         reinterpret_cast<uint4*>(sK + j * kShTile)[i] = z;
         reinterpret_cast<uint4*>(sV + j * kShTile)[i] = z;
@@ -184,7 +201,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       const uint64_t pol_kv = policy_evict_first();  // every K/V tile is read by this CTA only
       const uint64_t pol_q = policy_evict_last();
       auto load_block = [&](int j) {
-        const int s = j % kShStages;
+        const int s = j % Cfg::kStages;
         mbar_arrive_expect_tx(&kv_full[s], 2 * 128 * (j < nb1 ? a.box1 : a.box2) + (a.mask_tma ? a.Sq * kShRows : 0));
         if (a.mask_tma)
           tma_load_2d(sMk + s * kShMaskTile, &a.tm, &kv_full[s], j < nb1 ? j * kShRows : a.S1 + (j - nb1) * kShRows,
@@ -201,15 +218,15 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       // cache blocks stream in before the programmatic-launch wait when no
       // earlier kernel of the chain writes them
       if (a.kv1_const)
-        for (; issued < kShStages && issued < nb1; ++issued) load_block(issued);
+        for (; issued < Cfg::kStages && issued < nb1; ++issued) load_block(issued);
       pdl_wait();
       mbar_arrive_expect_tx(q_full, 4 * a.Sq * 128);
       for (int r = 0; r < 4; ++r) tma_load_3d(sQ + r * kShQ * 128, &a.tq, q_full, h * kShHd, 0, b, pol_q);
       for (int j = issued; j < nb; ++j) {
-        const int s = j % kShStages;
+        const int s = j % Cfg::kStages;
         if (*abort_flag) break;
-        if (j >= kShStages &&
-            !mbar_wait(&kv_empty[s], static_cast<uint32_t>(j / kShStages - 1) & 1, a.status, kErrShortWait)) {
+        if (j >= Cfg::kStages &&
+            !mbar_wait(&kv_empty[s], static_cast<uint32_t>(j / Cfg::kStages - 1) & 1, a.status, kErrShortWait)) {
           *abort_flag = 1;
           break;
         }
@@ -218,8 +235,8 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       }
       // every issued copy has landed before the CTA can exit
       mbar_wait(q_full, 0, a.status, kErrShortWait);
-      for (int j = max(0, issued - kShStages); j < issued; ++j)
-        mbar_wait(&kv_full[j % kShStages], static_cast<uint32_t>(j / kShStages) & 1, a.status, kErrShortWait);
+      for (int j = max(0, issued - Cfg::kStages); j < issued; ++j)
+        mbar_wait(&kv_full[j % Cfg::kStages], static_cast<uint32_t>(j / Cfg::kStages) & 1, a.status, kErrShortWait);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -227,33 +244,33 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
       const uint32_t idesc_pv = umma_idesc_bf16_bmn(kShRows, kShHd);
       bool ok = mbar_wait(q_full, 0, a.status, kErrShortWait);
       auto issue_s = [&](int j) -> bool {
-        const int s = j % kShStages;
-        if (!mbar_wait(&kv_full[s], static_cast<uint32_t>(j / kShStages) & 1, a.status, kErrShortWait)) return false;
+        const int s = j % Cfg::kStages;
+        if (!mbar_wait(&kv_full[s], static_cast<uint32_t>(j / Cfg::kStages) & 1, a.status, kErrShortWait)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kShHd / 16; ++kk)
-          umma_bf16_ss(tmem_base + kShColS + 128 * (j & 1), umma_desc_sw128(sQ) + 2 * kk,
+          umma_bf16_ss(tmem_base + Cfg::kColS + 128 * (j % kSB), umma_desc_sw128(sQ) + 2 * kk,
                        umma_desc_sw128(sK + s * kShTile) + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[j % kSB]);
         return true;
       };
       if (ok && nb > 0) ok = issue_s(0);
-      if (ok && nb > 1) ok = issue_s(1);
+      if (kSB > 1 && ok && nb > 1) ok = issue_s(1);
       for (int j = 0; ok && j < nb; ++j) {
         if (*abort_flag ||
-            !mbar_wait(&p_full[j & 1], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrShortWait)) {
+            !mbar_wait(&p_full[j % kPB], static_cast<uint32_t>(j / kPB) & 1, a.status, kErrShortWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int s = j % kShStages;
+        const int s = j % Cfg::kStages;
 #pragma unroll
         for (int kk = 0; kk < kShRows / 16; ++kk)
-          umma_bf16_ts(tmem_base + kShColO, tmem_base + kShColP + 64 * (j & 1) + 8 * kk,
+          umma_bf16_ts(tmem_base + Cfg::kColO, tmem_base + Cfg::kColP + 64 * (j % kPB) + 8 * kk,
                        umma_desc_sw128_mn(sV + s * kShTile + kk * 16 * 128), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[j & 1]);
+        umma_commit(&pv_done[j % kPB]);
         umma_commit(&kv_empty[s]);  // K_j (read by S(j)) and V_j consumed
-        if (j + 2 < nb) ok = issue_s(j + 2);
+        if (j + kSB < nb) ok = issue_s(j + kSB);  // S buffer j % kSB was read by softmax(j)
       }
       if (!ok) *abort_flag = 1;
     }
@@ -264,7 +281,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
     {
       const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) tmem_st16(lane_addr + kShColP + 16 * c, z);
+      for (int c = 0; c < 4 * kPB; ++c) tmem_st16(lane_addr + Cfg::kColP + 16 * c, z);
       tmem_wait_st();
     }
     const int q = lane;
@@ -296,14 +313,14 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
     bool ok = true;
     for (int j = 0; j < nb && ok; ++j) {
       // warp-uniform outcome of every wait: the TMEM loads and stores are warp-collective
-      bool got = mbar_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1, a.status, kErrShortWait);
+      bool got = mbar_wait(&s_full[j % kSB], static_cast<uint32_t>(j / kSB) & 1, a.status, kErrShortWait);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float sv[32];
-      tmem_ld32(lane_addr + kShColS + 128 * (j & 1) + 32 * wq, sv);
+      tmem_ld32(lane_addr + Cfg::kColS + 128 * (j % kSB) + 32 * wq, sv);
       int kg0, nv;
       block_keys(j, kg0, nv);
       uint32_t bits = nv >= 32 ? 0xffffffffu : ((1u << nv) - 1u);
@@ -312,8 +329,8 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
         bits = 0u;
       } else if (a.mask_tma) {
         // the block's attend tile landed with its K / V (kv_full of the stage)
-        const int s = j % kShStages;
-        got = mbar_wait(&kv_full[s], static_cast<uint32_t>(j / kShStages) & 1, a.status, kErrShortWait);
+        const int s = j % Cfg::kStages;
+        got = mbar_wait(&kv_full[s], static_cast<uint32_t>(j / Cfg::kStages) & 1, a.status, kErrShortWait);
         const uint4* t4 = reinterpret_cast<const uint4*>(sMk + s * kShMaskTile + q * kShRows + 32 * wq);
         bits = got ? bits & word_bits(t4[0], t4[1]) : 0u;
       } else if (mrow != nullptr) {
@@ -357,15 +374,15 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
         pk[i / 2] = pack2_bf16(p0, p1);
       }
       const float ps = (psa[0] + psa[1]) + (psa[2] + psa[3]);
-      // P buffer j & 1 was last read by P(j-2).V(j-2)
-      got = j < 2 || mbar_wait(&pv_done[j & 1], static_cast<uint32_t>((j >> 1) - 1) & 1, a.status, kErrShortWait);
+      // P buffer j % kPB was last read by P(j-kPB).V(j-kPB)
+      got = j < kPB || mbar_wait(&pv_done[j % kPB], static_cast<uint32_t>(j / kPB - 1) & 1, a.status, kErrShortWait);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       if (j > 0 && !__all_sync(0xffffffffu, alpha == 1.f)) {
         // rescale O once P(j-1).V(j-1) (and with it every earlier P.V) is complete
-        got = mbar_wait(&pv_done[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1, a.status, kErrShortWait);
+        got = mbar_wait(&pv_done[(j - 1) % kPB], static_cast<uint32_t>((j - 1) / kPB) & 1, a.status, kErrShortWait);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -375,32 +392,32 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             float ov[32];
-            tmem_ld32(lane_addr + kShColO + 32 * c, ov);
+            tmem_ld32(lane_addr + Cfg::kColO + 32 * c, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(lane_addr + kShColO + 32 * c, ov);
+            tmem_st32(lane_addr + Cfg::kColO + 32 * c, ov);
           }
         }
       }
       tc_fence_after();
-      tmem_st16(lane_addr + kShColP + 64 * (j & 1) + 16 * wq, pk);
+      tmem_st16(lane_addr + Cfg::kColP + 64 * (j % kPB) + 16 * wq, pk);
       l = l * alpha + ps;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      if (lane == 0) mbar_arrive(&p_full[j % kPB]);
     }
     if (!ok) *abort_flag = 1;
     const bool fin = ok && nb > 0 &&
-                     mbar_wait(&pv_done[(nb - 1) & 1], static_cast<uint32_t>((nb - 1) >> 1) & 1, a.status, kErrShortWait);
+                     mbar_wait(&pv_done[(nb - 1) % kPB], static_cast<uint32_t>((nb - 1) / kPB) & 1, a.status, kErrShortWait);
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
       float* orow = so + (wq * kShQ + q) * kShMergeRow;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         float ov[32];
-        tmem_ld32(lane_addr + kShColO + 32 * c, ov);
+        tmem_ld32(lane_addr + Cfg::kColO + 32 * c, ov);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -462,7 +479,7 @@ __global__ void __launch_bounds__(256, 1) attention_short_tc_kernel(const __grid
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kShTmemCols);
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -515,12 +532,12 @@ static bool prepare_attention_short_tc(const AttnArgs& a, int B, int head_dim, A
   return true;
 }
 
-cudaError_t launch_attention_auto(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl) {
-  AttnShortArgs s;
-  if (!prepare_attention_short_tc(a, B, head_dim, &s)) return launch_attention(a, B, head_dim, st, pdl);
+template <bool kCompact>
+static cudaError_t launch_short_cfg(const AttnShortArgs& s, int B, int H, cudaStream_t st, bool pdl) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attention_short_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kShSmem);
+    cudaError_t e = cudaFuncSetAttribute(attention_short_tc_kernel<kCompact>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, ShCfg<kCompact>::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -528,13 +545,21 @@ cudaError_t launch_attention_auto(const AttnArgs& a, int B, int head_dim, cudaSt
   attr_l[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr_l[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.H, B);
+  cfg.gridDim = dim3(H, B);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = kShSmem;
+  cfg.dynamicSmemBytes = ShCfg<kCompact>::kSmem;
   cfg.stream = st;
   cfg.attrs = attr_l;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_short_tc_kernel, s);
+  return cudaLaunchKernelEx(&cfg, attention_short_tc_kernel<kCompact>, s);
+}
+
+cudaError_t launch_attention_auto(const AttnArgs& a, int B, int head_dim, cudaStream_t st, bool pdl) {
+  AttnShortArgs s;
+  if (!prepare_attention_short_tc(a, B, head_dim, &s)) return launch_attention(a, B, head_dim, st, pdl);
+  // beyond two waves of one CTA per SM, two CTAs share each SM
+  return static_cast<long long>(B) * a.H > 2 * 148 ? launch_short_cfg<true>(s, B, a.H, st, pdl)
+                                                    : launch_short_cfg<false>(s, B, a.H, st, pdl);
 }
 
 bool attention_short_tc_taken(const AttnArgs& a, int B, int head_dim) {

@@ -126,7 +126,9 @@ def _workspace_bytes(fam_ops, q, k1, v1, H, k2=None, v2=None, mask=None, key_mas
     (8, 16, 32, 64, 0, False, True),      # its cross attention over the context tokens
     (4, 32, 20, 300, 17, True, True),     # ragged: 20 queries, sources not multiples of 128 keys
     (2, 64, 32, 129, 0, False, False),
-    (128, 1, 1, 5, 3, True, False)])
+    (128, 1, 1, 5, 3, True, False),
+    (32, 16, 32, 1760, 32, True, False),  # > 2 waves: the compact two-CTAs-per-SM variant
+    (20, 16, 20, 300, 17, True, True)])
 def test_tcgen05_short_query_attention(fam_ops, B, H, Sq, S1, S2, use_mask, use_km):
     """At most 32 queries per (batch, head), head dim 64, >= 128 (batch, head) pairs: the
     tcgen05 kernel with the queries replicated over the four TMEM lane quarters (each
@@ -178,10 +180,12 @@ def test_tcgen05_short_query_attention(fam_ops, B, H, Sq, S1, S2, use_mask, use_
     assert (alt.float()[:, live] - o).abs().max().item() < 2e-2
 
 
-def test_tcgen05_short_query_attention_sharp_rising_logits(fam_ops):
+@pytest.mark.parametrize("B", [8, 32])
+def test_tcgen05_short_query_attention_sharp_rising_logits(fam_ops, B):
     """Scores that grow along the keys move each quarter's running maximum by more than
-    the lazy-rescale margin again and again (O rows rescaled in TMEM)."""
-    B, H, Sq, S = 8, 16, 32, 1792
+    the lazy-rescale margin again and again (O rows rescaled in TMEM); batch 8 runs the
+    double-buffered variant, batch 32 the compact one."""
+    H, Sq, S = 16, 32, 1792
     g = torch.Generator(device="cuda").manual_seed(11)
     HD = H * 64
     q = (3.0 * torch.randn(B, Sq, HD, device="cuda", generator=g)).bfloat16()
