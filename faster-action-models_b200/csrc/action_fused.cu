@@ -1175,23 +1175,32 @@ __device__ void attention_item(const FusedArgs& a, uint8_t* stg, FusedSmemTail* 
         }
       }
       tmem_wait_ld();
-      float mx = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const float kf = m.sKsc[64 * wq + i];
         const bool bit = ((i < 32 ? mb0 >> i : mb1 >> (i - 32)) & 1u) != 0u;
         sv[i] = (v0 && kf != 0.f && bit) ? sv[i] * kf : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
       }
+      // short dependency chains (one warp per SM sub-partition runs this): a
+      // tree maximum and four partial sums
+      float t32[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t32[i] = fmaxf(sv[i], sv[i + 32]);
+#pragma unroll
+      for (int w2 = 16; w2 >= 1; w2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < w2; ++i) t32[i] = fmaxf(t32[i], t32[i + w2]);
+      const float mx = t32[0];
       const float base = mx == -INFINITY ? 0.f : mx;
       uint32_t pk[32];
-      float ps = 0.f;
+      float psa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
         const float p0 = exp2f(sv[i] - base), p1 = exp2f(sv[i + 1] - base);
-        ps += p0 + p1;
+        psa[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
       }
+      const float ps = (psa[0] + psa[1]) + (psa[2] + psa[3]);
       tmem_st16(lane_addr + kAttnColP + 32 * wq, pk);
       tmem_st16(lane_addr + kAttnColP + 32 * wq + 16, pk + 16);
       tmem_wait_st();
