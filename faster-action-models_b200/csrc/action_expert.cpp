@@ -31,15 +31,26 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 const __nv_bfloat16* bf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
 
-// Split-K so that tiles x splits fills ~one wave of 148 SMs, at least two
-// 64-wide K blocks per split.
+// Token-tile width of the chain's split-K weights-as-A GEMMs: 64 for 65..256
+// token rows, else the plan's own width.  Measured at 256 rows (batch 8 of 32
+// action tokens, graphs over weights beyond L2): 64-wide tiles with fewer
+// k-splits beat 256-wide tiles with more — qkv 12.8 -> 8.1 us, o / cross-q /
+// cross-o -> 6.1 us, ffn.2 > 13 -> 8.8 us — and leave fewer fp32 partials for
+// the row kernel that sums them.
+int chain_tile_n(int rows) { return rows > 64 && rows <= 256 ? 64 : 0; }
+
+// Split-K: with 64-wide token tiles about 256 CTAs, at least four 64-wide K
+// blocks per split; otherwise tiles x splits fills ~one wave of 148 SMs, at
+// least two K blocks per split.
 int choose_splits(int n_out, int k, int rows) {
-  const int bn = gemm_pick_bn(rows);
+  const int tn = chain_tile_n(rows);
+  const int bn = tn > 0 ? tn : gemm_pick_bn(rows);
   const int tiles = ((n_out + 127) / 128) * ((rows + bn - 1) / bn);
   const int kb = (k + 63) / 64;
-  int s = 148 / tiles;
+  const int min_kb = tn > 0 ? 4 : 2;
+  int s = tn > 0 ? (256 + tiles / 2) / tiles : 148 / tiles;
   if (s < 1) s = 1;
-  if (s > kb / 2) s = kb / 2 > 0 ? kb / 2 : 1;
+  if (s > kb / min_kb) s = kb / min_kb > 0 ? kb / min_kb : 1;
   const int kps = (kb + s - 1) / s;
   return (kb + kps - 1) / kps;
 }
@@ -202,7 +213,8 @@ int gemm_w(const Ctx& c, const void* W, const void* bias, int n_out, int k, cons
     e.bias = bf(bias);
   }
   GemmPlan p;
-  FAM_TRYI(gemm_plan(&p, W, k, act, act_ld, n_out, rows, k, splits, 0, e, true, false, c.e->status));
+  FAM_TRYI(gemm_plan(&p, W, k, act, act_ld, n_out, rows, k, splits, splits > 1 ? chain_tile_n(rows) : 0, e, true,
+                     false, c.e->status));
   FAM_LAUNCH(gemm_launch(p, c.st, c.pdl));
   return 0;
 }
